@@ -1,0 +1,455 @@
+#!/usr/bin/env python
+"""MoE-block tokens/s on B200 -- BASELINE config[1] (Kimi-K3-style MXFP4 decode).
+
+One step = one routed MoE layer over a batch of B tokens: token permutation,
+expert FFN (gate/up + SiTU, down) over the 8 routed experts of every token plus
+the always-on shared expert, ordered combine.  Workload per rank: hidden 7168,
+expert intermediate 2048, 256 routed experts (top-8, uniform-random router
+draws) + 1 shared expert, MXFP4 weights (e2m1 + ue8m0 per 32) drawn N(0, 0.02)
+and packed on the GPU, bf16 activations N(0, 1).  Weights total 6.0 GB, far
+above L2, so no flush is needed between steps; 16 distinct routings cycle.
+
+N>1 (torchrun): each rank runs its own replica of the workload (decode
+replicas, weak scaling, no data-path collective); timing is the max over ranks.
+`--impl reference` times the reference's own CPU moe_block (oracle/_ref) on
+the host cores for the same config and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "micro-vllm_b200"))
+
+CFG = dict(D=7168, I=2048, E=256, K=8, n_shared=1, fmt=7, act=2, act_a=4.0, act_b=25.0)
+EXPERT_BYTES = 3 * (CFG["I"] * CFG["D"] // 2 + CFG["I"] * CFG["D"] // 32)  # 23,396,352
+METRIC = "MoE-block tokens/sec (config[1] MXFP4 decode)"
+N_INPUTS = 16
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_ratio():
+    """DRAM bytes per algorithmic byte of the expert kernels, from the
+    committed ncu summary (profiles/decode_ffn_config1.txt), or None."""
+    p = os.path.join(ROOT, "profiles", "decode_ffn_config1.txt")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            if line.startswith("dram_bytes_per_algorithmic_byte:"):
+                return float(line.split(":", 1)[1])
+    return None
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML during a region."""
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, index):
+        self.samples, self.reasons = [], 0
+        self.stop_ev = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML missing: report no clocks
+            self.nv = None
+            self.max_mhz = None
+
+    def _run(self):
+        while not self.stop_ev.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h) & ~0x1
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop_ev.set()
+        if self.nv:
+            self.t.join()
+
+    def report(self):
+        if not self.nv or not self.samples:
+            return None
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "samples": len(self.samples),
+                "reasons": [n for b, n in self.REASONS.items() if self.reasons & b]}
+
+
+# ---------------------------------------------------------------- workload --
+class Workload:
+    """Config[1] weights on the device and N_INPUTS routed batches."""
+
+    def __init__(self, moe, torch, B, seed):
+        D, I, E, K, ns = CFG["D"], CFG["I"], CFG["E"], CFG["K"], CFG["n_shared"]
+        EE = E + ns
+        self.B = B
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        u8 = torch.uint8
+        self.gp = torch.empty((EE, I, D // 2), dtype=u8, device="cuda")
+        self.up = torch.empty((EE, I, D // 2), dtype=u8, device="cuda")
+        self.dp = torch.empty((EE, D, I // 2), dtype=u8, device="cuda")
+        self.gs = torch.empty((EE, I, D // 32), dtype=u8, device="cuda")
+        self.us = torch.empty((EE, I, D // 32), dtype=u8, device="cuda")
+        self.ds = torch.empty((EE, D, I // 32), dtype=u8, device="cuda")
+        for e in range(EE):
+            for p, s, shape in ((self.gp, self.gs, (I, D)), (self.up, self.us, (I, D)),
+                                (self.dp, self.ds, (D, I))):
+                w = torch.randn(shape, generator=g, device="cuda").mul_(0.02)
+                moe.pack_mxfp4_dev(w, p[e], s[e])
+        torch.cuda.synchronize()
+        self.host_tables = [[t[e].data_ptr() for e in range(EE)]
+                            for t in (self.gp, self.up, self.dp, self.gs, self.us, self.ds)]
+        self.tables = [torch.tensor(t, dtype=torch.int64, device="cuda")
+                       for t in self.host_tables]
+        self.inputs = []
+        for _ in range(N_INPUTS):
+            choice = torch.rand((B, E), generator=g, device="cuda")
+            vals, idx = torch.topk(choice, K, dim=1)  # moe_topk with mix = null
+            wt = (vals / vals.sum(dim=1, keepdim=True)).float()
+            x = torch.randn((B, D), generator=g, device="cuda").to(torch.bfloat16)
+            self.inputs.append((idx.int().contiguous(), wt.contiguous(), x))
+        self.out = torch.zeros((B, D), dtype=torch.float32, device="cuda")
+        self.ws = torch.empty(moe.layer_workspace_bytes(B, K, E, ns, D, I, CFG["fmt"]),
+                              dtype=torch.uint8, device="cuda")
+        # Experts each step touches (routed union + shared) -> algorithmic bytes.
+        self.experts_per_input = [len(set(i.flatten().tolist())) + ns
+                                  for (i, _, _) in self.inputs]
+
+    def step(self, moe, i):
+        idx, wt, x = self.inputs[i % N_INPUTS]
+        self.out.zero_()
+        moe.layer_dev(self.B, CFG["K"], CFG["E"], CFG["n_shared"], CFG["D"], CFG["I"], CFG["fmt"],
+                      idx, wt, x, self.tables, self.out, CFG["act"], CFG["act_a"], CFG["act_b"],
+                      self.ws)
+
+
+def graph_throughput(moe, torch, wl, steps, warmup):
+    """Tokens/s of `steps` steps replayed from a CUDA graph of N_INPUTS steps."""
+    for i in range(3):
+        wl.step(moe, i)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(N_INPUTS):
+                wl.step(moe, i)
+    torch.cuda.synchronize()
+    reps = max(1, steps // N_INPUTS)
+    for _ in range(max(1, warmup // N_INPUTS)):
+        graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    del graph
+    return wl.B * reps * N_INPUTS / (ms / 1e3), ms / (reps * N_INPUTS)
+
+
+# ------------------------------------------------------------ CPU baseline --
+def cpu_reference_rate(n_threads, rounds, expert_rows_per_call, host_experts=None):
+    """Reference moe_block (oracle/_ref) on host threads.
+
+    Each thread calls the reference moe_block on one token row through
+    `expert_rows_per_call` experts of config[1]; returns (tokens/s, seconds,
+    tokens).  A config[1] token is 9 expert rows (8 routed + shared)."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Oracle
+    ref = Oracle("reference")
+    D, I = CFG["D"], CFG["I"]
+    if host_experts is None:
+        rng = np.random.default_rng(7)
+        host_experts = []
+        for _ in range(min(expert_rows_per_call, 9)):
+            mats = [ref.pack_mxfp4((rng.standard_normal(s) * 0.02).astype(np.float32))
+                    for s in ((I, D), (I, D), (D, I))]
+            host_experts.append(mats)
+    ne = expert_rows_per_call
+    mats = [host_experts[e % len(host_experts)] for e in range(ne)]
+    g = [m[0][0] for m in mats]
+    u = [m[1][0] for m in mats]
+    d = [m[2][0] for m in mats]
+    gs = [m[0][1] for m in mats]
+    us = [m[1][1] for m in mats]
+    ds = [m[2][1] for m in mats]
+    xs = [np.random.default_rng(t).standard_normal((1, D)).astype(np.float32)
+          for t in range(n_threads)]
+
+    def work(t):
+        out = np.zeros((1, D), np.float32)
+        ref.moe_block(ne, D, I, 7, g, u, d, gs, us, ds, xs[t], np.zeros(ne, np.int32),
+                      np.ones(ne, np.int32), np.zeros(ne, np.int32), np.full(ne, 1.0 / 9,
+                                                                               np.float32),
+                      out, 1, 2, 4.0, 25.0)
+
+    def one_round():
+        ths = [threading.Thread(target=work, args=(t,)) for t in range(n_threads)]
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+
+    t0 = time.perf_counter()
+    for _ in range(rounds):
+        one_round()
+    sec = time.perf_counter() - t0
+    tokens = rounds * n_threads * ne / 9.0
+    return tokens / sec, sec, tokens
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    threads = host_threads()
+    # Each step: `threads` parallel reference calls of a few expert rows,
+    # sized so steps+warmup finish in about 90 s (0.05 s per expert row).
+    per_step_budget = 90.0 / max(args.steps + args.warmup, 1)
+    rows = max(1, int(per_step_budget / 0.05))
+    cpu_reference_rate(threads, max(args.warmup, 0) and 1, rows)  # warm-up (1 round)
+    rate, sec, tokens = cpu_reference_rate(threads, args.steps, rows)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1e3 / max(args.steps, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config[1] MXFP4 decode, hidden 7168, inter 2048, 256 experts "
+                               "top-8 + 1 shared, SiTU(4,25)", "batch": args.batch,
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": threads,
+                         "kind": "reference",
+                         "sample": f"per step {threads} threads x 1 token row through {rows} "
+                                   f"expert(s) of config[1] (9 expert rows = 1 token)"},
+        "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------------- ours --
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import build as mvbuild
+    mvbuild.build()
+    import mvllm_moe as moe
+
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    moe.init(local_rank)
+    B = args.batch
+    wl = Workload(moe, torch, B, seed=1234 + rank)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # warm-up
+    for i in range(max(args.warmup, 3)):
+        wl.step(moe, i)
+    barrier()
+
+    # timed region (eager launches; each step is ~1 ms of device work, so the
+    # host stays ahead and the phase events measure device time)
+    moe.profile_enable(True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        a.record()
+        for i in range(args.steps):
+            wl.step(moe, i)
+        b.record()
+        barrier()
+    ms = a.elapsed_time(b)
+    phases = moe.profile_read()
+    moe.profile_enable(False)
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    tokens = B * args.steps * world
+    value = tokens / (ms_max / 1e3)
+
+    # roofline of the expert kernels (decode_ffn phase 1 + phase 2)
+    e_steps = [wl.experts_per_input[i % N_INPUTS] for i in range(args.steps)]
+    alg_bytes = sum(e_steps) * EXPERT_BYTES / args.steps  # per step
+    k_ms = (phases["expert_phase1"][0] + phases["expert_phase2"][0]) / args.steps
+    achieved = alg_bytes / (k_ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    ratio = traffic_ratio()
+
+    # end to end: host buffers through the C ABI (copies inside the region)
+    idx_h, wt_h, x_h = [], [], []
+    for (idx, wt, x) in wl.inputs:
+        idx_h.append(idx.cpu().numpy())
+        wt_h.append(wt.cpu().numpy())
+        x_h.append(x.float().cpu().numpy())
+    out_h = np.zeros((B, CFG["D"]), np.float32)
+    for i in range(3):
+        moe.layer_host(B, CFG["K"], CFG["E"], CFG["n_shared"], CFG["D"], CFG["I"], CFG["fmt"],
+                       idx_h[i], wt_h[i], x_h[i], wl.host_tables, out_h, CFG["act"],
+                       CFG["act_a"], CFG["act_b"])
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(args.e2e_steps):
+        out_h[:] = 0
+        moe.layer_host(B, CFG["K"], CFG["E"], CFG["n_shared"], CFG["D"], CFG["I"], CFG["fmt"],
+                       idx_h[i % N_INPUTS], wt_h[i % N_INPUTS], x_h[i % N_INPUTS],
+                       wl.host_tables, out_h, CFG["act"], CFG["act_a"], CFG["act_b"])
+    e2e_s = time.perf_counter() - t0
+    t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = B * args.e2e_steps * world / float(t.item())
+    EE = CFG["E"] + CFG["n_shared"]
+    h2d = 6 * EE * 8 + 2 * B * CFG["K"] * 4 + 2 * B * CFG["D"] * 4
+    d2h = B * CFG["D"] * 4
+
+    # batch sweep (graph replays; same per-rank workload shape)
+    sweep = None
+    if not args.no_sweep:
+        sweep = {}
+        for bb in (1, 8, 32):
+            wb = wl if bb == B else None
+            if wb is None:
+                wb = Workload.__new__(Workload)
+                wb.__dict__.update({k: v for k, v in wl.__dict__.items()
+                                    if k not in ("inputs", "out", "ws", "B")})
+                wb.B = bb
+                g = torch.Generator(device="cuda").manual_seed(99 + bb)
+                wb.inputs = []
+                for _ in range(N_INPUTS):
+                    choice = torch.rand((bb, CFG["E"]), generator=g, device="cuda")
+                    vals, idx = torch.topk(choice, CFG["K"], dim=1)
+                    wt = (vals / vals.sum(dim=1, keepdim=True)).float()
+                    x = torch.randn((bb, CFG["D"]), generator=g, device="cuda").to(torch.bfloat16)
+                    wb.inputs.append((idx.int().contiguous(), wt.contiguous(), x))
+                wb.out = torch.zeros((bb, CFG["D"]), dtype=torch.float32, device="cuda")
+                wb.ws = torch.empty(moe.layer_workspace_bytes(bb, CFG["K"], CFG["E"],
+                                                              CFG["n_shared"], CFG["D"], CFG["I"],
+                                                              CFG["fmt"]),
+                                    dtype=torch.uint8, device="cuda")
+            tps, mstep = graph_throughput(moe, torch, wb, 320, 32)
+            sweep[f"B{bb}"] = {"tokens_per_s": tps * world, "ms_per_step": mstep}
+
+    # CPU baseline (rank 0, N=1 only): reference moe_block on host threads
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            host_experts = []
+            for e in [int(v) for v in wl.inputs[0][0][0].tolist()] + [CFG["E"]]:
+                host_experts.append([(wl.gp[e].cpu().numpy(), wl.gs[e].cpu().numpy()),
+                                     (wl.up[e].cpu().numpy(), wl.us[e].cpu().numpy()),
+                                     (wl.dp[e].cpu().numpy(), wl.ds[e].cpu().numpy())])
+            nth = min(host_threads(), 16)
+            rate, sec, toks = cpu_reference_rate(nth, 2, 9, host_experts)
+            cpu = {"value": rate, "unit": "tokens/s", "cores": nth, "kind": "reference",
+                   "sample": f"{int(toks)} token rows of config[1] (token 0's 8 routed + shared "
+                             f"experts), {nth} threads x 2 rounds, {sec:.1f} s wall"}
+        except Exception as ex:  # the reference build may be absent
+            cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
+                   "sample": f"unavailable: {ex}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "mxfp4 weights, f16 MMA operands, f32 accumulate", "data": "synthetic",
+            "config": {"workload": "config[1] MXFP4 decode MoE block: hidden 7168, inter 2048, "
+                                   "256 experts top-8 + 1 shared, SiTU(4,25), bf16 activations",
+                       "batch_per_gpu": B, "global_batch": B * world,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (6.0 GB of expert weights per rank, 16 "
+                             "distinct routings)"},
+            "roofline": {"bound": "hbm", "kernel": "decode_ffn (expert phase 1 + phase 2)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": None if ratio is None else ratio * alg_bytes,
+                         "algorithmic_bytes_per_step": alg_bytes,
+                         "kernel_ms_per_step": k_ms},
+            "phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
+            "gpu_launches": int(sum(v[1] for v in phases.values()) + args.steps),
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "api": "mvllm_moe_layer_host"},
+            "cpu_baseline": cpu,
+            "clocks": clk.report(),
+            "sweep": sweep,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,183 @@
+/*
+ * mvllm_moe.h -- C ABI of the B200 (sm_100a) routed-expert MoE block.
+ *
+ * Drop-in for micro-vllm's expert compute tier.  The reference reaches its
+ * expert GEMMs through mvllm::metal_ops::moe_block (src/gpu/metal_ops.hpp:
+ * 99-108) and, as a fallback, the coli_cuda tier (src/gpu/coli_cuda.hpp,
+ * whose only device hook is extern "C" coli_cuda_gemm_f32_dev,
+ * src/gpu/coli_cuda.cu:22-34).  This header replaces both with plain C entry
+ * points: plain pointers and sizes, int status codes, no C++ or torch types.
+ * include/mvllm_metal_ops.hpp puts the reference's exact C++ signature on
+ * top of mvllm_moe_block so reference call sites link unchanged.
+ *
+ * Error convention (as the reference tiers: "returns false on bad args; never
+ * throws", src/gpu/coli_cuda.hpp:13): every entry returns MVLLM_OK (0) or a
+ * positive code and never aborts.  MVLLM_ERR_INVALID is exactly the set of
+ * argument checks for which the reference moe_block returns false.
+ *
+ * Formats (src/quant/quant.hpp):
+ *   fmt 0  f32 row-major [O, I]
+ *   fmt 4  int4-g64: packed uint8 [O, ceil(I/2)] (low nibble = even column,
+ *          value = nibble - 8), f32 scales [O, ceil(I/64)]
+ *   fmt 7  MXFP4: packed e2m1 uint8 [O, ceil(I/2)] (bit 3 = sign), ue8m0
+ *          scales uint8 [O, ceil(I/32)], passed through the float* slots
+ * Gate/up weights are [Iinter, D]; down weights are [D, Iinter].
+ */
+#ifndef MVLLM_MOE_H
+#define MVLLM_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MVLLM_API __attribute__((visibility("default")))
+#else
+#define MVLLM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    MVLLM_OK = 0,
+    MVLLM_ERR_INVALID = 1,     /* argument rejected (reference: returns false) */
+    MVLLM_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed */
+    MVLLM_ERR_NOMEM = 3,       /* device or pinned allocation failed */
+    MVLLM_ERR_UNSUPPORTED = 4, /* shape/format the requested entry cannot run */
+    MVLLM_ERR_TIMEOUT = 5,     /* a bounded device-side wait ran out */
+    MVLLM_ERR_NOT_INIT = 6,    /* mvllm_moe_init has not succeeded */
+    MVLLM_ERR_DEVICE = 7,      /* a device-side bounds check rejected an index */
+    MVLLM_ERR_WORKSPACE = 8    /* caller workspace smaller than required */
+};
+
+/* metal_ops::Act (src/gpu/metal_ops.hpp:44); any other value behaves as SILU. */
+enum { MVLLM_ACT_SILU = 0, MVLLM_ACT_CLAMP_SWIGLU = 1, MVLLM_ACT_SITU = 2 };
+enum { MVLLM_FMT_F32 = 0, MVLLM_FMT_INT4_G64 = 4, MVLLM_FMT_MXFP4 = 7 };
+enum { MVLLM_DTYPE_F32 = 0, MVLLM_DTYPE_BF16 = 1 };
+
+/* ---- lifecycle: metal_ops::init/shutdown/available/backend_name
+ *      (src/gpu/metal_ops.hpp:15-18); coli_cuda::init (coli_cuda.hpp:25) ---- */
+MVLLM_API int mvllm_moe_init(int device);
+MVLLM_API void mvllm_moe_shutdown(void);
+MVLLM_API int mvllm_moe_available(void);
+MVLLM_API const char *mvllm_moe_backend_name(void); /* "cuda-sm100a" */
+MVLLM_API const char *mvllm_moe_last_error(void);   /* text of the last failure in this process */
+
+/* coli_cuda::group_stats (src/gpu/coli_cuda.hpp:35-36): calls, experts, rows
+ * and host-timed h2d / kernel / d2h milliseconds of the host-pointer entries. */
+MVLLM_API void mvllm_moe_stats(uint64_t *calls, uint64_t *experts, uint64_t *rows, double *h2d_ms,
+                     double *kernel_ms, double *d2h_ms);
+
+/* ---- the hot path, host pointers: metal_ops::moe_block
+ *      (src/gpu/metal_ops.hpp:104-108, body src/gpu/metal_ops.cpp:278-342) --
+ * For expert e in call order with nr[e] > 0: rows xg[xoff[e] .. +nr[e]) of D
+ * floats; hh = down(act(gate, up)); out[rows[base+r]] += rw[base+r] * hh[r]
+ * (skipped when the destination is < 0 or >= S with S > 0).  base advances by
+ * nr[e] for every expert with nr[e] > 0, also ones skipped for null weights.
+ * `out` is accumulated into.  qgs is ignored (group sizes are fixed by fmt).
+ * All pointers are caller-owned host memory, borrowed for the call.  Weight
+ * and scale arrays inside a range given to mvllm_moe_cache_register are read
+ * from the device copy; any other array is uploaded for this call only.
+ * Synchronous: returns after `out` holds the result. */
+MVLLM_API int mvllm_moe_block(int nb, int D, int Iinter, int fmt, int qgs, const void *const *g,
+                    const void *const *u, const void *const *d, const float *const *gs,
+                    const float *const *us, const float *const *ds, const float *xg,
+                    const int *xoff, const int *nr, const int *rows, const float *rw, float *out,
+                    int S, int act, float act_a, float act_b);
+
+/* ---- device-resident expert cache (mirrors an ExpertStore slot,
+ *      src/store/expert_store.hpp:71-175; the host pointer of a pinned slot
+ *      is the key, `generation` must change whenever the slot is refilled,
+ *      e.g. on the REPIN events of src/store/expert_store.cpp:306-316) ---- */
+MVLLM_API int mvllm_moe_cache_register(const void *host, size_t bytes, uint64_t generation);
+MVLLM_API int mvllm_moe_cache_unregister(const void *host);
+MVLLM_API void mvllm_moe_cache_clear(void);
+MVLLM_API size_t mvllm_moe_cache_bytes(void);
+
+/* ---- device-pointer entries (stream-ordered, no host sync, no allocation:
+ *      the caller passes a workspace of at least the *_workspace size) ---- */
+
+/* moe_block on device memory.  g,u,d,gs,us,ds are DEVICE arrays of nb device
+ * pointers; xoff, nr [nb], rows, rw [rows_cap] and x (rows of D elements,
+ * dtype MVLLM_DTYPE_*) are device arrays; out is device f32 [S, D].  S must be
+ * > 0.  rows_cap bounds sum(max(nr,0)); x_rows bounds max(xoff+nr) (the rows
+ * of x that may be read).  Same semantics as mvllm_moe_block. */
+MVLLM_API size_t mvllm_moe_block_dev_workspace(int nb, int D, int Iinter, int fmt, int rows_cap, int x_rows,
+                                     int S);
+MVLLM_API int mvllm_moe_block_dev(void *stream, int nb, int D, int Iinter, int fmt, const void *const *g,
+                        const void *const *u, const void *const *d, const void *const *gs,
+                        const void *const *us, const void *const *ds, const void *x, int x_dtype,
+                        int x_rows, const int *xoff, const int *nr, const int *rows,
+                        const float *rw, float *out, int S, int act, float act_a, float act_b,
+                        int rows_cap, void *workspace, size_t workspace_bytes);
+
+/* Token permutation of the callers (src/model/glm53.cpp:1958-1971,
+ * src/model/kimi_k3.cpp:2036-2050): from top-k ids idx[T,K] and weights
+ * wt[T,K] (device), for each expert in ascending id the tokens c ascending
+ * whose wsum = sum_t wt[c,t]*[idx[c,t]==e] (t ascending, f32) is non-zero.
+ * Writes nr[E+n_shared], xoff[E+n_shared] (segment starts), rows[R] (token
+ * ids), rw[R] (wsums) and tok_pos[T, K+n_shared] (segment position of each
+ * token's entry, -1 where none).  n_shared = 1 appends an always-on expert
+ * (id E, weight 1 for every token) after the routed ones.  Ids outside
+ * [0, E) are ignored (the reference union drops ids < 0).  *n_rows (device
+ * int) receives R. */
+MVLLM_API size_t mvllm_moe_permute_workspace(int T, int K, int E, int n_shared);
+MVLLM_API int mvllm_moe_permute_dev(void *stream, const int *idx, const float *wt, int T, int K, int E,
+                          int n_shared, int *nr, int *xoff, int *rows, float *rw, int *tok_pos,
+                          int *n_rows, void *workspace, size_t workspace_bytes);
+
+/* A whole routed MoE layer on device, as moe_layer_n's routed part
+ * (src/model/glm53.cpp:1936-1994, src/model/kimi_k3.cpp:2024-2075) plus an
+ * optional always-on shared expert: permute -> expert FFN -> ordered combine
+ * out[c] += sum over the token's experts in ascending id of wsum * hh.
+ * x is device [T, D] (dtype MVLLM_DTYPE_*); g..ds are device arrays of
+ * E + n_shared device pointers (the shared expert last); out is device f32
+ * [T, D], accumulated. */
+MVLLM_API size_t mvllm_moe_layer_workspace(int T, int K, int E, int n_shared, int D, int Iinter, int fmt);
+MVLLM_API int mvllm_moe_layer_dev(void *stream, int T, int K, int E, int n_shared, int D, int Iinter,
+                        int fmt, const int *idx, const float *wt, const void *x, int x_dtype,
+                        const void *const *g, const void *const *u, const void *const *d,
+                        const void *const *gs, const void *const *us, const void *const *ds,
+                        float *out, int act, float act_a, float act_b, void *workspace,
+                        size_t workspace_bytes);
+
+/* The same layer with HOST buffers (x f32 [T,D], idx/wt [T,K], out f32
+ * [T,D] accumulated) and weights already resident on the device: the
+ * end-to-end entry.  Copies in, runs, copies out, synchronises. */
+MVLLM_API int mvllm_moe_layer_host(int T, int K, int E, int n_shared, int D, int Iinter, int fmt,
+                         const int *idx, const float *wt, const float *x, const void *const *g,
+                         const void *const *u, const void *const *d, const void *const *gs,
+                         const void *const *us, const void *const *ds, float *out, int act,
+                         float act_a, float act_b);
+
+/* ---- weight preparation on the device, bit-identical to
+ *      quant::quantize_int4_g64 (src/quant/quant.cpp:170-201) and
+ *      quant::pack_mxfp4 (src/quant/quant.cpp:270-296).  w is device f32
+ *      [O, I]; outputs as the formats above. ---- */
+MVLLM_API int mvllm_quantize_int4_g64_dev(void *stream, const float *w, int O, int I, uint8_t *packed,
+                                float *scales);
+MVLLM_API int mvllm_pack_mxfp4_dev(void *stream, const float *w, int O, int I, uint8_t *packed,
+                         uint8_t *scales);
+
+/* Dequantised GEMM y[S,O] = x[S,I] . W[O,I]^T on device (f32 in/out): the
+ * role of coli_cuda::matmul / matmul_mxfp4 (src/gpu/coli_cuda.hpp:58-61) and
+ * quant::matmul_* (src/quant/quant.hpp:53-70). */
+MVLLM_API int mvllm_matmul_dev(void *stream, int fmt, float *y, const float *x, const void *w,
+                     const void *scales, int S, int I, int O);
+
+/* Per-phase device time of the device-pointer entries, from CUDA events
+ * recorded on the launch stream after each phase while enabled (the role of
+ * the reference's AccTimer accumulators, src/model/glm53.cpp:39-46, on the
+ * device).  Phases: 0 permute, 1 gather, 2 plan, 3 expert phase 1 (gate/up
+ * + activation), 4 expert phase 2 (down), 5 combine.  enable(1) starts a new
+ * window; read() synchronises, fills ms[]/launches[] (n entries) and returns
+ * the number of phases. */
+MVLLM_API void mvllm_moe_profile_enable(int on);
+MVLLM_API int mvllm_moe_profile_read(double *ms, long long *launches, int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MVLLM_MOE_H */

@@ -1,0 +1,626 @@
+// aux_kernels.cuh -- everything around the expert GEMMs: planning, operand
+// staging, token permutation, ordered combine, the generic (any shape, any
+// format) expert kernels and the device-side weight packers.
+#pragma once
+
+#include "common.cuh"
+
+namespace mvb {
+
+// ---------------------------------------------------------------------------
+// Block-wide exclusive scan of one int per thread (blockDim.x multiple of 32,
+// <= 1024).  Returns the exclusive prefix; *total gets the block sum.
+__device__ __forceinline__ int block_exclusive_scan(int v, int *warp_sums, int *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o)
+            x += y;
+    }
+    if (lane == 31)
+        warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int s = lane < nwarps ? warp_sums[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o)
+                s += y;
+        }
+        if (lane < nwarps)
+            warp_sums[lane] = s; // inclusive
+    }
+    __syncthreads();
+    const int before = (warp > 0 ? warp_sums[warp - 1] : 0) + x - v;
+    *total = warp_sums[nwarps - 1];
+    __syncthreads();
+    return before;
+}
+
+// ---------------------------------------------------------------------------
+// Plan (one CTA): the reference's per-expert bookkeeping of cpu_moe_block
+// (src/gpu/metal_ops.cpp:285-300): base advances by nr for every expert with
+// nr > 0; an expert runs only when its weight (and, for fmt 4/7, scale)
+// pointers are all non-null.  Emits base[], cnt[] (rows that run, else 0)
+// and the item prefix arrays of both phases (blocks x token chunks).
+struct PlanArgs {
+    int nb, fmt;
+    const int *nr;
+    const void *const *g, *const *u, *const *d, *const *gs, *const *us, *const *ds;
+    int chunk1, blocks1; // phase 1 token chunk and row blocks per expert
+    int chunk2, blocks2;
+    int *base, *cnt, *off1, *off2, *total_rows;
+    const int *xoff; // operand rows must satisfy 0 <= xoff[e], xoff[e]+nr[e] <= x_rows
+    int x_rows;
+    int align16; // fast path: every weight and scale pointer must be 16-byte aligned
+    int *err;
+};
+
+__global__ void plan_kernel(const PlanArgs a) {
+    __shared__ int warp_sums[32];
+    __shared__ int carry[3];
+    if (threadIdx.x == 0)
+        carry[0] = carry[1] = carry[2] = 0;
+    __syncthreads();
+    for (int e0 = 0; e0 < a.nb; e0 += blockDim.x) {
+        const int e = e0 + threadIdx.x;
+        int n = 0, c = 0, i1 = 0, i2 = 0;
+        if (e < a.nb) {
+            n = max(a.nr[e], 0);
+            bool ok = n > 0 && a.g[e] && a.u[e] && a.d[e];
+            if (a.fmt != MVLLM_FMT_F32)
+                ok = ok && a.gs[e] && a.us[e] && a.ds[e];
+            if (ok && a.align16) {
+                const uintptr_t bits = reinterpret_cast<uintptr_t>(a.g[e]) |
+                                       reinterpret_cast<uintptr_t>(a.u[e]) |
+                                       reinterpret_cast<uintptr_t>(a.d[e]) |
+                                       reinterpret_cast<uintptr_t>(a.gs[e]) |
+                                       reinterpret_cast<uintptr_t>(a.us[e]) |
+                                       reinterpret_cast<uintptr_t>(a.ds[e]);
+                if (bits & 15u) {
+                    set_error(a.err, MVLLM_ERR_DEVICE); // would break the bulk copies: skip
+                    ok = false;
+                }
+            }
+            if (ok && (a.xoff[e] < 0 || a.xoff[e] + n > a.x_rows)) {
+                set_error(a.err, MVLLM_ERR_DEVICE); // out-of-range operand rows: skip
+                ok = false;
+            }
+            c = ok ? n : 0;
+            i1 = c ? a.blocks1 * ((c + a.chunk1 - 1) / a.chunk1) : 0;
+            i2 = c ? a.blocks2 * ((c + a.chunk2 - 1) / a.chunk2) : 0;
+        }
+        int tot;
+        const int b = block_exclusive_scan(n, warp_sums, &tot);
+        int t1;
+        const int o1 = block_exclusive_scan(i1, warp_sums, &t1);
+        int t2;
+        const int o2 = block_exclusive_scan(i2, warp_sums, &t2);
+        if (e < a.nb) {
+            a.base[e] = carry[0] + b;
+            a.cnt[e] = c;
+            a.off1[e] = carry[1] + o1;
+            a.off2[e] = carry[2] + o2;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            carry[0] += tot;
+            carry[1] += t1;
+            carry[2] += t2;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        a.off1[a.nb] = carry[1];
+        a.off2[a.nb] = carry[2];
+        *a.total_rows = carry[0];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Operand staging: rows of x (f32 or bf16, row length D) into f16 rows in the
+// column order of the format (stage_pos), or into plain f32 rows.  With
+// `index`, output row r reads input row index[r] (the permutation gather).
+template <typename TIn, typename TOut>
+__global__ void stage_rows_kernel(const TIn *__restrict__ x, const int *__restrict__ index,
+                                  const int *__restrict__ nrows_dev, int nrows_host, int D,
+                                  int fmt, TOut *__restrict__ out) {
+    const int nrows = nrows_dev ? *nrows_dev : nrows_host;
+    for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
+        const int src = index ? index[r] : r;
+        const TIn *xr = x + static_cast<size_t>(src) * D;
+        TOut *orow = out + static_cast<size_t>(r) * D;
+        for (int k = threadIdx.x; k < D; k += blockDim.x) {
+            float v;
+            if constexpr (sizeof(TIn) == 4)
+                v = xr[k];
+            else
+                v = __bfloat162float(xr[k]);
+            if constexpr (sizeof(TOut) == 4)
+                orow[k] = v;
+            else
+                orow[stage_pos(k, fmt)] = __float2half_rn(v);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Token permutation (caller gather order, src/model/glm53.cpp:1958-1971).
+// Step 1, thread per token: for each distinct valid id among the token's K
+// entries (first occurrence), wsum = sum_t wt[c,t]*[idx[c,t]==e] in t order
+// from 0.f; a non-zero wsum sets membership bit (e, c).
+__global__ void permute_member_kernel(const int *__restrict__ idx, const float *__restrict__ wt,
+                                      int T, int K, int E, int n_shared, int words,
+                                      uint32_t *__restrict__ bitmap, float *__restrict__ wsum_out,
+                                      int *__restrict__ tok_pos) {
+    const int KK = K + n_shared;
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < T; c += gridDim.x * blockDim.x) {
+        const int *ic = idx + static_cast<size_t>(c) * K;
+        const float *wc = wt + static_cast<size_t>(c) * K;
+        for (int t = 0; t < K; ++t) {
+            const int e = ic[t];
+            tok_pos[static_cast<size_t>(c) * KK + t] = -1;
+            if (e < 0 || e >= E)
+                continue;
+            bool dup = false;
+            for (int t2 = 0; t2 < t; ++t2)
+                dup |= (ic[t2] == e);
+            if (dup)
+                continue;
+            float wsum = 0.f;
+            for (int t2 = 0; t2 < K; ++t2)
+                if (ic[t2] == e)
+                    wsum = __fadd_rn(wsum, wc[t2]);
+            if (wsum == 0.f)
+                continue;
+            wsum_out[static_cast<size_t>(c) * KK + t] = wsum;
+            tok_pos[static_cast<size_t>(c) * KK + t] = -2; // placed in step 2
+            atomicOr(&bitmap[static_cast<size_t>(e) * words + (c >> 5)], 1u << (c & 31));
+        }
+        if (n_shared) {
+            wsum_out[static_cast<size_t>(c) * KK + K] = 1.f;
+            tok_pos[static_cast<size_t>(c) * KK + K] = -2;
+            atomicOr(&bitmap[static_cast<size_t>(E) * words + (c >> 5)], 1u << (c & 31));
+        }
+    }
+}
+
+// Step 2 (one CTA): per expert a warp counts its members (popc), a block scan
+// gives the segment starts in ascending expert id, then each warp walks its
+// bitmap row 32 words at a time, ballot-free: a warp prefix sum of the word
+// popcounts plus popc(word & lanemask) ranks every token, ascending.
+__global__ void permute_segments_kernel(const int *__restrict__ idx, int T, int K, int E,
+                                        int n_shared, int words,
+                                        const uint32_t *__restrict__ bitmap,
+                                        const float *__restrict__ wsum_in, int *__restrict__ nr,
+                                        int *__restrict__ xoff, int *__restrict__ rows,
+                                        float *__restrict__ rw, int *__restrict__ tok_pos,
+                                        int *__restrict__ n_rows) {
+    __shared__ int warp_sums[32];
+    __shared__ int carry;
+    const int EE = E + n_shared, KK = K + n_shared;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int e = warp; e < EE; e += nw) {
+        int cnt = 0;
+        for (int j = lane; j < words; j += 32)
+            cnt += __popc(bitmap[static_cast<size_t>(e) * words + j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+        if (lane == 0)
+            nr[e] = cnt;
+    }
+    if (threadIdx.x == 0)
+        carry = 0;
+    __syncthreads();
+    for (int e0 = 0; e0 < EE; e0 += blockDim.x) {
+        const int e = e0 + threadIdx.x;
+        const int v = e < EE ? nr[e] : 0;
+        int tot;
+        const int ex = block_exclusive_scan(v, warp_sums, &tot);
+        if (e < EE)
+            xoff[e] = carry + ex;
+        __syncthreads();
+        if (threadIdx.x == 0)
+            carry += tot;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0)
+        *n_rows = carry;
+    __syncthreads();
+    for (int e = warp; e < EE; e += nw) {
+        int run = xoff[e];
+        for (int j0 = 0; j0 < words; j0 += 32) {
+            const int j = j0 + lane;
+            uint32_t m = j < words ? bitmap[static_cast<size_t>(e) * words + j] : 0u;
+            const int pc = __popc(m);
+            int incl = pc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o)
+                    incl += y;
+            }
+            int pos = run + incl - pc;
+            while (m) {
+                const int b = __ffs(m) - 1;
+                m &= m - 1;
+                const int c = 32 * j + b;
+                int slot = K; // the shared expert's slot
+                if (e < E) {
+                    for (int t = 0; t < K; ++t)
+                        if (idx[static_cast<size_t>(c) * K + t] == e) {
+                            slot = t;
+                            break;
+                        }
+                }
+                rows[pos] = c;
+                rw[pos] = wsum_in[static_cast<size_t>(c) * KK + slot];
+                tok_pos[static_cast<size_t>(c) * KK + slot] = pos;
+                ++pos;
+            }
+            run += __shfl_sync(0xffffffffu, incl, 31);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Ordered combine, layer form: out[c] += wsum*y over the token's segment
+// positions in ascending order (= ascending expert id), one multiply and one
+// add per term as in glm53.cpp:1978-1984 (no fused multiply-add).
+__global__ void combine_tokens_kernel(float *__restrict__ out, const float *__restrict__ y,
+                                      const float *__restrict__ rw,
+                                      const int *__restrict__ tok_pos, int T, int KK, int D) {
+    for (int c = blockIdx.y; c < T; c += gridDim.y) {
+    int pos[17];
+    int n = 0;
+    for (int t = 0; t < KK && n < 17; ++t) {
+        const int p = tok_pos[static_cast<size_t>(c) * KK + t];
+        if (p >= 0) {
+            int j = n++;
+            while (j > 0 && pos[j - 1] > p) {
+                pos[j] = pos[j - 1];
+                --j;
+            }
+            pos[j] = p;
+        }
+    }
+    for (int col = (blockIdx.x * blockDim.x + threadIdx.x) * 4; col < D;
+         col += gridDim.x * blockDim.x * 4) {
+        float4 acc = *reinterpret_cast<const float4 *>(out + static_cast<size_t>(c) * D + col);
+        for (int j = 0; j < n; ++j) {
+            const float w = rw[pos[j]];
+            const float4 v =
+                *reinterpret_cast<const float4 *>(y + static_cast<size_t>(pos[j]) * D + col);
+            acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+        }
+        *reinterpret_cast<float4 *>(out + static_cast<size_t>(c) * D + col) = acc;
+    }
+    }
+}
+
+// Ordered combine, moe_block form: CSR of destination rows (row ids ascending
+// within each destination), scatter order of metal_ops.cpp:328-339.
+__global__ void combine_csr_kernel(float *__restrict__ out, const float *__restrict__ y,
+                                   const float *__restrict__ rw, const int *__restrict__ off,
+                                   const int *__restrict__ ids, int S, int D) {
+    for (int s = blockIdx.y; s < S; s += gridDim.y) {
+    const int j0 = off[s], j1 = off[s + 1];
+    if (j0 == j1)
+        continue;
+    for (int col = blockIdx.x * blockDim.x + threadIdx.x; col < D; col += gridDim.x * blockDim.x) {
+        float acc = out[static_cast<size_t>(s) * D + col];
+        for (int j = j0; j < j1; ++j) {
+            const int r = ids[j];
+            acc = __fadd_rn(acc, __fmul_rn(rw[r], y[static_cast<size_t>(r) * D + col]));
+        }
+        out[static_cast<size_t>(s) * D + col] = acc;
+    }
+    }
+}
+
+// Device CSR builder for the device-pointer moe_block (one CTA): rows of
+// experts that ran (found through base/cnt) with 0 <= dest < S are bucketed
+// by destination; buckets are then sorted so row ids ascend.
+__global__ void build_csr_kernel(const int *__restrict__ rows, const int *__restrict__ base,
+                                 const int *__restrict__ cnt, int nb,
+                                 const int *__restrict__ total_rows, int S,
+                                 int *__restrict__ hist, int *__restrict__ off,
+                                 int *__restrict__ ids) {
+    __shared__ int warp_sums[32];
+    __shared__ int carry;
+    const int R = *total_rows;
+    for (int s = threadIdx.x; s < S; s += blockDim.x)
+        hist[s] = 0;
+    __syncthreads();
+    auto valid_dest = [&](int r) -> int {
+        // owner expert: largest e with base[e] <= r (it has rows, see plan)
+        int lo = 0, hi = nb;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (base[mid] <= r)
+                lo = mid;
+            else
+                hi = mid;
+        }
+        if (cnt[lo] == 0)
+            return -1;
+        const int dest = rows[r];
+        return (dest >= 0 && dest < S) ? dest : -1;
+    };
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+        const int dest = valid_dest(r);
+        if (dest >= 0)
+            atomicAdd(&hist[dest], 1);
+    }
+    if (threadIdx.x == 0)
+        carry = 0;
+    __syncthreads();
+    for (int s0 = 0; s0 < S; s0 += blockDim.x) {
+        const int s = s0 + threadIdx.x;
+        const int v = s < S ? hist[s] : 0;
+        int tot;
+        const int ex = block_exclusive_scan(v, warp_sums, &tot);
+        if (s < S) {
+            off[s] = carry + ex;
+            hist[s] = carry + ex; // becomes the fill cursor
+        }
+        __syncthreads();
+        if (threadIdx.x == 0)
+            carry += tot;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0)
+        off[S] = carry;
+    __syncthreads();
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+        const int dest = valid_dest(r);
+        if (dest >= 0)
+            ids[atomicAdd(&hist[dest], 1)] = r;
+    }
+    __syncthreads();
+    for (int s = threadIdx.x; s < S; s += blockDim.x) {
+        const int j0 = off[s], j1 = off[s + 1];
+        for (int j = j0 + 1; j < j1; ++j) {
+            const int v = ids[j];
+            int k = j;
+            while (k > j0 && ids[k - 1] > v) {
+                ids[k] = ids[k - 1];
+                --k;
+            }
+            ids[k] = v;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Generic expert kernels: any D / Iinter, any of fmt 0/4/7, f32 arithmetic.
+// Dequantised element (o, k) of a weight matrix with row length K
+// (src/quant/quant.cpp:203-228 and :298-321).
+__device__ __forceinline__ float deq_elem(const void *w, const void *s, int fmt, int o, int k,
+                                          int K) {
+    if (fmt == MVLLM_FMT_F32)
+        return static_cast<const float *>(w)[static_cast<size_t>(o) * K + k];
+    const uint8_t b = static_cast<const uint8_t *>(w)[static_cast<size_t>(o) * ((K + 1) / 2) +
+                                                      (k >> 1)];
+    const uint32_t nib = (k & 1) ? (b >> 4) : (b & 15u);
+    if (fmt == MVLLM_FMT_INT4_G64) {
+        const float sc = static_cast<const float *>(s)[static_cast<size_t>(o) * ((K + 63) / 64) +
+                                                       (k >> 6)];
+        return static_cast<float>(static_cast<int>(nib) - 8) * sc;
+    }
+    const uint8_t e = static_cast<const uint8_t *>(s)[static_cast<size_t>(o) * ((K + 31) / 32) +
+                                                      (k >> 5)];
+    const float mag = (nib & 7u) == 0   ? 0.f
+                      : (nib & 7u) == 1 ? 0.5f
+                      : (nib & 7u) == 2 ? 1.f
+                      : (nib & 7u) == 3 ? 1.5f
+                      : (nib & 7u) == 4 ? 2.f
+                      : (nib & 7u) == 5 ? 3.f
+                      : (nib & 7u) == 6 ? 4.f
+                                        : 6.f;
+    return ((nib & 8u) ? -mag : mag) * ue8m0_to_f32(e);
+}
+
+struct GenericArgs {
+    const void *const *w0, *const *w1, *const *s0, *const *s1;
+    const int *xrow, *orow, *cnt, *item_off;
+    int nb, fmt;
+    const float *x; // f32 rows of length K
+    int K, O;       // phase 1: K = D, O = Iinter; phase 2: K = Iinter, O = D
+    float *out;     // phase 1: h f32 [R, Iinter]; phase 2: y f32 [R, D]
+    int act;
+    float act_a, act_b;
+};
+
+// Item = (expert, 8 output rows); warp w computes row o = 8*blk + w for all
+// the expert's tokens, 4 tokens at a time, lanes striding over k.
+template <int PHASE> __global__ void __launch_bounds__(256) generic_ffn_kernel(const GenericArgs a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int total = a.item_off[a.nb];
+    for (int i = blockIdx.x; i < total; i += gridDim.x) {
+        const int e = find_owner(a.item_off, a.nb, i);
+        const int o = (i - a.item_off[e]) * 8 + warp;
+        if (o >= a.O)
+            continue;
+        const int ce = a.cnt[e];
+        const float *xe = a.x + static_cast<size_t>(a.xrow[e]) * a.K;
+        const size_t ob = static_cast<size_t>(a.orow[e]);
+        for (int r0 = 0; r0 < ce; r0 += 4) {
+            const int nrr = min(4, ce - r0);
+            float g4[4] = {0.f, 0.f, 0.f, 0.f}, u4[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int k = lane; k < a.K; k += 32) {
+                const float wg = deq_elem(a.w0[e], a.s0 ? a.s0[e] : nullptr, a.fmt, o, k, a.K);
+                float wu = 0.f;
+                if (PHASE == 1)
+                    wu = deq_elem(a.w1[e], a.s1 ? a.s1[e] : nullptr, a.fmt, o, k, a.K);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (j < nrr) {
+                        const float xv = xe[static_cast<size_t>(r0 + j) * a.K + k];
+                        g4[j] = fmaf(xv, wg, g4[j]);
+                        if (PHASE == 1)
+                            u4[j] = fmaf(xv, wu, u4[j]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+#pragma unroll
+                for (int s = 16; s > 0; s >>= 1) {
+                    g4[j] += __shfl_xor_sync(0xffffffffu, g4[j], s);
+                    if (PHASE == 1)
+                        u4[j] += __shfl_xor_sync(0xffffffffu, u4[j], s);
+                }
+            }
+            if (lane == 0) {
+                for (int j = 0; j < nrr; ++j) {
+                    const float v =
+                        (PHASE == 1) ? apply_act(g4[j], u4[j], a.act, a.act_a, a.act_b) : g4[j];
+                    a.out[(ob + r0 + j) * a.O + o] = v;
+                }
+            }
+        }
+    }
+}
+
+// Generic dequantised GEMM y[S,O] = x[S,I] . W[O,I]^T (warp per output row).
+__global__ void __launch_bounds__(256) matmul_generic_kernel(int fmt, float *y, const float *x,
+                                                             const void *w, const void *sc,
+                                                             int S, int I, int O) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int o = blockIdx.x * 8 + warp;
+    if (o >= O)
+        return;
+    for (int s = 0; s < S; ++s) {
+        float acc = 0.f;
+        for (int k = lane; k < I; k += 32)
+            acc = fmaf(x[static_cast<size_t>(s) * I + k], deq_elem(w, sc, fmt, o, k, I), acc);
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1)
+            acc += __shfl_xor_sync(0xffffffffu, acc, m);
+        if (lane == 0)
+            y[static_cast<size_t>(s) * O + o] = acc;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Device weight packers, one thread per (row, group); same arithmetic as the
+// reference (IEEE division, roundf = std::round, ties to the lower e2m1 code).
+__global__ void quantize_int4_g64_kernel(const float *__restrict__ w, int O, int I,
+                                         uint8_t *__restrict__ packed, float *__restrict__ scales) {
+    const int ng = (I + 63) / 64, stride = (I + 1) / 2;
+    const size_t total = static_cast<size_t>(O) * ng;
+    for (size_t id = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; id < total;
+         id += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int o = static_cast<int>(id / ng), gidx = static_cast<int>(id % ng);
+        const int i0 = gidx * 64, i1 = min(i0 + 64, I);
+        const float *row = w + static_cast<size_t>(o) * I;
+        float amax = 0.f;
+        for (int i = i0; i < i1; ++i) {
+            const float a = fabsf(row[i]);
+            if (a > amax)
+                amax = a;
+        }
+        float scale = __fdiv_rn(amax, 7.f);
+        if (scale < 1e-8f)
+            scale = 1e-8f;
+        scales[static_cast<size_t>(o) * ng + gidx] = scale;
+        const float inv = __fdiv_rn(1.f, scale);
+        uint8_t *prow = packed + static_cast<size_t>(o) * stride;
+        for (int i = i0; i < i1; i += 2) {
+            int q0 = static_cast<int>(roundf(__fmul_rn(row[i], inv)));
+            q0 = min(max(q0, -8), 7);
+            int q1 = 0;
+            uint32_t hi = 0;
+            if (i + 1 < i1) {
+                q1 = static_cast<int>(roundf(__fmul_rn(row[i + 1], inv)));
+                q1 = min(max(q1, -8), 7);
+                hi = static_cast<uint32_t>(q1 + 8);
+            }
+            prow[i >> 1] = static_cast<uint8_t>(static_cast<uint32_t>(q0 + 8) | (hi << 4));
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t ue8m0_cover_dev(float need) {
+    // src/quant/quant.cpp:47-77
+    if (!(need > 0.f))
+        return 0;
+    if (!isfinite(need))
+        return 255;
+    const uint32_t bits = __float_as_uint(need);
+    const int exp_field = static_cast<int>((bits >> 23) & 0xffu);
+    const uint32_t frac = bits & 0x7fffffu;
+    int e;
+    if (exp_field == 0)
+        e = 1;
+    else if (exp_field == 255)
+        e = 255;
+    else
+        e = (frac == 0) ? exp_field : exp_field + 1;
+    e = min(max(e, 0), 255);
+    while (e < 255 && ue8m0_to_f32(static_cast<uint32_t>(e)) < need)
+        ++e;
+    while (e > 0 && ue8m0_to_f32(static_cast<uint32_t>(e - 1)) >= need)
+        --e;
+    return static_cast<uint32_t>(e);
+}
+
+__device__ __forceinline__ uint32_t closest_mx4_dev(float w, float scale) {
+    // src/quant/quant.cpp:79-96
+    const float lut[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+    float target = 0.f;
+    if (scale > 0.f && isfinite(scale))
+        target = __fdiv_rn(w, scale);
+    const float a = fabsf(target);
+    int best = 0;
+    float best_d = fabsf(lut[0] - a);
+#pragma unroll
+    for (int k = 1; k < 8; ++k) {
+        const float d = fabsf(__fsub_rn(lut[k], a));
+        if (d < best_d) {
+            best_d = d;
+            best = k;
+        }
+    }
+    if (signbit(w))
+        best |= 8;
+    return static_cast<uint32_t>(best);
+}
+
+__global__ void pack_mxfp4_kernel(const float *__restrict__ w, int O, int I,
+                                  uint8_t *__restrict__ packed, uint8_t *__restrict__ scales) {
+    const int ng = (I + 31) / 32, stride = (I + 1) / 2;
+    const size_t total = static_cast<size_t>(O) * ng;
+    for (size_t id = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; id < total;
+         id += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int o = static_cast<int>(id / ng), gidx = static_cast<int>(id % ng);
+        const int i0 = gidx * 32, i1 = min(i0 + 32, I);
+        const float *row = w + static_cast<size_t>(o) * I;
+        float amax = 0.f;
+        for (int i = i0; i < i1; ++i) {
+            const float a = fabsf(row[i]);
+            if (a > amax)
+                amax = a;
+        }
+        const uint32_t e = ue8m0_cover_dev(__fdiv_rn(amax, 6.f));
+        scales[static_cast<size_t>(o) * ng + gidx] = static_cast<uint8_t>(e);
+        const float scale = ue8m0_to_f32(e);
+        uint8_t *prow = packed + static_cast<size_t>(o) * stride;
+        for (int i = i0; i < i1; i += 2) {
+            const uint32_t lo = closest_mx4_dev(row[i], scale);
+            const uint32_t hi = (i + 1 < i1) ? closest_mx4_dev(row[i + 1], scale) : 0u;
+            prow[i >> 1] = static_cast<uint8_t>(lo | (hi << 4));
+        }
+    }
+}
+
+} // namespace mvb

@@ -1,0 +1,1182 @@
+// mvllm_moe.cu -- host side of the sm_100a MoE block: the C ABI of
+// include/mvllm_moe.h, the device-resident expert cache, and the launch
+// sequence plan -> operand staging -> expert phase 1 -> phase 2 -> ordered
+// combine.  No CPU fallback: every entry either runs the CUDA path or
+// returns an error code.
+#include "aux_kernels.cuh"
+#include "decode_ffn.cuh"
+
+#include <algorithm>
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+using namespace mvb;
+
+namespace {
+
+// ------------------------------------------------------------------ context --
+struct CacheEntry {
+    void *dev = nullptr;
+    size_t bytes = 0;
+    uint64_t generation = 0;
+};
+
+struct DevBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+};
+
+struct Context {
+    std::mutex mu;
+    bool inited = false;
+    int device = -1;
+    int sms = 0;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev[4] = {};
+    DevBuf ws;        // workspace of the host-pointer entries
+    DevBuf transient; // per-call copies of unregistered weight arrays
+    void *pinned = nullptr;
+    size_t pinned_bytes = 0;
+    std::map<uintptr_t, CacheEntry> cache; // host start -> device copy
+    size_t cache_bytes = 0;
+    uint64_t calls = 0, experts = 0, rows = 0;
+    double h2d_ms = 0, kernel_ms = 0, d2h_ms = 0;
+};
+
+Context &ctx() {
+    static Context c;
+    return c;
+}
+
+thread_local std::string g_last_error;
+
+// ------------------------------------------------------------- profiling --
+// Optional per-phase device timing of the device-pointer entries: a CUDA
+// event is recorded on the launch stream after each phase; durations are the
+// elapsed times between consecutive events of one call.
+enum ProfPhase { kPhStart = -1, kPhPermute = 0, kPhGather, kPhPlan, kPhExpert1, kPhExpert2,
+                 kPhCombine, kPhCount };
+struct Prof {
+    std::mutex mu;
+    bool on = false;
+    std::vector<cudaEvent_t> pool;
+    std::vector<std::pair<cudaEvent_t, int>> marks;
+    size_t used = 0;
+};
+Prof &prof() {
+    static Prof p;
+    return p;
+}
+void prof_mark(cudaStream_t st, int phase) {
+    Prof &p = prof();
+    if (!p.on)
+        return;
+    std::lock_guard<std::mutex> lk(p.mu);
+    if (p.used == p.pool.size()) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess)
+            return;
+        p.pool.push_back(e);
+    }
+    cudaEvent_t e = p.pool[p.used++];
+    cudaEventRecord(e, st);
+    p.marks.push_back({e, phase});
+}
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                          \
+    do {                                                                                        \
+        cudaError_t e_ = (expr);                                                                \
+        if (e_ != cudaSuccess)                                                                  \
+            return fail(MVLLM_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_));        \
+    } while (0)
+
+int ensure_dev(DevBuf &b, size_t bytes) {
+    if (b.bytes >= bytes)
+        return MVLLM_OK;
+    if (b.p)
+        cudaFree(b.p);
+    b.p = nullptr;
+    b.bytes = 0;
+    const size_t want = std::max(bytes, size_t(1) << 20);
+    if (cudaMalloc(&b.p, want) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(MVLLM_ERR_NOMEM, "cudaMalloc(%zu) failed", want);
+    }
+    b.bytes = want;
+    return MVLLM_OK;
+}
+
+int ensure_pinned(Context &c, size_t bytes) {
+    if (c.pinned_bytes >= bytes)
+        return MVLLM_OK;
+    if (c.pinned)
+        cudaFreeHost(c.pinned);
+    c.pinned = nullptr;
+    c.pinned_bytes = 0;
+    const size_t want = std::max(bytes, size_t(1) << 20);
+    if (cudaMallocHost(&c.pinned, want) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(MVLLM_ERR_NOMEM, "cudaMallocHost(%zu) failed", want);
+    }
+    c.pinned_bytes = want;
+    return MVLLM_OK;
+}
+
+// Bump allocator over a caller- or context-owned workspace.
+struct Carve {
+    uint8_t *base;
+    size_t cap, used = 0;
+    bool overflow = false;
+    Carve(void *b, size_t c) : base(static_cast<uint8_t *>(b)), cap(c) {}
+    template <typename T> T *take(size_t n) {
+        used = (used + 255) & ~size_t(255);
+        T *p = reinterpret_cast<T *>(base ? base + used : nullptr);
+        used += n * sizeof(T);
+        if (used > cap)
+            overflow = true;
+        return p;
+    }
+};
+
+// ------------------------------------------------------------ shapes / plan --
+size_t row_bytes_packed(int fmt, int cols) {
+    return fmt == MVLLM_FMT_F32 ? size_t(cols) * 4 : size_t((cols + 1) / 2);
+}
+size_t scale_row_bytes(int fmt, int cols) {
+    if (fmt == MVLLM_FMT_INT4_G64)
+        return size_t((cols + 63) / 64) * 4;
+    if (fmt == MVLLM_FMT_MXFP4)
+        return size_t((cols + 31) / 32);
+    return 0;
+}
+
+bool fast_path_ok(int fmt, int D, int I) {
+    if (fmt != MVLLM_FMT_INT4_G64 && fmt != MVLLM_FMT_MXFP4)
+        return false;
+    if (getenv("MVLLM_FORCE_GENERIC"))
+        return false;
+    return D >= 512 && I >= 512 && D % 512 == 0 && I % 512 == 0;
+}
+
+int chunk_tiles(int max_rows) { return max_rows <= 8 ? 1 : (max_rows <= 16 ? 2 : 4); }
+int pick_ks(int K) { return ((K / 2) % 512 == 0) ? 512 : 256; }
+
+struct RunWs {
+    int *base, *cnt, *off1, *off2, *total_rows, *err;
+    void *xs; // staged operand (fast: f16, generic: f32)
+    void *h;  // fast: f16 [rows, I]; generic: f32 [rows, I]
+    float *y; // [rows, D]
+};
+
+// Carves the expert-run workspace; x_rows = operand rows to stage (0 when the
+// operand is already staged by the caller of run_experts).
+void carve_run(Carve &cv, RunWs &w, int nb, int D, int I, bool fast, int rows_cap, int x_rows) {
+    w.base = cv.take<int>(nb);
+    w.cnt = cv.take<int>(nb);
+    w.off1 = cv.take<int>(nb + 1);
+    w.off2 = cv.take<int>(nb + 1);
+    w.total_rows = cv.take<int>(1);
+    w.err = cv.take<int>(1);
+    const size_t esz = fast ? 2 : 4;
+    w.xs = cv.take<uint8_t>(size_t(std::max(x_rows, 1)) * D * esz);
+    w.h = cv.take<uint8_t>(size_t(std::max(rows_cap, 1)) * I * esz);
+    w.y = cv.take<float>(size_t(std::max(rows_cap, 1)) * D);
+}
+
+struct Tables {
+    const void *const *g, *const *u, *const *d, *const *gs, *const *us, *const *ds;
+};
+
+template <int FMT, int PHASE, int KS, int NT>
+int launch_decode_t(DecodeArgs a, cudaStream_t st, int sms) {
+    using L = DecodeLayout<KS, NT>;
+    auto kern = decode_ffn_kernel<FMT, PHASE, KS, NT>;
+    static int budget_kb = [] {
+        const char *s = getenv("MVLLM_DECODE_SMEM_KB");
+        return s ? atoi(s) : 220;
+    }();
+    static int ns = 0, smem = 0, per_sm = 0; // per instantiation, set once
+    if (per_sm == 0) {
+        ns = (budget_kb * 1024 - L::HEAD_BYTES - 128) / L::STAGE_BYTES;
+        ns = std::max(2, std::min(8, ns));
+        smem = L::smem_bytes(ns);
+        CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        int occ = 0;
+        CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kDecodeThreads, smem));
+        per_sm = std::max(occ, 1);
+    }
+    a.nstages = ns;
+    kern<<<sms * std::max(per_sm, 1), kDecodeThreads, smem, st>>>(a);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+template <int FMT, int PHASE>
+int launch_decode(const DecodeArgs &a, int ks, int nt, cudaStream_t st, int sms) {
+    if (ks == 512) {
+        if (nt == 1)
+            return launch_decode_t<FMT, PHASE, 512, 1>(a, st, sms);
+        if (nt == 2)
+            return launch_decode_t<FMT, PHASE, 512, 2>(a, st, sms);
+        return launch_decode_t<FMT, PHASE, 512, 4>(a, st, sms);
+    }
+    if (nt == 1)
+        return launch_decode_t<FMT, PHASE, 256, 1>(a, st, sms);
+    if (nt == 2)
+        return launch_decode_t<FMT, PHASE, 256, 2>(a, st, sms);
+    return launch_decode_t<FMT, PHASE, 256, 4>(a, st, sms);
+}
+
+// The expert FFN over nb experts: plan, optional operand staging, phase 1,
+// phase 2.  Leaves y [rows, D] (reference base order) in w.y.  When
+// `x_staged` is set, x already is the staged operand (f16 in stage_pos order
+// on the fast path, f32 on the generic path) indexed by xoff.
+int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const Tables &tb,
+                const int *nr, const int *xoff, const void *x, int x_dtype, int x_rows,
+                bool x_staged, int max_rows, int act, float act_a, float act_b, RunWs &w) {
+    const bool fast = fast_path_ok(fmt, D, I);
+    const int nt = chunk_tiles(max_rows);
+    const int mt = 8 * nt;
+    PlanArgs pa{};
+    pa.nb = nb;
+    pa.fmt = fmt;
+    pa.nr = nr;
+    pa.g = tb.g, pa.u = tb.u, pa.d = tb.d, pa.gs = tb.gs, pa.us = tb.us, pa.ds = tb.ds;
+    if (fast) {
+        pa.chunk1 = mt, pa.blocks1 = I / 32;
+        pa.chunk2 = mt, pa.blocks2 = D / 64;
+    } else {
+        pa.chunk1 = 1 << 30, pa.blocks1 = (I + 7) / 8;
+        pa.chunk2 = 1 << 30, pa.blocks2 = (D + 7) / 8;
+    }
+    pa.base = w.base, pa.cnt = w.cnt, pa.off1 = w.off1, pa.off2 = w.off2;
+    pa.total_rows = w.total_rows;
+    pa.xoff = xoff, pa.x_rows = x_rows, pa.err = w.err, pa.align16 = fast ? 1 : 0;
+    plan_kernel<<<1, 1024, 0, st>>>(pa);
+    CUDA_TRY(cudaGetLastError());
+    prof_mark(st, kPhPlan);
+
+    const void *xop = x;
+    if (!x_staged) {
+        if (fast) {
+            if (x_dtype == MVLLM_DTYPE_BF16)
+                stage_rows_kernel<__nv_bfloat16, __half><<<std::max(1, std::min(x_rows, 4 * sms)), 256, 0, st>>>(
+                    static_cast<const __nv_bfloat16 *>(x), nullptr, nullptr, x_rows, D, fmt,
+                    static_cast<__half *>(w.xs));
+            else
+                stage_rows_kernel<float, __half><<<std::max(1, std::min(x_rows, 4 * sms)), 256, 0, st>>>(
+                    static_cast<const float *>(x), nullptr, nullptr, x_rows, D, fmt,
+                    static_cast<__half *>(w.xs));
+            CUDA_TRY(cudaGetLastError());
+            xop = w.xs;
+        } else if (x_dtype == MVLLM_DTYPE_BF16) {
+            stage_rows_kernel<__nv_bfloat16, float><<<std::max(1, std::min(x_rows, 4 * sms)), 256, 0, st>>>(
+                static_cast<const __nv_bfloat16 *>(x), nullptr, nullptr, x_rows, D, fmt,
+                static_cast<float *>(w.xs));
+            CUDA_TRY(cudaGetLastError());
+            xop = w.xs;
+        }
+    }
+
+    if (fast) {
+        DecodeArgs a{};
+        a.w0 = tb.g, a.w1 = tb.u, a.s0 = tb.gs, a.s1 = tb.us;
+        a.xrow = xoff, a.orow = w.base, a.cnt = w.cnt, a.item_off = w.off1, a.nb = nb;
+        a.x = static_cast<const __half *>(xop);
+        a.K = D, a.O = I, a.out = w.h;
+        a.act = act, a.act_a = act_a, a.act_b = act_b, a.err = w.err;
+        int rc = (fmt == MVLLM_FMT_MXFP4)
+                     ? launch_decode<MVLLM_FMT_MXFP4, 1>(a, pick_ks(D), nt, st, sms)
+                     : launch_decode<MVLLM_FMT_INT4_G64, 1>(a, pick_ks(D), nt, st, sms);
+        if (rc)
+            return rc;
+        prof_mark(st, kPhExpert1);
+        DecodeArgs b = a;
+        b.w0 = tb.d, b.w1 = nullptr, b.s0 = tb.ds, b.s1 = nullptr;
+        b.xrow = w.base, b.item_off = w.off2;
+        b.x = static_cast<const __half *>(w.h);
+        b.K = I, b.O = D, b.out = w.y;
+        rc = (fmt == MVLLM_FMT_MXFP4)
+                 ? launch_decode<MVLLM_FMT_MXFP4, 2>(b, pick_ks(I), nt, st, sms)
+                 : launch_decode<MVLLM_FMT_INT4_G64, 2>(b, pick_ks(I), nt, st, sms);
+        prof_mark(st, kPhExpert2);
+        return rc;
+    }
+    GenericArgs a{};
+    a.w0 = tb.g, a.w1 = tb.u, a.s0 = (fmt == MVLLM_FMT_F32) ? nullptr : tb.gs;
+    a.s1 = (fmt == MVLLM_FMT_F32) ? nullptr : tb.us;
+    a.xrow = xoff, a.orow = w.base, a.cnt = w.cnt, a.item_off = w.off1, a.nb = nb, a.fmt = fmt;
+    a.x = static_cast<const float *>(xop);
+    a.K = D, a.O = I, a.out = static_cast<float *>(w.h);
+    a.act = act, a.act_a = act_a, a.act_b = act_b;
+    generic_ffn_kernel<1><<<sms * 8, 256, 0, st>>>(a);
+    CUDA_TRY(cudaGetLastError());
+    prof_mark(st, kPhExpert1);
+    GenericArgs b = a;
+    b.w0 = tb.d, b.w1 = nullptr, b.s0 = (fmt == MVLLM_FMT_F32) ? nullptr : tb.ds, b.s1 = nullptr;
+    b.xrow = w.base, b.item_off = w.off2;
+    b.x = static_cast<const float *>(w.h);
+    b.K = I, b.O = D, b.out = w.y;
+    generic_ffn_kernel<2><<<sms * 8, 256, 0, st>>>(b);
+    CUDA_TRY(cudaGetLastError());
+    prof_mark(st, kPhExpert2);
+    return MVLLM_OK;
+}
+
+int check_device_error(const int *err_dev, cudaStream_t st) {
+    int err = 0;
+    CUDA_TRY(cudaMemcpyAsync(&err, err_dev, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    if (err)
+        return fail(err, "device-side error code %d", err);
+    return MVLLM_OK;
+}
+
+int init_locked(Context &c, int device) {
+    if (c.inited && c.device == device)
+        return MVLLM_OK;
+    if (c.inited)
+        return fail(MVLLM_ERR_INVALID, "already initialised on device %d", c.device);
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return fail(MVLLM_ERR_CUDA, "no CUDA device");
+    }
+    if (device < 0 || device >= n)
+        return fail(MVLLM_ERR_INVALID, "device %d out of range (%d devices)", device, n);
+    CUDA_TRY(cudaSetDevice(device));
+    cudaDeviceProp prop{};
+    CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(MVLLM_ERR_UNSUPPORTED, "device %d is sm_%d%d, this build targets sm_100a",
+                    device, prop.major, prop.minor);
+    CUDA_TRY(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+    for (auto &e : c.ev)
+        CUDA_TRY(cudaEventCreate(&e));
+    c.sms = prop.multiProcessorCount;
+    c.device = device;
+    c.inited = true;
+    return MVLLM_OK;
+}
+
+int ensure_current(Context &c) {
+    if (!c.inited)
+        return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
+    CUDA_TRY(cudaSetDevice(c.device));
+    return MVLLM_OK;
+}
+
+// Device address for a host array of `len` bytes: the registered cache copy
+// when one covers it, else a per-call upload into the transient arena.
+struct Resolver {
+    Context &c;
+    std::unordered_map<const void *, void *> seen;
+    std::vector<std::pair<const void *, size_t>> uploads; // host ptr, bytes
+    std::vector<size_t> up_off;
+    size_t transient_bytes = 0;
+
+    explicit Resolver(Context &cc) : c(cc) {}
+
+    // First pass: returns the cached device pointer or nullptr (to upload).
+    void *cached(const void *host, size_t len) {
+        if (!host)
+            return nullptr;
+        auto it = c.cache.upper_bound(reinterpret_cast<uintptr_t>(host));
+        if (it == c.cache.begin())
+            return nullptr;
+        --it;
+        const uintptr_t start = it->first, h = reinterpret_cast<uintptr_t>(host);
+        if (h >= start && h + len <= start + it->second.bytes)
+            return static_cast<uint8_t *>(it->second.dev) + (h - start);
+        return nullptr;
+    }
+
+    // Returns an index into uploads (or -1 when cached/null) and, through
+    // *dev_or_null, the device pointer for cached arrays.
+    long note(const void *host, size_t len, void **dev) {
+        *dev = nullptr;
+        if (!host)
+            return -1;
+        if (void *p = cached(host, len)) {
+            *dev = p;
+            return -1;
+        }
+        auto it = seen.find(host);
+        if (it != seen.end())
+            return reinterpret_cast<long>(it->second);
+        const long idx = static_cast<long>(uploads.size());
+        uploads.push_back({host, len});
+        transient_bytes = (transient_bytes + 255) & ~size_t(255);
+        up_off.push_back(transient_bytes);
+        transient_bytes += len;
+        seen[host] = reinterpret_cast<void *>(idx);
+        return idx;
+    }
+};
+
+} // namespace
+
+// =================================================================== C ABI ==
+extern "C" {
+
+int mvllm_moe_init(int device) {
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    return init_locked(c, device);
+}
+
+void mvllm_moe_shutdown(void) {
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (!c.inited)
+        return;
+    cudaSetDevice(c.device);
+    cudaStreamSynchronize(c.stream);
+    for (auto &kv : c.cache)
+        cudaFree(kv.second.dev);
+    c.cache.clear();
+    c.cache_bytes = 0;
+    if (c.ws.p)
+        cudaFree(c.ws.p);
+    if (c.transient.p)
+        cudaFree(c.transient.p);
+    if (c.pinned)
+        cudaFreeHost(c.pinned);
+    c.ws = DevBuf{};
+    c.transient = DevBuf{};
+    c.pinned = nullptr;
+    c.pinned_bytes = 0;
+    for (auto &e : c.ev)
+        cudaEventDestroy(e);
+    cudaStreamDestroy(c.stream);
+    c.stream = nullptr;
+    c.inited = false;
+    c.device = -1;
+}
+
+int mvllm_moe_available(void) { return ctx().inited ? 1 : 0; }
+
+const char *mvllm_moe_backend_name(void) { return "cuda-sm100a"; }
+
+const char *mvllm_moe_last_error(void) { return g_last_error.c_str(); }
+
+void mvllm_moe_stats(uint64_t *calls, uint64_t *experts, uint64_t *rows, double *h2d_ms,
+                     double *kernel_ms, double *d2h_ms) {
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (calls)
+        *calls = c.calls;
+    if (experts)
+        *experts = c.experts;
+    if (rows)
+        *rows = c.rows;
+    if (h2d_ms)
+        *h2d_ms = c.h2d_ms;
+    if (kernel_ms)
+        *kernel_ms = c.kernel_ms;
+    if (d2h_ms)
+        *d2h_ms = c.d2h_ms;
+}
+
+// ----------------------------------------------------------- expert cache --
+int mvllm_moe_cache_register(const void *host, size_t bytes, uint64_t generation) {
+    if (!host || bytes == 0)
+        return fail(MVLLM_ERR_INVALID, "cache_register: null pointer or zero size");
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (int rc = ensure_current(c))
+        return rc;
+    const uintptr_t key = reinterpret_cast<uintptr_t>(host);
+    auto it = c.cache.find(key);
+    if (it != c.cache.end()) {
+        if (it->second.bytes == bytes && it->second.generation == generation)
+            return MVLLM_OK;
+        cudaFree(it->second.dev);
+        c.cache_bytes -= it->second.bytes;
+        c.cache.erase(it);
+    }
+    // Ranges may not overlap: an overlapping older entry is dropped.
+    for (auto jt = c.cache.begin(); jt != c.cache.end();) {
+        const uintptr_t s = jt->first, e = s + jt->second.bytes;
+        if (s < key + bytes && key < e) {
+            cudaFree(jt->second.dev);
+            c.cache_bytes -= jt->second.bytes;
+            jt = c.cache.erase(jt);
+        } else {
+            ++jt;
+        }
+    }
+    CacheEntry ce;
+    if (cudaMalloc(&ce.dev, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(MVLLM_ERR_NOMEM, "cache_register: cudaMalloc(%zu) failed", bytes);
+    }
+    if (cudaMemcpy(ce.dev, host, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(ce.dev);
+        return fail(MVLLM_ERR_CUDA, "cache_register: upload failed");
+    }
+    ce.bytes = bytes;
+    ce.generation = generation;
+    c.cache[key] = ce;
+    c.cache_bytes += bytes;
+    return MVLLM_OK;
+}
+
+int mvllm_moe_cache_unregister(const void *host) {
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    auto it = c.cache.find(reinterpret_cast<uintptr_t>(host));
+    if (it == c.cache.end())
+        return fail(MVLLM_ERR_INVALID, "cache_unregister: pointer not registered");
+    if (c.inited)
+        cudaSetDevice(c.device);
+    cudaFree(it->second.dev);
+    c.cache_bytes -= it->second.bytes;
+    c.cache.erase(it);
+    return MVLLM_OK;
+}
+
+void mvllm_moe_cache_clear(void) {
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (c.inited)
+        cudaSetDevice(c.device);
+    for (auto &kv : c.cache)
+        cudaFree(kv.second.dev);
+    c.cache.clear();
+    c.cache_bytes = 0;
+}
+
+size_t mvllm_moe_cache_bytes(void) {
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    return c.cache_bytes;
+}
+
+// ----------------------------------------------------- moe_block (host) --
+int mvllm_moe_block(int nb, int D, int Iinter, int fmt, int qgs, const void *const *g,
+                    const void *const *u, const void *const *d, const float *const *gs,
+                    const float *const *us, const float *const *ds, const float *xg,
+                    const int *xoff, const int *nr, const int *rows, const float *rw, float *out,
+                    int S, int act, float act_a, float act_b) {
+    (void)qgs;
+    // Argument checks of metal_ops.cpp:452-457.
+    if (nb < 1 || D < 1 || !out || !xg || (fmt != 0 && fmt != 4 && fmt != 7))
+        return fail(MVLLM_ERR_INVALID, "moe_block: invalid nb/D/out/xg/fmt");
+    if (!xoff || !nr)
+        return fail(MVLLM_ERR_INVALID, "moe_block: xoff and nr are required");
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (int rc = ensure_current(c))
+        return rc;
+
+    // Host pass over experts: cpu_moe_block's base/skip rules.
+    const bool packed = fmt != MVLLM_FMT_F32;
+    int R = 0, n_valid = 0, max_rows = 0;
+    int64_t x_rows = 0;
+    std::vector<int> base(nb), valid(nb);
+    for (int e = 0; e < nb; ++e) {
+        const int n = nr[e];
+        base[e] = R;
+        valid[e] = 0;
+        if (n <= 0)
+            continue;
+        bool ok = Iinter >= 1 && g && u && d && g[e] && u[e] && d[e];
+        if (packed)
+            ok = ok && gs && us && ds && gs[e] && us[e] && ds[e];
+        if (ok) {
+            if (xoff[e] < 0)
+                return fail(MVLLM_ERR_INVALID, "moe_block: negative xoff for expert %d", e);
+            valid[e] = 1;
+            ++n_valid;
+            max_rows = std::max(max_rows, n);
+            x_rows = std::max<int64_t>(x_rows, int64_t(xoff[e]) + n);
+        }
+        R += n;
+    }
+    // Nothing observable happens without rows+rw (the reference computes and
+    // discards) or without an expert that runs.
+    if (!rows || !rw || n_valid == 0)
+        return MVLLM_OK;
+    if (x_rows > (int64_t(1) << 31) / std::max(D, 1))
+        return fail(MVLLM_ERR_INVALID, "moe_block: activation extent too large");
+
+    // Destinations -> CSR (ascending row id within each destination).
+    int S_ext = S;
+    if (S <= 0) {
+        S_ext = 0;
+        for (int e = 0; e < nb; ++e)
+            if (valid[e])
+                for (int r = 0; r < nr[e]; ++r)
+                    S_ext = std::max(S_ext, rows[base[e] + r] + 1);
+    }
+    std::vector<int> csr_off(size_t(S_ext) + 1, 0), csr_ids;
+    for (int e = 0; e < nb; ++e)
+        if (valid[e])
+            for (int r = 0; r < nr[e]; ++r) {
+                const int dest = rows[base[e] + r];
+                if (dest >= 0 && dest < S_ext)
+                    ++csr_off[size_t(dest) + 1];
+            }
+    for (int s = 0; s < S_ext; ++s)
+        csr_off[size_t(s) + 1] += csr_off[size_t(s)];
+    csr_ids.resize(size_t(csr_off[size_t(S_ext)]));
+    {
+        std::vector<int> cur(csr_off.begin(), csr_off.end() - 1);
+        for (int e = 0; e < nb; ++e)
+            if (valid[e])
+                for (int r = 0; r < nr[e]; ++r) {
+                    const int dest = rows[base[e] + r];
+                    if (dest >= 0 && dest < S_ext)
+                        csr_ids[size_t(cur[size_t(dest)]++)] = base[e] + r;
+                }
+    }
+    if (csr_ids.empty())
+        return MVLLM_OK; // every destination filtered out
+
+    // Resolve weights: cached device copies or per-call uploads.
+    const size_t gu_b = size_t(Iinter) * row_bytes_packed(fmt, D);
+    const size_t d_b = size_t(D) * row_bytes_packed(fmt, Iinter);
+    const size_t gus_b = size_t(Iinter) * scale_row_bytes(fmt, D);
+    const size_t ds_b = size_t(D) * scale_row_bytes(fmt, Iinter);
+    Resolver rs(c);
+    std::vector<void *> tdev(size_t(6) * nb, nullptr);
+    std::vector<long> tidx(size_t(6) * nb, -1);
+    for (int e = 0; e < nb; ++e) {
+        if (!valid[e])
+            continue;
+        const void *hp[6] = {g[e], u[e], d[e], packed ? gs[e] : nullptr, packed ? us[e] : nullptr,
+                             packed ? ds[e] : nullptr};
+        const size_t len[6] = {gu_b, gu_b, d_b, gus_b, gus_b, ds_b};
+        for (int k = 0; k < 6; ++k)
+            tidx[size_t(6) * e + k] = rs.note(hp[k], len[k], &tdev[size_t(6) * e + k]);
+    }
+    if (rs.transient_bytes) {
+        if (int rc = ensure_dev(c.transient, rs.transient_bytes))
+            return rc;
+        for (size_t i = 0; i < rs.uploads.size(); ++i)
+            CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t *>(c.transient.p) + rs.up_off[i],
+                                     rs.uploads[i].first, rs.uploads[i].second,
+                                     cudaMemcpyHostToDevice, c.stream));
+        for (size_t i = 0; i < tidx.size(); ++i)
+            if (tidx[i] >= 0)
+                tdev[i] = static_cast<uint8_t *>(c.transient.p) + rs.up_off[size_t(tidx[i])];
+    }
+    // Fast path needs 16-byte aligned weight and scale rows.
+    bool fast = fast_path_ok(fmt, D, Iinter);
+    for (size_t i = 0; i < tdev.size() && fast; ++i)
+        if (reinterpret_cast<uintptr_t>(tdev[i]) & 15u)
+            fast = false;
+    const int fmt_run = fmt;
+
+    // Device tables + metadata + activations + out, one upload.
+    std::vector<void *> tab(size_t(6) * nb, nullptr);
+    for (int e = 0; e < nb; ++e)
+        for (int k = 0; k < 6; ++k)
+            tab[size_t(k) * nb + e] = tdev[size_t(6) * e + k];
+    std::vector<int> nr_run(nb), xoff_run(nb);
+    for (int e = 0; e < nb; ++e) {
+        nr_run[e] = nr[e];
+        xoff_run[e] = valid[e] ? xoff[e] : 0;
+    }
+    const size_t xb = size_t(x_rows) * D * 4, ob = size_t(S_ext) * D * 4;
+    Carve hcv(nullptr, ~size_t(0));
+    const size_t o_tab = (hcv.take<void *>(tab.size()), hcv.used - tab.size() * sizeof(void *));
+    const size_t o_nr = (hcv.take<int>(nb), hcv.used - nb * 4);
+    const size_t o_xoff = (hcv.take<int>(nb), hcv.used - nb * 4);
+    const size_t o_coff = (hcv.take<int>(csr_off.size()), hcv.used - csr_off.size() * 4);
+    const size_t o_cids = (hcv.take<int>(csr_ids.size()), hcv.used - csr_ids.size() * 4);
+    const size_t o_rw = (hcv.take<float>(R), hcv.used - size_t(R) * 4);
+    const size_t o_x = (hcv.take<uint8_t>(xb), hcv.used - xb);
+    const size_t o_out = (hcv.take<uint8_t>(ob), hcv.used - ob);
+    const size_t up_bytes = hcv.used;
+    if (int rc = ensure_pinned(c, up_bytes))
+        return rc;
+    uint8_t *hp = static_cast<uint8_t *>(c.pinned);
+    memcpy(hp + o_tab, tab.data(), tab.size() * sizeof(void *));
+    memcpy(hp + o_nr, nr_run.data(), size_t(nb) * 4);
+    memcpy(hp + o_xoff, xoff_run.data(), size_t(nb) * 4);
+    memcpy(hp + o_coff, csr_off.data(), csr_off.size() * 4);
+    memcpy(hp + o_cids, csr_ids.data(), csr_ids.size() * 4);
+    memcpy(hp + o_rw, rw, size_t(R) * 4);
+    memcpy(hp + o_x, xg, xb);
+    if (S_ext > 0)
+        memcpy(hp + o_out, out, ob);
+
+    Carve dcv(nullptr, ~size_t(0));
+    dcv.take<uint8_t>(up_bytes);
+    RunWs w{};
+    carve_run(dcv, w, nb, D, Iinter, fast, R, int(x_rows));
+    if (int rc = ensure_dev(c.ws, dcv.used))
+        return rc;
+    uint8_t *db = static_cast<uint8_t *>(c.ws.p);
+    Carve dcv2(db, c.ws.bytes);
+    dcv2.take<uint8_t>(up_bytes);
+    carve_run(dcv2, w, nb, D, Iinter, fast, R, int(x_rows));
+
+    CUDA_TRY(cudaEventRecord(c.ev[0], c.stream));
+    CUDA_TRY(cudaMemcpyAsync(db, hp, up_bytes, cudaMemcpyHostToDevice, c.stream));
+    CUDA_TRY(cudaMemsetAsync(w.err, 0, sizeof(int), c.stream));
+    CUDA_TRY(cudaEventRecord(c.ev[1], c.stream));
+    prof_mark(c.stream, kPhStart);
+    void *const *dt = reinterpret_cast<void *const *>(db + o_tab);
+    Tables tb{dt, dt + nb, dt + 2 * nb, dt + 3 * nb, dt + 4 * nb, dt + 5 * nb};
+    const int *d_nr = reinterpret_cast<const int *>(db + o_nr);
+    const int *d_xoff = reinterpret_cast<const int *>(db + o_xoff);
+    float *d_out = reinterpret_cast<float *>(db + o_out);
+    const float *d_x = reinterpret_cast<const float *>(db + o_x);
+    int rc;
+    if (fast) {
+        rc = run_experts(c.stream, c.sms, nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
+                         MVLLM_DTYPE_F32, int(x_rows), false, max_rows, act, act_a, act_b, w);
+    } else {
+        // Generic path reads the uploaded f32 rows directly.
+        RunWs w2 = w;
+        w2.xs = const_cast<float *>(d_x);
+        rc = run_experts(c.stream, c.sms, nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
+                         MVLLM_DTYPE_F32, int(x_rows), true, max_rows, act, act_a, act_b, w2);
+    }
+    if (rc)
+        return rc;
+    {
+        dim3 grid((D + 255) / 256, std::min(S_ext, 65535));
+        combine_csr_kernel<<<grid, 256, 0, c.stream>>>(
+            d_out, w.y, reinterpret_cast<const float *>(db + o_rw),
+            reinterpret_cast<const int *>(db + o_coff), reinterpret_cast<const int *>(db + o_cids),
+            S_ext, D);
+        CUDA_TRY(cudaGetLastError());
+        prof_mark(c.stream, kPhCombine);
+    }
+    CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
+    CUDA_TRY(cudaMemcpyAsync(out, d_out, ob, cudaMemcpyDeviceToHost, c.stream));
+    CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
+    if (int rc2 = check_device_error(w.err, c.stream))
+        return rc2;
+    float a = 0, b = 0, cc = 0;
+    cudaEventElapsedTime(&a, c.ev[0], c.ev[1]);
+    cudaEventElapsedTime(&b, c.ev[1], c.ev[2]);
+    cudaEventElapsedTime(&cc, c.ev[2], c.ev[3]);
+    c.h2d_ms += a;
+    c.kernel_ms += b;
+    c.d2h_ms += cc;
+    c.calls += 1;
+    c.experts += uint64_t(n_valid);
+    c.rows += uint64_t(R);
+    return MVLLM_OK;
+}
+
+// ------------------------------------------------------ moe_block (device) --
+size_t mvllm_moe_block_dev_workspace(int nb, int D, int Iinter, int fmt, int rows_cap, int x_rows,
+                                     int S) {
+    if (nb < 1 || D < 1 || Iinter < 1 || rows_cap < 0 || x_rows < 0 || S < 1)
+        return 0;
+    const bool fast = fast_path_ok(fmt, D, Iinter);
+    Carve cv(nullptr, ~size_t(0));
+    RunWs w{};
+    carve_run(cv, w, nb, D, Iinter, fast, rows_cap, x_rows);
+    cv.take<int>(S);          // hist
+    cv.take<int>(size_t(S) + 1); // off
+    cv.take<int>(std::max(rows_cap, 1));
+    return cv.used + 256;
+}
+
+int mvllm_moe_block_dev(void *stream, int nb, int D, int Iinter, int fmt, const void *const *g,
+                        const void *const *u, const void *const *d, const void *const *gs,
+                        const void *const *us, const void *const *ds, const void *x, int x_dtype,
+                        int x_rows, const int *xoff, const int *nr, const int *rows,
+                        const float *rw, float *out, int S, int act, float act_a, float act_b,
+                        int rows_cap, void *workspace, size_t workspace_bytes) {
+    if (nb < 1 || D < 1 || !out || !x || (fmt != 0 && fmt != 4 && fmt != 7) || !xoff || !nr)
+        return fail(MVLLM_ERR_INVALID, "moe_block_dev: invalid arguments");
+    if (!g || !u || !d || (fmt != MVLLM_FMT_F32 && (!gs || !us || !ds)) || S < 1 || Iinter < 1 ||
+        rows_cap < 0 || x_rows < 0)
+        return fail(MVLLM_ERR_INVALID, "moe_block_dev: invalid tables or sizes");
+    if (x_dtype != MVLLM_DTYPE_F32 && x_dtype != MVLLM_DTYPE_BF16)
+        return fail(MVLLM_ERR_INVALID, "moe_block_dev: unknown x dtype");
+    if (!rows || !rw)
+        return MVLLM_OK;
+    const size_t need = mvllm_moe_block_dev_workspace(nb, D, Iinter, fmt, rows_cap, x_rows, S);
+    if (!workspace || workspace_bytes < need)
+        return fail(MVLLM_ERR_WORKSPACE, "moe_block_dev: workspace %zu < %zu", workspace_bytes,
+                    need);
+    Context &c = ctx();
+    int sms;
+    {
+        std::lock_guard<std::mutex> lk(c.mu);
+        if (int rc = ensure_current(c))
+            return rc;
+        sms = c.sms;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool fast = fast_path_ok(fmt, D, Iinter);
+    Carve cv(workspace, workspace_bytes);
+    RunWs w{};
+    carve_run(cv, w, nb, D, Iinter, fast, rows_cap, x_rows);
+    int *hist = cv.take<int>(S);
+    int *off = cv.take<int>(size_t(S) + 1);
+    int *ids = cv.take<int>(std::max(rows_cap, 1));
+    CUDA_TRY(cudaMemsetAsync(w.err, 0, sizeof(int), st));
+    prof_mark(st, kPhStart);
+    Tables tb{g, u, d, gs, us, ds};
+    const bool staged = !fast && x_dtype == MVLLM_DTYPE_F32;
+    int rc = run_experts(st, sms, nb, D, Iinter, fmt, tb, nr, xoff, x, x_dtype, x_rows, staged,
+                         rows_cap, act, act_a, act_b, w);
+    if (rc)
+        return rc;
+    build_csr_kernel<<<1, 1024, 0, st>>>(rows, w.base, w.cnt, nb, w.total_rows, S, hist, off, ids);
+    CUDA_TRY(cudaGetLastError());
+    dim3 grid((D + 255) / 256, std::min(S, 65535));
+    combine_csr_kernel<<<grid, 256, 0, st>>>(out, w.y, rw, off, ids, S, D);
+    CUDA_TRY(cudaGetLastError());
+    prof_mark(st, kPhCombine);
+    return MVLLM_OK;
+}
+
+// --------------------------------------------------------------- permute --
+namespace {
+struct PermWs {
+    uint32_t *bitmap;
+    float *wsum;
+    int words;
+};
+void carve_perm(Carve &cv, PermWs &p, int T, int K, int E, int n_shared) {
+    p.words = (T + 31) / 32;
+    p.bitmap = cv.take<uint32_t>(size_t(E + n_shared) * p.words);
+    p.wsum = cv.take<float>(size_t(T) * (K + n_shared));
+}
+int run_permute(cudaStream_t st, int sms, const int *idx, const float *wt, int T, int K, int E,
+                int n_shared, int *nr, int *xoff, int *rows, float *rw, int *tok_pos,
+                int *n_rows, const PermWs &p) {
+    CUDA_TRY(cudaMemsetAsync(p.bitmap, 0, size_t(E + n_shared) * p.words * 4, st));
+    permute_member_kernel<<<std::max(1, std::min((T + 127) / 128, 4 * sms)), 128, 0, st>>>(
+        idx, wt, T, K, E, n_shared, p.words, p.bitmap, p.wsum, tok_pos);
+    CUDA_TRY(cudaGetLastError());
+    permute_segments_kernel<<<1, 1024, 0, st>>>(idx, T, K, E, n_shared, p.words, p.bitmap, p.wsum,
+                                                nr, xoff, rows, rw, tok_pos, n_rows);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+} // namespace
+
+size_t mvllm_moe_permute_workspace(int T, int K, int E, int n_shared) {
+    if (T < 1 || K < 1 || E < 1 || n_shared < 0 || n_shared > 1)
+        return 0;
+    Carve cv(nullptr, ~size_t(0));
+    PermWs p{};
+    carve_perm(cv, p, T, K, E, n_shared);
+    return cv.used + 256;
+}
+
+int mvllm_moe_permute_dev(void *stream, const int *idx, const float *wt, int T, int K, int E,
+                          int n_shared, int *nr, int *xoff, int *rows, float *rw, int *tok_pos,
+                          int *n_rows, void *workspace, size_t workspace_bytes) {
+    if (!idx || !wt || T < 1 || K < 1 || E < 1 || n_shared < 0 || n_shared > 1 || !nr || !xoff ||
+        !rows || !rw || !tok_pos || !n_rows)
+        return fail(MVLLM_ERR_INVALID, "permute_dev: invalid arguments");
+    const size_t need = mvllm_moe_permute_workspace(T, K, E, n_shared);
+    if (!workspace || workspace_bytes < need)
+        return fail(MVLLM_ERR_WORKSPACE, "permute_dev: workspace too small");
+    Context &c = ctx();
+    int sms;
+    {
+        std::lock_guard<std::mutex> lk(c.mu);
+        if (int rc = ensure_current(c))
+            return rc;
+        sms = c.sms;
+    }
+    Carve cv(workspace, workspace_bytes);
+    PermWs p{};
+    carve_perm(cv, p, T, K, E, n_shared);
+    return run_permute(static_cast<cudaStream_t>(stream), sms, idx, wt, T, K, E, n_shared, nr,
+                       xoff, rows, rw, tok_pos, n_rows, p);
+}
+
+// ----------------------------------------------------------------- layer --
+namespace {
+struct LayerWs {
+    PermWs perm;
+    int *nr, *xoff, *rows, *tok_pos, *n_rows;
+    float *rw;
+    RunWs run;
+};
+void carve_layer(Carve &cv, LayerWs &l, int T, int K, int E, int n_shared, int D, int I,
+                 bool fast) {
+    const int EE = E + n_shared, R = T * (K + n_shared);
+    carve_perm(cv, l.perm, T, K, E, n_shared);
+    l.nr = cv.take<int>(EE);
+    l.xoff = cv.take<int>(EE);
+    l.rows = cv.take<int>(R);
+    l.rw = cv.take<float>(R);
+    l.tok_pos = cv.take<int>(R);
+    l.n_rows = cv.take<int>(1);
+    carve_run(cv, l.run, EE, D, I, fast, R, R);
+}
+} // namespace
+
+size_t mvllm_moe_layer_workspace(int T, int K, int E, int n_shared, int D, int Iinter, int fmt) {
+    if (T < 1 || K < 1 || E < 1 || n_shared < 0 || n_shared > 1 || D < 1 || Iinter < 1)
+        return 0;
+    Carve cv(nullptr, ~size_t(0));
+    LayerWs l{};
+    carve_layer(cv, l, T, K, E, n_shared, D, Iinter, fast_path_ok(fmt, D, Iinter));
+    return cv.used + 256;
+}
+
+static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_shared, int D,
+                          int Iinter, int fmt, const int *idx, const float *wt, const void *x,
+                          int x_dtype, const Tables &tb, float *out, int act, float act_a,
+                          float act_b, const LayerWs &l) {
+    const bool fast = fast_path_ok(fmt, D, Iinter);
+    const int EE = E + n_shared, KK = K + n_shared, R = T * KK;
+    CUDA_TRY(cudaMemsetAsync(l.run.err, 0, sizeof(int), st));
+    prof_mark(st, kPhStart);
+    if (int rc = run_permute(st, sms, idx, wt, T, K, E, n_shared, l.nr, l.xoff, l.rows, l.rw,
+                             l.tok_pos, l.n_rows, l.perm))
+        return rc;
+    prof_mark(st, kPhPermute);
+    // Gather + stage the token rows into expert-major order.
+    const int gblocks = std::min(R, 8 * sms);
+    if (fast) {
+        if (x_dtype == MVLLM_DTYPE_BF16)
+            stage_rows_kernel<__nv_bfloat16, __half><<<gblocks, 256, 0, st>>>(
+                static_cast<const __nv_bfloat16 *>(x), l.rows, l.n_rows, 0, D, fmt,
+                static_cast<__half *>(l.run.xs));
+        else
+            stage_rows_kernel<float, __half><<<gblocks, 256, 0, st>>>(
+                static_cast<const float *>(x), l.rows, l.n_rows, 0, D, fmt,
+                static_cast<__half *>(l.run.xs));
+    } else {
+        if (x_dtype == MVLLM_DTYPE_BF16)
+            stage_rows_kernel<__nv_bfloat16, float><<<gblocks, 256, 0, st>>>(
+                static_cast<const __nv_bfloat16 *>(x), l.rows, l.n_rows, 0, D, fmt,
+                static_cast<float *>(l.run.xs));
+        else
+            stage_rows_kernel<float, float><<<gblocks, 256, 0, st>>>(
+                static_cast<const float *>(x), l.rows, l.n_rows, 0, D, fmt,
+                static_cast<float *>(l.run.xs));
+    }
+    CUDA_TRY(cudaGetLastError());
+    prof_mark(st, kPhGather);
+    RunWs w = l.run;
+    if (int rc = run_experts(st, sms, EE, D, Iinter, fmt, tb, l.nr, l.xoff, l.run.xs,
+                             MVLLM_DTYPE_F32, R, true, T, act, act_a, act_b, w))
+        return rc;
+    dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
+    combine_tokens_kernel<<<grid, 256, 0, st>>>(out, w.y, l.rw, l.tok_pos, T, KK, D);
+    CUDA_TRY(cudaGetLastError());
+    prof_mark(st, kPhCombine);
+    return MVLLM_OK;
+}
+
+int mvllm_moe_layer_dev(void *stream, int T, int K, int E, int n_shared, int D, int Iinter,
+                        int fmt, const int *idx, const float *wt, const void *x, int x_dtype,
+                        const void *const *g, const void *const *u, const void *const *d,
+                        const void *const *gs, const void *const *us, const void *const *ds,
+                        float *out, int act, float act_a, float act_b, void *workspace,
+                        size_t workspace_bytes) {
+    if (T < 1 || K < 1 || K > 16 || E < 1 || n_shared < 0 || n_shared > 1 || D < 1 ||
+        Iinter < 1 || (fmt != 0 && fmt != 4 && fmt != 7) || !idx || !wt || !x || !g || !u || !d ||
+        !out || (fmt != MVLLM_FMT_F32 && (!gs || !us || !ds)) || D % 4 != 0)
+        return fail(MVLLM_ERR_INVALID, "layer_dev: invalid arguments");
+    if (x_dtype != MVLLM_DTYPE_F32 && x_dtype != MVLLM_DTYPE_BF16)
+        return fail(MVLLM_ERR_INVALID, "layer_dev: unknown x dtype");
+    const size_t need = mvllm_moe_layer_workspace(T, K, E, n_shared, D, Iinter, fmt);
+    if (!workspace || workspace_bytes < need)
+        return fail(MVLLM_ERR_WORKSPACE, "layer_dev: workspace %zu < %zu", workspace_bytes, need);
+    Context &c = ctx();
+    int sms;
+    {
+        std::lock_guard<std::mutex> lk(c.mu);
+        if (int rc = ensure_current(c))
+            return rc;
+        sms = c.sms;
+    }
+    Carve cv(workspace, workspace_bytes);
+    LayerWs l{};
+    carve_layer(cv, l, T, K, E, n_shared, D, Iinter, fast_path_ok(fmt, D, Iinter));
+    Tables tb{g, u, d, gs, us, ds};
+    return layer_dev_impl(static_cast<cudaStream_t>(stream), sms, T, K, E, n_shared, D, Iinter,
+                          fmt, idx, wt, x, x_dtype, tb, out, act, act_a, act_b, l);
+}
+
+int mvllm_moe_layer_host(int T, int K, int E, int n_shared, int D, int Iinter, int fmt,
+                         const int *idx, const float *wt, const float *x, const void *const *g,
+                         const void *const *u, const void *const *d, const void *const *gs,
+                         const void *const *us, const void *const *ds, float *out, int act,
+                         float act_a, float act_b) {
+    if (T < 1 || K < 1 || K > 16 || E < 1 || n_shared < 0 || n_shared > 1 || D < 1 ||
+        Iinter < 1 || (fmt != 0 && fmt != 4 && fmt != 7) || !idx || !wt || !x || !g || !u || !d ||
+        !out || (fmt != MVLLM_FMT_F32 && (!gs || !us || !ds)) || D % 4 != 0)
+        return fail(MVLLM_ERR_INVALID, "layer_host: invalid arguments");
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (int rc = ensure_current(c))
+        return rc;
+    const int EE = E + n_shared;
+    const bool fast = fast_path_ok(fmt, D, Iinter);
+    const size_t tab_b = size_t(6) * EE * sizeof(void *);
+    const size_t idx_b = size_t(T) * K * 4, x_b = size_t(T) * D * 4;
+    const size_t up = tab_b + 2 * idx_b + 2 * x_b + 1024;
+    if (int rc = ensure_pinned(c, up))
+        return rc;
+    Carve hcv(c.pinned, c.pinned_bytes);
+    void **htab = hcv.take<void *>(size_t(6) * EE);
+    int *hidx = hcv.take<int>(size_t(T) * K);
+    float *hwt = hcv.take<float>(size_t(T) * K);
+    float *hx = hcv.take<float>(size_t(T) * D);
+    float *hout = hcv.take<float>(size_t(T) * D);
+    const size_t up_bytes = reinterpret_cast<uint8_t *>(hout) - static_cast<uint8_t *>(c.pinned) +
+                            x_b;
+    for (int e = 0; e < EE; ++e) {
+        htab[e] = const_cast<void *>(g[e]);
+        htab[EE + e] = const_cast<void *>(u[e]);
+        htab[2 * EE + e] = const_cast<void *>(d[e]);
+        htab[3 * EE + e] = gs ? const_cast<void *>(gs[e]) : nullptr;
+        htab[4 * EE + e] = us ? const_cast<void *>(us[e]) : nullptr;
+        htab[5 * EE + e] = ds ? const_cast<void *>(ds[e]) : nullptr;
+    }
+    memcpy(hidx, idx, idx_b);
+    memcpy(hwt, wt, idx_b);
+    memcpy(hx, x, x_b);
+    memcpy(hout, out, x_b);
+    Carve dcv(nullptr, ~size_t(0));
+    dcv.take<uint8_t>(up_bytes);
+    LayerWs l{};
+    carve_layer(dcv, l, T, K, E, n_shared, D, Iinter, fast);
+    if (int rc = ensure_dev(c.ws, dcv.used + 256))
+        return rc;
+    uint8_t *db = static_cast<uint8_t *>(c.ws.p);
+    Carve dcv2(db, c.ws.bytes);
+    dcv2.take<uint8_t>(up_bytes);
+    carve_layer(dcv2, l, T, K, E, n_shared, D, Iinter, fast);
+    auto dptr = [&](const void *hp) {
+        return db + (static_cast<const uint8_t *>(hp) - static_cast<uint8_t *>(c.pinned));
+    };
+    CUDA_TRY(cudaEventRecord(c.ev[0], c.stream));
+    CUDA_TRY(cudaMemcpyAsync(db, c.pinned, up_bytes, cudaMemcpyHostToDevice, c.stream));
+    CUDA_TRY(cudaEventRecord(c.ev[1], c.stream));
+    void *const *dt = reinterpret_cast<void *const *>(dptr(htab));
+    Tables tb{dt, dt + EE, dt + 2 * EE, dt + 3 * EE, dt + 4 * EE, dt + 5 * EE};
+    float *dout = reinterpret_cast<float *>(dptr(hout));
+    if (int rc = layer_dev_impl(c.stream, c.sms, T, K, E, n_shared, D, Iinter, fmt,
+                                reinterpret_cast<const int *>(dptr(hidx)),
+                                reinterpret_cast<const float *>(dptr(hwt)), dptr(hx),
+                                MVLLM_DTYPE_F32, tb, dout, act, act_a, act_b, l))
+        return rc;
+    CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
+    CUDA_TRY(cudaMemcpyAsync(out, dout, x_b, cudaMemcpyDeviceToHost, c.stream));
+    CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
+    if (int rc = check_device_error(l.run.err, c.stream))
+        return rc;
+    float a = 0, b = 0, cc = 0;
+    cudaEventElapsedTime(&a, c.ev[0], c.ev[1]);
+    cudaEventElapsedTime(&b, c.ev[1], c.ev[2]);
+    cudaEventElapsedTime(&cc, c.ev[2], c.ev[3]);
+    c.h2d_ms += a;
+    c.kernel_ms += b;
+    c.d2h_ms += cc;
+    c.calls += 1;
+    c.rows += uint64_t(T) * (K + n_shared);
+    return MVLLM_OK;
+}
+
+// ------------------------------------------------------------ packers etc --
+int mvllm_quantize_int4_g64_dev(void *stream, const float *w, int O, int I, uint8_t *packed,
+                                float *scales) {
+    if (!w || O < 1 || I < 1 || !packed || !scales)
+        return fail(MVLLM_ERR_INVALID, "quantize_int4_g64_dev: invalid arguments");
+    Context &c = ctx();
+    if (!c.inited)
+        return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
+    const size_t groups = size_t(O) * ((I + 63) / 64);
+    const int blocks = int(std::min<size_t>((groups + 255) / 256, size_t(c.sms) * 16));
+    quantize_int4_g64_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(w, O, I,
+                                                                                  packed, scales);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+int mvllm_pack_mxfp4_dev(void *stream, const float *w, int O, int I, uint8_t *packed,
+                         uint8_t *scales) {
+    if (!w || O < 1 || I < 1 || !packed || !scales)
+        return fail(MVLLM_ERR_INVALID, "pack_mxfp4_dev: invalid arguments");
+    Context &c = ctx();
+    if (!c.inited)
+        return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
+    const size_t groups = size_t(O) * ((I + 31) / 32);
+    const int blocks = int(std::min<size_t>((groups + 255) / 256, size_t(c.sms) * 16));
+    pack_mxfp4_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(w, O, I, packed,
+                                                                           scales);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+int mvllm_matmul_dev(void *stream, int fmt, float *y, const float *x, const void *w,
+                     const void *scales, int S, int I, int O) {
+    if ((fmt != 0 && fmt != 4 && fmt != 7) || !y || !x || !w || S < 1 || I < 1 || O < 1 ||
+        (fmt != 0 && !scales))
+        return fail(MVLLM_ERR_INVALID, "matmul_dev: invalid arguments");
+    if (!ctx().inited)
+        return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
+    matmul_generic_kernel<<<(O + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        fmt, y, x, w, scales, S, I, O);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+// ------------------------------------------------------------- profiling --
+void mvllm_moe_profile_enable(int on) {
+    Prof &p = prof();
+    std::lock_guard<std::mutex> lk(p.mu);
+    p.on = on != 0;
+    p.marks.clear();
+    p.used = 0;
+}
+
+int mvllm_moe_profile_read(double *ms, long long *launches, int n) {
+    Prof &p = prof();
+    std::lock_guard<std::mutex> lk(p.mu);
+    for (int i = 0; i < n; ++i) {
+        if (ms)
+            ms[i] = 0.0;
+        if (launches)
+            launches[i] = 0;
+    }
+    if (!p.marks.empty())
+        CUDA_TRY(cudaEventSynchronize(p.marks.back().first));
+    for (size_t i = 1; i < p.marks.size(); ++i) {
+        const int ph = p.marks[i].second;
+        if (ph < 0 || ph >= n) // an interval ending at a call start spans host time
+            continue;
+        float t = 0.f;
+        if (cudaEventElapsedTime(&t, p.marks[i - 1].first, p.marks[i].first) != cudaSuccess)
+            continue;
+        if (ms)
+            ms[ph] += t;
+        if (launches)
+            launches[ph] += 1;
+    }
+    p.marks.clear();
+    p.used = 0;
+    return kPhCount;
+}
+
+} // extern "C"

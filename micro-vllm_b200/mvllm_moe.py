@@ -1,0 +1,265 @@
+"""Python host binding of libmvllm_moe.so (the sm_100a MoE block).
+
+Mirrors the reference's operator interface for this path: ``moe_block`` has
+the argument list, meaning and error behaviour of
+``mvllm::metal_ops::moe_block`` (src/gpu/metal_ops.hpp:104-108): it returns
+True on success and False exactly where the reference returns false; a CUDA
+failure raises ``MoeError``.  There is no CPU fallback: importing this module
+on a machine without the built library raises, and every call runs the CUDA
+library.
+
+Host buffers are numpy arrays; device buffers are torch CUDA tensors (torch is
+only used for device memory and streams).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libmvllm_moe.so")
+
+OK, ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_NOT_INIT, ERR_DEVICE, \
+    ERR_WORKSPACE = range(9)
+ACT_SILU, ACT_CLAMP_SWIGLU, ACT_SITU = 0, 1, 2
+FMT_F32, FMT_INT4_G64, FMT_MXFP4 = 0, 4, 7
+DTYPE_F32, DTYPE_BF16 = 0, 1
+
+# Every symbol include/mvllm_moe.h declares (checked by tests/test_abi.py).
+C_SYMBOLS = (
+    "mvllm_moe_init", "mvllm_moe_shutdown", "mvllm_moe_available", "mvllm_moe_backend_name",
+    "mvllm_moe_last_error", "mvllm_moe_stats", "mvllm_moe_block", "mvllm_moe_cache_register",
+    "mvllm_moe_cache_unregister", "mvllm_moe_cache_clear", "mvllm_moe_cache_bytes",
+    "mvllm_moe_block_dev_workspace", "mvllm_moe_block_dev", "mvllm_moe_permute_workspace",
+    "mvllm_moe_permute_dev", "mvllm_moe_layer_workspace", "mvllm_moe_layer_dev",
+    "mvllm_moe_layer_host", "mvllm_quantize_int4_g64_dev", "mvllm_pack_mxfp4_dev",
+    "mvllm_matmul_dev", "mvllm_moe_profile_enable", "mvllm_moe_profile_read",
+)
+PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
+
+
+class MoeError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"mvllm_moe error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def lib():
+    """Loads the CUDA library (fails loudly if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run micro-vllm_b200/build.py")
+        L = C.CDLL(LIB_PATH)
+        vp, i, f, sz = C.c_void_p, C.c_int, C.c_float, C.c_size_t
+        sig = {
+            "mvllm_moe_init": (i, [i]),
+            "mvllm_moe_shutdown": (None, []),
+            "mvllm_moe_available": (i, []),
+            "mvllm_moe_backend_name": (C.c_char_p, []),
+            "mvllm_moe_last_error": (C.c_char_p, []),
+            "mvllm_moe_stats": (None, [vp] * 6),
+            "mvllm_moe_block": (i, [i, i, i, i, i] + [vp] * 6 + [vp] * 6 + [i, i, f, f]),
+            "mvllm_moe_cache_register": (i, [vp, sz, C.c_uint64]),
+            "mvllm_moe_cache_unregister": (i, [vp]),
+            "mvllm_moe_cache_clear": (None, []),
+            "mvllm_moe_cache_bytes": (sz, []),
+            "mvllm_moe_block_dev_workspace": (sz, [i] * 7),
+            "mvllm_moe_block_dev": (i, [vp, i, i, i, i] + [vp] * 6 + [vp, i, i] + [vp] * 5 +
+                                    [i, i, f, f, i, vp, sz]),
+            "mvllm_moe_permute_workspace": (sz, [i] * 4),
+            "mvllm_moe_permute_dev": (i, [vp, vp, vp, i, i, i, i] + [vp] * 6 + [vp, sz]),
+            "mvllm_moe_layer_workspace": (sz, [i] * 7),
+            "mvllm_moe_layer_dev": (i, [vp] + [i] * 7 + [vp, vp, vp, i] + [vp] * 6 +
+                                    [vp, i, f, f, vp, sz]),
+            "mvllm_moe_layer_host": (i, [i] * 7 + [vp] * 3 + [vp] * 6 + [vp, i, f, f]),
+            "mvllm_quantize_int4_g64_dev": (i, [vp, vp, i, i, vp, vp]),
+            "mvllm_pack_mxfp4_dev": (i, [vp, vp, i, i, vp, vp]),
+            "mvllm_matmul_dev": (i, [vp, i, vp, vp, vp, vp, i, i, i]),
+            "mvllm_moe_profile_enable": (None, [i]),
+            "mvllm_moe_profile_read": (i, [vp, vp, i]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().mvllm_moe_last_error().decode()
+
+
+def _check(rc):
+    if rc != OK:
+        raise MoeError(rc, last_error())
+
+
+def init(device: int = 0) -> None:
+    _check(lib().mvllm_moe_init(device))
+
+
+def shutdown() -> None:
+    lib().mvllm_moe_shutdown()
+
+
+def available() -> bool:
+    return bool(lib().mvllm_moe_available())
+
+
+def backend_name() -> str:
+    return lib().mvllm_moe_backend_name().decode()
+
+
+def stats():
+    vals = [C.c_uint64(), C.c_uint64(), C.c_uint64(), C.c_double(), C.c_double(), C.c_double()]
+    lib().mvllm_moe_stats(*[C.byref(v) for v in vals])
+    return {"calls": vals[0].value, "experts": vals[1].value, "rows": vals[2].value,
+            "h2d_ms": vals[3].value, "kernel_ms": vals[4].value, "d2h_ms": vals[5].value}
+
+
+def profile_enable(on: bool = True) -> None:
+    lib().mvllm_moe_profile_enable(1 if on else 0)
+
+
+def profile_read():
+    """{phase: (device ms, launches)} since profile_enable."""
+    n = len(PHASES)
+    ms = (C.c_double * n)()
+    cnt = (C.c_longlong * n)()
+    lib().mvllm_moe_profile_read(ms, cnt, n)
+    return {PHASES[i]: (ms[i], cnt[i]) for i in range(n)}
+
+
+def _p(a):
+    return None if a is None else C.c_void_p(a.ctypes.data)
+
+
+def _parr(arrs):
+    if arrs is None:
+        return None
+    out = (C.c_void_p * len(arrs))()
+    for k, a in enumerate(arrs):
+        out[k] = None if a is None else a.ctypes.data
+    return out
+
+
+# --------------------------------------------------------------- host path --
+def moe_block(nb, D, Iinter, fmt, g, u, d, gs, us, ds, xg, xoff, nr, rows, rw, out, S, act=0,
+              act_a=0.0, act_b=0.0, qgs=0) -> bool:
+    """metal_ops::moe_block on host numpy buffers (``out`` is accumulated in place).
+
+    Returns False where the reference returns false (invalid arguments);
+    raises MoeError on a CUDA failure.
+    """
+    rc = lib().mvllm_moe_block(nb, D, Iinter, fmt, qgs, _parr(g), _parr(u), _parr(d), _parr(gs),
+                               _parr(us), _parr(ds), _p(xg), _p(xoff), _p(nr), _p(rows), _p(rw),
+                               _p(out), S, act, act_a, act_b)
+    if rc == ERR_INVALID:
+        return False
+    _check(rc)
+    return True
+
+
+def cache_register(arr: np.ndarray, generation: int = 0) -> None:
+    _check(lib().mvllm_moe_cache_register(C.c_void_p(arr.ctypes.data), arr.nbytes, generation))
+
+
+def cache_unregister(arr: np.ndarray) -> None:
+    _check(lib().mvllm_moe_cache_unregister(C.c_void_p(arr.ctypes.data)))
+
+
+def cache_clear() -> None:
+    lib().mvllm_moe_cache_clear()
+
+
+def cache_bytes() -> int:
+    return lib().mvllm_moe_cache_bytes()
+
+
+def layer_host(T, K, E, n_shared, D, Iinter, fmt, idx, wt, x, tables, out, act, act_a=0.0,
+               act_b=0.0):
+    """Routed layer with host activations/routing and device-resident weights.
+
+    ``tables`` holds six sequences of device addresses (ints): g, u, d, gs, us, ds.
+    """
+    arrs = [(C.c_void_p * len(t))(*t) for t in tables]
+    _check(lib().mvllm_moe_layer_host(T, K, E, n_shared, D, Iinter, fmt, _p(idx), _p(wt), _p(x),
+                                      *arrs, _p(out), act, act_a, act_b))
+
+
+# -------------------------------------------------------------- device path --
+def _dp(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream)
+
+
+def layer_workspace_bytes(T, K, E, n_shared, D, Iinter, fmt) -> int:
+    return lib().mvllm_moe_layer_workspace(T, K, E, n_shared, D, Iinter, fmt)
+
+
+def layer_dev(T, K, E, n_shared, D, Iinter, fmt, idx, wt, x, tables, out, act, act_a, act_b,
+              workspace, stream=None):
+    """Routed layer on device tensors; ``tables`` = six int64 CUDA tensors of addresses."""
+    x_dtype = DTYPE_BF16 if str(x.dtype) == "torch.bfloat16" else DTYPE_F32
+    _check(lib().mvllm_moe_layer_dev(_stream(stream), T, K, E, n_shared, D, Iinter, fmt, _dp(idx),
+                                     _dp(wt), _dp(x), x_dtype, *[_dp(t) for t in tables],
+                                     _dp(out), act, act_a, act_b, _dp(workspace),
+                                     workspace.numel() * workspace.element_size()))
+
+
+def block_dev_workspace_bytes(nb, D, Iinter, fmt, rows_cap, x_rows, S) -> int:
+    return lib().mvllm_moe_block_dev_workspace(nb, D, Iinter, fmt, rows_cap, x_rows, S)
+
+
+def block_dev(nb, D, Iinter, fmt, tables, x, x_rows, xoff, nr, rows, rw, out, S, act, act_a,
+              act_b, rows_cap, workspace, stream=None):
+    x_dtype = DTYPE_BF16 if str(x.dtype) == "torch.bfloat16" else DTYPE_F32
+    _check(lib().mvllm_moe_block_dev(_stream(stream), nb, D, Iinter, fmt,
+                                     *[_dp(t) for t in tables], _dp(x), x_dtype, x_rows,
+                                     _dp(xoff), _dp(nr), _dp(rows), _dp(rw), _dp(out), S, act,
+                                     act_a, act_b, rows_cap, _dp(workspace),
+                                     workspace.numel() * workspace.element_size()))
+
+
+def permute_workspace_bytes(T, K, E, n_shared) -> int:
+    return lib().mvllm_moe_permute_workspace(T, K, E, n_shared)
+
+
+def permute_dev(idx, wt, E, n_shared, nr, xoff, rows, rw, tok_pos, n_rows, workspace,
+                stream=None):
+    T, K = idx.shape
+    _check(lib().mvllm_moe_permute_dev(_stream(stream), _dp(idx), _dp(wt), T, K, E, n_shared,
+                                       _dp(nr), _dp(xoff), _dp(rows), _dp(rw), _dp(tok_pos),
+                                       _dp(n_rows), _dp(workspace),
+                                       workspace.numel() * workspace.element_size()))
+
+
+def quantize_int4_g64_dev(w, packed, scales, stream=None):
+    O, I = w.shape
+    _check(lib().mvllm_quantize_int4_g64_dev(_stream(stream), _dp(w), O, I, _dp(packed),
+                                             _dp(scales)))
+
+
+def pack_mxfp4_dev(w, packed, scales, stream=None):
+    O, I = w.shape
+    _check(lib().mvllm_pack_mxfp4_dev(_stream(stream), _dp(w), O, I, _dp(packed), _dp(scales)))
+
+
+def matmul_dev(fmt, y, x, w, scales, stream=None):
+    S, I = x.shape
+    O = y.shape[1]
+    _check(lib().mvllm_matmul_dev(_stream(stream), fmt, _dp(y), _dp(x), _dp(w), _dp(scales), S,
+                                  I, O))

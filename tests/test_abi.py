@@ -1,0 +1,100 @@
+"""The C-ABI library: it loads, exports every symbol include/*.h declares, and
+its host-side argument checks behave as the reference's (no GPU needed)."""
+import ctypes as C
+import os
+import re
+import shutil
+import subprocess
+
+import numpy as np
+import pytest
+
+import build as mvbuild
+import cases
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    mvbuild.build()
+    import mvllm_moe
+    return mvllm_moe
+
+
+def header_symbols():
+    with open(os.path.join(ROOT, "include", "mvllm_moe.h")) as f:
+        text = f.read()
+    return sorted(set(re.findall(r"MVLLM_API [^;(]*?\b(mvllm_\w+)\(", text)))
+
+
+def test_exports_every_declared_symbol(lib):
+    declared = header_symbols()
+    assert len(declared) >= 20
+    assert set(declared) == set(lib.C_SYMBOLS)
+    L = C.CDLL(lib.LIB_PATH)
+    for name in declared:
+        assert hasattr(L, name), name
+
+
+def test_cpp_adapter_symbol_matches_reference_signature(lib):
+    """The library exports metal_ops::moe_block with the reference's mangled name."""
+    out = subprocess.run(["nm", "-D", "--defined-only", lib.LIB_PATH], capture_output=True,
+                         text=True).stdout
+    ours = [l.split()[-1] for l in out.splitlines() if "metal_ops9moe_block" in l]
+    assert len(ours) == 1
+    ref_hdr = "/root/reference/src/gpu/metal_ops.hpp"
+    if not os.path.exists(ref_hdr) or not shutil.which("g++"):
+        pytest.skip("reference header not present")
+    src = ('#include "%s"\nvoid f(){mvllm::metal_ops::moe_block(0,0,0,0,0,0,0,0,0,0,0,0,0,0,0,'
+           '0,0,0);}\n' % ref_hdr)
+    tmp = os.path.join(ROOT, "_work", "abi_probe")
+    os.makedirs(tmp, exist_ok=True)
+    with open(os.path.join(tmp, "p.cpp"), "w") as f:
+        f.write(src)
+    subprocess.run(["g++", "-std=c++17", "-c", os.path.join(tmp, "p.cpp"), "-o",
+                    os.path.join(tmp, "p.o")], check=True)
+    und = subprocess.run(["nm", "-u", os.path.join(tmp, "p.o")], capture_output=True,
+                         text=True).stdout
+    assert ours[0] in und
+
+
+def test_invalid_arguments_rejected_without_gpu(lib):
+    """metal_ops.cpp:452-457 argument checks return false before any device work."""
+    c = cases.kat_identity(cases.ACT_SILU, 0.0)
+    out = np.zeros((1, 4), np.float32)
+    args = dict(g=c["g"], u=c["u"], d=c["d"], gs=None, us=None, ds=None, xg=c["xg"],
+                xoff=c["xoff"], nr=c["nr"], rows=c["rows"], rw=c["rw"], out=out, S=1)
+    assert lib.moe_block(0, 4, 4, 0, **args) is False
+    assert lib.moe_block(1, 0, 4, 0, **args) is False
+    assert lib.moe_block(1, 4, 4, 3, **args) is False
+    bad = dict(args, xoff=None)
+    assert lib.moe_block(1, 4, 4, 0, **bad) is False
+    bad = dict(args, xg=None)
+    assert lib.moe_block(1, 4, 4, 0, **bad) is False
+
+
+def test_backend_identity_and_uninitialised_errors(lib):
+    assert lib.backend_name() == "cuda-sm100a"
+    if lib.available():
+        pytest.skip("library already initialised in this process")
+    c = cases.kat_identity(cases.ACT_SILU, 0.0)
+    out = np.zeros((1, 4), np.float32)
+    with pytest.raises(lib.MoeError) as ei:
+        lib.moe_block(1, 4, 4, 0, c["g"], c["u"], c["d"], None, None, None, c["xg"], c["xoff"],
+                      c["nr"], c["rows"], c["rw"], out, 1)
+    assert ei.value.code == lib.ERR_NOT_INIT
+    assert lib.lib().mvllm_moe_block_dev_workspace(0, 4, 4, 0, 1, 1, 1) == 0
+    assert lib.lib().mvllm_moe_layer_workspace(4, 2, 8, 0, 512, 512, 7) > 0
+
+
+def test_init_without_gpu_reports_error(lib):
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except ImportError:
+        pass
+    rc = lib.lib().mvllm_moe_init(0)
+    assert rc in (lib.ERR_CUDA, lib.ERR_INVALID)
+    assert lib.last_error()
