@@ -127,6 +127,27 @@ MVLLM_API int mvllm_moe_permute_dev(void *stream, const int *idx, const float *w
                           int n_shared, int *nr, int *xoff, int *rows, float *rw, int *tok_pos,
                           int *n_rows, void *workspace, size_t workspace_bytes);
 
+/* The permutation above with no workspace argument and no allocation at
+ * all.  No counterpart in the reference: it exists for callers that cannot
+ * allocate device memory when they need the permutation -- code inside a CUDA
+ * graph capture (cudaMalloc would break the capture), engines that fix their
+ * HBM budget at start-up and forbid allocation in the decode loop, and
+ * plugins whose host process owns the GPU allocator.  The scratch (bitmap and
+ * per-token weight sums) is a file-scope __device__ array of
+ * MVLLM_PERMUTE_STATIC_BYTES that every GPU loading the library keeps until
+ * the process exits.  Sizes whose mvllm_moe_permute_workspace() exceeds it
+ * are rejected with MVLLM_ERR_WORKSPACE (e.g. T=8192, K=8, E=384 fits).  The
+ * first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture.  All calls share the one array: calls whose executions overlap
+ * on the GPU (different streams, or graphs replayed concurrently) race.
+ * Outputs, ordering and error codes are those of mvllm_moe_permute_dev; does
+ * not require mvllm_moe_init. */
+#define MVLLM_PERMUTE_STATIC_BYTES (1u << 20)
+MVLLM_API int mvllm_moe_permute_dev_noalloc(void *stream, const int *idx, const float *wt, int T,
+                                            int K, int E, int n_shared, int *nr, int *xoff,
+                                            int *rows, float *rw, int *tok_pos, int *n_rows);
+
 /* A whole routed MoE layer on device, as moe_layer_n's routed part
  * (src/model/glm53.cpp:1936-1994, src/model/kimi_k3.cpp:2024-2075) plus an
  * optional always-on shared expert: permute -> expert FFN -> ordered combine

@@ -909,6 +909,72 @@ int mvllm_moe_permute_dev(void *stream, const int *idx, const float *wt, int T, 
                        xoff, rows, rw, tok_pos, n_rows, p);
 }
 
+// ------------------------------------------------ permutation, no allocation --
+// Some callers cannot allocate device memory at the moment they need the
+// permutation: code running while a CUDA graph is being captured (cudaMalloc
+// is not a stream operation and breaks the capture), engines that partition
+// HBM once at start-up and forbid allocation in the decode loop, and plugins
+// living inside a host process whose allocator owns the GPU.  For them
+// mvllm_moe_permute_dev_noalloc keeps its scratch (membership bitmap and
+// per-token weight sums) in this file-scope device array.  Every GPU that
+// loads the library holds it until the process exits.
+namespace {
+constexpr size_t kPermuteStaticBytes = MVLLM_PERMUTE_STATIC_BYTES;
+__device__ __align__(256) uint8_t g_permute_scratch[kPermuteStaticBytes];
+
+struct StaticScratch {
+    void *ptr = nullptr;
+    int sms = 0;
+};
+std::mutex g_static_mu;
+std::map<int, StaticScratch> g_static_by_device;
+
+// Device address of g_permute_scratch on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address comes from
+// cudaGetSymbolAddress, once per device, with that device current.
+int static_scratch(StaticScratch *out) {
+    int dev = -1;
+    CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    auto it = g_static_by_device.find(dev);
+    if (it == g_static_by_device.end()) {
+        StaticScratch s;
+        const cudaError_t e = cudaGetSymbolAddress(&s.ptr, g_permute_scratch);
+        if (e != cudaSuccess || !s.ptr)
+            return fail(MVLLM_ERR_CUDA, "cudaGetSymbolAddress(g_permute_scratch) on device %d: %s",
+                        dev, cudaGetErrorString(e));
+        CUDA_TRY(cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, dev));
+        it = g_static_by_device.emplace(dev, s).first;
+    }
+    *out = it->second;
+    return MVLLM_OK;
+}
+} // namespace
+
+int mvllm_moe_permute_dev_noalloc(void *stream, const int *idx, const float *wt, int T, int K,
+                                  int E, int n_shared, int *nr, int *xoff, int *rows, float *rw,
+                                  int *tok_pos, int *n_rows) {
+    if (!idx || !wt || T < 1 || K < 1 || E < 1 || n_shared < 0 || n_shared > 1 || !nr || !xoff ||
+        !rows || !rw || !tok_pos || !n_rows)
+        return fail(MVLLM_ERR_INVALID, "permute_dev_noalloc: invalid arguments");
+    const size_t need = mvllm_moe_permute_workspace(T, K, E, n_shared);
+    if (need > kPermuteStaticBytes)
+        return fail(MVLLM_ERR_WORKSPACE,
+                    "permute_dev_noalloc: T=%d K=%d E=%d n_shared=%d needs %zu bytes of scratch, "
+                    "above the %zu-byte static maximum; use mvllm_moe_permute_dev",
+                    T, K, E, n_shared, need, kPermuteStaticBytes);
+    StaticScratch s;
+    if (int rc = static_scratch(&s))
+        return rc;
+    Carve cv(s.ptr, kPermuteStaticBytes);
+    PermWs p{};
+    carve_perm(cv, p, T, K, E, n_shared);
+    // run_permute clears the bitmap before use (the array keeps the previous
+    // call's contents); the weight sums are written before they are read.
+    return run_permute(static_cast<cudaStream_t>(stream), s.sms, idx, wt, T, K, E, n_shared, nr,
+                       xoff, rows, rw, tok_pos, n_rows, p);
+}
+
 // ----------------------------------------------------------------- layer --
 namespace {
 struct LayerWs {

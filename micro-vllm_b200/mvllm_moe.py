@@ -36,6 +36,7 @@ C_SYMBOLS = (
     "mvllm_moe_permute_dev", "mvllm_moe_layer_workspace", "mvllm_moe_layer_dev",
     "mvllm_moe_layer_host", "mvllm_quantize_int4_g64_dev", "mvllm_pack_mxfp4_dev",
     "mvllm_matmul_dev", "mvllm_moe_profile_enable", "mvllm_moe_profile_read",
+    "mvllm_moe_permute_dev_noalloc",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -83,6 +84,7 @@ def lib():
             "mvllm_matmul_dev": (i, [vp, i, vp, vp, vp, vp, i, i, i]),
             "mvllm_moe_profile_enable": (None, [i]),
             "mvllm_moe_profile_read": (i, [vp, vp, i]),
+            "mvllm_moe_permute_dev_noalloc": (i, [vp, vp, vp, i, i, i, i] + [vp] * 6),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
