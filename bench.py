@@ -43,6 +43,9 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--experts", type=int, default=256,
+                    help="routed experts (BASELINE config[1]: 256); fewer only to size a "
+                         "profiler capture")
     return ap.parse_args()
 
 
@@ -300,6 +303,7 @@ def main():
     mvbuild.build()
     import mvllm_moe as moe
 
+    CFG["E"] = args.experts
     rank, local_rank, world = dist_env()
     torch.cuda.set_device(local_rank)
     if world > 1:

@@ -122,6 +122,38 @@ __global__ void plan_kernel(const PlanArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Per-expert tensor maps for the decode kernels: each is a host-encoded
+// template (shape, strides, box, swizzle) with the global address swapped in
+// on the device (tensormap.replace), so the device-pointer entries need no
+// host copy of the expert tables.  Maps of null pointers keep the template
+// address; the plan never schedules those experts.
+constexpr int kTmapsPerExpert = 6; // gate, up, down packed rows; gate, up, down scales
+struct TmapTemplates {
+    CUtensorMap m[kTmapsPerExpert];
+};
+
+__global__ void build_tmaps_kernel(const __grid_constant__ TmapTemplates tpl,
+                                   const void *const *g, const void *const *u,
+                                   const void *const *d, const void *const *gs,
+                                   const void *const *us, const void *const *ds, int nb,
+                                   uint8_t *__restrict__ out) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= nb * kTmapsPerExpert)
+        return;
+    const int e = idx / kTmapsPerExpert, k = idx % kTmapsPerExpert;
+    const void *const *tabs[kTmapsPerExpert] = {g, u, d, gs, us, ds};
+    const void *src = tabs[k] ? tabs[k][e] : nullptr;
+    uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<size_t>(idx) * 128);
+    const uint4 *from = reinterpret_cast<const uint4 *>(&tpl.m[k]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        dst[i] = from[i];
+    if (src)
+        tmap_replace_address(dst, src);
+    tmap_release();
+}
+
+// ---------------------------------------------------------------------------
 // Operand staging: rows of x (f32 or bf16, row length D) into f16 rows in the
 // column order of the format (stage_pos), or into plain f32 rows.  With
 // `index`, output row r reads input row index[r] (the permutation gather).
@@ -145,6 +177,50 @@ __global__ void stage_rows_kernel(const TIn *__restrict__ x, const int *__restri
             else
                 orow[stage_pos(k, fmt)] = __float2half_rn(v);
         }
+    }
+}
+
+// Vectorised form for the fast path (D % 8 == 0): one thread per aligned
+// 8-column chunk, 16-byte stores of f16 in stage_pos order.
+template <typename TIn>
+__global__ void stage_rows_f16x8_kernel(const TIn *__restrict__ x, const int *__restrict__ index,
+                                        const int *__restrict__ nrows_dev, int nrows_host, int D,
+                                        int fmt, __half *__restrict__ out) {
+    const int nrows = nrows_dev ? *nrows_dev : nrows_host;
+    const int chunks = D >> 3;
+    const size_t total = static_cast<size_t>(nrows) * chunks;
+    for (size_t id = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; id < total;
+         id += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int r = static_cast<int>(id / chunks), c = static_cast<int>(id % chunks);
+        const int src = index ? index[r] : r;
+        float v[8];
+        if constexpr (sizeof(TIn) == 4) {
+            const float4 *p = reinterpret_cast<const float4 *>(x + static_cast<size_t>(src) * D) +
+                              2 * c;
+            const float4 a = p[0], b = p[1];
+            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+            v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+        } else {
+            const uint4 a = *(reinterpret_cast<const uint4 *>(x + static_cast<size_t>(src) * D) + c);
+            const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[2 * j] = __uint_as_float(w[j] << 16);
+                v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+            }
+        }
+        __half2 h[4];
+        if (fmt == MVLLM_FMT_INT4_G64) { // k0,k4,k1,k5,k2,k6,k3,k7
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                h[j] = __floats2half2_rn(v[j], v[j + 4]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+        }
+        *(reinterpret_cast<uint4 *>(out + static_cast<size_t>(r) * D) + c) =
+            *reinterpret_cast<const uint4 *>(h);
     }
 }
 

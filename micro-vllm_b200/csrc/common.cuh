@@ -7,6 +7,7 @@
 // false, so a broken pipeline ends the kernel instead of hanging the GPU.
 #pragma once
 
+#include <cuda.h> // CUtensorMap (header only; the driver entry point is fetched at run time)
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -112,6 +113,51 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
                  : "memory");
+}
+
+// 16-byte Ampere-style async copy global -> shared (L2 only, bypassing L1).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+
+// One arrival on `bar` once every cp.async this thread issued before has
+// landed (the barrier's expected count must include this arrival).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
+// ---- tensor TMA (2-D tiles, never multicast) -------------------------------
+// Box load described by a tensor map in global or param space; x is the
+// innermost coordinate (its byte offset must be a multiple of 16).
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y,
+                                            uint64_t *bar, uint64_t policy) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes"
+                 ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+                 "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+                 : "memory");
+}
+
+// Writer side of a device-built tensor map: swap the global address of a
+// 128-byte map in global memory, then release it to the tensormap proxy.
+__device__ __forceinline__ void tmap_replace_address(void *tmap, const void *addr) {
+    asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;" ::"l"(tmap),
+                 "l"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void tmap_release() {
+    asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
+}
+// Reader side: acquire a map written through the generic proxy before use.
+__device__ __forceinline__ void tmap_acquire(const void *tmap) {
+    asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(tmap) : "memory");
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {

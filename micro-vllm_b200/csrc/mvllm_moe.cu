@@ -6,6 +6,8 @@
 #include "aux_kernels.cuh"
 #include "decode_ffn.cuh"
 
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <chrono>
 #include <cstdarg>
@@ -176,11 +178,15 @@ bool fast_path_ok(int fmt, int D, int I) {
     return D >= 512 && I >= 512 && D % 512 == 0 && I % 512 == 0;
 }
 
-int chunk_tiles(int max_rows) { return max_rows <= 8 ? 1 : (max_rows <= 16 ? 2 : 4); }
+// Token tiles per item: 8 tokens, or 16 when experts average more than 8
+// rows (prefill-like); experts with more rows are split into chunks, whose
+// items run back to back so the repeated weight rows come from L2.
+int chunk_tiles(int avg_rows) { return avg_rows > 8 ? 2 : 1; }
 int pick_ks(int K) { return ((K / 2) % 512 == 0) ? 512 : 256; }
 
 struct RunWs {
     int *base, *cnt, *off1, *off2, *total_rows, *err;
+    uint8_t *tmaps; // fast path: [nb][6] tensor maps
     void *xs; // staged operand (fast: f16, generic: f32)
     void *h;  // fast: f16 [rows, I]; generic: f32 [rows, I]
     float *y; // [rows, D]
@@ -195,6 +201,7 @@ void carve_run(Carve &cv, RunWs &w, int nb, int D, int I, bool fast, int rows_ca
     w.off2 = cv.take<int>(nb + 1);
     w.total_rows = cv.take<int>(1);
     w.err = cv.take<int>(1);
+    w.tmaps = fast ? cv.take<uint8_t>(size_t(nb) * kTmapsPerExpert * 128) : nullptr;
     const size_t esz = fast ? 2 : 4;
     w.xs = cv.take<uint8_t>(size_t(std::max(x_rows, 1)) * D * esz);
     w.h = cv.take<uint8_t>(size_t(std::max(rows_cap, 1)) * I * esz);
@@ -205,9 +212,67 @@ struct Tables {
     const void *const *g, *const *u, *const *d, *const *gs, *const *us, *const *ds;
 };
 
+// ---------------------------------------------------------- tensor maps --
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// 2-D map over a row-major [rows, inner] matrix; box = box_inner x box_rows.
+int encode_2d(CUtensorMap *m, CUtensorMapDataType dt, void *addr, uint64_t inner, uint64_t rows,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
+    auto enc = tmap_encoder();
+    if (!enc)
+        return fail(MVLLM_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(m, dt, 2, addr, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(MVLLM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    return MVLLM_OK;
+}
+
+// Templates for one (fmt, D, I) shape: phase-1 boxes are 32 rows (gate and up
+// halves of an item), phase-2 boxes 64 rows; weights use the 128-byte swizzle
+// the decode consumers read through, scales are dense.
+int make_templates(TmapTemplates *t, int fmt, int D, int I, int ks1, int ks2, void *placeholder) {
+    const bool mx = fmt == MVLLM_FMT_MXFP4;
+    const auto u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8, f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const auto sw = CU_TENSOR_MAP_SWIZZLE_128B, none = CU_TENSOR_MAP_SWIZZLE_NONE;
+    int rc = 0;
+    rc |= encode_2d(&t->m[0], u8, placeholder, D / 2, I, D / 2, 128, 32, sw);
+    rc |= encode_2d(&t->m[1], u8, placeholder, D / 2, I, D / 2, 128, 32, sw);
+    rc |= encode_2d(&t->m[2], u8, placeholder, I / 2, D, I / 2, 128, 64, sw);
+    const int sb1 = mx ? ks1 / 16 : ks1 / 8, sb2 = mx ? ks2 / 16 : ks2 / 8; // bytes per row
+    if (mx) {
+        rc |= encode_2d(&t->m[3], u8, placeholder, D / 32, I, D / 32, sb1, 32, none);
+        rc |= encode_2d(&t->m[4], u8, placeholder, D / 32, I, D / 32, sb1, 32, none);
+        rc |= encode_2d(&t->m[5], u8, placeholder, I / 32, D, I / 32, sb2, 64, none);
+    } else {
+        rc |= encode_2d(&t->m[3], f32, placeholder, D / 64, I, D / 16, sb1 / 4, 32, none);
+        rc |= encode_2d(&t->m[4], f32, placeholder, D / 64, I, D / 16, sb1 / 4, 32, none);
+        rc |= encode_2d(&t->m[5], f32, placeholder, I / 64, D, I / 16, sb2 / 4, 64, none);
+    }
+    return rc ? MVLLM_ERR_CUDA : MVLLM_OK;
+}
+
 template <int FMT, int PHASE, int KS, int NT>
 int launch_decode_t(DecodeArgs a, cudaStream_t st, int sms) {
-    using L = DecodeLayout<KS, NT>;
+    using L = DecodeLayout<FMT, KS, NT>;
     auto kern = decode_ffn_kernel<FMT, PHASE, KS, NT>;
     static int budget_kb = [] {
         const char *s = getenv("MVLLM_DECODE_SMEM_KB");
@@ -231,18 +296,11 @@ int launch_decode_t(DecodeArgs a, cudaStream_t st, int sms) {
 
 template <int FMT, int PHASE>
 int launch_decode(const DecodeArgs &a, int ks, int nt, cudaStream_t st, int sms) {
-    if (ks == 512) {
-        if (nt == 1)
-            return launch_decode_t<FMT, PHASE, 512, 1>(a, st, sms);
-        if (nt == 2)
-            return launch_decode_t<FMT, PHASE, 512, 2>(a, st, sms);
-        return launch_decode_t<FMT, PHASE, 512, 4>(a, st, sms);
-    }
-    if (nt == 1)
-        return launch_decode_t<FMT, PHASE, 256, 1>(a, st, sms);
-    if (nt == 2)
-        return launch_decode_t<FMT, PHASE, 256, 2>(a, st, sms);
-    return launch_decode_t<FMT, PHASE, 256, 4>(a, st, sms);
+    if (ks == 512)
+        return nt == 1 ? launch_decode_t<FMT, PHASE, 512, 1>(a, st, sms)
+                       : launch_decode_t<FMT, PHASE, 512, 2>(a, st, sms);
+    return nt == 1 ? launch_decode_t<FMT, PHASE, 256, 1>(a, st, sms)
+                   : launch_decode_t<FMT, PHASE, 256, 2>(a, st, sms);
 }
 
 // The expert FFN over nb experts: plan, optional operand staging, phase 1,
@@ -251,9 +309,9 @@ int launch_decode(const DecodeArgs &a, int ks, int nt, cudaStream_t st, int sms)
 // on the fast path, f32 on the generic path) indexed by xoff.
 int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const Tables &tb,
                 const int *nr, const int *xoff, const void *x, int x_dtype, int x_rows,
-                bool x_staged, int max_rows, int act, float act_a, float act_b, RunWs &w) {
+                bool x_staged, int avg_rows, int act, float act_a, float act_b, RunWs &w) {
     const bool fast = fast_path_ok(fmt, D, I);
-    const int nt = chunk_tiles(max_rows);
+    const int nt = chunk_tiles(avg_rows);
     const int mt = 8 * nt;
     PlanArgs pa{};
     pa.nb = nb;
@@ -277,12 +335,13 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     const void *xop = x;
     if (!x_staged) {
         if (fast) {
+            const int blocks = std::max(1, std::min((x_rows * (D / 8) + 255) / 256, 8 * sms));
             if (x_dtype == MVLLM_DTYPE_BF16)
-                stage_rows_kernel<__nv_bfloat16, __half><<<std::max(1, std::min(x_rows, 4 * sms)), 256, 0, st>>>(
+                stage_rows_f16x8_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
                     static_cast<const __nv_bfloat16 *>(x), nullptr, nullptr, x_rows, D, fmt,
                     static_cast<__half *>(w.xs));
             else
-                stage_rows_kernel<float, __half><<<std::max(1, std::min(x_rows, 4 * sms)), 256, 0, st>>>(
+                stage_rows_f16x8_kernel<float><<<blocks, 256, 0, st>>>(
                     static_cast<const float *>(x), nullptr, nullptr, x_rows, D, fmt,
                     static_cast<__half *>(w.xs));
             CUDA_TRY(cudaGetLastError());
@@ -297,8 +356,16 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     }
 
     if (fast) {
+        // Per-expert tensor maps: host templates, device-side address swap.
+        TmapTemplates tpl;
+        if (int rc = make_templates(&tpl, fmt, D, I, pick_ks(D), pick_ks(I), w.y))
+            return rc;
+        const int nmaps = nb * kTmapsPerExpert;
+        build_tmaps_kernel<<<(nmaps + 127) / 128, 128, 0, st>>>(tpl, tb.g, tb.u, tb.d, tb.gs,
+                                                               tb.us, tb.ds, nb, w.tmaps);
+        CUDA_TRY(cudaGetLastError());
         DecodeArgs a{};
-        a.w0 = tb.g, a.w1 = tb.u, a.s0 = tb.gs, a.s1 = tb.us;
+        a.tmaps = w.tmaps;
         a.xrow = xoff, a.orow = w.base, a.cnt = w.cnt, a.item_off = w.off1, a.nb = nb;
         a.x = static_cast<const __half *>(xop);
         a.K = D, a.O = I, a.out = w.h;
@@ -310,7 +377,6 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             return rc;
         prof_mark(st, kPhExpert1);
         DecodeArgs b = a;
-        b.w0 = tb.d, b.w1 = nullptr, b.s0 = tb.ds, b.s1 = nullptr;
         b.xrow = w.base, b.item_off = w.off2;
         b.x = static_cast<const __half *>(w.h);
         b.K = I, b.O = D, b.out = w.y;
@@ -590,7 +656,7 @@ int mvllm_moe_block(int nb, int D, int Iinter, int fmt, int qgs, const void *con
 
     // Host pass over experts: cpu_moe_block's base/skip rules.
     const bool packed = fmt != MVLLM_FMT_F32;
-    int R = 0, n_valid = 0, max_rows = 0;
+    int R = 0, n_valid = 0;
     int64_t x_rows = 0;
     std::vector<int> base(nb), valid(nb);
     for (int e = 0; e < nb; ++e) {
@@ -607,7 +673,6 @@ int mvllm_moe_block(int nb, int D, int Iinter, int fmt, int qgs, const void *con
                 return fail(MVLLM_ERR_INVALID, "moe_block: negative xoff for expert %d", e);
             valid[e] = 1;
             ++n_valid;
-            max_rows = std::max(max_rows, n);
             x_rows = std::max<int64_t>(x_rows, int64_t(xoff[e]) + n);
         }
         R += n;
@@ -746,13 +811,13 @@ int mvllm_moe_block(int nb, int D, int Iinter, int fmt, int qgs, const void *con
     int rc;
     if (fast) {
         rc = run_experts(c.stream, c.sms, nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
-                         MVLLM_DTYPE_F32, int(x_rows), false, max_rows, act, act_a, act_b, w);
+                         MVLLM_DTYPE_F32, int(x_rows), false, R / n_valid, act, act_a, act_b, w);
     } else {
         // Generic path reads the uploaded f32 rows directly.
         RunWs w2 = w;
         w2.xs = const_cast<float *>(d_x);
         rc = run_experts(c.stream, c.sms, nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
-                         MVLLM_DTYPE_F32, int(x_rows), true, max_rows, act, act_a, act_b, w2);
+                         MVLLM_DTYPE_F32, int(x_rows), true, R / n_valid, act, act_a, act_b, w2);
     }
     if (rc)
         return rc;
@@ -838,7 +903,7 @@ int mvllm_moe_block_dev(void *stream, int nb, int D, int Iinter, int fmt, const 
     Tables tb{g, u, d, gs, us, ds};
     const bool staged = !fast && x_dtype == MVLLM_DTYPE_F32;
     int rc = run_experts(st, sms, nb, D, Iinter, fmt, tb, nr, xoff, x, x_dtype, x_rows, staged,
-                         rows_cap, act, act_a, act_b, w);
+                         rows_cap / nb, act, act_a, act_b, w);
     if (rc)
         return rc;
     build_csr_kernel<<<1, 1024, 0, st>>>(rows, w.base, w.cnt, nb, w.total_rows, S, hist, off, ids);
@@ -1021,12 +1086,13 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
     // Gather + stage the token rows into expert-major order.
     const int gblocks = std::min(R, 8 * sms);
     if (fast) {
+        const int vblocks = std::max(1, std::min((R * (D / 8) + 255) / 256, 8 * sms));
         if (x_dtype == MVLLM_DTYPE_BF16)
-            stage_rows_kernel<__nv_bfloat16, __half><<<gblocks, 256, 0, st>>>(
+            stage_rows_f16x8_kernel<__nv_bfloat16><<<vblocks, 256, 0, st>>>(
                 static_cast<const __nv_bfloat16 *>(x), l.rows, l.n_rows, 0, D, fmt,
                 static_cast<__half *>(l.run.xs));
         else
-            stage_rows_kernel<float, __half><<<gblocks, 256, 0, st>>>(
+            stage_rows_f16x8_kernel<float><<<vblocks, 256, 0, st>>>(
                 static_cast<const float *>(x), l.rows, l.n_rows, 0, D, fmt,
                 static_cast<__half *>(l.run.xs));
     } else {
@@ -1043,7 +1109,7 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
     prof_mark(st, kPhGather);
     RunWs w = l.run;
     if (int rc = run_experts(st, sms, EE, D, Iinter, fmt, tb, l.nr, l.xoff, l.run.xs,
-                             MVLLM_DTYPE_F32, R, true, T, act, act_a, act_b, w))
+                             MVLLM_DTYPE_F32, R, true, R / EE, act, act_a, act_b, w))
         return rc;
     dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
     combine_tokens_kernel<<<grid, 256, 0, st>>>(out, w.y, l.rw, l.tok_pos, T, KK, D);
