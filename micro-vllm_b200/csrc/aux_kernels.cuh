@@ -126,7 +126,10 @@ __global__ void plan_kernel(const PlanArgs a) {
 // template (shape, strides, box, swizzle) with the global address swapped in
 // on the device (tensormap.replace), so the device-pointer entries need no
 // host copy of the expert tables.  Maps of null pointers keep the template
-// address; the plan never schedules those experts.
+// address; the plan never schedules those experts.  A map is rewritten only
+// when its bytes change, and any rewrite raises *dirty, which tells the
+// decode kernels to acquire maps through the tensormap proxy before use; with
+// static weights the maps never change and no fence is needed.
 constexpr int kTmapsPerExpert = 6; // gate, up, down packed rows; gate, up, down scales
 struct TmapTemplates {
     CUtensorMap m[kTmapsPerExpert];
@@ -136,7 +139,7 @@ __global__ void build_tmaps_kernel(const __grid_constant__ TmapTemplates tpl,
                                    const void *const *g, const void *const *u,
                                    const void *const *d, const void *const *gs,
                                    const void *const *us, const void *const *ds, int nb,
-                                   uint8_t *__restrict__ out) {
+                                   uint8_t *__restrict__ out, int *dirty) {
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= nb * kTmapsPerExpert)
         return;
@@ -144,13 +147,31 @@ __global__ void build_tmaps_kernel(const __grid_constant__ TmapTemplates tpl,
     const void *const *tabs[kTmapsPerExpert] = {g, u, d, gs, us, ds};
     const void *src = tabs[k] ? tabs[k][e] : nullptr;
     uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<size_t>(idx) * 128);
+    // The wanted map in registers: template with the address swapped in.
+    __shared__ __align__(128) uint8_t staged[128 * 128];
+    uint4 *mine = reinterpret_cast<uint4 *>(staged + threadIdx.x * 128);
     const uint4 *from = reinterpret_cast<const uint4 *>(&tpl.m[k]);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-        dst[i] = from[i];
+        mine[i] = from[i];
     if (src)
-        tmap_replace_address(dst, src);
-    tmap_release();
+        asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(
+                         smem_u32(mine)),
+                     "l"(src)
+                     : "memory");
+    bool same = true;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint4 a = mine[i], b = dst[i];
+        same &= (a.x == b.x) & (a.y == b.y) & (a.z == b.z) & (a.w == b.w);
+    }
+    if (!same) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            dst[i] = mine[i];
+        tmap_release();
+        atomicExch(dirty, 1);
+    }
 }
 
 // ---------------------------------------------------------------------------

@@ -237,14 +237,33 @@ __device__ __forceinline__ void int4x8_to_f16x8(uint32_t w, uint32_t &h0, uint32
 __device__ __forceinline__ float ue8m0_to_f32(uint32_t s) { return __uint_as_float(s << 23); }
 
 // ---- warp-level MMA (m16n8k16, f16 in, f32 accumulate) ------------------------
+// Not volatile: a pure function of its operands, so the compiler may
+// interleave it with the next group's loads and conversions.
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
                                               uint32_t a2, uint32_t a3, uint32_t b0,
                                               uint32_t b1, const float (&c)[4]) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
                  "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
                  : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
                    "f"(c[2]), "f"(c[3]));
+}
+
+// d0,d1 += a0,a1 * s with one packed f32x2 FMA (sm_100).
+__device__ __forceinline__ void ffma2(float &d0, float &d1, float a0, float a1, float s) {
+    asm("{\n\t.reg .b64 acc, av, sv;\n\t"
+        "mov.b64 acc, {%0, %1};\n\t"
+        "mov.b64 av, {%2, %3};\n\t"
+        "mov.b64 sv, {%4, %4};\n\t"
+        "fma.rn.f32x2 acc, av, sv, acc;\n\t"
+        "mov.b64 {%0, %1}, acc;\n\t}\n"
+        : "+f"(d0), "+f"(d1)
+        : "f"(a0), "f"(a1), "f"(s));
+}
+
+// Byte k of w as a ue8m0 scale (2^(b-127), the reference's decoding).
+__device__ __forceinline__ float ue8m0_byte(uint32_t w, int k) {
+    return __uint_as_float(__byte_perm(w, 0u, 0x4440u | static_cast<uint32_t>(k)) << 23);
 }
 
 // ---- activations (metal_ops.cpp:197-211, quant.hpp:22-50) ---------------------

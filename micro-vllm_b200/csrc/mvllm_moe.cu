@@ -186,7 +186,8 @@ int pick_ks(int K) { return ((K / 2) % 512 == 0) ? 512 : 256; }
 
 struct RunWs {
     int *base, *cnt, *off1, *off2, *total_rows, *err;
-    uint8_t *tmaps; // fast path: [nb][6] tensor maps
+    int *tmaps_dirty; // set when build_tmaps_kernel rewrote a map this call
+    uint8_t *tmaps;   // fast path: [nb][6] tensor maps
     void *xs; // staged operand (fast: f16, generic: f32)
     void *h;  // fast: f16 [rows, I]; generic: f32 [rows, I]
     float *y; // [rows, D]
@@ -201,6 +202,7 @@ void carve_run(Carve &cv, RunWs &w, int nb, int D, int I, bool fast, int rows_ca
     w.off2 = cv.take<int>(nb + 1);
     w.total_rows = cv.take<int>(1);
     w.err = cv.take<int>(1);
+    w.tmaps_dirty = cv.take<int>(1);
     w.tmaps = fast ? cv.take<uint8_t>(size_t(nb) * kTmapsPerExpert * 128) : nullptr;
     const size_t esz = fast ? 2 : 4;
     w.xs = cv.take<uint8_t>(size_t(std::max(x_rows, 1)) * D * esz);
@@ -276,7 +278,7 @@ int launch_decode_t(DecodeArgs a, cudaStream_t st, int sms) {
     auto kern = decode_ffn_kernel<FMT, PHASE, KS, NT>;
     static int budget_kb = [] {
         const char *s = getenv("MVLLM_DECODE_SMEM_KB");
-        return s ? atoi(s) : 220;
+        return s ? atoi(s) : 226;
     }();
     static int ns = 0, smem = 0, per_sm = 0; // per instantiation, set once
     if (per_sm == 0) {
@@ -361,11 +363,13 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
         if (int rc = make_templates(&tpl, fmt, D, I, pick_ks(D), pick_ks(I), w.y))
             return rc;
         const int nmaps = nb * kTmapsPerExpert;
-        build_tmaps_kernel<<<(nmaps + 127) / 128, 128, 0, st>>>(tpl, tb.g, tb.u, tb.d, tb.gs,
-                                                               tb.us, tb.ds, nb, w.tmaps);
+        CUDA_TRY(cudaMemsetAsync(w.tmaps_dirty, 0, sizeof(int), st));
+        build_tmaps_kernel<<<(nmaps + 127) / 128, 128, 0, st>>>(
+            tpl, tb.g, tb.u, tb.d, tb.gs, tb.us, tb.ds, nb, w.tmaps, w.tmaps_dirty);
         CUDA_TRY(cudaGetLastError());
         DecodeArgs a{};
         a.tmaps = w.tmaps;
+        a.tmaps_dirty = w.tmaps_dirty;
         a.xrow = xoff, a.orow = w.base, a.cnt = w.cnt, a.item_off = w.off1, a.nb = nb;
         a.x = static_cast<const __half *>(xop);
         a.K = D, a.O = I, a.out = w.h;
