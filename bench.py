@@ -308,7 +308,8 @@ def main():
     torch.cuda.set_device(local_rank)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
     moe.init(local_rank)
     B = args.batch
     wl = Workload(moe, torch, B, seed=1234 + rank)
