@@ -48,7 +48,10 @@ enum {
     MVLLM_ERR_TIMEOUT = 5,     /* a bounded device-side wait ran out */
     MVLLM_ERR_NOT_INIT = 6,    /* mvllm_moe_init has not succeeded */
     MVLLM_ERR_DEVICE = 7,      /* a device-side bounds check rejected an index */
-    MVLLM_ERR_WORKSPACE = 8    /* caller workspace smaller than required */
+    MVLLM_ERR_WORKSPACE = 8,   /* caller workspace smaller than required */
+    MVLLM_ERR_RANGE = 9        /* an MXFP4 scale code in 141..254 reached the tensor-core path,
+                                  whose f16 weights cannot hold it; the host-pointer entries
+                                  rerun such a call on the decode path and never return it */
 };
 
 /* metal_ops::Act (src/gpu/metal_ops.hpp:44); any other value behaves as SILU. */

@@ -58,17 +58,22 @@ struct PlanArgs {
     int x_rows;
     int align16; // fast path: every weight and scale pointer must be 16-byte aligned
     int *err;
+    // Tensor-core path: experts with at least tc_min rows get tc_blocks{1,2}
+    // items per tc_nt-row token tile there (offsets toff1/toff2) and no
+    // decode items.  tc_min <= 0 disables the path.
+    int tc_min, tc_nt, tc_blocks1, tc_blocks2;
+    int *toff1, *toff2;
 };
 
 __global__ void plan_kernel(const PlanArgs a) {
     __shared__ int warp_sums[32];
-    __shared__ int carry[3];
-    if (threadIdx.x == 0)
-        carry[0] = carry[1] = carry[2] = 0;
+    __shared__ int carry[5];
+    if (threadIdx.x < 5)
+        carry[threadIdx.x] = 0;
     __syncthreads();
     for (int e0 = 0; e0 < a.nb; e0 += blockDim.x) {
         const int e = e0 + threadIdx.x;
-        int n = 0, c = 0, i1 = 0, i2 = 0;
+        int n = 0, c = 0, i1 = 0, i2 = 0, j1 = 0, j2 = 0;
         if (e < a.nb) {
             n = max(a.nr[e], 0);
             bool ok = n > 0 && a.g[e] && a.u[e] && a.d[e];
@@ -91,8 +96,13 @@ __global__ void plan_kernel(const PlanArgs a) {
                 ok = false;
             }
             c = ok ? n : 0;
-            i1 = c ? a.blocks1 * ((c + a.chunk1 - 1) / a.chunk1) : 0;
-            i2 = c ? a.blocks2 * ((c + a.chunk2 - 1) / a.chunk2) : 0;
+            if (a.tc_min > 0 && c >= a.tc_min) {
+                j1 = a.tc_blocks1 * ((c + a.tc_nt - 1) / a.tc_nt);
+                j2 = a.tc_blocks2 * ((c + a.tc_nt - 1) / a.tc_nt);
+            } else {
+                i1 = c ? a.blocks1 * ((c + a.chunk1 - 1) / a.chunk1) : 0;
+                i2 = c ? a.blocks2 * ((c + a.chunk2 - 1) / a.chunk2) : 0;
+            }
         }
         int tot;
         const int b = block_exclusive_scan(n, warp_sums, &tot);
@@ -100,23 +110,33 @@ __global__ void plan_kernel(const PlanArgs a) {
         const int o1 = block_exclusive_scan(i1, warp_sums, &t1);
         int t2;
         const int o2 = block_exclusive_scan(i2, warp_sums, &t2);
+        int u1;
+        const int p1 = block_exclusive_scan(j1, warp_sums, &u1);
+        int u2;
+        const int p2 = block_exclusive_scan(j2, warp_sums, &u2);
         if (e < a.nb) {
             a.base[e] = carry[0] + b;
             a.cnt[e] = c;
             a.off1[e] = carry[1] + o1;
             a.off2[e] = carry[2] + o2;
+            a.toff1[e] = carry[3] + p1;
+            a.toff2[e] = carry[4] + p2;
         }
         __syncthreads();
         if (threadIdx.x == 0) {
             carry[0] += tot;
             carry[1] += t1;
             carry[2] += t2;
+            carry[3] += u1;
+            carry[4] += u2;
         }
         __syncthreads();
     }
     if (threadIdx.x == 0) {
         a.off1[a.nb] = carry[1];
         a.off2[a.nb] = carry[2];
+        a.toff1[a.nb] = carry[3];
+        a.toff2[a.nb] = carry[4];
         *a.total_rows = carry[0];
     }
 }
@@ -131,21 +151,23 @@ __global__ void plan_kernel(const PlanArgs a) {
 // decode kernels to acquire maps through the tensormap proxy before use; with
 // static weights the maps never change and no fence is needed.
 constexpr int kTmapsPerExpert = 6; // gate, up, down packed rows; gate, up, down scales
-struct TmapTemplates {
-    CUtensorMap m[kTmapsPerExpert];
+template <int N> struct TmapSet {
+    CUtensorMap m[N];
 };
+template <int N> struct TableSet {
+    const void *const *t[N];
+};
+using TmapTemplates = TmapSet<kTmapsPerExpert>;
 
-__global__ void build_tmaps_kernel(const __grid_constant__ TmapTemplates tpl,
-                                   const void *const *g, const void *const *u,
-                                   const void *const *d, const void *const *gs,
-                                   const void *const *us, const void *const *ds, int nb,
-                                   uint8_t *__restrict__ out, int *dirty) {
+// One thread per (expert, map): map k of expert e gets table t[k]'s entry e.
+template <int N>
+__global__ void build_tmaps_kernel(const __grid_constant__ TmapSet<N> tpl, const TableSet<N> tabs,
+                                   int nb, uint8_t *__restrict__ out, int *dirty) {
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= nb * kTmapsPerExpert)
+    if (idx >= nb * N)
         return;
-    const int e = idx / kTmapsPerExpert, k = idx % kTmapsPerExpert;
-    const void *const *tabs[kTmapsPerExpert] = {g, u, d, gs, us, ds};
-    const void *src = tabs[k] ? tabs[k][e] : nullptr;
+    const int e = idx / N, k = idx % N;
+    const void *src = tabs.t[k] ? tabs.t[k][e] : nullptr;
     uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<size_t>(idx) * 128);
     // The wanted map in registers: template with the address swapped in.
     __shared__ __align__(128) uint8_t staged[128 * 128];

@@ -5,6 +5,7 @@
 // returns an error code.
 #include "aux_kernels.cuh"
 #include "decode_ffn.cuh"
+#include "tc_ffn.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -186,6 +187,9 @@ int pick_ks(int K) { return ((K / 2) % 512 == 0) ? 512 : 256; }
 
 struct RunWs {
     int *base, *cnt, *off1, *off2, *total_rows, *err;
+    int *toff1, *toff2; // tensor-core path item offsets [nb + 1]
+    uint8_t *tc_tmaps;  // fast path: [nb][kTcMapCount] tensor maps
+    int h_rows;         // rows of h and y
     int *tmaps_dirty; // set when build_tmaps_kernel rewrote a map this call
     uint8_t *tmaps;   // fast path: [nb][6] tensor maps
     void *xs; // staged operand (fast: f16, generic: f32)
@@ -204,6 +208,10 @@ void carve_run(Carve &cv, RunWs &w, int nb, int D, int I, bool fast, int rows_ca
     w.err = cv.take<int>(1);
     w.tmaps_dirty = cv.take<int>(1);
     w.tmaps = fast ? cv.take<uint8_t>(size_t(nb) * kTmapsPerExpert * 128) : nullptr;
+    w.toff1 = cv.take<int>(nb + 1);
+    w.toff2 = cv.take<int>(nb + 1);
+    w.tc_tmaps = fast ? cv.take<uint8_t>(size_t(nb) * kTcMapCount * kTcMapBytes) : nullptr;
+    w.h_rows = std::max(rows_cap, 1);
     const size_t esz = fast ? 2 : 4;
     w.xs = cv.take<uint8_t>(size_t(std::max(x_rows, 1)) * D * esz);
     w.h = cv.take<uint8_t>(size_t(std::max(rows_cap, 1)) * I * esz);
@@ -272,6 +280,61 @@ int make_templates(TmapTemplates *t, int fmt, int D, int I, int ks1, int ks2, vo
     return rc ? MVLLM_ERR_CUDA : MVLLM_OK;
 }
 
+// Templates of the tensor-core path: packed rows only (its dequant warps read
+// the scales directly), boxes of 64 bytes (two k-blocks) by 64 gate / up rows
+// or 128 down rows, 64-byte swizzle.
+int make_tc_templates(TmapSet<kTcMapCount> *t, int D, int I, void *placeholder) {
+    const auto u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    const auto sw = CU_TENSOR_MAP_SWIZZLE_64B;
+    int rc = 0;
+    rc |= encode_2d(&t->m[kTcGateP], u8, placeholder, D / 2, I, D / 2, 64, 64, sw);
+    rc |= encode_2d(&t->m[kTcUpP], u8, placeholder, D / 2, I, D / 2, 64, 64, sw);
+    rc |= encode_2d(&t->m[kTcDownP], u8, placeholder, I / 2, D, I / 2, 64, 128, sw);
+    return rc ? MVLLM_ERR_CUDA : MVLLM_OK;
+}
+
+// Token tiles of the tensor-core path: f16 rows of `cols` elements, boxes of
+// 64 elements (one 128-byte swizzle atom) by 64 rows.
+int make_tok_map(CUtensorMap *m, const void *rows_ptr, int cols, int rows) {
+    return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void *>(rows_ptr),
+                     uint64_t(cols), uint64_t(std::max(rows, 1)), uint64_t(cols) * 2, kTcKb,
+                     kTcTokBox, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int FMT, int PHASE, int WT>
+int launch_tc_t(const TcArgs &a, const CUtensorMap &tok, cudaStream_t st, int sms) {
+    using L = TcLayout<WT>;
+    auto kern = tc_ffn_kernel<FMT, PHASE, WT>;
+    static bool attr = false;
+    if (!attr) {
+        CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
+        attr = true;
+    }
+    kern<<<sms, kTcThreads, L::SMEM, st>>>(a, tok);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+template <int PHASE>
+int launch_tc(int fmt, const TcArgs &a, const CUtensorMap &tok, cudaStream_t st, int sms) {
+    return fmt == MVLLM_FMT_MXFP4 ? launch_tc_t<MVLLM_FMT_MXFP4, PHASE, kTcWt>(a, tok, st, sms)
+                                  : launch_tc_t<MVLLM_FMT_INT4_G64, PHASE, kTcWt>(a, tok, st, sms);
+}
+
+// Which experts take the tensor-core path: calls with at least
+// MVLLM_TC_MIN_TOTAL routed rows (default 1024: prefill chunks, not decode
+// batches) send their experts with at least MVLLM_TC_MIN_ROWS rows (default
+// 17) there.  Returns 0 when the path is off for this call.
+int tc_min_rows(int total_rows) {
+    const char *t = getenv("MVLLM_TC_MIN_TOTAL");
+    const char *r = getenv("MVLLM_TC_MIN_ROWS");
+    const int min_total = t ? atoi(t) : 1024;
+    const int min_rows = r ? atoi(r) : 17;
+    if (getenv("MVLLM_TC_OFF") || total_rows < min_total || min_rows <= 0)
+        return 0;
+    return min_rows;
+}
+
 template <int FMT, int PHASE, int KS, int NT>
 int launch_decode_t(DecodeArgs a, cudaStream_t st, int sms) {
     using L = DecodeLayout<FMT, KS, NT>;
@@ -311,8 +374,10 @@ int launch_decode(const DecodeArgs &a, int ks, int nt, cudaStream_t st, int sms)
 // on the fast path, f32 on the generic path) indexed by xoff.
 int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const Tables &tb,
                 const int *nr, const int *xoff, const void *x, int x_dtype, int x_rows,
-                bool x_staged, int avg_rows, int act, float act_a, float act_b, RunWs &w) {
+                bool x_staged, int avg_rows, int act, float act_a, float act_b, RunWs &w,
+                bool allow_tc = true) {
     const bool fast = fast_path_ok(fmt, D, I);
+    const int tc_min = (fast && allow_tc) ? tc_min_rows(x_rows) : 0;
     const int nt = chunk_tiles(avg_rows);
     const int mt = 8 * nt;
     PlanArgs pa{};
@@ -330,6 +395,11 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     pa.base = w.base, pa.cnt = w.cnt, pa.off1 = w.off1, pa.off2 = w.off2;
     pa.total_rows = w.total_rows;
     pa.xoff = xoff, pa.x_rows = x_rows, pa.err = w.err, pa.align16 = fast ? 1 : 0;
+    pa.tc_min = tc_min;
+    pa.tc_nt = TcLayout<kTcWt>::NT;
+    pa.tc_blocks1 = I / (kTcWt * tc_cols_per_tile<1>());
+    pa.tc_blocks2 = D / (kTcWt * tc_cols_per_tile<2>());
+    pa.toff1 = w.toff1, pa.toff2 = w.toff2;
     plan_kernel<<<1, 1024, 0, st>>>(pa);
     CUDA_TRY(cudaGetLastError());
     prof_mark(st, kPhPlan);
@@ -364,9 +434,31 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             return rc;
         const int nmaps = nb * kTmapsPerExpert;
         CUDA_TRY(cudaMemsetAsync(w.tmaps_dirty, 0, sizeof(int), st));
-        build_tmaps_kernel<<<(nmaps + 127) / 128, 128, 0, st>>>(
-            tpl, tb.g, tb.u, tb.d, tb.gs, tb.us, tb.ds, nb, w.tmaps, w.tmaps_dirty);
+        build_tmaps_kernel<kTmapsPerExpert><<<(nmaps + 127) / 128, 128, 0, st>>>(
+            tpl, TableSet<kTmapsPerExpert>{{tb.g, tb.u, tb.d, tb.gs, tb.us, tb.ds}}, nb, w.tmaps,
+            w.tmaps_dirty);
         CUDA_TRY(cudaGetLastError());
+        CUtensorMap tok1{}, tok2{};
+        TcArgs t1{};
+        if (tc_min) {
+            TmapSet<kTcMapCount> ttpl;
+            if (int rc = make_tc_templates(&ttpl, D, I, w.y))
+                return rc;
+            const int ntc = nb * kTcMapCount;
+            build_tmaps_kernel<kTcMapCount><<<(ntc + 127) / 128, 128, 0, st>>>(
+                ttpl, TableSet<kTcMapCount>{{tb.g, tb.u, tb.d}}, nb, w.tc_tmaps, w.tmaps_dirty);
+            CUDA_TRY(cudaGetLastError());
+            if (int rc = make_tok_map(&tok1, xop, D, x_rows))
+                return rc;
+            if (int rc = make_tok_map(&tok2, w.h, I, w.h_rows))
+                return rc;
+            t1.tmaps = w.tc_tmaps;
+            t1.tmaps_dirty = w.tmaps_dirty;
+            t1.s0 = tb.gs, t1.s1 = tb.us;
+            t1.xrow = xoff, t1.orow = w.base, t1.cnt = w.cnt, t1.item_off = w.toff1, t1.nb = nb;
+            t1.K = D, t1.O = I, t1.out = w.h;
+            t1.act = act, t1.act_a = act_a, t1.act_b = act_b, t1.err = w.err;
+        }
         DecodeArgs a{};
         a.tmaps = w.tmaps;
         a.tmaps_dirty = w.tmaps_dirty;
@@ -379,6 +471,8 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
                      : launch_decode<MVLLM_FMT_INT4_G64, 1>(a, pick_ks(D), nt, st, sms);
         if (rc)
             return rc;
+        if (tc_min && (rc = launch_tc<1>(fmt, t1, tok1, st, sms)))
+            return rc;
         prof_mark(st, kPhExpert1);
         DecodeArgs b = a;
         b.xrow = w.base, b.item_off = w.off2;
@@ -387,8 +481,18 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
         rc = (fmt == MVLLM_FMT_MXFP4)
                  ? launch_decode<MVLLM_FMT_MXFP4, 2>(b, pick_ks(I), nt, st, sms)
                  : launch_decode<MVLLM_FMT_INT4_G64, 2>(b, pick_ks(I), nt, st, sms);
+        if (rc)
+            return rc;
+        if (tc_min) {
+            TcArgs t2 = t1;
+            t2.s0 = tb.ds, t2.s1 = nullptr;
+            t2.xrow = w.base, t2.item_off = w.toff2;
+            t2.K = I, t2.O = D, t2.out = w.y;
+            if ((rc = launch_tc<2>(fmt, t2, tok2, st, sms)))
+                return rc;
+        }
         prof_mark(st, kPhExpert2);
-        return rc;
+        return MVLLM_OK;
     }
     GenericArgs a{};
     a.w0 = tb.g, a.w1 = tb.u, a.s0 = (fmt == MVLLM_FMT_F32) ? nullptr : tb.gs;
@@ -642,12 +746,31 @@ size_t mvllm_moe_cache_bytes(void) {
 }
 
 // ----------------------------------------------------- moe_block (host) --
+static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const *g,
+                          const void *const *u, const void *const *d, const float *const *gs,
+                          const float *const *us, const float *const *ds, const float *xg,
+                          const int *xoff, const int *nr, const int *rows, const float *rw,
+                          float *out, int S, int act, float act_a, float act_b, bool allow_tc);
+
 int mvllm_moe_block(int nb, int D, int Iinter, int fmt, int qgs, const void *const *g,
                     const void *const *u, const void *const *d, const float *const *gs,
                     const float *const *us, const float *const *ds, const float *xg,
                     const int *xoff, const int *nr, const int *rows, const float *rw, float *out,
                     int S, int act, float act_a, float act_b) {
     (void)qgs;
+    int rc = moe_block_impl(nb, D, Iinter, fmt, g, u, d, gs, us, ds, xg, xoff, nr, rows, rw, out,
+                            S, act, act_a, act_b, true);
+    if (rc == MVLLM_ERR_RANGE) // scale codes the f16 tensor-core operands cannot hold
+        rc = moe_block_impl(nb, D, Iinter, fmt, g, u, d, gs, us, ds, xg, xoff, nr, rows, rw, out,
+                            S, act, act_a, act_b, false);
+    return rc;
+}
+
+static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const *g,
+                          const void *const *u, const void *const *d, const float *const *gs,
+                          const float *const *us, const float *const *ds, const float *xg,
+                          const int *xoff, const int *nr, const int *rows, const float *rw,
+                          float *out, int S, int act, float act_a, float act_b, bool allow_tc) {
     // Argument checks of metal_ops.cpp:452-457.
     if (nb < 1 || D < 1 || !out || !xg || (fmt != 0 && fmt != 4 && fmt != 7))
         return fail(MVLLM_ERR_INVALID, "moe_block: invalid nb/D/out/xg/fmt");
@@ -815,7 +938,8 @@ int mvllm_moe_block(int nb, int D, int Iinter, int fmt, int qgs, const void *con
     int rc;
     if (fast) {
         rc = run_experts(c.stream, c.sms, nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
-                         MVLLM_DTYPE_F32, int(x_rows), false, R / n_valid, act, act_a, act_b, w);
+                         MVLLM_DTYPE_F32, int(x_rows), false, R / n_valid, act, act_a, act_b, w,
+                         allow_tc);
     } else {
         // Generic path reads the uploaded f32 rows directly.
         RunWs w2 = w;
@@ -835,10 +959,11 @@ int mvllm_moe_block(int nb, int D, int Iinter, int fmt, int qgs, const void *con
         prof_mark(c.stream, kPhCombine);
     }
     CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
-    CUDA_TRY(cudaMemcpyAsync(out, d_out, ob, cudaMemcpyDeviceToHost, c.stream));
+    CUDA_TRY(cudaMemcpyAsync(hp + o_out, d_out, ob, cudaMemcpyDeviceToHost, c.stream));
     CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
     if (int rc2 = check_device_error(w.err, c.stream))
-        return rc2;
+        return rc2; // `out` untouched: a rerun starts from the caller's rows
+    memcpy(out, hp + o_out, ob);
     float a = 0, b = 0, cc = 0;
     cudaEventElapsedTime(&a, c.ev[0], c.ev[1]);
     cudaEventElapsedTime(&b, c.ev[1], c.ev[2]);
@@ -1078,7 +1203,7 @@ size_t mvllm_moe_layer_workspace(int T, int K, int E, int n_shared, int D, int I
 static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_shared, int D,
                           int Iinter, int fmt, const int *idx, const float *wt, const void *x,
                           int x_dtype, const Tables &tb, float *out, int act, float act_a,
-                          float act_b, const LayerWs &l) {
+                          float act_b, const LayerWs &l, bool allow_tc = true) {
     const bool fast = fast_path_ok(fmt, D, Iinter);
     const int EE = E + n_shared, KK = K + n_shared, R = T * KK;
     CUDA_TRY(cudaMemsetAsync(l.run.err, 0, sizeof(int), st));
@@ -1113,7 +1238,7 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
     prof_mark(st, kPhGather);
     RunWs w = l.run;
     if (int rc = run_experts(st, sms, EE, D, Iinter, fmt, tb, l.nr, l.xoff, l.run.xs,
-                             MVLLM_DTYPE_F32, R, true, R / EE, act, act_a, act_b, w))
+                             MVLLM_DTYPE_F32, R, true, R / EE, act, act_a, act_b, w, allow_tc))
         return rc;
     dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
     combine_tokens_kernel<<<grid, 256, 0, st>>>(out, w.y, l.rw, l.tok_pos, T, KK, D);
@@ -1153,11 +1278,30 @@ int mvllm_moe_layer_dev(void *stream, int T, int K, int E, int n_shared, int D, 
                           fmt, idx, wt, x, x_dtype, tb, out, act, act_a, act_b, l);
 }
 
+static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter, int fmt,
+                           const int *idx, const float *wt, const float *x,
+                           const void *const *g, const void *const *u, const void *const *d,
+                           const void *const *gs, const void *const *us, const void *const *ds,
+                           float *out, int act, float act_a, float act_b, bool allow_tc);
+
 int mvllm_moe_layer_host(int T, int K, int E, int n_shared, int D, int Iinter, int fmt,
                          const int *idx, const float *wt, const float *x, const void *const *g,
                          const void *const *u, const void *const *d, const void *const *gs,
                          const void *const *us, const void *const *ds, float *out, int act,
                          float act_a, float act_b) {
+    int rc = layer_host_impl(T, K, E, n_shared, D, Iinter, fmt, idx, wt, x, g, u, d, gs, us, ds,
+                             out, act, act_a, act_b, true);
+    if (rc == MVLLM_ERR_RANGE) // scale codes the f16 tensor-core operands cannot hold
+        rc = layer_host_impl(T, K, E, n_shared, D, Iinter, fmt, idx, wt, x, g, u, d, gs, us, ds,
+                             out, act, act_a, act_b, false);
+    return rc;
+}
+
+static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter, int fmt,
+                           const int *idx, const float *wt, const float *x,
+                           const void *const *g, const void *const *u, const void *const *d,
+                           const void *const *gs, const void *const *us, const void *const *ds,
+                           float *out, int act, float act_a, float act_b, bool allow_tc) {
     if (T < 1 || K < 1 || K > 16 || E < 1 || n_shared < 0 || n_shared > 1 || D < 1 ||
         Iinter < 1 || (fmt != 0 && fmt != 4 && fmt != 7) || !idx || !wt || !x || !g || !u || !d ||
         !out || (fmt != MVLLM_FMT_F32 && (!gs || !us || !ds)) || D % 4 != 0)
@@ -1215,13 +1359,14 @@ int mvllm_moe_layer_host(int T, int K, int E, int n_shared, int D, int Iinter, i
     if (int rc = layer_dev_impl(c.stream, c.sms, T, K, E, n_shared, D, Iinter, fmt,
                                 reinterpret_cast<const int *>(dptr(hidx)),
                                 reinterpret_cast<const float *>(dptr(hwt)), dptr(hx),
-                                MVLLM_DTYPE_F32, tb, dout, act, act_a, act_b, l))
+                                MVLLM_DTYPE_F32, tb, dout, act, act_a, act_b, l, allow_tc))
         return rc;
     CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
-    CUDA_TRY(cudaMemcpyAsync(out, dout, x_b, cudaMemcpyDeviceToHost, c.stream));
+    CUDA_TRY(cudaMemcpyAsync(hout, dout, x_b, cudaMemcpyDeviceToHost, c.stream));
     CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
     if (int rc = check_device_error(l.run.err, c.stream))
-        return rc;
+        return rc; // `out` untouched: a rerun starts from the caller's rows
+    memcpy(out, hout, x_b);
     float a = 0, b = 0, cc = 0;
     cudaEventElapsedTime(&a, c.ev[0], c.ev[1]);
     cudaEventElapsedTime(&b, c.ev[1], c.ev[2]);

@@ -22,7 +22,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libmvllm_moe.so")
 
 OK, ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_NOT_INIT, ERR_DEVICE, \
-    ERR_WORKSPACE = range(9)
+    ERR_WORKSPACE, ERR_RANGE = range(10)
 ACT_SILU, ACT_CLAMP_SWIGLU, ACT_SITU = 0, 1, 2
 FMT_F32, FMT_INT4_G64, FMT_MXFP4 = 0, 4, 7
 DTYPE_F32, DTYPE_BF16 = 0, 1

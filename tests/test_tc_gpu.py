@@ -1,0 +1,127 @@
+"""Parity of the tensor-core (tcgen05/TMEM) expert path against the CPU oracle.
+
+The path takes experts with many rows (prefill chunks, skewed routing).  The
+environment switches the routing between paths per call:
+MVLLM_TC_MIN_TOTAL / MVLLM_TC_MIN_ROWS (thresholds) and MVLLM_TC_OFF.
+Tolerance as everywhere: <= 1e-2 relative L2 and <= 2e-2 max-abs.
+"""
+import numpy as np
+import pytest
+
+import cases
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def force_tc(monkeypatch, min_rows=1):
+    monkeypatch.setenv("MVLLM_TC_MIN_TOTAL", "0")
+    monkeypatch.setenv("MVLLM_TC_MIN_ROWS", str(min_rows))
+    monkeypatch.delenv("MVLLM_TC_OFF", raising=False)
+
+
+def host_block(moe, c):
+    out = np.zeros((max(c["S"], 1), c["D"]), np.float32)
+    ok = moe.moe_block(c["nb"], c["D"], c["I"], c["fmt"], c["g"], c["u"], c["d"], c["gs"],
+                       c["us"], c["ds"], c["xg"], c["xoff"], c["nr"], c["rows"], c["rw"], out,
+                       c["S"], c["act"], c["act_a"], c["act_b"])
+    assert ok, moe.last_error()
+    return out
+
+
+CASES = {
+    # ~53 rows per expert: one ragged token tile each, plus a 160-row shared expert.
+    "mxfp4_one_tile": dict(seed=31, D=512, I=512, E=6, K=2, T=160, fmt=cases.FMT_MXFP4,
+                           act=cases.ACT_SITU, act_a=4.0, act_b=25.0, n_shared=1,
+                           router="uniform", bf16_x=True),
+    "int4_one_tile": dict(seed=32, D=1024, I=512, E=6, K=2, T=160, fmt=cases.FMT_INT4,
+                          act=cases.ACT_CLAMP, act_a=7.0, act_b=0.0, n_shared=0,
+                          router="softmax", bf16_x=True),
+    # ~150 rows per expert: a full 128-row tile and a ragged one.
+    "mxfp4_two_tiles": dict(seed=33, D=1024, I=1024, E=2, K=1, T=300, fmt=cases.FMT_MXFP4,
+                            act=cases.ACT_SITU, act_a=4.0, act_b=25.0, n_shared=0,
+                            router="uniform", bf16_x=True),
+    "int4_two_tiles": dict(seed=34, D=512, I=1024, E=3, K=2, T=200, fmt=cases.FMT_INT4,
+                           act=cases.ACT_CLAMP, act_a=7.0, act_b=0.0, n_shared=0,
+                           router="softmax", bf16_x=False),
+}
+
+
+def make(port, name):
+    kw = dict(CASES[name])
+    seed = kw.pop("seed")
+    return cases.layer_case(port, seed, **kw)
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_tc_matches_oracle(moe, port, monkeypatch, name):
+    c = make(port, name)
+    _, want = cases.run_block(port, c)
+    force_tc(monkeypatch)
+    got = host_block(moe, c)
+    assert_close(got, want, name + " tensor-core")
+    again = host_block(moe, c)
+    np.testing.assert_array_equal(got, again)  # deterministic run to run
+    monkeypatch.setenv("MVLLM_TC_OFF", "1")
+    dec = host_block(moe, c)
+    assert_close(dec, want, name + " decode")
+
+
+def test_tc_mixed_paths(moe, port, monkeypatch):
+    """Experts above the row threshold on the tensor cores, the rest on the
+    decode kernels, in one call."""
+    c = make(port, "mxfp4_one_tile")
+    _, want = cases.run_block(port, c)
+    force_tc(monkeypatch, min_rows=60)  # the 160-row shared expert and a few routed ones
+    assert_close(host_block(moe, c), want, "mixed")
+
+
+def test_tc_device_layer(moe, port, monkeypatch):
+    """The device-pointer layer entry (permute -> gather -> experts -> combine)."""
+    c = make(port, "mxfp4_one_tile")
+    _, want = cases.run_block(port, c)
+    force_tc(monkeypatch)
+    T, K, E, ns, D, I = c["T"], c["K"], c["E"], c["n_shared"], c["D"], c["I"]
+    keep, tabs = [], [[], [], [], [], [], []]
+    for (gp, gsc), (up, usc), (dp, dsc) in c["experts"]:
+        for k, a in enumerate((gp, up, dp, gsc, usc, dsc)):
+            t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+            keep.append(t)
+            tabs[k].append(t.data_ptr())
+    tables = [torch.tensor(t, dtype=torch.int64, device="cuda") for t in tabs]
+    ws = torch.empty(moe.layer_workspace_bytes(T, K, E, ns, D, I, c["fmt"]), dtype=torch.uint8,
+                     device="cuda")
+    out = torch.zeros((T, D), dtype=torch.float32, device="cuda")
+    xd = torch.from_numpy(c["x"]).cuda().to(torch.bfloat16)
+    moe.layer_dev(T, K, E, ns, D, I, c["fmt"], torch.from_numpy(c["idx"]).cuda(),
+                  torch.from_numpy(c["wt"]).cuda(), xd, tables, out, c["act"], c["act_a"],
+                  c["act_b"], ws)
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy(), want, "layer_dev tensor-core")
+
+
+def test_tc_scale_range_reruns_on_decode(moe, port, monkeypatch):
+    """Scale codes above 140 do not fit the f16 operands: the host entry sees
+    MVLLM_ERR_RANGE from the tensor-core kernels and reruns the call on the
+    decode kernels, so the caller still gets the reference's result."""
+    rng = np.random.default_rng(35)
+    D, I, n = 512, 512, 40
+    w = [(rng.standard_normal((o, i)) * 0.02).astype(np.float32)
+         for (o, i) in ((I, D), (I, D), (D, I))]
+    w[0][0, 5] = 65536.0  # one group of gate row 0 needs scale code 141
+    big = [[port.pack_mxfp4(m) for m in w]]
+    assert max(int(s.max()) for _, s in big[0]) > 140
+    x = cases.bf16_round(rng.standard_normal((n, D)).astype(np.float32))
+    x[:, 5] = 0.0  # keeps the reference's output finite
+    c = dict(D=D, I=I, fmt=cases.FMT_MXFP4, act=cases.ACT_SILU, act_a=0.0, act_b=0.0, nb=1,
+             g=[big[0][0][0]], u=[big[0][1][0]], d=[big[0][2][0]], gs=[big[0][0][1]],
+             us=[big[0][1][1]], ds=[big[0][2][1]], xg=x, xoff=np.array([0], np.int32),
+             nr=np.array([n], np.int32), rows=np.arange(n, dtype=np.int32),
+             rw=np.ones(n, np.float32), S=n)
+    _, want = cases.run_block(port, c)
+    assert np.isfinite(want).all()
+    force_tc(monkeypatch)
+    got = host_block(moe, c)
+    assert_close(got, want, "range rerun")
