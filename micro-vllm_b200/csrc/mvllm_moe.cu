@@ -280,16 +280,26 @@ int make_templates(TmapTemplates *t, int fmt, int D, int I, int ks1, int ks2, vo
     return rc ? MVLLM_ERR_CUDA : MVLLM_OK;
 }
 
-// Templates of the tensor-core path: packed rows only (its dequant warps read
-// the scales directly), boxes of 64 bytes (two k-blocks) by 64 gate / up rows
-// or 128 down rows, 64-byte swizzle.
-int make_tc_templates(TmapSet<kTcMapCount> *t, int D, int I, void *placeholder) {
-    const auto u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-    const auto sw = CU_TENSOR_MAP_SWIZZLE_64B;
+// Templates of the tensor-core path: packed rows in boxes of 64 bytes (two
+// k-blocks) by 64 gate / up rows or 128 down rows with the 64-byte swizzle,
+// and the rows' scales in 16-byte windows (8 k-blocks of ue8m0 pairs or 4
+// k-blocks of f32), unswizzled.
+int make_tc_templates(TmapSet<kTcMapCount> *t, int fmt, int D, int I, void *placeholder) {
+    const auto u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8, f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const auto sw = CU_TENSOR_MAP_SWIZZLE_64B, none = CU_TENSOR_MAP_SWIZZLE_NONE;
     int rc = 0;
     rc |= encode_2d(&t->m[kTcGateP], u8, placeholder, D / 2, I, D / 2, 64, 64, sw);
     rc |= encode_2d(&t->m[kTcUpP], u8, placeholder, D / 2, I, D / 2, 64, 64, sw);
     rc |= encode_2d(&t->m[kTcDownP], u8, placeholder, I / 2, D, I / 2, 64, 128, sw);
+    if (fmt == MVLLM_FMT_MXFP4) {
+        rc |= encode_2d(&t->m[kTcGateS], u8, placeholder, D / 32, I, D / 32, 16, 64, none);
+        rc |= encode_2d(&t->m[kTcUpS], u8, placeholder, D / 32, I, D / 32, 16, 64, none);
+        rc |= encode_2d(&t->m[kTcDownS], u8, placeholder, I / 32, D, I / 32, 16, 128, none);
+    } else {
+        rc |= encode_2d(&t->m[kTcGateS], f32, placeholder, D / 64, I, D / 16, 4, 64, none);
+        rc |= encode_2d(&t->m[kTcUpS], f32, placeholder, D / 64, I, D / 16, 4, 64, none);
+        rc |= encode_2d(&t->m[kTcDownS], f32, placeholder, I / 64, D, I / 16, 4, 128, none);
+    }
     return rc ? MVLLM_ERR_CUDA : MVLLM_OK;
 }
 
@@ -301,24 +311,36 @@ int make_tok_map(CUtensorMap *m, const void *rows_ptr, int cols, int rows) {
                      kTcTokBox, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int FMT, int PHASE, int WT>
+template <int FMT, int PHASE>
 int launch_tc_t(const TcArgs &a, const CUtensorMap &tok, cudaStream_t st, int sms) {
-    using L = TcLayout<WT>;
-    auto kern = tc_ffn_kernel<FMT, PHASE, WT>;
+    using L = TcLayout;
+    auto kern = tc_ffn_kernel<FMT, PHASE>;
     static bool attr = false;
     if (!attr) {
         CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
         attr = true;
     }
-    kern<<<sms, kTcThreads, L::SMEM, st>>>(a, tok);
-    CUDA_TRY(cudaGetLastError());
+    // CTA pairs: clusters of 2 on the two SMs of a TPC, one pair per TPC.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(std::max(2, sms & ~1));
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = L::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, tok));
     return MVLLM_OK;
 }
 
 template <int PHASE>
 int launch_tc(int fmt, const TcArgs &a, const CUtensorMap &tok, cudaStream_t st, int sms) {
-    return fmt == MVLLM_FMT_MXFP4 ? launch_tc_t<MVLLM_FMT_MXFP4, PHASE, kTcWt>(a, tok, st, sms)
-                                  : launch_tc_t<MVLLM_FMT_INT4_G64, PHASE, kTcWt>(a, tok, st, sms);
+    return fmt == MVLLM_FMT_MXFP4 ? launch_tc_t<MVLLM_FMT_MXFP4, PHASE>(a, tok, st, sms)
+                                  : launch_tc_t<MVLLM_FMT_INT4_G64, PHASE>(a, tok, st, sms);
 }
 
 // Which experts take the tensor-core path: calls with at least
@@ -396,9 +418,9 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     pa.total_rows = w.total_rows;
     pa.xoff = xoff, pa.x_rows = x_rows, pa.err = w.err, pa.align16 = fast ? 1 : 0;
     pa.tc_min = tc_min;
-    pa.tc_nt = TcLayout<kTcWt>::NT;
-    pa.tc_blocks1 = I / (kTcWt * tc_cols_per_tile<1>());
-    pa.tc_blocks2 = D / (kTcWt * tc_cols_per_tile<2>());
+    pa.tc_nt = kTcNT;
+    pa.tc_blocks1 = I / tc_cols_per_item<1>();
+    pa.tc_blocks2 = D / tc_cols_per_item<2>();
     pa.toff1 = w.toff1, pa.toff2 = w.toff2;
     plan_kernel<<<1, 1024, 0, st>>>(pa);
     CUDA_TRY(cudaGetLastError());
@@ -442,11 +464,12 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
         TcArgs t1{};
         if (tc_min) {
             TmapSet<kTcMapCount> ttpl;
-            if (int rc = make_tc_templates(&ttpl, D, I, w.y))
+            if (int rc = make_tc_templates(&ttpl, fmt, D, I, w.y))
                 return rc;
             const int ntc = nb * kTcMapCount;
             build_tmaps_kernel<kTcMapCount><<<(ntc + 127) / 128, 128, 0, st>>>(
-                ttpl, TableSet<kTcMapCount>{{tb.g, tb.u, tb.d}}, nb, w.tc_tmaps, w.tmaps_dirty);
+                ttpl, TableSet<kTcMapCount>{{tb.g, tb.u, tb.d, tb.gs, tb.us, tb.ds}}, nb,
+                w.tc_tmaps, w.tmaps_dirty);
             CUDA_TRY(cudaGetLastError());
             if (int rc = make_tok_map(&tok1, xop, D, x_rows))
                 return rc;

@@ -32,18 +32,19 @@ def host_block(moe, c):
 
 
 CASES = {
-    # ~53 rows per expert: one ragged token tile each, plus a 160-row shared expert.
+    # ~53 rows per expert: one ragged token tile each (128-column accumulator
+    # halves), plus a 160-row shared expert (the whole 256-column accumulator).
     "mxfp4_one_tile": dict(seed=31, D=512, I=512, E=6, K=2, T=160, fmt=cases.FMT_MXFP4,
                            act=cases.ACT_SITU, act_a=4.0, act_b=25.0, n_shared=1,
                            router="uniform", bf16_x=True),
     "int4_one_tile": dict(seed=32, D=1024, I=512, E=6, K=2, T=160, fmt=cases.FMT_INT4,
                           act=cases.ACT_CLAMP, act_a=7.0, act_b=0.0, n_shared=0,
                           router="softmax", bf16_x=True),
-    # ~150 rows per expert: a full 128-row tile and a ragged one.
-    "mxfp4_two_tiles": dict(seed=33, D=1024, I=1024, E=2, K=1, T=300, fmt=cases.FMT_MXFP4,
+    # ~300 rows per expert: a full 256-row tile and a ragged one.
+    "mxfp4_two_tiles": dict(seed=33, D=1024, I=1024, E=2, K=1, T=600, fmt=cases.FMT_MXFP4,
                             act=cases.ACT_SITU, act_a=4.0, act_b=25.0, n_shared=0,
                             router="uniform", bf16_x=True),
-    "int4_two_tiles": dict(seed=34, D=512, I=1024, E=3, K=2, T=200, fmt=cases.FMT_INT4,
+    "int4_two_tiles": dict(seed=34, D=512, I=1024, E=3, K=2, T=450, fmt=cases.FMT_INT4,
                            act=cases.ACT_CLAMP, act_a=7.0, act_b=0.0, n_shared=0,
                            router="softmax", bf16_x=False),
 }
