@@ -58,22 +58,24 @@ struct PlanArgs {
     int x_rows;
     int align16; // fast path: every weight and scale pointer must be 16-byte aligned
     int *err;
-    // Tensor-core path: experts with at least tc_min rows get tc_blocks{1,2}
-    // items per tc_nt-row token tile there (offsets toff1/toff2) and no
-    // decode items.  tc_min <= 0 disables the path.
-    int tc_min, tc_nt, tc_blocks1, tc_blocks2;
-    int *toff1, *toff2;
+    // Tensor-core path: experts with at least tc_min rows get no decode items;
+    // their 256-row token tiles (and a rest wider than tc_small rows) become
+    // tc_blocks{1,2} CTA-pair items per tile (offsets toff1/toff2), a rest of
+    // at most tc_small rows tc_sblocks{1,2} single-CTA items (soff1/soff2).
+    // tc_min <= 0 disables the path.
+    int tc_min, tc_small, tc_blocks1, tc_blocks2, tc_sblocks1, tc_sblocks2;
+    int *toff1, *toff2, *soff1, *soff2;
 };
 
 __global__ void plan_kernel(const PlanArgs a) {
     __shared__ int warp_sums[32];
-    __shared__ int carry[5];
-    if (threadIdx.x < 5)
+    __shared__ int carry[7];
+    if (threadIdx.x < 7)
         carry[threadIdx.x] = 0;
     __syncthreads();
     for (int e0 = 0; e0 < a.nb; e0 += blockDim.x) {
         const int e = e0 + threadIdx.x;
-        int n = 0, c = 0, i1 = 0, i2 = 0, j1 = 0, j2 = 0;
+        int n = 0, c = 0, i1 = 0, i2 = 0, j1 = 0, j2 = 0, k1 = 0, k2 = 0;
         if (e < a.nb) {
             n = max(a.nr[e], 0);
             bool ok = n > 0 && a.g[e] && a.u[e] && a.d[e];
@@ -97,8 +99,13 @@ __global__ void plan_kernel(const PlanArgs a) {
             }
             c = ok ? n : 0;
             if (a.tc_min > 0 && c >= a.tc_min) {
-                j1 = a.tc_blocks1 * ((c + a.tc_nt - 1) / a.tc_nt);
-                j2 = a.tc_blocks2 * ((c + a.tc_nt - 1) / a.tc_nt);
+                const int f = c >> 8, r = c & 255;
+                const int npair = f + (r > a.tc_small ? 1 : 0);
+                const int nsolo = (r > 0 && r <= a.tc_small) ? 1 : 0;
+                j1 = a.tc_blocks1 * npair;
+                j2 = a.tc_blocks2 * npair;
+                k1 = a.tc_sblocks1 * nsolo;
+                k2 = a.tc_sblocks2 * nsolo;
             } else {
                 i1 = c ? a.blocks1 * ((c + a.chunk1 - 1) / a.chunk1) : 0;
                 i2 = c ? a.blocks2 * ((c + a.chunk2 - 1) / a.chunk2) : 0;
@@ -114,6 +121,10 @@ __global__ void plan_kernel(const PlanArgs a) {
         const int p1 = block_exclusive_scan(j1, warp_sums, &u1);
         int u2;
         const int p2 = block_exclusive_scan(j2, warp_sums, &u2);
+        int v1;
+        const int q1 = block_exclusive_scan(k1, warp_sums, &v1);
+        int v2;
+        const int q2 = block_exclusive_scan(k2, warp_sums, &v2);
         if (e < a.nb) {
             a.base[e] = carry[0] + b;
             a.cnt[e] = c;
@@ -121,6 +132,8 @@ __global__ void plan_kernel(const PlanArgs a) {
             a.off2[e] = carry[2] + o2;
             a.toff1[e] = carry[3] + p1;
             a.toff2[e] = carry[4] + p2;
+            a.soff1[e] = carry[5] + q1;
+            a.soff2[e] = carry[6] + q2;
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -129,6 +142,8 @@ __global__ void plan_kernel(const PlanArgs a) {
             carry[2] += t2;
             carry[3] += u1;
             carry[4] += u2;
+            carry[5] += v1;
+            carry[6] += v2;
         }
         __syncthreads();
     }
@@ -137,6 +152,8 @@ __global__ void plan_kernel(const PlanArgs a) {
         a.off2[a.nb] = carry[2];
         a.toff1[a.nb] = carry[3];
         a.toff2[a.nb] = carry[4];
+        a.soff1[a.nb] = carry[5];
+        a.soff2[a.nb] = carry[6];
         *a.total_rows = carry[0];
     }
 }

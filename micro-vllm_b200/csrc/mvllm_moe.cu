@@ -187,7 +187,8 @@ int pick_ks(int K) { return ((K / 2) % 512 == 0) ? 512 : 256; }
 
 struct RunWs {
     int *base, *cnt, *off1, *off2, *total_rows, *err;
-    int *toff1, *toff2; // tensor-core path item offsets [nb + 1]
+    int *toff1, *toff2; // tensor-core path, CTA-pair item offsets [nb + 1]
+    int *soff1, *soff2; // tensor-core path, single-CTA item offsets [nb + 1]
     uint8_t *tc_tmaps;  // fast path: [nb][kTcMapCount] tensor maps
     int h_rows;         // rows of h and y
     int *tmaps_dirty; // set when build_tmaps_kernel rewrote a map this call
@@ -210,6 +211,8 @@ void carve_run(Carve &cv, RunWs &w, int nb, int D, int I, bool fast, int rows_ca
     w.tmaps = fast ? cv.take<uint8_t>(size_t(nb) * kTmapsPerExpert * 128) : nullptr;
     w.toff1 = cv.take<int>(nb + 1);
     w.toff2 = cv.take<int>(nb + 1);
+    w.soff1 = cv.take<int>(nb + 1);
+    w.soff2 = cv.take<int>(nb + 1);
     w.tc_tmaps = fast ? cv.take<uint8_t>(size_t(nb) * kTcMapCount * kTcMapBytes) : nullptr;
     w.h_rows = std::max(rows_cap, 1);
     const size_t esz = fast ? 2 : 4;
@@ -311,36 +314,46 @@ int make_tok_map(CUtensorMap *m, const void *rows_ptr, int cols, int rows) {
                      kTcTokBox, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int FMT, int PHASE>
+template <int FMT, int PHASE, bool PAIR>
 int launch_tc_t(const TcArgs &a, const CUtensorMap &tok, cudaStream_t st, int sms) {
-    using L = TcLayout;
-    auto kern = tc_ffn_kernel<FMT, PHASE>;
+    using L = TcLayout<PAIR>;
+    auto kern = tc_ffn_kernel<FMT, PHASE, PAIR>;
     static bool attr = false;
     if (!attr) {
         CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
         attr = true;
     }
-    // CTA pairs: clusters of 2 on the two SMs of a TPC, one pair per TPC.
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(std::max(2, sms & ~1));
-    cfg.blockDim = dim3(kTcThreads);
+    cfg.blockDim = dim3(TcCfg<PAIR>::THREADS);
     cfg.dynamicSmemBytes = L::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 2;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
+    if (PAIR) {
+        // CTA pairs: clusters of 2 on the two SMs of a TPC, one pair per TPC.
+        cfg.gridDim = dim3(std::max(2, sms & ~1));
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+    } else {
+        cfg.gridDim = dim3(sms * TcCfg<PAIR>::CTAS_PER_SM);
+    }
     CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, tok));
     return MVLLM_OK;
 }
 
 template <int PHASE>
-int launch_tc(int fmt, const TcArgs &a, const CUtensorMap &tok, cudaStream_t st, int sms) {
-    return fmt == MVLLM_FMT_MXFP4 ? launch_tc_t<MVLLM_FMT_MXFP4, PHASE>(a, tok, st, sms)
-                                  : launch_tc_t<MVLLM_FMT_INT4_G64, PHASE>(a, tok, st, sms);
+int launch_tc(int fmt, const TcArgs &pair, const TcArgs &solo, const CUtensorMap &tok,
+              cudaStream_t st, int sms) {
+    int rc = fmt == MVLLM_FMT_MXFP4
+                 ? launch_tc_t<MVLLM_FMT_MXFP4, PHASE, true>(pair, tok, st, sms)
+                 : launch_tc_t<MVLLM_FMT_INT4_G64, PHASE, true>(pair, tok, st, sms);
+    if (rc)
+        return rc;
+    return fmt == MVLLM_FMT_MXFP4 ? launch_tc_t<MVLLM_FMT_MXFP4, PHASE, false>(solo, tok, st, sms)
+                                  : launch_tc_t<MVLLM_FMT_INT4_G64, PHASE, false>(solo, tok, st, sms);
 }
 
 // Which experts take the tensor-core path: calls with at least
@@ -418,10 +431,12 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     pa.total_rows = w.total_rows;
     pa.xoff = xoff, pa.x_rows = x_rows, pa.err = w.err, pa.align16 = fast ? 1 : 0;
     pa.tc_min = tc_min;
-    pa.tc_nt = kTcNT;
-    pa.tc_blocks1 = I / tc_cols_per_item<1>();
-    pa.tc_blocks2 = D / tc_cols_per_item<2>();
-    pa.toff1 = w.toff1, pa.toff2 = w.toff2;
+    pa.tc_small = getenv("MVLLM_TC_NO_SOLO") ? 0 : kTcSoloMax;
+    pa.tc_blocks1 = I / tc_cols_per_item<1, true>();
+    pa.tc_blocks2 = D / tc_cols_per_item<2, true>();
+    pa.tc_sblocks1 = I / tc_cols_per_item<1, false>();
+    pa.tc_sblocks2 = D / tc_cols_per_item<2, false>();
+    pa.toff1 = w.toff1, pa.toff2 = w.toff2, pa.soff1 = w.soff1, pa.soff2 = w.soff2;
     plan_kernel<<<1, 1024, 0, st>>>(pa);
     CUDA_TRY(cudaGetLastError());
     prof_mark(st, kPhPlan);
@@ -479,6 +494,7 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             t1.tmaps_dirty = w.tmaps_dirty;
             t1.s0 = tb.gs, t1.s1 = tb.us;
             t1.xrow = xoff, t1.orow = w.base, t1.cnt = w.cnt, t1.item_off = w.toff1, t1.nb = nb;
+            t1.small_max = pa.tc_small; // the plan's split of each expert's tiles
             t1.K = D, t1.O = I, t1.out = w.h;
             t1.act = act, t1.act_a = act_a, t1.act_b = act_b, t1.err = w.err;
         }
@@ -494,8 +510,12 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
                      : launch_decode<MVLLM_FMT_INT4_G64, 1>(a, pick_ks(D), nt, st, sms);
         if (rc)
             return rc;
-        if (tc_min && (rc = launch_tc<1>(fmt, t1, tok1, st, sms)))
-            return rc;
+        if (tc_min) {
+            TcArgs s1 = t1;
+            s1.item_off = w.soff1;
+            if ((rc = launch_tc<1>(fmt, t1, s1, tok1, st, sms)))
+                return rc;
+        }
         prof_mark(st, kPhExpert1);
         DecodeArgs b = a;
         b.xrow = w.base, b.item_off = w.off2;
@@ -511,7 +531,9 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             t2.s0 = tb.ds, t2.s1 = nullptr;
             t2.xrow = w.base, t2.item_off = w.toff2;
             t2.K = I, t2.O = D, t2.out = w.y;
-            if ((rc = launch_tc<2>(fmt, t2, tok2, st, sms)))
+            TcArgs s2 = t2;
+            s2.item_off = w.soff2;
+            if ((rc = launch_tc<2>(fmt, t2, s2, tok2, st, sms)))
                 return rc;
         }
         prof_mark(st, kPhExpert2);

@@ -59,17 +59,40 @@
 
 namespace mvb {
 
-constexpr int kTcEpiWarps = 8;             // warps 0-7: quadrant = warp % 4, column half = warp / 4
-constexpr int kTcDqWarp0 = 8, kTcDqWarps = 8; // warps 8-15: quadrant = warp % 4, k-block parity set
-constexpr int kTcProdWarp = 16, kTcMmaWarp = 17, kTcPkWarp = 18;
-constexpr int kTcThreads = 19 * 32;
 constexpr int kTcKb = 64;         // k elements per k-block: one 128-byte swizzle atom of f16
 constexpr int kTcTokBox = 64;     // token rows per TMA box
-constexpr int kTcNT = 256;        // token tile of a pair: the largest MMA N
-constexpr int kTcTmemCols = 512;  // whole TMEM of the SM
-constexpr int kTcStages = 7;      // token half-tile + A operand ring (k-blocks)
 constexpr int kTcPkSlots = 8;     // packed-weight ring depth (2 k-blocks per slot)
 constexpr int kTcScSlots = 3;     // scale ring depth (one 16-byte window per row per slot)
+constexpr int kTcSoloMax = 64;    // token tiles of at most this many rows run on single CTAs
+
+// The two forms of the kernel.  PAIR: CTA pairs, M = 256 weight rows per MMA,
+// token tiles of up to 256 rows, one CTA per SM.  Solo: one CTA, M = 128,
+// token tiles of up to 64 rows, two CTAs per SM.  A pair MMA takes about 108
+// cycles to issue whatever its N (measured on B200), a single-CTA MMA about
+// 45: the pair wins once N passes 128 (an N = 256 pair MMA runs at the tensor
+// rate), while a tile of a few dozen tokens is bound by issue, so it runs on
+// single CTAs, two per SM, each with its own issuing thread.
+template <bool PAIR> struct TcCfg {
+    static constexpr int EPI_WARPS = PAIR ? 8 : 4; // quadrant = warp % 4, chunk half = warp / 4
+    static constexpr int DQ_SETS = PAIR ? 2 : 1;   // sets of 4 dequant warps (k-block parity)
+    static constexpr int DQ_WARP0 = EPI_WARPS;
+    static constexpr int DQ_WARPS = 4 * DQ_SETS;
+    static constexpr int PROD_WARP = DQ_WARP0 + DQ_WARPS;
+    static constexpr int MMA_WARP = PROD_WARP + 1;
+    static constexpr int PK_WARP = PROD_WARP + 2;
+    static constexpr int THREADS = (PK_WARP + 1) * 32; // 608 / 352
+    static constexpr int CTAS_PER_SM = PAIR ? 1 : 2;
+    static constexpr int NT = PAIR ? 256 : kTcSoloMax; // token tile of an item
+    static constexpr int NALIGN = PAIR ? 32 : 16;      // MMA N granularity
+    static constexpr int ACC_HALF = PAIR ? 128 : 64;   // TMEM columns of one accumulator half
+    static constexpr int A_BASE = 2 * ACC_HALF;
+    static constexpr int STAGES = PAIR ? 7 : 4;        // token + A operand ring (k-blocks)
+    static constexpr int TMEM_COLS = PAIR ? 512 : 256;
+    static constexpr int TOK_ROWS = PAIR ? NT / 2 : NT; // token rows one CTA holds
+    static constexpr int FULL_ARRIVALS = 1 + (PAIR ? 8 : 4);
+    static constexpr int ACC_EMPTY_ARRIVALS = PAIR ? 2 * EPI_WARPS : EPI_WARPS;
+    static_assert(A_BASE + STAGES * 32 <= TMEM_COLS, "TMEM budget");
+};
 enum { kTcGateP = 0, kTcUpP, kTcDownP, kTcGateS, kTcUpS, kTcDownS, kTcMapCount };
 constexpr int kTcMapBytes = 128;
 
@@ -81,7 +104,8 @@ struct TcArgs {
     const int *xrow;          // per expert: first operand row (token map row)
     const int *orow;          // per expert: first output row
     const int *cnt;           // per expert: rows on this path (0 = decode path)
-    const int *item_off;      // [nb + 1] item prefix of this path
+    const int *item_off;      // [nb + 1] item prefix of this list
+    int small_max;            // rest tiles of at most this many rows are single-CTA items
     int nb;
     int K, O;                 // reduction length, output width (I or D)
     void *out;                // phase 1: f16 h [rows, I]; phase 2: f32 y [rows, D]
@@ -90,29 +114,38 @@ struct TcArgs {
     int *err;
 };
 
-// Per CTA: TMEM columns [0, 256) accumulators -- one 256-column buffer for a
-// tile of more than 128 tokens, or two 128-column buffers that alternate
-// between smaller tiles (the epilogue of one overlaps the MMAs of the next);
-// then one 32-column A stage (128 weight rows x 64 f16) per ring stage.
-struct TcLayout {
-    static constexpr int TOK_STAGE = (kTcNT / 2) * 128; // this CTA's half tile, one k-block
+// Per CTA: TMEM columns [0, 2 * ACC_HALF) accumulators -- one buffer of both
+// halves for a tile wider than a half, or two halves that alternate between
+// narrower tiles (the epilogue of one overlaps the MMAs of the next); then
+// one 32-column A stage (128 weight rows x 64 f16) per ring stage.
+template <bool PAIR> struct TcLayout {
+    using C = TcCfg<PAIR>;
+    static constexpr int TOK_STAGE = C::TOK_ROWS * 128; // this CTA's token rows, one k-block
     static constexpr int PK_STAGE = 128 * 64;           // 128 weight rows x 64 B (2 k-blocks)
     static constexpr int SC_STAGE = 128 * 16;           // 128 weight rows x one scale window
-    static constexpr int A_BASE = 256;
     static constexpr int A_COLS = 32;
-    static constexpr int OFF_PK = kTcStages * TOK_STAGE;
+    static constexpr int OFF_PK = C::STAGES * TOK_STAGE;
     static constexpr int OFF_SC = OFF_PK + kTcPkSlots * PK_STAGE;
     static constexpr int OFF_BAR = OFF_SC + kTcScSlots * SC_STAGE;
-    static constexpr int NBARS = 2 * kTcStages + 2 * kTcPkSlots + 2 * kTcScSlots + 4 + 1;
+    static constexpr int NBARS = 2 * C::STAGES + 2 * kTcPkSlots + 2 * kTcScSlots + 4 + 1;
     static constexpr int SMEM = OFF_BAR + NBARS * 8 + 16 + 1024; // + tmem slot + alignment
-    static_assert(A_BASE + kTcStages * A_COLS <= kTcTmemCols, "TMEM budget");
-    static_assert(SMEM <= 232448, "dynamic shared memory of one CTA");
+    static_assert(SMEM * C::CTAS_PER_SM <= 232448, "dynamic shared memory per SM");
 };
 
-// Weight rows per item of a pair: phase 1 takes 128 h columns (128 gate + 128
-// up rows), phase 2 takes 256 down rows; each CTA holds half.
-template <int PHASE> __host__ __device__ constexpr int tc_cols_per_item() {
-    return PHASE == 1 ? 128 : 256;
+// Output columns per item: phase 1 takes 64 h columns (64 gate + 64 up rows)
+// per 128 weight rows, phase 2 takes 128 down rows; a pair item holds twice
+// that, half in each CTA.
+template <int PHASE, bool PAIR> __host__ __device__ constexpr int tc_cols_per_item() {
+    return (PHASE == 1 ? 64 : 128) * (PAIR ? 2 : 1);
+}
+
+// Token tiles of an expert with c rows: full 256-row tiles and the rest; the
+// rest runs on single CTAs when it has at most kTcSoloMax rows (small_max),
+// else as one more (narrower) pair tile.
+__host__ __device__ __forceinline__ void tc_tiles(int c, int small_max, int &npair, int &nsolo) {
+    const int f = c >> 8, r = c & 255;
+    npair = f + (r > small_max ? 1 : 0);
+    nsolo = (r > 0 && r <= small_max) ? 1 : 0;
 }
 
 // k-blocks per 16-byte scale window of a row: 8 for MXFP4 (two ue8m0 bytes per
@@ -190,6 +223,20 @@ __device__ __forceinline__ void tc_mma_pair(uint32_t d, uint32_t a, uint64_t bde
                  "r"(a), "l"(bdesc), "r"(idesc), "r"(accumulate)
                  : "memory");
 }
+__device__ __forceinline__ void tc_commit_solo(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]^T on this CTA, f16 in, f32 accumulate.
+__device__ __forceinline__ void tc_mma_solo(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+                 "r"(a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
 __device__ __forceinline__ void tc_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -238,9 +285,9 @@ __device__ __forceinline__ uint64_t tc_desc_sw128(uint32_t saddr) {
            (static_cast<uint64_t>(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 // Instruction descriptor: f32 accumulate [4,6)=1, A and B f16 (0), both
-// K-major, N >> 3 at [17,23), M >> 4 at [24,29); M = 256 over the pair.
-__device__ __forceinline__ uint32_t tc_idesc(int n) {
-    return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(256 >> 4) << 24);
+// K-major, N >> 3 at [17,23), M >> 4 at [24,29) (256 over a pair, else 128).
+__device__ __forceinline__ uint32_t tc_idesc(int m, int n) {
+    return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // Word i (0..3) of v without a local-memory array.
@@ -250,27 +297,31 @@ __device__ __forceinline__ uint32_t sel4(const uint4 &v, int i) {
 
 struct TcItem {
     int e;     // expert
-    int t0;    // first row of the pair's token tile (relative to the expert)
-    int n;     // real rows in the pair's tile
-    int nmma;  // MMA N: n rounded up to 32
-    int c0;    // first output column of the pair's item (h column or y column)
+    int t0;    // first row of the item's token tile (relative to the expert)
+    int n;     // real rows in the tile
+    int nmma;  // MMA N: n rounded up to the MMA's granularity
+    int c0;    // first output column of the item (h column or y column)
 };
 
-// Item i of the path: experts in plan order; inside an expert the weight tile
-// varies slowest and the token tile fastest, so pairs working at the same
-// time share the weight rows through L2.
-template <int PHASE>
+// Item i of a list: experts in plan order; inside an expert the weight tile
+// varies slowest and the token tile fastest, so CTAs working at the same
+// time share the weight rows through L2.  Pair lists hold an expert's
+// 256-row tiles (and a wider rest); solo lists its narrow rest, if any.
+template <int PHASE, bool PAIR>
 __device__ __forceinline__ void tc_item(const TcArgs &p, int i, TcItem &it) {
+    using C = TcCfg<PAIR>;
     const int e = find_owner(p.item_off, p.nb, i);
     const int local = i - __ldg(p.item_off + e);
     const int c = __ldg(p.cnt + e);
-    const int ntt = (c + kTcNT - 1) / kTcNT;
+    int npair, nsolo;
+    tc_tiles(c, p.small_max, npair, nsolo);
+    const int ntt = PAIR ? npair : 1;
     const int wg = local / ntt, tt = local - wg * ntt;
     it.e = e;
-    it.t0 = tt * kTcNT;
-    it.n = min(kTcNT, c - it.t0);
-    it.nmma = (it.n + 31) & ~31;
-    it.c0 = wg * tc_cols_per_item<PHASE>();
+    it.t0 = PAIR ? tt * 256 : (c >> 8) * 256;
+    it.n = min(C::NT, c - it.t0);
+    it.nmma = (it.n + C::NALIGN - 1) & ~(C::NALIGN - 1);
+    it.c0 = wg * tc_cols_per_item<PHASE, PAIR>();
 }
 
 // Accumulator buffers: a tile of more than 128 tokens takes both 128-column
@@ -312,87 +363,109 @@ __device__ __forceinline__ void tc_dequant_row(const uint4 &w0, const uint4 &w1,
     }
 }
 
-template <int FMT, int PHASE>
-__global__ void __launch_bounds__(kTcThreads, 1)
+template <int FMT, int PHASE, bool PAIR>
+__global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM)
     tc_ffn_kernel(const TcArgs p, const __grid_constant__ CUtensorMap tok_map) {
-    using L = TcLayout;
+    using C = TcCfg<PAIR>;
+    using L = TcLayout<PAIR>;
+    constexpr int S = C::STAGES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
-    uint64_t *full = bars, *empty = bars + kTcStages;              // tokens + A stage
-    uint64_t *pk_full = empty + kTcStages, *pk_empty = pk_full + kTcPkSlots;
+    uint64_t *full = bars, *empty = bars + S; // tokens + A stage
+    uint64_t *pk_full = empty + S, *pk_empty = pk_full + kTcPkSlots;
     uint64_t *sc_full = pk_empty + kTcPkSlots, *sc_empty = sc_full + kTcScSlots;
     uint64_t *acc_full = sc_empty + kTcScSlots, *acc_empty = acc_full + 2, *done = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_ctarank();           // 0 = leader of the pair
-    const int pair = static_cast<int>(cluster_id_x()), npairs = static_cast<int>(nclusters_x());
+    // A pair's CTAs walk the pair's list together; rank 0 is the leader.
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const int unit = PAIR ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+    const int nunits = PAIR ? static_cast<int>(nclusters_x()) : static_cast<int>(gridDim.x);
     const int total = __ldg(p.item_off + p.nb);
-    if (pair >= total)
-        return; // no item for this pair (both CTAs leave): before touching TMEM
+    if (unit >= total)
+        return; // no item (for a pair: both CTAs leave) -- before touching TMEM
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kTcStages; ++s) {
-            // Leader: its producer's expect_tx (both halves' bytes) + the
-            // k-block's 4 dequant warps of each CTA.  The other CTA's copy of
-            // this barrier is unused.
-            mbar_init(&full[s], 1 + 8);
-            mbar_init(&empty[s], 1); // the leader's tcgen05.commit
+        for (int s = 0; s < S; ++s) {
+            // Producer's expect_tx (a pair's leader counts both CTAs' token
+            // bytes) + the k-block's dequant warps (both CTAs' for a pair; the
+            // other CTA's copy of this barrier is unused).
+            mbar_init(&full[s], C::FULL_ARRIVALS);
+            mbar_init(&empty[s], 1); // the (leader's) tcgen05.commit
         }
         for (int s = 0; s < kTcPkSlots; ++s) {
             mbar_init(&pk_full[s], 1);
-            mbar_init(&pk_empty[s], kTcDqWarps);
+            mbar_init(&pk_empty[s], C::DQ_WARPS);
         }
         for (int s = 0; s < kTcScSlots; ++s) {
             mbar_init(&sc_full[s], 1);
-            mbar_init(&sc_empty[s], kTcDqWarps);
+            mbar_init(&sc_empty[s], C::DQ_WARPS);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&acc_full[b], 1);                   // the leader's tcgen05.commit
-            mbar_init(&acc_empty[b], 2 * kTcEpiWarps);    // leader: both CTAs' epilogue warps
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], C::ACC_EMPTY_ARRIVALS);
         }
         mbar_init(done, 1);
         fence_barrier_init();
     }
-    if (warp == kTcMmaWarp) {
-        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         smem_u32(tmem_slot)),
-                     "r"(kTcTmemCols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    if (warp == C::MMA_WARP) {
+        if (PAIR) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(tmem_slot)),
+                         "r"(C::TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(tmem_slot)),
+                         "r"(C::TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
     tc_fence_before();
-    cluster_sync(); // barriers of both CTAs initialised, TMEM allocated
+    if (PAIR)
+        cluster_sync(); // barriers of both CTAs initialised, TMEM allocated
+    else
+        __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
     const int nk = p.K / kTcKb;
 
-    if (warp == kTcProdWarp) {
+    if (warp == C::PROD_WARP) {
         // ---------------------------------------------------- token producer
         if (lane == 0) {
             const uint64_t pol_t = policy_evict_last();
             uint32_t st_it = 0;
             bool ok = true;
-            for (int i = pair; ok && i < total; i += npairs) {
+            for (int i = unit; ok && i < total; i += nunits) {
                 TcItem it;
-                tc_item<PHASE>(p, i, it);
-                const int half = it.nmma >> 1; // this CTA's token rows
-                const int xr = __ldg(p.xrow + it.e) + it.t0 + static_cast<int>(rank) * half;
-                const int nbox = (half + kTcTokBox - 1) / kTcTokBox;
+                tc_item<PHASE, PAIR>(p, i, it);
+                const int rows = PAIR ? it.nmma >> 1 : it.nmma; // this CTA's token rows
+                const int xr = __ldg(p.xrow + it.e) + it.t0 + static_cast<int>(rank) * rows;
+                const int nbox = (rows + kTcTokBox - 1) / kTcTokBox;
                 for (int kb = 0; kb < nk; ++kb) {
-                    const uint32_t s = st_it % kTcStages, par = (st_it / kTcStages) & 1u;
-                    if (!mbar_wait_cluster(&empty[s], par ^ 1u, p.err)) {
+                    const uint32_t s = st_it % S, par = (st_it / S) & 1u;
+                    if (!mbar_wait(&empty[s], par ^ 1u, p.err)) {
                         ok = false;
                         break;
                     }
-                    if (rank == 0)
-                        mbar_arrive_expect_tx(&full[s], 2u * nbox * kTcTokBox * 128);
-                    const uint32_t fb = cluster_addr(&full[s], 0);
                     uint8_t *dst = smem + s * L::TOK_STAGE;
-                    for (int j = 0; j < nbox; ++j)
-                        tma_load_2d_pair(dst + j * kTcTokBox * 128, &tok_map, kb * kTcKb,
-                                         xr + j * kTcTokBox, fb, pol_t);
+                    if (PAIR) {
+                        if (rank == 0)
+                            mbar_arrive_expect_tx(&full[s], 2u * nbox * kTcTokBox * 128);
+                        const uint32_t fb = cluster_addr(&full[s], 0);
+                        for (int j = 0; j < nbox; ++j)
+                            tma_load_2d_pair(dst + j * kTcTokBox * 128, &tok_map, kb * kTcKb,
+                                             xr + j * kTcTokBox, fb, pol_t);
+                    } else {
+                        mbar_arrive_expect_tx(&full[s], nbox * kTcTokBox * 128);
+                        for (int j = 0; j < nbox; ++j)
+                            tma_load_2d(dst + j * kTcTokBox * 128, &tok_map, kb * kTcKb,
+                                        xr + j * kTcTokBox, &full[s], pol_t);
+                    }
                     ++st_it;
                 }
             }
@@ -405,22 +478,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
         }
-    } else if (warp == kTcPkWarp) {
+    } else if (warp == C::PK_WARP) {
         // ------------------------------------------- packed-weight producer
         if (lane == 0) {
             const uint64_t pol_w = policy_evict_first();
             const bool fence_maps = __ldg(p.tmaps_dirty) != 0;
             uint32_t pk_it = 0, sc_it = 0;
             bool ok = true;
-            for (int i = pair; ok && i < total; i += npairs) {
+            for (int i = unit; ok && i < total; i += nunits) {
                 TcItem it;
-                tc_item<PHASE>(p, i, it);
+                tc_item<PHASE, PAIR>(p, i, it);
                 const uint8_t *tm = p.tmaps + static_cast<size_t>(it.e) * kTcMapCount * kTcMapBytes;
                 if (fence_maps)
                     for (int m = 0; m < kTcMapCount; ++m)
                         tmap_acquire(tm + m * kTcMapBytes);
                 // This CTA's 128 weight rows: 64 gate + 64 up, or 128 down.
-                const int r0 = it.c0 + static_cast<int>(rank) * (tc_cols_per_item<PHASE>() / 2);
+                const int r0 = it.c0 + static_cast<int>(rank) * tc_cols_per_item<PHASE, false>();
                 for (int kb = 0; kb < nk; kb += 2) {
                     if (kb % tc_kb_per_window<FMT>() == 0) {
                         // The rows' next scale window (16 bytes per row).
@@ -468,42 +541,49 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (uint32_t j = sc_it > kTcScSlots ? sc_it - kTcScSlots : 0; j < sc_it; ++j)
                 mbar_wait(&sc_full[j % kTcScSlots], (j / kTcScSlots) & 1u, nullptr);
         }
-    } else if (warp == kTcMmaWarp) {
-        // ------------------------------------------- MMA issuer (leader only)
+    } else if (warp == C::MMA_WARP) {
+        // ------------------------------------ MMA issuer (a pair's leader only)
         if (lane == 0 && rank == 0) {
             uint32_t st_it = 0;
             TcAccState acc;
             bool ok = true;
             const uint32_t tok_base = smem_u32(smem);
-            for (int i = pair; ok && i < total; i += npairs) {
+            for (int i = unit; ok && i < total; i += nunits) {
                 TcItem it;
-                tc_item<PHASE>(p, i, it);
-                const int b = acc.take(it.nmma > 128);
-                if (b != 1 && !mbar_wait_cluster(&acc_empty[0], (acc.use[0] & 1u) ^ 1u, p.err))
+                tc_item<PHASE, PAIR>(p, i, it);
+                const int b = acc.take(it.nmma > C::ACC_HALF);
+                if (b != 1 && !mbar_wait(&acc_empty[0], (acc.use[0] & 1u) ^ 1u, p.err))
                     ok = false;
-                if (ok && b != 0 &&
-                    !mbar_wait_cluster(&acc_empty[1], (acc.use[1] & 1u) ^ 1u, p.err))
+                if (ok && b != 0 && !mbar_wait(&acc_empty[1], (acc.use[1] & 1u) ^ 1u, p.err))
                     ok = false;
                 if (!ok)
                     break;
                 tc_fence_after();
-                const uint32_t d = tmem + (b == 1 ? 128u : 0u);
-                const uint32_t idesc = tc_idesc(it.nmma);
+                const uint32_t d = tmem + (b == 1 ? static_cast<uint32_t>(C::ACC_HALF) : 0u);
+                const uint32_t idesc = tc_idesc(PAIR ? 256 : 128, it.nmma);
                 for (int kb = 0; kb < nk; ++kb) {
-                    const uint32_t s = st_it % kTcStages;
-                    if (!mbar_wait_cluster(&full[s], (st_it / kTcStages) & 1u, p.err)) {
+                    const uint32_t s = st_it % S;
+                    if (!mbar_wait(&full[s], (st_it / S) & 1u, p.err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint64_t bdesc = tc_desc_sw128(tok_base + s * L::TOK_STAGE);
-                    const uint32_t a0 = tmem + L::A_BASE + s * L::A_COLS;
-                    tc_mma_pair(d, a0, bdesc, idesc, kb != 0);
-                    tc_mma_pair(d, a0 + 8, bdesc + 2, idesc, 1u);
-                    tc_mma_pair(d, a0 + 16, bdesc + 4, idesc, 1u);
-                    tc_mma_pair(d, a0 + 24, bdesc + 6, idesc, 1u);
-                    tc_commit_pair(cluster_addr(&empty[s], 0));
-                    tc_commit_pair(cluster_addr(&empty[s], 1));
+                    const uint32_t a0 = tmem + C::A_BASE + s * L::A_COLS;
+                    if (PAIR) {
+                        tc_mma_pair(d, a0, bdesc, idesc, kb != 0);
+                        tc_mma_pair(d, a0 + 8, bdesc + 2, idesc, 1u);
+                        tc_mma_pair(d, a0 + 16, bdesc + 4, idesc, 1u);
+                        tc_mma_pair(d, a0 + 24, bdesc + 6, idesc, 1u);
+                        tc_commit_pair(cluster_addr(&empty[s], 0));
+                        tc_commit_pair(cluster_addr(&empty[s], 1));
+                    } else {
+                        tc_mma_solo(d, a0, bdesc, idesc, kb != 0);
+                        tc_mma_solo(d, a0 + 8, bdesc + 2, idesc, 1u);
+                        tc_mma_solo(d, a0 + 16, bdesc + 4, idesc, 1u);
+                        tc_mma_solo(d, a0 + 24, bdesc + 6, idesc, 1u);
+                        tc_commit_solo(&empty[s]);
+                    }
                     ++st_it;
                 }
                 if (!ok)
@@ -511,18 +591,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int h = 0; h < 2; ++h) {
                     if (b == 1 - h)
                         continue; // the other half
-                    tc_commit_pair(cluster_addr(&acc_full[h], 0));
-                    tc_commit_pair(cluster_addr(&acc_full[h], 1));
+                    if (PAIR) {
+                        tc_commit_pair(cluster_addr(&acc_full[h], 0));
+                        tc_commit_pair(cluster_addr(&acc_full[h], 1));
+                    } else {
+                        tc_commit_solo(&acc_full[h]);
+                    }
                     ++acc.use[h];
                 }
             }
             // Every MMA this thread issued has completed once `done` flips.
-            tc_commit_pair(cluster_addr(done, 0));
+            if (PAIR)
+                tc_commit_pair(cluster_addr(done, 0));
+            else
+                tc_commit_solo(done);
             mbar_wait(done, 0, nullptr);
         }
-    } else if (warp >= kTcDqWarp0 && warp < kTcDqWarp0 + kTcDqWarps) {
+    } else if (warp >= C::DQ_WARP0 && warp < C::DQ_WARP0 + C::DQ_WARPS) {
         // -------------------------------------------------------------- dequant
-        const int q = warp & 3, set = (warp - kTcDqWarp0) >> 2;
+        const int q = warp & 3, set = (warp - C::DQ_WARP0) >> 2;
         uint32_t pk_it = 0, sc_it = 0, st_it = 0;
         bool ok = true;
         const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
@@ -543,9 +630,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // SW64: 16-byte chunk c of box row j sits at chunk c ^ ((j >> 1) & 3).
         const uint32_t sw = static_cast<uint32_t>((((pk_off & 4095) >> 6) >> 1) & 3);
         uint4 win = make_uint4(0, 0, 0, 0);
-        for (int i = pair; ok && i < total; i += npairs) {
+        for (int i = unit; ok && i < total; i += nunits) {
             for (int sl = 0; sl < nk / 2 && ok; ++sl) {
-                const int kb = 2 * sl + set;
                 if ((2 * sl) % KPW == 0) {
                     // First slot of a scale window: this row's 16 bytes to registers.
                     const uint32_t w = sc_it % kTcScSlots;
@@ -567,71 +653,88 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     break;
                 }
                 const uint32_t pk_addr = smem_u32(smem + L::OFF_PK + ps * L::PK_STAGE + pk_off);
-                const uint4 w0 = lds128(pk_addr + ((static_cast<uint32_t>(2 * set) ^ sw) << 4));
-                const uint4 w1 = lds128(pk_addr + ((static_cast<uint32_t>(2 * set + 1) ^ sw) << 4));
+                // The slot's two k-blocks: one each for two sets, both for one.
+                uint4 w0[2], w1[2];
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                    if (C::DQ_SETS == 2 && jj != set)
+                        continue;
+                    w0[jj] = lds128(pk_addr + ((static_cast<uint32_t>(2 * jj) ^ sw) << 4));
+                    w1[jj] = lds128(pk_addr + ((static_cast<uint32_t>(2 * jj + 1) ^ sw) << 4));
+                }
                 __syncwarp();
                 if (lane == 0)
                     mbar_arrive(&pk_empty[ps]); // the slot's bytes are in registers
                 ++pk_it;
-                const int kw = kb % KPW;
-                __half2 sc0, sc1;
-                if (FMT == MVLLM_FMT_MXFP4) {
-                    const uint32_t word = sel4(win, kw >> 1);
-                    const uint32_t e0 = (word >> (16 * (kw & 1))) & 0xFFu;
-                    const uint32_t e1 = (word >> (16 * (kw & 1) + 8)) & 0xFFu;
-                    if ((e0 > 140u && e0 != 255u) || (e1 > 140u && e1 != 255u))
-                        set_error(p.err, MVLLM_ERR_RANGE);
-                    sc0 = __float2half2_rn(ue8m0_to_f32(e0));
-                    sc1 = __float2half2_rn(ue8m0_to_f32(e1));
-                } else {
-                    sc0 = __float2half2_rn(__uint_as_float(sel4(win, kw)));
-                    sc1 = sc0;
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                    if (C::DQ_SETS == 2 && jj != set)
+                        continue;
+                    const int kw = (2 * sl + jj) % KPW;
+                    __half2 sc0, sc1;
+                    if (FMT == MVLLM_FMT_MXFP4) {
+                        const uint32_t word = sel4(win, kw >> 1);
+                        const uint32_t e0 = (word >> (16 * (kw & 1))) & 0xFFu;
+                        const uint32_t e1 = (word >> (16 * (kw & 1) + 8)) & 0xFFu;
+                        if ((e0 > 140u && e0 != 255u) || (e1 > 140u && e1 != 255u))
+                            set_error(p.err, MVLLM_ERR_RANGE);
+                        sc0 = __float2half2_rn(ue8m0_to_f32(e0));
+                        sc1 = __float2half2_rn(ue8m0_to_f32(e1));
+                    } else {
+                        sc0 = __float2half2_rn(__uint_as_float(sel4(win, kw)));
+                        sc1 = sc0;
+                    }
+                    uint32_t v[32];
+                    tc_dequant_row<FMT>(w0[jj], w1[jj], sc0, sc1, v);
+                    // The k-block's stage of the shared ring.
+                    const uint32_t sidx = st_it + static_cast<uint32_t>(jj);
+                    const uint32_t s = sidx % S;
+                    if (!__all_sync(0xffffffffu,
+                                    mbar_wait(&empty[s], ((sidx / S) & 1u) ^ 1u, p.err))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    tc_st32(tmem + lane_addr + C::A_BASE + s * L::A_COLS, v);
+                    tc_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (PAIR)
+                            mbar_arrive_cluster(cluster_addr(&full[s], 0));
+                        else
+                            mbar_arrive(&full[s]);
+                    }
                 }
-                uint32_t v[32];
-                tc_dequant_row<FMT>(w0, w1, sc0, sc1, v);
-                // This set's k-block is stage st_it + set of the shared ring.
-                const uint32_t sidx = st_it + static_cast<uint32_t>(set);
-                const uint32_t s = sidx % kTcStages;
-                if (!__all_sync(0xffffffffu, mbar_wait_cluster(&empty[s],
-                                                               ((sidx / kTcStages) & 1u) ^ 1u,
-                                                               p.err))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                tc_st32(tmem + lane_addr + L::A_BASE + s * L::A_COLS, v);
-                tc_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0)
-                    mbar_arrive_cluster(cluster_addr(&full[s], 0));
                 st_it += 2;
             }
         }
-    } else if (warp < kTcEpiWarps) {
+    } else if (warp < C::EPI_WARPS) {
         // ------------------------------------------------------------- epilogue
         const int q = warp & 3, whalf = warp >> 2;
+        constexpr int CH_STEP = 32 * (C::EPI_WARPS / 4);
         const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
         TcAccState acc;
         bool ok = true;
-        for (int i = pair; ok && i < total; i += npairs) {
+        for (int i = unit; ok && i < total; i += nunits) {
             TcItem it;
-            tc_item<PHASE>(p, i, it);
-            const int b = acc.take(it.nmma > 128);
+            tc_item<PHASE, PAIR>(p, i, it);
+            const int b = acc.take(it.nmma > C::ACC_HALF);
             bool got = true;
             if (b != 1)
-                got = mbar_wait_cluster(&acc_full[0], acc.use[0] & 1u, p.err);
+                got = mbar_wait(&acc_full[0], acc.use[0] & 1u, p.err);
             if (got && b != 0)
-                got = mbar_wait_cluster(&acc_full[1], acc.use[1] & 1u, p.err);
+                got = mbar_wait(&acc_full[1], acc.use[1] & 1u, p.err);
             if (!__all_sync(0xffffffffu, got)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const int orow = __ldg(p.orow + it.e) + it.t0;
-            const uint32_t accb = tmem + lane_addr + (b == 1 ? 128u : 0u);
+            const uint32_t accb =
+                tmem + lane_addr + (b == 1 ? static_cast<uint32_t>(C::ACC_HALF) : 0u);
 #pragma unroll 1
-            for (int ch = 32 * whalf; ch < it.n; ch += 64) {
+            for (int ch = 32 * whalf; ch < it.n; ch += CH_STEP) {
                 uint32_t v[32];
                 tc_ld32(accb + ch, v);
                 tc_wait_ld();
@@ -665,10 +768,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                if (b != 1)
-                    mbar_arrive_cluster(cluster_addr(&acc_empty[0], 0));
-                if (b != 0)
-                    mbar_arrive_cluster(cluster_addr(&acc_empty[1], 0));
+                for (int h = 0; h < 2; ++h) {
+                    if (b == 1 - h)
+                        continue;
+                    if (PAIR)
+                        mbar_arrive_cluster(cluster_addr(&acc_empty[h], 0));
+                    else
+                        mbar_arrive(&acc_empty[h]);
+                }
             }
             if (b != 1)
                 ++acc.use[0];
@@ -678,12 +785,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 
     tc_fence_before();
-    cluster_sync(); // the pair's MMAs, copies and remote arrivals are all done
-    if (warp == kTcMmaWarp) {
+    if (PAIR)
+        cluster_sync(); // the pair's MMAs, copies and remote arrivals are all done
+    else
+        __syncthreads();
+    if (warp == C::MMA_WARP) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(kTcTmemCols)
-                     : "memory");
+        if (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                         "r"(C::TMEM_COLS)
+                         : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                         "r"(C::TMEM_COLS)
+                         : "memory");
     }
 }
 

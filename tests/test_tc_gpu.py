@@ -1,8 +1,9 @@
 """Parity of the tensor-core (tcgen05/TMEM) expert path against the CPU oracle.
 
-The path takes experts with many rows (prefill chunks, skewed routing).  The
-environment switches the routing between paths per call:
-MVLLM_TC_MIN_TOTAL / MVLLM_TC_MIN_ROWS (thresholds) and MVLLM_TC_OFF.
+The path takes experts with many rows (prefill chunks, skewed routing): their
+256-row token tiles run on CTA pairs, a rest of at most 64 rows on single
+CTAs.  The environment switches the routing per call: MVLLM_TC_MIN_TOTAL /
+MVLLM_TC_MIN_ROWS (thresholds), MVLLM_TC_NO_SOLO (pairs only), MVLLM_TC_OFF.
 Tolerance as everywhere: <= 1e-2 relative L2 and <= 2e-2 max-abs.
 """
 import numpy as np
@@ -65,6 +66,9 @@ def test_tc_matches_oracle(moe, port, monkeypatch, name):
     assert_close(got, want, name + " tensor-core")
     again = host_block(moe, c)
     np.testing.assert_array_equal(got, again)  # deterministic run to run
+    monkeypatch.setenv("MVLLM_TC_NO_SOLO", "1")  # every tile on CTA pairs
+    assert_close(host_block(moe, c), want, name + " tensor-core, pairs only")
+    monkeypatch.delenv("MVLLM_TC_NO_SOLO")
     monkeypatch.setenv("MVLLM_TC_OFF", "1")
     dec = host_block(moe, c)
     assert_close(dec, want, name + " decode")
