@@ -292,6 +292,43 @@ __device__ __forceinline__ float apply_act(float g, float u, int act, float a, f
     return g * sigmoid_ref(g) * u;
 }
 
+// The same activations from the SFU's approximate tanh and exp2 (PTX
+// tanh.approx.f32 and ex2.approx.f32, relative errors near 2^-11 and 2^-22)
+// and an approximate reciprocal.  The result is rounded to f16 (2^-11)
+// anyway; the tensor-core epilogue, which evaluates one activation per
+// output element and token, uses these so that it keeps pace with the MMAs.
+__device__ __forceinline__ float tanh_fast(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float sigmoid_fast(float x) {
+    // 1 / (1 + e^-x) with e^-x = 2^(-x log2 e); saturates to 0 / 1 at the ends.
+    float t, r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(-1.4426950408889634f * x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + t));
+    return r;
+}
+// ia, ib: 1/a and 1/b, computed once per launch by the caller.
+__device__ __forceinline__ float apply_act_fast(float g, float u, int act, float a, float b,
+                                                float ia, float ib) {
+    if (act == MVLLM_ACT_CLAMP_SWIGLU) {
+        if (a > 0.f && g > a)
+            g = a;
+        const float s = g * sigmoid_fast(g);
+        if (a > 0.f) {
+            if (u > a)
+                u = a;
+            if (u < -a)
+                u = -a;
+        }
+        return s * u;
+    }
+    if (act == MVLLM_ACT_SITU)
+        return a * tanh_fast(g * ia) * sigmoid_fast(g) * b * tanh_fast(u * ib);
+    return g * sigmoid_fast(g) * u;
+}
+
 // Position of source column k inside the f16 operand layout of a format.
 // MXFP4 keeps natural order; int4-g64 interleaves each aligned 8-chunk as
 // k0,k4,k1,k5,k2,k6,k3,k7 to match int4x8_to_f16x8's pair order.

@@ -666,6 +666,8 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                 if (lane == 0)
                     mbar_arrive(&pk_empty[ps]); // the slot's bytes are in registers
                 ++pk_it;
+                // Convert and store this warp's k-blocks of the slot, then wait
+                // for the stores once (the registers are free at issue).
 #pragma unroll
                 for (int jj = 0; jj < 2; ++jj) {
                     if (C::DQ_SETS == 2 && jj != set)
@@ -696,10 +698,18 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                     }
                     tc_fence_after();
                     tc_st32(tmem + lane_addr + C::A_BASE + s * L::A_COLS, v);
-                    tc_wait_st();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
+                }
+                if (!ok)
+                    break;
+                tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+#pragma unroll
+                    for (int jj = 0; jj < 2; ++jj) {
+                        if (C::DQ_SETS == 2 && jj != set)
+                            continue;
+                        const uint32_t s = (st_it + static_cast<uint32_t>(jj)) % S;
                         if (PAIR)
                             mbar_arrive_cluster(cluster_addr(&full[s], 0));
                         else
@@ -713,6 +723,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
         // ------------------------------------------------------------- epilogue
         const int q = warp & 3, whalf = warp >> 2;
         constexpr int CH_STEP = 32 * (C::EPI_WARPS / 4);
+        const float ia = 1.f / p.act_a, ib = 1.f / p.act_b; // SiTU's divisions, once
         const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
         TcAccState acc;
         bool ok = true;
@@ -753,7 +764,8 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                         const float u = gate ? other : mine_hi;
                         if (tb + t < it.n)
                             hp[static_cast<size_t>(orow + tb + t) * p.O + stage_pos(col, FMT)] =
-                                __float2half_rn(apply_act(g, u, p.act, p.act_a, p.act_b));
+                                __float2half_rn(
+                                    apply_act_fast(g, u, p.act, p.act_a, p.act_b, ia, ib));
                     }
                 } else {
                     float *yp = static_cast<float *>(p.out);
