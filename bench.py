@@ -43,6 +43,11 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the config[3] prefill measurement")
+    ap.add_argument("--prefill-steps", type=int, default=10)
+    ap.add_argument("--prefill-tokens", type=int, default=4096,
+                    help="config[3]: 4096; fewer only to size a profiler capture")
     ap.add_argument("--experts", type=int, default=256,
                     help="routed experts (BASELINE config[1]: 256); fewer only to size a "
                          "profiler capture")
@@ -61,6 +66,14 @@ def peaks():
             d = json.load(f)
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def bf16_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"])
+    return 1590.0
 
 
 def traffic_ratio():
@@ -199,6 +212,76 @@ def graph_throughput(moe, torch, wl, steps, warmup):
     ms = a.elapsed_time(b)
     del graph
     return wl.B * reps * N_INPUTS / (ms / 1e3), ms / (reps * N_INPUTS)
+
+
+# ------------------------------------------------------------ prefill --
+PREFILL_T = 4096
+
+
+def zipf_routing(torch, T, E, K, g, s=1.1):
+    """BASELINE config[3] routing: logits = -s ln(rank) + Gumbel noise per token
+    over a seeded random ranking of the experts, softmax, top-K renormalised."""
+    perm = torch.randperm(E, generator=g, device="cuda")
+    rank = torch.empty(E, device="cuda")
+    rank[perm] = torch.arange(1, E + 1, device="cuda", dtype=torch.float32)
+    u = torch.rand((T, E), generator=g, device="cuda").clamp_min(1e-20)
+    logits = -s * torch.log(rank)[None, :] - torch.log(-torch.log(u))
+    vals, idx = torch.topk(torch.softmax(logits, dim=1), K, dim=1)
+    return idx.int().contiguous(), (vals / vals.sum(1, keepdim=True)).float().contiguous()
+
+
+def prefill_bench(moe, torch, wl, steps, peak_tf, peak_gbs, T=PREFILL_T):
+    """Config[3]: 4096 tokens, the 256 routed MXFP4 experts of the decode
+    workload (same shape and format), Zipf s=1.1 routing, no shared expert,
+    bf16 activations, f32 accumulation.  Large experts run on the tensor-core
+    kernels, the smallest on the decode kernels."""
+    D, I, E, K = CFG["D"], CFG["I"], CFG["E"], CFG["K"]
+    g = torch.Generator(device="cuda").manual_seed(4242)
+    idx, wt = zipf_routing(torch, T, E, K, g)
+    x = torch.randn((T, D), generator=g, device="cuda").to(torch.bfloat16)
+    out = torch.zeros((T, D), dtype=torch.float32, device="cuda")
+    ws = torch.empty(moe.layer_workspace_bytes(T, K, E, 0, D, I, CFG["fmt"]), dtype=torch.uint8,
+                     device="cuda")
+    cnt = torch.bincount(idx.flatten().long(), minlength=E).cpu()
+
+    def step():
+        out.zero_()
+        moe.layer_dev(T, K, E, 0, D, I, CFG["fmt"], idx, wt, x, wl.tables, out, CFG["act"],
+                      CFG["act_a"], CFG["act_b"], ws)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    moe.profile_enable(True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ph = moe.profile_read()
+    moe.profile_enable(False)
+    ms = a.elapsed_time(b) / steps
+    e_ms = (ph["expert_phase1"][0] + ph["expert_phase2"][0]) / steps
+    flops = 2.0 * T * K * 3 * D * I
+    touched = int((cnt > 0).sum())
+    alg_bytes = touched * EXPERT_BYTES + T * D * 2 + T * D * 4
+    tf = flops / (e_ms / 1e3) / 1e12
+    return {
+        "workload": f"config[3] MXFP4 prefill: {T} tokens, hidden 7168, inter 2048, {E} experts "
+                    "top-8 (Zipf s=1.1 routing), SiTU(4,25), bf16 activations",
+        "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms, "steps": steps,
+        "expert_rows_per_expert": {"min": int(cnt.min()), "max": int(cnt.max()),
+                                   "below_128": int((cnt < 128).sum())},
+        "phases_ms_per_step": {k: v[0] / steps for k, v in ph.items()},
+        "tensor": {"flops_per_step": flops, "achieved_tflops": tf, "peak_tflops": peak_tf,
+                   "frac": tf / peak_tf if peak_tf else None,
+                   "peak_kind": "measured bf16 dense (the kernels run kind::f16 MMAs)",
+                   "kernel_ms_per_step": e_ms},
+        "hbm": {"algorithmic_bytes_per_step": alg_bytes,
+                "achieved_gbs": alg_bytes / (ms / 1e3) / 1e9, "peak_gbs": peak_gbs,
+                "frac": alg_bytes / (ms / 1e3) / 1e9 / peak_gbs},
+    }
 
 
 # ------------------------------------------------------------ CPU baseline --
@@ -406,6 +489,12 @@ def main():
             tps, mstep = graph_throughput(moe, torch, wb, 320, 32)
             sweep[f"B{bb}"] = {"tokens_per_s": tps * world, "ms_per_step": mstep}
 
+    # config[3] prefill (tensor-core kernels), per rank
+    prefill = None
+    if not args.no_prefill:
+        prefill = prefill_bench(moe, torch, wl, args.prefill_steps, bf16_peak(), peak,
+                                args.prefill_tokens)
+
     # CPU baseline (rank 0, N=1 only): reference moe_block on host threads
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -443,13 +532,21 @@ def main():
                          "algorithmic_bytes_per_step": alg_bytes,
                          "kernel_ms_per_step": k_ms},
             "phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
-            "gpu_launches": int(sum(v[1] for v in phases.values()) + args.steps),
+            # per decode step: permute (2 kernels), gather, plan, tensor-map
+            # build, decode phase 1, decode phase 2, combine
+            "gpu_launches": 8 * args.steps,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "mvllm_moe_layer_host"},
             "cpu_baseline": cpu,
             "clocks": clk.report(),
             "sweep": sweep,
+            "prefill": prefill,
         }
+        if prefill and cpu and cpu.get("value"):
+            # The reference's rate in expert rows/s (9 rows per config[1] token)
+            # extrapolated to one config[3] step of 32768 rows.
+            prefill["cpu_reference_ms_per_step_extrapolated"] = (
+                args.prefill_tokens * CFG["K"] / (cpu["value"] * 9.0) * 1e3)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
