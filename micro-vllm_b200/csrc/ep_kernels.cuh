@@ -1,0 +1,124 @@
+// ep_kernels.cuh -- expert-parallel dispatch and combine for the MoE layer
+// sharded over ranks (one GPU each).
+//
+// Expert e lives on rank e % nranks as that rank's local expert e / nranks
+// (strided placement: with Zipf-skewed routing it balances the ranks far
+// better than contiguous blocks).  A step on rank r:
+//   plan     which of r's tokens each rank needs (a token goes to rank d once,
+//            however many of its experts d owns) and where each lands in the
+//            destination-major send buffer;
+//   pack     token rows + per-slot local expert ids (-1 where another rank
+//            owns the slot) + routing weights into the send buffer;
+//   (all-to-all: NCCL, counts then rows)
+//   compute  the received rows through the rank's local experts
+//            (mvllm_moe_layer_dev: slots marked -1 are skipped);
+//   (all-to-all back: each token's partial sums per rank)
+//   combine  out[c] += the partials of token c in ascending rank order.
+// The reference runs every expert on one host (metal_ops.cpp:466-509 over the
+// rows that moe_layer_n gathers, glm53.cpp:1936-1994); the partition, the
+// exchanges and the combine order are this layer's own.  Every sum has a
+// fixed order, so runs are bit-reproducible; the association differs from the
+// single-GPU order, within the parity tolerance.
+#pragma once
+
+#include "aux_kernels.cuh"
+
+namespace mvb {
+
+// One CTA: per destination rank a block scan over the tokens gives the
+// position of each sent token among those of that rank; a second pass adds the
+// destination offsets.  pos[c * nranks + d] = send-buffer row or -1.
+__global__ void ep_plan_kernel(const int *__restrict__ idx, int T, int K, int E, int nranks,
+                               int *__restrict__ pos, int *__restrict__ send_cnt) {
+    __shared__ int warp_sums[32];
+    __shared__ int carry[32];
+    __shared__ int off[33];
+    if (threadIdx.x < 32)
+        carry[threadIdx.x] = 0;
+    __syncthreads();
+    for (int c0 = 0; c0 < T; c0 += blockDim.x) {
+        const int c = c0 + threadIdx.x;
+        uint32_t mask = 0;
+        if (c < T)
+            for (int k = 0; k < K; ++k) {
+                const int e = idx[static_cast<size_t>(c) * K + k];
+                if (e >= 0 && e < E)
+                    mask |= 1u << (e % nranks);
+            }
+        for (int d = 0; d < nranks; ++d) {
+            const int f = (mask >> d) & 1;
+            int tot;
+            const int ex = block_exclusive_scan(f, warp_sums, &tot);
+            if (c < T)
+                pos[static_cast<size_t>(c) * nranks + d] = f ? carry[d] + ex : -1;
+            __syncthreads();
+            if (threadIdx.x == 0)
+                carry[d] += tot;
+            __syncthreads();
+        }
+    }
+    if (threadIdx.x == 0) {
+        off[0] = 0;
+        for (int d = 0; d < nranks; ++d) {
+            send_cnt[d] = carry[d];
+            off[d + 1] = off[d] + carry[d];
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * nranks; i += blockDim.x) {
+        const int p = pos[i];
+        if (p >= 0)
+            pos[i] = p + off[i % nranks];
+    }
+}
+
+// One CTA per token: its row (16-byte vectors) to every destination that
+// needs it, with the slots' local ids (or -1) and weights.
+template <typename TX>
+__global__ void ep_pack_kernel(const TX *__restrict__ x, const int *__restrict__ idx,
+                               const float *__restrict__ wt, int T, int K, int D, int E,
+                               int nranks, const int *__restrict__ pos, TX *__restrict__ send_x,
+                               int *__restrict__ send_idx, float *__restrict__ send_wt) {
+    constexpr int VEC = 16 / sizeof(TX);
+    for (int c = blockIdx.x; c < T; c += gridDim.x) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(c) * D);
+        for (int d = 0; d < nranks; ++d) {
+            const int p = pos[static_cast<size_t>(c) * nranks + d];
+            if (p < 0)
+                continue;
+            uint4 *dst = reinterpret_cast<uint4 *>(send_x + static_cast<size_t>(p) * D);
+            for (int v = threadIdx.x; v < D / VEC; v += blockDim.x)
+                dst[v] = src[v];
+            for (int k = threadIdx.x; k < K; k += blockDim.x) {
+                const int e = idx[static_cast<size_t>(c) * K + k];
+                const bool mine = e >= 0 && e < E && e % nranks == d;
+                send_idx[static_cast<size_t>(p) * K + k] = mine ? e / nranks : -1;
+                send_wt[static_cast<size_t>(p) * K + k] = wt[static_cast<size_t>(c) * K + k];
+            }
+        }
+    }
+}
+
+// out[c] += sum over ranks d ascending of back[pos[c, d]] (f32, float4).
+__global__ void ep_combine_kernel(const float *__restrict__ back, const int *__restrict__ pos,
+                                  int T, int nranks, int D, float *__restrict__ out) {
+    const int n4 = D / 4;
+    for (int c = blockIdx.y; c < T; c += gridDim.y) {
+        for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < n4; v += gridDim.x * blockDim.x) {
+            float4 acc = reinterpret_cast<const float4 *>(out + static_cast<size_t>(c) * D)[v];
+            for (int d = 0; d < nranks; ++d) {
+                const int p = pos[static_cast<size_t>(c) * nranks + d];
+                if (p < 0)
+                    continue;
+                const float4 b = reinterpret_cast<const float4 *>(back + static_cast<size_t>(p) * D)[v];
+                acc.x = __fadd_rn(acc.x, b.x);
+                acc.y = __fadd_rn(acc.y, b.y);
+                acc.z = __fadd_rn(acc.z, b.z);
+                acc.w = __fadd_rn(acc.w, b.w);
+            }
+            reinterpret_cast<float4 *>(out + static_cast<size_t>(c) * D)[v] = acc;
+        }
+    }
+}
+
+} // namespace mvb

@@ -6,6 +6,7 @@
 #include "aux_kernels.cuh"
 #include "decode_ffn.cuh"
 #include "tc_ffn.cuh"
+#include "ep_kernels.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -1421,6 +1422,57 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     c.d2h_ms += cc;
     c.calls += 1;
     c.rows += uint64_t(T) * (K + n_shared);
+    return MVLLM_OK;
+}
+
+// ------------------------------------------------------ expert parallelism --
+int mvllm_moe_ep_plan_dev(void *stream, const int *idx, int T, int K, int E, int nranks, int *pos,
+                          int *send_cnt) {
+    if (!idx || !pos || !send_cnt || T < 0 || K < 1 || E < 1 || nranks < 1 || nranks > 32)
+        return fail(MVLLM_ERR_INVALID, "ep_plan_dev: invalid arguments");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    ep_plan_kernel<<<1, 1024, 0, st>>>(idx, T, K, E, nranks, pos, send_cnt);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+int mvllm_moe_ep_pack_dev(void *stream, const void *x, int x_dtype, const int *idx,
+                          const float *wt, int T, int K, int D, int E, int nranks, const int *pos,
+                          void *send_x, int *send_idx, float *send_wt) {
+    if (!x || !idx || !wt || !pos || !send_x || !send_idx || !send_wt || T < 0 || K < 1 ||
+        D < 8 || D % 8 != 0 || E < 1 || nranks < 1 || nranks > 32 ||
+        (x_dtype != MVLLM_DTYPE_F32 && x_dtype != MVLLM_DTYPE_BF16) ||
+        ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(send_x)) & 15u))
+        return fail(MVLLM_ERR_INVALID, "ep_pack_dev: invalid arguments");
+    if (T == 0)
+        return MVLLM_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int blocks = std::min(T, 65535);
+    if (x_dtype == MVLLM_DTYPE_BF16)
+        ep_pack_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+            static_cast<const __nv_bfloat16 *>(x), idx, wt, T, K, D, E, nranks, pos,
+            static_cast<__nv_bfloat16 *>(send_x), send_idx, send_wt);
+    else
+        ep_pack_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float *>(x), idx, wt, T, K,
+                                                       D, E, nranks, pos,
+                                                       static_cast<float *>(send_x), send_idx,
+                                                       send_wt);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+int mvllm_moe_ep_combine_dev(void *stream, const float *back, const int *pos, int T, int nranks,
+                             int D, float *out) {
+    if (!pos || !out || T < 0 || nranks < 1 || nranks > 32 || D < 4 || D % 4 != 0 ||
+        (!back && T > 0) ||
+        ((reinterpret_cast<uintptr_t>(back) | reinterpret_cast<uintptr_t>(out)) & 15u))
+        return fail(MVLLM_ERR_INVALID, "ep_combine_dev: invalid arguments");
+    if (T == 0)
+        return MVLLM_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
+    ep_combine_kernel<<<grid, 256, 0, st>>>(back, pos, T, nranks, D, out);
+    CUDA_TRY(cudaGetLastError());
     return MVLLM_OK;
 }
 

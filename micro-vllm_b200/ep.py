@@ -1,0 +1,156 @@
+"""Expert-parallel routed MoE layer: one rank per GPU, experts sharded.
+
+Expert e lives on rank e % nranks as that rank's local expert e // nranks
+(strided placement balances Zipf-skewed routing far better than contiguous
+blocks).  One layer step on rank r, for r's own tokens:
+
+  1. plan      which ranks need each token, and its row in the
+               destination-major send buffer        (mvllm_moe_ep_plan_dev)
+  2. counts    all-to-all of the per-destination row counts      (NCCL)
+  3. pack      token rows, per-slot local expert ids (-1 where another rank
+               owns the slot) and weights into the send buffer
+                                                     (mvllm_moe_ep_pack_dev)
+  4. dispatch  all-to-all of rows, ids and weights                (NCCL)
+  5. compute   the received rows through r's local experts: the routed layer
+               on device (mvllm_moe_layer_dev) with E = r's expert count;
+               slots marked -1 are skipped by its permutation
+  6. return    all-to-all of the f32 partial sums back to the token owners
+  7. combine   out[c] += partials of token c in ascending rank order
+                                                     (mvllm_moe_ep_combine_dev)
+
+The reference runs every expert on one host; the partition, the exchanges
+and the combine order belong to this layer.  Every sum has a fixed order, so
+runs are bit-reproducible; the association differs from the single-GPU
+order, within the parity tolerance.
+
+The device steps go through an ``ops`` object so that the orchestration
+(counts, splits, buffers, exchange order) is the same code whether the ops
+are the CUDA library (``CudaOps``) or a CPU test double, and whether the
+exchange is torch.distributed (NCCL on GPUs, gloo on CPU) or an in-process
+emulation of several ranks.
+"""
+from __future__ import annotations
+
+import mvllm_moe as moe
+
+
+def owner(e, nranks):
+    return e % nranks
+
+
+def local_id(e, nranks):
+    return e // nranks
+
+
+def local_experts(rank, nranks, E):
+    """Global ids of the experts rank `rank` holds, in local-id order."""
+    return list(range(rank, E, nranks))
+
+
+class CudaOps:
+    """Device steps of a rank through the sm_100a library."""
+
+    def __init__(self, torch, E, K, D, I, fmt, act, act_a, act_b, local_tables, nranks,
+                 max_recv_rows):
+        self.torch = torch
+        self.E, self.K, self.D, self.I, self.fmt = E, K, D, I, fmt
+        self.act, self.act_a, self.act_b = act, act_a, act_b
+        self.tables = local_tables
+        self.nranks = nranks
+        self.E_local = len(local_tables[0]) if local_tables else 0
+        self.ws = torch.empty(moe.layer_workspace_bytes(max(max_recv_rows, 1), K,
+                                                        max(self.E_local, 1), 0, D, I, fmt),
+                              dtype=torch.uint8, device="cuda")
+        self.max_recv_rows = max_recv_rows
+
+    def plan(self, idx):
+        T = idx.shape[0]
+        pos = self.torch.empty((T, self.nranks), dtype=self.torch.int32, device=idx.device)
+        cnt = self.torch.empty(self.nranks, dtype=self.torch.int32, device=idx.device)
+        moe.ep_plan_dev(idx, self.E, self.nranks, pos, cnt)
+        return pos, cnt
+
+    def pack(self, x, idx, wt, pos, rows):
+        t = self.torch
+        send_x = t.empty((rows, self.D), dtype=x.dtype, device=x.device)
+        send_idx = t.empty((rows, self.K), dtype=t.int32, device=x.device)
+        send_wt = t.empty((rows, self.K), dtype=t.float32, device=x.device)
+        if rows:
+            moe.ep_pack_dev(x, idx, wt, self.E, self.nranks, pos, send_x, send_idx, send_wt)
+        return send_x, send_idx, send_wt
+
+    def compute(self, rx, ridx, rwt):
+        R = rx.shape[0]
+        part = self.torch.zeros((R, self.D), dtype=self.torch.float32, device=rx.device)
+        if R and self.E_local:
+            if R > self.max_recv_rows:
+                raise ValueError(f"received {R} rows, above the {self.max_recv_rows} sized for")
+            moe.layer_dev(R, self.K, self.E_local, 0, self.D, self.I, self.fmt, ridx, rwt, rx,
+                          self.tables, part, self.act, self.act_a, self.act_b, self.ws)
+        return part
+
+    def combine(self, back, pos, out):
+        moe.ep_combine_dev(back, pos, out)
+
+
+class EPLayer:
+    """The layer step of one rank; `ops` holds the device steps."""
+
+    def __init__(self, ops, rank, nranks, D, K):
+        self.ops, self.rank, self.nranks, self.D, self.K = ops, rank, nranks, D, K
+
+    # ---- phases (the distributed forward and the in-process emulation both use them)
+    def prepare(self, x, idx, wt):
+        pos, cnt = self.ops.plan(idx)
+        return pos, cnt
+
+    def pack(self, x, idx, wt, pos, send_splits):
+        return self.ops.pack(x, idx, wt, pos, int(sum(send_splits)))
+
+    def forward(self, x, idx, wt, out, dist, group=None):
+        """One step through torch.distributed (all ranks call it in step)."""
+        t = self.ops.torch
+        pos, cnt = self.prepare(x, idx, wt)
+        rcnt = t.empty_like(cnt)
+        dist.all_to_all_single(rcnt, cnt, group=group)
+        sc = [int(v) for v in cnt.tolist()]
+        rc = [int(v) for v in rcnt.tolist()]
+        sx, sidx, swt = self.pack(x, idx, wt, pos, sc)
+        R = sum(rc)
+        rx = t.empty((R, self.D), dtype=x.dtype, device=x.device)
+        ridx = t.empty((R, self.K), dtype=t.int32, device=x.device)
+        rwt = t.empty((R, self.K), dtype=t.float32, device=x.device)
+        dist.all_to_all_single(rx, sx, rc, sc, group=group)
+        dist.all_to_all_single(ridx, sidx, rc, sc, group=group)
+        dist.all_to_all_single(rwt, swt, rc, sc, group=group)
+        part = self.ops.compute(rx, ridx, rwt)
+        back = t.empty((sum(sc), self.D), dtype=t.float32, device=x.device)
+        dist.all_to_all_single(back, part, sc, rc, group=group)
+        self.ops.combine(back, pos, out)
+        return {"sent_rows": sum(sc), "received_rows": R}
+
+
+def emulate_step(layers, xs, idxs, wts, outs, torch):
+    """All ranks' steps in one process: the exchanges become slicing and
+    concatenation of the ranks' buffers in the order NCCL's all-to-all uses
+    (rank d receives, from each source s ascending, s's rows for d)."""
+    N = len(layers)
+    plans = [L.prepare(x, i, w) for L, x, i, w in zip(layers, xs, idxs, wts)]
+    sc = [[int(v) for v in cnt.tolist()] for (_, cnt) in plans]  # sc[s][d]
+    packs = [L.pack(x, i, w, pos, sc[s]) for s, (L, x, i, w, (pos, _)) in
+             enumerate(zip(layers, xs, idxs, wts, plans))]
+
+    def chunk(buf, splits, d):
+        a = sum(splits[:d])
+        return buf[a:a + splits[d]]
+
+    parts = []
+    for d in range(N):
+        rx = torch.cat([chunk(packs[s][0], sc[s], d) for s in range(N)])
+        ridx = torch.cat([chunk(packs[s][1], sc[s], d) for s in range(N)])
+        rwt = torch.cat([chunk(packs[s][2], sc[s], d) for s in range(N)])
+        parts.append(layers[d].ops.compute(rx, ridx, rwt))
+    rc = [[sc[s][d] for s in range(N)] for d in range(N)]  # rc[d][s]
+    for s in range(N):
+        back = torch.cat([chunk(parts[d], rc[d], s) for d in range(N)])
+        layers[s].ops.combine(back, plans[s][0], outs[s])

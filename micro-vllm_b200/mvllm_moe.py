@@ -36,7 +36,8 @@ C_SYMBOLS = (
     "mvllm_moe_permute_dev", "mvllm_moe_layer_workspace", "mvllm_moe_layer_dev",
     "mvllm_moe_layer_host", "mvllm_quantize_int4_g64_dev", "mvllm_pack_mxfp4_dev",
     "mvllm_matmul_dev", "mvllm_moe_profile_enable", "mvllm_moe_profile_read",
-    "mvllm_moe_permute_dev_noalloc",
+    "mvllm_moe_permute_dev_noalloc", "mvllm_moe_ep_plan_dev", "mvllm_moe_ep_pack_dev",
+    "mvllm_moe_ep_combine_dev",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -85,6 +86,9 @@ def lib():
             "mvllm_moe_profile_enable": (None, [i]),
             "mvllm_moe_profile_read": (i, [vp, vp, i]),
             "mvllm_moe_permute_dev_noalloc": (i, [vp, vp, vp, i, i, i, i] + [vp] * 6),
+            "mvllm_moe_ep_plan_dev": (i, [vp, vp, i, i, i, i, vp, vp]),
+            "mvllm_moe_ep_pack_dev": (i, [vp, vp, i, vp, vp, i, i, i, i, i, vp, vp, vp, vp]),
+            "mvllm_moe_ep_combine_dev": (i, [vp, vp, vp, i, i, i, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -265,3 +269,27 @@ def matmul_dev(fmt, y, x, w, scales, stream=None):
     O = y.shape[1]
     _check(lib().mvllm_matmul_dev(_stream(stream), fmt, _dp(y), _dp(x), _dp(w), _dp(scales), S,
                                   I, O))
+
+
+# -------------------------------------------------------- expert parallelism --
+def ep_plan_dev(idx, E, nranks, pos, send_cnt, stream=None):
+    """pos [T, nranks] int32, send_cnt [nranks] int32 (device)."""
+    T, K = idx.shape
+    _check(lib().mvllm_moe_ep_plan_dev(_stream(stream), _dp(idx), T, K, E, nranks, _dp(pos),
+                                       _dp(send_cnt)))
+
+
+def ep_pack_dev(x, idx, wt, E, nranks, pos, send_x, send_idx, send_wt, stream=None):
+    T, K = idx.shape
+    D = x.shape[1]
+    x_dtype = DTYPE_BF16 if str(x.dtype) == "torch.bfloat16" else DTYPE_F32
+    _check(lib().mvllm_moe_ep_pack_dev(_stream(stream), _dp(x), x_dtype, _dp(idx), _dp(wt), T, K,
+                                       D, E, nranks, _dp(pos), _dp(send_x), _dp(send_idx),
+                                       _dp(send_wt)))
+
+
+def ep_combine_dev(back, pos, out, stream=None):
+    T, nranks = pos.shape
+    D = out.shape[1]
+    _check(lib().mvllm_moe_ep_combine_dev(_stream(stream), _dp(back), _dp(pos), T, nranks, D,
+                                          _dp(out)))

@@ -1,0 +1,126 @@
+"""Expert-parallel layer (micro-vllm_b200/ep.py) on CPU: the orchestration with
+the CPU test double of the device steps.
+
+* In-process emulation of 3 ranks (the exchanges as slicing / concatenation).
+* Two gloo ranks through torch.distributed all-to-all (spawned processes,
+  127.0.0.1 rendezvous).
+Both against the oracle's single-host moe_block of the whole layer; tolerance
+as everywhere (the sum association differs from the single-host order).
+"""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+import cases
+from conftest import assert_close
+
+torch = pytest.importorskip("torch")
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "micro-vllm_b200"))
+
+CASE = dict(D=128, I=64, E=6, K=2, fmt=cases.FMT_INT4, act=cases.ACT_CLAMP, act_a=7.0,
+            act_b=0.0)
+
+
+def layer(port, T, seed=41):
+    c = cases.layer_case(port, seed, CASE["D"], CASE["I"], CASE["E"], CASE["K"], T, CASE["fmt"],
+                         CASE["act"], CASE["act_a"], CASE["act_b"])
+    _, want = cases.run_block(port, c)
+    return c, want
+
+
+def rank_ops(port, c, rank, nranks):
+    from ep_cpu_ops import CpuOps
+    import ep
+    local = [c["experts"][e] for e in ep.local_experts(rank, nranks, CASE["E"])]
+    return CpuOps(torch, port, CASE["E"], CASE["K"], CASE["D"], CASE["I"], CASE["fmt"],
+                  CASE["act"], CASE["act_a"], CASE["act_b"], local, nranks)
+
+
+def test_ep_emulated_three_ranks(port):
+    import ep
+    N, T_loc = 3, 7
+    c, want = layer(port, N * T_loc)
+    layers, xs, idxs, wts, outs = [], [], [], [], []
+    for r in range(N):
+        sl = slice(r * T_loc, (r + 1) * T_loc)
+        layers.append(ep.EPLayer(rank_ops(port, c, r, N), r, N, CASE["D"], CASE["K"]))
+        xs.append(torch.from_numpy(np.ascontiguousarray(c["x"][sl])))
+        idxs.append(torch.from_numpy(np.ascontiguousarray(c["idx"][sl])))
+        wts.append(torch.from_numpy(np.ascontiguousarray(c["wt"][sl])))
+        outs.append(torch.zeros((T_loc, CASE["D"])))
+    ep.emulate_step(layers, xs, idxs, wts, outs, torch)
+    got = torch.cat(outs).numpy()
+    assert_close(got, want, "emulated 3-rank EP")
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _gloo_rank(rank, nranks, port_no, T_loc, out_dir):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port_no))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "micro-vllm_b200"))
+    from datetime import timedelta
+    from oracle import Oracle
+    import ep
+    dist.init_process_group("gloo", rank=rank, world_size=nranks, timeout=timedelta(seconds=60))
+    port = Oracle("port")
+    c, _ = layer(port, nranks * T_loc)
+    sl = slice(rank * T_loc, (rank + 1) * T_loc)
+    L = ep.EPLayer(rank_ops(port, c, rank, nranks), rank, nranks, CASE["D"], CASE["K"])
+    out = torch.zeros((T_loc, CASE["D"]))
+    L.forward(torch.from_numpy(np.ascontiguousarray(c["x"][sl])),
+              torch.from_numpy(np.ascontiguousarray(c["idx"][sl])),
+              torch.from_numpy(np.ascontiguousarray(c["wt"][sl])), out, dist)
+    np.save(os.path.join(out_dir, f"out{rank}.npy"), out.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ep_two_gloo_ranks(port, tmp_path):
+    import multiprocessing as mp
+    N, T_loc = 2, 9
+    ctx = mp.get_context("spawn")
+    p_no = _free_port()
+    procs = [ctx.Process(target=_gloo_rank, args=(r, N, p_no, T_loc, str(tmp_path)))
+             for r in range(N)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = np.concatenate([np.load(tmp_path / f"out{r}.npy") for r in range(N)])
+    _, want = layer(port, N * T_loc)
+    assert_close(got, want, "2 gloo ranks EP")
+
+
+def test_ep_plan_positions(port):
+    """The plan's send-buffer layout: destination-major, tokens ascending, one
+    row per (token, destination) however many of its experts the rank owns."""
+    c, _ = layer(port, 10)
+    ops = rank_ops(port, c, 0, 4)
+    pos, cnt = ops.plan(torch.from_numpy(c["idx"]))
+    P, idx = pos.numpy(), c["idx"]
+    expect_rows = 0
+    for d in range(4):
+        toks = [t for t in range(10) if any(e % 4 == d for e in idx[t])]
+        assert cnt[d] == len(toks)
+        for j, t in enumerate(toks):
+            assert P[t, d] == expect_rows + j
+        expect_rows += len(toks)

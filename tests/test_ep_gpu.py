@@ -1,0 +1,102 @@
+"""Expert-parallel layer on the GPU: plan / pack / combine kernels and the
+local expert compute through the library.
+
+* 4 ranks emulated in one process on one GPU (exchanges as slicing), against
+  the oracle and against the single-GPU layer.
+* 2 ranks on 2 GPUs over NCCL (torchrun), when the box has 2 GPUs.
+"""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import cases
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "micro-vllm_b200"))
+
+CASE = dict(D=512, I=512, E=8, K=2, fmt=cases.FMT_MXFP4, act=cases.ACT_SITU, act_a=4.0,
+            act_b=25.0)
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def tables_of(experts):
+    keep, tabs = [], [[], [], [], [], [], []]
+    for (gp, gsc), (up, usc), (dp, dsc) in experts:
+        for k, a in enumerate((gp, up, dp, gsc, usc, dsc)):
+            t = dev(a)
+            keep.append(t)
+            tabs[k].append(t.data_ptr())
+    return [torch.tensor(t, dtype=torch.int64, device="cuda") for t in tabs], keep
+
+
+def test_ep_emulated_four_ranks_gpu(moe, port):
+    import ep
+    N, T_loc = 4, 40
+    c = cases.layer_case(port, 51, CASE["D"], CASE["I"], CASE["E"], CASE["K"], N * T_loc,
+                         CASE["fmt"], CASE["act"], CASE["act_a"], CASE["act_b"], bf16_x=True)
+    _, want = cases.run_block(port, c)
+    layers, xs, idxs, wts, outs, keep = [], [], [], [], [], []
+    for r in range(N):
+        tabs, k = tables_of([c["experts"][e] for e in ep.local_experts(r, N, CASE["E"])])
+        keep.append(k)
+        ops = ep.CudaOps(torch, CASE["E"], CASE["K"], CASE["D"], CASE["I"], CASE["fmt"],
+                         CASE["act"], CASE["act_a"], CASE["act_b"], tabs, N, N * T_loc)
+        layers.append(ep.EPLayer(ops, r, N, CASE["D"], CASE["K"]))
+        sl = slice(r * T_loc, (r + 1) * T_loc)
+        xs.append(dev(c["x"][sl]).to(torch.bfloat16))
+        idxs.append(dev(c["idx"][sl]))
+        wts.append(dev(c["wt"][sl]))
+        outs.append(torch.zeros((T_loc, CASE["D"]), device="cuda"))
+    ep.emulate_step(layers, xs, idxs, wts, outs, torch)
+    torch.cuda.synchronize()
+    got = torch.cat(outs).cpu().numpy()
+    assert_close(got, want, "emulated 4-rank EP")
+    # The plan kernel against its definition.
+    pos, cnt = layers[0].ops.plan(idxs[0])
+    P, idx = pos.cpu().numpy(), c["idx"][:T_loc]
+    row = 0
+    for d in range(N):
+        toks = [t for t in range(T_loc) if any(e % N == d for e in idx[t])]
+        assert int(cnt[d]) == len(toks)
+        for j, t in enumerate(toks):
+            assert P[t, d] == row + j
+        row += len(toks)
+    # One rank holding every expert is the single-GPU layer, bit for bit.
+    tabs, k = tables_of(c["experts"])
+    ops = ep.CudaOps(torch, CASE["E"], CASE["K"], CASE["D"], CASE["I"], CASE["fmt"], CASE["act"],
+                     CASE["act_a"], CASE["act_b"], tabs, 1, N * T_loc)
+    one = torch.zeros((N * T_loc, CASE["D"]), device="cuda")
+    ep.emulate_step([ep.EPLayer(ops, 0, 1, CASE["D"], CASE["K"])],
+                    [dev(c["x"]).to(torch.bfloat16)], [dev(c["idx"])], [dev(c["wt"])], [one], torch)
+    direct = torch.zeros_like(one)
+    ws = torch.empty(moe.layer_workspace_bytes(N * T_loc, CASE["K"], CASE["E"], 0, CASE["D"],
+                                               CASE["I"], CASE["fmt"]), dtype=torch.uint8,
+                     device="cuda")
+    moe.layer_dev(N * T_loc, CASE["K"], CASE["E"], 0, CASE["D"], CASE["I"], CASE["fmt"],
+                  dev(c["idx"]), dev(c["wt"]), dev(c["x"]).to(torch.bfloat16), tabs, direct,
+                  CASE["act"], CASE["act_a"], CASE["act_b"], ws)
+    torch.cuda.synchronize()
+    assert torch.equal(one, direct)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_ep_nccl_two_gpus():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29561",
+           os.path.join(ROOT, "tests", "ep_nccl_check.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=330)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert "EP-NCCL-OK" in r.stdout
