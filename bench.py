@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the config[3] prefill measurement")
     ap.add_argument("--prefill-steps", type=int, default=10)
+    ap.add_argument("--no-ep", action="store_true", help="skip the config[4] expert-parallel leg")
+    ap.add_argument("--ep-steps", type=int, default=5)
     ap.add_argument("--prefill-tokens", type=int, default=4096,
                     help="config[3]: 4096; fewer only to size a profiler capture")
     ap.add_argument("--experts", type=int, default=256,
@@ -284,6 +286,91 @@ def prefill_bench(moe, torch, wl, steps, peak_tf, peak_gbs, T=PREFILL_T):
     }
 
 
+# ----------------------------------------------------- expert parallelism --
+EP_E, EP_T = 384, 8192
+
+
+def ep_bench(moe, torch, dist, rank, world, steps):
+    """Config[4]: 384 MXFP4 experts sharded over the ranks (expert e on rank
+    e % world), 8192 tokens per step split evenly over the ranks, top-8;
+    uniform and Zipf s=1.1 routing.  Weights are drawn per global expert id, so
+    the model is the same whatever the rank count; total work per step is
+    fixed (strong scaling), tokens/s = 8192 / step time (max over ranks)."""
+    import ep
+    D, I, K = CFG["D"], CFG["I"], CFG["K"]
+    mine = ep.local_experts(rank, world, EP_E)
+    u8 = torch.uint8
+    n = len(mine)
+    gp = torch.empty((n, I, D // 2), dtype=u8, device="cuda")
+    up = torch.empty_like(gp)
+    dp = torch.empty((n, D, I // 2), dtype=u8, device="cuda")
+    gs = torch.empty((n, I, D // 32), dtype=u8, device="cuda")
+    us = torch.empty_like(gs)
+    ds = torch.empty((n, D, I // 32), dtype=u8, device="cuda")
+    for j, e in enumerate(mine):
+        g = torch.Generator(device="cuda").manual_seed(100000 + e)
+        for pk, sc, shape in ((gp, gs, (I, D)), (up, us, (I, D)), (dp, ds, (D, I))):
+            w = torch.randn(shape, generator=g, device="cuda").mul_(0.02)
+            moe.pack_mxfp4_dev(w, pk[j], sc[j])
+    tabs = [torch.tensor([t[j].data_ptr() for j in range(n)], dtype=torch.int64, device="cuda")
+            for t in (gp, up, dp, gs, us, ds)]
+    ops = ep.CudaOps(torch, EP_E, K, D, I, CFG["fmt"], CFG["act"], CFG["act_a"], CFG["act_b"],
+                     tabs, world, EP_T)
+    layer = ep.EPLayer(ops, rank, world, D, K)
+    T_loc = EP_T // world
+    g = torch.Generator(device="cuda").manual_seed(777)
+    x_all = torch.randn((EP_T, D), generator=g, device="cuda").to(torch.bfloat16)
+    x = x_all[rank * T_loc:(rank + 1) * T_loc].contiguous()
+    del x_all
+    out = torch.zeros((T_loc, D), dtype=torch.float32, device="cuda")
+    res = {}
+    for name in ("uniform", "zipf"):
+        gr = torch.Generator(device="cuda").manual_seed(778 if name == "uniform" else 779)
+        if name == "uniform":
+            choice = torch.rand((EP_T, EP_E), generator=gr, device="cuda")
+            vals, idx = torch.topk(choice, K, dim=1)
+            wt = (vals / vals.sum(1, keepdim=True)).float()
+            idx = idx.int()
+        else:
+            idx, wt = zipf_routing(torch, EP_T, EP_E, K, gr)
+        idx = idx[rank * T_loc:(rank + 1) * T_loc].contiguous()
+        wt = wt[rank * T_loc:(rank + 1) * T_loc].contiguous()
+
+        def step():
+            out.zero_()
+            if world > 1:
+                return layer.forward(x, idx, wt, out, dist)
+            ep.emulate_step([layer], [x], [idx], [wt], [out], torch)
+            return None
+
+        for _ in range(2):
+            step()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        info = None
+        for _ in range(steps):
+            info = step()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        res[name] = {"tokens_per_s": EP_T / (ms / 1e3), "ms_per_step": ms, "steps": steps}
+        if info:
+            res[name]["rank0_sent_rows"] = info["sent_rows"]
+            res[name]["rank0_received_rows"] = info["received_rows"]
+    del gp, up, dp, gs, us, ds
+    return {"workload": "config[4] expert-parallel MXFP4 layer: 384 experts strided over the "
+                        "ranks, hidden 7168, inter 2048, top-8, 8192 tokens per step, bf16 "
+                        "activations; NCCL all-to-all dispatch and return",
+            "n_gpus": world, "scaling": "strong", "experts_per_rank": n, **res}
+
+
 # ------------------------------------------------------------ CPU baseline --
 def cpu_reference_rate(n_threads, rounds, expert_rows_per_call, host_experts=None):
     """Reference moe_block (oracle/_ref) on host threads.
@@ -489,6 +576,11 @@ def main():
             tps, mstep = graph_throughput(moe, torch, wb, 320, 32)
             sweep[f"B{bb}"] = {"tokens_per_s": tps * world, "ms_per_step": mstep}
 
+    # config[4] expert-parallel layer (all ranks together)
+    ep_res = None
+    if not args.no_ep:
+        ep_res = ep_bench(moe, torch, dist, rank, world, args.ep_steps)
+
     # config[3] prefill (tensor-core kernels), per rank
     prefill = None
     if not args.no_prefill:
@@ -541,6 +633,7 @@ def main():
             "clocks": clk.report(),
             "sweep": sweep,
             "prefill": prefill,
+            "expert_parallel": ep_res,
         }
         if prefill and cpu and cpu.get("value"):
             # The reference's rate in expert rows/s (9 rows per config[1] token)
