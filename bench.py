@@ -361,6 +361,15 @@ def ep_bench(moe, torch, dist, rank, world, steps):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         res[name] = {"tokens_per_s": EP_T / (ms / 1e3), "ms_per_step": ms, "steps": steps}
+        if world > 1:
+            # One more step with phase events (not part of the timed steps).
+            tm = {}
+            out.zero_()
+            layer.forward(x, idx, wt, out, dist, timing=tm)
+            keys = sorted(tm)
+            tt = torch.tensor([tm[k] for k in keys], dtype=torch.float64, device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            res[name]["phase_ms_max_over_ranks"] = dict(zip(keys, tt.tolist()))
         if info:
             res[name]["rank0_sent_rows"] = info["sent_rows"]
             res[name]["rank0_received_rows"] = info["received_rows"]

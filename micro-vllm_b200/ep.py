@@ -107,26 +107,49 @@ class EPLayer:
     def pack(self, x, idx, wt, pos, send_splits):
         return self.ops.pack(x, idx, wt, pos, int(sum(send_splits)))
 
-    def forward(self, x, idx, wt, out, dist, group=None):
-        """One step through torch.distributed (all ranks call it in step)."""
+    def forward(self, x, idx, wt, out, dist, group=None, timing=None):
+        """One step through torch.distributed (all ranks call it in step).
+        With ``timing`` (a dict), CUDA events on the current stream split the
+        step into its phases; the dict receives their device milliseconds."""
         t = self.ops.torch
+        ev = []
+
+        def mark():
+            if timing is not None:
+                e = t.cuda.Event(enable_timing=True)
+                e.record()
+                ev.append(e)
+
+        mark()
         pos, cnt = self.prepare(x, idx, wt)
+        mark()
         rcnt = t.empty_like(cnt)
         dist.all_to_all_single(rcnt, cnt, group=group)
         sc = [int(v) for v in cnt.tolist()]
         rc = [int(v) for v in rcnt.tolist()]
+        mark()
         sx, sidx, swt = self.pack(x, idx, wt, pos, sc)
         R = sum(rc)
         rx = t.empty((R, self.D), dtype=x.dtype, device=x.device)
         ridx = t.empty((R, self.K), dtype=t.int32, device=x.device)
         rwt = t.empty((R, self.K), dtype=t.float32, device=x.device)
+        mark()
         dist.all_to_all_single(rx, sx, rc, sc, group=group)
         dist.all_to_all_single(ridx, sidx, rc, sc, group=group)
         dist.all_to_all_single(rwt, swt, rc, sc, group=group)
+        mark()
         part = self.ops.compute(rx, ridx, rwt)
+        mark()
         back = t.empty((sum(sc), self.D), dtype=t.float32, device=x.device)
         dist.all_to_all_single(back, part, sc, rc, group=group)
+        mark()
         self.ops.combine(back, pos, out)
+        mark()
+        if timing is not None:
+            t.cuda.synchronize()
+            names = ("plan", "counts", "pack", "dispatch", "experts", "return", "combine")
+            for n, a, b in zip(names, ev[:-1], ev[1:]):
+                timing[n] = timing.get(n, 0.0) + a.elapsed_time(b)
         return {"sent_rows": sum(sc), "received_rows": R}
 
 
