@@ -190,6 +190,23 @@ MVLLM_API int mvllm_pack_mxfp4_dev(void *stream, const float *w, int O, int I, u
 MVLLM_API int mvllm_matmul_dev(void *stream, int fmt, float *y, const float *x, const void *w,
                      const void *scales, int S, int I, int O);
 
+/* ---- routing on the device (glm53.cpp:1921-1931, kimi_k3.cpp:1986-1998). ----
+ * moe_topk for T rows of choice [T, E] (device): the K largest choices, equal
+ * values to the lower expert id, in that order; w = mix[id] (or choice[id] when
+ * mix is null) clamped at 0, divided by their sum in selection order, or 1/K
+ * each when the sum is 0 (ops.cpp:860-890).  K > E fills the tail with -1 / 0.
+ * E <= 1024, K <= 32.  Bit-identical to the reference's moe_topk. */
+MVLLM_API int mvllm_moe_topk_dev(void *stream, const float *choice, const float *mix, int T, int E,
+                                 int K, int *idx, float *wt);
+/* The router in front of it: scores[t, e] = sigmoid(x[t] . router[e]) with the
+ * dot product in the reference's order (sequential f32 over H, product and sum
+ * rounded separately, quant.cpp:156-168), choice = scores + bias (bias may be
+ * null), then mvllm_moe_topk_dev(choice, mix = scores).  x: x_dtype [T, H];
+ * router f32 [E, H]; scores, choice: f32 [T, E] outputs. */
+MVLLM_API int mvllm_moe_route_dev(void *stream, const void *x, int x_dtype, int T, int H,
+                                  const float *router, const float *bias, int E, int K, int *idx,
+                                  float *wt, float *scores, float *choice);
+
 /* ---- expert parallelism (one rank per GPU).  No single counterpart in the
  *      reference, which runs every expert on one host; these are the
  *      device steps of the sharded layer around the NCCL exchanges.

@@ -7,6 +7,7 @@
 #include "decode_ffn.cuh"
 #include "tc_ffn.cuh"
 #include "ep_kernels.cuh"
+#include "route_kernels.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -1423,6 +1424,45 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     c.calls += 1;
     c.rows += uint64_t(T) * (K + n_shared);
     return MVLLM_OK;
+}
+
+// --------------------------------------------------------------- routing --
+int mvllm_moe_topk_dev(void *stream, const float *choice, const float *mix, int T, int E, int K,
+                       int *idx, float *wt) {
+    if (!choice || !idx || !wt || T < 0 || E < 1 || E > 32 * kTopkMaxPerLane || K < 1 ||
+        K > kTopkMaxK)
+        return fail(MVLLM_ERR_INVALID, "topk_dev: invalid arguments");
+    if (T == 0)
+        return MVLLM_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int warps = 8;
+    topk_kernel<<<std::min((T + warps - 1) / warps, 65535), 32 * warps, 0, st>>>(choice, mix, T,
+                                                                                E, K, idx, wt);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+int mvllm_moe_route_dev(void *stream, const void *x, int x_dtype, int T, int H,
+                        const float *router, const float *bias, int E, int K, int *idx,
+                        float *wt, float *scores, float *choice) {
+    if (!x || !router || !idx || !wt || !scores || !choice || T < 0 || H < 1 || E < 1 ||
+        E > 32 * kTopkMaxPerLane || K < 1 || K > kTopkMaxK ||
+        (x_dtype != MVLLM_DTYPE_F32 && x_dtype != MVLLM_DTYPE_BF16))
+        return fail(MVLLM_ERR_INVALID, "route_dev: invalid arguments");
+    if (T == 0)
+        return MVLLM_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    dim3 grid((E + 31) / 32, (T + 31) / 32);
+    if (grid.y > 65535)
+        return fail(MVLLM_ERR_INVALID, "route_dev: T too large");
+    if (x_dtype == MVLLM_DTYPE_BF16)
+        route_scores_kernel<__nv_bfloat16><<<grid, 1024, 0, st>>>(
+            static_cast<const __nv_bfloat16 *>(x), router, bias, T, H, E, scores, choice);
+    else
+        route_scores_kernel<float><<<grid, 1024, 0, st>>>(static_cast<const float *>(x), router,
+                                                           bias, T, H, E, scores, choice);
+    CUDA_TRY(cudaGetLastError());
+    return mvllm_moe_topk_dev(stream, choice, scores, T, E, K, idx, wt);
 }
 
 // ------------------------------------------------------ expert parallelism --

@@ -1,0 +1,151 @@
+// route_kernels.cuh -- expert routing on the device: router scores and the
+// deterministic top-k that feeds the permutation.
+//
+// Reference (both MoE families route the same way):
+//   scores[e] = sigmoid(x . router[e])        quant::matmul_f32 (quant.cpp:156-168),
+//                                             quant::sigmoid (quant.hpp:22-29)
+//   choice[e] = scores[e] + bias[e]           glm53.cpp:1921-1931, kimi_k3.cpp:1986-1998
+//   idx, w    = moe_topk(choice, E, K, mix = scores)            ops.cpp:860-890
+// moe_topk keeps the K largest choices (equal values: the lower expert id
+// first), takes w[i] = mix[idx[i]] (or the choice) clamped at 0, and divides
+// by their sum accumulated in selection order (1/K each when the sum is 0).
+#pragma once
+
+#include "common.cuh"
+
+namespace mvb {
+
+// Correctly rounded single-precision e^x through double precision: the double
+// result is within one double ulp, so rounding it to float is exact except
+// within 2^-29 of a float rounding boundary.  It matches a correctly rounded
+// host expf (glibc's is within 0.502 ulp) far more often than the
+// single-precision device expf (within 2 ulp).
+__device__ __forceinline__ float expf_cr(float x) {
+    return static_cast<float>(exp(static_cast<double>(x)));
+}
+
+// quant::sigmoid with the exponential above.
+__device__ __forceinline__ float sigmoid_route(float x) {
+    if (x >= 0.f)
+        return __fdiv_rn(1.f, __fadd_rn(1.f, expf_cr(-x)));
+    const float z = expf_cr(x);
+    return __fdiv_rn(z, __fadd_rn(1.f, z));
+}
+
+template <typename TX> __device__ __forceinline__ float to_f32(TX v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+    return __bfloat162float(v);
+}
+
+// One CTA per 32 tokens x 32 experts, one thread per (token, expert): the dot
+// product runs sequentially over the hidden dimension, each product and each
+// sum rounded on its own (no contraction), exactly the reference's order.
+// x and router columns are staged 64 at a time in shared memory.
+template <typename TX>
+__global__ void __launch_bounds__(1024)
+    route_scores_kernel(const TX *__restrict__ x, const float *__restrict__ w,
+                        const float *__restrict__ bias, int T, int H, int E,
+                        float *__restrict__ scores, float *__restrict__ choice) {
+    __shared__ float xs[32][65];
+    __shared__ float wsm[32][65];
+    const int te = threadIdx.x & 31, tt = threadIdx.x >> 5; // expert lane, token warp
+    const int t0 = blockIdx.y * 32, e0 = blockIdx.x * 32;
+    float acc = 0.f;
+    for (int i0 = 0; i0 < H; i0 += 64) {
+        for (int j = threadIdx.x; j < 32 * 64; j += blockDim.x) {
+            const int r = j >> 6, c = j & 63;
+            const int i = i0 + c;
+            xs[r][c] = (t0 + r < T && i < H) ? to_f32(x[static_cast<size_t>(t0 + r) * H + i]) : 0.f;
+            wsm[r][c] = (e0 + r < E && i < H) ? w[static_cast<size_t>(e0 + r) * H + i] : 0.f;
+        }
+        __syncthreads();
+        const int n = min(64, H - i0);
+        for (int c = 0; c < n; ++c)
+            acc = __fadd_rn(acc, __fmul_rn(xs[tt][c], wsm[te][c]));
+        __syncthreads();
+    }
+    const int t = t0 + tt, e = e0 + te;
+    if (t < T && e < E) {
+        const float s = sigmoid_route(acc);
+        scores[static_cast<size_t>(t) * E + e] = s;
+        choice[static_cast<size_t>(t) * E + e] = bias ? __fadd_rn(s, bias[e]) : s;
+    }
+}
+
+constexpr int kTopkMaxPerLane = 32; // E <= 1024
+constexpr int kTopkMaxK = 32;       // one lane per selected expert
+
+// One warp per token: K rounds of a warp-wide arg-max over the choices not yet
+// taken, ordered by (value descending, id ascending) -- the order of the
+// reference's partial_sort comparator -- then the weights as moe_topk forms
+// them.  Slots K > E get id -1 and weight 0, as the callers preset them.
+__global__ void topk_kernel(const float *__restrict__ choice, const float *__restrict__ mix, int T,
+                            int E, int K, int *__restrict__ idx, float *__restrict__ wt) {
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int per = (E + 31) >> 5;
+    for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+        const float *ch = choice + static_cast<size_t>(t) * E;
+        float v[kTopkMaxPerLane];
+#pragma unroll
+        for (int j = 0; j < kTopkMaxPerLane; ++j)
+            v[j] = (j < per && lane + 32 * j < E) ? ch[lane + 32 * j] : 0.f;
+        uint32_t taken = 0;
+        for (int j = 0; j < per; ++j)
+            if (lane + 32 * j >= E)
+                taken |= 1u << j;
+        const int k = min(K, E);
+        int sel = -1; // lane r keeps the id chosen in round r
+        for (int r = 0; r < k; ++r) {
+            float bv = 0.f;
+            int be = -1;
+#pragma unroll
+            for (int j = 0; j < kTopkMaxPerLane; ++j) {
+                if (j >= per || ((taken >> j) & 1u))
+                    continue;
+                const int e = lane + 32 * j;
+                if (be < 0 || v[j] > bv || (v[j] == bv && e < be)) {
+                    bv = v[j];
+                    be = e;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+                if (oe >= 0 && (be < 0 || ov > bv || (ov == bv && oe < be))) {
+                    bv = ov;
+                    be = oe;
+                }
+            }
+            if (be >= 0 && (be & 31) == lane)
+                taken |= 1u << (be >> 5);
+            if (lane == r)
+                sel = be;
+        }
+        // Lane r holds round r's id; its weight, clamped at 0.
+        float w_r = 0.f;
+        if (lane < k) {
+            const float m = mix ? mix[static_cast<size_t>(t) * E + sel] : ch[sel];
+            w_r = m < 0.f ? 0.f : m;
+        }
+        // Sum in selection order (the reference's order), the same on every lane.
+        float sum = 0.f;
+        for (int r = 0; r < k; ++r)
+            sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, w_r, r));
+        if (lane < K) {
+            int *io = idx + static_cast<size_t>(t) * K;
+            float *wo = wt + static_cast<size_t>(t) * K;
+            if (lane < k) {
+                io[lane] = sel;
+                wo[lane] = sum > 0.f ? __fdiv_rn(w_r, sum) : __fdiv_rn(1.f, static_cast<float>(k));
+            } else {
+                io[lane] = -1;
+                wo[lane] = 0.f;
+            }
+        }
+    }
+}
+
+} // namespace mvb

@@ -37,7 +37,7 @@ C_SYMBOLS = (
     "mvllm_moe_layer_host", "mvllm_quantize_int4_g64_dev", "mvllm_pack_mxfp4_dev",
     "mvllm_matmul_dev", "mvllm_moe_profile_enable", "mvllm_moe_profile_read",
     "mvllm_moe_permute_dev_noalloc", "mvllm_moe_ep_plan_dev", "mvllm_moe_ep_pack_dev",
-    "mvllm_moe_ep_combine_dev",
+    "mvllm_moe_ep_combine_dev", "mvllm_moe_topk_dev", "mvllm_moe_route_dev",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -89,6 +89,8 @@ def lib():
             "mvllm_moe_ep_plan_dev": (i, [vp, vp, i, i, i, i, vp, vp]),
             "mvllm_moe_ep_pack_dev": (i, [vp, vp, i, vp, vp, i, i, i, i, i, vp, vp, vp, vp]),
             "mvllm_moe_ep_combine_dev": (i, [vp, vp, vp, i, i, i, vp]),
+            "mvllm_moe_topk_dev": (i, [vp, vp, vp, i, i, i, vp, vp]),
+            "mvllm_moe_route_dev": (i, [vp, vp, i, i, i, vp, vp, i, i, vp, vp, vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -293,3 +295,21 @@ def ep_combine_dev(back, pos, out, stream=None):
     D = out.shape[1]
     _check(lib().mvllm_moe_ep_combine_dev(_stream(stream), _dp(back), _dp(pos), T, nranks, D,
                                           _dp(out)))
+
+
+# ------------------------------------------------------------------ routing --
+def topk_dev(choice, K, idx, wt, mix=None, stream=None):
+    """Device moe_topk over the rows of choice [T, E]."""
+    T, E = choice.shape
+    _check(lib().mvllm_moe_topk_dev(_stream(stream), _dp(choice), _dp(mix), T, E, K, _dp(idx),
+                                    _dp(wt)))
+
+
+def route_dev(x, router, bias, K, idx, wt, scores, choice, stream=None):
+    """Router scores (sigmoid of x . router^T, + bias) and top-K on device."""
+    T, H = x.shape
+    E = router.shape[0]
+    x_dtype = DTYPE_BF16 if str(x.dtype) == "torch.bfloat16" else DTYPE_F32
+    _check(lib().mvllm_moe_route_dev(_stream(stream), _dp(x), x_dtype, T, H, _dp(router),
+                                     _dp(bias), E, K, _dp(idx), _dp(wt), _dp(scores),
+                                     _dp(choice)))
