@@ -4,7 +4,8 @@
   and weights, with ties, negative choices, mix on and off, K > E.
 * mvllm_moe_route_dev: the router dot products follow the reference's order
   exactly; the sigmoid's exponential is the correctly rounded one, so scores
-  match the host's to the last bit except where the host expf misrounds.
+  match the host's to the last bit except where the host expf misrounds (then
+  by at most 2 ulp, in under 0.1% of the scores).
   Routing ids must match for every token; weights to 1e-6.
 """
 import numpy as np
@@ -89,7 +90,9 @@ def test_route_dev_matches_reference(moe, port, dtype):
     ri, rw = ref_topk(port, ch, K, sc)
     gs = scores.cpu().numpy()
     ulps = np.abs(gs.view(np.int32).astype(np.int64) - sc.view(np.int32).astype(np.int64))
-    assert ulps.max() <= 1, ulps.max()
+    # One ulp of difference in e^x (where the host expf misrounds) can move the
+    # sigmoid's quotient by up to two.
+    assert ulps.max() <= 2, ulps.max()
     assert (ulps > 0).mean() < 1e-3, (ulps > 0).mean()
     np.testing.assert_array_equal(idx.cpu().numpy(), ri)
     np.testing.assert_allclose(wt.cpu().numpy(), rw, rtol=1e-6, atol=0)
