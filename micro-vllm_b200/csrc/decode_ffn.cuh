@@ -87,12 +87,15 @@ template <int FMT, int KS, int NT> struct DecodeLayout {
     static constexpr int RED_BYTES = kDecodeKParts * kDecodeRows * RS * 4; // per buffer
     static constexpr int BAR_BYTES = 256; // 8 full + 8 empty + 2 + 2 reduction barriers
     static constexpr int RHDR_BYTES = 32; // two item headers for the epilogue
+    static constexpr int ITEM_TAB = 512;  // item offsets of up to 511 experts, in shared memory
     static constexpr int OFF_W = 0;          // 1024-aligned: the 128-byte swizzle needs it
     static constexpr int OFF_SC = OFF_W + NBOX * BOX_BYTES;
     static constexpr int OFF_HDR = OFF_SC + kDecodeRows * SB;
     static constexpr int OFF_X = OFF_HDR + 16;
     static constexpr int STAGE_BYTES = (OFF_X + MT * XROW + 1023) / 1024 * 1024;
-    static constexpr int HEAD_BYTES = (BAR_BYTES + RHDR_BYTES + 2 * RED_BYTES + 1023) / 1024 * 1024;
+    static constexpr int HEAD_BYTES =
+        (BAR_BYTES + RHDR_BYTES + 2 * RED_BYTES + ITEM_TAB * 4 + 1023) / 1024 * 1024;
+    static constexpr int OFF_ITEMS = BAR_BYTES + RHDR_BYTES + 2 * RED_BYTES;
     static int smem_bytes(int nstages) { return HEAD_BYTES + nstages * STAGE_BYTES + 1024; }
 };
 
@@ -119,6 +122,49 @@ __device__ __forceinline__ void lds_scales(StageScales<FMT, KS> &sc, const uint8
         const uint4 y = *reinterpret_cast<const uint4 *>(a1);
         sc.r0[0] = x.x, sc.r0[1] = x.y, sc.r0[2] = x.z, sc.r0[3] = x.w;
         sc.r1[0] = y.x, sc.r1[1] = y.y, sc.r1[2] = y.z, sc.r1[3] = y.w;
+    }
+}
+
+// The MXFP4 single-tile stage split in two: every shared-memory operand of
+// the warp's quarter (weights, token fragments) goes to registers first, so
+// the warp can release the stage before it computes; the producer then
+// refills the slot while the math runs.
+template <int KS> struct Mx4StageRegs {
+    static constexpr int NG = KS / 64;
+    uint32_t w0[NG], w1[NG];
+    uint4 xb[NG];
+};
+
+template <int KS>
+__device__ __forceinline__ void mx4_stage_load(const uint8_t *wl, const uint32_t (&swz)[KS / 64],
+                                               const uint8_t *xl, Mx4StageRegs<KS> &r) {
+    constexpr int kRow8 = 8 * 128;
+#pragma unroll
+    for (int j = 0; j < Mx4StageRegs<KS>::NG; ++j) {
+        const uint8_t *a = wl + swz[j];
+        r.w0[j] = *reinterpret_cast<const uint32_t *>(a);
+        r.w1[j] = *reinterpret_cast<const uint32_t *>(a + kRow8);
+        r.xb[j] = *reinterpret_cast<const uint4 *>(xl + j * 64);
+    }
+}
+
+template <int KS>
+__device__ __forceinline__ void mx4_stage_math(const Mx4StageRegs<KS> &r,
+                                               const StageScales<MVLLM_FMT_MXFP4, KS> &sc,
+                                               float (&acc)[1][4]) {
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < Mx4StageRegs<KS>::NG; ++j) {
+        uint32_t p0, p1, p2, p3, q0, q1, q2, q3;
+        e2m1x8_to_f16x8(r.w0[j], p0, p1, p2, p3);
+        e2m1x8_to_f16x8(r.w1[j], q0, q1, q2, q3);
+        const float s0 = ue8m0_byte(sc.r0[j >> 2], j & 3);
+        const float s1 = ue8m0_byte(sc.r1[j >> 2], j & 3);
+        float tmp[4];
+        mma_f16_16816(tmp, p0, q0, p1, q1, r.xb[j].x, r.xb[j].y, zero);
+        mma_f16_16816(tmp, p2, q2, p3, q3, r.xb[j].z, r.xb[j].w, tmp);
+        ffma2(acc[0][0], acc[0][1], tmp[0], tmp[1], s0);
+        ffma2(acc[0][2], acc[0][3], tmp[2], tmp[3], s1);
     }
 }
 
@@ -201,22 +247,51 @@ struct DecodeItem {
     int rb, nv, orow0;
 };
 
-// Resolved by the producer one item ahead, so these dependent global loads
-// are hidden behind the current item's stages.
-template <int NT> __device__ __forceinline__ DecodeItem resolve_item(const DecodeArgs &p, int i) {
+// Items are resolved one ahead by the producer in two halves: at the start of
+// item i it finds the next item's expert (binary search over the item offsets,
+// kept in shared memory when they fit) and issues that expert's three loads;
+// their values are first used at the start of the next item, so the producer
+// never waits on them.
+struct PendingItem {
+    int i, e, off, cnt, xrow, orow;
+};
+
+__device__ __forceinline__ int find_owner_smem(const int *off, int nb, int i) {
+    int lo = 0, hi = nb;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (off[mid] <= i)
+            lo = mid;
+        else
+            hi = mid;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ PendingItem issue_item(const DecodeArgs &p, const int *off_s, int i) {
+    PendingItem q;
+    q.i = i;
+    q.e = off_s ? find_owner_smem(off_s, p.nb, i) : find_owner(p.item_off, p.nb, i);
+    q.off = off_s ? off_s[q.e] : __ldg(p.item_off + q.e);
+    q.cnt = __ldg(p.cnt + q.e);
+    q.xrow = __ldg(p.xrow + q.e);
+    q.orow = __ldg(p.orow + q.e);
+    return q;
+}
+
+template <int NT> __device__ __forceinline__ DecodeItem finish_item(const DecodeArgs &p,
+                                                                    const PendingItem &q) {
     constexpr int MT = 8 * NT;
-    const int e = find_owner(p.item_off, p.nb, i);
-    const int local = i - __ldg(p.item_off + e);
-    const int ce = __ldg(p.cnt + e);
-    const int chunks = (ce + MT - 1) / MT;
+    const int local = q.i - q.off;
+    const int chunks = (q.cnt + MT - 1) / MT;
     const int rb = local / chunks, chunk = local - rb * chunks;
     const int n0 = chunk * MT;
     DecodeItem it;
     it.rb = rb;
-    it.nv = min(MT, ce - n0);
-    it.tm = p.tmaps + static_cast<size_t>(e) * kTmCount * kTmBytes;
-    it.x = p.x + static_cast<size_t>(__ldg(p.xrow + e) + n0) * p.K;
-    it.orow0 = __ldg(p.orow + e) + n0;
+    it.nv = min(MT, q.cnt - n0);
+    it.tm = p.tmaps + static_cast<size_t>(q.e) * kTmCount * kTmBytes;
+    it.x = p.x + static_cast<size_t>(q.xrow + n0) * p.K;
+    it.orow0 = q.orow + n0;
     return it;
 }
 
@@ -236,6 +311,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
     int4 *rhdr = reinterpret_cast<int4 *>(smem + L::BAR_BYTES);
     float *red = reinterpret_cast<float *>(smem + L::BAR_BYTES + L::RHDR_BYTES);
     uint8_t *stages = smem + L::HEAD_BYTES;
+    int *items_s = reinterpret_cast<int *>(smem + L::OFF_ITEMS);
+    const bool items_in_smem = p.nb + 1 <= L::ITEM_TAB;
+    if (items_in_smem)
+        for (int e = threadIdx.x; e <= p.nb; e += blockDim.x)
+            items_s[e] = __ldg(p.item_off + e);
 
     const int NS = p.nstages;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -266,17 +346,19 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
         int i = blockIdx.x;
         const int G = gridDim.x;
         const bool fence_maps = __ldg(p.tmaps_dirty) != 0;
+        const int *off_s = items_in_smem ? items_s : nullptr;
         DecodeItem nxt{};
+        PendingItem pend{};
         if (i < total) {
-            nxt = resolve_item<NT>(p, i);
+            nxt = finish_item<NT>(p, issue_item(p, off_s, i));
             if (fence_maps)
                 tmap_acquire(nxt.tm + (lane % kTmCount) * kTmBytes);
         }
         for (; i < total && ok; i += G) {
             const DecodeItem cur = nxt;
             const bool more = i + G < total;
-            if (more) // dependent loads in flight while this item streams
-                nxt = resolve_item<NT>(p, i + G);
+            if (more) // the next item's loads fly while this item streams
+                pend = issue_item(p, off_s, i + G);
             const uint8_t *tm_w0 = cur.tm + (PHASE == 1 ? kTmGateP : kTmDownP) * kTmBytes;
             const uint8_t *tm_w1 = cur.tm + kTmUpP * kTmBytes;
             const uint8_t *tm_s0 = cur.tm + (PHASE == 1 ? kTmGateS : kTmDownS) * kTmBytes;
@@ -320,10 +402,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
                              4 * KS, &full[slot], pol_x);
                 }
                 __syncwarp();
-                // After the item's first stage is on its way: acquire the next
-                // item's tensor maps (one convergent fence per lane).
-                if (ks == 0 && more && fence_maps)
-                    tmap_acquire(nxt.tm + (lane % kTmCount) * kTmBytes);
+                // With the item's last stage on its way: finish the next item
+                // (its loads landed while this item streamed) and acquire its
+                // tensor maps (one convergent fence per lane).
+                if (ks == nks - 1 && more) {
+                    nxt = finish_item<NT>(p, pend);
+                    if (fence_maps)
+                        tmap_acquire(nxt.tm + (lane % kTmCount) * kTmBytes);
+                }
             }
         }
         // Drain: no copy may still be in flight when this warp leaves, also
@@ -412,7 +498,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
                     hdr = *reinterpret_cast<const int4 *>(st + L::OFF_HDR);
                 StageScales<FMT, KS> sc;
                 lds_scales<FMT, KS>(sc, st + s0_off, st + s0_off + 8 * L::SB);
-                decode_stage_compute<FMT, KS, NT>(st + wl_off, swz, st + xl_off, sc, acc);
+                if constexpr (FMT == MVLLM_FMT_MXFP4 && NT == 1) {
+                    Mx4StageRegs<KS> r;
+                    mx4_stage_load<KS>(st + wl_off, swz, st + xl_off, r);
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive(&empty[slot]); // operands are in registers
+                    mx4_stage_math<KS>(r, sc, acc);
+                    continue;
+                } else {
+                    decode_stage_compute<FMT, KS, NT>(st + wl_off, swz, st + xl_off, sc, acc);
+                }
             }
             __syncwarp();
             if (lane == 0)

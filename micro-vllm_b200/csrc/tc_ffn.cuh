@@ -128,7 +128,9 @@ template <bool PAIR> struct TcLayout {
     static constexpr int OFF_SC = OFF_PK + kTcPkSlots * PK_STAGE;
     static constexpr int OFF_BAR = OFF_SC + kTcScSlots * SC_STAGE;
     static constexpr int NBARS = 2 * C::STAGES + 2 * kTcPkSlots + 2 * kTcScSlots + 4 + 1;
-    static constexpr int SMEM = OFF_BAR + NBARS * 8 + 16 + 1024; // + tmem slot + alignment
+    static constexpr int ITEM_TAB = 512; // item offsets and row counts of up to 511 experts
+    static constexpr int OFF_ITEMS = OFF_BAR + NBARS * 8 + 16;
+    static constexpr int SMEM = OFF_ITEMS + 2 * ITEM_TAB * 4 + 1024; // + alignment
     static_assert(SMEM * C::CTAS_PER_SM <= 232448, "dynamic shared memory per SM");
 };
 
@@ -307,12 +309,28 @@ struct TcItem {
 // varies slowest and the token tile fastest, so CTAs working at the same
 // time share the weight rows through L2.  Pair lists hold an expert's
 // 256-row tiles (and a wider rest); solo lists its narrow rest, if any.
+// The item offsets and row counts live in shared memory (when the experts
+// fit the table), so the binary search costs no global round trips: every
+// role resolves every item itself.
+struct TcItemTab {
+    const int *off; // [nb + 1] item offsets of this list
+    const int *cnt; // [nb] rows per expert
+};
+
 template <int PHASE, bool PAIR>
-__device__ __forceinline__ void tc_item(const TcArgs &p, int i, TcItem &it) {
+__device__ __forceinline__ void tc_item(const TcArgs &p, const TcItemTab &tab, int i, TcItem &it) {
     using C = TcCfg<PAIR>;
-    const int e = find_owner(p.item_off, p.nb, i);
-    const int local = i - __ldg(p.item_off + e);
-    const int c = __ldg(p.cnt + e);
+    int lo = 0, hi = p.nb;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (tab.off[mid] <= i)
+            lo = mid;
+        else
+            hi = mid;
+    }
+    const int e = lo;
+    const int local = i - tab.off[e];
+    const int c = tab.cnt[e];
     int npair, nsolo;
     tc_tiles(c, p.small_max, npair, nsolo);
     const int ntt = PAIR ? npair : 1;
@@ -377,6 +395,16 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
     uint64_t *sc_full = pk_empty + kTcPkSlots, *sc_empty = sc_full + kTcScSlots;
     uint64_t *acc_full = sc_empty + kTcScSlots, *acc_empty = acc_full + 2, *done = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    int *off_s = reinterpret_cast<int *>(smem + L::OFF_ITEMS);
+    int *cnt_s = off_s + L::ITEM_TAB;
+    const bool tab_in_smem = p.nb + 1 <= L::ITEM_TAB;
+    if (tab_in_smem) {
+        for (int e = threadIdx.x; e <= p.nb; e += blockDim.x) {
+            off_s[e] = __ldg(p.item_off + e);
+            cnt_s[e] = e < p.nb ? __ldg(p.cnt + e) : 0;
+        }
+    }
+    const TcItemTab tab{tab_in_smem ? off_s : p.item_off, tab_in_smem ? cnt_s : p.cnt};
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // A pair's CTAs walk the pair's list together; rank 0 is the leader.
@@ -442,7 +470,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
             bool ok = true;
             for (int i = unit; ok && i < total; i += nunits) {
                 TcItem it;
-                tc_item<PHASE, PAIR>(p, i, it);
+                tc_item<PHASE, PAIR>(p, tab, i, it);
                 const int rows = PAIR ? it.nmma >> 1 : it.nmma; // this CTA's token rows
                 const int xr = __ldg(p.xrow + it.e) + it.t0 + static_cast<int>(rank) * rows;
                 const int nbox = (rows + kTcTokBox - 1) / kTcTokBox;
@@ -487,7 +515,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
             bool ok = true;
             for (int i = unit; ok && i < total; i += nunits) {
                 TcItem it;
-                tc_item<PHASE, PAIR>(p, i, it);
+                tc_item<PHASE, PAIR>(p, tab, i, it);
                 const uint8_t *tm = p.tmaps + static_cast<size_t>(it.e) * kTcMapCount * kTcMapBytes;
                 if (fence_maps)
                     for (int m = 0; m < kTcMapCount; ++m)
@@ -550,7 +578,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
             const uint32_t tok_base = smem_u32(smem);
             for (int i = unit; ok && i < total; i += nunits) {
                 TcItem it;
-                tc_item<PHASE, PAIR>(p, i, it);
+                tc_item<PHASE, PAIR>(p, tab, i, it);
                 const int b = acc.take(it.nmma > C::ACC_HALF);
                 if (b != 1 && !mbar_wait(&acc_empty[0], (acc.use[0] & 1u) ^ 1u, p.err))
                     ok = false;
@@ -729,7 +757,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
         bool ok = true;
         for (int i = unit; ok && i < total; i += nunits) {
             TcItem it;
-            tc_item<PHASE, PAIR>(p, i, it);
+            tc_item<PHASE, PAIR>(p, tab, i, it);
             const int b = acc.take(it.nmma > C::ACC_HALF);
             bool got = true;
             if (b != 1)
