@@ -145,6 +145,15 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, 
                  : "memory");
 }
 
+// 3-D box, coordinates innermost first.
+__device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, int x, int y, int z,
+                                            uint64_t *bar, uint64_t policy) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cta.global.mbarrier::complete_tx::bytes"
+                 ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+                 "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+                 : "memory");
+}
+
 // Writer side of a device-built tensor map: swap the global address of a
 // 128-byte map in global memory, then release it to the tensormap proxy.
 __device__ __forceinline__ void tmap_replace_address(void *tmap, const void *addr) {

@@ -74,6 +74,7 @@ struct DecodeArgs {
     float act_a, act_b;
     int nstages;
     const int *tmaps_dirty; // non-zero: maps were rewritten, acquire before use
+    int wbox3d;             // weight maps are 3-D: one box per matrix per stage
     int *err;
 };
 
@@ -379,7 +380,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
                                                            cur.nv * 4 * KS);
                 }
                 __syncwarp();
-                if (lane < L::NBOX) {
+                if (p.wbox3d) {
+                    // One box per matrix: [column chunk][rows][128 B] -- phase 1
+                    // puts the gate rows' chunks first, then the up rows'.
+                    if (lane == 0)
+                        tma_load_3d(st + L::OFF_W, tm_w0, 0, row0, ks * L::NBOX, &full[slot],
+                                    pol_w);
+                    else if (lane == 1 && PHASE == 1)
+                        tma_load_3d(st + L::OFF_W + L::NBOX * 32 * 128, tm_w1, 0, row0,
+                                    ks * L::NBOX, &full[slot], pol_w);
+                } else if (lane < L::NBOX) {
                     uint8_t *dst = st + L::OFF_W + lane * L::BOX_BYTES;
                     const int x = ks * KS + lane * 128;
                     if (PHASE == 1) {
@@ -388,7 +398,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
                     } else {
                         tma_load_2d(dst, tm_w0, x, row0, &full[slot], pol_w);
                     }
-                } else if (lane == 8) {
+                }
+                if (lane == 8) {
                     tma_load_2d(st + L::OFF_SC, tm_s0, ks * SX, row0, &full[slot], pol_w);
                 } else if (lane == 9 && PHASE == 1) {
                     tma_load_2d(st + L::OFF_SC + 32 * L::SB, tm_s1, ks * SX, row0, &full[slot],
@@ -476,7 +487,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
 #pragma unroll
     for (int c = 0; c < KS / 64; ++c)
         swz[c] = static_cast<uint32_t>(((((qbyte & 127) >> 4) + c) & 7) ^ g) << 4;
-    const int wl_off = L::OFF_W + (qbyte >> 7) * L::BOX_BYTES + R0 * 128 + 4 * t;
+    // Weight rows of the stage: 2-D boxes give [chunk][64 rows][128 B]; the
+    // 3-D phase-1 boxes give [chunk][32 gate rows][128 B] then the same for
+    // the up rows.  Both keep 128-byte rows, so the swizzle phase is row % 8.
+    const int wl_off =
+        (PHASE == 1 && p.wbox3d)
+            ? L::OFF_W + (R0 >= 32 ? L::NBOX * 32 * 128 : 0) + (qbyte >> 7) * 32 * 128 +
+                  (R0 & 31) * 128 + 4 * t
+            : L::OFF_W + (qbyte >> 7) * L::BOX_BYTES + R0 * 128 + 4 * t;
     const int xl_off = L::OFF_X + g * L::XROW + (kp * KQ + t * 8) * 2;
     const int s0_off = L::OFF_SC + R0 * L::SB + kp * (L::SB / 4);
     uint32_t it = 0, n_items = 0;

@@ -185,7 +185,18 @@ bool fast_path_ok(int fmt, int D, int I) {
 // rows (prefill-like); experts with more rows are split into chunks, whose
 // items run back to back so the repeated weight rows come from L2.
 int chunk_tiles(int avg_rows) { return avg_rows > 8 ? 2 : 1; }
-int pick_ks(int K) { return ((K / 2) % 512 == 0) ? 512 : 256; }
+// Stage K-slice of the decode kernels (bytes of packed row per stage):
+// 512 when the row divides, else 256; MVLLM_DECODE_KS=256 forces the smaller
+// slice (twice the stages in the same shared memory).
+int pick_ks(int K) {
+    static const int forced = [] {
+        const char *s = getenv("MVLLM_DECODE_KS");
+        return s ? atoi(s) : 0;
+    }();
+    if (forced == 256 && (K / 2) % 256 == 0)
+        return 256;
+    return ((K / 2) % 512 == 0) ? 512 : 256;
+}
 
 struct RunWs {
     int *base, *cnt, *off1, *off2, *total_rows, *err;
@@ -261,17 +272,47 @@ int encode_2d(CUtensorMap *m, CUtensorMapDataType dt, void *addr, uint64_t inner
     return MVLLM_OK;
 }
 
+// 3-D map over a row-major [rows, row_bytes] u8 matrix seen as (128-byte
+// column chunk, row, chunk index): box = 128 B x box_rows x box_chunks, so one
+// copy brings box_chunks chunks of box_rows rows laid out chunk-major.
+int encode_3d_rows(CUtensorMap *m, void *addr, uint64_t row_bytes, uint64_t rows,
+                   uint32_t box_rows, uint32_t box_chunks) {
+    auto enc = tmap_encoder();
+    if (!enc)
+        return fail(MVLLM_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    const cuuint64_t dims[3] = {128, rows, row_bytes / 128};
+    const cuuint64_t strides[2] = {row_bytes, 128};
+    const cuuint32_t box[3] = {128, box_rows, box_chunks};
+    const cuuint32_t es[3] = {1, 1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, addr, dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MVLLM_OK : MVLLM_ERR_UNSUPPORTED;
+}
+
 // Templates for one (fmt, D, I) shape: phase-1 boxes are 32 rows (gate and up
 // halves of an item), phase-2 boxes 64 rows; weights use the 128-byte swizzle
 // the decode consumers read through, scales are dense.
-int make_templates(TmapTemplates *t, int fmt, int D, int I, int ks1, int ks2, void *placeholder) {
+// With *box3d set on entry, the weight maps are first tried as 3-D maps (one
+// copy per matrix per stage); *box3d says on return which form was encoded.
+int make_templates(TmapTemplates *t, int fmt, int D, int I, int ks1, int ks2, void *placeholder,
+                   int *box3d) {
     const bool mx = fmt == MVLLM_FMT_MXFP4;
     const auto u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8, f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     const auto sw = CU_TENSOR_MAP_SWIZZLE_128B, none = CU_TENSOR_MAP_SWIZZLE_NONE;
     int rc = 0;
-    rc |= encode_2d(&t->m[0], u8, placeholder, D / 2, I, D / 2, 128, 32, sw);
-    rc |= encode_2d(&t->m[1], u8, placeholder, D / 2, I, D / 2, 128, 32, sw);
-    rc |= encode_2d(&t->m[2], u8, placeholder, I / 2, D, I / 2, 128, 64, sw);
+    if (*box3d) {
+        const int r3 = encode_3d_rows(&t->m[0], placeholder, D / 2, I, 32, ks1 / 128) |
+                       encode_3d_rows(&t->m[1], placeholder, D / 2, I, 32, ks1 / 128) |
+                       encode_3d_rows(&t->m[2], placeholder, I / 2, D, 64, ks2 / 128);
+        if (r3 != MVLLM_OK)
+            *box3d = 0; // the driver refused the chunk-major view: 2-D boxes
+    }
+    if (!*box3d) {
+        rc |= encode_2d(&t->m[0], u8, placeholder, D / 2, I, D / 2, 128, 32, sw);
+        rc |= encode_2d(&t->m[1], u8, placeholder, D / 2, I, D / 2, 128, 32, sw);
+        rc |= encode_2d(&t->m[2], u8, placeholder, I / 2, D, I / 2, 128, 64, sw);
+    }
     const int sb1 = mx ? ks1 / 16 : ks1 / 8, sb2 = mx ? ks2 / 16 : ks2 / 8; // bytes per row
     if (mx) {
         rc |= encode_2d(&t->m[3], u8, placeholder, D / 32, I, D / 32, sb1, 32, none);
@@ -469,7 +510,8 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     if (fast) {
         // Per-expert tensor maps: host templates, device-side address swap.
         TmapTemplates tpl;
-        if (int rc = make_templates(&tpl, fmt, D, I, pick_ks(D), pick_ks(I), w.y))
+        int box3d = getenv("MVLLM_DECODE_2D_BOXES") ? 0 : 1;
+        if (int rc = make_templates(&tpl, fmt, D, I, pick_ks(D), pick_ks(I), w.y, &box3d))
             return rc;
         const int nmaps = nb * kTmapsPerExpert;
         CUDA_TRY(cudaMemsetAsync(w.tmaps_dirty, 0, sizeof(int), st));
@@ -507,6 +549,7 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
         a.x = static_cast<const __half *>(xop);
         a.K = D, a.O = I, a.out = w.h;
         a.act = act, a.act_a = act_a, a.act_b = act_b, a.err = w.err;
+        a.wbox3d = box3d;
         int rc = (fmt == MVLLM_FMT_MXFP4)
                      ? launch_decode<MVLLM_FMT_MXFP4, 1>(a, pick_ks(D), nt, st, sms)
                      : launch_decode<MVLLM_FMT_INT4_G64, 1>(a, pick_ks(D), nt, st, sms);
