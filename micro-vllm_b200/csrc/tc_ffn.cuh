@@ -86,12 +86,12 @@ template <bool PAIR> struct TcCfg {
     static constexpr int NALIGN = PAIR ? 32 : 16;      // MMA N granularity
     static constexpr int ACC_HALF = PAIR ? 128 : 64;   // TMEM columns of one accumulator half
     static constexpr int A_BASE = 2 * ACC_HALF;
-    static constexpr int STAGES = PAIR ? 7 : 4;        // token + A operand ring (k-blocks)
+    static constexpr int STAGES = PAIR ? 4 : 2;        // token + A operand ring (2 k-blocks each)
     static constexpr int TMEM_COLS = PAIR ? 512 : 256;
     static constexpr int TOK_ROWS = PAIR ? NT / 2 : NT; // token rows one CTA holds
-    static constexpr int FULL_ARRIVALS = 1 + (PAIR ? 8 : 4);
+    static constexpr int FULL_ARRIVALS = 1 + (PAIR ? 16 : 4); // producer + dequant warps
     static constexpr int ACC_EMPTY_ARRIVALS = PAIR ? 2 * EPI_WARPS : EPI_WARPS;
-    static_assert(A_BASE + STAGES * 32 <= TMEM_COLS, "TMEM budget");
+    static_assert(A_BASE + STAGES * 64 <= TMEM_COLS, "TMEM budget");
 };
 enum { kTcGateP = 0, kTcUpP, kTcDownP, kTcGateS, kTcUpS, kTcDownS, kTcMapCount };
 constexpr int kTcMapBytes = 128;
@@ -117,13 +117,16 @@ struct TcArgs {
 // Per CTA: TMEM columns [0, 2 * ACC_HALF) accumulators -- one buffer of both
 // halves for a tile wider than a half, or two halves that alternate between
 // narrower tiles (the epilogue of one overlaps the MMAs of the next); then
-// one 32-column A stage (128 weight rows x 64 f16) per ring stage.
+// one 64-column A stage (128 weight rows x 128 f16: two k-blocks) per ring
+// stage.  A stage holds two k-blocks so that one wait and one commit cover
+// eight MMAs.
 template <bool PAIR> struct TcLayout {
     using C = TcCfg<PAIR>;
-    static constexpr int TOK_STAGE = C::TOK_ROWS * 128; // this CTA's token rows, one k-block
+    static constexpr int TOK_KB = C::TOK_ROWS * 128;   // this CTA's token rows, one k-block
+    static constexpr int TOK_STAGE = 2 * TOK_KB;        // a stage holds two k-blocks
     static constexpr int PK_STAGE = 128 * 64;           // 128 weight rows x 64 B (2 k-blocks)
     static constexpr int SC_STAGE = 128 * 16;           // 128 weight rows x one scale window
-    static constexpr int A_COLS = 32;
+    static constexpr int A_COLS = 64; // two k-blocks of 128 rows x 64 f16
     static constexpr int OFF_PK = C::STAGES * TOK_STAGE;
     static constexpr int OFF_SC = OFF_PK + kTcPkSlots * PK_STAGE;
     static constexpr int OFF_BAR = OFF_SC + kTcScSlots * SC_STAGE;
@@ -474,7 +477,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                 const int rows = PAIR ? it.nmma >> 1 : it.nmma; // this CTA's token rows
                 const int xr = __ldg(p.xrow + it.e) + it.t0 + static_cast<int>(rank) * rows;
                 const int nbox = (rows + kTcTokBox - 1) / kTcTokBox;
-                for (int kb = 0; kb < nk; ++kb) {
+                for (int kb = 0; kb < nk; kb += 2) {
                     const uint32_t s = st_it % S, par = (st_it / S) & 1u;
                     if (!mbar_wait(&empty[s], par ^ 1u, p.err)) {
                         ok = false;
@@ -483,16 +486,20 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                     uint8_t *dst = smem + s * L::TOK_STAGE;
                     if (PAIR) {
                         if (rank == 0)
-                            mbar_arrive_expect_tx(&full[s], 2u * nbox * kTcTokBox * 128);
+                            mbar_arrive_expect_tx(&full[s], 2u * 2u * nbox * kTcTokBox * 128);
                         const uint32_t fb = cluster_addr(&full[s], 0);
-                        for (int j = 0; j < nbox; ++j)
-                            tma_load_2d_pair(dst + j * kTcTokBox * 128, &tok_map, kb * kTcKb,
-                                             xr + j * kTcTokBox, fb, pol_t);
+                        for (int kk = 0; kk < 2; ++kk)
+                            for (int j = 0; j < nbox; ++j)
+                                tma_load_2d_pair(dst + kk * L::TOK_KB + j * kTcTokBox * 128,
+                                                 &tok_map, (kb + kk) * kTcKb, xr + j * kTcTokBox,
+                                                 fb, pol_t);
                     } else {
-                        mbar_arrive_expect_tx(&full[s], nbox * kTcTokBox * 128);
-                        for (int j = 0; j < nbox; ++j)
-                            tma_load_2d(dst + j * kTcTokBox * 128, &tok_map, kb * kTcKb,
-                                        xr + j * kTcTokBox, &full[s], pol_t);
+                        mbar_arrive_expect_tx(&full[s], 2u * nbox * kTcTokBox * 128);
+                        for (int kk = 0; kk < 2; ++kk)
+                            for (int j = 0; j < nbox; ++j)
+                                tma_load_2d(dst + kk * L::TOK_KB + j * kTcTokBox * 128, &tok_map,
+                                            (kb + kk) * kTcKb, xr + j * kTcTokBox, &full[s],
+                                            pol_t);
                     }
                     ++st_it;
                 }
@@ -589,27 +596,35 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                 tc_fence_after();
                 const uint32_t d = tmem + (b == 1 ? static_cast<uint32_t>(C::ACC_HALF) : 0u);
                 const uint32_t idesc = tc_idesc(PAIR ? 256 : 128, it.nmma);
-                for (int kb = 0; kb < nk; ++kb) {
+                for (int kb = 0; kb < nk; kb += 2) {
                     const uint32_t s = st_it % S;
                     if (!mbar_wait(&full[s], (st_it / S) & 1u, p.err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t bdesc = tc_desc_sw128(tok_base + s * L::TOK_STAGE);
                     const uint32_t a0 = tmem + C::A_BASE + s * L::A_COLS;
+#pragma unroll
+                    for (int kk = 0; kk < 2; ++kk) {
+                        const uint64_t bdesc =
+                            tc_desc_sw128(tok_base + s * L::TOK_STAGE + kk * L::TOK_KB);
+                        const uint32_t ak = a0 + kk * 32;
+                        if (PAIR) {
+                            tc_mma_pair(d, ak, bdesc, idesc, (kb | kk) != 0);
+                            tc_mma_pair(d, ak + 8, bdesc + 2, idesc, 1u);
+                            tc_mma_pair(d, ak + 16, bdesc + 4, idesc, 1u);
+                            tc_mma_pair(d, ak + 24, bdesc + 6, idesc, 1u);
+                        } else {
+                            tc_mma_solo(d, ak, bdesc, idesc, (kb | kk) != 0);
+                            tc_mma_solo(d, ak + 8, bdesc + 2, idesc, 1u);
+                            tc_mma_solo(d, ak + 16, bdesc + 4, idesc, 1u);
+                            tc_mma_solo(d, ak + 24, bdesc + 6, idesc, 1u);
+                        }
+                    }
                     if (PAIR) {
-                        tc_mma_pair(d, a0, bdesc, idesc, kb != 0);
-                        tc_mma_pair(d, a0 + 8, bdesc + 2, idesc, 1u);
-                        tc_mma_pair(d, a0 + 16, bdesc + 4, idesc, 1u);
-                        tc_mma_pair(d, a0 + 24, bdesc + 6, idesc, 1u);
                         tc_commit_pair(cluster_addr(&empty[s], 0));
                         tc_commit_pair(cluster_addr(&empty[s], 1));
                     } else {
-                        tc_mma_solo(d, a0, bdesc, idesc, kb != 0);
-                        tc_mma_solo(d, a0 + 8, bdesc + 2, idesc, 1u);
-                        tc_mma_solo(d, a0 + 16, bdesc + 4, idesc, 1u);
-                        tc_mma_solo(d, a0 + 24, bdesc + 6, idesc, 1u);
                         tc_commit_solo(&empty[s]);
                     }
                     ++st_it;
@@ -716,16 +731,16 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                     }
                     uint32_t v[32];
                     tc_dequant_row<FMT>(w0[jj], w1[jj], sc0, sc1, v);
-                    // The k-block's stage of the shared ring.
-                    const uint32_t sidx = st_it + static_cast<uint32_t>(jj);
-                    const uint32_t s = sidx % S;
+                    // The slot's stage of the shared ring; k-block jj is its
+                    // 32-column half.
+                    const uint32_t s = st_it % S;
                     if (!__all_sync(0xffffffffu,
-                                    mbar_wait(&empty[s], ((sidx / S) & 1u) ^ 1u, p.err))) {
+                                    mbar_wait(&empty[s], ((st_it / S) & 1u) ^ 1u, p.err))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    tc_st32(tmem + lane_addr + C::A_BASE + s * L::A_COLS, v);
+                    tc_st32(tmem + lane_addr + C::A_BASE + s * L::A_COLS + jj * 32, v);
                 }
                 if (!ok)
                     break;
@@ -733,18 +748,13 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-#pragma unroll
-                    for (int jj = 0; jj < 2; ++jj) {
-                        if (C::DQ_SETS == 2 && jj != set)
-                            continue;
-                        const uint32_t s = (st_it + static_cast<uint32_t>(jj)) % S;
-                        if (PAIR)
-                            mbar_arrive_cluster(cluster_addr(&full[s], 0));
-                        else
-                            mbar_arrive(&full[s]);
-                    }
+                    const uint32_t s = st_it % S;
+                    if (PAIR)
+                        mbar_arrive_cluster(cluster_addr(&full[s], 0));
+                    else
+                        mbar_arrive(&full[s]);
                 }
-                st_it += 2;
+                ++st_it;
             }
         }
     } else if (warp < C::EPI_WARPS) {
