@@ -240,47 +240,48 @@ __global__ void stage_rows_kernel(const TIn *__restrict__ x, const int *__restri
     }
 }
 
-// Vectorised form for the fast path (D % 8 == 0): one thread per aligned
-// 8-column chunk, 16-byte stores of f16 in stage_pos order.
+// Vectorised form for the fast path (D % 8 == 0): a CTA per row at a time,
+// a thread per aligned 8-column chunk, 16-byte stores of f16 in stage_pos
+// order (several chunks per thread in flight).
 template <typename TIn>
 __global__ void stage_rows_f16x8_kernel(const TIn *__restrict__ x, const int *__restrict__ index,
                                         const int *__restrict__ nrows_dev, int nrows_host, int D,
                                         int fmt, __half *__restrict__ out) {
     const int nrows = nrows_dev ? *nrows_dev : nrows_host;
     const int chunks = D >> 3;
-    const size_t total = static_cast<size_t>(nrows) * chunks;
-    for (size_t id = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; id < total;
-         id += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const int r = static_cast<int>(id / chunks), c = static_cast<int>(id % chunks);
-        const int src = index ? index[r] : r;
-        float v[8];
-        if constexpr (sizeof(TIn) == 4) {
-            const float4 *p = reinterpret_cast<const float4 *>(x + static_cast<size_t>(src) * D) +
-                              2 * c;
-            const float4 a = p[0], b = p[1];
-            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
-            v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-        } else {
-            const uint4 a = *(reinterpret_cast<const uint4 *>(x + static_cast<size_t>(src) * D) + c);
-            const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+    for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
+        const int src = index ? __ldg(index + r) : r;
+        const TIn *xr = x + static_cast<size_t>(src) * D;
+        uint4 *orow = reinterpret_cast<uint4 *>(out + static_cast<size_t>(r) * D);
+#pragma unroll 4
+        for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+            float v[8];
+            if constexpr (sizeof(TIn) == 4) {
+                const float4 *p = reinterpret_cast<const float4 *>(xr) + 2 * c;
+                const float4 a = __ldg(p), b = __ldg(p + 1);
+                v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+                v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+            } else {
+                const uint4 a = __ldg(reinterpret_cast<const uint4 *>(xr) + c);
+                const uint32_t w[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                v[2 * j] = __uint_as_float(w[j] << 16);
-                v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+                for (int j = 0; j < 4; ++j) {
+                    v[2 * j] = __uint_as_float(w[j] << 16);
+                    v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+                }
             }
-        }
-        __half2 h[4];
-        if (fmt == MVLLM_FMT_INT4_G64) { // k0,k4,k1,k5,k2,k6,k3,k7
+            __half2 h[4];
+            if (fmt == MVLLM_FMT_INT4_G64) { // k0,k4,k1,k5,k2,k6,k3,k7
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                h[j] = __floats2half2_rn(v[j], v[j + 4]);
-        } else {
+                for (int j = 0; j < 4; ++j)
+                    h[j] = __floats2half2_rn(v[j], v[j + 4]);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+                for (int j = 0; j < 4; ++j)
+                    h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+            }
+            orow[c] = *reinterpret_cast<const uint4 *>(h);
         }
-        *(reinterpret_cast<uint4 *>(out + static_cast<size_t>(r) * D) + c) =
-            *reinterpret_cast<const uint4 *>(h);
     }
 }
 
@@ -325,34 +326,34 @@ __global__ void permute_member_kernel(const int *__restrict__ idx, const float *
     }
 }
 
-// Step 2 (one CTA): per expert a warp counts its members (popc), a block scan
-// gives the segment starts in ascending expert id, then each warp walks its
-// bitmap row 32 words at a time, ballot-free: a warp prefix sum of the word
-// popcounts plus popc(word & lanemask) ranks every token, ascending.
-__global__ void permute_segments_kernel(const int *__restrict__ idx, int T, int K, int E,
-                                        int n_shared, int words,
-                                        const uint32_t *__restrict__ bitmap,
-                                        const float *__restrict__ wsum_in, int *__restrict__ nr,
-                                        int *__restrict__ xoff, int *__restrict__ rows,
-                                        float *__restrict__ rw, int *__restrict__ tok_pos,
-                                        int *__restrict__ n_rows) {
+// Step 2, one CTA per expert: the popcount of every bitmap word and their
+// exclusive prefix (the rank, inside the expert's segment, of the word's first
+// member), and the member count.
+__global__ void permute_count_kernel(int words, const uint32_t *__restrict__ bitmap,
+                                     int *__restrict__ wpre, int *__restrict__ nr) {
     __shared__ int warp_sums[32];
-    __shared__ int carry;
-    const int EE = E + n_shared, KK = K + n_shared;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int e = warp; e < EE; e += nw) {
-        int cnt = 0;
-        for (int j = lane; j < words; j += 32)
-            cnt += __popc(bitmap[static_cast<size_t>(e) * words + j]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-            cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-        if (lane == 0)
-            nr[e] = cnt;
+    const int e = blockIdx.x;
+    const uint32_t *row = bitmap + static_cast<size_t>(e) * words;
+    int *pre = wpre + static_cast<size_t>(e) * words;
+    int carry = 0;
+    for (int j0 = 0; j0 < words; j0 += blockDim.x) {
+        const int j = j0 + threadIdx.x;
+        const int v = j < words ? __popc(row[j]) : 0;
+        int tot;
+        const int ex = block_exclusive_scan(v, warp_sums, &tot);
+        if (j < words)
+            pre[j] = carry + ex;
+        carry += tot;
     }
     if (threadIdx.x == 0)
-        carry = 0;
-    __syncthreads();
+        nr[e] = carry;
+}
+
+// Step 3 (one CTA): segment starts in ascending expert id.
+__global__ void permute_offsets_kernel(int EE, const int *__restrict__ nr, int *__restrict__ xoff,
+                                       int *__restrict__ n_rows) {
+    __shared__ int warp_sums[32];
+    int carry = 0;
     for (int e0 = 0; e0 < EE; e0 += blockDim.x) {
         const int e = e0 + threadIdx.x;
         const int v = e < EE ? nr[e] : 0;
@@ -360,47 +361,33 @@ __global__ void permute_segments_kernel(const int *__restrict__ idx, int T, int 
         const int ex = block_exclusive_scan(v, warp_sums, &tot);
         if (e < EE)
             xoff[e] = carry + ex;
-        __syncthreads();
-        if (threadIdx.x == 0)
-            carry += tot;
-        __syncthreads();
+        carry += tot;
     }
     if (threadIdx.x == 0)
         *n_rows = carry;
-    __syncthreads();
-    for (int e = warp; e < EE; e += nw) {
-        int run = xoff[e];
-        for (int j0 = 0; j0 < words; j0 += 32) {
-            const int j = j0 + lane;
-            uint32_t m = j < words ? bitmap[static_cast<size_t>(e) * words + j] : 0u;
-            const int pc = __popc(m);
-            int incl = pc;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o)
-                    incl += y;
-            }
-            int pos = run + incl - pc;
-            while (m) {
-                const int b = __ffs(m) - 1;
-                m &= m - 1;
-                const int c = 32 * j + b;
-                int slot = K; // the shared expert's slot
-                if (e < E) {
-                    for (int t = 0; t < K; ++t)
-                        if (idx[static_cast<size_t>(c) * K + t] == e) {
-                            slot = t;
-                            break;
-                        }
-                }
-                rows[pos] = c;
-                rw[pos] = wsum_in[static_cast<size_t>(c) * KK + slot];
-                tok_pos[static_cast<size_t>(c) * KK + slot] = pos;
-                ++pos;
-            }
-            run += __shfl_sync(0xffffffffu, incl, 31);
-        }
+}
+
+// Step 4, thread per (token, slot): each member slot marked by step 1 (the
+// first slot of the token holding that expert) takes the position of its
+// bit in the expert's bitmap row -- ascending token order inside the segment.
+__global__ void permute_place_kernel(const int *__restrict__ idx, int T, int K, int E,
+                                     int n_shared, int words, const uint32_t *__restrict__ bitmap,
+                                     const int *__restrict__ wpre, const int *__restrict__ xoff,
+                                     const float *__restrict__ wsum_in, int *__restrict__ rows,
+                                     float *__restrict__ rw, int *__restrict__ tok_pos) {
+    const int KK = K + n_shared;
+    const size_t n = static_cast<size_t>(T) * KK;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        if (tok_pos[i] != -2)
+            continue;
+        const int c = static_cast<int>(i / KK), s = static_cast<int>(i - static_cast<size_t>(c) * KK);
+        const int e = s < K ? idx[static_cast<size_t>(c) * K + s] : E;
+        const size_t wi = static_cast<size_t>(e) * words + (c >> 5);
+        const int pos = xoff[e] + wpre[wi] + __popc(bitmap[wi] & ((1u << (c & 31)) - 1u));
+        rows[pos] = c;
+        rw[pos] = wsum_in[i];
+        tok_pos[i] = pos;
     }
 }
 
@@ -411,34 +398,49 @@ __global__ void permute_segments_kernel(const int *__restrict__ idx, int T, int 
 __global__ void combine_tokens_kernel(float *__restrict__ out, const float *__restrict__ y,
                                       const float *__restrict__ rw,
                                       const int *__restrict__ tok_pos, int T, int KK, int D) {
+    constexpr int kB = 4; // rows loaded per batch
     for (int c = blockIdx.y; c < T; c += gridDim.y) {
-    int pos[17];
-    int n = 0;
-    for (int t = 0; t < KK && n < 17; ++t) {
-        const int p = tok_pos[static_cast<size_t>(c) * KK + t];
-        if (p >= 0) {
-            int j = n++;
-            while (j > 0 && pos[j - 1] > p) {
-                pos[j] = pos[j - 1];
-                --j;
+        int pos[17];
+        int n = 0;
+        for (int t = 0; t < KK && n < 17; ++t) {
+            const int p = tok_pos[static_cast<size_t>(c) * KK + t];
+            if (p >= 0) {
+                int j = n++;
+                while (j > 0 && pos[j - 1] > p) {
+                    pos[j] = pos[j - 1];
+                    --j;
+                }
+                pos[j] = p;
             }
-            pos[j] = p;
         }
-    }
-    for (int col = (blockIdx.x * blockDim.x + threadIdx.x) * 4; col < D;
-         col += gridDim.x * blockDim.x * 4) {
-        float4 acc = *reinterpret_cast<const float4 *>(out + static_cast<size_t>(c) * D + col);
-        for (int j = 0; j < n; ++j) {
-            const float w = rw[pos[j]];
-            const float4 v =
-                *reinterpret_cast<const float4 *>(y + static_cast<size_t>(pos[j]) * D + col);
-            acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
-            acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
-            acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
-            acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+        for (int col = (blockIdx.x * blockDim.x + threadIdx.x) * 4; col < D;
+             col += gridDim.x * blockDim.x * 4) {
+            float4 acc = *reinterpret_cast<const float4 *>(out + static_cast<size_t>(c) * D + col);
+            for (int j0 = 0; j0 < n; j0 += kB) {
+                // Every row of the batch in flight before the ordered adds.
+                float4 v[kB];
+                float w[kB];
+#pragma unroll
+                for (int b = 0; b < kB; ++b) {
+                    if (j0 + b < n) {
+                        const int r = pos[j0 + b];
+                        w[b] = __ldg(rw + r);
+                        v[b] = __ldcs(reinterpret_cast<const float4 *>(y + static_cast<size_t>(r) * D +
+                                                                       col));
+                    }
+                }
+#pragma unroll
+                for (int b = 0; b < kB; ++b) {
+                    if (j0 + b < n) {
+                        acc.x = __fadd_rn(acc.x, __fmul_rn(w[b], v[b].x));
+                        acc.y = __fadd_rn(acc.y, __fmul_rn(w[b], v[b].y));
+                        acc.z = __fadd_rn(acc.z, __fmul_rn(w[b], v[b].z));
+                        acc.w = __fadd_rn(acc.w, __fmul_rn(w[b], v[b].w));
+                    }
+                }
+            }
+            *reinterpret_cast<float4 *>(out + static_cast<size_t>(c) * D + col) = acc;
         }
-        *reinterpret_cast<float4 *>(out + static_cast<size_t>(c) * D + col) = acc;
-    }
     }
 }
 

@@ -487,7 +487,7 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     const void *xop = x;
     if (!x_staged) {
         if (fast) {
-            const int blocks = std::max(1, std::min((x_rows * (D / 8) + 255) / 256, 8 * sms));
+            const int blocks = std::max(1, std::min(x_rows, 8 * sms));
             if (x_dtype == MVLLM_DTYPE_BF16)
                 stage_rows_f16x8_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
                     static_cast<const __nv_bfloat16 *>(x), nullptr, nullptr, x_rows, D, fmt,
@@ -1138,12 +1138,14 @@ int mvllm_moe_block_dev(void *stream, int nb, int D, int Iinter, int fmt, const 
 namespace {
 struct PermWs {
     uint32_t *bitmap;
+    int *wpre;
     float *wsum;
     int words;
 };
 void carve_perm(Carve &cv, PermWs &p, int T, int K, int E, int n_shared) {
     p.words = (T + 31) / 32;
     p.bitmap = cv.take<uint32_t>(size_t(E + n_shared) * p.words);
+    p.wpre = cv.take<int>(size_t(E + n_shared) * p.words);
     p.wsum = cv.take<float>(size_t(T) * (K + n_shared));
 }
 int run_permute(cudaStream_t st, int sms, const int *idx, const float *wt, int T, int K, int E,
@@ -1153,8 +1155,14 @@ int run_permute(cudaStream_t st, int sms, const int *idx, const float *wt, int T
     permute_member_kernel<<<std::max(1, std::min((T + 127) / 128, 4 * sms)), 128, 0, st>>>(
         idx, wt, T, K, E, n_shared, p.words, p.bitmap, p.wsum, tok_pos);
     CUDA_TRY(cudaGetLastError());
-    permute_segments_kernel<<<1, 1024, 0, st>>>(idx, T, K, E, n_shared, p.words, p.bitmap, p.wsum,
-                                                nr, xoff, rows, rw, tok_pos, n_rows);
+    permute_count_kernel<<<E + n_shared, 256, 0, st>>>(p.words, p.bitmap, p.wpre, nr);
+    CUDA_TRY(cudaGetLastError());
+    permute_offsets_kernel<<<1, 1024, 0, st>>>(E + n_shared, nr, xoff, n_rows);
+    CUDA_TRY(cudaGetLastError());
+    const size_t slots = size_t(T) * (K + n_shared);
+    permute_place_kernel<<<static_cast<int>(std::min<size_t>((slots + 255) / 256, 16 * sms)), 256, 0,
+                           st>>>(idx, T, K, E, n_shared, p.words, p.bitmap, p.wpre, xoff, p.wsum,
+                                 rows, rw, tok_pos);
     CUDA_TRY(cudaGetLastError());
     return MVLLM_OK;
 }
@@ -1305,7 +1313,7 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
     // Gather + stage the token rows into expert-major order.
     const int gblocks = std::min(R, 8 * sms);
     if (fast) {
-        const int vblocks = std::max(1, std::min((R * (D / 8) + 255) / 256, 8 * sms));
+        const int vblocks = std::max(1, std::min(R, 8 * sms));
         if (x_dtype == MVLLM_DTYPE_BF16)
             stage_rows_f16x8_kernel<__nv_bfloat16><<<vblocks, 256, 0, st>>>(
                 static_cast<const __nv_bfloat16 *>(x), l.rows, l.n_rows, 0, D, fmt,
