@@ -24,6 +24,8 @@ import sys
 import threading
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "micro-vllm_b200"))
 
@@ -166,6 +168,8 @@ class Workload:
                             for t in (self.gp, self.up, self.dp, self.gs, self.us, self.ds)]
         self.tables = [torch.tensor(t, dtype=torch.int64, device="cuda")
                        for t in self.host_tables]
+        # The host API's address tables as int64 arrays (passed without a copy).
+        self.host_tables = [np.asarray(t, dtype=np.int64) for t in self.host_tables]
         self.inputs = []
         for _ in range(N_INPUTS):
             choice = torch.rand((B, E), generator=g, device="cuda")
@@ -290,12 +294,14 @@ def prefill_bench(moe, torch, wl, steps, peak_tf, peak_gbs, T=PREFILL_T):
 EP_E, EP_T = 384, 8192
 
 
-def ep_bench(moe, torch, dist, rank, world, steps):
+def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
     """Config[4]: 384 MXFP4 experts sharded over the ranks (expert e on rank
-    e % world), 8192 tokens per step split evenly over the ranks, top-8;
-    uniform and Zipf s=1.1 routing.  Weights are drawn per global expert id, so
-    the model is the same whatever the rank count; total work per step is
-    fixed (strong scaling), tokens/s = 8192 / step time (max over ranks)."""
+    e % world), top-8; uniform and Zipf s=1.1 routing.  Weights are drawn per
+    global expert id, so the model is the same whatever the rank count.
+    Strong scaling (default): 8192 tokens per step split evenly over the
+    ranks.  Weak scaling (`weak`): 8192 tokens per rank per step (each rank
+    brings its own batch, as data-parallel attention feeds an expert-parallel
+    layer).  tokens/s = all ranks' tokens / step time (max over ranks)."""
     import ep
     D, I, K = CFG["D"], CFG["I"], CFG["K"]
     mine = ep.local_experts(rank, world, EP_E)
@@ -314,12 +320,13 @@ def ep_bench(moe, torch, dist, rank, world, steps):
             moe.pack_mxfp4_dev(w, pk[j], sc[j])
     tabs = [torch.tensor([t[j].data_ptr() for j in range(n)], dtype=torch.int64, device="cuda")
             for t in (gp, up, dp, gs, us, ds)]
+    T_loc = EP_T if weak else EP_T // world
+    T_all = T_loc * world
     ops = ep.CudaOps(torch, EP_E, K, D, I, CFG["fmt"], CFG["act"], CFG["act_a"], CFG["act_b"],
-                     tabs, world, EP_T)
+                     tabs, world, T_all)
     layer = ep.EPLayer(ops, rank, world, D, K)
-    T_loc = EP_T // world
     g = torch.Generator(device="cuda").manual_seed(777)
-    x_all = torch.randn((EP_T, D), generator=g, device="cuda").to(torch.bfloat16)
+    x_all = torch.randn((T_all, D), generator=g, device="cuda").to(torch.bfloat16)
     x = x_all[rank * T_loc:(rank + 1) * T_loc].contiguous()
     del x_all
     out = torch.zeros((T_loc, D), dtype=torch.float32, device="cuda")
@@ -327,12 +334,13 @@ def ep_bench(moe, torch, dist, rank, world, steps):
     for name in ("uniform", "zipf"):
         gr = torch.Generator(device="cuda").manual_seed(778 if name == "uniform" else 779)
         if name == "uniform":
-            choice = torch.rand((EP_T, EP_E), generator=gr, device="cuda")
+            choice = torch.rand((T_all, EP_E), generator=gr, device="cuda")
             vals, idx = torch.topk(choice, K, dim=1)
             wt = (vals / vals.sum(1, keepdim=True)).float()
             idx = idx.int()
+            del choice, vals
         else:
-            idx, wt = zipf_routing(torch, EP_T, EP_E, K, gr)
+            idx, wt = zipf_routing(torch, T_all, EP_E, K, gr)
         idx = idx[rank * T_loc:(rank + 1) * T_loc].contiguous()
         wt = wt[rank * T_loc:(rank + 1) * T_loc].contiguous()
 
@@ -360,7 +368,7 @@ def ep_bench(moe, torch, dist, rank, world, steps):
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-        res[name] = {"tokens_per_s": EP_T / (ms / 1e3), "ms_per_step": ms, "steps": steps}
+        res[name] = {"tokens_per_s": T_all / (ms / 1e3), "ms_per_step": ms, "steps": steps}
         if world > 1:
             # One more step with phase events (not part of the timed steps).
             tm = {}
@@ -373,11 +381,14 @@ def ep_bench(moe, torch, dist, rank, world, steps):
         if info:
             res[name]["rank0_sent_rows"] = info["sent_rows"]
             res[name]["rank0_received_rows"] = info["received_rows"]
-    del gp, up, dp, gs, us, ds
+    del gp, up, dp, gs, us, ds, layer, ops
+    torch.cuda.empty_cache()
+    per = "8192 tokens per rank per step" if weak else "8192 tokens per step"
     return {"workload": "config[4] expert-parallel MXFP4 layer: 384 experts strided over the "
-                        "ranks, hidden 7168, inter 2048, top-8, 8192 tokens per step, bf16 "
+                        f"ranks, hidden 7168, inter 2048, top-8, {per}, bf16 "
                         "activations; NCCL all-to-all dispatch and return",
-            "n_gpus": world, "scaling": "strong", "experts_per_rank": n, **res}
+            "n_gpus": world, "scaling": "weak" if weak else "strong", "tokens_per_step": T_all,
+            "experts_per_rank": n, **res}
 
 
 # ------------------------------------------------------------ CPU baseline --
@@ -589,6 +600,9 @@ def main():
     ep_res = None
     if not args.no_ep:
         ep_res = ep_bench(moe, torch, dist, rank, world, args.ep_steps)
+        # Weak scaling: 8192 tokens per rank (at 1 GPU the same run as above).
+        ep_res["weak_scaling"] = (ep_bench(moe, torch, dist, rank, world, args.ep_steps, weak=True)
+                                  if world > 1 else "same workload as the strong run at 1 GPU")
 
     # config[3] prefill (tensor-core kernels), per rank
     prefill = None

@@ -17,6 +17,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <mutex>
 #include <string>
@@ -1298,10 +1299,19 @@ size_t mvllm_moe_layer_workspace(int T, int K, int E, int n_shared, int D, int I
     return cv.used + 256;
 }
 
+// Host work a caller can slot in before the stages that first read x
+// (`before_gather`) and out (`before_combine`): the host-buffer entry stages
+// those rows there, so their host copies overlap the device work queued
+// ahead of them.
+struct LayerHooks {
+    std::function<int()> before_gather, before_combine;
+};
+
 static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_shared, int D,
                           int Iinter, int fmt, const int *idx, const float *wt, const void *x,
                           int x_dtype, const Tables &tb, float *out, int act, float act_a,
-                          float act_b, const LayerWs &l, bool allow_tc = true) {
+                          float act_b, const LayerWs &l, bool allow_tc = true,
+                          const LayerHooks *hooks = nullptr) {
     const bool fast = fast_path_ok(fmt, D, Iinter);
     const int EE = E + n_shared, KK = K + n_shared, R = T * KK;
     CUDA_TRY(cudaMemsetAsync(l.run.err, 0, sizeof(int), st));
@@ -1310,6 +1320,9 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
                              l.tok_pos, l.n_rows, l.perm))
         return rc;
     prof_mark(st, kPhPermute);
+    if (hooks && hooks->before_gather)
+        if (int rc = hooks->before_gather())
+            return rc;
     // Gather + stage the token rows into expert-major order.
     const int gblocks = std::min(R, 8 * sms);
     if (fast) {
@@ -1338,6 +1351,9 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
     if (int rc = run_experts(st, sms, EE, D, Iinter, fmt, tb, l.nr, l.xoff, l.run.xs,
                              MVLLM_DTYPE_F32, R, true, R / EE, act, act_a, act_b, w, allow_tc))
         return rc;
+    if (hooks && hooks->before_combine)
+        if (int rc = hooks->before_combine())
+            return rc;
     dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
     combine_tokens_kernel<<<grid, 256, 0, st>>>(out, w.y, l.rw, l.tok_pos, T, KK, D);
     CUDA_TRY(cudaGetLastError());
@@ -1415,14 +1431,18 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     const size_t up = tab_b + 2 * idx_b + 2 * x_b + 1024;
     if (int rc = ensure_pinned(c, up))
         return rc;
+    // Pinned staging, uploaded in three pieces: tables + routing (read by the
+    // permutation), x (first read by the gather), out (read by the combine).
     Carve hcv(c.pinned, c.pinned_bytes);
     void **htab = hcv.take<void *>(size_t(6) * EE);
     int *hidx = hcv.take<int>(size_t(T) * K);
     float *hwt = hcv.take<float>(size_t(T) * K);
     float *hx = hcv.take<float>(size_t(T) * D);
     float *hout = hcv.take<float>(size_t(T) * D);
-    const size_t up_bytes = reinterpret_cast<uint8_t *>(hout) - static_cast<uint8_t *>(c.pinned) +
-                            x_b;
+    uint8_t *hbase = static_cast<uint8_t *>(c.pinned);
+    const size_t x_off = reinterpret_cast<uint8_t *>(hx) - hbase;
+    const size_t out_off = reinterpret_cast<uint8_t *>(hout) - hbase;
+    const size_t up_bytes = out_off + x_b;
     for (int e = 0; e < EE; ++e) {
         htab[e] = const_cast<void *>(g[e]);
         htab[EE + e] = const_cast<void *>(u[e]);
@@ -1433,8 +1453,6 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     }
     memcpy(hidx, idx, idx_b);
     memcpy(hwt, wt, idx_b);
-    memcpy(hx, x, x_b);
-    memcpy(hout, out, x_b);
     Carve dcv(nullptr, ~size_t(0));
     dcv.take<uint8_t>(up_bytes);
     LayerWs l{};
@@ -1445,20 +1463,31 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     Carve dcv2(db, c.ws.bytes);
     dcv2.take<uint8_t>(up_bytes);
     carve_layer(dcv2, l, T, K, E, n_shared, D, Iinter, fast);
-    auto dptr = [&](const void *hp) {
-        return db + (static_cast<const uint8_t *>(hp) - static_cast<uint8_t *>(c.pinned));
-    };
+    auto dptr = [&](const void *hp) { return db + (static_cast<const uint8_t *>(hp) - hbase); };
     CUDA_TRY(cudaEventRecord(c.ev[0], c.stream));
-    CUDA_TRY(cudaMemcpyAsync(db, c.pinned, up_bytes, cudaMemcpyHostToDevice, c.stream));
+    CUDA_TRY(cudaMemcpyAsync(db, c.pinned, x_off, cudaMemcpyHostToDevice, c.stream));
     CUDA_TRY(cudaEventRecord(c.ev[1], c.stream));
     void *const *dt = reinterpret_cast<void *const *>(dptr(htab));
     Tables tb{dt, dt + EE, dt + 2 * EE, dt + 3 * EE, dt + 4 * EE, dt + 5 * EE};
     float *dout = reinterpret_cast<float *>(dptr(hout));
+    LayerHooks hooks;
+    hooks.before_gather = [&]() -> int {
+        memcpy(hx, x, x_b); // the permutation kernels run meanwhile
+        CUDA_TRY(cudaMemcpyAsync(db + x_off, hx, x_b, cudaMemcpyHostToDevice, c.stream));
+        return MVLLM_OK;
+    };
+    hooks.before_combine = [&]() -> int {
+        memcpy(hout, out, x_b); // the expert kernels run meanwhile
+        CUDA_TRY(cudaMemcpyAsync(dout, hout, x_b, cudaMemcpyHostToDevice, c.stream));
+        return MVLLM_OK;
+    };
     if (int rc = layer_dev_impl(c.stream, c.sms, T, K, E, n_shared, D, Iinter, fmt,
                                 reinterpret_cast<const int *>(dptr(hidx)),
                                 reinterpret_cast<const float *>(dptr(hwt)), dptr(hx),
-                                MVLLM_DTYPE_F32, tb, dout, act, act_a, act_b, l, allow_tc))
+                                MVLLM_DTYPE_F32, tb, dout, act, act_a, act_b, l, allow_tc, &hooks)) {
+        cudaStreamSynchronize(c.stream); // no copy may still read the staging buffer
         return rc;
+    }
     CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
     CUDA_TRY(cudaMemcpyAsync(hout, dout, x_b, cudaMemcpyDeviceToHost, c.stream));
     CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));

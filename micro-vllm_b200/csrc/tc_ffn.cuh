@@ -87,6 +87,7 @@ template <bool PAIR> struct TcCfg {
     static constexpr int ACC_HALF = PAIR ? 128 : 64;   // TMEM columns of one accumulator half
     static constexpr int A_BASE = 2 * ACC_HALF;
     static constexpr int STAGES = PAIR ? 4 : 2;        // token + A operand ring (2 k-blocks each)
+    static constexpr int PK_SLOTS = kTcPkSlots;        // packed-weight ring depth
     static constexpr int TMEM_COLS = PAIR ? 512 : 256;
     static constexpr int TOK_ROWS = PAIR ? NT / 2 : NT; // token rows one CTA holds
     static constexpr int FULL_ARRIVALS = 1 + (PAIR ? 16 : 4); // producer + dequant warps
@@ -128,9 +129,9 @@ template <bool PAIR> struct TcLayout {
     static constexpr int SC_STAGE = 128 * 16;           // 128 weight rows x one scale window
     static constexpr int A_COLS = 64; // two k-blocks of 128 rows x 64 f16
     static constexpr int OFF_PK = C::STAGES * TOK_STAGE;
-    static constexpr int OFF_SC = OFF_PK + kTcPkSlots * PK_STAGE;
+    static constexpr int OFF_SC = OFF_PK + C::PK_SLOTS * PK_STAGE;
     static constexpr int OFF_BAR = OFF_SC + kTcScSlots * SC_STAGE;
-    static constexpr int NBARS = 2 * C::STAGES + 2 * kTcPkSlots + 2 * kTcScSlots + 4 + 1;
+    static constexpr int NBARS = 2 * C::STAGES + 2 * C::PK_SLOTS + 2 * kTcScSlots + 4 + 1;
     static constexpr int ITEM_TAB = 512; // item offsets and row counts of up to 511 experts
     static constexpr int OFF_ITEMS = OFF_BAR + NBARS * 8 + 16;
     static constexpr int SMEM = OFF_ITEMS + 2 * ITEM_TAB * 4 + 1024; // + alignment
@@ -394,8 +395,8 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
     uint64_t *full = bars, *empty = bars + S; // tokens + A stage
-    uint64_t *pk_full = empty + S, *pk_empty = pk_full + kTcPkSlots;
-    uint64_t *sc_full = pk_empty + kTcPkSlots, *sc_empty = sc_full + kTcScSlots;
+    uint64_t *pk_full = empty + S, *pk_empty = pk_full + C::PK_SLOTS;
+    uint64_t *sc_full = pk_empty + C::PK_SLOTS, *sc_empty = sc_full + kTcScSlots;
     uint64_t *acc_full = sc_empty + kTcScSlots, *acc_empty = acc_full + 2, *done = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     int *off_s = reinterpret_cast<int *>(smem + L::OFF_ITEMS);
@@ -426,7 +427,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
             mbar_init(&full[s], C::FULL_ARRIVALS);
             mbar_init(&empty[s], 1); // the (leader's) tcgen05.commit
         }
-        for (int s = 0; s < kTcPkSlots; ++s) {
+        for (int s = 0; s < C::PK_SLOTS; ++s) {
             mbar_init(&pk_full[s], 1);
             mbar_init(&pk_empty[s], C::DQ_WARPS);
         }
@@ -552,7 +553,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                         }
                         ++sc_it;
                     }
-                    const uint32_t s = pk_it % kTcPkSlots, par = (pk_it / kTcPkSlots) & 1u;
+                    const uint32_t s = pk_it % C::PK_SLOTS, par = (pk_it / C::PK_SLOTS) & 1u;
                     if (!mbar_wait(&pk_empty[s], par ^ 1u, p.err)) {
                         ok = false;
                         break;
@@ -571,8 +572,8 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                 }
             }
             // Drain: wait for every copy still in flight before the CTA ends.
-            for (uint32_t j = pk_it > kTcPkSlots ? pk_it - kTcPkSlots : 0; j < pk_it; ++j)
-                mbar_wait(&pk_full[j % kTcPkSlots], (j / kTcPkSlots) & 1u, nullptr);
+            for (uint32_t j = pk_it > C::PK_SLOTS ? pk_it - C::PK_SLOTS : 0; j < pk_it; ++j)
+                mbar_wait(&pk_full[j % C::PK_SLOTS], (j / C::PK_SLOTS) & 1u, nullptr);
             for (uint32_t j = sc_it > kTcScSlots ? sc_it - kTcScSlots : 0; j < sc_it; ++j)
                 mbar_wait(&sc_full[j % kTcScSlots], (j / kTcScSlots) & 1u, nullptr);
         }
@@ -689,9 +690,9 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                         mbar_arrive(&sc_empty[w]);
                     ++sc_it;
                 }
-                const uint32_t ps = pk_it % kTcPkSlots;
+                const uint32_t ps = pk_it % C::PK_SLOTS;
                 if (!__all_sync(0xffffffffu,
-                                mbar_wait(&pk_full[ps], (pk_it / kTcPkSlots) & 1u, p.err))) {
+                                mbar_wait(&pk_full[ps], (pk_it / C::PK_SLOTS) & 1u, p.err))) {
                     ok = false;
                     break;
                 }

@@ -191,13 +191,23 @@ def cache_bytes() -> int:
     return lib().mvllm_moe_cache_bytes()
 
 
+def _addr_array(t):
+    """A table of device addresses for the C ABI: a contiguous int64/uint64
+    numpy array is passed in place, any other sequence of ints is copied."""
+    if isinstance(t, np.ndarray) and t.dtype in (np.int64, np.uint64) and t.ndim == 1 \
+            and t.flags["C_CONTIGUOUS"]:
+        return C.cast(t.ctypes.data, C.POINTER(C.c_void_p))
+    return (C.c_void_p * len(t))(*t)
+
+
 def layer_host(T, K, E, n_shared, D, Iinter, fmt, idx, wt, x, tables, out, act, act_a=0.0,
                act_b=0.0):
     """Routed layer with host activations/routing and device-resident weights.
 
-    ``tables`` holds six sequences of device addresses (ints): g, u, d, gs, us, ds.
+    ``tables`` holds six sequences of device addresses (ints, or int64 numpy
+    arrays, which are passed without a copy): g, u, d, gs, us, ds.
     """
-    arrs = [(C.c_void_p * len(t))(*t) for t in tables]
+    arrs = [_addr_array(t) for t in tables]
     _check(lib().mvllm_moe_layer_host(T, K, E, n_shared, D, Iinter, fmt, _p(idx), _p(wt), _p(x),
                                       *arrs, _p(out), act, act_a, act_b))
 
