@@ -224,10 +224,13 @@ def graph_throughput(moe, torch, wl, steps, warmup):
 PREFILL_T = 4096
 
 
-def zipf_routing(torch, T, E, K, g, s=1.1):
+def zipf_routing(torch, T, E, K, g, s=1.1, perm=None):
     """BASELINE config[3] routing: logits = -s ln(rank) + Gumbel noise per token
-    over a seeded random ranking of the experts, softmax, top-K renormalised."""
-    perm = torch.randperm(E, generator=g, device="cuda")
+    over a seeded random ranking of the experts, softmax, top-K renormalised.
+    `perm` (optional) fixes the ranking, so that draws with different token
+    noise share the same popular experts."""
+    if perm is None:
+        perm = torch.randperm(E, generator=g, device="cuda")
     rank = torch.empty(E, device="cuda")
     rank[perm] = torch.arange(1, E + 1, device="cuda", dtype=torch.float32)
     u = torch.rand((T, E), generator=g, device="cuda").clamp_min(1e-20)
@@ -294,6 +297,20 @@ def prefill_bench(moe, torch, wl, steps, peak_tf, peak_gbs, T=PREFILL_T):
 EP_E, EP_T = 384, 8192
 
 
+def ep_routing(torch, name, T, K, seed):
+    """Config[4] routing draws; every Zipf draw ranks the experts the same way
+    (the model's popular experts), the token noise comes from `seed`."""
+    gr = torch.Generator(device="cuda").manual_seed(seed)
+    if name == "uniform":
+        choice = torch.rand((T, EP_E), generator=gr, device="cuda")
+        vals, idx = torch.topk(choice, K, dim=1)
+        wt = (vals / vals.sum(1, keepdim=True)).float()
+        return idx.int(), wt
+    perm = torch.randperm(EP_E, generator=torch.Generator(device="cuda").manual_seed(779),
+                          device="cuda")
+    return zipf_routing(torch, T, EP_E, K, gr, perm=perm)
+
+
 def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
     """Config[4]: 384 MXFP4 experts sharded over the ranks (expert e on rank
     e % world), top-8; uniform and Zipf s=1.1 routing.  Weights are drawn per
@@ -301,30 +318,30 @@ def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
     Strong scaling (default): 8192 tokens per step split evenly over the
     ranks.  Weak scaling (`weak`): 8192 tokens per rank per step (each rank
     brings its own batch, as data-parallel attention feeds an expert-parallel
-    layer).  tokens/s = all ranks' tokens / step time (max over ranks)."""
+    layer).  tokens/s = all ranks' tokens / step time (max over ranks).
+    Hot experts are replicated on every rank (ep.balance_replicas, at most
+    2 per rank) from the loads of a separate calibration draw of the same
+    routing distribution; each rank serves its own tokens' rows for them."""
     import ep
     D, I, K = CFG["D"], CFG["I"], CFG["K"]
-    mine = ep.local_experts(rank, world, EP_E)
     u8 = torch.uint8
-    n = len(mine)
-    gp = torch.empty((n, I, D // 2), dtype=u8, device="cuda")
-    up = torch.empty_like(gp)
-    dp = torch.empty((n, D, I // 2), dtype=u8, device="cuda")
-    gs = torch.empty((n, I, D // 32), dtype=u8, device="cuda")
-    us = torch.empty_like(gs)
-    ds = torch.empty((n, D, I // 32), dtype=u8, device="cuda")
-    for j, e in enumerate(mine):
-        g = torch.Generator(device="cuda").manual_seed(100000 + e)
-        for pk, sc, shape in ((gp, gs, (I, D)), (up, us, (I, D)), (dp, ds, (D, I))):
-            w = torch.randn(shape, generator=g, device="cuda").mul_(0.02)
-            moe.pack_mxfp4_dev(w, pk[j], sc[j])
-    tabs = [torch.tensor([t[j].data_ptr() for j in range(n)], dtype=torch.int64, device="cuda")
-            for t in (gp, up, dp, gs, us, ds)]
     T_loc = EP_T if weak else EP_T // world
     T_all = T_loc * world
-    ops = ep.CudaOps(torch, EP_E, K, D, I, CFG["fmt"], CFG["act"], CFG["act_a"], CFG["act_b"],
-                     tabs, world, T_all)
-    layer = ep.EPLayer(ops, rank, world, D, K)
+    wcache = {}
+
+    def expert(e):  # the same weights for a global id on every rank and rank count
+        if e not in wcache:
+            g = torch.Generator(device="cuda").manual_seed(100000 + e)
+            mats = []
+            for shape in ((I, D), (I, D), (D, I)):
+                w = torch.randn(shape, generator=g, device="cuda").mul_(0.02)
+                pk = torch.empty((shape[0], shape[1] // 2), dtype=u8, device="cuda")
+                sc = torch.empty((shape[0], shape[1] // 32), dtype=u8, device="cuda")
+                moe.pack_mxfp4_dev(w, pk, sc)
+                mats.append((pk, sc))
+            wcache[e] = mats
+        return wcache[e]
+
     g = torch.Generator(device="cuda").manual_seed(777)
     x_all = torch.randn((T_all, D), generator=g, device="cuda").to(torch.bfloat16)
     x = x_all[rank * T_loc:(rank + 1) * T_loc].contiguous()
@@ -332,15 +349,24 @@ def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
     out = torch.zeros((T_loc, D), dtype=torch.float32, device="cuda")
     res = {}
     for name in ("uniform", "zipf"):
-        gr = torch.Generator(device="cuda").manual_seed(778 if name == "uniform" else 779)
-        if name == "uniform":
-            choice = torch.rand((T_all, EP_E), generator=gr, device="cuda")
-            vals, idx = torch.topk(choice, K, dim=1)
-            wt = (vals / vals.sum(1, keepdim=True)).float()
-            idx = idx.int()
-            del choice, vals
-        else:
-            idx, wt = zipf_routing(torch, T_all, EP_E, K, gr)
+        # Placement from a calibration draw of the same distribution.
+        cal, _ = ep_routing(torch, name, T_all, K, 990 if name == "uniform" else 991)
+        load = torch.bincount(cal.flatten().long(), minlength=EP_E).tolist()
+        del cal
+        rep = ep.balance_replicas(load, world, max_replicas=2 * world) if world > 1 else []
+        pl = ep.Placement(EP_E, world, rep)
+        mine = pl.local_experts(rank)
+        for e in list(wcache):
+            if e not in mine:
+                del wcache[e]
+        mats = [expert(e) for e in mine]
+        # (g, u, d, gs, us, ds) address tables in local-id order
+        tabs = [torch.tensor([m[j % 3][j // 3].data_ptr() for m in mats], dtype=torch.int64,
+                             device="cuda") for j in range(6)]
+        ops = ep.CudaOps(torch, EP_E, K, D, I, CFG["fmt"], CFG["act"], CFG["act_a"],
+                         CFG["act_b"], tabs, world, T_all, placement=pl, rank=rank)
+        layer = ep.EPLayer(ops, rank, world, D, K)
+        idx, wt = ep_routing(torch, name, T_all, K, 778 if name == "uniform" else 779)
         idx = idx[rank * T_loc:(rank + 1) * T_loc].contiguous()
         wt = wt[rank * T_loc:(rank + 1) * T_loc].contiguous()
 
@@ -368,7 +394,8 @@ def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-        res[name] = {"tokens_per_s": T_all / (ms / 1e3), "ms_per_step": ms, "steps": steps}
+        res[name] = {"tokens_per_s": T_all / (ms / 1e3), "ms_per_step": ms, "steps": steps,
+                     "replicated_experts": len(rep), "experts_per_rank": len(mine)}
         if world > 1:
             # One more step with phase events (not part of the timed steps).
             tm = {}
@@ -381,14 +408,15 @@ def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
         if info:
             res[name]["rank0_sent_rows"] = info["sent_rows"]
             res[name]["rank0_received_rows"] = info["received_rows"]
-    del gp, up, dp, gs, us, ds, layer, ops
+        del layer, ops, tabs, mats
+    wcache.clear()
     torch.cuda.empty_cache()
     per = "8192 tokens per rank per step" if weak else "8192 tokens per step"
     return {"workload": "config[4] expert-parallel MXFP4 layer: 384 experts strided over the "
-                        f"ranks, hidden 7168, inter 2048, top-8, {per}, bf16 "
-                        "activations; NCCL all-to-all dispatch and return",
+                        f"ranks (hot experts replicated), hidden 7168, inter 2048, top-8, {per}, "
+                        "bf16 activations; NCCL all-to-all dispatch and return",
             "n_gpus": world, "scaling": "weak" if weak else "strong", "tokens_per_step": T_all,
-            "experts_per_rank": n, **res}
+            **res}
 
 
 # ------------------------------------------------------------ CPU baseline --

@@ -210,19 +210,25 @@ MVLLM_API int mvllm_moe_route_dev(void *stream, const void *x, int x_dtype, int 
 /* ---- expert parallelism (one rank per GPU).  No single counterpart in the
  *      reference, which runs every expert on one host; these are the
  *      device steps of the sharded layer around the NCCL exchanges.
- *      Expert e lives on rank e % nranks as local expert e / nranks. ---- */
-/* Dispatch plan for this rank's T tokens (idx [T,K] device, global ids; ids
- * outside [0, E) ignored): pos[T, nranks] = row of token c in the
+ *      Placement: dest, lid (device int32 [E], both given or both NULL).
+ *      dest[e] = the rank that serves expert e, or -1 for a replicated
+ *      expert that every rank holds and serves for its own tokens;
+ *      lid[e] = e's local id on the rank that serves it.  NULL: strided,
+ *      expert e on rank e % nranks as local expert e / nranks.  dest
+ *      entries must lie in [-1, nranks). ---- */
+/* Dispatch plan for the T tokens of rank self_rank (idx [T,K] device, global
+ * ids; ids outside [0, E) ignored): pos[T, nranks] = row of token c in the
  * destination-major send buffer for rank d (tokens ascending within a rank),
- * or -1 when rank d owns none of c's experts; send_cnt[nranks] = rows per
+ * or -1 when rank d serves none of c's experts; send_cnt[nranks] = rows per
  * destination.  nranks <= 32. */
 MVLLM_API int mvllm_moe_ep_plan_dev(void *stream, const int *idx, int T, int K, int E, int nranks,
-                                    int *pos, int *send_cnt);
+                                    const int *dest, int self_rank, int *pos, int *send_cnt);
 /* Fills the send buffer from the plan: send_x[p] = x[c] (x_dtype rows of D,
- * D a multiple of 8), send_idx[p, k] = local id of idx[c, k] when rank d owns
- * it else -1, send_wt[p, k] = wt[c, k]. */
+ * D a multiple of 8), send_idx[p, k] = local id of idx[c, k] when rank d
+ * serves it else -1, send_wt[p, k] = wt[c, k]. */
 MVLLM_API int mvllm_moe_ep_pack_dev(void *stream, const void *x, int x_dtype, const int *idx,
                                     const float *wt, int T, int K, int D, int E, int nranks,
+                                    const int *dest, const int *lid, int self_rank,
                                     const int *pos, void *send_x, int *send_idx, float *send_wt);
 /* out[c] += back[pos[c, d]] for d = 0, 1, ... (f32 rows of D, D a multiple of 4):
  * the partial sums each rank returned, added in ascending rank order. */

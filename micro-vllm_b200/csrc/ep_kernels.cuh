@@ -1,9 +1,12 @@
 // ep_kernels.cuh -- expert-parallel dispatch and combine for the MoE layer
 // sharded over ranks (one GPU each).
 //
-// Expert e lives on rank e % nranks as that rank's local expert e / nranks
-// (strided placement: with Zipf-skewed routing it balances the ranks far
-// better than contiguous blocks).  A step on rank r:
+// Placement: by default expert e lives on rank e % nranks as that rank's
+// local expert e / nranks (strided: with Zipf-skewed routing it balances the
+// ranks far better than contiguous blocks).  A placement table may instead
+// give, per expert, its rank or -1 -- a replicated expert that every rank
+// holds and serves for its own tokens (hot experts stop concentrating load on
+// one rank) -- and its local id on the rank that serves it.  A step on rank r:
 //   plan     which of r's tokens each rank needs (a token goes to rank d once,
 //            however many of its experts d owns) and where each lands in the
 //            destination-major send buffer;
@@ -25,11 +28,24 @@
 
 namespace mvb {
 
+// The rank that serves expert e for a token of rank `self`, and its local id
+// there (dest == nullptr: strided placement).
+__device__ __forceinline__ int ep_dest(int e, int nranks, const int *dest, int self) {
+    if (!dest)
+        return e % nranks;
+    const int d = __ldg(dest + e);
+    return d < 0 ? self : d;
+}
+__device__ __forceinline__ int ep_local_id(int e, int nranks, const int *lid) {
+    return lid ? __ldg(lid + e) : e / nranks;
+}
+
 // One CTA: per destination rank a block scan over the tokens gives the
 // position of each sent token among those of that rank; a second pass adds the
 // destination offsets.  pos[c * nranks + d] = send-buffer row or -1.
 __global__ void ep_plan_kernel(const int *__restrict__ idx, int T, int K, int E, int nranks,
-                               int *__restrict__ pos, int *__restrict__ send_cnt) {
+                               const int *__restrict__ dest, int self, int *__restrict__ pos,
+                               int *__restrict__ send_cnt) {
     __shared__ int warp_sums[32];
     __shared__ int carry[32];
     __shared__ int off[33];
@@ -43,7 +59,7 @@ __global__ void ep_plan_kernel(const int *__restrict__ idx, int T, int K, int E,
             for (int k = 0; k < K; ++k) {
                 const int e = idx[static_cast<size_t>(c) * K + k];
                 if (e >= 0 && e < E)
-                    mask |= 1u << (e % nranks);
+                    mask |= 1u << ep_dest(e, nranks, dest, self);
             }
         for (int d = 0; d < nranks; ++d) {
             const int f = (mask >> d) & 1;
@@ -77,8 +93,10 @@ __global__ void ep_plan_kernel(const int *__restrict__ idx, int T, int K, int E,
 template <typename TX>
 __global__ void ep_pack_kernel(const TX *__restrict__ x, const int *__restrict__ idx,
                                const float *__restrict__ wt, int T, int K, int D, int E,
-                               int nranks, const int *__restrict__ pos, TX *__restrict__ send_x,
-                               int *__restrict__ send_idx, float *__restrict__ send_wt) {
+                               int nranks, const int *__restrict__ dest,
+                               const int *__restrict__ lid, int self, const int *__restrict__ pos,
+                               TX *__restrict__ send_x, int *__restrict__ send_idx,
+                               float *__restrict__ send_wt) {
     constexpr int VEC = 16 / sizeof(TX);
     for (int c = blockIdx.x; c < T; c += gridDim.x) {
         const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(c) * D);
@@ -91,8 +109,8 @@ __global__ void ep_pack_kernel(const TX *__restrict__ x, const int *__restrict__
                 dst[v] = src[v];
             for (int k = threadIdx.x; k < K; k += blockDim.x) {
                 const int e = idx[static_cast<size_t>(c) * K + k];
-                const bool mine = e >= 0 && e < E && e % nranks == d;
-                send_idx[static_cast<size_t>(p) * K + k] = mine ? e / nranks : -1;
+                const bool mine = e >= 0 && e < E && ep_dest(e, nranks, dest, self) == d;
+                send_idx[static_cast<size_t>(p) * K + k] = mine ? ep_local_id(e, nranks, lid) : -1;
                 send_wt[static_cast<size_t>(p) * K + k] = wt[static_cast<size_t>(c) * K + k];
             }
         }

@@ -1546,21 +1546,24 @@ int mvllm_moe_route_dev(void *stream, const void *x, int x_dtype, int T, int H,
 }
 
 // ------------------------------------------------------ expert parallelism --
-int mvllm_moe_ep_plan_dev(void *stream, const int *idx, int T, int K, int E, int nranks, int *pos,
-                          int *send_cnt) {
-    if (!idx || !pos || !send_cnt || T < 0 || K < 1 || E < 1 || nranks < 1 || nranks > 32)
+int mvllm_moe_ep_plan_dev(void *stream, const int *idx, int T, int K, int E, int nranks,
+                          const int *dest, int self_rank, int *pos, int *send_cnt) {
+    if (!idx || !pos || !send_cnt || T < 0 || K < 1 || E < 1 || nranks < 1 || nranks > 32 ||
+        self_rank < 0 || self_rank >= nranks)
         return fail(MVLLM_ERR_INVALID, "ep_plan_dev: invalid arguments");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    ep_plan_kernel<<<1, 1024, 0, st>>>(idx, T, K, E, nranks, pos, send_cnt);
+    ep_plan_kernel<<<1, 1024, 0, st>>>(idx, T, K, E, nranks, dest, self_rank, pos, send_cnt);
     CUDA_TRY(cudaGetLastError());
     return MVLLM_OK;
 }
 
 int mvllm_moe_ep_pack_dev(void *stream, const void *x, int x_dtype, const int *idx,
-                          const float *wt, int T, int K, int D, int E, int nranks, const int *pos,
-                          void *send_x, int *send_idx, float *send_wt) {
+                          const float *wt, int T, int K, int D, int E, int nranks, const int *dest,
+                          const int *lid, int self_rank, const int *pos, void *send_x,
+                          int *send_idx, float *send_wt) {
     if (!x || !idx || !wt || !pos || !send_x || !send_idx || !send_wt || T < 0 || K < 1 ||
-        D < 8 || D % 8 != 0 || E < 1 || nranks < 1 || nranks > 32 ||
+        D < 8 || D % 8 != 0 || E < 1 || nranks < 1 || nranks > 32 || self_rank < 0 ||
+        self_rank >= nranks || (!dest != !lid) ||
         (x_dtype != MVLLM_DTYPE_F32 && x_dtype != MVLLM_DTYPE_BF16) ||
         ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(send_x)) & 15u))
         return fail(MVLLM_ERR_INVALID, "ep_pack_dev: invalid arguments");
@@ -1570,13 +1573,12 @@ int mvllm_moe_ep_pack_dev(void *stream, const void *x, int x_dtype, const int *i
     const int blocks = std::min(T, 65535);
     if (x_dtype == MVLLM_DTYPE_BF16)
         ep_pack_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
-            static_cast<const __nv_bfloat16 *>(x), idx, wt, T, K, D, E, nranks, pos,
-            static_cast<__nv_bfloat16 *>(send_x), send_idx, send_wt);
+            static_cast<const __nv_bfloat16 *>(x), idx, wt, T, K, D, E, nranks, dest, lid,
+            self_rank, pos, static_cast<__nv_bfloat16 *>(send_x), send_idx, send_wt);
     else
-        ep_pack_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float *>(x), idx, wt, T, K,
-                                                       D, E, nranks, pos,
-                                                       static_cast<float *>(send_x), send_idx,
-                                                       send_wt);
+        ep_pack_kernel<float><<<blocks, 256, 0, st>>>(
+            static_cast<const float *>(x), idx, wt, T, K, D, E, nranks, dest, lid, self_rank, pos,
+            static_cast<float *>(send_x), send_idx, send_wt);
     CUDA_TRY(cudaGetLastError());
     return MVLLM_OK;
 }

@@ -1,8 +1,12 @@
 """Expert-parallel routed MoE layer: one rank per GPU, experts sharded.
 
-Expert e lives on rank e % nranks as that rank's local expert e // nranks
-(strided placement balances Zipf-skewed routing far better than contiguous
-blocks).  One layer step on rank r, for r's own tokens:
+By default expert e lives on rank e % nranks as that rank's local expert
+e // nranks (strided placement balances Zipf-skewed routing far better than
+contiguous blocks).  A `Placement` may also replicate hot experts on every
+rank: each rank then serves those experts for its own tokens, so a handful
+of very popular experts no longer pile their rows onto one rank
+(`balance_replicas` picks them from routing statistics).  One layer step on
+rank r, for r's own tokens:
 
   1. plan      which ranks need each token, and its row in the
                destination-major send buffer        (mvllm_moe_ep_plan_dev)
@@ -43,16 +47,87 @@ def local_id(e, nranks):
 
 
 def local_experts(rank, nranks, E):
-    """Global ids of the experts rank `rank` holds, in local-id order."""
+    """Global ids of the experts rank `rank` holds (strided), in local-id order."""
     return list(range(rank, E, nranks))
+
+
+class Placement:
+    """Which rank serves each expert, and under which local id.
+
+    Replicated experts come first in every rank's local table (local id j =
+    position in `replicated`), then the rank's strided own experts (e on rank
+    e % nranks, replicated ones left out).  dest[e] = serving rank, or -1 for
+    a replicated expert (the token's own rank serves it)."""
+
+    def __init__(self, E, nranks, replicated=()):
+        self.E, self.nranks = E, nranks
+        self.replicated = sorted({int(e) for e in replicated if 0 <= int(e) < E})
+        rep = set(self.replicated)
+        R = len(self.replicated)
+        self.dest = [-1 if e in rep else e % nranks for e in range(E)]
+        self.lid = [0] * E
+        for j, e in enumerate(self.replicated):
+            self.lid[e] = j
+        self._local = []
+        for r in range(nranks):
+            own = [e for e in range(r, E, nranks) if e not in rep]
+            for i, e in enumerate(own):
+                self.lid[e] = R + i
+            self._local.append(self.replicated + own)
+
+    @property
+    def strided(self):
+        return not self.replicated
+
+    def local_experts(self, rank):
+        """Global ids rank `rank` holds, in local-id order."""
+        return list(self._local[rank])
+
+    def serving_rank(self, e, token_rank):
+        d = self.dest[e]
+        return token_rank if d < 0 else d
+
+
+def rank_loads(load, placement):
+    """Routed rows each rank serves under `placement`, for per-expert row
+    counts `load` summed over ranks whose tokens are alike (a replicated
+    expert's rows split evenly over the ranks)."""
+    N = placement.nranks
+    per = [0.0] * N
+    for e, n in enumerate(load):
+        if placement.dest[e] < 0:
+            for r in range(N):
+                per[r] += n / N
+        else:
+            per[placement.dest[e]] += n
+    return per
+
+
+def balance_replicas(load, nranks, max_replicas, tol=0.05):
+    """Experts to replicate, hottest first, until no rank serves more than
+    (1 + tol) x the mean routed rows or `max_replicas` are taken."""
+    E = len(load)
+    mean = sum(load) / nranks
+    order = sorted(range(E), key=lambda e: (-load[e], e))
+    rep = []
+    while len(rep) < max_replicas:
+        if max(rank_loads(load, Placement(E, nranks, rep))) <= (1.0 + tol) * mean:
+            break
+        rep.append(order[len(rep)])
+    return rep
 
 
 class CudaOps:
     """Device steps of a rank through the sm_100a library."""
 
     def __init__(self, torch, E, K, D, I, fmt, act, act_a, act_b, local_tables, nranks,
-                 max_recv_rows):
+                 max_recv_rows, placement=None, rank=0):
         self.torch = torch
+        self.rank = rank
+        self.dest = self.lid = None
+        if placement is not None and not placement.strided:
+            self.dest = torch.tensor(placement.dest, dtype=torch.int32, device="cuda")
+            self.lid = torch.tensor(placement.lid, dtype=torch.int32, device="cuda")
         self.E, self.K, self.D, self.I, self.fmt = E, K, D, I, fmt
         self.act, self.act_a, self.act_b = act, act_a, act_b
         self.tables = local_tables
@@ -67,7 +142,7 @@ class CudaOps:
         T = idx.shape[0]
         pos = self.torch.empty((T, self.nranks), dtype=self.torch.int32, device=idx.device)
         cnt = self.torch.empty(self.nranks, dtype=self.torch.int32, device=idx.device)
-        moe.ep_plan_dev(idx, self.E, self.nranks, pos, cnt)
+        moe.ep_plan_dev(idx, self.E, self.nranks, pos, cnt, self.dest, self.rank)
         return pos, cnt
 
     def pack(self, x, idx, wt, pos, rows):
@@ -76,7 +151,8 @@ class CudaOps:
         send_idx = t.empty((rows, self.K), dtype=t.int32, device=x.device)
         send_wt = t.empty((rows, self.K), dtype=t.float32, device=x.device)
         if rows:
-            moe.ep_pack_dev(x, idx, wt, self.E, self.nranks, pos, send_x, send_idx, send_wt)
+            moe.ep_pack_dev(x, idx, wt, self.E, self.nranks, pos, send_x, send_idx, send_wt,
+                            self.dest, self.lid, self.rank)
         return send_x, send_idx, send_wt
 
     def compute(self, rx, ridx, rwt):

@@ -86,8 +86,9 @@ def lib():
             "mvllm_moe_profile_enable": (None, [i]),
             "mvllm_moe_profile_read": (i, [vp, vp, i]),
             "mvllm_moe_permute_dev_noalloc": (i, [vp, vp, vp, i, i, i, i] + [vp] * 6),
-            "mvllm_moe_ep_plan_dev": (i, [vp, vp, i, i, i, i, vp, vp]),
-            "mvllm_moe_ep_pack_dev": (i, [vp, vp, i, vp, vp, i, i, i, i, i, vp, vp, vp, vp]),
+            "mvllm_moe_ep_plan_dev": (i, [vp, vp, i, i, i, i, vp, i, vp, vp]),
+            "mvllm_moe_ep_pack_dev": (i, [vp, vp, i, vp, vp, i, i, i, i, i, vp, vp, i, vp, vp, vp,
+                                          vp]),
             "mvllm_moe_ep_combine_dev": (i, [vp, vp, vp, i, i, i, vp]),
             "mvllm_moe_topk_dev": (i, [vp, vp, vp, i, i, i, vp, vp]),
             "mvllm_moe_route_dev": (i, [vp, vp, i, i, i, vp, vp, i, i, vp, vp, vp, vp]),
@@ -284,20 +285,22 @@ def matmul_dev(fmt, y, x, w, scales, stream=None):
 
 
 # -------------------------------------------------------- expert parallelism --
-def ep_plan_dev(idx, E, nranks, pos, send_cnt, stream=None):
-    """pos [T, nranks] int32, send_cnt [nranks] int32 (device)."""
+def ep_plan_dev(idx, E, nranks, pos, send_cnt, dest=None, self_rank=0, stream=None):
+    """pos [T, nranks] int32, send_cnt [nranks] int32 (device).  dest: device
+    int32 [E] placement (rank, or -1 = replicated), None = strided."""
     T, K = idx.shape
-    _check(lib().mvllm_moe_ep_plan_dev(_stream(stream), _dp(idx), T, K, E, nranks, _dp(pos),
-                                       _dp(send_cnt)))
+    _check(lib().mvllm_moe_ep_plan_dev(_stream(stream), _dp(idx), T, K, E, nranks, _dp(dest),
+                                       self_rank, _dp(pos), _dp(send_cnt)))
 
 
-def ep_pack_dev(x, idx, wt, E, nranks, pos, send_x, send_idx, send_wt, stream=None):
+def ep_pack_dev(x, idx, wt, E, nranks, pos, send_x, send_idx, send_wt, dest=None, lid=None,
+                self_rank=0, stream=None):
     T, K = idx.shape
     D = x.shape[1]
     x_dtype = DTYPE_BF16 if str(x.dtype) == "torch.bfloat16" else DTYPE_F32
     _check(lib().mvllm_moe_ep_pack_dev(_stream(stream), _dp(x), x_dtype, _dp(idx), _dp(wt), T, K,
-                                       D, E, nranks, _dp(pos), _dp(send_x), _dp(send_idx),
-                                       _dp(send_wt)))
+                                       D, E, nranks, _dp(dest), _dp(lid), self_rank, _dp(pos),
+                                       _dp(send_x), _dp(send_idx), _dp(send_wt)))
 
 
 def ep_combine_dev(back, pos, out, stream=None):

@@ -11,12 +11,22 @@ from oracle import permute  # test infrastructure only
 
 
 class CpuOps:
-    def __init__(self, torch, codec, E, K, D, I, fmt, act, act_a, act_b, local_experts, nranks):
+    def __init__(self, torch, codec, E, K, D, I, fmt, act, act_a, act_b, local_experts, nranks,
+                 placement=None, rank=0):
         self.torch, self.codec = torch, codec
+        self.placement, self.rank = placement, rank
         self.E, self.K, self.D, self.I, self.fmt = E, K, D, I, fmt
         self.act, self.act_a, self.act_b = act, act_a, act_b
         self.local = local_experts  # [(gate, up, down)] of (packed, scales), local-id order
         self.nranks = nranks
+
+    def _serving(self, e):
+        if self.placement is None:
+            return e % self.nranks
+        return self.placement.serving_rank(e, self.rank)
+
+    def _lid(self, e):
+        return e // self.nranks if self.placement is None else self.placement.lid[e]
 
     def plan(self, idx):
         ids = idx.numpy()
@@ -25,7 +35,7 @@ class CpuOps:
         for c in range(T):
             for e in ids[c]:
                 if 0 <= e < self.E:
-                    need[c, e % self.nranks] = True
+                    need[c, self._serving(e)] = True
         cnt = need.sum(axis=0).astype(np.int32)
         off = np.concatenate([[0], np.cumsum(cnt)[:-1]])
         pos = np.full((T, self.nranks), -1, np.int32)
@@ -49,7 +59,8 @@ class CpuOps:
                 sx[p] = x[c]
                 for k in range(self.K):
                     e = int(ids[c, k])
-                    sidx[p, k] = e // self.nranks if (0 <= e < self.E and e % self.nranks == d) else -1
+                    mine = 0 <= e < self.E and self._serving(e) == d
+                    sidx[p, k] = self._lid(e) if mine else -1
                 swt[p] = wt[c]
         return sx, sidx, swt
 

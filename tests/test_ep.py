@@ -33,12 +33,50 @@ def layer(port, T, seed=41):
     return c, want
 
 
-def rank_ops(port, c, rank, nranks):
+def rank_ops(port, c, rank, nranks, placement=None):
     from ep_cpu_ops import CpuOps
     import ep
-    local = [c["experts"][e] for e in ep.local_experts(rank, nranks, CASE["E"])]
+    ids = (ep.local_experts(rank, nranks, CASE["E"]) if placement is None
+           else placement.local_experts(rank))
+    local = [c["experts"][e] for e in ids]
     return CpuOps(torch, port, CASE["E"], CASE["K"], CASE["D"], CASE["I"], CASE["fmt"],
-                  CASE["act"], CASE["act_a"], CASE["act_b"], local, nranks)
+                  CASE["act"], CASE["act_a"], CASE["act_b"], local, nranks, placement, rank)
+
+
+def test_ep_emulated_replicated_experts(port):
+    """Experts 1 and 4 on every rank (each rank serves them for its own
+    tokens), the rest strided: same layer output."""
+    import ep
+    N, T_loc = 3, 7
+    c, want = layer(port, N * T_loc, seed=43)
+    pl = ep.Placement(CASE["E"], N, replicated=[4, 1])
+    assert pl.replicated == [1, 4] and pl.dest == [0, -1, 2, 0, -1, 2]
+    assert pl.local_experts(0) == [1, 4, 0, 3] and pl.local_experts(1) == [1, 4]
+    assert [pl.lid[e] for e in range(6)] == [2, 0, 2, 3, 1, 3]
+    layers, xs, idxs, wts, outs = [], [], [], [], []
+    for r in range(N):
+        sl = slice(r * T_loc, (r + 1) * T_loc)
+        layers.append(ep.EPLayer(rank_ops(port, c, r, N, pl), r, N, CASE["D"], CASE["K"]))
+        xs.append(torch.from_numpy(np.ascontiguousarray(c["x"][sl])))
+        idxs.append(torch.from_numpy(np.ascontiguousarray(c["idx"][sl])))
+        wts.append(torch.from_numpy(np.ascontiguousarray(c["wt"][sl])))
+        outs.append(torch.zeros((T_loc, CASE["D"])))
+    ep.emulate_step(layers, xs, idxs, wts, outs, torch)
+    assert_close(torch.cat(outs).numpy(), want, "emulated 3-rank EP, replicated experts")
+
+
+def test_balance_replicas():
+    import ep
+    # one expert with half of all rows: replicating it alone balances 4 ranks
+    load = [400] + [25] * 16
+    rep = ep.balance_replicas(load, 4, max_replicas=8)
+    assert rep == [0]
+    per = ep.rank_loads(load, ep.Placement(17, 4, rep))
+    assert max(per) <= 1.05 * sum(load) / 4
+    # uniform loads need no replica; the cap is honoured
+    assert ep.balance_replicas([10] * 16, 4, max_replicas=8) == []
+    zipf = [1000.0 / (i + 1) ** 1.1 for i in range(64)]
+    assert len(ep.balance_replicas(zipf, 8, max_replicas=3)) == 3
 
 
 def test_ep_emulated_three_ranks(port):

@@ -90,6 +90,39 @@ def test_ep_emulated_four_ranks_gpu(moe, port):
     assert torch.equal(one, direct)
 
 
+def test_ep_emulated_replicated_experts_gpu(moe, port):
+    """Experts 1 and 5 replicated on every rank (served locally for each
+    rank's own tokens), the rest strided: the layer output is unchanged."""
+    import ep
+    N, T_loc = 4, 40
+    c = cases.layer_case(port, 53, CASE["D"], CASE["I"], CASE["E"], CASE["K"], N * T_loc,
+                         CASE["fmt"], CASE["act"], CASE["act_a"], CASE["act_b"], bf16_x=True)
+    _, want = cases.run_block(port, c)
+    pl = ep.Placement(CASE["E"], N, replicated=[5, 1])
+    layers, xs, idxs, wts, outs, keep = [], [], [], [], [], []
+    for r in range(N):
+        tabs, k = tables_of([c["experts"][e] for e in pl.local_experts(r)])
+        keep.append(k)
+        ops = ep.CudaOps(torch, CASE["E"], CASE["K"], CASE["D"], CASE["I"], CASE["fmt"],
+                         CASE["act"], CASE["act_a"], CASE["act_b"], tabs, N, N * T_loc,
+                         placement=pl, rank=r)
+        layers.append(ep.EPLayer(ops, r, N, CASE["D"], CASE["K"]))
+        sl = slice(r * T_loc, (r + 1) * T_loc)
+        xs.append(dev(c["x"][sl]).to(torch.bfloat16))
+        idxs.append(dev(c["idx"][sl]))
+        wts.append(dev(c["wt"][sl]))
+        outs.append(torch.zeros((T_loc, CASE["D"]), device="cuda"))
+    ep.emulate_step(layers, xs, idxs, wts, outs, torch)
+    torch.cuda.synchronize()
+    assert_close(torch.cat(outs).cpu().numpy(), want, "emulated 4-rank EP, replicated experts")
+    # rank 2's plan: a token goes to itself for experts 1/5, to e % 4 otherwise
+    pos, cnt = layers[2].ops.plan(idxs[2])
+    P, idx = pos.cpu().numpy(), c["idx"][2 * T_loc:3 * T_loc]
+    for t in range(T_loc):
+        need = {2 if e in (1, 5) else e % N for e in idx[t] if 0 <= e < CASE["E"]}
+        assert {d for d in range(N) if P[t, d] >= 0} == need
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
 def test_ep_nccl_two_gpus():
