@@ -49,7 +49,7 @@ def parse():
                     help="skip the config[3] prefill measurement")
     ap.add_argument("--prefill-steps", type=int, default=10)
     ap.add_argument("--no-ep", action="store_true", help="skip the config[4] expert-parallel leg")
-    ap.add_argument("--ep-steps", type=int, default=5)
+    ap.add_argument("--ep-steps", type=int, default=20)
     ap.add_argument("--prefill-tokens", type=int, default=4096,
                     help="config[3]: 4096; fewer only to size a profiler capture")
     ap.add_argument("--experts", type=int, default=256,

@@ -234,6 +234,26 @@ MVLLM_API int mvllm_moe_ep_pack_dev(void *stream, const void *x, int x_dtype, co
  * the partial sums each rank returned, added in ascending rank order. */
 MVLLM_API int mvllm_moe_ep_combine_dev(void *stream, const float *back, const int *pos, int T,
                                        int nranks, int D, float *out);
+/* The same from partial rows in the form mvllm_moe_layer_partial_dev writes
+ * (pitch 2*D + 16 bytes: D f16 values, then the row's f32 power-of-two scale):
+ * out[c] += f16 value x scale, ranks ascending.  D a multiple of 8. */
+MVLLM_API int mvllm_moe_ep_combine16_dev(void *stream, const void *back16, const int *pos,
+                                         int T, int nranks, int D, float *out);
+/* mvllm_moe_layer_dev whose per-token result goes to a partial row for the
+ * expert-parallel return instead of being added into f32 `out`: row c of
+ * out16 (pitch 2*D + 16 bytes, 16-byte aligned) holds the D values of the
+ * token's ordered sum (from zero) as f16 of v / 2^s and, in its 16-byte tail,
+ * the f32 2^s, chosen per row so that the largest |v| / 2^s lies in
+ * [2^14, 2^15).  Relative error at most 2^-11 per element; half the bytes of
+ * f32 rows.  D a multiple of 8, at most 32768; same workspace as layer_dev. */
+MVLLM_API int mvllm_moe_layer_partial_dev(void *stream, int T, int K, int E, int n_shared, int D,
+                                          int Iinter, int fmt, const int *idx, const float *wt,
+                                          const void *x, int x_dtype, const void *const *g,
+                                          const void *const *u, const void *const *d,
+                                          const void *const *gs, const void *const *us,
+                                          const void *const *ds, void *out16, int act,
+                                          float act_a, float act_b, void *workspace,
+                                          size_t workspace_bytes);
 
 /* Per-phase device time of the device-pointer entries, from CUDA events
  * recorded on the launch stream after each phase while enabled (the role of

@@ -444,6 +444,77 @@ __global__ void combine_tokens_kernel(float *__restrict__ out, const float *__re
     }
 }
 
+// Partial-sum rows for the expert-parallel return: the sums of
+// combine_tokens_kernel taken from zero, stored as f16 of v / 2^s with one
+// power-of-two scale per row (the row's largest |v| / 2^s lands in
+// [2^14, 2^15), so no value overflows), 2^s as an f32 in the row's 16-byte
+// tail.  Row pitch 2*D + 16 bytes; relative error at most 2^-11 per element
+// (f16 rounding), half the bytes of f32 rows.  One CTA per token at a time,
+// the f32 row staged in shared memory (D floats) for the row maximum.
+__global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const float *__restrict__ y,
+                                          const float *__restrict__ rw,
+                                          const int *__restrict__ tok_pos, int T, int KK, int D) {
+    extern __shared__ float4 srow[];
+    __shared__ float wmax[32];
+    const int n4 = D / 4;
+    const size_t pitch = 2 * static_cast<size_t>(D) + 16;
+    for (int c = blockIdx.x; c < T; c += gridDim.x) {
+        int pos[17];
+        int n = 0;
+        for (int t = 0; t < KK && n < 17; ++t) {
+            const int p = tok_pos[static_cast<size_t>(c) * KK + t];
+            if (p >= 0) {
+                int j = n++;
+                while (j > 0 && pos[j - 1] > p) {
+                    pos[j] = pos[j - 1];
+                    --j;
+                }
+                pos[j] = p;
+            }
+        }
+        float m = 0.f;
+        for (int v = threadIdx.x; v < n4; v += blockDim.x) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int j = 0; j < n; ++j) {
+                const float w = rw[pos[j]];
+                const float4 a = __ldcs(reinterpret_cast<const float4 *>(
+                    y + static_cast<size_t>(pos[j]) * D + 4 * static_cast<size_t>(v)));
+                acc.x = __fadd_rn(acc.x, __fmul_rn(w, a.x));
+                acc.y = __fadd_rn(acc.y, __fmul_rn(w, a.y));
+                acc.z = __fadd_rn(acc.z, __fmul_rn(w, a.z));
+                acc.w = __fadd_rn(acc.w, __fmul_rn(w, a.w));
+            }
+            srow[v] = acc;
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(acc.x), fabsf(acc.y)), fmaxf(fabsf(acc.z), fabsf(acc.w))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((threadIdx.x & 31) == 0)
+            wmax[threadIdx.x >> 5] = m;
+        __syncthreads();
+        float M = 0.f;
+        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w)
+            M = fmaxf(M, wmax[w]);
+        // 2^s: s = floor(log2 M) - 14 for a finite non-zero maximum, else 0
+        // (zeros stay zeros; inf / NaN pass through the f16 conversion).
+        const int s = (M > 0.f && M <= 3.4e38f) ? ilogbf(M) - 14 : 0;
+        const float inv = ldexpf(1.f, -s);
+        uint8_t *row = out16 + static_cast<size_t>(c) * pitch;
+        for (int v = threadIdx.x; v < n4; v += blockDim.x) {
+            const float4 a = srow[v];
+            __half2 h[2] = {__floats2half2_rn(a.x * inv, a.y * inv),
+                            __floats2half2_rn(a.z * inv, a.w * inv)};
+            *reinterpret_cast<uint2 *>(row + 8 * static_cast<size_t>(v)) =
+                *reinterpret_cast<const uint2 *>(h);
+        }
+        if (threadIdx.x == 0)
+            *reinterpret_cast<float4 *>(row + 2 * static_cast<size_t>(D)) =
+                make_float4(ldexpf(1.f, s), 0.f, 0.f, 0.f);
+        __syncthreads();
+    }
+}
+
 // Ordered combine, moe_block form: CSR of destination rows (row ids ascending
 // within each destination), scatter order of metal_ops.cpp:328-339.
 __global__ void combine_csr_kernel(float *__restrict__ out, const float *__restrict__ y,

@@ -139,4 +139,32 @@ __global__ void ep_combine_kernel(const float *__restrict__ back, const int *__r
     }
 }
 
+// out[c] += sum over ranks d ascending of the partial row back16[pos[c, d]]:
+// f16 values times the row's power-of-two scale (exact in f32), then f32 adds.
+__global__ void ep_combine16_kernel(const uint8_t *__restrict__ back16, const int *__restrict__ pos,
+                                    int T, int nranks, int D, float *__restrict__ out) {
+    const int n4 = D / 4;
+    const size_t pitch = 2 * static_cast<size_t>(D) + 16;
+    for (int c = blockIdx.y; c < T; c += gridDim.y) {
+        for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < n4; v += gridDim.x * blockDim.x) {
+            float4 acc = reinterpret_cast<const float4 *>(out + static_cast<size_t>(c) * D)[v];
+            for (int d = 0; d < nranks; ++d) {
+                const int p = pos[static_cast<size_t>(c) * nranks + d];
+                if (p < 0)
+                    continue;
+                const uint8_t *row = back16 + static_cast<size_t>(p) * pitch;
+                const float sc = *reinterpret_cast<const float *>(row + 2 * static_cast<size_t>(D));
+                const uint2 u = *reinterpret_cast<const uint2 *>(row + 8 * static_cast<size_t>(v));
+                const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+                const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+                acc.x = __fadd_rn(acc.x, __fmul_rn(lo.x, sc));
+                acc.y = __fadd_rn(acc.y, __fmul_rn(lo.y, sc));
+                acc.z = __fadd_rn(acc.z, __fmul_rn(hi.x, sc));
+                acc.w = __fadd_rn(acc.w, __fmul_rn(hi.y, sc));
+            }
+            reinterpret_cast<float4 *>(out + static_cast<size_t>(c) * D)[v] = acc;
+        }
+    }
+}
+
 } // namespace mvb

@@ -1311,7 +1311,7 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
                           int Iinter, int fmt, const int *idx, const float *wt, const void *x,
                           int x_dtype, const Tables &tb, float *out, int act, float act_a,
                           float act_b, const LayerWs &l, bool allow_tc = true,
-                          const LayerHooks *hooks = nullptr) {
+                          const LayerHooks *hooks = nullptr, uint8_t *out16 = nullptr) {
     const bool fast = fast_path_ok(fmt, D, Iinter);
     const int EE = E + n_shared, KK = K + n_shared, R = T * KK;
     CUDA_TRY(cudaMemsetAsync(l.run.err, 0, sizeof(int), st));
@@ -1354,8 +1354,17 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
     if (hooks && hooks->before_combine)
         if (int rc = hooks->before_combine())
             return rc;
-    dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
-    combine_tokens_kernel<<<grid, 256, 0, st>>>(out, w.y, l.rw, l.tok_pos, T, KK, D);
+    if (out16) {
+        const size_t sm = size_t(D) * 4;
+        if (sm > 48 * 1024)
+            CUDA_TRY(cudaFuncSetAttribute(combine_tokens_f16_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
+        combine_tokens_f16_kernel<<<std::min(T, 8 * sms), 256, sm, st>>>(out16, w.y, l.rw,
+                                                                         l.tok_pos, T, KK, D);
+    } else {
+        dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
+        combine_tokens_kernel<<<grid, 256, 0, st>>>(out, w.y, l.rw, l.tok_pos, T, KK, D);
+    }
     CUDA_TRY(cudaGetLastError());
     prof_mark(st, kPhCombine);
     return MVLLM_OK;
@@ -1390,6 +1399,41 @@ int mvllm_moe_layer_dev(void *stream, int T, int K, int E, int n_shared, int D, 
     Tables tb{g, u, d, gs, us, ds};
     return layer_dev_impl(static_cast<cudaStream_t>(stream), sms, T, K, E, n_shared, D, Iinter,
                           fmt, idx, wt, x, x_dtype, tb, out, act, act_a, act_b, l);
+}
+
+int mvllm_moe_layer_partial_dev(void *stream, int T, int K, int E, int n_shared, int D,
+                                int Iinter, int fmt, const int *idx, const float *wt,
+                                const void *x, int x_dtype, const void *const *g,
+                                const void *const *u, const void *const *d,
+                                const void *const *gs, const void *const *us,
+                                const void *const *ds, void *out16, int act, float act_a,
+                                float act_b, void *workspace, size_t workspace_bytes) {
+    if (T < 1 || K < 1 || K > 16 || E < 1 || n_shared < 0 || n_shared > 1 || D < 8 ||
+        Iinter < 1 || (fmt != 0 && fmt != 4 && fmt != 7) || !idx || !wt || !x || !g || !u || !d ||
+        !out16 || (fmt != MVLLM_FMT_F32 && (!gs || !us || !ds)) || D % 8 != 0 ||
+        D > 32768 || (reinterpret_cast<uintptr_t>(out16) & 15u))
+        return fail(MVLLM_ERR_INVALID, "layer_partial_dev: invalid arguments");
+    if (x_dtype != MVLLM_DTYPE_F32 && x_dtype != MVLLM_DTYPE_BF16)
+        return fail(MVLLM_ERR_INVALID, "layer_partial_dev: unknown x dtype");
+    const size_t need = mvllm_moe_layer_workspace(T, K, E, n_shared, D, Iinter, fmt);
+    if (!workspace || workspace_bytes < need)
+        return fail(MVLLM_ERR_WORKSPACE, "layer_partial_dev: workspace %zu < %zu",
+                    workspace_bytes, need);
+    Context &c = ctx();
+    int sms;
+    {
+        std::lock_guard<std::mutex> lk(c.mu);
+        if (int rc = ensure_current(c))
+            return rc;
+        sms = c.sms;
+    }
+    Carve cv(workspace, workspace_bytes);
+    LayerWs l{};
+    carve_layer(cv, l, T, K, E, n_shared, D, Iinter, fast_path_ok(fmt, D, Iinter));
+    Tables tb{g, u, d, gs, us, ds};
+    return layer_dev_impl(static_cast<cudaStream_t>(stream), sms, T, K, E, n_shared, D, Iinter,
+                          fmt, idx, wt, x, x_dtype, tb, nullptr, act, act_a, act_b, l, true,
+                          nullptr, static_cast<uint8_t *>(out16));
 }
 
 static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter, int fmt,
@@ -1579,6 +1623,22 @@ int mvllm_moe_ep_pack_dev(void *stream, const void *x, int x_dtype, const int *i
         ep_pack_kernel<float><<<blocks, 256, 0, st>>>(
             static_cast<const float *>(x), idx, wt, T, K, D, E, nranks, dest, lid, self_rank, pos,
             static_cast<float *>(send_x), send_idx, send_wt);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+int mvllm_moe_ep_combine16_dev(void *stream, const void *back16, const int *pos, int T,
+                               int nranks, int D, float *out) {
+    if (!pos || !out || T < 0 || nranks < 1 || nranks > 32 || D < 8 || D % 8 != 0 ||
+        (!back16 && T > 0) ||
+        ((reinterpret_cast<uintptr_t>(back16) | reinterpret_cast<uintptr_t>(out)) & 15u))
+        return fail(MVLLM_ERR_INVALID, "ep_combine16_dev: invalid arguments");
+    if (T == 0)
+        return MVLLM_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
+    ep_combine16_kernel<<<grid, 256, 0, st>>>(static_cast<const uint8_t *>(back16), pos, T,
+                                               nranks, D, out);
     CUDA_TRY(cudaGetLastError());
     return MVLLM_OK;
 }

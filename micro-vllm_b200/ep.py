@@ -18,7 +18,8 @@ rank r, for r's own tokens:
   5. compute   the received rows through r's local experts: the routed layer
                on device (mvllm_moe_layer_dev) with E = r's expert count;
                slots marked -1 are skipped by its permutation
-  6. return    all-to-all of the f32 partial sums back to the token owners
+  6. return    all-to-all of the partial sums back to the token owners (f16
+               rows with a power-of-two scale per row; f32 for one rank)
   7. combine   out[c] += partials of token c in ascending rank order
                                                      (mvllm_moe_ep_combine_dev)
 
@@ -121,9 +122,13 @@ class CudaOps:
     """Device steps of a rank through the sm_100a library."""
 
     def __init__(self, torch, E, K, D, I, fmt, act, act_a, act_b, local_tables, nranks,
-                 max_recv_rows, placement=None, rank=0):
+                 max_recv_rows, placement=None, rank=0, partial16=None):
         self.torch = torch
         self.rank = rank
+        # Return the partial sums as f16 rows with a power-of-two scale per row
+        # (half the bytes of f32 over NVLink, relative error <= 2^-11); one
+        # rank keeps f32, so it matches the single-GPU layer bit for bit.
+        self.partial16 = (nranks > 1) if partial16 is None else partial16
         self.dest = self.lid = None
         if placement is not None and not placement.strided:
             self.dest = torch.tensor(placement.dest, dtype=torch.int32, device="cuda")
@@ -157,16 +162,29 @@ class CudaOps:
 
     def compute(self, rx, ridx, rwt):
         R = rx.shape[0]
-        part = self.torch.zeros((R, self.D), dtype=self.torch.float32, device=rx.device)
+        if R > self.max_recv_rows:
+            raise ValueError(f"received {R} rows, above the {self.max_recv_rows} sized for")
+        t = self.torch
+        if self.partial16:
+            part = t.empty((R, moe.partial_row_bytes(self.D)), dtype=t.uint8, device=rx.device)
+            if R and self.E_local:
+                moe.layer_partial_dev(R, self.K, self.E_local, 0, self.D, self.I, self.fmt, ridx,
+                                      rwt, rx, self.tables, part, self.act, self.act_a,
+                                      self.act_b, self.ws)
+            elif R:
+                part.zero_()
+            return part
+        part = t.zeros((R, self.D), dtype=t.float32, device=rx.device)
         if R and self.E_local:
-            if R > self.max_recv_rows:
-                raise ValueError(f"received {R} rows, above the {self.max_recv_rows} sized for")
             moe.layer_dev(R, self.K, self.E_local, 0, self.D, self.I, self.fmt, ridx, rwt, rx,
                           self.tables, part, self.act, self.act_a, self.act_b, self.ws)
         return part
 
     def combine(self, back, pos, out):
-        moe.ep_combine_dev(back, pos, out)
+        if self.partial16:
+            moe.ep_combine16_dev(back, pos, out)
+        else:
+            moe.ep_combine_dev(back, pos, out)
 
 
 class EPLayer:
@@ -216,7 +234,7 @@ class EPLayer:
         mark()
         part = self.ops.compute(rx, ridx, rwt)
         mark()
-        back = t.empty((sum(sc), self.D), dtype=t.float32, device=x.device)
+        back = t.empty((sum(sc),) + tuple(part.shape[1:]), dtype=part.dtype, device=x.device)
         dist.all_to_all_single(back, part, sc, rc, group=group)
         mark()
         self.ops.combine(back, pos, out)

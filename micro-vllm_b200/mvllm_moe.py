@@ -38,6 +38,7 @@ C_SYMBOLS = (
     "mvllm_matmul_dev", "mvllm_moe_profile_enable", "mvllm_moe_profile_read",
     "mvllm_moe_permute_dev_noalloc", "mvllm_moe_ep_plan_dev", "mvllm_moe_ep_pack_dev",
     "mvllm_moe_ep_combine_dev", "mvllm_moe_topk_dev", "mvllm_moe_route_dev",
+    "mvllm_moe_ep_combine16_dev", "mvllm_moe_layer_partial_dev",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -90,6 +91,9 @@ def lib():
             "mvllm_moe_ep_pack_dev": (i, [vp, vp, i, vp, vp, i, i, i, i, i, vp, vp, i, vp, vp, vp,
                                           vp]),
             "mvllm_moe_ep_combine_dev": (i, [vp, vp, vp, i, i, i, vp]),
+            "mvllm_moe_ep_combine16_dev": (i, [vp, vp, vp, i, i, i, vp]),
+            "mvllm_moe_layer_partial_dev": (i, [vp] + [i] * 7 + [vp, vp, vp, i] + [vp] * 6 +
+                                            [vp, i, f, f, vp, sz]),
             "mvllm_moe_topk_dev": (i, [vp, vp, vp, i, i, i, vp, vp]),
             "mvllm_moe_route_dev": (i, [vp, vp, i, i, i, vp, vp, i, i, vp, vp, vp, vp]),
         }
@@ -239,6 +243,29 @@ def layer_dev(T, K, E, n_shared, D, Iinter, fmt, idx, wt, x, tables, out, act, a
                                      workspace.numel() * workspace.element_size()))
 
 
+def partial_row_bytes(D) -> int:
+    """Pitch of a partial row (mvllm_moe_layer_partial_dev): D f16 + 16-byte tail."""
+    return 2 * D + 16
+
+
+def layer_partial_dev(T, K, E, n_shared, D, Iinter, fmt, idx, wt, x, tables, out16, act, act_a,
+                      act_b, workspace, stream=None):
+    """The routed layer into partial rows: ``out16`` is a uint8 CUDA tensor of
+    [T, partial_row_bytes(D)] (see decode_partial_rows)."""
+    x_dtype = DTYPE_BF16 if str(x.dtype) == "torch.bfloat16" else DTYPE_F32
+    _check(lib().mvllm_moe_layer_partial_dev(
+        _stream(stream), T, K, E, n_shared, D, Iinter, fmt, _dp(idx), _dp(wt), _dp(x), x_dtype,
+        *[_dp(t) for t in tables], _dp(out16), act, act_a, act_b, _dp(workspace),
+        workspace.numel() * workspace.element_size()))
+
+
+def decode_partial_rows(torch, rows, D):
+    """f32 values of partial rows (uint8 [R, 2*D + 16]) -- for checks and tests."""
+    h = rows[:, :2 * D].contiguous().view(torch.float16).float()
+    sc = rows[:, 2 * D:2 * D + 4].contiguous().view(torch.float32)
+    return h * sc
+
+
 def block_dev_workspace_bytes(nb, D, Iinter, fmt, rows_cap, x_rows, S) -> int:
     return lib().mvllm_moe_block_dev_workspace(nb, D, Iinter, fmt, rows_cap, x_rows, S)
 
@@ -308,6 +335,13 @@ def ep_combine_dev(back, pos, out, stream=None):
     D = out.shape[1]
     _check(lib().mvllm_moe_ep_combine_dev(_stream(stream), _dp(back), _dp(pos), T, nranks, D,
                                           _dp(out)))
+
+
+def ep_combine16_dev(back16, pos, out, stream=None):
+    T, nranks = pos.shape
+    D = out.shape[1]
+    _check(lib().mvllm_moe_ep_combine16_dev(_stream(stream), _dp(back16), _dp(pos), T, nranks, D,
+                                            _dp(out)))
 
 
 # ------------------------------------------------------------------ routing --

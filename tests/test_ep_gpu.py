@@ -123,6 +123,40 @@ def test_ep_emulated_replicated_experts_gpu(moe, port):
         assert {d for d in range(N) if P[t, d] >= 0} == need
 
 
+def test_layer_partial_rows(moe, port):
+    """mvllm_moe_layer_partial_dev: each row is the f32 layer result rounded
+    once to f16 after a power-of-two scale that puts the row maximum in
+    [2^14, 2^15); tokens without a slot give zero rows."""
+    T = 48
+    c = cases.layer_case(port, 57, CASE["D"], CASE["I"], CASE["E"], CASE["K"], T, CASE["fmt"],
+                         CASE["act"], CASE["act_a"], CASE["act_b"], bf16_x=True)
+    idx = c["idx"].copy()
+    idx[5] = -1  # a token routed nowhere
+    tabs, keep = tables_of(c["experts"])
+    ws = torch.empty(moe.layer_workspace_bytes(T, CASE["K"], CASE["E"], 0, CASE["D"], CASE["I"],
+                                               CASE["fmt"]), dtype=torch.uint8, device="cuda")
+    args = (T, CASE["K"], CASE["E"], 0, CASE["D"], CASE["I"], CASE["fmt"], dev(idx), dev(c["wt"]),
+            dev(c["x"]).to(torch.bfloat16), tabs)
+    ref = torch.zeros((T, CASE["D"]), device="cuda")
+    moe.layer_dev(*args, ref, CASE["act"], CASE["act_a"], CASE["act_b"], ws)
+    rows = torch.full((T, moe.partial_row_bytes(CASE["D"])), 0xAB, dtype=torch.uint8,
+                      device="cuda")
+    moe.layer_partial_dev(*args, rows, CASE["act"], CASE["act_a"], CASE["act_b"], ws)
+    torch.cuda.synchronize()
+    got = moe.decode_partial_rows(torch, rows, CASE["D"])
+    sc = rows[:, 2 * CASE["D"]:2 * CASE["D"] + 4].contiguous().view(torch.float32).flatten()
+    assert torch.all(got[5] == 0) and float(sc[5]) == 1.0
+    m = ref.abs().amax(dim=1)
+    live = m > 0
+    q = (m[live] / sc[live]).cpu().numpy()
+    assert np.all(q >= 2.0 ** 14) and np.all(q < 2.0 ** 15)
+    assert np.all(np.log2(sc.cpu().numpy()) == np.round(np.log2(sc.cpu().numpy())))
+    # one f16 rounding of v / 2^s: |err| <= 2^-11 |v| (normal range) or half an f16 ulp
+    err = (got - ref).abs()
+    bound = torch.maximum(ref.abs() * 2.0 ** -11, sc[:, None] * 2.0 ** -25)
+    assert torch.all(err <= bound), float((err - bound).max())
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
 def test_ep_nccl_two_gpus():
