@@ -98,6 +98,32 @@ MVLLM_API int mvllm_moe_cache_unregister(const void *host);
 MVLLM_API void mvllm_moe_cache_clear(void);
 MVLLM_API size_t mvllm_moe_cache_bytes(void);
 
+/* ---- device expert tier: the VRAM level above an ExpertStore
+ *      (src/store/expert_store.hpp:59-175, expert_store.cpp:273-405).
+ *      A budget of equal VRAM slots holds copies of bound host blobs, least
+ *      recently used out first.  mvllm_moe_block finds its weight arrays in
+ *      bound blobs: resident ones are read from their slot; cold ones are
+ *      copied into a slot on a second stream while the call's resident
+ *      experts compute, then run.  Explicit cache_register ranges take
+ *      precedence; arrays in no bound blob are uploaded for the call. ---- */
+/* budget_bytes / slot_bytes slots (slot_bytes rounded up to 256); a budget
+ * below one slot turns the tier off.  Drops every residency (bindings stay). */
+MVLLM_API int mvllm_moe_tier_configure(size_t budget_bytes, size_t slot_bytes);
+/* Binds a host blob (an ExpertStore slot: start, bytes, generation).  A new
+ * generation or size for the same start drops the stale device copy; a blob
+ * overlapping an older binding replaces it.  No copy is made until a call
+ * uses the blob.  Blobs larger than a slot stay per-call uploads. */
+MVLLM_API int mvllm_moe_expert_bind(const void *host_blob, size_t bytes, uint64_t generation);
+MVLLM_API int mvllm_moe_expert_unbind(const void *host_blob);
+/* Counters since init: blob acquisitions that found the blob resident
+ * (hits), that copied it in (misses), slots taken from another blob
+ * (evictions), bytes copied in, acquisitions that found no slot (overflow:
+ * every slot held by a blob the call uses, or the blob too large); and the
+ * bytes now resident. */
+MVLLM_API void mvllm_moe_tier_stats(uint64_t *hits, uint64_t *misses, uint64_t *evictions,
+                                    uint64_t *bytes_in, uint64_t *overflow,
+                                    size_t *resident_bytes);
+
 /* ---- device-pointer entries (stream-ordered, no host sync, no allocation:
  *      the caller passes a workspace of at least the *_workspace size) ---- */
 

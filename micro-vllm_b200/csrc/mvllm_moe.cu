@@ -8,6 +8,7 @@
 #include "tc_ffn.cuh"
 #include "ep_kernels.cuh"
 #include "route_kernels.cuh"
+#include "expert_tier.hpp"
 
 #include <cudaTypedefs.h>
 
@@ -53,6 +54,11 @@ struct Context {
     size_t pinned_bytes = 0;
     std::map<uintptr_t, CacheEntry> cache; // host start -> device copy
     size_t cache_bytes = 0;
+    // Device expert tier: bound host blobs, streamed into equal VRAM slots.
+    TierPolicy tier;
+    void *tier_arena = nullptr;
+    cudaStream_t copy_stream = nullptr; // stream-ins of cold blobs
+    cudaEvent_t copy_done = nullptr;
     uint64_t calls = 0, experts = 0, rows = 0;
     double h2d_ms = 0, kernel_ms = 0, d2h_ms = 0;
 };
@@ -634,6 +640,8 @@ int init_locked(Context &c, int device) {
         return fail(MVLLM_ERR_UNSUPPORTED, "device %d is sm_%d%d, this build targets sm_100a",
                     device, prop.major, prop.minor);
     CUDA_TRY(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+    CUDA_TRY(cudaStreamCreateWithFlags(&c.copy_stream, cudaStreamNonBlocking));
+    CUDA_TRY(cudaEventCreateWithFlags(&c.copy_done, cudaEventDisableTiming));
     for (auto &e : c.ev)
         CUDA_TRY(cudaEventCreate(&e));
     c.sms = prop.multiProcessorCount;
@@ -674,14 +682,50 @@ struct Resolver {
         return nullptr;
     }
 
+    // Blobs of the device tier this call copies into their slots (issued on
+    // the copy stream before the call's second batch of experts).
+    std::vector<TierEntry *> stream_in;
+    bool tier_miss = false; // the array lies in a blob being streamed in
+
+    // Through the device tier: a resident blob's slot, or a slot the blob is
+    // streamed into (noted in stream_in), or nullptr (not bound, or no slot).
+    void *tiered(const void *host, size_t len) {
+        tier_miss = false;
+        if (!c.tier_arena)
+            return nullptr;
+        TierEntry *e = c.tier.find(reinterpret_cast<uintptr_t>(host), len);
+        if (!e)
+            return nullptr;
+        bool copy = false;
+        const int slot = c.tier.acquire(*e, &copy);
+        if (slot < 0)
+            return nullptr;
+        if (copy)
+            stream_in.push_back(e);
+        for (TierEntry *s : stream_in)
+            if (s == e)
+                tier_miss = true;
+        return static_cast<uint8_t *>(c.tier_arena) + size_t(slot) * c.tier.slot_bytes() +
+               (reinterpret_cast<uintptr_t>(host) - e->host);
+    }
+
     // Returns an index into uploads (or -1 when cached/null) and, through
-    // *dev_or_null, the device pointer for cached arrays.
-    long note(const void *host, size_t len, void **dev) {
+    // *dev_or_null, the device pointer for cached arrays.  *late: the array
+    // arrives with the stream-in copies (its expert runs in the second batch).
+    long note(const void *host, size_t len, void **dev, bool *late = nullptr) {
         *dev = nullptr;
+        if (late)
+            *late = false;
         if (!host)
             return -1;
         if (void *p = cached(host, len)) {
             *dev = p;
+            return -1;
+        }
+        if (void *p = tiered(host, len)) {
+            *dev = p;
+            if (late)
+                *late = tier_miss;
             return -1;
         }
         auto it = seen.find(host);
@@ -715,10 +759,15 @@ void mvllm_moe_shutdown(void) {
         return;
     cudaSetDevice(c.device);
     cudaStreamSynchronize(c.stream);
+    cudaStreamSynchronize(c.copy_stream);
     for (auto &kv : c.cache)
         cudaFree(kv.second.dev);
     c.cache.clear();
     c.cache_bytes = 0;
+    if (c.tier_arena)
+        cudaFree(c.tier_arena);
+    c.tier_arena = nullptr;
+    c.tier.configure(0, 0);
     if (c.ws.p)
         cudaFree(c.ws.p);
     if (c.transient.p)
@@ -731,8 +780,12 @@ void mvllm_moe_shutdown(void) {
     c.pinned_bytes = 0;
     for (auto &e : c.ev)
         cudaEventDestroy(e);
+    cudaEventDestroy(c.copy_done);
+    cudaStreamDestroy(c.copy_stream);
     cudaStreamDestroy(c.stream);
     c.stream = nullptr;
+    c.copy_stream = nullptr;
+    c.copy_done = nullptr;
     c.inited = false;
     c.device = -1;
 }
@@ -834,6 +887,70 @@ size_t mvllm_moe_cache_bytes(void) {
     Context &c = ctx();
     std::lock_guard<std::mutex> lk(c.mu);
     return c.cache_bytes;
+}
+
+// ----------------------------------------------------- device expert tier --
+int mvllm_moe_tier_configure(size_t budget_bytes, size_t slot_bytes) {
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (int rc = ensure_current(c))
+        return rc;
+    if (budget_bytes > 0 && slot_bytes == 0)
+        return fail(MVLLM_ERR_INVALID, "tier_configure: zero slot size");
+    cudaStreamSynchronize(c.copy_stream);
+    if (c.tier_arena)
+        cudaFree(c.tier_arena);
+    c.tier_arena = nullptr;
+    const size_t slot = (slot_bytes + 255) & ~size_t(255);
+    const size_t n = slot ? budget_bytes / slot : 0;
+    c.tier.configure(0, slot);
+    if (n == 0)
+        return MVLLM_OK; // tier off
+    if (n > size_t(1) << 20)
+        return fail(MVLLM_ERR_INVALID, "tier_configure: %zu slots", n);
+    if (cudaMalloc(&c.tier_arena, n * slot) != cudaSuccess) {
+        cudaGetLastError();
+        c.tier_arena = nullptr;
+        return fail(MVLLM_ERR_NOMEM, "tier_configure: cudaMalloc(%zu) failed", n * slot);
+    }
+    c.tier.configure(static_cast<int>(n), slot);
+    return MVLLM_OK;
+}
+
+int mvllm_moe_expert_bind(const void *host_blob, size_t bytes, uint64_t generation) {
+    if (!host_blob || bytes == 0)
+        return fail(MVLLM_ERR_INVALID, "expert_bind: null pointer or zero size");
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    c.tier.bind(reinterpret_cast<uintptr_t>(host_blob), bytes, generation);
+    return MVLLM_OK;
+}
+
+int mvllm_moe_expert_unbind(const void *host_blob) {
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (!c.tier.unbind(reinterpret_cast<uintptr_t>(host_blob)))
+        return fail(MVLLM_ERR_INVALID, "expert_unbind: blob not bound");
+    return MVLLM_OK;
+}
+
+void mvllm_moe_tier_stats(uint64_t *hits, uint64_t *misses, uint64_t *evictions,
+                          uint64_t *bytes_in, uint64_t *overflow, size_t *resident_bytes) {
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    const TierStats &t = c.tier.stats();
+    if (hits)
+        *hits = t.hits;
+    if (misses)
+        *misses = t.misses;
+    if (evictions)
+        *evictions = t.evictions;
+    if (bytes_in)
+        *bytes_in = t.bytes_in;
+    if (overflow)
+        *overflow = t.overflow;
+    if (resident_bytes)
+        *resident_bytes = c.tier.resident_bytes();
 }
 
 // ----------------------------------------------------- moe_block (host) --
@@ -941,17 +1058,44 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     const size_t gus_b = size_t(Iinter) * scale_row_bytes(fmt, D);
     const size_t ds_b = size_t(D) * scale_row_bytes(fmt, Iinter);
     Resolver rs(c);
+    if (c.tier_arena)
+        c.tier.begin_call();
     std::vector<void *> tdev(size_t(6) * nb, nullptr);
     std::vector<long> tidx(size_t(6) * nb, -1);
+    std::vector<char> late(size_t(nb), 0); // weights arrive with the tier's stream-in copies
     for (int e = 0; e < nb; ++e) {
         if (!valid[e])
             continue;
         const void *hp[6] = {g[e], u[e], d[e], packed ? gs[e] : nullptr, packed ? us[e] : nullptr,
                              packed ? ds[e] : nullptr};
         const size_t len[6] = {gu_b, gu_b, d_b, gus_b, gus_b, ds_b};
-        for (int k = 0; k < 6; ++k)
-            tidx[size_t(6) * e + k] = rs.note(hp[k], len[k], &tdev[size_t(6) * e + k]);
+        for (int k = 0; k < 6; ++k) {
+            bool lt = false;
+            tidx[size_t(6) * e + k] = rs.note(hp[k], len[k], &tdev[size_t(6) * e + k], &lt);
+            if (lt)
+                late[size_t(e)] = 1;
+        }
     }
+    // Cold tier blobs stream into their slots on the copy stream while the
+    // experts whose weights are already on the device run (first batch).
+    for (size_t i = 0; i < rs.stream_in.size(); ++i) {
+        TierEntry *t = rs.stream_in[i];
+        void *dst = static_cast<uint8_t *>(c.tier_arena) + size_t(t->slot) * c.tier.slot_bytes();
+        if (cudaMemcpyAsync(dst, reinterpret_cast<const void *>(t->host), t->bytes,
+                            cudaMemcpyHostToDevice, c.copy_stream) != cudaSuccess) {
+            for (size_t j = i; j < rs.stream_in.size(); ++j)
+                c.tier.abandon(*rs.stream_in[j]);
+            cudaStreamSynchronize(c.copy_stream);
+            return fail(MVLLM_ERR_CUDA, "moe_block: tier stream-in failed: %s",
+                        cudaGetErrorString(cudaGetLastError()));
+        }
+    }
+    if (!rs.stream_in.empty())
+        CUDA_TRY(cudaEventRecord(c.copy_done, c.copy_stream));
+    int n_late = 0;
+    for (int e = 0; e < nb; ++e)
+        n_late += late[size_t(e)];
+    const bool two_batches = n_late > 0;
     if (rs.transient_bytes) {
         if (int rc = ensure_dev(c.transient, rs.transient_bytes))
             return rc;
@@ -970,11 +1114,18 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
             fast = false;
     const int fmt_run = fmt;
 
-    // Device tables + metadata + activations + out, one upload.
-    std::vector<void *> tab(size_t(6) * nb, nullptr);
+    // Device tables + metadata + activations + out, one upload.  With
+    // stream-ins, two table sets: the first batch sees the other experts'
+    // pointers as null (skipped, its base still advancing -- the plan's
+    // rule), the second batch the reverse; both write their own y rows.
+    std::vector<void *> tab(size_t(two_batches ? 12 : 6) * nb, nullptr);
     for (int e = 0; e < nb; ++e)
-        for (int k = 0; k < 6; ++k)
-            tab[size_t(k) * nb + e] = tdev[size_t(6) * e + k];
+        for (int k = 0; k < 6; ++k) {
+            void *p = tdev[size_t(6) * e + k];
+            tab[size_t(k) * nb + e] = (two_batches && late[size_t(e)]) ? nullptr : p;
+            if (two_batches)
+                tab[size_t(6 + k) * nb + e] = late[size_t(e)] ? p : nullptr;
+        }
     std::vector<int> nr_run(nb), xoff_run(nb);
     for (int e = 0; e < nb; ++e) {
         nr_run[e] = nr[e];
@@ -1021,25 +1172,35 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     CUDA_TRY(cudaEventRecord(c.ev[1], c.stream));
     prof_mark(c.stream, kPhStart);
     void *const *dt = reinterpret_cast<void *const *>(db + o_tab);
-    Tables tb{dt, dt + nb, dt + 2 * nb, dt + 3 * nb, dt + 4 * nb, dt + 5 * nb};
     const int *d_nr = reinterpret_cast<const int *>(db + o_nr);
     const int *d_xoff = reinterpret_cast<const int *>(db + o_xoff);
     float *d_out = reinterpret_cast<float *>(db + o_out);
     const float *d_x = reinterpret_cast<const float *>(db + o_x);
-    int rc;
-    if (fast) {
-        rc = run_experts(c.stream, c.sms, nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
-                         MVLLM_DTYPE_F32, int(x_rows), false, R / n_valid, act, act_a, act_b, w,
-                         allow_tc);
-    } else {
+    auto run_batch = [&](void *const *t) -> int {
+        Tables tb{t, t + nb, t + 2 * nb, t + 3 * nb, t + 4 * nb, t + 5 * nb};
+        if (fast)
+            return run_experts(c.stream, c.sms, nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
+                               MVLLM_DTYPE_F32, int(x_rows), false, R / n_valid, act, act_a,
+                               act_b, w, allow_tc);
         // Generic path reads the uploaded f32 rows directly.
         RunWs w2 = w;
         w2.xs = const_cast<float *>(d_x);
-        rc = run_experts(c.stream, c.sms, nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
-                         MVLLM_DTYPE_F32, int(x_rows), true, R / n_valid, act, act_a, act_b, w2);
+        return run_experts(c.stream, c.sms, nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
+                           MVLLM_DTYPE_F32, int(x_rows), true, R / n_valid, act, act_a, act_b,
+                           w2);
+    };
+    int rc = MVLLM_OK;
+    if (n_late < n_valid)
+        rc = run_batch(dt);
+    if (!rc && two_batches) {
+        CUDA_TRY(cudaStreamWaitEvent(c.stream, c.copy_done, 0));
+        rc = run_batch(dt + 6 * nb);
     }
-    if (rc)
+    if (rc) {
+        cudaStreamSynchronize(c.copy_stream);
+        cudaStreamSynchronize(c.stream);
         return rc;
+    }
     {
         dim3 grid((D + 255) / 256, std::min(S_ext, 65535));
         combine_csr_kernel<<<grid, 256, 0, c.stream>>>(

@@ -38,7 +38,8 @@ C_SYMBOLS = (
     "mvllm_matmul_dev", "mvllm_moe_profile_enable", "mvllm_moe_profile_read",
     "mvllm_moe_permute_dev_noalloc", "mvllm_moe_ep_plan_dev", "mvllm_moe_ep_pack_dev",
     "mvllm_moe_ep_combine_dev", "mvllm_moe_topk_dev", "mvllm_moe_route_dev",
-    "mvllm_moe_ep_combine16_dev", "mvllm_moe_layer_partial_dev",
+    "mvllm_moe_ep_combine16_dev", "mvllm_moe_layer_partial_dev", "mvllm_moe_tier_configure",
+    "mvllm_moe_expert_bind", "mvllm_moe_expert_unbind", "mvllm_moe_tier_stats",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -92,6 +93,10 @@ def lib():
                                           vp]),
             "mvllm_moe_ep_combine_dev": (i, [vp, vp, vp, i, i, i, vp]),
             "mvllm_moe_ep_combine16_dev": (i, [vp, vp, vp, i, i, i, vp]),
+            "mvllm_moe_tier_configure": (i, [sz, sz]),
+            "mvllm_moe_expert_bind": (i, [vp, sz, C.c_uint64]),
+            "mvllm_moe_expert_unbind": (i, [vp]),
+            "mvllm_moe_tier_stats": (None, [vp] * 6),
             "mvllm_moe_layer_partial_dev": (i, [vp] + [i] * 7 + [vp, vp, vp, i] + [vp] * 6 +
                                             [vp, i, f, f, vp, sz]),
             "mvllm_moe_topk_dev": (i, [vp, vp, vp, i, i, i, vp, vp]),
@@ -178,6 +183,27 @@ def moe_block(nb, D, Iinter, fmt, g, u, d, gs, us, ds, xg, xoff, nr, rows, rw, o
         return False
     _check(rc)
     return True
+
+
+def tier_configure(budget_bytes: int, slot_bytes: int) -> None:
+    _check(lib().mvllm_moe_tier_configure(budget_bytes, slot_bytes))
+
+
+def expert_bind(arr: np.ndarray, generation: int = 0) -> None:
+    """Binds a host blob (a numpy array, e.g. one expert's packed arrays in
+    one buffer) to the device expert tier."""
+    _check(lib().mvllm_moe_expert_bind(arr.ctypes.data, arr.nbytes, generation))
+
+
+def expert_unbind(arr: np.ndarray) -> None:
+    _check(lib().mvllm_moe_expert_unbind(arr.ctypes.data))
+
+
+def tier_stats():
+    v = [C.c_uint64() for _ in range(5)] + [C.c_size_t()]
+    lib().mvllm_moe_tier_stats(*[C.byref(x) for x in v])
+    keys = ("hits", "misses", "evictions", "bytes_in", "overflow", "resident_bytes")
+    return {k: x.value for k, x in zip(keys, v)}
 
 
 def cache_register(arr: np.ndarray, generation: int = 0) -> None:
