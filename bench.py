@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--no-tier", action="store_true",
+                    help="skip the device expert tier measurement (host moe_block entry)")
+    ap.add_argument("--tier-steps", type=int, default=16)
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the config[3] prefill measurement")
     ap.add_argument("--prefill-steps", type=int, default=10)
@@ -237,6 +240,126 @@ def zipf_routing(torch, T, E, K, g, s=1.1, perm=None):
     logits = -s * torch.log(rank)[None, :] - torch.log(-torch.log(u))
     vals, idx = torch.topk(torch.softmax(logits, dim=1), K, dim=1)
     return idx.int().contiguous(), (vals / vals.sum(1, keepdim=True)).float().contiguous()
+
+
+def host_routing(idx, wt, E, with_shared):
+    """The caller's side of moe_block for one batch (glm53.cpp:1958-1971 /
+    kimi_k3.cpp:2036-2050 order): experts ascending, tokens ascending inside
+    each, wsum = sum of the token's weights for that expert; the shared expert
+    (id E) last with weight 1.  Returns ids, nr, xoff, rows, rw."""
+    B, K = idx.shape
+    ids = sorted({int(e) for e in idx.flatten() if 0 <= e < E})
+    nr, rows, rw = [], [], []
+    for e in ids:
+        n = 0
+        for c in range(B):
+            m = idx[c] == e
+            if m.any():
+                rows.append(c)
+                rw.append(float(np.float32(wt[c][m].sum(dtype=np.float32))))
+                n += 1
+        nr.append(n)
+    if with_shared:
+        ids.append(E)
+        nr.append(B)
+        rows.extend(range(B))
+        rw.extend([1.0] * B)
+    nr = np.array(nr, np.int32)
+    xoff = np.concatenate([[0], np.cumsum(nr)[:-1]]).astype(np.int32)
+    return ids, nr, xoff, np.array(rows, np.int32), np.array(rw, np.float32)
+
+
+def pinned_h2d_gbs(torch):
+    """Pinned host -> device copy bandwidth (1 GiB, best of 3, CUDA events)."""
+    n = 1 << 30
+    h = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(n, dtype=torch.uint8, device="cuda")
+    best = 0.0
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        d.copy_(h, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        best = max(best, n / (a.elapsed_time(b) / 1e3) / 1e9)
+    del h, d
+    return best
+
+
+def tier_bench(moe, torch, wl, steps):
+    """Device expert tier: config[1] decode (batch wl.B) through the
+    reference-facing mvllm_moe_block, each expert's six arrays in one pinned
+    host blob (an ExpertStore slot) bound to the tier.  VRAM budgets: every
+    expert fits; half of them fit (least recently used blobs give their slots
+    up, cold ones stream over PCIe while the resident ones compute); and no
+    tier (every call uploads its experts).  The routing/permutation is the
+    caller's work and is prepared outside the timed region."""
+    D, I, E, ns = CFG["D"], CFG["I"], CFG["E"], CFG["n_shared"]
+    EE = E + ns
+    parts = (wl.gp, wl.up, wl.dp, wl.gs, wl.us, wl.ds)
+    sizes = [t[0].numel() for t in parts]
+    offs, n = [], 0
+    for z in sizes:
+        offs.append(n)
+        n += (z + 255) // 256 * 256
+    blob = n
+    host = torch.empty((EE, blob), dtype=torch.uint8, pin_memory=True)
+    for e in range(EE):
+        for t, o, z in zip(parts, offs, sizes):
+            host[e, o:o + z].copy_(t[e].flatten())
+    torch.cuda.synchronize()
+    hn = host.numpy()
+    views = [[hn[e, o:o + z] for o, z in zip(offs, sizes)] for e in range(EE)]
+    batches = []
+    for (idx, wt, x) in wl.inputs:
+        ih, wh, xh = idx.cpu().numpy(), wt.cpu().numpy(), x.float().cpu().numpy()
+        ids, nr, xoff, rows, rw = host_routing(ih, wh, E, ns > 0)
+        batches.append((ids, nr, xoff, rows, rw, np.ascontiguousarray(xh[rows])))
+    out = np.zeros((wl.B, D), np.float32)
+
+    def call(b):
+        ids, nr, xoff, rows, rw, xg = b
+        v = [views[e] for e in ids]
+        out[:] = 0
+        moe.moe_block(len(ids), D, I, CFG["fmt"], [a[0] for a in v], [a[1] for a in v],
+                      [a[2] for a in v], [a[3] for a in v], [a[4] for a in v],
+                      [a[5] for a in v], xg, xoff, nr, rows, rw, out, wl.B, CFG["act"],
+                      CFG["act_a"], CFG["act_b"])
+
+    res = {"blob_bytes": blob, "experts": EE, "batch": wl.B,
+           "pinned_h2d_gbs": pinned_h2d_gbs(torch)}
+    for name, nslots, n_steps in (("all_resident", EE, steps), ("half_resident", EE // 2, steps),
+                                  ("no_tier", 0, max(2, steps // 4))):
+        moe.tier_configure(nslots * blob, blob)
+        if nslots:
+            for e in range(EE):
+                moe.expert_bind(hn[e], 1)
+        for i in range(len(batches)):  # warm: fills the slots
+            call(batches[i])
+        s0 = moe.tier_stats()
+        t0 = time.perf_counter()
+        for i in range(n_steps):
+            call(batches[i % len(batches)])
+        dt = time.perf_counter() - t0
+        s1 = moe.tier_stats()
+        bin_ = (s1["bytes_in"] - s0["bytes_in"]) / n_steps
+        bov = (s1["overflow_bytes"] - s0["overflow_bytes"]) / n_steps
+        if not nslots:  # no tier: every touched expert's blob is uploaded per call
+            bov = sum(len(batches[i % len(batches)][0]) for i in range(n_steps)) * blob / n_steps
+        acq = (s1["hits"] - s0["hits"]) + (s1["misses"] - s0["misses"]) + \
+              (s1["overflow"] - s0["overflow"])
+        h2d = (bin_ + bov) * n_steps / dt / 1e9
+        res[name] = {"slots": nslots, "steps": n_steps, "ms_per_step": dt / n_steps * 1e3,
+                     "tokens_per_s": wl.B * n_steps / dt,
+                     "hit_rate": (s1["hits"] - s0["hits"]) / acq if acq else None,
+                     "streamed_bytes_per_step": bin_, "uploaded_bytes_per_step": bov,
+                     "h2d_gbs": h2d, "h2d_frac_of_pinned_peak": h2d / res["pinned_h2d_gbs"]}
+        if nslots:
+            for e in range(EE):
+                moe.expert_unbind(hn[e])
+        moe.tier_configure(0, 0)
+    del host
+    return res
 
 
 def prefill_bench(moe, torch, wl, steps, peak_tf, peak_gbs, T=PREFILL_T):
@@ -634,6 +757,9 @@ def main():
 
     # config[3] prefill (tensor-core kernels), per rank
     prefill = None
+    tier = None
+    if not args.no_tier and world == 1:
+        tier = tier_bench(moe, torch, wl, args.tier_steps)
     if not args.no_prefill:
         prefill = prefill_bench(moe, torch, wl, args.prefill_steps, bf16_peak(), peak,
                                 args.prefill_tokens)
@@ -684,6 +810,7 @@ def main():
             "clocks": clk.report(),
             "sweep": sweep,
             "prefill": prefill,
+            "expert_tier": tier,
             "expert_parallel": ep_res,
         }
         if prefill and cpu and cpu.get("value"):

@@ -118,11 +118,11 @@ MVLLM_API int mvllm_moe_expert_unbind(const void *host_blob);
 /* Counters since init: blob acquisitions that found the blob resident
  * (hits), that copied it in (misses), slots taken from another blob
  * (evictions), bytes copied in, acquisitions that found no slot (overflow:
- * every slot held by a blob the call uses, or the blob too large); and the
- * bytes now resident. */
+ * every slot held by a blob the call uses, or the blob too large) and their
+ * bytes (uploaded for the call only); and the bytes now resident. */
 MVLLM_API void mvllm_moe_tier_stats(uint64_t *hits, uint64_t *misses, uint64_t *evictions,
                                     uint64_t *bytes_in, uint64_t *overflow,
-                                    size_t *resident_bytes);
+                                    uint64_t *overflow_bytes, size_t *resident_bytes);
 
 /* ---- device-pointer entries (stream-ordered, no host sync, no allocation:
  *      the caller passes a workspace of at least the *_workspace size) ---- */

@@ -34,6 +34,7 @@ struct TierEntry {
 
 struct TierStats {
     uint64_t hits = 0, misses = 0, evictions = 0, bytes_in = 0, overflow = 0;
+    uint64_t overflow_bytes = 0; // blobs uploaded for the call only
 };
 
 class TierPolicy {
@@ -125,6 +126,7 @@ class TierPolicy {
         }
         if (e.bytes > slot_bytes_ || owner_.empty()) {
             ++stats_.overflow;
+            stats_.overflow_bytes += e.bytes;
             return -1;
         }
         int victim = -1;
@@ -144,6 +146,7 @@ class TierPolicy {
         }
         if (victim < 0) {
             ++stats_.overflow;
+            stats_.overflow_bytes += e.bytes;
             return -1;
         }
         if (owner_[size_t(victim)] != 0) {

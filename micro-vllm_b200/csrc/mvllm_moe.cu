@@ -935,7 +935,8 @@ int mvllm_moe_expert_unbind(const void *host_blob) {
 }
 
 void mvllm_moe_tier_stats(uint64_t *hits, uint64_t *misses, uint64_t *evictions,
-                          uint64_t *bytes_in, uint64_t *overflow, size_t *resident_bytes) {
+                          uint64_t *bytes_in, uint64_t *overflow, uint64_t *overflow_bytes,
+                          size_t *resident_bytes) {
     Context &c = ctx();
     std::lock_guard<std::mutex> lk(c.mu);
     const TierStats &t = c.tier.stats();
@@ -949,6 +950,8 @@ void mvllm_moe_tier_stats(uint64_t *hits, uint64_t *misses, uint64_t *evictions,
         *bytes_in = t.bytes_in;
     if (overflow)
         *overflow = t.overflow;
+    if (overflow_bytes)
+        *overflow_bytes = t.overflow_bytes;
     if (resident_bytes)
         *resident_bytes = c.tier.resident_bytes();
 }

@@ -96,7 +96,7 @@ def lib():
             "mvllm_moe_tier_configure": (i, [sz, sz]),
             "mvllm_moe_expert_bind": (i, [vp, sz, C.c_uint64]),
             "mvllm_moe_expert_unbind": (i, [vp]),
-            "mvllm_moe_tier_stats": (None, [vp] * 6),
+            "mvllm_moe_tier_stats": (None, [vp] * 7),
             "mvllm_moe_layer_partial_dev": (i, [vp] + [i] * 7 + [vp, vp, vp, i] + [vp] * 6 +
                                             [vp, i, f, f, vp, sz]),
             "mvllm_moe_topk_dev": (i, [vp, vp, vp, i, i, i, vp, vp]),
@@ -200,9 +200,10 @@ def expert_unbind(arr: np.ndarray) -> None:
 
 
 def tier_stats():
-    v = [C.c_uint64() for _ in range(5)] + [C.c_size_t()]
+    v = [C.c_uint64() for _ in range(6)] + [C.c_size_t()]
     lib().mvllm_moe_tier_stats(*[C.byref(x) for x in v])
-    keys = ("hits", "misses", "evictions", "bytes_in", "overflow", "resident_bytes")
+    keys = ("hits", "misses", "evictions", "bytes_in", "overflow", "overflow_bytes",
+            "resident_bytes")
     return {k: x.value for k, x in zip(keys, v)}
 
 
