@@ -362,6 +362,44 @@ def tier_bench(moe, torch, wl, steps):
     return res
 
 
+def epilogue_bench(moe, torch, peak_gbs, reps=200):
+    """Layer epilogue after the routed combine, Kimi-K3 form at config[1]'s
+    decode batch: rmsnorm over a 2048-wide latent, int8-row up-projection to
+    7168 (QuantMat fmt 8), routed scale, shared-expert add, residual update.
+    Bound by the up-projection's weight bytes (14.7 MB per call)."""
+    T, H, L = 32, CFG["D"], 2048
+    g = torch.Generator(device="cuda").manual_seed(31)
+    acc = torch.randn((T, L), generator=g, device="cuda")
+    h = torch.randn((T, H), generator=g, device="cuda")
+    sh = torch.randn((T, H), generator=g, device="cuda")
+    lat_n = torch.ones(L, device="cuda")
+    q = torch.randint(-127, 128, (H, L), generator=g, device="cuda", dtype=torch.int32).to(
+        torch.int8)
+    sc = torch.full((H,), 0.01, device="cuda")
+    ws = torch.empty(moe.epilogue_workspace_bytes(T, H, L), dtype=torch.uint8, device="cuda")
+
+    def step():
+        moe.epilogue_dev(acc, h, 2.0, lat_n, 1e-6, 8, q, sc, sh, ws)
+
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) / reps * 1e3
+    nbytes = H * L + H * 4 + T * L * 4 * 2 + T * H * 4 * 4  # weights, scales, acc/norm, h/sh/u
+    return {"workload": f"K3 epilogue: {T} tokens, latent {L} -> hidden {H}, int8-row "
+                        "up-projection, rmsnorm, routed scale, shared add",
+            "us_per_call": us, "algorithmic_bytes": nbytes,
+            "achieved_gbs": nbytes / (us / 1e6) / 1e9,
+            "frac_of_hbm": nbytes / (us / 1e6) / 1e9 / peak_gbs if peak_gbs else None,
+            "launches_per_call": 3}
+
+
 def prefill_bench(moe, torch, wl, steps, peak_tf, peak_gbs, T=PREFILL_T):
     """Config[3]: 4096 tokens, the 256 routed MXFP4 experts of the decode
     workload (same shape and format), Zipf s=1.1 routing, no shared expert,
@@ -760,6 +798,7 @@ def main():
     tier = None
     if not args.no_tier and world == 1:
         tier = tier_bench(moe, torch, wl, args.tier_steps)
+    epilogue = epilogue_bench(moe, torch, peak) if world == 1 else None
     if not args.no_prefill:
         prefill = prefill_bench(moe, torch, wl, args.prefill_steps, bf16_peak(), peak,
                                 args.prefill_tokens)
@@ -811,6 +850,7 @@ def main():
             "sweep": sweep,
             "prefill": prefill,
             "expert_tier": tier,
+            "epilogue": epilogue,
             "expert_parallel": ep_res,
         }
         if prefill and cpu and cpu.get("value"):

@@ -57,6 +57,9 @@ enum {
 /* metal_ops::Act (src/gpu/metal_ops.hpp:44); any other value behaves as SILU. */
 enum { MVLLM_ACT_SILU = 0, MVLLM_ACT_CLAMP_SWIGLU = 1, MVLLM_ACT_SITU = 2 };
 enum { MVLLM_FMT_F32 = 0, MVLLM_FMT_INT4_G64 = 4, MVLLM_FMT_MXFP4 = 7 };
+/* int8 with one f32 scale per row: QuantMat fmt 8 (src/quant/weight.cpp:37-40,
+ * quant.cpp:230-268); accepted by mvllm_matmul_dev and the layer epilogue. */
+enum { MVLLM_FMT_INT8_ROW = 8 };
 enum { MVLLM_DTYPE_F32 = 0, MVLLM_DTYPE_BF16 = 1 };
 
 /* ---- lifecycle: metal_ops::init/shutdown/available/backend_name
@@ -212,7 +215,9 @@ MVLLM_API int mvllm_pack_mxfp4_dev(void *stream, const float *w, int O, int I, u
 
 /* Dequantised GEMM y[S,O] = x[S,I] . W[O,I]^T on device (f32 in/out): the
  * role of coli_cuda::matmul / matmul_mxfp4 (src/gpu/coli_cuda.hpp:58-61) and
- * quant::matmul_* (src/quant/quant.hpp:53-70). */
+ * quant::matmul_* (src/quant/quant.hpp:53-70).  fmt 0, 4, 7 or 8 (int8 rows:
+ * y = (sum x.q) x scale[o], quant.cpp:255-268).  Each weight row is read once
+ * for up to 32 rows of x. */
 MVLLM_API int mvllm_matmul_dev(void *stream, int fmt, float *y, const float *x, const void *w,
                      const void *scales, int S, int I, int O);
 
@@ -280,6 +285,21 @@ MVLLM_API int mvllm_moe_layer_partial_dev(void *stream, int T, int K, int E, int
                                           const void *const *ds, void *out16, int act,
                                           float act_a, float act_b, void *workspace,
                                           size_t workspace_bytes);
+
+/* ---- layer epilogue after the routed combine (SURVEY (f)3): the step both
+ *      callers take after moe_block, kimi_k3.cpp:2074-2108 and
+ *      glm53.cpp:1993-2027 ---- */
+/* For each token c: a = acc[c] (L floats, the routed sum); if lat_n:
+ * a = rmsnorm(a, lat_n, eps) (quant.cpp:384-398); if up_w: u = a . W_up^T
+ * (QuantMat::gemm, fmt 0/4/8, W_up [H, L]) else u = a (then L == H);
+ * h[c][i] += u[i] * routed_scale; if shared: h[c][i] += shared[c][i] (the
+ * shared expert's output, not scaled).  All device pointers; h accumulated. */
+MVLLM_API size_t mvllm_moe_epilogue_workspace(int T, int H, int L);
+MVLLM_API int mvllm_moe_epilogue_dev(void *stream, int T, int H, int L, const float *acc,
+                                     const float *lat_n, float eps, int up_fmt, const void *up_w,
+                                     const void *up_scales, float routed_scale,
+                                     const float *shared, float *h, void *workspace,
+                                     size_t workspace_bytes);
 
 /* Per-phase device time of the device-pointer entries, from CUDA events
  * recorded on the launch stream after each phase while enabled (the role of

@@ -701,22 +701,91 @@ template <int PHASE> __global__ void __launch_bounds__(256) generic_ffn_kernel(c
 }
 
 // Generic dequantised GEMM y[S,O] = x[S,I] . W[O,I]^T (warp per output row).
+// y[S,O] = x[S,I] . W[O,I]^T: a warp per output row, up to 32 rows of x per
+// pass, so each weight element is read (and dequantised) once per 32 rows.
+// fmt 8 (int8 rows) sums x.q and applies the row scale at the end, as
+// quant::matmul_int8_row does.
 __global__ void __launch_bounds__(256) matmul_generic_kernel(int fmt, float *y, const float *x,
                                                              const void *w, const void *sc,
                                                              int S, int I, int O) {
+    constexpr int kS = 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int o = blockIdx.x * 8 + warp;
     if (o >= O)
         return;
-    for (int s = 0; s < S; ++s) {
-        float acc = 0.f;
-        for (int k = lane; k < I; k += 32)
-            acc = fmaf(x[static_cast<size_t>(s) * I + k], deq_elem(w, sc, fmt, o, k, I), acc);
+    for (int s0 = 0; s0 < S; s0 += kS) {
+        const int ns = min(kS, S - s0);
+        float acc[kS];
+#pragma unroll
+        for (int j = 0; j < kS; ++j)
+            acc[j] = 0.f;
+        for (int k = lane; k < I; k += 32) {
+            const float wv = fmt == MVLLM_FMT_INT8_ROW
+                                 ? static_cast<float>(
+                                       static_cast<const int8_t *>(w)[static_cast<size_t>(o) * I + k])
+                                 : deq_elem(w, sc, fmt, o, k, I);
+#pragma unroll
+            for (int j = 0; j < kS; ++j)
+                if (j < ns)
+                    acc[j] = fmaf(x[static_cast<size_t>(s0 + j) * I + k], wv, acc[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < kS; ++j) {
+            if (j >= ns)
+                break;
+            float a = acc[j];
+#pragma unroll
+            for (int m = 16; m > 0; m >>= 1)
+                a += __shfl_xor_sync(0xffffffffu, a, m);
+            if (lane == 0)
+                y[static_cast<size_t>(s0 + j) * O + o] =
+                    fmt == MVLLM_FMT_INT8_ROW ? a * static_cast<const float *>(sc)[o] : a;
+        }
+    }
+}
+
+// rmsnorm per row (quant.cpp:384-398): y = x * (1 / sqrt(mean(x^2) + eps)) * w,
+// the sum of squares as a tree (the reference sums sequentially: the norm
+// agrees to a few ulp).  One CTA per row.
+__global__ void rmsnorm_rows_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                    float *__restrict__ y, int T, int n, float eps) {
+    __shared__ float part[32];
+    for (int r = blockIdx.x; r < T; r += gridDim.x) {
+        const float *xr = x + static_cast<size_t>(r) * n;
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < n; i += blockDim.x)
+            ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
 #pragma unroll
         for (int m = 16; m > 0; m >>= 1)
-            acc += __shfl_xor_sync(0xffffffffu, acc, m);
-        if (lane == 0)
-            y[static_cast<size_t>(s) * O + o] = acc;
+            ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, m));
+        if ((threadIdx.x & 31) == 0)
+            part[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float tot = 0.f;
+        for (int j = 0; j < static_cast<int>(blockDim.x >> 5); ++j)
+            tot = __fadd_rn(tot, part[j]);
+        const float inv =
+            __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(n)), eps)));
+        float *yr = y + static_cast<size_t>(r) * n;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const float v = __fmul_rn(xr[i], inv);
+            yr[i] = w ? __fmul_rn(v, w[i]) : v;
+        }
+        __syncthreads();
+    }
+}
+
+// h += u * routed_scale, then h += shared (kimi_k3.cpp:2090-2105,
+// glm53.cpp:1997-2026): separate roundings, in that order.
+__global__ void epilogue_residual_kernel(float *__restrict__ h, const float *__restrict__ u,
+                                         const float *__restrict__ shared, float routed_scale,
+                                         size_t n) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        float v = __fadd_rn(h[i], __fmul_rn(u[i], routed_scale));
+        if (shared)
+            v = __fadd_rn(v, shared[i]);
+        h[i] = v;
     }
 }
 

@@ -1855,13 +1855,58 @@ int mvllm_pack_mxfp4_dev(void *stream, const float *w, int O, int I, uint8_t *pa
 
 int mvllm_matmul_dev(void *stream, int fmt, float *y, const float *x, const void *w,
                      const void *scales, int S, int I, int O) {
-    if ((fmt != 0 && fmt != 4 && fmt != 7) || !y || !x || !w || S < 1 || I < 1 || O < 1 ||
-        (fmt != 0 && !scales))
+    if ((fmt != 0 && fmt != 4 && fmt != 7 && fmt != MVLLM_FMT_INT8_ROW) || !y || !x || !w ||
+        S < 1 || I < 1 || O < 1 || (fmt != 0 && !scales))
         return fail(MVLLM_ERR_INVALID, "matmul_dev: invalid arguments");
     if (!ctx().inited)
         return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
     matmul_generic_kernel<<<(O + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
         fmt, y, x, w, scales, S, I, O);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+// ------------------------------------------------------------- epilogue --
+size_t mvllm_moe_epilogue_workspace(int T, int H, int L) {
+    if (T < 1 || H < 1 || L < 1)
+        return 0;
+    return (size_t(T) * L + size_t(T) * H) * sizeof(float) + 256;
+}
+
+int mvllm_moe_epilogue_dev(void *stream, int T, int H, int L, const float *acc,
+                           const float *lat_n, float eps, int up_fmt, const void *up_w,
+                           const void *up_scales, float routed_scale, const float *shared,
+                           float *h, void *workspace, size_t workspace_bytes) {
+    if (T < 1 || H < 1 || L < 1 || !acc || !h || (!up_w && L != H) ||
+        (up_w && up_fmt != 0 && up_fmt != MVLLM_FMT_INT4_G64 && up_fmt != MVLLM_FMT_INT8_ROW) ||
+        (up_w && up_fmt != 0 && !up_scales) ||
+        (up_w && up_fmt == MVLLM_FMT_INT4_G64 && L % 64 != 0))
+        return fail(MVLLM_ERR_INVALID, "epilogue_dev: invalid arguments");
+    const size_t need = mvllm_moe_epilogue_workspace(T, H, L);
+    if ((lat_n || up_w) && (!workspace || workspace_bytes < need))
+        return fail(MVLLM_ERR_WORKSPACE, "epilogue_dev: workspace %zu < %zu", workspace_bytes,
+                    need);
+    Context &c = ctx();
+    if (!c.inited)
+        return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const float *src = acc;
+    float *norm = static_cast<float *>(workspace);
+    float *up = norm ? norm + size_t(T) * L : nullptr;
+    if (lat_n) {
+        rmsnorm_rows_kernel<<<std::min(T, 8 * c.sms), 256, 0, st>>>(acc, lat_n, norm, T, L, eps);
+        CUDA_TRY(cudaGetLastError());
+        src = norm;
+    }
+    if (up_w) {
+        matmul_generic_kernel<<<(H + 7) / 8, 256, 0, st>>>(up_fmt, up, src, up_w, up_scales, T, L,
+                                                           H);
+        CUDA_TRY(cudaGetLastError());
+        src = up;
+    }
+    const size_t n = size_t(T) * H;
+    epilogue_residual_kernel<<<int(std::min<size_t>((n + 255) / 256, size_t(c.sms) * 16)), 256, 0,
+                               st>>>(h, src, shared, routed_scale, n);
     CUDA_TRY(cudaGetLastError());
     return MVLLM_OK;
 }

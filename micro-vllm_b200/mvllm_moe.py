@@ -40,6 +40,7 @@ C_SYMBOLS = (
     "mvllm_moe_ep_combine_dev", "mvllm_moe_topk_dev", "mvllm_moe_route_dev",
     "mvllm_moe_ep_combine16_dev", "mvllm_moe_layer_partial_dev", "mvllm_moe_tier_configure",
     "mvllm_moe_expert_bind", "mvllm_moe_expert_unbind", "mvllm_moe_tier_stats",
+    "mvllm_moe_epilogue_workspace", "mvllm_moe_epilogue_dev",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -94,6 +95,8 @@ def lib():
             "mvllm_moe_ep_combine_dev": (i, [vp, vp, vp, i, i, i, vp]),
             "mvllm_moe_ep_combine16_dev": (i, [vp, vp, vp, i, i, i, vp]),
             "mvllm_moe_tier_configure": (i, [sz, sz]),
+            "mvllm_moe_epilogue_workspace": (sz, [i, i, i]),
+            "mvllm_moe_epilogue_dev": (i, [vp, i, i, i, vp, vp, f, i, vp, vp, f, vp, vp, vp, sz]),
             "mvllm_moe_expert_bind": (i, [vp, sz, C.c_uint64]),
             "mvllm_moe_expert_unbind": (i, [vp]),
             "mvllm_moe_tier_stats": (None, [vp] * 7),
@@ -336,6 +339,23 @@ def matmul_dev(fmt, y, x, w, scales, stream=None):
     O = y.shape[1]
     _check(lib().mvllm_matmul_dev(_stream(stream), fmt, _dp(y), _dp(x), _dp(w), _dp(scales), S,
                                   I, O))
+
+
+# ----------------------------------------------------------- layer epilogue --
+def epilogue_dev(acc, h, routed_scale=1.0, lat_n=None, eps=1e-6, up_fmt=0, up_w=None,
+                 up_scales=None, shared=None, workspace=None, stream=None):
+    """h += (lat_up . rmsnorm(acc)) * routed_scale + shared (device tensors)."""
+    T, L = acc.shape
+    H = h.shape[1]
+    ws = workspace
+    _check(lib().mvllm_moe_epilogue_dev(
+        _stream(stream), T, H, L, _dp(acc), _dp(lat_n), eps, up_fmt, _dp(up_w), _dp(up_scales),
+        routed_scale, _dp(shared), _dp(h), _dp(ws),
+        0 if ws is None else ws.numel() * ws.element_size()))
+
+
+def epilogue_workspace_bytes(T, H, L) -> int:
+    return lib().mvllm_moe_epilogue_workspace(T, H, L)
 
 
 # -------------------------------------------------------- expert parallelism --

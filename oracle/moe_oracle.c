@@ -100,6 +100,61 @@ EXPORT void orc_matmul_f32(float *y, const float *x, const float *w, int S, int 
     }
 }
 
+/* int8 per-row quantiser: scale = absmax/127, q = clamp(round(w * (1/scale)),
+ * -127, 127), all zero for a zero row.  quant.cpp:230-253 */
+EXPORT void orc_quantize_int8_row(const float *w, int O, int I, int8_t *q, float *scales) {
+    for (int o = 0; o < O; ++o) {
+        const float *row = w + (size_t)o * I;
+        int8_t *qrow = q + (size_t)o * I;
+        float amax = 0.f;
+        for (int i = 0; i < I; ++i) {
+            const float a = fabsf(row[i]);
+            if (a > amax)
+                amax = a;
+        }
+        const float scale = amax / 127.f;
+        scales[o] = scale;
+        if (scale == 0.f) {
+            memset(qrow, 0, (size_t)I);
+            continue;
+        }
+        const float inv = 1.f / scale;
+        for (int i = 0; i < I; ++i) {
+            int qi = (int)roundf(row[i] * inv);
+            qi = qi < -127 ? -127 : (qi > 127 ? 127 : qi);
+            qrow[i] = (int8_t)qi;
+        }
+    }
+}
+
+/* y[s,o] = (sum_i x[s,i] * q[o,i]) * scale[o], sequential in i.  quant.cpp:255-268 */
+EXPORT void orc_matmul_int8_row(float *y, const float *x, const int8_t *q, const float *scales,
+                                int S, int I, int O) {
+    for (int s = 0; s < S; ++s) {
+        const float *xs = x + (size_t)s * I;
+        float *ys = y + (size_t)s * O;
+        for (int o = 0; o < O; ++o) {
+            const int8_t *qrow = q + (size_t)o * I;
+            float acc = 0.f;
+            for (int i = 0; i < I; ++i)
+                acc += xs[i] * (float)qrow[i];
+            ys[o] = acc * scales[o];
+        }
+    }
+}
+
+/* y = x * (1 / sqrt(sum(x^2)/n + eps)) * w (w may be null).  quant.cpp:384-398 */
+EXPORT void orc_rmsnorm(const float *x, const float *w, float *y, int n, float eps) {
+    if (n <= 0)
+        return;
+    float ss = 0.f;
+    for (int i = 0; i < n; ++i)
+        ss += x[i] * x[i];
+    const float inv = 1.f / sqrtf(ss / (float)n + eps);
+    for (int i = 0; i < n; ++i)
+        y[i] = w ? x[i] * inv * w[i] : x[i] * inv;
+}
+
 /* int4-g64 quantiser: scale = absmax/7 floored at 1e-8, q = clamp(round(w/scale),-8,7),
  * nibble q+8, low nibble = even column.  quant.cpp:170-201 */
 EXPORT void orc_quantize_int4_g64(const float *w, int O, int I, uint8_t *packed, float *scales) {
@@ -532,6 +587,46 @@ EXPORT int orc_moe_permute(const int *idx, const float *wt, int C, int K, const 
  * scales, up, up scales, down, down scales.  K3 MXFP4 (kimi_k3.cpp:83-102):
  * w1 (gate), w1 scales, w2 (down), w2 scales, w3 (up), w3 scales.
  * off[0..5] = byte offsets of g, gs, u, us, d, ds; returns the slot size. */
+/* Layer epilogue after the routed combine, per token c (kimi_k3.cpp:2074-2108;
+ * glm53.cpp:1993-2027 is the L == H case without norm or projection):
+ *   a = acc[c] (L floats); if lat_n: a = rmsnorm(a, lat_n, eps);
+ *   u = up_w ? QuantMat::gemm(up, a) (weight.cpp:47-64: fmt 4 int4-g64 when
+ *       L % 64 == 0, fmt 8 int8 rows, else f32) : a;
+ *   h[c][i] += u[i] * routed_scale;  if shared: h[c][i] += shared[c][i]. */
+EXPORT void orc_moe_epilogue(int T, int H, int L, const float *acc, const float *lat_n, float eps,
+                             int up_fmt, const void *up_w, const void *up_scales,
+                             float routed_scale, const float *shared, float *h) {
+    float *a = (float *)malloc(sizeof(float) * (size_t)L);
+    float *u = (float *)malloc(sizeof(float) * (size_t)H);
+    for (int c = 0; c < T; ++c) {
+        const float *ac = acc + (size_t)c * L;
+        if (lat_n)
+            orc_rmsnorm(ac, lat_n, a, L, eps);
+        else
+            memcpy(a, ac, sizeof(float) * (size_t)L);
+        if (up_w) {
+            if (up_fmt == 4 && L % 64 == 0)
+                orc_matmul_int4_g64(u, a, (const uint8_t *)up_w, (const float *)up_scales, 1, L,
+                                    H);
+            else if (up_fmt == 8)
+                orc_matmul_int8_row(u, a, (const int8_t *)up_w, (const float *)up_scales, 1, L,
+                                    H);
+            else
+                orc_matmul_f32(u, a, (const float *)up_w, 1, L, H);
+        } else {
+            memcpy(u, a, sizeof(float) * (size_t)H);
+        }
+        float *hc = h + (size_t)c * H;
+        for (int i = 0; i < H; ++i)
+            hc[i] += u[i] * routed_scale;
+        if (shared)
+            for (int i = 0; i < H; ++i)
+                hc[i] += shared[(size_t)c * H + i];
+    }
+    free(a);
+    free(u);
+}
+
 EXPORT int64_t orc_glm_geom(int hidden, int inter, int64_t *off) {
     int64_t pack_go, sc_go, pack_d, sc_d, slot;
     if (hidden > 0 && inter > 0 && hidden % 64 == 0 && inter % 64 == 0) {

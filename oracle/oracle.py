@@ -80,6 +80,16 @@ class Oracle:
         self._mm4.argtypes = [_f32p, _f32p, _u8p, _f32p, C.c_int, C.c_int, C.c_int]
         self._mmx = getattr(L, p + "matmul_mxfp4")
         self._mmx.argtypes = [_f32p, _f32p, _u8p, _u8p, C.c_int, C.c_int, C.c_int]
+        self._q8 = getattr(L, p + "quantize_int8_row")
+        self._q8.argtypes = [_f32p, C.c_int, C.c_int, C.c_void_p, _f32p]
+        self._mm8 = getattr(L, p + "matmul_int8_row")
+        self._mm8.argtypes = [_f32p, _f32p, C.c_void_p, _f32p, C.c_int, C.c_int, C.c_int]
+        self._rms = getattr(L, p + "rmsnorm")
+        self._rms.argtypes = [_f32p, C.c_void_p, _f32p, C.c_int, C.c_float]
+        self._epi = getattr(L, "orc_moe_epilogue", None)  # the port only
+        if self._epi is not None:
+            self._epi.argtypes = [C.c_int, C.c_int, C.c_int, _f32p, C.c_void_p, C.c_float,
+                                  C.c_int, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, _f32p]
         for name in ("situ_glu", "clamped_swiglu", "sigmoid"):
             f = getattr(L, p + name)
             f.restype = C.c_float
@@ -138,6 +148,42 @@ class Oracle:
         y = np.zeros((S, O), np.float32)
         self._mmx(y, x, np.ascontiguousarray(p), np.ascontiguousarray(s), S, I, O)
         return y
+
+    def quantize_int8_row(self, w):
+        w = np.ascontiguousarray(w, np.float32)
+        O, I = w.shape
+        q = np.zeros((O, I), np.int8)
+        s = np.zeros(O, np.float32)
+        self._q8(w, O, I, q.ctypes.data, s)
+        return q, s
+
+    def matmul_int8_row(self, x, q, s, O):
+        x = np.ascontiguousarray(x, np.float32)
+        S, I = x.shape
+        y = np.zeros((S, O), np.float32)
+        q = np.ascontiguousarray(q, np.int8)
+        self._mm8(y, x, q.ctypes.data, np.ascontiguousarray(s, np.float32), S, I, O)
+        return y
+
+    def rmsnorm(self, x, w, eps):
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.zeros_like(x)
+        wp = None if w is None else np.ascontiguousarray(w, np.float32)
+        self._rms(x, None if wp is None else wp.ctypes.data, y, x.shape[0], eps)
+        return y
+
+    def moe_epilogue(self, acc, h, routed_scale, lat_n=None, eps=1e-6, up_fmt=0, up_w=None,
+                     up_scales=None, shared=None):
+        """Returns h + epilogue(acc) (kimi_k3.cpp:2074-2108 order); port only."""
+        acc = np.ascontiguousarray(acc, np.float32)
+        out = np.array(h, np.float32, copy=True)
+        T, L = acc.shape
+        H = out.shape[1]
+        keep = [None if a is None else np.ascontiguousarray(a) for a in
+                (lat_n, up_w, up_scales, shared)]
+        ptr = [None if a is None else a.ctypes.data for a in keep]
+        self._epi(T, H, L, acc, ptr[0], eps, up_fmt, ptr[1], ptr[2], routed_scale, ptr[3], out)
+        return out
 
     def situ_glu(self, g, u, b1, b2):
         return self._situ_glu(g, u, b1, b2)

@@ -56,6 +56,16 @@ REF_API void ref_matmul_mxfp4(float *y, const float *x, const uint8_t *p, const 
                               int I, int O) {
     mvllm::quant::matmul_mxfp4(y, x, p, s, S, I, O);
 }
+REF_API void ref_quantize_int8_row(const float *w, int O, int I, int8_t *q, float *s) {
+    mvllm::quant::quantize_int8_row(w, O, I, q, s);
+}
+REF_API void ref_matmul_int8_row(float *y, const float *x, const int8_t *q, const float *s, int S,
+                                 int I, int O) {
+    mvllm::quant::matmul_int8_row(y, x, q, s, S, I, O);
+}
+REF_API void ref_rmsnorm(const float *x, const float *w, float *y, int n, float eps) {
+    mvllm::quant::rmsnorm(x, w, y, n, eps);
+}
 REF_API float ref_situ_glu(float g, float u, float b1, float b2) {
     return mvllm::quant::situ_glu(g, u, b1, b2);
 }

@@ -1,0 +1,110 @@
+"""Layer epilogue after the routed combine (kimi_k3.cpp:2074-2108, glm53.cpp:1993-2027):
+rmsnorm of the routed sum, the latent up-projection (QuantMat fmt 0 / 4 / 8), the
+routed scale and the shared expert's output added to the residual stream.
+
+* CPU: the oracle's int8-row codec, rmsnorm and epilogue against the reference build
+  (bit-exact; the epilogue against the reference's own pieces composed in its order).
+* GPU: mvllm_moe_epilogue_dev and the int8-row mvllm_matmul_dev against the oracle.
+"""
+import numpy as np
+import pytest
+
+from conftest import assert_close
+
+torch = pytest.importorskip("torch")
+
+
+def _case(seed, T, H, L, up_fmt, norm, shared, port):
+    rng = np.random.default_rng(seed)
+    acc = rng.standard_normal((T, L)).astype(np.float32)
+    h = rng.standard_normal((T, H)).astype(np.float32)
+    lat_n = (1.0 + 0.1 * rng.standard_normal(L)).astype(np.float32) if norm else None
+    up_w = up_s = None
+    if up_fmt is not None:
+        w = (rng.standard_normal((H, L)) * (1.0 / np.sqrt(L))).astype(np.float32)
+        if up_fmt == 0:
+            up_w = w
+        elif up_fmt == 4:
+            up_w, up_s = port.quantize_int4_g64(w)
+        else:
+            up_w, up_s = port.quantize_int8_row(w)
+    sh = rng.standard_normal((T, H)).astype(np.float32) if shared else None
+    return acc, h, lat_n, up_w, up_s, sh
+
+
+CASES = [  # (T, H, L, up_fmt, norm, shared, routed_scale)
+    (5, 256, 256, None, False, True, 2.5),   # GLM: no latent, shared expert
+    (4, 256, 128, 8, True, True, 1.75),      # K3: norm, int8 up-projection, shared
+    (3, 192, 128, 4, True, False, 1.0),      # int4-g64 up-projection
+    (2, 160, 96, 0, False, True, 0.5),       # f32 up-projection, no norm
+]
+
+
+@pytest.mark.parametrize("T,H,L,fmt,norm,shared,scale", CASES)
+def test_epilogue_oracle_pinned(port, ref, T, H, L, fmt, norm, shared, scale):
+    acc, h, lat_n, up_w, up_s, sh = _case(T * 7 + H, T, H, L, fmt, norm, shared, port)
+    got = port.moe_epilogue(acc, h, scale, lat_n, 1e-6, 0 if fmt is None else fmt, up_w, up_s, sh)
+    # the reference's pieces in the reference's order
+    want = h.copy()
+    for c in range(T):
+        a = ref.rmsnorm(acc[c], lat_n, 1e-6) if norm else acc[c]
+        if fmt is None:
+            u = a
+        elif fmt == 0:
+            u = ref.matmul_f32(a[None], up_w)[0]
+        elif fmt == 4:
+            u = ref.matmul_int4_g64(a[None], up_w, up_s, H)[0]
+        else:
+            u = ref.matmul_int8_row(a[None], up_w, up_s, H)[0]
+        want[c] = (want[c] + (u * np.float32(scale)).astype(np.float32)).astype(np.float32)
+        if shared:
+            want[c] = (want[c] + sh[c]).astype(np.float32)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_int8_row_codec_pinned(port, ref):
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((40, 192)) * 0.05).astype(np.float32)
+    w[7] = 0.0  # a zero row: scale 0, all codes 0
+    qp, sp = port.quantize_int8_row(w)
+    qr, sr = ref.quantize_int8_row(w)
+    np.testing.assert_array_equal(qp, qr)
+    np.testing.assert_array_equal(sp, sr)
+    x = rng.standard_normal((3, 192)).astype(np.float32)
+    np.testing.assert_array_equal(port.matmul_int8_row(x, qp, sp, 40),
+                                  ref.matmul_int8_row(x, qr, sr, 40))
+    v = rng.standard_normal(777).astype(np.float32)
+    np.testing.assert_array_equal(port.rmsnorm(v, None, 1e-5), ref.rmsnorm(v, None, 1e-5))
+
+
+def _dev(a):
+    return None if a is None else torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T,H,L,fmt,norm,shared,scale", CASES + [(32, 7168, 2048, 8, True, True, 2.0)])
+def test_epilogue_dev(moe, port, T, H, L, fmt, norm, shared, scale):
+    acc, h, lat_n, up_w, up_s, sh = _case(T * 11 + L, T, H, L, fmt, norm, shared, port)
+    want = port.moe_epilogue(acc, h, scale, lat_n, 1e-6, 0 if fmt is None else fmt, up_w, up_s,
+                             sh)
+    hd = _dev(h)
+    ws = torch.empty(moe.epilogue_workspace_bytes(T, H, L), dtype=torch.uint8, device="cuda")
+    moe.epilogue_dev(_dev(acc), hd, scale, _dev(lat_n), 1e-6, 0 if fmt is None else fmt,
+                     _dev(up_w), _dev(up_s), _dev(sh), ws)
+    torch.cuda.synchronize()
+    assert_close(hd.cpu().numpy(), want, f"epilogue T={T} H={H} L={L} fmt={fmt}")
+    if fmt is None:  # no projection: every operation matches the reference's rounding
+        np.testing.assert_array_equal(hd.cpu().numpy(), want)
+
+
+@pytest.mark.gpu
+def test_matmul_int8_row_dev(moe, port):
+    rng = np.random.default_rng(9)
+    for S, I, O in ((1, 256, 40), (37, 512, 96)):  # 37 rows: two passes of 32
+        w = (rng.standard_normal((O, I)) * 0.05).astype(np.float32)
+        q, s = port.quantize_int8_row(w)
+        x = rng.standard_normal((S, I)).astype(np.float32)
+        y = torch.zeros((S, O), device="cuda")
+        moe.matmul_dev(8, y, _dev(x), _dev(q), _dev(s))
+        torch.cuda.synchronize()
+        assert_close(y.cpu().numpy(), port.matmul_int8_row(x, q, s, O), f"int8 {S}x{I}x{O}")
