@@ -9,7 +9,6 @@
 #include "ep_kernels.cuh"
 #include "route_kernels.cuh"
 #include "expert_tier.hpp"
-#include "host_copy.hpp"
 
 #include <cudaTypedefs.h>
 
@@ -1155,9 +1154,9 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     memcpy(hp + o_coff, csr_off.data(), csr_off.size() * 4);
     memcpy(hp + o_cids, csr_ids.data(), csr_ids.size() * 4);
     memcpy(hp + o_rw, rw, size_t(R) * 4);
-    host_copy(hp + o_x, xg, xb);
+    memcpy(hp + o_x, xg, xb);
     if (S_ext > 0)
-        host_copy(hp + o_out, out, ob);
+        memcpy(hp + o_out, out, ob);
 
     Carve dcv(nullptr, ~size_t(0));
     dcv.take<uint8_t>(up_bytes);
@@ -1219,7 +1218,7 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
     if (int rc2 = check_device_error(w.err, c.stream))
         return rc2; // `out` untouched: a rerun starts from the caller's rows
-    host_copy(out, hp + o_out, ob);
+    memcpy(out, hp + o_out, ob);
     float a = 0, b = 0, cc = 0;
     cudaEventElapsedTime(&a, c.ev[0], c.ev[1]);
     cudaEventElapsedTime(&b, c.ev[1], c.ev[2]);
@@ -1681,12 +1680,12 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     float *dout = reinterpret_cast<float *>(dptr(hout));
     LayerHooks hooks;
     hooks.before_gather = [&]() -> int {
-        host_copy(hx, x, x_b); // the permutation kernels run meanwhile
+        memcpy(hx, x, x_b); // the permutation kernels run meanwhile
         CUDA_TRY(cudaMemcpyAsync(db + x_off, hx, x_b, cudaMemcpyHostToDevice, c.stream));
         return MVLLM_OK;
     };
     hooks.before_combine = [&]() -> int {
-        host_copy(hout, out, x_b); // the expert kernels run meanwhile
+        memcpy(hout, out, x_b); // the expert kernels run meanwhile
         CUDA_TRY(cudaMemcpyAsync(dout, hout, x_b, cudaMemcpyHostToDevice, c.stream));
         return MVLLM_OK;
     };
@@ -1702,7 +1701,7 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
     if (int rc = check_device_error(l.run.err, c.stream))
         return rc; // `out` untouched: a rerun starts from the caller's rows
-    host_copy(out, hout, x_b);
+    memcpy(out, hout, x_b);
     float a = 0, b = 0, cc = 0;
     cudaEventElapsedTime(&a, c.ev[0], c.ev[1]);
     cudaEventElapsedTime(&b, c.ev[1], c.ev[2]);
