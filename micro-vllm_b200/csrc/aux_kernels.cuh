@@ -701,71 +701,85 @@ template <int PHASE> __global__ void __launch_bounds__(256) generic_ffn_kernel(c
 }
 
 // Generic dequantised GEMM y[S,O] = x[S,I] . W[O,I]^T (warp per output row).
-// y[S,O] = x[S,I] . W[O,I]^T: a warp per output row, up to 32 rows of x per
-// pass, so each weight element is read (and dequantised) once per 32 rows.
-// fmt 8 (int8 rows) sums x.q and applies the row scale at the end, as
-// quant::matmul_int8_row does.
+// y[S,O] = x[S,I] . W[O,I]^T, the reference's arithmetic per output
+// (quant.cpp:143-156, 203-228, 255-268, 298-321): acc += x[i] * w[i] in
+// ascending i, each product and sum rounded on its own, w = q * scale as the
+// reference decodes it; int8 rows (fmt 8) take the row scale at the end.  So
+// the result is bit-identical to the reference's matmuls.  A lane per row of
+// x (up to 32 per CTA column), a warp per 8 rows of W; K tiles of x staged in
+// shared memory, W read once per CTA (broadcast loads across the lanes).
+constexpr int kMmRows = 8;   // W rows per warp
+constexpr int kMmWarps = 8;  // warps per CTA
+constexpr int kMmKt = 128;   // K tile of x in shared memory
 __global__ void __launch_bounds__(256) matmul_generic_kernel(int fmt, float *y, const float *x,
                                                              const void *w, const void *sc,
                                                              int S, int I, int O) {
-    constexpr int kS = 32;
+    __shared__ float xs[32][kMmKt + 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int o = blockIdx.x * 8 + warp;
-    if (o >= O)
-        return;
-    for (int s0 = 0; s0 < S; s0 += kS) {
-        const int ns = min(kS, S - s0);
-        float acc[kS];
+    const int s0 = blockIdx.y * 32, ns = min(32, S - s0);
+    const int o0 = (blockIdx.x * kMmWarps + warp) * kMmRows;
+    float acc[kMmRows];
 #pragma unroll
-        for (int j = 0; j < kS; ++j)
-            acc[j] = 0.f;
-        for (int k = lane; k < I; k += 32) {
-            const float wv = fmt == MVLLM_FMT_INT8_ROW
-                                 ? static_cast<float>(
-                                       static_cast<const int8_t *>(w)[static_cast<size_t>(o) * I + k])
-                                 : deq_elem(w, sc, fmt, o, k, I);
-#pragma unroll
-            for (int j = 0; j < kS; ++j)
-                if (j < ns)
-                    acc[j] = fmaf(x[static_cast<size_t>(s0 + j) * I + k], wv, acc[j]);
+    for (int r = 0; r < kMmRows; ++r)
+        acc[r] = 0.f;
+    for (int k0 = 0; k0 < I; k0 += kMmKt) {
+        const int kn = min(kMmKt, I - k0);
+        __syncthreads();
+        for (int j = threadIdx.x; j < 32 * kMmKt; j += blockDim.x) {
+            const int s = j / kMmKt, k = j - s * kMmKt;
+            xs[s][k] = (s < ns && k < kn) ? x[static_cast<size_t>(s0 + s) * I + k0 + k] : 0.f;
         }
+        __syncthreads();
+        for (int kk = 0; kk < kn; ++kk) {
+            const float xv = xs[lane][kk];
 #pragma unroll
-        for (int j = 0; j < kS; ++j) {
-            if (j >= ns)
+            for (int r = 0; r < kMmRows; ++r) {
+                const int o = o0 + r;
+                if (o >= O)
+                    break;
+                const int k = k0 + kk;
+                const float wv =
+                    fmt == MVLLM_FMT_INT8_ROW
+                        ? static_cast<float>(
+                              static_cast<const int8_t *>(w)[static_cast<size_t>(o) * I + k])
+                        : deq_elem(w, sc, fmt, o, k, I);
+                acc[r] = __fadd_rn(acc[r], __fmul_rn(xv, wv));
+            }
+        }
+    }
+    if (lane < ns) {
+#pragma unroll
+        for (int r = 0; r < kMmRows; ++r) {
+            const int o = o0 + r;
+            if (o >= O)
                 break;
-            float a = acc[j];
-#pragma unroll
-            for (int m = 16; m > 0; m >>= 1)
-                a += __shfl_xor_sync(0xffffffffu, a, m);
-            if (lane == 0)
-                y[static_cast<size_t>(s0 + j) * O + o] =
-                    fmt == MVLLM_FMT_INT8_ROW ? a * static_cast<const float *>(sc)[o] : a;
+            y[static_cast<size_t>(s0 + lane) * O + o] =
+                fmt == MVLLM_FMT_INT8_ROW ? __fmul_rn(acc[r], static_cast<const float *>(sc)[o])
+                                          : acc[r];
         }
     }
 }
+inline dim3 matmul_grid(int S, int O) {
+    return dim3((O + kMmWarps * kMmRows - 1) / (kMmWarps * kMmRows), (S + 31) / 32);
+}
 
-// rmsnorm per row (quant.cpp:384-398): y = x * (1 / sqrt(mean(x^2) + eps)) * w,
-// the sum of squares as a tree (the reference sums sequentially: the norm
-// agrees to a few ulp).  One CTA per row.
+// rmsnorm per row, exactly as quant.cpp:384-398: the sum of squares in
+// ascending order on one thread (each product and sum rounded on its own),
+// inv = 1 / sqrt(ss / n + eps) with IEEE division and square root, then
+// y = x * inv * w.  One CTA per row.
 __global__ void rmsnorm_rows_kernel(const float *__restrict__ x, const float *__restrict__ w,
                                     float *__restrict__ y, int T, int n, float eps) {
-    __shared__ float part[32];
+    __shared__ float inv_s;
     for (int r = blockIdx.x; r < T; r += gridDim.x) {
         const float *xr = x + static_cast<size_t>(r) * n;
-        float ss = 0.f;
-        for (int i = threadIdx.x; i < n; i += blockDim.x)
-            ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
-#pragma unroll
-        for (int m = 16; m > 0; m >>= 1)
-            ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, m));
-        if ((threadIdx.x & 31) == 0)
-            part[threadIdx.x >> 5] = ss;
+        if (threadIdx.x == 0) {
+            float ss = 0.f;
+            for (int i = 0; i < n; ++i)
+                ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+            inv_s = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(n)), eps)));
+        }
         __syncthreads();
-        float tot = 0.f;
-        for (int j = 0; j < static_cast<int>(blockDim.x >> 5); ++j)
-            tot = __fadd_rn(tot, part[j]);
-        const float inv =
-            __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(n)), eps)));
+        const float inv = inv_s;
         float *yr = y + static_cast<size_t>(r) * n;
         for (int i = threadIdx.x; i < n; i += blockDim.x) {
             const float v = __fmul_rn(xr[i], inv);

@@ -1860,7 +1860,7 @@ int mvllm_matmul_dev(void *stream, int fmt, float *y, const float *x, const void
         return fail(MVLLM_ERR_INVALID, "matmul_dev: invalid arguments");
     if (!ctx().inited)
         return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
-    matmul_generic_kernel<<<(O + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    matmul_generic_kernel<<<matmul_grid(S, O), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         fmt, y, x, w, scales, S, I, O);
     CUDA_TRY(cudaGetLastError());
     return MVLLM_OK;
@@ -1899,8 +1899,8 @@ int mvllm_moe_epilogue_dev(void *stream, int T, int H, int L, const float *acc,
         src = norm;
     }
     if (up_w) {
-        matmul_generic_kernel<<<(H + 7) / 8, 256, 0, st>>>(up_fmt, up, src, up_w, up_scales, T, L,
-                                                           H);
+        matmul_generic_kernel<<<matmul_grid(T, H), 256, 0, st>>>(up_fmt, up, src, up_w,
+                                                                 up_scales, T, L, H);
         CUDA_TRY(cudaGetLastError());
         src = up;
     }
