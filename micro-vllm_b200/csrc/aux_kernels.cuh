@@ -766,16 +766,23 @@ inline dim3 matmul_grid(int S, int O) {
 // rmsnorm per row, exactly as quant.cpp:384-398: the sum of squares in
 // ascending order on one thread (each product and sum rounded on its own),
 // inv = 1 / sqrt(ss / n + eps) with IEEE division and square root, then
-// y = x * inv * w.  One CTA per row.
+// y = x * inv * w.  One CTA per row; the row is staged in shared memory
+// (n floats of dynamic shared memory) so the serial sum reads it at shared
+// latency, its squares computed by all threads first.
 __global__ void rmsnorm_rows_kernel(const float *__restrict__ x, const float *__restrict__ w,
                                     float *__restrict__ y, int T, int n, float eps) {
+    extern __shared__ float sq[];
     __shared__ float inv_s;
     for (int r = blockIdx.x; r < T; r += gridDim.x) {
         const float *xr = x + static_cast<size_t>(r) * n;
+        for (int i = threadIdx.x; i < n; i += blockDim.x)
+            sq[i] = __fmul_rn(xr[i], xr[i]);
+        __syncthreads();
         if (threadIdx.x == 0) {
             float ss = 0.f;
+#pragma unroll 8
             for (int i = 0; i < n; ++i)
-                ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+                ss = __fadd_rn(ss, sq[i]);
             inv_s = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(n)), eps)));
         }
         __syncthreads();

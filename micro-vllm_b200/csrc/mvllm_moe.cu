@@ -1894,7 +1894,13 @@ int mvllm_moe_epilogue_dev(void *stream, int T, int H, int L, const float *acc,
     float *norm = static_cast<float *>(workspace);
     float *up = norm ? norm + size_t(T) * L : nullptr;
     if (lat_n) {
-        rmsnorm_rows_kernel<<<std::min(T, 8 * c.sms), 256, 0, st>>>(acc, lat_n, norm, T, L, eps);
+        const size_t sm = size_t(L) * sizeof(float);
+        if (sm > 227 * 1024)
+            return fail(MVLLM_ERR_INVALID, "epilogue_dev: latent width %d too large", L);
+        if (sm > 48 * 1024)
+            CUDA_TRY(cudaFuncSetAttribute(rmsnorm_rows_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
+        rmsnorm_rows_kernel<<<std::min(T, 8 * c.sms), 256, sm, st>>>(acc, lat_n, norm, T, L, eps);
         CUDA_TRY(cudaGetLastError());
         src = norm;
     }
