@@ -706,18 +706,21 @@ template <int PHASE> __global__ void __launch_bounds__(256) generic_ffn_kernel(c
 // ascending i, each product and sum rounded on its own, w = q * scale as the
 // reference decodes it; int8 rows (fmt 8) take the row scale at the end.  So
 // the result is bit-identical to the reference's matmuls.  A lane per row of
-// x (up to 32 per CTA column), a warp per 8 rows of W; K tiles of x staged in
-// shared memory, W read once per CTA (broadcast loads across the lanes).
-constexpr int kMmRows = 8;   // W rows per warp
+// x (up to 32 per CTA column), a warp per kMmRows rows of W.  Each K tile of
+// x and of the CTA's W rows (decoded to f32) is staged in shared memory with
+// coalesced loads; the inner loop reads x per lane and W as a broadcast.
+constexpr int kMmRows = 4;   // W rows per warp
 constexpr int kMmWarps = 8;  // warps per CTA
-constexpr int kMmKt = 128;   // K tile of x in shared memory
+constexpr int kMmKt = 64;    // K tile
 __global__ void __launch_bounds__(256) matmul_generic_kernel(int fmt, float *y, const float *x,
                                                              const void *w, const void *sc,
                                                              int S, int I, int O) {
+    constexpr int RC = kMmWarps * kMmRows; // W rows per CTA
     __shared__ float xs[32][kMmKt + 1];
+    __shared__ float wsm[RC][kMmKt];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int s0 = blockIdx.y * 32, ns = min(32, S - s0);
-    const int o0 = (blockIdx.x * kMmWarps + warp) * kMmRows;
+    const int oc = blockIdx.x * RC; // the CTA's first W row
     float acc[kMmRows];
 #pragma unroll
     for (int r = 0; r < kMmRows; ++r)
@@ -729,33 +732,33 @@ __global__ void __launch_bounds__(256) matmul_generic_kernel(int fmt, float *y, 
             const int s = j / kMmKt, k = j - s * kMmKt;
             xs[s][k] = (s < ns && k < kn) ? x[static_cast<size_t>(s0 + s) * I + k0 + k] : 0.f;
         }
+        for (int j = threadIdx.x; j < RC * kMmKt; j += blockDim.x) {
+            const int r = j / kMmKt, k = j - r * kMmKt, o = oc + r;
+            float v = 0.f;
+            if (o < O && k < kn)
+                v = fmt == MVLLM_FMT_INT8_ROW
+                        ? static_cast<float>(static_cast<const int8_t *>(
+                              w)[static_cast<size_t>(o) * I + k0 + k])
+                        : deq_elem(w, sc, fmt, o, k0 + k, I);
+            wsm[r][k] = v;
+        }
         __syncthreads();
+#pragma unroll 4
         for (int kk = 0; kk < kn; ++kk) {
             const float xv = xs[lane][kk];
 #pragma unroll
-            for (int r = 0; r < kMmRows; ++r) {
-                const int o = o0 + r;
-                if (o >= O)
-                    break;
-                const int k = k0 + kk;
-                const float wv =
-                    fmt == MVLLM_FMT_INT8_ROW
-                        ? static_cast<float>(
-                              static_cast<const int8_t *>(w)[static_cast<size_t>(o) * I + k])
-                        : deq_elem(w, sc, fmt, o, k, I);
-                acc[r] = __fadd_rn(acc[r], __fmul_rn(xv, wv));
-            }
+            for (int r = 0; r < kMmRows; ++r)
+                acc[r] = __fadd_rn(acc[r], __fmul_rn(xv, wsm[warp * kMmRows + r][kk]));
         }
     }
     if (lane < ns) {
 #pragma unroll
         for (int r = 0; r < kMmRows; ++r) {
-            const int o = o0 + r;
-            if (o >= O)
-                break;
-            y[static_cast<size_t>(s0 + lane) * O + o] =
-                fmt == MVLLM_FMT_INT8_ROW ? __fmul_rn(acc[r], static_cast<const float *>(sc)[o])
-                                          : acc[r];
+            const int o = oc + warp * kMmRows + r;
+            if (o < O)
+                y[static_cast<size_t>(s0 + lane) * O + o] =
+                    fmt == MVLLM_FMT_INT8_ROW ? __fmul_rn(acc[r], static_cast<const float *>(sc)[o])
+                                              : acc[r];
         }
     }
 }
