@@ -725,41 +725,24 @@ __global__ void __launch_bounds__(256) matmul_generic_kernel(int fmt, float *y, 
 #pragma unroll
     for (int r = 0; r < kMmRows; ++r)
         acc[r] = 0.f;
-    // Each thread stages kPer elements of x and of W per tile; the next
-    // tile's elements are loaded into registers while the current one runs.
-    constexpr int kPer = 32 * kMmKt / 256;
-    static_assert(RC * kMmKt == 32 * kMmKt, "x and W tiles have the same size");
-    float px[kPer], pw[kPer];
-    auto fetch = [&](int k0) {
+    for (int k0 = 0; k0 < I; k0 += kMmKt) {
         const int kn = min(kMmKt, I - k0);
-#pragma unroll
-        for (int q = 0; q < kPer; ++q) {
-            const int j = threadIdx.x + q * 256;
-            const int s = j / kMmKt, k = j - s * kMmKt, o = oc + s;
-            px[q] = (s < ns && k < kn) ? x[static_cast<size_t>(s0 + s) * I + k0 + k] : 0.f;
+        __syncthreads();
+        for (int j = threadIdx.x; j < 32 * kMmKt; j += blockDim.x) {
+            const int s = j / kMmKt, k = j - s * kMmKt;
+            xs[s][k] = (s < ns && k < kn) ? x[static_cast<size_t>(s0 + s) * I + k0 + k] : 0.f;
+        }
+        for (int j = threadIdx.x; j < RC * kMmKt; j += blockDim.x) {
+            const int r = j / kMmKt, k = j - r * kMmKt, o = oc + r;
             float v = 0.f;
             if (o < O && k < kn)
                 v = fmt == MVLLM_FMT_INT8_ROW
                         ? static_cast<float>(static_cast<const int8_t *>(
                               w)[static_cast<size_t>(o) * I + k0 + k])
                         : deq_elem(w, sc, fmt, o, k0 + k, I);
-            pw[q] = v;
-        }
-    };
-    fetch(0);
-    for (int k0 = 0; k0 < I; k0 += kMmKt) {
-        const int kn = min(kMmKt, I - k0);
-        __syncthreads();
-#pragma unroll
-        for (int q = 0; q < kPer; ++q) {
-            const int j = threadIdx.x + q * 256;
-            const int s = j / kMmKt, k = j - s * kMmKt;
-            xs[s][k] = px[q];
-            wsm[s][k] = pw[q];
+            wsm[r][k] = v;
         }
         __syncthreads();
-        if (k0 + kMmKt < I)
-            fetch(k0 + kMmKt);
 #pragma unroll 4
         for (int kk = 0; kk < kn; ++kk) {
             const float xv = xs[lane][kk];
