@@ -783,16 +783,26 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
             const int orow = __ldg(p.orow + it.e) + it.t0;
             const uint32_t accb =
                 tmem + lane_addr + (b == 1 ? static_cast<uint32_t>(C::ACC_HALF) : 0u);
-#pragma unroll 1
-            for (int ch = 32 * whalf; ch < it.n; ch += CH_STEP) {
-                uint32_t v[32];
+            // The accumulator is released as soon as it has been read, so the
+            // next tile's MMAs need not wait for the global stores: phase 1
+            // keeps every chunk's activations in registers (two tokens per
+            // word) and stores them after the release; phase 2 stores the rows
+            // of all chunks but the last as they are read, and the last after
+            // the release.
+            constexpr int MAXCH = (C::NT + CH_STEP - 1) / CH_STEP;
+            uint32_t hpk[PHASE == 1 ? MAXCH * 8 : 1];
+            uint32_t v[32];
+            int nch = 0;
+            const bool gate = lane < 16;
+#pragma unroll
+            for (int j = 0; j < MAXCH; ++j) {
+                const int ch = 32 * whalf + j * CH_STEP;
+                if (ch >= it.n)
+                    break;
                 tc_ld32(accb + ch, v);
                 tc_wait_ld();
+                ++nch;
                 if (PHASE == 1) {
-                    const bool gate = lane < 16;
-                    const int col = it.c0 + static_cast<int>(rank) * 64 + 16 * q + (lane & 15);
-                    const int tb = ch + (gate ? 0 : 16);
-                    __half *hp = static_cast<__half *>(p.out);
 #pragma unroll
                     for (int t = 0; t < 16; ++t) {
                         const float mine_lo = __uint_as_float(v[t]);
@@ -801,12 +811,14 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                             __shfl_xor_sync(0xffffffffu, gate ? mine_hi : mine_lo, 16);
                         const float g = gate ? mine_lo : other;
                         const float u = gate ? other : mine_hi;
-                        if (tb + t < it.n)
-                            hp[static_cast<size_t>(orow + tb + t) * p.O + stage_pos(col, FMT)] =
-                                __float2half_rn(
-                                    apply_act_fast(g, u, p.act, p.act_a, p.act_b, ia, ib));
+                        const uint32_t hb = __half_as_ushort(__float2half_rn(
+                            apply_act_fast(g, u, p.act, p.act_a, p.act_b, ia, ib)));
+                        if (t & 1)
+                            hpk[j * 8 + (t >> 1)] |= hb << 16;
+                        else
+                            hpk[j * 8 + (t >> 1)] = hb;
                     }
-                } else {
+                } else if (ch + CH_STEP < it.n) {
                     float *yp = static_cast<float *>(p.out);
                     const int col = it.c0 + static_cast<int>(rank) * 128 + 32 * q + lane;
 #pragma unroll
@@ -827,6 +839,30 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                     else
                         mbar_arrive(&acc_empty[h]);
                 }
+            }
+            if (PHASE == 1) {
+                const int col = it.c0 + static_cast<int>(rank) * 64 + 16 * q + (lane & 15);
+                __half *hp = static_cast<__half *>(p.out);
+#pragma unroll
+                for (int j = 0; j < MAXCH; ++j) {
+                    if (j >= nch)
+                        break;
+                    const int tb = 32 * whalf + j * CH_STEP + (gate ? 0 : 16);
+#pragma unroll
+                    for (int t = 0; t < 16; ++t)
+                        if (tb + t < it.n)
+                            hp[static_cast<size_t>(orow + tb + t) * p.O + stage_pos(col, FMT)] =
+                                __ushort_as_half(static_cast<unsigned short>(
+                                    hpk[j * 8 + (t >> 1)] >> (16 * (t & 1))));
+                }
+            } else if (nch > 0) {
+                const int ch = 32 * whalf + (nch - 1) * CH_STEP;
+                float *yp = static_cast<float *>(p.out);
+                const int col = it.c0 + static_cast<int>(rank) * 128 + 32 * q + lane;
+#pragma unroll
+                for (int t = 0; t < 32; ++t)
+                    if (ch + t < it.n)
+                        yp[static_cast<size_t>(orow + ch + t) * p.O + col] = __uint_as_float(v[t]);
             }
             if (b != 1)
                 ++acc.use[0];
