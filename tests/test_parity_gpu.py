@@ -196,13 +196,23 @@ def test_matmul_dev(moe, port):
         assert np.allclose(y.cpu().numpy(), want, atol=1e-4, rtol=1e-4)
 
 
-def _full_size(moe, port, D, I, E, K, T, fmt, act, a, b, n_shared, check_tokens, seed):
+def _full_size(moe, port, D, I, E, K, T, fmt, act, a, b, n_shared, check_tokens, seed,
+               zipf=False):
     """Full BASELINE shapes: weights generated and packed on the GPU for the
     experts the routing touches; the oracle checks a sample of tokens (tokens
-    are independent, so any subset is a complete check of those rows)."""
+    are independent, so any subset is a complete check of those rows).
+    `zipf`: config[3]'s skewed routing (softmax of -1.1 ln(rank) + Gumbel noise,
+    then the reference's top-k), so the tensor-core tiles of every size run."""
     g = torch.Generator(device="cuda").manual_seed(seed)
     rng = np.random.default_rng(seed)
-    choice = rng.random((T, E), dtype=np.float32)
+    if zipf:
+        rank = rng.permutation(E) + 1
+        logits = -1.1 * np.log(rank)[None, :] - np.log(-np.log(rng.random((T, E)) + 1e-20))
+        logits = logits - logits.max(axis=1, keepdims=True)
+        p = np.exp(logits)
+        choice = (p / p.sum(axis=1, keepdims=True)).astype(np.float32)
+    else:
+        choice = rng.random((T, E), dtype=np.float32)
     idx, wt = cases.route(port, choice, K)
     x = cases.bf16_round(rng.standard_normal((T, D)).astype(np.float32))
     used = sorted(set(idx.reshape(-1).tolist())) + ([E] if n_shared else [])
@@ -259,6 +269,14 @@ def test_full_size_config1_mxfp4(moe, port):
 
 def test_full_size_config2_int4(moe, port):
     _full_size(moe, port, 6144, 1536, 160, 8, 16, 4, cases.ACT_CLAMP, 7.0, 0.0, 0, [3, 15], 22)
+
+
+def test_full_size_config3_prefill(moe, port):
+    """config[3]: 4096 tokens over 256 MXFP4 experts, Zipf routing: 256-row pair
+    tiles, ragged pair tiles, single-CTA tiles and the decode kernels for the
+    smallest experts, all in one call; sampled tokens against the oracle."""
+    _full_size(moe, port, 7168, 2048, 256, 8, 4096, 7, cases.ACT_SITU, 4.0, 25.0, 0,
+               [0, 1234, 4095], 23, zipf=True)
 
 
 def test_combine_linearity(moe, port):
