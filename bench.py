@@ -738,6 +738,10 @@ def main():
         wt_h.append(wt.cpu().numpy())
         x_h.append(x.float().cpu().numpy())
     out_h = np.zeros((B, CFG["D"]), np.float32)
+    # The caller's activation and output rows live in page-locked memory (as a
+    # serving engine's I/O buffers do): registered once, copied directly.
+    for a in x_h + [out_h]:
+        moe.host_register(a)
     for i in range(3):
         moe.layer_host(B, CFG["K"], CFG["E"], CFG["n_shared"], CFG["D"], CFG["I"], CFG["fmt"],
                        idx_h[i], wt_h[i], x_h[i], wl.host_tables, out_h, CFG["act"],
@@ -750,6 +754,8 @@ def main():
                        idx_h[i % N_INPUTS], wt_h[i % N_INPUTS], x_h[i % N_INPUTS],
                        wl.host_tables, out_h, CFG["act"], CFG["act_a"], CFG["act_b"])
     e2e_s = time.perf_counter() - t0
+    for a in x_h + [out_h]:
+        moe.host_unregister(a)
     t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -844,7 +850,8 @@ def main():
             # build, decode phase 1, decode phase 2, combine
             "gpu_launches": 8 * args.steps,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "api": "mvllm_moe_layer_host"},
+                    "d2h_bytes_per_step": d2h, "api": "mvllm_moe_layer_host",
+                    "host_buffers": "caller x / out page-locked with mvllm_moe_host_register"},
             "cpu_baseline": cpu,
             "clocks": clk.report(),
             "sweep": sweep,

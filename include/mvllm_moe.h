@@ -101,6 +101,14 @@ MVLLM_API int mvllm_moe_cache_unregister(const void *host);
 MVLLM_API void mvllm_moe_cache_clear(void);
 MVLLM_API size_t mvllm_moe_cache_bytes(void);
 
+/* Page-locks a caller buffer (cudaHostRegister) for the host-pointer entries:
+ * mvllm_moe_layer_host copies x and out that lie inside registered buffers
+ * straight to and from the device instead of through its pinned staging
+ * copy.  The buffer must stay allocated until mvllm_moe_host_unregister (or
+ * mvllm_moe_shutdown).  Registered buffers may not overlap. */
+MVLLM_API int mvllm_moe_host_register(void *host, size_t bytes);
+MVLLM_API int mvllm_moe_host_unregister(void *host);
+
 /* ---- device expert tier: the VRAM level above an ExpertStore
  *      (src/store/expert_store.hpp:59-175, expert_store.cpp:273-405).
  *      A budget of equal VRAM slots holds copies of bound host blobs, least

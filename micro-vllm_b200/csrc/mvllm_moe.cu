@@ -57,6 +57,7 @@ struct Context {
     // Device expert tier: bound host blobs, streamed into equal VRAM slots.
     TierPolicy tier;
     void *tier_arena = nullptr;
+    std::map<uintptr_t, size_t> host_reg; // caller buffers page-locked by host_register
     cudaStream_t copy_stream = nullptr; // stream-ins of cold blobs
     cudaEvent_t copy_done = nullptr;
     uint64_t calls = 0, experts = 0, rows = 0;
@@ -612,6 +613,16 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     return MVLLM_OK;
 }
 
+// [p, p + n) lies inside a buffer the caller page-locked with host_register.
+bool host_registered(const Context &c, const void *p, size_t n) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    auto it = c.host_reg.upper_bound(a);
+    if (it == c.host_reg.begin())
+        return false;
+    --it;
+    return a >= it->first && a + n <= it->first + it->second;
+}
+
 int check_device_error(const int *err_dev, cudaStream_t st) {
     int err = 0;
     CUDA_TRY(cudaMemcpyAsync(&err, err_dev, sizeof(int), cudaMemcpyDeviceToHost, st));
@@ -768,6 +779,9 @@ void mvllm_moe_shutdown(void) {
         cudaFree(c.tier_arena);
     c.tier_arena = nullptr;
     c.tier.configure(0, 0);
+    for (auto &kv : c.host_reg)
+        cudaHostUnregister(reinterpret_cast<void *>(kv.first));
+    c.host_reg.clear();
     if (c.ws.p)
         cudaFree(c.ws.p);
     if (c.transient.p)
@@ -887,6 +901,44 @@ size_t mvllm_moe_cache_bytes(void) {
     Context &c = ctx();
     std::lock_guard<std::mutex> lk(c.mu);
     return c.cache_bytes;
+}
+
+// ------------------------------------------------ page-locked caller buffers --
+int mvllm_moe_host_register(void *host, size_t bytes) {
+    if (!host || bytes == 0)
+        return fail(MVLLM_ERR_INVALID, "host_register: null pointer or zero size");
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (int rc = ensure_current(c))
+        return rc;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(host);
+    auto it = c.host_reg.find(a);
+    if (it != c.host_reg.end() && it->second == bytes)
+        return MVLLM_OK;
+    for (auto &kv : c.host_reg)
+        if (kv.first < a + bytes && a < kv.first + kv.second)
+            return fail(MVLLM_ERR_INVALID, "host_register: overlaps a registered buffer");
+    if (cudaHostRegister(host, bytes, cudaHostRegisterDefault) != cudaSuccess) {
+        const cudaError_t e = cudaGetLastError();
+        return fail(MVLLM_ERR_CUDA, "host_register: %s", cudaGetErrorString(e));
+    }
+    c.host_reg[a] = bytes;
+    return MVLLM_OK;
+}
+
+int mvllm_moe_host_unregister(void *host) {
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    auto it = c.host_reg.find(reinterpret_cast<uintptr_t>(host));
+    if (it == c.host_reg.end())
+        return fail(MVLLM_ERR_INVALID, "host_unregister: buffer not registered");
+    if (c.inited) {
+        cudaSetDevice(c.device);
+        cudaStreamSynchronize(c.stream);
+    }
+    cudaHostUnregister(host);
+    c.host_reg.erase(it);
+    return MVLLM_OK;
 }
 
 // ----------------------------------------------------- device expert tier --
@@ -1678,13 +1730,24 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     void *const *dt = reinterpret_cast<void *const *>(dptr(htab));
     Tables tb{dt, dt + EE, dt + 2 * EE, dt + 3 * EE, dt + 4 * EE, dt + 5 * EE};
     float *dout = reinterpret_cast<float *>(dptr(hout));
+    // Caller buffers page-locked with mvllm_moe_host_register are copied
+    // straight to and from the device; others go through the pinned staging.
+    const bool x_reg = host_registered(c, x, x_b), out_reg = host_registered(c, out, x_b);
     LayerHooks hooks;
     hooks.before_gather = [&]() -> int {
+        if (x_reg) {
+            CUDA_TRY(cudaMemcpyAsync(db + x_off, x, x_b, cudaMemcpyHostToDevice, c.stream));
+            return MVLLM_OK;
+        }
         memcpy(hx, x, x_b); // the permutation kernels run meanwhile
         CUDA_TRY(cudaMemcpyAsync(db + x_off, hx, x_b, cudaMemcpyHostToDevice, c.stream));
         return MVLLM_OK;
     };
     hooks.before_combine = [&]() -> int {
+        if (out_reg) {
+            CUDA_TRY(cudaMemcpyAsync(dout, out, x_b, cudaMemcpyHostToDevice, c.stream));
+            return MVLLM_OK;
+        }
         memcpy(hout, out, x_b); // the expert kernels run meanwhile
         CUDA_TRY(cudaMemcpyAsync(dout, hout, x_b, cudaMemcpyHostToDevice, c.stream));
         return MVLLM_OK;
@@ -1696,12 +1759,22 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
         cudaStreamSynchronize(c.stream); // no copy may still read the staging buffer
         return rc;
     }
-    CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
-    CUDA_TRY(cudaMemcpyAsync(hout, dout, x_b, cudaMemcpyDeviceToHost, c.stream));
-    CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
-    if (int rc = check_device_error(l.run.err, c.stream))
-        return rc; // `out` untouched: a rerun starts from the caller's rows
-    memcpy(out, hout, x_b);
+    if (out_reg) {
+        // The error word first: on an error `out` must stay untouched.
+        if (int rc = check_device_error(l.run.err, c.stream))
+            return rc;
+        CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
+        CUDA_TRY(cudaMemcpyAsync(out, dout, x_b, cudaMemcpyDeviceToHost, c.stream));
+        CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
+        CUDA_TRY(cudaStreamSynchronize(c.stream));
+    } else {
+        CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
+        CUDA_TRY(cudaMemcpyAsync(hout, dout, x_b, cudaMemcpyDeviceToHost, c.stream));
+        CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
+        if (int rc = check_device_error(l.run.err, c.stream))
+            return rc; // `out` untouched: a rerun starts from the caller's rows
+        memcpy(out, hout, x_b);
+    }
     float a = 0, b = 0, cc = 0;
     cudaEventElapsedTime(&a, c.ev[0], c.ev[1]);
     cudaEventElapsedTime(&b, c.ev[1], c.ev[2]);

@@ -40,7 +40,8 @@ C_SYMBOLS = (
     "mvllm_moe_ep_combine_dev", "mvllm_moe_topk_dev", "mvllm_moe_route_dev",
     "mvllm_moe_ep_combine16_dev", "mvllm_moe_layer_partial_dev", "mvllm_moe_tier_configure",
     "mvllm_moe_expert_bind", "mvllm_moe_expert_unbind", "mvllm_moe_tier_stats",
-    "mvllm_moe_epilogue_workspace", "mvllm_moe_epilogue_dev",
+    "mvllm_moe_epilogue_workspace", "mvllm_moe_epilogue_dev", "mvllm_moe_host_register",
+    "mvllm_moe_host_unregister",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -95,6 +96,8 @@ def lib():
             "mvllm_moe_ep_combine_dev": (i, [vp, vp, vp, i, i, i, vp]),
             "mvllm_moe_ep_combine16_dev": (i, [vp, vp, vp, i, i, i, vp]),
             "mvllm_moe_tier_configure": (i, [sz, sz]),
+            "mvllm_moe_host_register": (i, [vp, sz]),
+            "mvllm_moe_host_unregister": (i, [vp]),
             "mvllm_moe_epilogue_workspace": (sz, [i, i, i]),
             "mvllm_moe_epilogue_dev": (i, [vp, i, i, i, vp, vp, f, i, vp, vp, f, vp, vp, vp, sz]),
             "mvllm_moe_expert_bind": (i, [vp, sz, C.c_uint64]),
@@ -186,6 +189,15 @@ def moe_block(nb, D, Iinter, fmt, g, u, d, gs, us, ds, xg, xoff, nr, rows, rw, o
         return False
     _check(rc)
     return True
+
+
+def host_register(arr: np.ndarray) -> None:
+    """Page-locks a host array for the host-pointer entries (see the header)."""
+    _check(lib().mvllm_moe_host_register(arr.ctypes.data, arr.nbytes))
+
+
+def host_unregister(arr: np.ndarray) -> None:
+    _check(lib().mvllm_moe_host_unregister(arr.ctypes.data))
 
 
 def tier_configure(budget_bytes: int, slot_bytes: int) -> None:

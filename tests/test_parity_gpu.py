@@ -279,6 +279,33 @@ def test_full_size_config3_prefill(moe, port):
                [0, 1234, 4095], 23, zipf=True)
 
 
+def test_layer_host_registered_buffers(moe, port, golden):
+    """mvllm_moe_layer_host with the caller's x / out page-locked (direct copies)
+    gives the same bits as through the pinned staging copy."""
+    c = cases.make_layer(port, "small_mxfp4")
+    keep, tabs = [], [[], [], [], [], [], []]
+    for (gp, gsc), (up, usc), (dp, dsc) in c["experts"]:
+        for k, a in enumerate((gp, up, dp, gsc, usc, dsc)):
+            t = dev(a)
+            keep.append(t)
+            tabs[k].append(t.data_ptr())
+    T, D = c["T"], c["D"]
+    args = (T, c["K"], c["E"], c["n_shared"], D, c["I"], c["fmt"], c["idx"], c["wt"])
+    x = np.ascontiguousarray(c["x"], np.float32)
+    base = np.random.default_rng(5).standard_normal((T, D)).astype(np.float32)
+    out_a = base.copy()
+    moe.layer_host(*args, x, tabs, out_a, c["act"], c["act_a"], c["act_b"])
+    x_r, out_b = x.copy(), base.copy()
+    moe.host_register(x_r)
+    moe.host_register(out_b)
+    try:
+        moe.layer_host(*args, x_r, tabs, out_b, c["act"], c["act_a"], c["act_b"])
+    finally:
+        moe.host_unregister(x_r)
+        moe.host_unregister(out_b)
+    np.testing.assert_array_equal(out_b, out_a)
+
+
 def test_combine_linearity(moe, port):
     """Doubling every routing weight doubles the routed output exactly."""
     c = cases.make_layer(port, "small_int4")
