@@ -314,17 +314,20 @@ def tier_bench(moe, torch, wl, steps):
     for (idx, wt, x) in wl.inputs:
         ih, wh, xh = idx.cpu().numpy(), wt.cpu().numpy(), x.float().cpu().numpy()
         ids, nr, xoff, rows, rw = host_routing(ih, wh, E, ns > 0)
-        batches.append((ids, nr, xoff, rows, rw, np.ascontiguousarray(xh[rows])))
+        # the caller's six pointer arrays for the batch, built once
+        ptrs = [np.array([views[e][k].ctypes.data for e in ids], np.int64) for k in range(6)]
+        batches.append((ids, nr, xoff, rows, rw, np.ascontiguousarray(xh[rows]), ptrs))
     out = np.zeros((wl.B, D), np.float32)
+    # activation rows and the output in page-locked memory, as the engine's I/O buffers
+    for b in batches:
+        moe.host_register(b[5])
+    moe.host_register(out)
 
     def call(b):
-        ids, nr, xoff, rows, rw, xg = b
-        v = [views[e] for e in ids]
+        ids, nr, xoff, rows, rw, xg, ptrs = b
         out[:] = 0
-        moe.moe_block(len(ids), D, I, CFG["fmt"], [a[0] for a in v], [a[1] for a in v],
-                      [a[2] for a in v], [a[3] for a in v], [a[4] for a in v],
-                      [a[5] for a in v], xg, xoff, nr, rows, rw, out, wl.B, CFG["act"],
-                      CFG["act_a"], CFG["act_b"])
+        moe.moe_block(len(ids), D, I, CFG["fmt"], *ptrs, xg, xoff, nr, rows, rw, out, wl.B,
+                      CFG["act"], CFG["act_a"], CFG["act_b"])
 
     res = {"blob_bytes": blob, "experts": EE, "batch": wl.B,
            "pinned_h2d_gbs": pinned_h2d_gbs(torch)}
@@ -358,6 +361,9 @@ def tier_bench(moe, torch, wl, steps):
             for e in range(EE):
                 moe.expert_unbind(hn[e])
         moe.tier_configure(0, 0)
+    for b in batches:
+        moe.host_unregister(b[5])
+    moe.host_unregister(out)
     del host
     return res
 

@@ -1206,8 +1206,13 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     memcpy(hp + o_coff, csr_off.data(), csr_off.size() * 4);
     memcpy(hp + o_cids, csr_ids.data(), csr_ids.size() * 4);
     memcpy(hp + o_rw, rw, size_t(R) * 4);
-    memcpy(hp + o_x, xg, xb);
-    if (S_ext > 0)
+    // Caller rows page-locked with mvllm_moe_host_register go straight to
+    // the device; the others through the pinned staging buffer.
+    const bool x_reg = host_registered(c, xg, xb);
+    const bool out_reg = S_ext > 0 && host_registered(c, out, ob);
+    if (!x_reg)
+        memcpy(hp + o_x, xg, xb);
+    if (S_ext > 0 && !out_reg)
         memcpy(hp + o_out, out, ob);
 
     Carve dcv(nullptr, ~size_t(0));
@@ -1222,7 +1227,12 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     carve_run(dcv2, w, nb, D, Iinter, fast, R, int(x_rows));
 
     CUDA_TRY(cudaEventRecord(c.ev[0], c.stream));
-    CUDA_TRY(cudaMemcpyAsync(db, hp, up_bytes, cudaMemcpyHostToDevice, c.stream));
+    CUDA_TRY(cudaMemcpyAsync(db, hp, o_x, cudaMemcpyHostToDevice, c.stream));
+    CUDA_TRY(cudaMemcpyAsync(db + o_x, x_reg ? static_cast<const void *>(xg) : hp + o_x, xb,
+                             cudaMemcpyHostToDevice, c.stream));
+    if (S_ext > 0)
+        CUDA_TRY(cudaMemcpyAsync(db + o_out, out_reg ? static_cast<const void *>(out) : hp + o_out,
+                                 ob, cudaMemcpyHostToDevice, c.stream));
     CUDA_TRY(cudaMemsetAsync(w.err, 0, sizeof(int), c.stream));
     CUDA_TRY(cudaEventRecord(c.ev[1], c.stream));
     prof_mark(c.stream, kPhStart);
@@ -1265,12 +1275,22 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
         CUDA_TRY(cudaGetLastError());
         prof_mark(c.stream, kPhCombine);
     }
-    CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
-    CUDA_TRY(cudaMemcpyAsync(hp + o_out, d_out, ob, cudaMemcpyDeviceToHost, c.stream));
-    CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
-    if (int rc2 = check_device_error(w.err, c.stream))
-        return rc2; // `out` untouched: a rerun starts from the caller's rows
-    memcpy(out, hp + o_out, ob);
+    if (out_reg) {
+        // The error word first: on an error `out` must stay untouched.
+        if (int rc2 = check_device_error(w.err, c.stream))
+            return rc2;
+        CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
+        CUDA_TRY(cudaMemcpyAsync(out, d_out, ob, cudaMemcpyDeviceToHost, c.stream));
+        CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
+        CUDA_TRY(cudaStreamSynchronize(c.stream));
+    } else {
+        CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
+        CUDA_TRY(cudaMemcpyAsync(hp + o_out, d_out, ob, cudaMemcpyDeviceToHost, c.stream));
+        CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
+        if (int rc2 = check_device_error(w.err, c.stream))
+            return rc2; // `out` untouched: a rerun starts from the caller's rows
+        memcpy(out, hp + o_out, ob);
+    }
     float a = 0, b = 0, cc = 0;
     cudaEventElapsedTime(&a, c.ev[0], c.ev[1]);
     cudaEventElapsedTime(&b, c.ev[1], c.ev[2]);

@@ -166,8 +166,12 @@ def _p(a):
 
 
 def _parr(arrs):
+    """Pointer array for the C ABI: a list of numpy arrays (their data
+    pointers), or a contiguous int64 numpy array of addresses passed in place."""
     if arrs is None:
         return None
+    if isinstance(arrs, np.ndarray) and arrs.dtype in (np.int64, np.uint64) and arrs.ndim == 1:
+        return C.cast(arrs.ctypes.data, C.POINTER(C.c_void_p))
     out = (C.c_void_p * len(arrs))()
     for k, a in enumerate(arrs):
         out[k] = None if a is None else a.ctypes.data

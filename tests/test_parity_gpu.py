@@ -306,6 +306,26 @@ def test_layer_host_registered_buffers(moe, port, golden):
     np.testing.assert_array_equal(out_b, out_a)
 
 
+def test_moe_block_registered_buffers(moe, port):
+    """mvllm_moe_block with the caller's xg / out page-locked (direct copies)
+    gives the same bits as through the pinned staging copy."""
+    c = cases.make_layer(port, "small_int4")
+    ok, want = run_host_block(moe, c)
+    assert ok
+    xg = np.ascontiguousarray(c["xg"], np.float32).copy()
+    out = np.zeros((max(c["S"], 1), c["D"]), np.float32)
+    moe.host_register(xg)
+    moe.host_register(out)
+    try:
+        assert moe.moe_block(c["nb"], c["D"], c["I"], c["fmt"], c["g"], c["u"], c["d"], c["gs"],
+                             c["us"], c["ds"], xg, c["xoff"], c["nr"], c["rows"], c["rw"], out,
+                             c["S"], c["act"], c["act_a"], c["act_b"])
+    finally:
+        moe.host_unregister(xg)
+        moe.host_unregister(out)
+    np.testing.assert_array_equal(out, want)
+
+
 def test_combine_linearity(moe, port):
     """Doubling every routing weight doubles the routed output exactly."""
     c = cases.make_layer(port, "small_int4")
