@@ -1113,8 +1113,12 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     const size_t gus_b = size_t(Iinter) * scale_row_bytes(fmt, D);
     const size_t ds_b = size_t(D) * scale_row_bytes(fmt, Iinter);
     Resolver rs(c);
-    if (c.tier_arena)
+    if (c.tier_arena) {
         c.tier.begin_call();
+        // Slots filled by an earlier call that returned early (an error after
+        // its copies were issued) are complete before this call reads them.
+        CUDA_TRY(cudaStreamWaitEvent(c.stream, c.copy_done, 0));
+    }
     std::vector<void *> tdev(size_t(6) * nb, nullptr);
     std::vector<long> tidx(size_t(6) * nb, -1);
     std::vector<char> late(size_t(nb), 0); // weights arrive with the tier's stream-in copies
