@@ -60,7 +60,15 @@ enum { MVLLM_FMT_F32 = 0, MVLLM_FMT_INT4_G64 = 4, MVLLM_FMT_MXFP4 = 7 };
 /* int8 with one f32 scale per row: QuantMat fmt 8 (src/quant/weight.cpp:37-40,
  * quant.cpp:230-268); accepted by mvllm_matmul_dev and the layer epilogue. */
 enum { MVLLM_FMT_INT8_ROW = 8 };
+/* e4m3fn bytes [O, I] with one ue8m0 scale byte per 128 x 128 tile, scales
+ * [ceil(O/128), ceil(I/128)]: DeepSeek-V4's FP8 tensors (dsv4_cuda.hpp:45-46,
+ * dequant dsv4_cuda.cpp:127-135).  Accepted by mvllm_matmul_dev and
+ * mvllm_moe_dense_ffn_dev. */
+enum { MVLLM_FMT_FP8_B128 = 9 };
 enum { MVLLM_DTYPE_F32 = 0, MVLLM_DTYPE_BF16 = 1 };
+/* Router score functions: sigmoid (GLM, Kimi K3: quant.hpp:22-29) and
+ * sqrt(softplus) (DeepSeek-V4: dsv4_cuda.cpp:26-34). */
+enum { MVLLM_SCORE_SIGMOID = 0, MVLLM_SCORE_SQRT_SOFTPLUS = 1 };
 
 /* ---- lifecycle: metal_ops::init/shutdown/available/backend_name
  *      (src/gpu/metal_ops.hpp:15-18); coli_cuda::init (coli_cuda.hpp:25) ---- */
@@ -224,8 +232,9 @@ MVLLM_API int mvllm_pack_mxfp4_dev(void *stream, const float *w, int O, int I, u
 /* Dequantised GEMM y[S,O] = x[S,I] . W[O,I]^T on device (f32 in/out): the
  * role of coli_cuda::matmul / matmul_mxfp4 (src/gpu/coli_cuda.hpp:58-61) and
  * quant::matmul_* (src/quant/quant.hpp:53-70).  fmt 0, 4, 7 or 8 (int8 rows:
- * y = (sum x.q) x scale[o], quant.cpp:255-268).  Each weight row is read once
- * for up to 32 rows of x. */
+ * y = (sum x.q) x scale[o], quant.cpp:255-268), or 9 (FP8 tiles: the sum of
+ * x[i] * (e4m3fn(q) * 2^(s-127)), dsv4_cuda.cpp:618-623).  Each weight row is
+ * read once for up to 32 rows of x. */
 MVLLM_API int mvllm_matmul_dev(void *stream, int fmt, float *y, const float *x, const void *w,
                      const void *scales, int S, int I, int O);
 
@@ -245,6 +254,16 @@ MVLLM_API int mvllm_moe_topk_dev(void *stream, const float *choice, const float 
 MVLLM_API int mvllm_moe_route_dev(void *stream, const void *x, int x_dtype, int T, int H,
                                   const float *router, const float *bias, int E, int K, int *idx,
                                   float *wt, float *scores, float *choice);
+/* The same with the score function chosen (MVLLM_SCORE_*) and every weight
+ * multiplied by routed_scale at the end.  score_fn MVLLM_SCORE_SQRT_SOFTPLUS,
+ * K 6 is DeepSeek-V4's dsv4_cuda::route (dsv4_cuda.cpp:1541-1587, without
+ * fixed ids): choice = sqrt(softplus(logit)) + bias, the top min(6, E),
+ * w = score / sum * routed_scale.  mvllm_moe_route_dev is score_fn
+ * MVLLM_SCORE_SIGMOID with routed_scale 1. */
+MVLLM_API int mvllm_moe_route_ex_dev(void *stream, const void *x, int x_dtype, int T, int H,
+                                     const float *router, const float *bias, int E, int K,
+                                     int score_fn, float routed_scale, int *idx, float *wt,
+                                     float *scores, float *choice);
 
 /* ---- expert parallelism (one rank per GPU).  No single counterpart in the
  *      reference, which runs every expert on one host; these are the
@@ -269,6 +288,19 @@ MVLLM_API int mvllm_moe_ep_pack_dev(void *stream, const void *x, int x_dtype, co
                                     const float *wt, int T, int K, int D, int E, int nranks,
                                     const int *dest, const int *lid, int self_rank,
                                     const int *pos, void *send_x, int *send_idx, float *send_wt);
+/* Expert parallelism without a token exchange, DeepSeek-V4's EP2
+ * (route_moe_ep2, dsv4_cuda.cpp:1841-1906; map_ep_expert :1356-1369): every
+ * rank sees all T tokens, serves its own experts and the ranks' partial
+ * outputs are summed (allreduce_pair, :1195-1204; NCCL all-reduce here).
+ * local_idx[T, K] = the local id of idx[t, k] when rank self_rank serves it,
+ * else -1.  Placement as above, except that each expert has exactly one
+ * serving rank (every rank holds all tokens, so a replicated expert would
+ * count once per rank; dest entries of -1 serve no rank).  Strided with
+ * nranks 2 is the reference's parity split, expert e on rank e % 2 as e / 2.
+ * The result feeds mvllm_moe_layer_dev with the rank's expert tables. */
+MVLLM_API int mvllm_moe_ep_local_ids_dev(void *stream, const int *idx, int T, int K, int E,
+                                         int nranks, const int *dest, const int *lid,
+                                         int self_rank, int *local_idx);
 /* out[c] += back[pos[c, d]] for d = 0, 1, ... (f32 rows of D, D a multiple of 4):
  * the partial sums each rank returned, added in ascending rank order. */
 MVLLM_API int mvllm_moe_ep_combine_dev(void *stream, const float *back, const int *pos, int T,
@@ -294,7 +326,7 @@ MVLLM_API int mvllm_moe_layer_partial_dev(void *stream, int T, int K, int E, int
                                           float act_a, float act_b, void *workspace,
                                           size_t workspace_bytes);
 
-/* ---- layer epilogue after the routed combine (SURVEY (f)3): the step both
+/* ---- layer epilogue after the routed combine: the step both
  *      callers take after moe_block, kimi_k3.cpp:2074-2108 and
  *      glm53.cpp:1993-2027 ---- */
 /* For each token c: a = acc[c] (L floats, the routed sum); if lat_n:
@@ -308,6 +340,23 @@ MVLLM_API int mvllm_moe_epilogue_dev(void *stream, int T, int H, int L, const fl
                                      const void *up_scales, float routed_scale,
                                      const float *shared, float *h, void *workspace,
                                      size_t workspace_bytes);
+
+/* A dense gated FFN for T rows, in the reference's arithmetic:
+ * g = x . gate^T, u = x . up^T (each [T, O], as mvllm_matmul_dev), the
+ * activation per element (act, act_a, act_b as in moe_block), then
+ * d = h . down^T ([T, H]); y = d, or y += d when accumulate.  All three
+ * weights in format fmt (0, 4, 8 or 9) with their scales.  This is
+ * DeepSeek-V4's shared expert (dsv4_cuda::expert_fp8 + moe,
+ * dsv4_cuda.cpp:169-189, 826-848) and its dense/shared MLP
+ * (dsv4.cpp:2849-2860, 2999-3008).  Workspace:
+ * mvllm_moe_dense_ffn_workspace(T, H, O) bytes. */
+MVLLM_API size_t mvllm_moe_dense_ffn_workspace(int T, int H, int O);
+MVLLM_API int mvllm_moe_dense_ffn_dev(void *stream, int fmt, int T, int H, int O,
+                                      const void *gate_w, const void *gate_s, const void *up_w,
+                                      const void *up_s, const void *down_w, const void *down_s,
+                                      const float *x, int act, float act_a, float act_b,
+                                      float *y, int accumulate, void *workspace,
+                                      size_t workspace_bytes);
 
 /* Per-phase device time of the device-pointer entries, from CUDA events
  * recorded on the launch stream after each phase while enabled (the role of

@@ -613,10 +613,36 @@ __global__ void build_csr_kernel(const int *__restrict__ rows, const int *__rest
 // Generic expert kernels: any D / Iinter, any of fmt 0/4/7, f32 arithmetic.
 // Dequantised element (o, k) of a weight matrix with row length K
 // (src/quant/quant.cpp:203-228 and :298-321).
+// DeepSeek-V4's e4m3fn and e8m0 decoders (native_act.cpp:65-69, 90-100):
+// e4m3fn code 0x7f/0xff is NaN, exponent 0 is man * 2^-9, else
+// (1 + man/8) * 2^(exp-7); e8m0 255 is NaN and 0 is 2^-127 (unlike the
+// MXFP4 scale decoder above, which maps them to inf and 0).  Both exact.
+__device__ __forceinline__ float e4m3fn_to_f32(uint32_t v) {
+    const uint32_t ex = (v >> 3) & 15u, man = v & 7u;
+    if (ex == 15u && man == 7u)
+        return __int_as_float(0x7fc00000);
+    const float mag = ex == 0u ? __fmul_rn(static_cast<float>(man), 0.001953125f)
+                               : __uint_as_float(((ex + 120u) << 23) | (man << 20));
+    return (v & 0x80u) ? -mag : mag;
+}
+__device__ __forceinline__ float e8m0_to_f32(uint32_t e) {
+    if (e == 255u)
+        return __int_as_float(0x7fc00000);
+    return e == 0u ? __uint_as_float(0x00400000u) : __uint_as_float(e << 23);
+}
+
 __device__ __forceinline__ float deq_elem(const void *w, const void *s, int fmt, int o, int k,
                                           int K) {
     if (fmt == MVLLM_FMT_F32)
         return static_cast<const float *>(w)[static_cast<size_t>(o) * K + k];
+    if (fmt == MVLLM_FMT_FP8_B128) {
+        // dsv4_cuda.cpp:127-135: q * scale of the (o / 128, k / 128) tile
+        const uint8_t q = static_cast<const uint8_t *>(w)[static_cast<size_t>(o) * K + k];
+        const uint8_t e =
+            static_cast<const uint8_t *>(s)[static_cast<size_t>(o >> 7) * ((K + 127) / 128) +
+                                            (k >> 7)];
+        return __fmul_rn(e4m3fn_to_f32(q), e8m0_to_f32(e));
+    }
     const uint8_t b = static_cast<const uint8_t *>(w)[static_cast<size_t>(o) * ((K + 1) / 2) +
                                                       (k >> 1)];
     const uint32_t nib = (k & 1) ? (b >> 4) : (b & 15u);
@@ -702,9 +728,10 @@ template <int PHASE> __global__ void __launch_bounds__(256) generic_ffn_kernel(c
 
 // Generic dequantised GEMM y[S,O] = x[S,I] . W[O,I]^T (warp per output row).
 // y[S,O] = x[S,I] . W[O,I]^T, the reference's arithmetic per output
-// (quant.cpp:143-156, 203-228, 255-268, 298-321): acc += x[i] * w[i] in
-// ascending i, each product and sum rounded on its own, w = q * scale as the
-// reference decodes it; int8 rows (fmt 8) take the row scale at the end.  So
+// (quant.cpp:143-156, 203-228, 255-268, 298-321; DeepSeek-V4's FP8 tiles,
+// dsv4_cuda.cpp:618-623): acc += x[i] * w[i] in ascending i, each product and
+// sum rounded on its own, w = q * scale as the reference decodes it; int8
+// rows (fmt 8) take the row scale at the end.  So
 // the result is bit-identical to the reference's matmuls.  A lane per row of
 // x (up to 32 per CTA column), a warp per kMmRows rows of W.  Each K tile of
 // x and of the CTA's W rows (decoded to f32) is staged in shared memory with

@@ -40,6 +40,25 @@ __device__ __forceinline__ int ep_local_id(int e, int nranks, const int *lid) {
     return lid ? __ldg(lid + e) : e / nranks;
 }
 
+// Expert parallelism without a token exchange (DeepSeek-V4's EP2,
+// route_moe_ep2 with map_ep_expert's parity split, dsv4_cuda.cpp:1356-1369,
+// 1841-1906): every rank holds all tokens and keeps only the slots it serves,
+// as local ids; the other slots become -1 and the layer skips them.  The
+// ranks' partial sums are then added by an all-reduce.  Every expert has
+// exactly one serving rank here (dest[e] in [0, nranks); a replicated expert
+// would be counted once per rank, so -1 entries serve no rank).
+__global__ void ep_local_ids_kernel(const int *__restrict__ idx, int n, int E, int nranks,
+                                    const int *__restrict__ dest, const int *__restrict__ lid,
+                                    int self, int *__restrict__ out) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int e = idx[i];
+        int v = -1;
+        if (e >= 0 && e < E && (dest ? __ldg(dest + e) : e % nranks) == self)
+            v = ep_local_id(e, nranks, lid);
+        out[i] = v;
+    }
+}
+
 // One CTA: per destination rank a block scan over the tokens gives the
 // position of each sent token among those of that rank; a second pass adds the
 // destination offsets.  pos[c * nranks + d] = send-buffer row or -1.

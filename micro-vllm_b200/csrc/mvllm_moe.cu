@@ -8,6 +8,7 @@
 #include "tc_ffn.cuh"
 #include "ep_kernels.cuh"
 #include "route_kernels.cuh"
+#include "dense_ffn.cuh"
 #include "expert_tier.hpp"
 
 #include <cudaTypedefs.h>
@@ -1812,6 +1813,15 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
 }
 
 // --------------------------------------------------------------- routing --
+static int topk_launch(cudaStream_t st, const float *choice, const float *mix, int T, int E,
+                       int K, float scale, int *idx, float *wt) {
+    const int warps = 8;
+    topk_kernel<<<std::min((T + warps - 1) / warps, 65535), 32 * warps, 0, st>>>(
+        choice, mix, T, E, K, scale, idx, wt);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
 int mvllm_moe_topk_dev(void *stream, const float *choice, const float *mix, int T, int E, int K,
                        int *idx, float *wt) {
     if (!choice || !idx || !wt || T < 0 || E < 1 || E > 32 * kTopkMaxPerLane || K < 1 ||
@@ -1819,20 +1829,17 @@ int mvllm_moe_topk_dev(void *stream, const float *choice, const float *mix, int 
         return fail(MVLLM_ERR_INVALID, "topk_dev: invalid arguments");
     if (T == 0)
         return MVLLM_OK;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int warps = 8;
-    topk_kernel<<<std::min((T + warps - 1) / warps, 65535), 32 * warps, 0, st>>>(choice, mix, T,
-                                                                                E, K, idx, wt);
-    CUDA_TRY(cudaGetLastError());
-    return MVLLM_OK;
+    return topk_launch(static_cast<cudaStream_t>(stream), choice, mix, T, E, K, 1.f, idx, wt);
 }
 
-int mvllm_moe_route_dev(void *stream, const void *x, int x_dtype, int T, int H,
-                        const float *router, const float *bias, int E, int K, int *idx,
-                        float *wt, float *scores, float *choice) {
+int mvllm_moe_route_ex_dev(void *stream, const void *x, int x_dtype, int T, int H,
+                           const float *router, const float *bias, int E, int K, int score_fn,
+                           float routed_scale, int *idx, float *wt, float *scores,
+                           float *choice) {
     if (!x || !router || !idx || !wt || !scores || !choice || T < 0 || H < 1 || E < 1 ||
         E > 32 * kTopkMaxPerLane || K < 1 || K > kTopkMaxK ||
-        (x_dtype != MVLLM_DTYPE_F32 && x_dtype != MVLLM_DTYPE_BF16))
+        (x_dtype != MVLLM_DTYPE_F32 && x_dtype != MVLLM_DTYPE_BF16) ||
+        (score_fn != MVLLM_SCORE_SIGMOID && score_fn != MVLLM_SCORE_SQRT_SOFTPLUS))
         return fail(MVLLM_ERR_INVALID, "route_dev: invalid arguments");
     if (T == 0)
         return MVLLM_OK;
@@ -1842,15 +1849,39 @@ int mvllm_moe_route_dev(void *stream, const void *x, int x_dtype, int T, int H,
         return fail(MVLLM_ERR_INVALID, "route_dev: T too large");
     if (x_dtype == MVLLM_DTYPE_BF16)
         route_scores_kernel<__nv_bfloat16><<<grid, 1024, 0, st>>>(
-            static_cast<const __nv_bfloat16 *>(x), router, bias, T, H, E, scores, choice);
+            static_cast<const __nv_bfloat16 *>(x), router, bias, T, H, E, score_fn, scores,
+            choice);
     else
         route_scores_kernel<float><<<grid, 1024, 0, st>>>(static_cast<const float *>(x), router,
-                                                           bias, T, H, E, scores, choice);
+                                                           bias, T, H, E, score_fn, scores,
+                                                           choice);
     CUDA_TRY(cudaGetLastError());
-    return mvllm_moe_topk_dev(stream, choice, scores, T, E, K, idx, wt);
+    return topk_launch(st, choice, scores, T, E, K, routed_scale, idx, wt);
+}
+
+int mvllm_moe_route_dev(void *stream, const void *x, int x_dtype, int T, int H,
+                        const float *router, const float *bias, int E, int K, int *idx,
+                        float *wt, float *scores, float *choice) {
+    return mvllm_moe_route_ex_dev(stream, x, x_dtype, T, H, router, bias, E, K,
+                                  MVLLM_SCORE_SIGMOID, 1.f, idx, wt, scores, choice);
 }
 
 // ------------------------------------------------------ expert parallelism --
+int mvllm_moe_ep_local_ids_dev(void *stream, const int *idx, int T, int K, int E, int nranks,
+                               const int *dest, const int *lid, int self_rank, int *local_idx) {
+    if (!idx || !local_idx || T < 0 || K < 1 || E < 1 || nranks < 1 || self_rank < 0 ||
+        self_rank >= nranks || (!dest) != (!lid))
+        return fail(MVLLM_ERR_INVALID, "ep_local_ids_dev: invalid arguments");
+    const size_t n = size_t(T) * K;
+    if (n == 0)
+        return MVLLM_OK;
+    const int blocks = int(std::min<size_t>((n + 255) / 256, 4096));
+    ep_local_ids_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        idx, int(n), E, nranks, dest, lid, self_rank, local_idx);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
 int mvllm_moe_ep_plan_dev(void *stream, const int *idx, int T, int K, int E, int nranks,
                           const int *dest, int self_rank, int *pos, int *send_cnt) {
     if (!idx || !pos || !send_cnt || T < 0 || K < 1 || E < 1 || nranks < 1 || nranks > 32 ||
@@ -1952,8 +1983,9 @@ int mvllm_pack_mxfp4_dev(void *stream, const float *w, int O, int I, uint8_t *pa
 
 int mvllm_matmul_dev(void *stream, int fmt, float *y, const float *x, const void *w,
                      const void *scales, int S, int I, int O) {
-    if ((fmt != 0 && fmt != 4 && fmt != 7 && fmt != MVLLM_FMT_INT8_ROW) || !y || !x || !w ||
-        S < 1 || I < 1 || O < 1 || (fmt != 0 && !scales))
+    if ((fmt != 0 && fmt != 4 && fmt != 7 && fmt != MVLLM_FMT_INT8_ROW &&
+         fmt != MVLLM_FMT_FP8_B128) ||
+        !y || !x || !w || S < 1 || I < 1 || O < 1 || (fmt != 0 && !scales))
         return fail(MVLLM_ERR_INVALID, "matmul_dev: invalid arguments");
     if (!ctx().inited)
         return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
@@ -2011,6 +2043,55 @@ int mvllm_moe_epilogue_dev(void *stream, int T, int H, int L, const float *acc,
     epilogue_residual_kernel<<<int(std::min<size_t>((n + 255) / 256, size_t(c.sms) * 16)), 256, 0,
                                st>>>(h, src, shared, routed_scale, n);
     CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+// ------------------------------------------------------------- dense FFN --
+size_t mvllm_moe_dense_ffn_workspace(int T, int H, int O) {
+    if (T < 1 || H < 1 || O < 1)
+        return 0;
+    return (2 * size_t(T) * O + size_t(T) * H) * sizeof(float) + 256;
+}
+
+int mvllm_moe_dense_ffn_dev(void *stream, int fmt, int T, int H, int O, const void *gate_w,
+                            const void *gate_s, const void *up_w, const void *up_s,
+                            const void *down_w, const void *down_s, const float *x, int act,
+                            float act_a, float act_b, float *y, int accumulate, void *workspace,
+                            size_t workspace_bytes) {
+    const bool scaled = fmt != MVLLM_FMT_F32;
+    if (T < 1 || H < 1 || O < 1 || !x || !y || !gate_w || !up_w || !down_w ||
+        (fmt != MVLLM_FMT_F32 && fmt != MVLLM_FMT_INT4_G64 && fmt != MVLLM_FMT_INT8_ROW &&
+         fmt != MVLLM_FMT_FP8_B128) ||
+        (scaled && (!gate_s || !up_s || !down_s)))
+        return fail(MVLLM_ERR_INVALID, "dense_ffn_dev: invalid arguments");
+    const size_t need = mvllm_moe_dense_ffn_workspace(T, H, O);
+    if (!workspace || workspace_bytes < need)
+        return fail(MVLLM_ERR_WORKSPACE, "dense_ffn_dev: workspace %zu < %zu", workspace_bytes,
+                    need);
+    Context &c = ctx();
+    if (!c.inited)
+        return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float *g = static_cast<float *>(workspace);
+    float *u = g + size_t(T) * O;
+    float *d = u + size_t(T) * O;
+    matmul_generic_kernel<<<matmul_grid(T, O), 256, 0, st>>>(fmt, g, x, gate_w, gate_s, T, H, O);
+    CUDA_TRY(cudaGetLastError());
+    matmul_generic_kernel<<<matmul_grid(T, O), 256, 0, st>>>(fmt, u, x, up_w, up_s, T, H, O);
+    CUDA_TRY(cudaGetLastError());
+    const size_t nh = size_t(T) * O;
+    dense_act_kernel<<<int(std::min<size_t>((nh + 255) / 256, size_t(c.sms) * 16)), 256, 0, st>>>(
+        g, u, nh, act, act_a, act_b);
+    CUDA_TRY(cudaGetLastError());
+    matmul_generic_kernel<<<matmul_grid(T, H), 256, 0, st>>>(fmt, accumulate ? d : y, g, down_w,
+                                                             down_s, T, O, H);
+    CUDA_TRY(cudaGetLastError());
+    if (accumulate) {
+        const size_t ny = size_t(T) * H;
+        add_rows_kernel<<<int(std::min<size_t>((ny + 255) / 256, size_t(c.sms) * 16)), 256, 0,
+                          st>>>(y, d, ny);
+        CUDA_TRY(cudaGetLastError());
+    }
     return MVLLM_OK;
 }
 

@@ -1,7 +1,7 @@
 // route_kernels.cuh -- expert routing on the device: router scores and the
 // deterministic top-k that feeds the permutation.
 //
-// Reference (both MoE families route the same way):
+// Reference (GLM and Kimi K3 route the same way):
 //   scores[e] = sigmoid(x . router[e])        quant::matmul_f32 (quant.cpp:156-168),
 //                                             quant::sigmoid (quant.hpp:22-29)
 //   choice[e] = scores[e] + bias[e]           glm53.cpp:1921-1931, kimi_k3.cpp:1986-1998
@@ -9,6 +9,9 @@
 // moe_topk keeps the K largest choices (equal values: the lower expert id
 // first), takes w[i] = mix[idx[i]] (or the choice) clamped at 0, and divides
 // by their sum accumulated in selection order (1/K each when the sum is 0).
+// DeepSeek-V4 (dsv4_cuda.cpp:1541-1587) scores with sqrt(softplus(logit))
+// (dsv4_cuda.cpp:26-34) instead of the sigmoid, selects the same way (top 6)
+// and multiplies each normalised weight by routed_scale.
 #pragma once
 
 #include "common.cuh"
@@ -24,12 +27,37 @@ __device__ __forceinline__ float expf_cr(float x) {
     return static_cast<float>(exp(static_cast<double>(x)));
 }
 
+// log(1 + x) correctly rounded the same way (through double precision).
+__device__ __forceinline__ float log1pf_cr(float x) {
+    return static_cast<float>(log1p(static_cast<double>(x)));
+}
+
 // quant::sigmoid with the exponential above.
 __device__ __forceinline__ float sigmoid_route(float x) {
     if (x >= 0.f)
         return __fdiv_rn(1.f, __fadd_rn(1.f, expf_cr(-x)));
     const float z = expf_cr(x);
     return __fdiv_rn(z, __fadd_rn(1.f, z));
+}
+
+// sqrt(max(softplus(z), 0)) with softplus's three branches (z > 20: z;
+// z < -20: e^z; else log1p(e^z)), dsv4_cuda.cpp:26-34; the square root is
+// IEEE (correctly rounded), as the host's sqrtf.
+__device__ __forceinline__ float sqrt_softplus_route(float z) {
+    float sp;
+    if (z > 20.f)
+        sp = z;
+    else if (z < -20.f)
+        sp = expf_cr(z);
+    else
+        sp = log1pf_cr(expf_cr(z));
+    return __fsqrt_rn(sp < 0.f ? 0.f : sp); // std::max(sp, 0.f)
+}
+
+// Router score functions (MVLLM_SCORE_*).
+__device__ __forceinline__ float route_score(float logit, int score_fn) {
+    return score_fn == MVLLM_SCORE_SQRT_SOFTPLUS ? sqrt_softplus_route(logit)
+                                                 : sigmoid_route(logit);
 }
 
 template <typename TX> __device__ __forceinline__ float to_f32(TX v);
@@ -45,7 +73,7 @@ template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16
 template <typename TX>
 __global__ void __launch_bounds__(1024)
     route_scores_kernel(const TX *__restrict__ x, const float *__restrict__ w,
-                        const float *__restrict__ bias, int T, int H, int E,
+                        const float *__restrict__ bias, int T, int H, int E, int score_fn,
                         float *__restrict__ scores, float *__restrict__ choice) {
     __shared__ float xs[32][65];
     __shared__ float wsm[32][65];
@@ -67,7 +95,7 @@ __global__ void __launch_bounds__(1024)
     }
     const int t = t0 + tt, e = e0 + te;
     if (t < T && e < E) {
-        const float s = sigmoid_route(acc);
+        const float s = route_score(acc, score_fn);
         scores[static_cast<size_t>(t) * E + e] = s;
         choice[static_cast<size_t>(t) * E + e] = bias ? __fadd_rn(s, bias[e]) : s;
     }
@@ -79,9 +107,12 @@ constexpr int kTopkMaxK = 32;       // one lane per selected expert
 // One warp per token: K rounds of a warp-wide arg-max over the choices not yet
 // taken, ordered by (value descending, id ascending) -- the order of the
 // reference's partial_sort comparator -- then the weights as moe_topk forms
-// them.  Slots K > E get id -1 and weight 0, as the callers preset them.
+// them, times `scale` (1 for moe_topk itself; DeepSeek-V4's routed_scale,
+// dsv4_cuda.cpp:1579-1585).  Slots K > E get id -1 and weight 0, as the
+// callers preset them.
 __global__ void topk_kernel(const float *__restrict__ choice, const float *__restrict__ mix, int T,
-                            int E, int K, int *__restrict__ idx, float *__restrict__ wt) {
+                            int E, int K, float scale, int *__restrict__ idx,
+                            float *__restrict__ wt) {
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     const int per = (E + 31) >> 5;
@@ -139,7 +170,9 @@ __global__ void topk_kernel(const float *__restrict__ choice, const float *__res
             float *wo = wt + static_cast<size_t>(t) * K;
             if (lane < k) {
                 io[lane] = sel;
-                wo[lane] = sum > 0.f ? __fdiv_rn(w_r, sum) : __fdiv_rn(1.f, static_cast<float>(k));
+                const float q =
+                    sum > 0.f ? __fdiv_rn(w_r, sum) : __fdiv_rn(1.f, static_cast<float>(k));
+                wo[lane] = __fmul_rn(q, scale); // exact for scale 1
             } else {
                 io[lane] = -1;
                 wo[lane] = 0.f;

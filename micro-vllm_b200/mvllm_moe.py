@@ -24,8 +24,9 @@ LIB_PATH = os.path.join(HERE, "lib", "libmvllm_moe.so")
 OK, ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_NOT_INIT, ERR_DEVICE, \
     ERR_WORKSPACE, ERR_RANGE = range(10)
 ACT_SILU, ACT_CLAMP_SWIGLU, ACT_SITU = 0, 1, 2
-FMT_F32, FMT_INT4_G64, FMT_MXFP4 = 0, 4, 7
+FMT_F32, FMT_INT4_G64, FMT_MXFP4, FMT_INT8_ROW, FMT_FP8_B128 = 0, 4, 7, 8, 9
 DTYPE_F32, DTYPE_BF16 = 0, 1
+SCORE_SIGMOID, SCORE_SQRT_SOFTPLUS = 0, 1
 
 # Every symbol include/mvllm_moe.h declares (checked by tests/test_abi.py).
 C_SYMBOLS = (
@@ -41,7 +42,8 @@ C_SYMBOLS = (
     "mvllm_moe_ep_combine16_dev", "mvllm_moe_layer_partial_dev", "mvllm_moe_tier_configure",
     "mvllm_moe_expert_bind", "mvllm_moe_expert_unbind", "mvllm_moe_tier_stats",
     "mvllm_moe_epilogue_workspace", "mvllm_moe_epilogue_dev", "mvllm_moe_host_register",
-    "mvllm_moe_host_unregister",
+    "mvllm_moe_host_unregister", "mvllm_moe_route_ex_dev", "mvllm_moe_ep_local_ids_dev",
+    "mvllm_moe_dense_ffn_workspace", "mvllm_moe_dense_ffn_dev",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -107,6 +109,11 @@ def lib():
                                             [vp, i, f, f, vp, sz]),
             "mvllm_moe_topk_dev": (i, [vp, vp, vp, i, i, i, vp, vp]),
             "mvllm_moe_route_dev": (i, [vp, vp, i, i, i, vp, vp, i, i, vp, vp, vp, vp]),
+            "mvllm_moe_route_ex_dev": (i, [vp, vp, i, i, i, vp, vp, i, i, i, f, vp, vp, vp, vp]),
+            "mvllm_moe_ep_local_ids_dev": (i, [vp, vp, i, i, i, i, vp, vp, i, vp]),
+            "mvllm_moe_dense_ffn_workspace": (sz, [i, i, i]),
+            "mvllm_moe_dense_ffn_dev": (i, [vp, i, i, i, i] + [vp] * 7 + [i, f, f, vp, i, vp,
+                                                                         sz]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -413,6 +420,46 @@ def topk_dev(choice, K, idx, wt, mix=None, stream=None):
     T, E = choice.shape
     _check(lib().mvllm_moe_topk_dev(_stream(stream), _dp(choice), _dp(mix), T, E, K, _dp(idx),
                                     _dp(wt)))
+
+
+def route_ex_dev(x, router, bias, K, idx, wt, scores, choice, score_fn=SCORE_SIGMOID,
+                 routed_scale=1.0, stream=None):
+    """Router scores (score_fn of x . router^T, + bias), top-K and the weights
+    times routed_scale, on device.  SCORE_SQRT_SOFTPLUS with K=6 is
+    DeepSeek-V4's route (dsv4_cuda.cpp:1541-1587)."""
+    T, H = x.shape
+    E = router.shape[0]
+    x_dtype = DTYPE_BF16 if str(x.dtype) == "torch.bfloat16" else DTYPE_F32
+    _check(lib().mvllm_moe_route_ex_dev(_stream(stream), _dp(x), x_dtype, T, H, _dp(router),
+                                        _dp(bias), E, K, score_fn, routed_scale, _dp(idx),
+                                        _dp(wt), _dp(scores), _dp(choice)))
+
+
+def ep_local_ids_dev(idx, E, nranks, self_rank, local_idx, dest=None, lid=None, stream=None):
+    """local_idx [T, K] = the local id of each slot rank self_rank serves, else -1."""
+    T, K = idx.shape
+    _check(lib().mvllm_moe_ep_local_ids_dev(_stream(stream), _dp(idx), T, K, E, nranks, _dp(dest),
+                                            _dp(lid), self_rank, _dp(local_idx)))
+
+
+def dense_ffn_workspace_bytes(T, H, O) -> int:
+    return lib().mvllm_moe_dense_ffn_workspace(T, H, O)
+
+
+def dense_ffn_dev(fmt, x, gate, up, down, y, act, act_a=0.0, act_b=0.0, accumulate=False,
+                  workspace=None, stream=None):
+    """y (+)= down . act(gate . x, up . x) on device; gate/up/down = (weights,
+    scales-or-None) device tensors in format fmt; x [T, H], y [T, H] f32."""
+    import torch
+    T, H = x.shape
+    O = gate[0].shape[0]
+    ws = workspace
+    if ws is None:
+        ws = torch.empty(dense_ffn_workspace_bytes(T, H, O), dtype=torch.uint8, device=x.device)
+    _check(lib().mvllm_moe_dense_ffn_dev(
+        _stream(stream), fmt, T, H, O, _dp(gate[0]), _dp(gate[1]), _dp(up[0]), _dp(up[1]),
+        _dp(down[0]), _dp(down[1]), _dp(x), act, act_a, act_b, _dp(y), 1 if accumulate else 0,
+        _dp(ws), ws.numel() * ws.element_size()))
 
 
 def route_dev(x, router, bias, K, idx, wt, scores, choice, stream=None):

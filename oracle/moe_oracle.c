@@ -674,3 +674,224 @@ EXPORT int64_t orc_k3_geom(int latent, int inter, int64_t *off) {
     off[3] = off[2] + w1p;         /* up scales */
     return 2 * (w1p + w1s) + w2p + w2s;
 }
+
+/* ======================================================================
+ * DeepSeek-V4 routed experts (src/gpu/dsv4_cuda.cpp, CPU tier; decoders in
+ * src/quant/native_act.cpp).  Routing by sqrt(softplus), MXFP4 experts
+ * through quant::matmul_mxfp4 with clamped SwiGLU, an optional FP8 shared
+ * expert, and the two-rank expert split (EP2) whose partial outputs are
+ * summed.  Per token, as the reference.
+ * ====================================================================== */
+
+/* ue8m0 -> 2^(v-127); 255 is NaN.  native_act.cpp:65-69 */
+EXPORT float orc_e8m0_decode(uint8_t v) {
+    if (v == 0xff)
+        return NAN;
+    return ldexpf(1.f, (int)v - 127);
+}
+
+/* e4m3fn: 0x7f / 0xff NaN, exponent 0 subnormal.  native_act.cpp:90-100 */
+EXPORT float orc_e4m3fn_decode(uint8_t v) {
+    const int sign = v >> 7, ex = (v >> 3) & 15, man = v & 7;
+    if (ex == 15 && man == 7)
+        return NAN;
+    const float mag = ex == 0 ? ldexpf((float)man, -9) : ldexpf(1.f + (float)man / 8.f, ex - 7);
+    return sign ? -mag : mag;
+}
+
+/* softplus with its +-20 cut-offs, then sqrt(max(., 0)).  dsv4_cuda.cpp:26-34 */
+EXPORT float orc_sqrt_softplus(float z) {
+    float sp;
+    if (z > 20.f)
+        sp = z;
+    else if (z < -20.f)
+        sp = expf(z);
+    else
+        sp = log1pf(expf(z));
+    return sqrtf(sp < 0.f ? 0.f : sp);
+}
+
+/* y = x . dequant(W)^T for FP8 tensors: s += x[i] * (e4m3fn(q) * e8m0(tile)),
+ * tile (o/128, i/128) of max(ceil(I/128), 1) per tile row.
+ * dsv4_cuda.cpp:127-135 (dequant), :618-623 (matvec loop) */
+EXPORT void orc_matmul_fp8_b128(float *y, const float *x, const uint8_t *w, const uint8_t *scales,
+                                int S, int I, int O) {
+    const int si = ceil_div(I, 128) > 1 ? ceil_div(I, 128) : 1;
+    for (int s = 0; s < S; ++s) {
+        const float *xs = x + (size_t)s * I;
+        float *ys = y + (size_t)s * O;
+        for (int o = 0; o < O; ++o) {
+            float acc = 0.f;
+            for (int i = 0; i < I; ++i) {
+                const float sc = orc_e8m0_decode(scales[(size_t)(o / 128) * si + i / 128]);
+                const float q = orc_e4m3fn_decode(w[(size_t)o * I + i]) * sc;
+                acc += xs[i] * q;
+            }
+            ys[o] = acc;
+        }
+    }
+}
+
+/* dsv4_cuda::route (dsv4_cuda.cpp:1541-1587): logits = router . x
+ * (quant::matmul_f32), score = sqrt_softplus, choice = score + bias; the top
+ * k = min(6, E) choices by moe_topk (or `fixed` ids), then each weight is the
+ * chosen score clipped at 0, divided by their sum over the 6 slots (1/k when
+ * the sum is 0), times routed_scale.  ids / w: 6 slots, -1 / 0 past k. */
+EXPORT int orc_dsv4_route(const float *x, int H, const float *router, const float *bias, int E,
+                          const int *fixed, float routed_scale, int *ids, float *w) {
+    if (!x || !router || !ids || !w || E <= 0 || H <= 0)
+        return 0;
+    float *logits = (float *)calloc((size_t)E * 3, sizeof(float));
+    float *score = logits + E, *choice = score + E;
+    orc_matmul_f32(logits, x, router, 1, H, E);
+    for (int e = 0; e < E; ++e) {
+        score[e] = orc_sqrt_softplus(logits[e]);
+        choice[e] = score[e] + (bias ? bias[e] : 0.f);
+    }
+    const int k = E < 6 ? E : 6;
+    if (fixed) {
+        for (int i = 0; i < 6; ++i)
+            ids[i] = i < k ? fixed[i] : -1;
+    } else {
+        orc_moe_topk(choice, E, k, ids, w, score);
+        for (int i = k; i < 6; ++i)
+            ids[i] = -1;
+    }
+    float sum = 0.f;
+    for (int i = 0; i < 6; ++i) {
+        const int e = ids[i];
+        float v = (e >= 0 && e < E) ? score[e] : 0.f;
+        if (v < 0.f)
+            v = 0.f;
+        w[i] = v;
+        sum += v;
+    }
+    for (int i = 0; i < 6; ++i) {
+        if (i >= k) {
+            w[i] = 0.f;
+            continue;
+        }
+        w[i] = (sum > 0.f ? w[i] / sum : 1.f / (float)k) * routed_scale;
+    }
+    free(logits);
+    return 1;
+}
+
+/* One expert, dsv4_cuda::one_expert (dsv4_cuda.cpp:169-189):
+ * g = gate . x, u = up . x ([O]), h = clamped_swiglu(g, u, limit),
+ * d = down . h ([H]), y[i] += weight * d[i].  fp8 = 0: MXFP4 tensors
+ * (quant::matmul_mxfp4); 1: FP8 tiles. */
+static void dsv4_one_expert(int fp8, int H, int O, const void *gw, const void *gs, const void *uw,
+                            const void *us, const void *dw, const void *ds, float weight,
+                            float limit, float *y, const float *x) {
+    float *g = (float *)malloc(sizeof(float) * ((size_t)O * 2 + (size_t)H));
+    float *u = g + O, *d = u + O;
+    if (fp8) {
+        orc_matmul_fp8_b128(g, x, gw, gs, 1, H, O);
+        orc_matmul_fp8_b128(u, x, uw, us, 1, H, O);
+    } else {
+        orc_matmul_mxfp4(g, x, gw, gs, 1, H, O);
+        orc_matmul_mxfp4(u, x, uw, us, 1, H, O);
+    }
+    for (int i = 0; i < O; ++i)
+        g[i] = orc_clamped_swiglu(g[i], u[i], limit);
+    if (fp8)
+        orc_matmul_fp8_b128(d, g, dw, ds, 1, O, H);
+    else
+        orc_matmul_mxfp4(d, g, dw, ds, 1, O, H);
+    for (int i = 0; i < H; ++i)
+        y[i] += weight * d[i];
+    free(g);
+}
+
+/* dsv4_cuda::moe (dsv4_cuda.cpp:812-848): y = 0; the n MXFP4 experts in order
+ * (expert_group; n <= 0 is the reference's false), then, when all six shared
+ * pointers are given (gate, gate scales, up, up scales, down, down scales;
+ * FP8 tiles), y[i] += sh[i] with sh = expert_fp8(x) (one_expert with weight 1
+ * from zero, :826-832). */
+EXPORT int orc_dsv4_moe(const float *x, int H, int O, int n, const void *const *g,
+                        const void *const *u, const void *const *d, const void *const *gs,
+                        const void *const *us, const void *const *ds, const float *weights,
+                        const void *const *sh, float limit, float *y) {
+    if (!x || !y || !weights || n <= 0 || H <= 0 || O <= 0)
+        return 0;
+    for (int i = 0; i < H; ++i)
+        y[i] = 0.f;
+    for (int e = 0; e < n; ++e)
+        dsv4_one_expert(0, H, O, g[e], gs[e], u[e], us[e], d[e], ds[e], weights[e], limit, y, x);
+    if (sh) {
+        float *s = (float *)calloc((size_t)H, sizeof(float));
+        dsv4_one_expert(1, H, O, sh[0], sh[1], sh[2], sh[3], sh[4], sh[5], 1.f, limit, s, x);
+        for (int i = 0; i < H; ++i)
+            y[i] += s[i];
+        free(s);
+    }
+    return 1;
+}
+
+/* map_ep_expert (dsv4_cuda.cpp:1356-1369): the bank slot serving global id e
+ * on the rank of parity r, or -1: e itself when present, else e / 2 (a bank
+ * packed per rank). */
+static int dsv4_map_ep(const void *const *g, int E, int e, int r) {
+    if (e < 0 || e % 2 != r)
+        return -1;
+    if (e < E && g[e])
+        return e;
+    if (e / 2 < E && g[e / 2])
+        return e / 2;
+    return -1;
+}
+
+/* dsv4_cuda::route_moe_ep2 (dsv4_cuda.cpp:1841-1906) for one token with one
+ * expert bank serving both ranks (local == peer, peer_input == input): route
+ * once per rank, rank r runs the routed slots whose expert id has parity r
+ * (map_ep_expert, :1356-1369) through moe_routed_parity (:1371-1404), the
+ * shared expert (if given) on rank 0 only, then allreduce_pair
+ * (:1195-1204): out = peer_out = rank0 + rank1.  Experts with a NULL gate
+ * pointer are absent from the bank and skipped. */
+EXPORT int orc_dsv4_route_moe_ep2(const float *x, int H, const float *router, const float *bias,
+                                  int E, float routed_scale, int O, const void *const *g,
+                                  const void *const *u, const void *const *d,
+                                  const void *const *gs, const void *const *us,
+                                  const void *const *ds, const void *const *sh, float limit,
+                                  float *out, float *peer_out) {
+    int ids[6];
+    float w[6];
+    if (!orc_dsv4_route(x, H, router, bias, E, NULL, routed_scale, ids, w))
+        return 0;
+    float *part[2] = {out, peer_out};
+    for (int r = 0; r < 2; ++r) {
+        const void *pg[6], *pu[6], *pd[6], *pgs[6], *pus[6], *pds[6];
+        float pw[6];
+        int n = 0;
+        for (int k = 0; k < 6; ++k) {
+            const int l = dsv4_map_ep(g, E, ids[k], r);
+            if (l < 0 || !u[l] || !d[l])
+                continue;
+            pg[n] = g[l];
+            pu[n] = u[l];
+            pd[n] = d[l];
+            pgs[n] = gs[l];
+            pus[n] = us[l];
+            pds[n] = ds[l];
+            pw[n] = w[k];
+            ++n;
+        }
+        const void *const *rsh = r == 0 ? sh : NULL;
+        if (n > 0) {
+            orc_dsv4_moe(x, H, O, n, pg, pu, pd, pgs, pus, pds, pw, rsh, limit, part[r]);
+        } else {
+            for (int i = 0; i < H; ++i)
+                part[r][i] = 0.f;
+            if (rsh) /* the shared expert's output copied in */
+                dsv4_one_expert(1, H, O, rsh[0], rsh[1], rsh[2], rsh[3], rsh[4], rsh[5], 1.f,
+                                limit, part[r], x);
+        }
+    }
+    for (int i = 0; i < H; ++i) {
+        const float s = out[i] + peer_out[i];
+        out[i] = s;
+        peer_out[i] = s;
+    }
+    return 1;
+}

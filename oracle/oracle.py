@@ -108,6 +108,30 @@ class Oracle:
         self._pick = getattr(L, p + "moe_topk_pick")
         self._pick.restype = C.c_int
         self._pick.argtypes = [_f32p, C.c_int, C.c_int, _i32p, _f32p]
+        # DeepSeek-V4 (dsv4_cuda.cpp, native_act.cpp)
+        for name in ("e8m0_decode", "e4m3fn_decode"):
+            f = getattr(L, p + name)
+            f.restype = C.c_float
+            f.argtypes = [C.c_uint8]
+            setattr(self, "_" + name, f)
+        self._mm8b = getattr(L, p + "matmul_fp8_b128")
+        self._mm8b.argtypes = [_f32p, _f32p, _u8p, _u8p, C.c_int, C.c_int, C.c_int]
+        self._d4route = getattr(L, p + "dsv4_route")
+        self._d4route.restype = C.c_int
+        self._d4route.argtypes = [_f32p, C.c_int, _f32p, C.c_void_p, C.c_int, C.c_void_p,
+                                  C.c_float, _i32p, _f32p]
+        self._d4moe = getattr(L, p + "dsv4_moe")
+        self._d4moe.restype = C.c_int
+        self._d4moe.argtypes = [_f32p, C.c_int, C.c_int, C.c_int] + [C.c_void_p] * 6 + [
+            C.c_void_p, C.c_void_p, C.c_float, _f32p]
+        self._d4ep2 = getattr(L, p + "dsv4_route_moe_ep2")
+        self._d4ep2.restype = C.c_int
+        self._d4ep2.argtypes = [_f32p, C.c_int, _f32p, C.c_void_p, C.c_int, C.c_float,
+                                C.c_int] + [C.c_void_p] * 7 + [C.c_float, _f32p, _f32p]
+        self._ssp = getattr(L, "orc_sqrt_softplus", None)  # the port only
+        if self._ssp is not None:
+            self._ssp.restype = C.c_float
+            self._ssp.argtypes = [C.c_float]
 
     # ---- codecs -----------------------------------------------------------
     def quantize_int4_g64(self, w):
@@ -234,6 +258,95 @@ class Oracle:
         w = np.zeros(max(k, 1), np.float32)
         r = self._pick(scores, scores.shape[0], k, idx, w)
         return idx[:r], w[:r]
+
+    # ---- DeepSeek-V4 -------------------------------------------------------
+    def e8m0_decode(self, v):
+        return self._e8m0_decode(v)
+
+    def e4m3fn_decode(self, v):
+        return self._e4m3fn_decode(v)
+
+    def sqrt_softplus(self, z):
+        """Port only (the reference's is file-local)."""
+        return self._ssp(z)
+
+    def matmul_fp8_b128(self, x, w, s, O):
+        """y = x . dequant(W)^T, W e4m3fn [O, I] with 128x128 e8m0 tiles."""
+        x = np.ascontiguousarray(x, np.float32)
+        S, I = x.shape
+        y = np.zeros((S, O), np.float32)
+        self._mm8b(y, x, np.ascontiguousarray(w, np.uint8), np.ascontiguousarray(s, np.uint8), S,
+                   I, O)
+        return y
+
+    def dsv4_route(self, x, router, bias, routed_scale, fixed=None):
+        """dsv4_cuda::route per row of x [T, H]: ids [T, 6] int32, w [T, 6]."""
+        x = np.ascontiguousarray(x, np.float32)
+        router = np.ascontiguousarray(router, np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        T, H = x.shape
+        E = router.shape[0]
+        ids = np.full((T, 6), -1, np.int32)
+        w = np.zeros((T, 6), np.float32)
+        fx = None if fixed is None else np.ascontiguousarray(fixed, np.int32)
+        for t in range(T):
+            i6 = np.zeros(6, np.int32)
+            w6 = np.zeros(6, np.float32)
+            ok = self._d4route(x[t], H, router, _ptr(b), E, _ptr(fx), routed_scale, i6, w6)
+            assert ok
+            ids[t], w[t] = i6, w6
+        return ids, w
+
+    @staticmethod
+    def _tables(experts, E=None):
+        """Six pointer arrays (gate, up, down, gate scales, up scales, down
+        scales) from [(gate, up, down)] of (packed, scales); None = absent."""
+        n = len(experts) if E is None else E
+        cols = [[None] * n for _ in range(6)]
+        for e, ex in enumerate(experts):
+            if ex is None:
+                continue
+            (gp, gsc), (up, usc), (dp, dsc) = ex
+            for j, a in enumerate((gp, up, dp, gsc, usc, dsc)):
+                cols[j][e] = a
+        return [_ptr_array(c) for c in cols]
+
+    @staticmethod
+    def _shared(shared):
+        if shared is None:
+            return None
+        (gw, gs), (uw, us), (dw, ds) = shared
+        return _ptr_array([gw, gs, uw, us, dw, ds])
+
+    def dsv4_moe(self, x, O, experts, weights, shared=None, limit=0.0):
+        """dsv4_cuda::moe for one token x [H]: MXFP4 experts [(gate, up, down)]
+        of (packed, scales) with their weights, then the FP8 shared expert
+        ((w, scales) x 3) if given.  Returns y [H] (None = reference false)."""
+        x = np.ascontiguousarray(x, np.float32)
+        H = x.shape[0]
+        t = self._tables(experts)
+        sh = self._shared(shared)
+        wv = np.ascontiguousarray(weights, np.float32)
+        y = np.zeros(H, np.float32)
+        ok = self._d4moe(x, H, O, len(experts), *t, wv.ctypes.data, sh, limit, y)
+        return y if ok else None
+
+    def dsv4_route_moe_ep2(self, x, router, bias, routed_scale, O, experts, shared=None,
+                           limit=0.0):
+        """dsv4_cuda::route_moe_ep2 for one token x [H] over a bank of
+        len(experts) MXFP4 experts (None = absent): (out, peer_out)."""
+        x = np.ascontiguousarray(x, np.float32)
+        router = np.ascontiguousarray(router, np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        H = x.shape[0]
+        E = len(experts)
+        t = self._tables(experts)
+        sh = self._shared(shared)
+        out = np.zeros(H, np.float32)
+        peer = np.zeros(H, np.float32)
+        ok = self._d4ep2(x, H, router, _ptr(b), E, routed_scale, O, *t, sh, limit, out, peer)
+        assert ok
+        return out, peer
 
 
 def permute(idx, wt, uniq):

@@ -2,18 +2,23 @@
 //
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together
 // with the reference's own src/quant/quant.cpp, src/gpu/metal_ops.cpp,
-// src/model/ops.cpp and src/model/moe_pick.cpp (read in place, never copied)
+// src/model/ops.cpp, src/model/moe_pick.cpp and, for DeepSeek-V4, the CPU
+// tier src/gpu/dsv4_cuda.cpp with src/quant/native_act.cpp and
+// src/quant/bf16.cpp (read in place, never copied)
 // into oracle/_ref/libmvllm_ref.so.  Tests use it to pin the C restatement in
 // moe_oracle.c, tests/golden/gen_golden.py uses it to produce the fixtures,
 // and bench.py's reference arm times ref_moe_block as the reference CPU path.
 //
 // Each wrapper forwards to the reference function named beside it; nothing
 // here computes anything itself.
+#include "src/gpu/dsv4_cuda.hpp"
 #include "src/gpu/metal_ops.hpp"
 #include "src/model/moe_pick.hpp"
+#include "src/quant/native_act.hpp"
 #include "src/quant/quant.hpp"
 
 #include <cstdint>
+#include <vector>
 
 namespace mvllm {
 // Declared in src/model/family.hpp:402 and :458, defined in src/model/ops.cpp.
@@ -85,4 +90,132 @@ REF_API int ref_moe_union_ids(const int *idx, int n_tok, int topk, int *out, int
 }
 REF_API int ref_moe_topk_pick(const float *scores, int n, int k, int *idx, float *w) {
     return mvllm::moe_topk_pick(scores, n, k, idx, w);
+}
+
+// ---- DeepSeek-V4 CPU tier (src/gpu/dsv4_cuda.hpp; src/quant/native_act.hpp) ----
+// Each wrapper builds the reference's own Tensor / Activation / ExpertSet
+// objects through its public upload calls and frees them afterwards.
+namespace dsv4 = mvllm::dsv4_cuda;
+
+REF_API float ref_e8m0_decode(uint8_t v) { return mvllm::e8m0_decode(v); }
+REF_API float ref_e4m3fn_decode(uint8_t v) { return mvllm::e4m3fn_decode(v); }
+
+// dsv4_cuda::matvec over FP8 tiles (dsv4_cuda.cpp:571-623), row by row.
+REF_API void ref_matmul_fp8_b128(float *y, const float *x, const uint8_t *w, const uint8_t *sc,
+                                 int S, int I, int O) {
+    dsv4::Tensor *t = nullptr;
+    if (!dsv4::upload_fp8(&t, w, sc, O, I, 0))
+        return;
+    for (int s = 0; s < S; ++s)
+        dsv4::matvec(t, y + static_cast<size_t>(s) * O, x + static_cast<size_t>(s) * I);
+    dsv4::tensor_free(t);
+}
+
+namespace {
+dsv4::Activation *act_from(const float *x, int n) {
+    dsv4::Activation *a = dsv4::activation_create(0, n);
+    if (a)
+        dsv4::activation_upload(a, x, n);
+    return a;
+}
+struct Experts { // one FP4 tensor triple per expert, nullptr where absent
+    std::vector<dsv4::Tensor *> g, u, d;
+    Experts(int n, int H, int O, const void *const *gp, const void *const *up,
+            const void *const *dp, const void *const *gs, const void *const *us,
+            const void *const *ds)
+        : g(n, nullptr), u(n, nullptr), d(n, nullptr) {
+        for (int e = 0; e < n; ++e) {
+            if (!gp[e] || !up[e] || !dp[e])
+                continue;
+            auto b = [](const void *p) { return static_cast<const uint8_t *>(p); };
+            dsv4::upload_fp4(&g[e], b(gp[e]), b(gs[e]), O, H, 0);
+            dsv4::upload_fp4(&u[e], b(up[e]), b(us[e]), O, H, 0);
+            dsv4::upload_fp4(&d[e], b(dp[e]), b(ds[e]), H, O, 0);
+        }
+    }
+    ~Experts() {
+        for (size_t e = 0; e < g.size(); ++e) {
+            dsv4::tensor_free(g[e]);
+            dsv4::tensor_free(u[e]);
+            dsv4::tensor_free(d[e]);
+        }
+    }
+};
+struct Shared { // FP8 shared expert: gate, gate scales, up, up scales, down, down scales
+    dsv4::Tensor *g = nullptr, *u = nullptr, *d = nullptr;
+    Shared(int H, int O, const void *const *sh) {
+        if (!sh)
+            return;
+        auto b = [](const void *p) { return static_cast<const uint8_t *>(p); };
+        dsv4::upload_fp8(&g, b(sh[0]), b(sh[1]), O, H, 0);
+        dsv4::upload_fp8(&u, b(sh[2]), b(sh[3]), O, H, 0);
+        dsv4::upload_fp8(&d, b(sh[4]), b(sh[5]), H, O, 0);
+    }
+    ~Shared() {
+        dsv4::tensor_free(g);
+        dsv4::tensor_free(u);
+        dsv4::tensor_free(d);
+    }
+};
+} // namespace
+
+// dsv4_cuda::route (dsv4_cuda.cpp:1541-1587) for one token.
+REF_API int ref_dsv4_route(const float *x, int H, const float *router, const float *bias, int E,
+                           const int *fixed, float routed_scale, int *ids, float *w) {
+    dsv4::Tensor *tg = nullptr, *tb = nullptr;
+    dsv4::upload_f32(&tg, router, E, H, 0);
+    if (bias)
+        dsv4::upload_f32(&tb, bias, E, 1, 0);
+    dsv4::Activation *a = act_from(x, H);
+    const bool ok = dsv4::route(a, tg, tb, fixed, routed_scale, ids, w);
+    dsv4::activation_free(a);
+    dsv4::tensor_free(tg);
+    dsv4::tensor_free(tb);
+    return ok ? 1 : 0;
+}
+
+// dsv4_cuda::moe (dsv4_cuda.cpp:834-848) for one token.
+REF_API int ref_dsv4_moe(const float *x, int H, int O, int n, const void *const *g,
+                         const void *const *u, const void *const *d, const void *const *gs,
+                         const void *const *us, const void *const *ds, const float *weights,
+                         const void *const *sh, float limit, float *y) {
+    Experts ex(n, H, O, g, u, d, gs, us, ds);
+    Shared s(H, O, sh);
+    return dsv4::moe(ex.g.data(), ex.u.data(), ex.d.data(), weights, n, s.g, s.u, s.d, limit, y,
+                     x)
+               ? 1
+               : 0;
+}
+
+// dsv4_cuda::route_moe_ep2 (dsv4_cuda.cpp:1841-1906) for one token, one bank
+// of E experts (plus the shared expert, if given) serving both ranks.
+REF_API int ref_dsv4_route_moe_ep2(const float *x, int H, const float *router, const float *bias,
+                                   int E, float routed_scale, int O, const void *const *g,
+                                   const void *const *u, const void *const *d,
+                                   const void *const *gs, const void *const *us,
+                                   const void *const *ds, const void *const *sh, float limit,
+                                   float *out, float *peer_out) {
+    Experts ex(E, H, O, g, u, d, gs, us, ds);
+    Shared s(H, O, sh);
+    dsv4::ExpertSet *set =
+        dsv4::expert_set_create(ex.g.data(), ex.u.data(), ex.d.data(), E, s.g, s.u, s.d);
+    dsv4::Tensor *tg = nullptr, *tb = nullptr;
+    dsv4::upload_f32(&tg, router, E, H, 0);
+    if (bias)
+        dsv4::upload_f32(&tb, bias, E, 1, 0);
+    dsv4::Activation *a = act_from(x, H);
+    dsv4::Activation *ao = dsv4::activation_create(0, H);
+    dsv4::Activation *po = dsv4::activation_create(0, H);
+    const bool ok = dsv4::route_moe_ep2(a, tg, tb, nullptr, nullptr, nullptr, 0, routed_scale,
+                                        set, set, limit, ao, po);
+    if (ok) {
+        dsv4::activation_download(out, ao, H);
+        dsv4::activation_download(peer_out, po, H);
+    }
+    for (dsv4::Activation *p : {a, ao, po})
+        dsv4::activation_free(p);
+    dsv4::tensor_free(tg);
+    dsv4::tensor_free(tb);
+    dsv4::expert_set_free(set);
+    return ok ? 1 : 0;
 }
