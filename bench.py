@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--prefill-steps", type=int, default=10)
     ap.add_argument("--no-ep", action="store_true", help="skip the config[4] expert-parallel leg")
     ap.add_argument("--ep-steps", type=int, default=20)
+    ap.add_argument("--no-dsv4", action="store_true",
+                    help="skip the DeepSeek-V4 expert-split (EP2) leg")
+    ap.add_argument("--dsv4-steps", type=int, default=100)
     ap.add_argument("--prefill-tokens", type=int, default=4096,
                     help="config[3]: 4096; fewer only to size a profiler capture")
     ap.add_argument("--experts", type=int, default=256,
@@ -587,6 +590,100 @@ def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
 
 
 # ------------------------------------------------------------ CPU baseline --
+def dsv4_bench(moe, torch, dist, rank, world, wl, steps, T=32):
+    """DeepSeek-V4 MoE step (the reference's moe_layer_ep2 with
+    route_moe_ep2, dsv4.cpp:2863-3010) at decode: T tokens, hidden 7168, 256
+    MXFP4 experts of intermediate 2048 (the config[1] bank), top-6 by
+    sqrt(softplus) + bias, clamped SwiGLU (limit 7), an int8-row dense shared
+    MLP in the tail and routed_scale 2.5.  The reference names no DeepSeek-V4
+    shape; these are stand-in sizes of that class.  The experts are split
+    over the ranks (e on rank e % world; two ranks is the reference's EP2)
+    and the partial outputs all-reduced over NCCL; every rank processes the
+    same T tokens, so tokens/s = T / step time (max over ranks)."""
+    import dsv4
+    D, I, E = CFG["D"], CFG["I"], CFG["E"]
+    g = torch.Generator(device="cuda").manual_seed(4242)  # the same on every rank
+    x = torch.randn((T, D), generator=g, device="cuda")
+    h0 = torch.randn((T, D), generator=g, device="cuda")
+    router = torch.randn((E, D), generator=g, device="cuda").mul_(2.0 / D ** 0.5)
+    bias = torch.randn((E,), generator=g, device="cuda").mul_(0.1)
+    dense = [moe.FMT_INT8_ROW]
+    for shape in ((I, D), (I, D), (D, I)):
+        q = torch.randint(-127, 128, shape, generator=g, device="cuda",
+                          dtype=torch.int32).to(torch.int8)
+        dense.append((q, torch.full((shape[0],), 4e-4, device="cuda")))
+    mine = list(range(rank, E, world))
+    tables = [t[mine].contiguous() for t in wl.tables]
+    ops = dsv4.CudaOps(torch, E, D, I, 7.0, router, bias, tables, rank, world, T,
+                       routed_scale=2.5, dense_shared=tuple(dense))
+    layer = dsv4.EP2Layer(ops, rank, world)
+    h = h0.clone()
+
+    def step():
+        layer.forward(x, h, dist)
+
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    idx, _ = ops.route(x)
+    experts_touched = len(set(idx.flatten().tolist()))
+    local_touched = len([e for e in set(idx.flatten().tolist()) if e % world == rank])
+    ebytes = 3 * (I * D // 2 + I * D // 32)
+    res = {"workload": f"DeepSeek-V4-class MoE step: {T} tokens, hidden {D}, {E} MXFP4 experts "
+                       f"(inter {I}) top-6 sqrt(softplus)+bias, clamped SwiGLU, int8-row dense "
+                       "shared MLP, routed_scale 2.5",
+           "ranks": world, "placement": "strided e % ranks (2 ranks = the reference's EP2 "
+                                        "parity split)",
+           "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms,
+           "experts_touched": experts_touched, "rank0_experts_touched": local_touched,
+           "rank0_expert_bytes_per_step": local_touched * ebytes,
+           "allreduce_bytes_per_step": T * D * 4 if world > 1 else 0,
+           "steps": steps, "warmup": 5}
+    if rank == 0 and world == 1:
+        res["cpu_reference"] = dsv4_cpu_reference(torch, wl, x, router, bias, idx)
+    return res
+
+
+def dsv4_cpu_reference(torch, wl, x, router, bias, idx, tokens=2):
+    """The reference's DeepSeek-V4 CPU tier (dsv4_cuda::route_moe_ep2 in
+    oracle/_ref, one thread) on the first tokens of the step: the bank holds
+    only the experts those tokens route to (host copies), the rest absent."""
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        from oracle import Oracle
+        ref = Oracle("reference")
+        E = CFG["E"]
+        used = sorted({int(e) for e in idx[:tokens].flatten().tolist()})
+        bank = [None] * E
+        for e in used:
+            bank[e] = [(wl.gp[e].cpu().numpy(), wl.gs[e].cpu().numpy()),
+                       (wl.up[e].cpu().numpy(), wl.us[e].cpu().numpy()),
+                       (wl.dp[e].cpu().numpy(), wl.ds[e].cpu().numpy())]
+        xs, rs, bs = x.cpu().numpy(), router.cpu().numpy(), bias.cpu().numpy()
+        t0 = time.perf_counter()
+        for t in range(tokens):
+            ref.dsv4_route_moe_ep2(xs[t], rs, bs, 1.0, CFG["I"], bank, None, 7.0)
+        sec = time.perf_counter() - t0
+        return {"tokens_per_s": tokens / sec, "cores": 1, "kind": "reference",
+                "sample": f"{tokens} tokens through route_moe_ep2 (both parity ranks in one "
+                          f"host process, as the reference runs them), {sec:.1f} s"}
+    except Exception as ex:  # the reference build may be absent
+        return {"tokens_per_s": None, "sample": f"unavailable: {ex}"}
+
+
 def cpu_reference_rate(n_threads, rounds, expert_rows_per_call, host_experts=None):
     """Reference moe_block (oracle/_ref) on host threads.
 
@@ -805,6 +902,11 @@ def main():
         ep_res["weak_scaling"] = (ep_bench(moe, torch, dist, rank, world, args.ep_steps, weak=True)
                                   if world > 1 else "same workload as the strong run at 1 GPU")
 
+    # DeepSeek-V4 MoE step, experts split over all ranks (two ranks = EP2)
+    dsv4_res = None
+    if not args.no_dsv4:
+        dsv4_res = dsv4_bench(moe, torch, dist, rank, world, wl, args.dsv4_steps)
+
     # config[3] prefill (tensor-core kernels), per rank
     prefill = None
     tier = None
@@ -865,6 +967,7 @@ def main():
             "expert_tier": tier,
             "epilogue": epilogue,
             "expert_parallel": ep_res,
+            "dsv4_expert_split": dsv4_res,
         }
         if prefill and cpu and cpu.get("value"):
             # The reference's rate in expert rows/s (9 rows per config[1] token)

@@ -726,71 +726,398 @@ template <int PHASE> __global__ void __launch_bounds__(256) generic_ffn_kernel(c
     }
 }
 
-// Generic dequantised GEMM y[S,O] = x[S,I] . W[O,I]^T (warp per output row).
-// y[S,O] = x[S,I] . W[O,I]^T, the reference's arithmetic per output
-// (quant.cpp:143-156, 203-228, 255-268, 298-321; DeepSeek-V4's FP8 tiles,
-// dsv4_cuda.cpp:618-623): acc += x[i] * w[i] in ascending i, each product and
-// sum rounded on its own, w = q * scale as the reference decodes it; int8
-// rows (fmt 8) take the row scale at the end.  So
-// the result is bit-identical to the reference's matmuls.  A lane per row of
-// x (up to 32 per CTA column), a warp per kMmRows rows of W.  Each K tile of
-// x and of the CTA's W rows (decoded to f32) is staged in shared memory with
-// coalesced loads; the inner loop reads x per lane and W as a broadcast.
-constexpr int kMmRows = 4;   // W rows per warp
-constexpr int kMmWarps = 8;  // warps per CTA
-constexpr int kMmKt = 64;    // K tile
-__global__ void __launch_bounds__(256) matmul_generic_kernel(int fmt, float *y, const float *x,
-                                                             const void *w, const void *sc,
-                                                             int S, int I, int O) {
-    constexpr int RC = kMmWarps * kMmRows; // W rows per CTA
-    __shared__ float xs[32][kMmKt + 1];
-    __shared__ float wsm[RC][kMmKt];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int s0 = blockIdx.y * 32, ns = min(32, S - s0);
-    const int oc = blockIdx.x * RC; // the CTA's first W row
-    float acc[kMmRows];
+// Sequential-order dot products for small row counts, the reference's
+// arithmetic per output (quant.cpp:143-156, 203-228, 255-268, 298-321;
+// DeepSeek-V4's FP8 tiles, dsv4_cuda.cpp:618-623): acc += x[i] * w[i] in
+// ascending i, each product and sum rounded on its own (no contraction),
+// w = q * scale as the reference decodes it.  So results are bit-identical
+// to the reference's host loops.
+//
+// A CTA covers 32 rows of x and 4*OT rows of W with 128 threads; thread
+// (s, og) = (tid / 4, tid % 4) owns rows og*OT .. og*OT+OT-1 of the tile for
+// x row s, so every thread runs OT independent chains.  Each K tile of 64
+// is staged in shared memory (x transposed to [k][s], W decoded to f32
+// [o][k], both padded against bank conflicts) from coalesced loads, and the
+// next tile's global loads are issued into registers before the current
+// tile is consumed, so their latency hides behind the chains.  The chains'
+// length (I) bounds a launch from below, so the grid spreads over W rows:
+// small row counts (decode batches, the router) still fill the SMs.
+constexpr int kSeqS = 32;        // x rows per CTA
+constexpr int kSeqKt = 64;       // K tile
+constexpr int kSeqThreads = 128; // (32 x rows) x (4 W-row groups)
+
+__device__ __forceinline__ float x_to_f32(float v) { return v; }
+__device__ __forceinline__ float x_to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// One W element as f32 (int8 rows: the raw code; the row scale comes last).
+__device__ __forceinline__ float seq_w(const void *w, const void *sc, int fmt, int o, int k,
+                                       int I) {
+    if (fmt == MVLLM_FMT_INT8_ROW)
+        return static_cast<float>(static_cast<const int8_t *>(w)[static_cast<size_t>(o) * I + k]);
+    return deq_elem(w, sc, fmt, o, k, I);
+}
+
+template <int OT, typename TX>
+__device__ __forceinline__ void seq_dot_tile(const TX *__restrict__ x, const void *w,
+                                             const void *sc, int fmt, int S, int I, int O,
+                                             int s0, int oc, float (&acc)[OT]) {
+    constexpr int RO = 4 * OT;                          // W rows per CTA
+    constexpr int XPER = kSeqS * kSeqKt / kSeqThreads;  // x values staged per thread
+    constexpr int WPER = RO * kSeqKt / kSeqThreads;     // W values staged per thread
+    static_assert(WPER >= 1 && (RO * kSeqKt) % kSeqThreads == 0, "tile shape");
+    __shared__ float xs[kSeqKt][kSeqS + 1];
+    __shared__ float wsm[RO][kSeqKt + 1];
+    const int tid = threadIdx.x;
+    const int s_loc = tid >> 2, og = tid & 3;
+    const int ns = min(kSeqS, S - s0), no = min(RO, O - oc);
+    float xr[XPER], wr[WPER];
+    auto fetch = [&](int k0) {
+        const int kn = min(kSeqKt, I - k0);
 #pragma unroll
-    for (int r = 0; r < kMmRows; ++r)
+        for (int i = 0; i < XPER; ++i) {
+            const int j = i * kSeqThreads + tid;
+            const int s = j / kSeqKt, k = j % kSeqKt;
+            xr[i] = (s < ns && k < kn) ? x_to_f32(x[static_cast<size_t>(s0 + s) * I + k0 + k])
+                                       : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < WPER; ++i) {
+            const int j = i * kSeqThreads + tid;
+            const int r = j / kSeqKt, k = j % kSeqKt;
+            wr[i] = (r < no && k < kn) ? seq_w(w, sc, fmt, oc + r, k0 + k, I) : 0.f;
+        }
+    };
+#pragma unroll
+    for (int r = 0; r < OT; ++r)
         acc[r] = 0.f;
-    for (int k0 = 0; k0 < I; k0 += kMmKt) {
-        const int kn = min(kMmKt, I - k0);
-        __syncthreads();
-        for (int j = threadIdx.x; j < 32 * kMmKt; j += blockDim.x) {
-            const int s = j / kMmKt, k = j - s * kMmKt;
-            xs[s][k] = (s < ns && k < kn) ? x[static_cast<size_t>(s0 + s) * I + k0 + k] : 0.f;
+    fetch(0);
+    for (int k0 = 0; k0 < I; k0 += kSeqKt) {
+        const int kn = min(kSeqKt, I - k0);
+        __syncthreads(); // the previous tile is consumed
+#pragma unroll
+        for (int i = 0; i < XPER; ++i) {
+            const int j = i * kSeqThreads + tid;
+            xs[j % kSeqKt][j / kSeqKt] = xr[i];
         }
-        for (int j = threadIdx.x; j < RC * kMmKt; j += blockDim.x) {
-            const int r = j / kMmKt, k = j - r * kMmKt, o = oc + r;
-            float v = 0.f;
-            if (o < O && k < kn)
-                v = fmt == MVLLM_FMT_INT8_ROW
-                        ? static_cast<float>(static_cast<const int8_t *>(
-                              w)[static_cast<size_t>(o) * I + k0 + k])
-                        : deq_elem(w, sc, fmt, o, k0 + k, I);
-            wsm[r][k] = v;
+#pragma unroll
+        for (int i = 0; i < WPER; ++i) {
+            const int j = i * kSeqThreads + tid;
+            wsm[j / kSeqKt][j % kSeqKt] = wr[i];
         }
         __syncthreads();
+        if (k0 + kSeqKt < I)
+            fetch(k0 + kSeqKt); // in flight while this tile's chains run
 #pragma unroll 4
         for (int kk = 0; kk < kn; ++kk) {
-            const float xv = xs[lane][kk];
+            const float xv = xs[kk][s_loc];
 #pragma unroll
-            for (int r = 0; r < kMmRows; ++r)
-                acc[r] = __fadd_rn(acc[r], __fmul_rn(xv, wsm[warp * kMmRows + r][kk]));
-        }
-    }
-    if (lane < ns) {
-#pragma unroll
-        for (int r = 0; r < kMmRows; ++r) {
-            const int o = oc + warp * kMmRows + r;
-            if (o < O)
-                y[static_cast<size_t>(s0 + lane) * O + o] =
-                    fmt == MVLLM_FMT_INT8_ROW ? __fmul_rn(acc[r], static_cast<const float *>(sc)[o])
-                                              : acc[r];
+            for (int r = 0; r < OT; ++r)
+                acc[r] = __fadd_rn(acc[r], __fmul_rn(xv, wsm[og * OT + r][kk]));
         }
     }
 }
-inline dim3 matmul_grid(int S, int O) {
-    return dim3((O + kMmWarps * kMmRows - 1) / (kMmWarps * kMmRows), (S + 31) / 32);
+
+// The same chains with the operands streamed through a cp.async ring
+// (kAsStages chunks of kAsKc in flight per CTA): the per-tile fetch above
+// leaves a few KB per CTA in flight, which bounds a weight stream far below
+// HBM bandwidth (Little's law); here three chunks of x and of the raw W rows
+// are always on their way.  Each landed W chunk is decoded once into f32 in
+// shared memory (the decoders of deq_elem), then every thread runs its
+// chains over it in ascending k, so results are identical to seq_dot_tile.
+// Needs 16-byte aligned x and W and rows that are whole 16-byte pieces
+// (seq_async_ok); other shapes take seq_dot_tile.
+constexpr int kAsKc = 128;   // K chunk
+constexpr int kAsStages = 4; // chunks in the ring
+
+__host__ __device__ constexpr int seq_w_bits(int fmt) {
+    return fmt == MVLLM_FMT_F32 ? 32
+           : (fmt == MVLLM_FMT_INT8_ROW || fmt == MVLLM_FMT_FP8_B128) ? 8
+                                                                      : 4;
+}
+template <typename TX>
+inline bool seq_async_ok(const TX *x, const void *w, int fmt, int I) {
+    const long xb = long(I) * static_cast<long>(sizeof(TX));
+    const long wbits = long(I) * seq_w_bits(fmt);
+    return (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(w) & 15) == 0 && xb % 16 == 0 && wbits % 128 == 0;
+}
+
+// RO W rows per CTA, OT of them per thread: 32 * RO / OT threads, thread
+// (s, g) = (tid / (RO/OT), tid % (RO/OT)).  Shared memory: the x ring
+// [stage][32][Kc + 16 bytes], the raw W ring [stage][RO][row chunk + 16
+// bytes] (the pads keep 16-byte alignment and spread rows over the banks)
+// and the decoded chunk [Kc][RO] f32.
+template <int RO, int OT, int FMT, typename TX> struct SeqAsync {
+    static constexpr int G = RO / OT;
+    static constexpr int THREADS = kSeqS * G;
+    static constexpr int XRB = kAsKc * static_cast<int>(sizeof(TX)) + 16;
+    static constexpr int WCB = kAsKc * seq_w_bits(FMT) / 8; // W bytes per row chunk
+    static constexpr int WRB = WCB + 16;
+    static constexpr int XPC = kAsKc * static_cast<int>(sizeof(TX)) / 16;
+    static constexpr int WPC = WCB / 16;
+    static constexpr size_t SMEM = size_t(kAsStages) * (kSeqS * XRB + RO * WRB) +
+                                   size_t(RO) * kAsKc * sizeof(float);
+};
+
+// Four consecutive x values (16-byte aligned for f32, 8-byte for bf16).
+__device__ __forceinline__ float4 ld4_x(const float *p) {
+    return *reinterpret_cast<const float4 *>(p);
+}
+__device__ __forceinline__ float4 ld4_x(const __nv_bfloat16 *p) {
+    const uint2 v = *reinterpret_cast<const uint2 *>(p);
+    return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u),
+                       __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
+}
+
+__device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Element kl of a raw W row chunk starting at global column k0 (k0 a
+// multiple of kAsKc, so nibble parity is kept), decoded as deq_elem does.
+template <int FMT>
+__device__ __forceinline__ float seq_deq_raw(const uint8_t *row, int kl, const void *sc, int o,
+                                             int k, int I) {
+    if constexpr (FMT == MVLLM_FMT_F32) {
+        return reinterpret_cast<const float *>(row)[kl];
+    } else if constexpr (FMT == MVLLM_FMT_INT8_ROW) {
+        return static_cast<float>(static_cast<int8_t>(row[kl]));
+    } else if constexpr (FMT == MVLLM_FMT_FP8_B128) {
+        const uint8_t e =
+            static_cast<const uint8_t *>(sc)[static_cast<size_t>(o >> 7) * ((I + 127) / 128) +
+                                             (k >> 7)];
+        return __fmul_rn(e4m3fn_to_f32(row[kl]), e8m0_to_f32(e));
+    } else {
+        const uint8_t b = row[kl >> 1];
+        const uint32_t nib = (kl & 1) ? (b >> 4) : (b & 15u);
+        if constexpr (FMT == MVLLM_FMT_INT4_G64) {
+            const float scv =
+                static_cast<const float *>(sc)[static_cast<size_t>(o) * ((I + 63) / 64) + (k >> 6)];
+            return static_cast<float>(static_cast<int>(nib) - 8) * scv;
+        } else {
+            const uint8_t e =
+                static_cast<const uint8_t *>(sc)[static_cast<size_t>(o) * ((I + 31) / 32) +
+                                                 (k >> 5)];
+            const float mag = (nib & 7u) == 0   ? 0.f
+                              : (nib & 7u) == 1 ? 0.5f
+                              : (nib & 7u) == 2 ? 1.f
+                              : (nib & 7u) == 3 ? 1.5f
+                              : (nib & 7u) == 4 ? 2.f
+                              : (nib & 7u) == 5 ? 3.f
+                              : (nib & 7u) == 6 ? 4.f
+                                                : 6.f;
+            return ((nib & 8u) ? -mag : mag) * ue8m0_to_f32(e);
+        }
+    }
+}
+
+template <int RO, int OT, int FMT, typename TX>
+__device__ __forceinline__ void seq_dot_async(const TX *__restrict__ x, const void *w,
+                                              const void *sc, int S, int I, int O, int s0,
+                                              int oc, float (&acc)[OT], uint8_t *smem) {
+    using L = SeqAsync<RO, OT, FMT, TX>;
+    uint8_t *xst = smem;                                             // [stage][32][XRB]
+    uint8_t *wst = xst + size_t(kAsStages) * kSeqS * L::XRB;         // [stage][RO][WRB]
+    float *wsm = reinterpret_cast<float *>(wst + size_t(kAsStages) * RO * L::WRB); // [Kc][RO]
+    const int tid = threadIdx.x;
+    const int s_loc = tid / L::G, og = tid % L::G;
+    const int ns = min(kSeqS, S - s0), no = min(RO, O - oc);
+    const size_t xrow = size_t(I) * sizeof(TX), wrow = size_t(I) * seq_w_bits(FMT) / 8;
+    const int nchunks = (I + kAsKc - 1) / kAsKc;
+    const uint8_t *xb = reinterpret_cast<const uint8_t *>(x);
+    const uint8_t *wbp = static_cast<const uint8_t *>(w);
+    auto issue = [&](int c) {
+        const int st = c % kAsStages;
+        const size_t xk0 = size_t(c) * kAsKc * sizeof(TX), wk0 = size_t(c) * L::WCB;
+        for (int p = tid; p < kSeqS * L::XPC; p += L::THREADS) {
+            const int srow = p / L::XPC, pc = p % L::XPC;
+            const size_t off = xk0 + size_t(pc) * 16;
+            const bool ok = srow < ns && off < xrow;
+            cp_async16_zfill(xst + (size_t(st) * kSeqS + srow) * L::XRB + pc * 16,
+                             ok ? xb + size_t(s0 + srow) * xrow + off : xb, ok ? 16 : 0);
+        }
+        for (int p = tid; p < RO * L::WPC; p += L::THREADS) {
+            const int r = p / L::WPC, pc = p % L::WPC;
+            const size_t off = wk0 + size_t(pc) * 16;
+            const bool ok = r < no && off < wrow;
+            cp_async16_zfill(wst + (size_t(st) * RO + r) * L::WRB + pc * 16,
+                             ok ? wbp + size_t(oc + r) * wrow + off : wbp, ok ? 16 : 0);
+        }
+    };
+#pragma unroll
+    for (int r = 0; r < OT; ++r)
+        acc[r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < kAsStages - 1; ++c) {
+        if (c < nchunks)
+            issue(c);
+        cp_async_commit();
+    }
+    for (int c = 0; c < nchunks; ++c) {
+        const int st = c % kAsStages;
+        const int k0 = c * kAsKc, kn = min(kAsKc, I - k0);
+        cp_async_wait<kAsStages - 2>();
+        __syncthreads(); // chunk c landed for every thread; chunk c-1 consumed
+        // decoded to [k][row]: consecutive threads take consecutive rows
+        for (int j = tid; j < RO * kAsKc; j += L::THREADS) {
+            const int r = j % RO, kl = j / RO;
+            float v = 0.f;
+            if (r < no && kl < kn)
+                v = seq_deq_raw<FMT>(wst + (size_t(st) * RO + r) * L::WRB, kl, sc, oc + r,
+                                     k0 + kl, I);
+            wsm[kl * RO + r] = v;
+        }
+        if (c + kAsStages - 1 < nchunks)
+            issue(c + kAsStages - 1);
+        cp_async_commit();
+        __syncthreads(); // decoded chunk visible
+        // kn is a multiple of 4 (whole 16-byte x pieces): x four k at a time,
+        // the thread's OT weights of one k in one vector load.
+        const TX *xs = reinterpret_cast<const TX *>(xst + (size_t(st) * kSeqS + s_loc) * L::XRB);
+        const float *wrow_s = wsm + og * OT;
+#pragma unroll 2
+        for (int kk = 0; kk < kn; kk += 4) {
+            const float4 x4 = ld4_x(xs + kk);
+            const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float *wq = wrow_s + (kk + q) * RO;
+                float wv[OT];
+                if constexpr (OT == 4) {
+                    const float4 w4 = *reinterpret_cast<const float4 *>(wq);
+                    wv[0] = w4.x;
+                    wv[1 % OT] = w4.y;
+                    wv[2 % OT] = w4.z;
+                    wv[3 % OT] = w4.w;
+                } else if constexpr (OT == 2) {
+                    const float2 w2 = *reinterpret_cast<const float2 *>(wq);
+                    wv[0] = w2.x;
+                    wv[1 % OT] = w2.y;
+                } else {
+#pragma unroll
+                    for (int r = 0; r < OT; ++r)
+                        wv[r] = wq[r];
+                }
+#pragma unroll
+                for (int r = 0; r < OT; ++r)
+                    acc[r] = __fadd_rn(acc[r], __fmul_rn(xv[q], wv[r]));
+            }
+        }
+    }
+    cp_async_wait<0>();
+}
+
+// Generic dequantised GEMM y[S,O] = x[S,I] . W[O,I]^T (f32), fmt 0 / 4 / 7 /
+// 8 / 9, bit-identical to the reference's matmuls; int8 rows (fmt 8) take the
+// row scale at the end (quant.cpp:255-268).  16 W rows per CTA: on the
+// cp.async ring 2 per thread (256 threads, so eight warps per SM hide the
+// chains' latency), otherwise seq_dot_tile's 4 per thread.
+constexpr int kMmRO = 16;
+constexpr int kMmOT = 2;
+// Up to two products over the same x in one launch (blockIdx.z picks one):
+// a gated FFN's gate and up projections share the x stream and fill twice
+// the CTAs.
+struct MmOut {
+    float *y[2];
+    const void *w[2];
+    const void *sc[2];
+};
+template <int FMT>
+__global__ void __launch_bounds__(SeqAsync<kMmRO, kMmOT, FMT, float>::THREADS)
+    matmul_async_kernel(const MmOut p, const float *x, int S, int I, int O) {
+    using L = SeqAsync<kMmRO, kMmOT, FMT, float>;
+    extern __shared__ __align__(16) uint8_t seq_smem[];
+    const int z = blockIdx.z;
+    const int s0 = blockIdx.y * kSeqS, oc = blockIdx.x * kMmRO;
+    float acc[kMmOT];
+    seq_dot_async<kMmRO, kMmOT, FMT>(x, p.w[z], p.sc[z], S, I, O, s0, oc, acc, seq_smem);
+    const int s = s0 + threadIdx.x / L::G;
+    if (s < S) {
+#pragma unroll
+        for (int r = 0; r < kMmOT; ++r) {
+            const int o = oc + (threadIdx.x % L::G) * kMmOT + r;
+            if (o < O)
+                p.y[z][static_cast<size_t>(s) * O + o] =
+                    FMT == MVLLM_FMT_INT8_ROW
+                        ? __fmul_rn(acc[r], static_cast<const float *>(p.sc[z])[o])
+                        : acc[r];
+        }
+    }
+}
+__global__ void __launch_bounds__(kSeqThreads) matmul_generic_kernel(int fmt, const MmOut p,
+                                                                     const float *x, int S,
+                                                                     int I, int O) {
+    const int z = blockIdx.z;
+    const int s0 = blockIdx.y * kSeqS, oc = blockIdx.x * kMmRO;
+    float acc[4];
+    seq_dot_tile<4>(x, p.w[z], p.sc[z], fmt, S, I, O, s0, oc, acc);
+    const int s = s0 + (threadIdx.x >> 2);
+    if (s < S) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int o = oc + (threadIdx.x & 3) * 4 + r;
+            if (o < O)
+                p.y[z][static_cast<size_t>(s) * O + o] =
+                    fmt == MVLLM_FMT_INT8_ROW
+                        ? __fmul_rn(acc[r], static_cast<const float *>(p.sc[z])[o])
+                        : acc[r];
+        }
+    }
+}
+inline dim3 matmul_grid(int S, int O, int n = 1) {
+    return dim3((O + kMmRO - 1) / kMmRO, (S + kSeqS - 1) / kSeqS, n);
+}
+
+template <int FMT>
+inline cudaError_t matmul_async_launch(cudaStream_t st, const MmOut &p, int n, const float *x,
+                                       int S, int I, int O) {
+    using L = SeqAsync<kMmRO, kMmOT, FMT, float>;
+    const cudaError_t e = cudaFuncSetAttribute(
+        matmul_async_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::SMEM));
+    if (e != cudaSuccess)
+        return e;
+    matmul_async_kernel<FMT><<<matmul_grid(S, O, n), L::THREADS, L::SMEM, st>>>(p, x, S, I, O);
+    return cudaGetLastError();
+}
+
+// y_j = x . W_j^T for the n (1 or 2) products of p, all of format fmt and
+// shape [O, I]: on the cp.async ring where x and every W allow it.
+inline cudaError_t matmul_generic_launch(cudaStream_t st, int fmt, const MmOut &p, int n,
+                                         const float *x, int S, int I, int O) {
+    bool async = true;
+    for (int j = 0; j < n; ++j)
+        async = async && seq_async_ok(x, p.w[j], fmt, I);
+    if (async) {
+        switch (fmt) {
+        case MVLLM_FMT_F32:
+            return matmul_async_launch<MVLLM_FMT_F32>(st, p, n, x, S, I, O);
+        case MVLLM_FMT_INT4_G64:
+            return matmul_async_launch<MVLLM_FMT_INT4_G64>(st, p, n, x, S, I, O);
+        case MVLLM_FMT_MXFP4:
+            return matmul_async_launch<MVLLM_FMT_MXFP4>(st, p, n, x, S, I, O);
+        case MVLLM_FMT_INT8_ROW:
+            return matmul_async_launch<MVLLM_FMT_INT8_ROW>(st, p, n, x, S, I, O);
+        case MVLLM_FMT_FP8_B128:
+            return matmul_async_launch<MVLLM_FMT_FP8_B128>(st, p, n, x, S, I, O);
+        default:
+            break;
+        }
+    }
+    matmul_generic_kernel<<<matmul_grid(S, O, n), kSeqThreads, 0, st>>>(fmt, p, x, S, I, O);
+    return cudaGetLastError();
+}
+inline cudaError_t matmul_generic_launch(cudaStream_t st, int fmt, float *y, const float *x,
+                                         const void *w, const void *sc, int S, int I, int O) {
+    const MmOut p{{y, nullptr}, {w, nullptr}, {sc, nullptr}};
+    return matmul_generic_launch(st, fmt, p, 1, x, S, I, O);
 }
 
 // rmsnorm per row, exactly as quant.cpp:384-398: the sum of squares in

@@ -1844,18 +1844,14 @@ int mvllm_moe_route_ex_dev(void *stream, const void *x, int x_dtype, int T, int 
     if (T == 0)
         return MVLLM_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    dim3 grid((E + 31) / 32, (T + 31) / 32);
-    if (grid.y > 65535)
+    if ((T + kSeqS - 1) / kSeqS > 65535)
         return fail(MVLLM_ERR_INVALID, "route_dev: T too large");
     if (x_dtype == MVLLM_DTYPE_BF16)
-        route_scores_kernel<__nv_bfloat16><<<grid, 1024, 0, st>>>(
-            static_cast<const __nv_bfloat16 *>(x), router, bias, T, H, E, score_fn, scores,
-            choice);
+        CUDA_TRY(route_scores_launch(st, static_cast<const __nv_bfloat16 *>(x), router, bias, T,
+                                     H, E, score_fn, scores, choice));
     else
-        route_scores_kernel<float><<<grid, 1024, 0, st>>>(static_cast<const float *>(x), router,
-                                                           bias, T, H, E, score_fn, scores,
-                                                           choice);
-    CUDA_TRY(cudaGetLastError());
+        CUDA_TRY(route_scores_launch(st, static_cast<const float *>(x), router, bias, T, H, E,
+                                     score_fn, scores, choice));
     return topk_launch(st, choice, scores, T, E, K, routed_scale, idx, wt);
 }
 
@@ -1989,9 +1985,8 @@ int mvllm_matmul_dev(void *stream, int fmt, float *y, const float *x, const void
         return fail(MVLLM_ERR_INVALID, "matmul_dev: invalid arguments");
     if (!ctx().inited)
         return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
-    matmul_generic_kernel<<<matmul_grid(S, O), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        fmt, y, x, w, scales, S, I, O);
-    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(matmul_generic_launch(static_cast<cudaStream_t>(stream), fmt, y, x, w, scales, S, I,
+                                   O));
     return MVLLM_OK;
 }
 
@@ -2034,9 +2029,7 @@ int mvllm_moe_epilogue_dev(void *stream, int T, int H, int L, const float *acc,
         src = norm;
     }
     if (up_w) {
-        matmul_generic_kernel<<<matmul_grid(T, H), 256, 0, st>>>(up_fmt, up, src, up_w,
-                                                                 up_scales, T, L, H);
-        CUDA_TRY(cudaGetLastError());
+        CUDA_TRY(matmul_generic_launch(st, up_fmt, up, src, up_w, up_scales, T, L, H));
         src = up;
     }
     const size_t n = size_t(T) * H;
@@ -2075,17 +2068,13 @@ int mvllm_moe_dense_ffn_dev(void *stream, int fmt, int T, int H, int O, const vo
     float *g = static_cast<float *>(workspace);
     float *u = g + size_t(T) * O;
     float *d = u + size_t(T) * O;
-    matmul_generic_kernel<<<matmul_grid(T, O), 256, 0, st>>>(fmt, g, x, gate_w, gate_s, T, H, O);
-    CUDA_TRY(cudaGetLastError());
-    matmul_generic_kernel<<<matmul_grid(T, O), 256, 0, st>>>(fmt, u, x, up_w, up_s, T, H, O);
-    CUDA_TRY(cudaGetLastError());
+    const MmOut gu{{g, u}, {gate_w, up_w}, {gate_s, up_s}};
+    CUDA_TRY(matmul_generic_launch(st, fmt, gu, 2, x, T, H, O));
     const size_t nh = size_t(T) * O;
     dense_act_kernel<<<int(std::min<size_t>((nh + 255) / 256, size_t(c.sms) * 16)), 256, 0, st>>>(
         g, u, nh, act, act_a, act_b);
     CUDA_TRY(cudaGetLastError());
-    matmul_generic_kernel<<<matmul_grid(T, H), 256, 0, st>>>(fmt, accumulate ? d : y, g, down_w,
-                                                             down_s, T, O, H);
-    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(matmul_generic_launch(st, fmt, accumulate ? d : y, g, down_w, down_s, T, O, H));
     if (accumulate) {
         const size_t ny = size_t(T) * H;
         add_rows_kernel<<<int(std::min<size_t>((ny + 255) / 256, size_t(c.sms) * 16)), 256, 0,

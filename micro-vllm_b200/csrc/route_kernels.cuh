@@ -14,7 +14,7 @@
 // and multiplies each normalised weight by routed_scale.
 #pragma once
 
-#include "common.cuh"
+#include "aux_kernels.cuh"
 
 namespace mvb {
 
@@ -60,45 +60,50 @@ __device__ __forceinline__ float route_score(float logit, int score_fn) {
                                                  : sigmoid_route(logit);
 }
 
-template <typename TX> __device__ __forceinline__ float to_f32(TX v);
-template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
-template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
-    return __bfloat162float(v);
-}
-
-// One CTA per 32 tokens x 32 experts, one thread per (token, expert): the dot
-// product runs sequentially over the hidden dimension, each product and each
-// sum rounded on its own (no contraction), exactly the reference's order.
-// x and router columns are staged 64 at a time in shared memory.
-template <typename TX>
-__global__ void __launch_bounds__(1024)
+// The router dot products in the reference's order (sequential f32 over H,
+// each product and sum rounded on its own): seq_dot_tile with one chain per
+// thread, CTAs of 32 tokens x 4 experts (E = 256, T = 32: 64 CTAs), then the
+// score function and the bias.
+template <typename TX, bool ASYNC>
+__global__ void __launch_bounds__(kSeqThreads)
     route_scores_kernel(const TX *__restrict__ x, const float *__restrict__ w,
                         const float *__restrict__ bias, int T, int H, int E, int score_fn,
                         float *__restrict__ scores, float *__restrict__ choice) {
-    __shared__ float xs[32][65];
-    __shared__ float wsm[32][65];
-    const int te = threadIdx.x & 31, tt = threadIdx.x >> 5; // expert lane, token warp
-    const int t0 = blockIdx.y * 32, e0 = blockIdx.x * 32;
-    float acc = 0.f;
-    for (int i0 = 0; i0 < H; i0 += 64) {
-        for (int j = threadIdx.x; j < 32 * 64; j += blockDim.x) {
-            const int r = j >> 6, c = j & 63;
-            const int i = i0 + c;
-            xs[r][c] = (t0 + r < T && i < H) ? to_f32(x[static_cast<size_t>(t0 + r) * H + i]) : 0.f;
-            wsm[r][c] = (e0 + r < E && i < H) ? w[static_cast<size_t>(e0 + r) * H + i] : 0.f;
-        }
-        __syncthreads();
-        const int n = min(64, H - i0);
-        for (int c = 0; c < n; ++c)
-            acc = __fadd_rn(acc, __fmul_rn(xs[tt][c], wsm[te][c]));
-        __syncthreads();
-    }
-    const int t = t0 + tt, e = e0 + te;
+    extern __shared__ __align__(16) uint8_t seq_smem[];
+    const int t0 = blockIdx.y * kSeqS, e0 = blockIdx.x * 4;
+    float acc[1];
+    if constexpr (ASYNC)
+        seq_dot_async<4, 1, MVLLM_FMT_F32>(x, w, nullptr, T, H, E, t0, e0, acc, seq_smem);
+    else
+        seq_dot_tile<1>(x, w, nullptr, MVLLM_FMT_F32, T, H, E, t0, e0, acc);
+    const int t = t0 + (threadIdx.x >> 2), e = e0 + (threadIdx.x & 3);
     if (t < T && e < E) {
-        const float s = route_score(acc, score_fn);
+        const float s = route_score(acc[0], score_fn);
         scores[static_cast<size_t>(t) * E + e] = s;
         choice[static_cast<size_t>(t) * E + e] = bias ? __fadd_rn(s, bias[e]) : s;
     }
+}
+
+template <typename TX>
+inline cudaError_t route_scores_launch(cudaStream_t st, const TX *x, const float *router,
+                                       const float *bias, int T, int H, int E, int score_fn,
+                                       float *scores, float *choice) {
+    const dim3 grid((E + 3) / 4, (T + kSeqS - 1) / kSeqS);
+    if (seq_async_ok(x, router, MVLLM_FMT_F32, H)) {
+        using L = SeqAsync<4, 1, MVLLM_FMT_F32, TX>;
+        static_assert(L::THREADS == kSeqThreads, "thread mapping");
+        const cudaError_t e = cudaFuncSetAttribute(
+            route_scores_kernel<TX, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            int(L::SMEM));
+        if (e != cudaSuccess)
+            return e;
+        route_scores_kernel<TX, true><<<grid, kSeqThreads, L::SMEM, st>>>(
+            x, router, bias, T, H, E, score_fn, scores, choice);
+    } else {
+        route_scores_kernel<TX, false><<<grid, kSeqThreads, 0, st>>>(x, router, bias, T, H, E,
+                                                                    score_fn, scores, choice);
+    }
+    return cudaGetLastError();
 }
 
 constexpr int kTopkMaxPerLane = 32; // E <= 1024
