@@ -843,7 +843,9 @@ inline bool seq_async_ok(const TX *x, const void *w, int fmt, int I) {
 }
 
 // RO W rows per CTA, OT of them per thread: 32 * RO / OT threads, thread
-// (s, g) = (tid / (RO/OT), tid % (RO/OT)).  Shared memory: the x ring
+// (s, g) = (lane, warp): a warp runs one group of OT rows for all 32 x rows,
+// so every W value it reads is one broadcast and the x values of a lane's
+// row come four at a time.  Shared memory: the x ring
 // [stage][32][Kc + 16 bytes], the raw W ring [stage][RO][row chunk + 16
 // bytes] (the pads keep 16-byte alignment and spread rows over the banks)
 // and the decoded chunk [Kc][RO] f32.
@@ -857,6 +859,8 @@ template <int RO, int OT, int FMT, typename TX> struct SeqAsync {
     static constexpr int WPC = WCB / 16;
     static constexpr size_t SMEM = size_t(kAsStages) * (kSeqS * XRB + RO * WRB) +
                                    size_t(RO) * kAsKc * sizeof(float);
+    __device__ static int s_of(int tid) { return tid & 31; }
+    __device__ static int g_of(int tid) { return tid >> 5; }
 };
 
 // Four consecutive x values (16-byte aligned for f32, 8-byte for bf16).
@@ -928,7 +932,7 @@ __device__ __forceinline__ void seq_dot_async(const TX *__restrict__ x, const vo
     uint8_t *wst = xst + size_t(kAsStages) * kSeqS * L::XRB;         // [stage][RO][WRB]
     float *wsm = reinterpret_cast<float *>(wst + size_t(kAsStages) * RO * L::WRB); // [Kc][RO]
     const int tid = threadIdx.x;
-    const int s_loc = tid / L::G, og = tid % L::G;
+    const int s_loc = L::s_of(tid), og = L::g_of(tid);
     const int ns = min(kSeqS, S - s0), no = min(RO, O - oc);
     const size_t xrow = size_t(I) * sizeof(TX), wrow = size_t(I) * seq_w_bits(FMT) / 8;
     const int nchunks = (I + kAsKc - 1) / kAsKc;
@@ -1039,11 +1043,11 @@ __global__ void __launch_bounds__(SeqAsync<kMmRO, kMmOT, FMT, float>::THREADS)
     const int s0 = blockIdx.y * kSeqS, oc = blockIdx.x * kMmRO;
     float acc[kMmOT];
     seq_dot_async<kMmRO, kMmOT, FMT>(x, p.w[z], p.sc[z], S, I, O, s0, oc, acc, seq_smem);
-    const int s = s0 + threadIdx.x / L::G;
+    const int s = s0 + L::s_of(threadIdx.x);
     if (s < S) {
 #pragma unroll
         for (int r = 0; r < kMmOT; ++r) {
-            const int o = oc + (threadIdx.x % L::G) * kMmOT + r;
+            const int o = oc + L::g_of(threadIdx.x) * kMmOT + r;
             if (o < O)
                 p.y[z][static_cast<size_t>(s) * O + o] =
                     FMT == MVLLM_FMT_INT8_ROW

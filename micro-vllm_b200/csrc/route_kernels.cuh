@@ -76,7 +76,9 @@ __global__ void __launch_bounds__(kSeqThreads)
         seq_dot_async<4, 1, MVLLM_FMT_F32>(x, w, nullptr, T, H, E, t0, e0, acc, seq_smem);
     else
         seq_dot_tile<1>(x, w, nullptr, MVLLM_FMT_F32, T, H, E, t0, e0, acc);
-    const int t = t0 + (threadIdx.x >> 2), e = e0 + (threadIdx.x & 3);
+    using L = SeqAsync<4, 1, MVLLM_FMT_F32, TX>;
+    const int t = t0 + (ASYNC ? L::s_of(threadIdx.x) : threadIdx.x >> 2);
+    const int e = e0 + (ASYNC ? L::g_of(threadIdx.x) : threadIdx.x & 3);
     if (t < T && e < E) {
         const float s = route_score(acc[0], score_fn);
         scores[static_cast<size_t>(t) * E + e] = s;
