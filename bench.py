@@ -594,8 +594,10 @@ def dsv4_bench(moe, torch, dist, rank, world, wl, steps, T=32):
     """DeepSeek-V4 MoE step (the reference's moe_layer_ep2 with
     route_moe_ep2, dsv4.cpp:2863-3010) at decode: T tokens, hidden 7168, 256
     MXFP4 experts of intermediate 2048 (the config[1] bank), top-6 by
-    sqrt(softplus) + bias, clamped SwiGLU (limit 7), an int8-row dense shared
-    MLP in the tail and routed_scale 2.5.  The reference names no DeepSeek-V4
+    sqrt(softplus) + bias, clamped SwiGLU (limit 7), an int4-g64 dense shared
+    MLP in the tail (QuantMat 4-bit, the reference's default dense_bits; run
+    through the MoE kernels as one expert) and routed_scale 2.5.  The
+    reference names no DeepSeek-V4
     shape; these are stand-in sizes of that class.  The experts are split
     over the ranks (e on rank e % world; two ranks is the reference's EP2)
     and the partial outputs all-reduced over NCCL; every rank processes the
@@ -607,11 +609,14 @@ def dsv4_bench(moe, torch, dist, rank, world, wl, steps, T=32):
     h0 = torch.randn((T, D), generator=g, device="cuda")
     router = torch.randn((E, D), generator=g, device="cuda").mul_(2.0 / D ** 0.5)
     bias = torch.randn((E,), generator=g, device="cuda").mul_(0.1)
-    dense = [moe.FMT_INT8_ROW]
+    dense = [moe.FMT_INT4_G64]
     for shape in ((I, D), (I, D), (D, I)):
-        q = torch.randint(-127, 128, shape, generator=g, device="cuda",
-                          dtype=torch.int32).to(torch.int8)
-        dense.append((q, torch.full((shape[0],), 4e-4, device="cuda")))
+        w = torch.randn(shape, generator=g, device="cuda").mul_(0.02)
+        pk = torch.empty((shape[0], shape[1] // 2), dtype=torch.uint8, device="cuda")
+        sc = torch.empty((shape[0], shape[1] // 64), dtype=torch.float32, device="cuda")
+        moe.quantize_int4_g64_dev(w, pk, sc)
+        dense.append((pk, sc))
+    del w
     mine = list(range(rank, E, world))
     tables = [t[mine].contiguous() for t in wl.tables]
     ops = dsv4.CudaOps(torch, E, D, I, 7.0, router, bias, tables, rank, world, T,
@@ -643,7 +648,7 @@ def dsv4_bench(moe, torch, dist, rank, world, wl, steps, T=32):
     local_touched = len([e for e in set(idx.flatten().tolist()) if e % world == rank])
     ebytes = 3 * (I * D // 2 + I * D // 32)
     res = {"workload": f"DeepSeek-V4-class MoE step: {T} tokens, hidden {D}, {E} MXFP4 experts "
-                       f"(inter {I}) top-6 sqrt(softplus)+bias, clamped SwiGLU, int8-row dense "
+                       f"(inter {I}) top-6 sqrt(softplus)+bias, clamped SwiGLU, int4-g64 dense "
                        "shared MLP, routed_scale 2.5",
            "ranks": world, "placement": "strided e % ranks (2 ranks = the reference's EP2 "
                                         "parity split)",

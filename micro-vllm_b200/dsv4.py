@@ -25,7 +25,8 @@ N = 2 with strided placement is the reference's parity split):
                  one addition per element, so every rank holds exactly the
                  reference's rank0 + rank1.
   6. tail        h += acc * routed_scale, then the dense shared MLP's output
-                                     (mvllm_moe_epilogue_dev, _dense_ffn_dev)
+                 (mvllm_moe_epilogue_dev; the MLP through mvllm_moe_layer_dev as
+                 one expert, or exactly with mvllm_moe_dense_ffn_dev)
 
 The device steps go through an ``ops`` object, so the orchestration is the
 same code over the CUDA library (``CudaOps``) or a CPU test double, and over
@@ -49,12 +50,16 @@ class CudaOps:
     and up [I, H] and down [H, I]; shared_fp8: the bank's shared expert
     ((w, scales) x 3, FP8 tiles, device) on the rank that holds it, else
     None; dense_shared: (fmt, gate, up, down) of the layer's shared MLP
-    (each (w, scales-or-None), device), or None.
+    (each (w, scales-or-None), device), or None.  An int4-g64 or MXFP4 shared
+    MLP (QuantMat 4-bit is the reference's default, config.hpp:143) runs
+    through the MoE kernels as one expert that every token takes with weight
+    1, within the MoE tolerance; with dense_exact, and for the other formats,
+    it runs on the sequential-order GEMM in the reference's exact arithmetic.
     """
 
     def __init__(self, torch, E, H, I, limit, router, bias, local_tables, rank, nranks,
                  max_tokens, route_scale=1.0, routed_scale=1.0, shared_fp8=None,
-                 dense_shared=None):
+                 dense_shared=None, dense_exact=False):
         self.torch = torch
         self.E, self.H, self.I, self.limit = E, H, I, limit
         self.router, self.bias = router, bias
@@ -78,6 +83,18 @@ class CudaOps:
         self.choice = torch.empty((T, E), dtype=torch.float32, device=dev)
         self.acc = torch.empty((T, H), dtype=torch.float32, device=dev)
         self.sd = torch.empty((T, H), dtype=torch.float32, device=dev)
+        self.dense_moe = None
+        if (dense_shared is not None and not dense_exact
+                and dense_shared[0] in (moe.FMT_INT4_G64, moe.FMT_MXFP4)):
+            fmt, g, u, d = dense_shared
+            tabs = [torch.tensor([a.data_ptr()], dtype=torch.int64, device=dev)
+                    for a in (g[0], u[0], d[0], g[1], u[1], d[1])]
+            self.dense_moe = dict(
+                fmt=fmt, tables=tabs,
+                idx=torch.zeros((T, 1), dtype=torch.int32, device=dev),
+                wt=torch.ones((T, 1), dtype=torch.float32, device=dev),
+                ws=torch.empty(moe.layer_workspace_bytes(T, 1, 1, 0, H, I, fmt),
+                               dtype=torch.uint8, device=dev))
 
     def _rows(self, x):
         T = x.shape[0]
@@ -115,10 +132,18 @@ class CudaOps:
     def tail(self, x, acc, h):
         sd = None
         if self.dense_shared is not None:
-            fmt, g, u, d = self.dense_shared
-            sd = self.sd[:x.shape[0]]
-            moe.dense_ffn_dev(fmt, x, g, u, d, sd, moe.ACT_CLAMP_SWIGLU, self.limit, 0.0,
-                              workspace=self.ffn_ws)
+            T = x.shape[0]
+            sd = self.sd[:T]
+            if self.dense_moe is not None:
+                m = self.dense_moe
+                sd.zero_()
+                moe.layer_dev(T, 1, 1, 0, self.H, self.I, m["fmt"], m["idx"][:T], m["wt"][:T],
+                              x, m["tables"], sd, moe.ACT_CLAMP_SWIGLU, self.limit, 0.0,
+                              m["ws"])
+            else:
+                fmt, g, u, d = self.dense_shared
+                moe.dense_ffn_dev(fmt, x, g, u, d, sd, moe.ACT_CLAMP_SWIGLU, self.limit, 0.0,
+                                  workspace=self.ffn_ws)
         moe.epilogue_dev(acc, h, self.routed_scale, shared=sd)
 
 

@@ -31,7 +31,7 @@ def fp8_tensor(rng, O, I, base=120):
     return fp8_codes(rng, (O, I)), tiles.astype(np.uint8)
 
 
-def dsv4_case(port, seed, H, I, E, T, shared=True, dense=True, absent=()):
+def dsv4_case(port, seed, H, I, E, T, shared=True, dense=True, absent=(), dense_fmt=8):
     rng = np.random.default_rng(seed)
     c = dict(H=H, I=I, E=E, T=T)
     c["x"] = rng.standard_normal((T, H)).astype(np.float32)
@@ -42,10 +42,11 @@ def dsv4_case(port, seed, H, I, E, T, shared=True, dense=True, absent=()):
     c["experts"] = [None if e in absent else ex[e] for e in range(E)]
     c["shared_fp8"] = ([fp8_tensor(rng, I, H), fp8_tensor(rng, I, H), fp8_tensor(rng, H, I)]
                        if shared else None)
-    c["dense"] = None
+    c["dense"], c["dense_fmt"] = None, dense_fmt
     if dense:
         ws = [(rng.standard_normal(s) * 0.05).astype(np.float32) for s in ((I, H), (I, H), (H, I))]
-        c["dense"] = [port.quantize_int8_row(w) for w in ws]
+        q = port.quantize_int8_row if dense_fmt == 8 else port.quantize_int4_g64
+        c["dense"] = [q(w) for w in ws]
     c["route_scale"], c["routed_scale"] = 1.0, 2.5
     return c
 
@@ -66,13 +67,14 @@ def fp8_shared_out(port, x, shared):
     return port.matmul_fp8_b128(clamped(port, g, u), dw, ds, H)
 
 
-def dense_out(port, x, dense):
-    """The layer's shared MLP (int8 rows) for rows x."""
+def dense_out(port, x, dense, fmt=8):
+    """The layer's shared MLP (QuantMat int8 rows or int4-g64) for rows x."""
     (gq, gs), (uq, us), (dq, ds) = dense
-    I, H = gq.shape
-    g = port.matmul_int8_row(x, gq, gs, I)
-    u = port.matmul_int8_row(x, uq, us, I)
-    return port.matmul_int8_row(clamped(port, g, u), dq, ds, H)
+    I, H = gq.shape[0], dq.shape[0]
+    mm = port.matmul_int8_row if fmt == 8 else port.matmul_int4_g64
+    g = mm(x, gq, gs, I)
+    u = mm(x, uq, us, I)
+    return mm(clamped(port, g, u), dq, ds, H)
 
 
 def expected(port, c):
@@ -83,7 +85,7 @@ def expected(port, c):
                                             c["I"], c["experts"], c["shared_fp8"], LIMIT)
         assert np.array_equal(out, peer)
         acc[t] = out
-    sd = dense_out(port, c["x"], c["dense"]) if c["dense"] is not None else None
+    sd = dense_out(port, c["x"], c["dense"], c["dense_fmt"]) if c["dense"] is not None else None
     h = port.moe_epilogue(acc, c["h"], c["routed_scale"], shared=sd)
     return acc, h
 
@@ -123,7 +125,8 @@ class CpuOps:
             acc += self.torch.from_numpy(fp8_shared_out(self.port, x.numpy(), self.shared_fp8))
 
     def tail(self, x, acc, h):
-        sd = dense_out(self.port, x.numpy(), self.c["dense"]) if self.c["dense"] else None
+        sd = (dense_out(self.port, x.numpy(), self.c["dense"], self.c["dense_fmt"])
+              if self.c["dense"] else None)
         h.copy_(self.torch.from_numpy(self.port.moe_epilogue(acc.numpy(), h.numpy(),
                                                              self.c["routed_scale"],
                                                              shared=sd)))

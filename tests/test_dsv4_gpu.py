@@ -156,19 +156,23 @@ def rank_ops(moe, c, rank, nranks, keep):
     sh = None
     if rank == 0 and c["shared_fp8"] is not None:
         sh = [(dev(w), dev(s)) for w, s in c["shared_fp8"]]
-    dense = (moe.FMT_INT8_ROW,) + tuple((dev(a), dev(b)) for a, b in c["dense"])
+    dense = (c["dense_fmt"],) + tuple((dev(a), dev(b)) for a, b in c["dense"])
     return dsv4.CudaOps(torch, c["E"], c["H"], c["I"], dc.LIMIT, dev(c["router"]),
                         dev(c["bias"]), tables, rank, nranks, c["T"], c["route_scale"],
                         c["routed_scale"], sh, dense)
 
 
-@pytest.mark.parametrize("H,I,E,T", [(512, 256, 16, 40), (1024, 512, 32, 8)])
-def test_ep2_emulated(moe, port, H, I, E, T):
+@pytest.mark.parametrize("H,I,E,T,dfmt", [(512, 256, 16, 40, 8), (1024, 512, 32, 8, 8),
+                                          (512, 256, 16, 24, 4)])
+def test_ep2_emulated(moe, port, H, I, E, T, dfmt):
+    """int8-row dense MLP: the exact sequential path; int4-g64 (the reference's
+    default dense_bits): through the MoE kernels as one expert."""
     import dsv4
-    c = dc.dsv4_case(port, H + T, H, I, E, T)
+    c = dc.dsv4_case(port, H + T, H, I, E, T, dense_fmt=dfmt)
     acc_w, h_w = dc.expected(port, c)
     keep = []
     layers = [dsv4.EP2Layer(rank_ops(moe, c, r, 2, keep), r, 2) for r in range(2)]
+    assert (layers[0].ops.dense_moe is not None) == (dfmt == 4)
     h = dev(c["h"])
     acc = dsv4.emulate_step(layers, dev(c["x"]), h)
     torch.cuda.synchronize()
