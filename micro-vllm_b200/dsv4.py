@@ -40,6 +40,35 @@ import mvllm_moe as moe
 TOPK = 6  # DeepSeek-V4 routes every token to 6 experts (dsv4_cuda.cpp:1561)
 
 
+def mx_geom(H, O):
+    """Byte sizes of one DeepSeek-V4 expert blob's parts (make_mx_geom,
+    dsv4.cpp:64-80): packed gate/up rows [O, H/2] and their ue8m0 scales
+    [O, H/32], packed down rows [H, O/2] and scales [H, O/32] (rounded up
+    when H or O is not a multiple of 32).  Returns (w1p, w1s, w2p, w2s, slot)."""
+    H, O = max(H, 1), max(O, 1)
+    if H >= 32 and O >= 32 and H % 32 == 0 and O % 32 == 0:
+        w1p, w1s, w2p, w2s = O * (H // 2), O * (H // 32), H * (O // 2), H * (O // 32)
+    else:
+        w1p, w1s = O * ((H + 1) // 2), O * ((H + 31) // 32)
+        w2p, w2s = H * ((O + 1) // 2), H * ((O + 31) // 32)
+    return w1p, w1s, w2p, w2s, 2 * (w1p + w1s) + w2p + w2s
+
+
+def blob_pointers(base, H, O):
+    """The six array addresses of an expert blob at address `base`, in the
+    order the pointer tables take them (gate, up, down, gate scales, up
+    scales, down scales).  The blob is w1 (gate) packed, w1 scales, w2 (down)
+    packed, w2 scales, w3 (up) packed, w3 scales (dsv4.cpp:2958-2965)."""
+    w1p, w1s, w2p, w2s, _ = mx_geom(H, O)
+    gate = base
+    gate_s = gate + w1p
+    down = gate_s + w1s
+    down_s = down + w2p
+    up = down_s + w2s
+    up_s = up + w1p
+    return gate, up, down, gate_s, up_s, down_s
+
+
 class CudaOps:
     """Device steps of one rank through the sm_100a library.
 

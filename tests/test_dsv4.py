@@ -238,3 +238,22 @@ def test_ep2_two_gloo_ranks(port, tmp_path):
     _, h_w = dc.expected(port, c)
     for r in range(N):  # every rank holds the reference's result, bit for bit
         np.testing.assert_array_equal(np.load(tmp_path / f"h{r}.npy"), h_w)
+
+
+def test_blob_geometry():
+    """make_mx_geom (dsv4.cpp:64-80) and the blob order of moe_layer_ep2
+    (dsv4.cpp:2958-2965): gate packed, gate scales, down packed, down scales,
+    up packed, up scales."""
+    import dsv4
+    H, O = 7168, 2048
+    w1p, w1s, w2p, w2s, slot = dsv4.mx_geom(H, O)
+    assert (w1p, w1s, w2p, w2s) == (O * H // 2, O * H // 32, H * O // 2, H * O // 32)
+    assert slot == 2 * (w1p + w1s) + w2p + w2s
+    g, u, d, gs, us, ds = dsv4.blob_pointers(1000, H, O)
+    assert (g, gs, d, ds, u, us) == (1000, 1000 + w1p, 1000 + w1p + w1s,
+                                     1000 + w1p + w1s + w2p, 1000 + w1p + w1s + w2p + w2s,
+                                     1000 + 2 * w1p + w1s + w2p + w2s)
+    assert us + w1s == 1000 + slot
+    # shapes off the 32 grid round up per row
+    w1p, w1s, w2p, w2s, _ = dsv4.mx_geom(40, 24)
+    assert (w1p, w1s, w2p, w2s) == (24 * 20, 24 * 2, 40 * 12, 40 * 1)
