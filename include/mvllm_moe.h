@@ -21,6 +21,11 @@
  *          value = nibble - 8), f32 scales [O, ceil(I/64)]
  *   fmt 7  MXFP4: packed e2m1 uint8 [O, ceil(I/2)] (bit 3 = sign), ue8m0
  *          scales uint8 [O, ceil(I/32)], passed through the float* slots
+ *   fmt 8  int8 rows: int8 [O, I], one f32 scale per row (QuantMat 8-bit)
+ *   fmt 9  FP8 tiles: e4m3fn uint8 [O, I], ue8m0 scales uint8
+ *          [ceil(O/128), ceil(I/128)] (DeepSeek-V4)
+ * moe_block and the layer entries take fmt 4 and 7 (and 0 on the generic
+ * path); the dense entries (matmul, epilogue, dense FFN) also 8 and 9.
  * Gate/up weights are [Iinter, D]; down weights are [D, Iinter].
  */
 #ifndef MVLLM_MOE_H
