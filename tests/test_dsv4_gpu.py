@@ -36,11 +36,18 @@ def dev(a):
     return None if a is None else torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-@pytest.mark.parametrize("E,H,rs", [(256, 1024, 1.0), (64, 512, 2.5), (5, 256, 1.0)])
-def test_route_sqrt_softplus(moe, port, E, H, rs):
+@pytest.mark.parametrize("E,H,rs,dtype", [(256, 1024, 1.0, "f32"), (64, 512, 2.5, "f32"),
+                                          (5, 256, 1.0, "f32"), (256, 1024, 1.0, "bf16"),
+                                          (96, 300, 1.0, "f32")])
+def test_route_sqrt_softplus(moe, port, E, H, rs, dtype):
+    """f32 and bf16 activations; H = 300 is not a whole number of 16-byte
+    pieces, so the router takes the register-staged tile instead of the
+    cp.async ring."""
     rng = np.random.default_rng(E * 7 + H)
     T = 96
     x = rng.standard_normal((T, H)).astype(np.float32)
+    if dtype == "bf16":
+        x = (x.view(np.uint32) & 0xFFFF0000).view(np.float32)  # bf16-exact values
     router = (rng.standard_normal((E, H)) * (3.0 / np.sqrt(H))).astype(np.float32)
     router[0] *= 30.0  # logits past the +-20 cut-offs
     router[1] *= -30.0
@@ -50,7 +57,8 @@ def test_route_sqrt_softplus(moe, port, E, H, rs):
     wt = torch.empty((T, K), dtype=torch.float32, device="cuda")
     scores = torch.empty((T, E), dtype=torch.float32, device="cuda")
     choice = torch.empty((T, E), dtype=torch.float32, device="cuda")
-    moe.route_ex_dev(dev(x), dev(router), dev(bias), K, idx, wt, scores, choice,
+    xd = dev(x) if dtype == "f32" else dev(x).to(torch.bfloat16)
+    moe.route_ex_dev(xd, dev(router), dev(bias), K, idx, wt, scores, choice,
                      moe.SCORE_SQRT_SOFTPLUS, rs)
     torch.cuda.synchronize()
     ri, rw = port.dsv4_route(x, router, bias, rs)
