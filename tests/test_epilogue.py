@@ -107,3 +107,37 @@ def test_matmul_int8_row_dev(moe, port):
         moe.matmul_dev(8, y, _dev(x), _dev(q), _dev(s))
         torch.cuda.synchronize()
         np.testing.assert_array_equal(y.cpu().numpy(), port.matmul_int8_row(x, q, s, O))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", [0, 4, 7, 8, 9])
+def test_matmul_dev_every_format(moe, port, fmt):
+    """mvllm_matmul_dev in every format, bit-identical to the reference's
+    matmul: shapes on the cp.async ring (whole 16-byte row pieces) and off it
+    (the register-staged tile), 1 to 40 rows of x, ragged W-row tiles."""
+    import dsv4_cases as dc
+    rng = np.random.default_rng(100 + fmt)
+    shapes = [(1, 256, 40), (40, 512, 200), (7, 2048, 129)]
+    if fmt in (0, 8, 9):
+        shapes.append((5, 300, 33))  # rows not whole 16-byte pieces
+    for S, I, O in shapes:
+        w = (rng.standard_normal((O, I)) * 0.05).astype(np.float32)
+        x = rng.standard_normal((S, I)).astype(np.float32)
+        if fmt == 0:
+            q, s, want = w, None, port.matmul_f32(x, w)
+        elif fmt == 4:
+            q, s = port.quantize_int4_g64(w)
+            want = port.matmul_int4_g64(x, q, s, O)
+        elif fmt == 7:
+            q, s = port.pack_mxfp4(w)
+            want = port.matmul_mxfp4(x, q, s, O)
+        elif fmt == 8:
+            q, s = port.quantize_int8_row(w)
+            want = port.matmul_int8_row(x, q, s, O)
+        else:
+            q, s = dc.fp8_tensor(rng, O, I)
+            want = port.matmul_fp8_b128(x, q, s, O)
+        y = torch.zeros((S, O), device="cuda")
+        moe.matmul_dev(fmt, y, _dev(x), _dev(q), _dev(s))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(y.cpu().numpy(), want, err_msg=f"{S}x{I}->{O}")
