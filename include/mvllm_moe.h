@@ -363,6 +363,13 @@ MVLLM_API int mvllm_moe_dense_ffn_dev(void *stream, int fmt, int T, int H, int O
                                       float *y, int accumulate, void *workspace,
                                       size_t workspace_bytes);
 
+/* Health check of the bounded device waits that every pipeline kernel uses:
+ * runs one small kernel that waits on an mbarrier one thread completes and
+ * then on one that nothing completes.  *completed = 1 when the first wait
+ * succeeded; *timed_out = 1 when the second gave up after its time limit
+ * (2 s) and recorded MVLLM_ERR_TIMEOUT.  The context stays usable. */
+MVLLM_API int mvllm_moe_wait_selftest(int *completed, int *timed_out);
+
 /* Per-phase device time of the device-pointer entries, from CUDA events
  * recorded on the launch stream after each phase while enabled (the role of
  * the reference's AccTimer accumulators, src/model/glm53.cpp:39-46, on the

@@ -2039,6 +2039,53 @@ int mvllm_moe_epilogue_dev(void *stream, int T, int H, int L, const float *acc,
     return MVLLM_OK;
 }
 
+// ---------------------------------------------------- bounded-wait check --
+// The failure path every pipeline kernel takes when a copy or a peer never
+// completes: a wait on an mbarrier that one thread completes (must succeed),
+// then on one that nothing completes (must give up after kWaitNs and record
+// MVLLM_ERR_TIMEOUT).  The kernel returns either way; nothing faults.
+__global__ void wait_selftest_kernel(int *err, int *result) {
+    __shared__ uint64_t bar[2];
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+        mbar_arrive(&bar[0]);
+    const bool completed = mbar_wait(&bar[0], 0, nullptr);
+    const bool never = mbar_wait(&bar[1], 0, err); // nothing arrives
+    if (threadIdx.x == 0)
+        result[0] = (completed ? 1 : 0) | (never ? 2 : 0);
+}
+
+int mvllm_moe_wait_selftest(int *completed, int *timed_out) {
+    Context &c = ctx();
+    if (!c.inited)
+        return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
+    int *d = nullptr;
+    CUDA_TRY(cudaMalloc(&d, 2 * sizeof(int)));
+    int h[2] = {0, 0};
+    cudaError_t e = cudaMemsetAsync(d, 0, 2 * sizeof(int), c.stream);
+    if (e == cudaSuccess) {
+        wait_selftest_kernel<<<1, 64, 0, c.stream>>>(d, d + 1);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(h, d, sizeof(h), cudaMemcpyDeviceToHost, c.stream);
+    if (e == cudaSuccess)
+        e = cudaStreamSynchronize(c.stream);
+    cudaFree(d);
+    if (e != cudaSuccess)
+        return fail(MVLLM_ERR_CUDA, "wait_selftest: %s", cudaGetErrorString(e));
+    if (completed)
+        *completed = h[1] & 1;
+    if (timed_out)
+        *timed_out = h[0] == MVLLM_ERR_TIMEOUT && !(h[1] & 2);
+    return MVLLM_OK;
+}
+
 // ------------------------------------------------------------- dense FFN --
 size_t mvllm_moe_dense_ffn_workspace(int T, int H, int O) {
     if (T < 1 || H < 1 || O < 1)

@@ -43,7 +43,7 @@ C_SYMBOLS = (
     "mvllm_moe_expert_bind", "mvllm_moe_expert_unbind", "mvllm_moe_tier_stats",
     "mvllm_moe_epilogue_workspace", "mvllm_moe_epilogue_dev", "mvllm_moe_host_register",
     "mvllm_moe_host_unregister", "mvllm_moe_route_ex_dev", "mvllm_moe_ep_local_ids_dev",
-    "mvllm_moe_dense_ffn_workspace", "mvllm_moe_dense_ffn_dev",
+    "mvllm_moe_dense_ffn_workspace", "mvllm_moe_dense_ffn_dev", "mvllm_moe_wait_selftest",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -112,6 +112,7 @@ def lib():
             "mvllm_moe_route_ex_dev": (i, [vp, vp, i, i, i, vp, vp, i, i, i, f, vp, vp, vp, vp]),
             "mvllm_moe_ep_local_ids_dev": (i, [vp, vp, i, i, i, i, vp, vp, i, vp]),
             "mvllm_moe_dense_ffn_workspace": (sz, [i, i, i]),
+            "mvllm_moe_wait_selftest": (i, [vp, vp]),
             "mvllm_moe_dense_ffn_dev": (i, [vp, i, i, i, i] + [vp] * 7 + [i, f, f, vp, i, vp,
                                                                          sz]),
         }
@@ -440,6 +441,13 @@ def ep_local_ids_dev(idx, E, nranks, self_rank, local_idx, dest=None, lid=None, 
     T, K = idx.shape
     _check(lib().mvllm_moe_ep_local_ids_dev(_stream(stream), _dp(idx), T, K, E, nranks, _dp(dest),
                                             _dp(lid), self_rank, _dp(local_idx)))
+
+
+def wait_selftest():
+    """(completed, timed_out) of the bounded-wait health check (about 2 s)."""
+    a, b = C.c_int(0), C.c_int(0)
+    _check(lib().mvllm_moe_wait_selftest(C.byref(a), C.byref(b)))
+    return bool(a.value), bool(b.value)
 
 
 def dense_ffn_workspace_bytes(T, H, O) -> int:
