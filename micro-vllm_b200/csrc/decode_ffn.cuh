@@ -55,6 +55,10 @@ constexpr int kDecodeEpilogue = kDecodeEpilogueWarps * 32;
 constexpr int kDecodeProducerWarp = kDecodeConsumerWarps; // weight rows
 constexpr int kDecodeSideWarp = kDecodeProducerWarp + 1;   // header, scales, token rows
 constexpr int kDecodeThreads = kDecodeConsumers + 64 + kDecodeEpilogue;
+// Reduction buffers between the consumers and the epilogue warps: consumers
+// start the next item while the epilogue drains earlier ones.
+constexpr int kDecodeRedBufs = 2;
+static_assert(16 + 2 * kDecodeRedBufs <= 32, "barrier block holds 32 barriers");
 
 // Per-expert tensor maps (128 bytes each), built on the device from the
 // expert pointer tables: packed gate, up, down rows, then their scales.
@@ -88,8 +92,8 @@ template <int FMT, int KS, int NT> struct DecodeLayout {
     static constexpr int XROW = 4 * KS + 64; // 2*KS f16 per row, +64 B for LDS.128
     static constexpr int RS = MT + 1;        // reduction row stride (floats)
     static constexpr int RED_BYTES = kDecodeKParts * kDecodeRows * RS * 4; // per buffer
-    static constexpr int BAR_BYTES = 256; // 8 full + 8 empty + 2 + 2 reduction barriers
-    static constexpr int RHDR_BYTES = 32; // two item headers for the epilogue
+    static constexpr int BAR_BYTES = 256; // 8 full + 8 empty + 2 x kDecodeRedBufs reduction
+    static constexpr int RHDR_BYTES = 16 * kDecodeRedBufs; // item headers for the epilogue
     static constexpr int ITEM_TAB = 512;  // item offsets of up to 511 experts, in shared memory
     static constexpr int OFF_W = 0;          // 1024-aligned: the 128-byte swizzle needs it
     static constexpr int OFF_SC = OFF_W + NBOX * BOX_BYTES;
@@ -97,8 +101,8 @@ template <int FMT, int KS, int NT> struct DecodeLayout {
     static constexpr int OFF_X = OFF_HDR + 16;
     static constexpr int STAGE_BYTES = (OFF_X + MT * XROW + 1023) / 1024 * 1024;
     static constexpr int HEAD_BYTES =
-        (BAR_BYTES + RHDR_BYTES + 2 * RED_BYTES + ITEM_TAB * 4 + 1023) / 1024 * 1024;
-    static constexpr int OFF_ITEMS = BAR_BYTES + RHDR_BYTES + 2 * RED_BYTES;
+        (BAR_BYTES + RHDR_BYTES + kDecodeRedBufs * RED_BYTES + ITEM_TAB * 4 + 1023) / 1024 * 1024;
+    static constexpr int OFF_ITEMS = BAR_BYTES + RHDR_BYTES + kDecodeRedBufs * RED_BYTES;
     static int smem_bytes(int nstages) { return HEAD_BYTES + nstages * STAGE_BYTES + 1024; }
 };
 
@@ -310,7 +314,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + 8;
     uint64_t *rfull = full + 16; // reduction buffer filled (16 consumer warps)
-    uint64_t *rempty = full + 18; // reduction buffer drained (64 epilogue threads)
+    uint64_t *rempty = rfull + kDecodeRedBufs; // reduction buffer drained (64 epilogue threads)
     int4 *rhdr = reinterpret_cast<int4 *>(smem + L::BAR_BYTES);
     float *red = reinterpret_cast<float *>(smem + L::BAR_BYTES + L::RHDR_BYTES);
     uint8_t *stages = smem + L::HEAD_BYTES;
@@ -327,7 +331,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
             mbar_init(&full[s], 2); // both producer warps' expect_tx arrivals; the rest is tx bytes
             mbar_init(&empty[s], kDecodeConsumerWarps);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kDecodeRedBufs; ++b) {
             mbar_init(&rfull[b], kDecodeConsumerWarps);
             mbar_init(&rempty[b], kDecodeEpilogue);
         }
@@ -451,8 +455,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
         uint32_t n_items = 0;
         bool ok = true;
         for (int i = blockIdx.x; i < total; i += gridDim.x, ++n_items) {
-            const int rs = n_items & 1;
-            if (ok && !mbar_wait(&rfull[rs], (n_items >> 1) & 1u, p.err))
+            const int rs = n_items % kDecodeRedBufs;
+            if (ok && !mbar_wait(&rfull[rs], (n_items / kDecodeRedBufs) & 1u, p.err))
                 ok = false;
             if (ok) {
                 const int4 h = rhdr[rs];
@@ -547,8 +551,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
                 mbar_arrive(&empty[slot]);
         }
         // Hand the partial sums to the epilogue warps and move on.
-        const int rs = n_items & 1;
-        if (ok && !mbar_wait(&rempty[rs], ((n_items >> 1) & 1u) ^ 1u, p.err))
+        const int rs = n_items % kDecodeRedBufs;
+        if (ok && !mbar_wait(&rempty[rs], ((n_items / kDecodeRedBufs) & 1u) ^ 1u, p.err))
             ok = false;
         if (ok) {
             float *rd = red + rs * (L::RED_BYTES / 4);
