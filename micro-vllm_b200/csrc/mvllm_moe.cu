@@ -59,8 +59,9 @@ struct Context {
     TierPolicy tier;
     void *tier_arena = nullptr;
     std::map<uintptr_t, size_t> host_reg; // caller buffers page-locked by host_register
-    cudaStream_t copy_stream = nullptr; // stream-ins of cold blobs
+    cudaStream_t copy_stream = nullptr; // stream-ins of cold blobs, caller rows of layer_host
     cudaEvent_t copy_done = nullptr;
+    cudaEvent_t call_start = nullptr, x_in = nullptr, out_in = nullptr; // layer_host copies
     uint64_t calls = 0, experts = 0, rows = 0;
     double h2d_ms = 0, kernel_ms = 0, d2h_ms = 0;
 };
@@ -654,6 +655,8 @@ int init_locked(Context &c, int device) {
     CUDA_TRY(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
     CUDA_TRY(cudaStreamCreateWithFlags(&c.copy_stream, cudaStreamNonBlocking));
     CUDA_TRY(cudaEventCreateWithFlags(&c.copy_done, cudaEventDisableTiming));
+    for (cudaEvent_t *e : {&c.call_start, &c.x_in, &c.out_in})
+        CUDA_TRY(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
     for (auto &e : c.ev)
         CUDA_TRY(cudaEventCreate(&e));
     c.sms = prop.multiProcessorCount;
@@ -796,6 +799,9 @@ void mvllm_moe_shutdown(void) {
     for (auto &e : c.ev)
         cudaEventDestroy(e);
     cudaEventDestroy(c.copy_done);
+    for (cudaEvent_t e : {c.call_start, c.x_in, c.out_in})
+        cudaEventDestroy(e);
+    c.call_start = c.x_in = c.out_in = nullptr;
     cudaStreamDestroy(c.copy_stream);
     cudaStreamDestroy(c.stream);
     c.stream = nullptr;
@@ -1756,12 +1762,27 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     Tables tb{dt, dt + EE, dt + 2 * EE, dt + 3 * EE, dt + 4 * EE, dt + 5 * EE};
     float *dout = reinterpret_cast<float *>(dptr(hout));
     // Caller buffers page-locked with mvllm_moe_host_register are copied
-    // straight to and from the device; others go through the pinned staging.
+    // straight to and from the device, on the copy stream from the start of the
+    // call, so x lands while the permutation runs and out while the experts
+    // run; the gather and the combine wait for them.  Other buffers go through
+    // the pinned staging, copied in by the host while the kernels run.
     const bool x_reg = host_registered(c, x, x_b), out_reg = host_registered(c, out, x_b);
+    if (x_reg || out_reg) {
+        CUDA_TRY(cudaEventRecord(c.call_start, c.stream)); // earlier work on these buffers
+        CUDA_TRY(cudaStreamWaitEvent(c.copy_stream, c.call_start, 0));
+        if (x_reg) {
+            CUDA_TRY(cudaMemcpyAsync(db + x_off, x, x_b, cudaMemcpyHostToDevice, c.copy_stream));
+            CUDA_TRY(cudaEventRecord(c.x_in, c.copy_stream));
+        }
+        if (out_reg) {
+            CUDA_TRY(cudaMemcpyAsync(dout, out, x_b, cudaMemcpyHostToDevice, c.copy_stream));
+            CUDA_TRY(cudaEventRecord(c.out_in, c.copy_stream));
+        }
+    }
     LayerHooks hooks;
     hooks.before_gather = [&]() -> int {
         if (x_reg) {
-            CUDA_TRY(cudaMemcpyAsync(db + x_off, x, x_b, cudaMemcpyHostToDevice, c.stream));
+            CUDA_TRY(cudaStreamWaitEvent(c.stream, c.x_in, 0));
             return MVLLM_OK;
         }
         memcpy(hx, x, x_b); // the permutation kernels run meanwhile
@@ -1770,7 +1791,7 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     };
     hooks.before_combine = [&]() -> int {
         if (out_reg) {
-            CUDA_TRY(cudaMemcpyAsync(dout, out, x_b, cudaMemcpyHostToDevice, c.stream));
+            CUDA_TRY(cudaStreamWaitEvent(c.stream, c.out_in, 0));
             return MVLLM_OK;
         }
         memcpy(hout, out, x_b); // the expert kernels run meanwhile
@@ -1782,6 +1803,7 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
                                 reinterpret_cast<const float *>(dptr(hwt)), dptr(hx),
                                 MVLLM_DTYPE_F32, tb, dout, act, act_a, act_b, l, allow_tc, &hooks)) {
         cudaStreamSynchronize(c.stream); // no copy may still read the staging buffer
+        cudaStreamSynchronize(c.copy_stream); // nor a caller buffer
         return rc;
     }
     if (out_reg) {
