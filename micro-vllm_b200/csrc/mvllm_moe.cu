@@ -1719,7 +1719,7 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     const bool fast = fast_path_ok(fmt, D, Iinter);
     const size_t tab_b = size_t(6) * EE * sizeof(void *);
     const size_t idx_b = size_t(T) * K * 4, x_b = size_t(T) * D * 4;
-    const size_t up = tab_b + 2 * idx_b + 2 * x_b + 1024;
+    const size_t up = tab_b + 2 * idx_b + 2 * x_b + 1024 + 64;
     if (int rc = ensure_pinned(c, up))
         return rc;
     // Pinned staging, uploaded in three pieces: tables + routing (read by the
@@ -1730,6 +1730,7 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     float *hwt = hcv.take<float>(size_t(T) * K);
     float *hx = hcv.take<float>(size_t(T) * D);
     float *hout = hcv.take<float>(size_t(T) * D);
+    int *herr = hcv.take<int>(16); // the error word, read back with `out`
     uint8_t *hbase = static_cast<uint8_t *>(c.pinned);
     const size_t x_off = reinterpret_cast<uint8_t *>(hx) - hbase;
     const size_t out_off = reinterpret_cast<uint8_t *>(hout) - hbase;
@@ -1748,12 +1749,14 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
     dcv.take<uint8_t>(up_bytes);
     LayerWs l{};
     carve_layer(dcv, l, T, K, E, n_shared, D, Iinter, fast);
+    dcv.take<float>(size_t(T) * D); // the caller's out rows as uploaded
     if (int rc = ensure_dev(c.ws, dcv.used + 256))
         return rc;
     uint8_t *db = static_cast<uint8_t *>(c.ws.p);
     Carve dcv2(db, c.ws.bytes);
     dcv2.take<uint8_t>(up_bytes);
     carve_layer(dcv2, l, T, K, E, n_shared, D, Iinter, fast);
+    float *dout_in = dcv2.take<float>(size_t(T) * D);
     auto dptr = [&](const void *hp) { return db + (static_cast<const uint8_t *>(hp) - hbase); };
     CUDA_TRY(cudaEventRecord(c.ev[0], c.stream));
     CUDA_TRY(cudaMemcpyAsync(db, c.pinned, x_off, cudaMemcpyHostToDevice, c.stream));
@@ -1776,6 +1779,9 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
         }
         if (out_reg) {
             CUDA_TRY(cudaMemcpyAsync(dout, out, x_b, cudaMemcpyHostToDevice, c.copy_stream));
+            // kept as uploaded: on a device error the caller's rows are put back
+            CUDA_TRY(cudaMemcpyAsync(dout_in, dout, x_b, cudaMemcpyDeviceToDevice,
+                                     c.copy_stream));
             CUDA_TRY(cudaEventRecord(c.out_in, c.copy_stream));
         }
     }
@@ -1807,13 +1813,19 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
         return rc;
     }
     if (out_reg) {
-        // The error word first: on an error `out` must stay untouched.
-        if (int rc = check_device_error(l.run.err, c.stream))
-            return rc;
+        // The error word and `out` in one round trip; on an error the rows the
+        // caller passed in are copied back, so `out` is left as it was.
         CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
+        CUDA_TRY(cudaMemcpyAsync(herr, l.run.err, sizeof(int), cudaMemcpyDeviceToHost, c.stream));
         CUDA_TRY(cudaMemcpyAsync(out, dout, x_b, cudaMemcpyDeviceToHost, c.stream));
         CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
         CUDA_TRY(cudaStreamSynchronize(c.stream));
+        if (*herr) {
+            const int err = *herr;
+            CUDA_TRY(cudaMemcpyAsync(out, dout_in, x_b, cudaMemcpyDeviceToHost, c.stream));
+            CUDA_TRY(cudaStreamSynchronize(c.stream));
+            return fail(err, "device-side error code %d", err);
+        }
     } else {
         CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
         CUDA_TRY(cudaMemcpyAsync(hout, dout, x_b, cudaMemcpyDeviceToHost, c.stream));

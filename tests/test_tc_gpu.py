@@ -130,3 +130,42 @@ def test_tc_scale_range_reruns_on_decode(moe, port, monkeypatch):
     force_tc(monkeypatch)
     got = host_block(moe, c)
     assert_close(got, want, "range rerun")
+
+
+def test_tc_scale_range_layer_host_registered(moe, port, monkeypatch):
+    """The same range case through mvllm_moe_layer_host with the caller's x
+    and out page-locked: the tensor-core run's error word comes back together
+    with out, the caller's rows are copied back, and the rerun on the decode
+    kernels adds the reference's result to the caller's original rows."""
+    rng = np.random.default_rng(36)
+    D, I, n = 512, 512, 40
+    w = [(rng.standard_normal((o, i)) * 0.02).astype(np.float32)
+         for (o, i) in ((I, D), (I, D), (D, I))]
+    w[0][0, 5] = 65536.0  # scale code 141 in gate row 0
+    packed = [port.pack_mxfp4(m) for m in w]
+    x = cases.bf16_round(rng.standard_normal((n, D)).astype(np.float32))
+    x[:, 5] = 0.0
+    base = rng.standard_normal((n, D)).astype(np.float32)
+    c = dict(D=D, I=I, fmt=cases.FMT_MXFP4, act=cases.ACT_SILU, act_a=0.0, act_b=0.0, nb=1,
+             g=[packed[0][0]], u=[packed[1][0]], d=[packed[2][0]], gs=[packed[0][1]],
+             us=[packed[1][1]], ds=[packed[2][1]], xg=x, xoff=np.array([0], np.int32),
+             nr=np.array([n], np.int32), rows=np.arange(n, dtype=np.int32),
+             rw=np.ones(n, np.float32), S=n)
+    _, want = cases.run_block(port, c, out=base.copy())
+    keep = [torch.from_numpy(np.ascontiguousarray(a)).cuda()
+            for a in (packed[0][0], packed[1][0], packed[2][0], packed[0][1], packed[1][1],
+                      packed[2][1])]
+    tabs = [[t.data_ptr()] for t in keep]
+    idx = np.zeros((n, 1), np.int32)
+    wt = np.ones((n, 1), np.float32)
+    xr, out = x.copy(), base.copy()
+    force_tc(monkeypatch)
+    moe.host_register(xr)
+    moe.host_register(out)
+    try:
+        moe.layer_host(n, 1, 1, 0, D, I, cases.FMT_MXFP4, idx, wt, xr, tabs, out,
+                       cases.ACT_SILU)
+    finally:
+        moe.host_unregister(xr)
+        moe.host_unregister(out)
+    assert_close(out, want, "range rerun through layer_host, registered rows")
