@@ -185,6 +185,12 @@ __global__ void build_tmaps_kernel(const __grid_constant__ TmapSet<N> tpl, const
         return;
     const int e = idx / N, k = idx % N;
     const void *src = tabs.t[k] ? tabs.t[k][e] : nullptr;
+    // A null array belongs to an expert this launch skips: its map is never
+    // read, so it keeps whatever an earlier call left there (a call that runs
+    // its experts in several batches, each with the others null, then finds
+    // every map unchanged and needs no proxy fences).
+    if (!src)
+        return;
     uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<size_t>(idx) * 128);
     // The wanted map in registers: template with the address swapped in.
     __shared__ __align__(128) uint8_t staged[128 * 128];
@@ -193,11 +199,10 @@ __global__ void build_tmaps_kernel(const __grid_constant__ TmapSet<N> tpl, const
 #pragma unroll
     for (int i = 0; i < 8; ++i)
         mine[i] = from[i];
-    if (src)
-        asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(
-                         smem_u32(mine)),
-                     "l"(src)
-                     : "memory");
+    asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(
+                     smem_u32(mine)),
+                 "l"(src)
+                 : "memory");
     bool same = true;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {

@@ -61,7 +61,7 @@ struct Context {
     std::map<uintptr_t, size_t> host_reg; // caller buffers page-locked by host_register
     cudaStream_t copy_stream = nullptr; // stream-ins of cold blobs, caller rows of layer_host
     cudaEvent_t copy_done = nullptr;
-    cudaEvent_t call_start = nullptr, x_in = nullptr, out_in = nullptr; // layer_host copies
+    cudaEvent_t call_start = nullptr, x_in = nullptr, out_in = nullptr; // caller-row copies
     uint64_t calls = 0, experts = 0, rows = 0;
     double h2d_ms = 0, kernel_ms = 0, d2h_ms = 0;
 };
@@ -1180,24 +1180,24 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
             fast = false;
     const int fmt_run = fmt;
 
-    // Device tables + metadata + activations + out, one upload.  With
-    // stream-ins, two table sets: the first batch sees the other experts'
-    // pointers as null (skipped, its base still advancing -- the plan's
-    // rule), the second batch the reverse; both write their own y rows.
-    std::vector<void *> tab(size_t(two_batches ? 12 : 6) * nb, nullptr);
+    // With tier stream-ins, two table sets: the first batch sees the late
+    // experts' pointers as null (skipped, their row base still advancing --
+    // the plan's rule), the second batch the reverse; both write their own y
+    // rows and the combine runs once.
+    const size_t xb = size_t(x_rows) * D * 4, ob = size_t(S_ext) * D * 4;
+    const int n_groups = two_batches ? 2 : 1;
+    std::vector<int> grp(size_t(nb), 0);
     for (int e = 0; e < nb; ++e)
-        for (int k = 0; k < 6; ++k) {
-            void *p = tdev[size_t(6) * e + k];
-            tab[size_t(k) * nb + e] = (two_batches && late[size_t(e)]) ? nullptr : p;
-            if (two_batches)
-                tab[size_t(6 + k) * nb + e] = late[size_t(e)] ? p : nullptr;
-        }
+        grp[size_t(e)] = (two_batches && late[size_t(e)]) ? 1 : 0;
+    std::vector<void *> tab(size_t(6) * n_groups * nb, nullptr);
+    for (int e = 0; e < nb; ++e)
+        for (int k = 0; k < 6; ++k)
+            tab[(size_t(6) * grp[size_t(e)] + k) * nb + e] = tdev[size_t(6) * e + k];
     std::vector<int> nr_run(nb), xoff_run(nb);
     for (int e = 0; e < nb; ++e) {
         nr_run[e] = nr[e];
         xoff_run[e] = valid[e] ? xoff[e] : 0;
     }
-    const size_t xb = size_t(x_rows) * D * 4, ob = size_t(S_ext) * D * 4;
     Carve hcv(nullptr, ~size_t(0));
     const size_t o_tab = (hcv.take<void *>(tab.size()), hcv.used - tab.size() * sizeof(void *));
     const size_t o_nr = (hcv.take<int>(nb), hcv.used - nb * 4);
@@ -1207,6 +1207,7 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     const size_t o_rw = (hcv.take<float>(R), hcv.used - size_t(R) * 4);
     const size_t o_x = (hcv.take<uint8_t>(xb), hcv.used - xb);
     const size_t o_out = (hcv.take<uint8_t>(ob), hcv.used - ob);
+    const size_t o_err = (hcv.take<int>(16), hcv.used - 64); // the error word, read back
     const size_t up_bytes = hcv.used;
     if (int rc = ensure_pinned(c, up_bytes))
         return rc;
@@ -1230,21 +1231,39 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     dcv.take<uint8_t>(up_bytes);
     RunWs w{};
     carve_run(dcv, w, nb, D, Iinter, fast, R, int(x_rows));
+    dcv.take<uint8_t>(ob); // the caller's out rows as uploaded
     if (int rc = ensure_dev(c.ws, dcv.used))
         return rc;
     uint8_t *db = static_cast<uint8_t *>(c.ws.p);
     Carve dcv2(db, c.ws.bytes);
     dcv2.take<uint8_t>(up_bytes);
     carve_run(dcv2, w, nb, D, Iinter, fast, R, int(x_rows));
+    uint8_t *d_out_in = dcv2.take<uint8_t>(ob);
 
+    // Metadata on the launch stream; the caller's rows on the copy stream (x,
+    // then out, which only the combine reads, so its copy overlaps the expert
+    // kernels), except when the tier's stream-ins occupy the copy stream:
+    // then on the launch stream ahead of the kernels.
+    const void *x_src = x_reg ? static_cast<const void *>(xg) : hp + o_x;
+    const void *o_src = out_reg ? static_cast<const void *>(out) : hp + o_out;
+    cudaStream_t rows_st = two_batches ? c.stream : c.copy_stream;
     CUDA_TRY(cudaEventRecord(c.ev[0], c.stream));
     CUDA_TRY(cudaMemcpyAsync(db, hp, o_x, cudaMemcpyHostToDevice, c.stream));
-    CUDA_TRY(cudaMemcpyAsync(db + o_x, x_reg ? static_cast<const void *>(xg) : hp + o_x, xb,
-                             cudaMemcpyHostToDevice, c.stream));
-    if (S_ext > 0)
-        CUDA_TRY(cudaMemcpyAsync(db + o_out, out_reg ? static_cast<const void *>(out) : hp + o_out,
-                                 ob, cudaMemcpyHostToDevice, c.stream));
     CUDA_TRY(cudaMemsetAsync(w.err, 0, sizeof(int), c.stream));
+    if (!two_batches) {
+        CUDA_TRY(cudaEventRecord(c.call_start, c.stream));
+        CUDA_TRY(cudaStreamWaitEvent(c.copy_stream, c.call_start, 0));
+    }
+    CUDA_TRY(cudaMemcpyAsync(db + o_x, x_src, xb, cudaMemcpyHostToDevice, rows_st));
+    CUDA_TRY(cudaEventRecord(c.x_in, rows_st));
+    if (S_ext > 0) {
+        CUDA_TRY(cudaMemcpyAsync(db + o_out, o_src, ob, cudaMemcpyHostToDevice, rows_st));
+        if (out_reg) // kept as uploaded: on a device error the caller's rows go back
+            CUDA_TRY(cudaMemcpyAsync(d_out_in, db + o_out, ob, cudaMemcpyDeviceToDevice,
+                                     rows_st));
+    }
+    CUDA_TRY(cudaEventRecord(c.out_in, rows_st));
+    CUDA_TRY(cudaStreamWaitEvent(c.stream, c.x_in, 0));
     CUDA_TRY(cudaEventRecord(c.ev[1], c.stream));
     prof_mark(c.stream, kPhStart);
     void *const *dt = reinterpret_cast<void *const *>(db + o_tab);
@@ -1266,17 +1285,22 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
                            w2);
     };
     int rc = MVLLM_OK;
-    if (n_late < n_valid)
+    if (two_batches) {
+        if (n_late < n_valid)
+            rc = run_batch(dt);
+        if (!rc) {
+            CUDA_TRY(cudaStreamWaitEvent(c.stream, c.copy_done, 0));
+            rc = run_batch(dt + 6 * nb);
+        }
+    } else {
         rc = run_batch(dt);
-    if (!rc && two_batches) {
-        CUDA_TRY(cudaStreamWaitEvent(c.stream, c.copy_done, 0));
-        rc = run_batch(dt + 6 * nb);
     }
     if (rc) {
         cudaStreamSynchronize(c.copy_stream);
         cudaStreamSynchronize(c.stream);
         return rc;
     }
+    CUDA_TRY(cudaStreamWaitEvent(c.stream, c.out_in, 0));
     {
         dim3 grid((D + 255) / 256, std::min(S_ext, 65535));
         combine_csr_kernel<<<grid, 256, 0, c.stream>>>(
@@ -1287,13 +1311,20 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
         prof_mark(c.stream, kPhCombine);
     }
     if (out_reg) {
-        // The error word first: on an error `out` must stay untouched.
-        if (int rc2 = check_device_error(w.err, c.stream))
-            return rc2;
+        // The error word and `out` in one round trip; on an error the rows the
+        // caller passed in are copied back, so `out` is left as it was.
+        int *herr = reinterpret_cast<int *>(hp + o_err);
         CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
+        CUDA_TRY(cudaMemcpyAsync(herr, w.err, sizeof(int), cudaMemcpyDeviceToHost, c.stream));
         CUDA_TRY(cudaMemcpyAsync(out, d_out, ob, cudaMemcpyDeviceToHost, c.stream));
         CUDA_TRY(cudaEventRecord(c.ev[3], c.stream));
         CUDA_TRY(cudaStreamSynchronize(c.stream));
+        if (*herr) {
+            const int err = *herr;
+            CUDA_TRY(cudaMemcpyAsync(out, d_out_in, ob, cudaMemcpyDeviceToHost, c.stream));
+            CUDA_TRY(cudaStreamSynchronize(c.stream));
+            return fail(err, "device-side error code %d", err);
+        }
     } else {
         CUDA_TRY(cudaEventRecord(c.ev[2], c.stream));
         CUDA_TRY(cudaMemcpyAsync(hp + o_out, d_out, ob, cudaMemcpyDeviceToHost, c.stream));

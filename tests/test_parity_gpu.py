@@ -334,3 +334,41 @@ def test_combine_linearity(moe, port):
     ok2, out2 = run_host_block(moe, c2)
     assert ok and ok2
     np.testing.assert_array_equal(out2, 2 * out1)
+
+
+def test_moe_block_large_rows(moe, port):
+    """A moe_block call with more than 4 MB of activation rows, 16 experts and
+    200 destination rows accumulated into: against the oracle, with the
+    caller's rows page-locked (direct copies on the copy stream, out read
+    back with the error word) and without (pinned staging); the two agree
+    bit for bit."""
+    rng = np.random.default_rng(77)
+    D, I, nb = 2048, 512, 16
+    ex = cases.make_experts(port, rng, cases.FMT_MXFP4, nb, D, I)
+    nr = rng.integers(20, 45, nb).astype(np.int32)
+    R = int(nr.sum())
+    assert R * D * 4 >= 4 << 20
+    xoff = np.concatenate([[0], np.cumsum(nr)[:-1]]).astype(np.int32)
+    xg = cases.bf16_round(rng.standard_normal((R, D)).astype(np.float32))
+    S = 200
+    rows = rng.integers(0, S, R).astype(np.int32)
+    rw = rng.random(R).astype(np.float32)
+    c = dict(D=D, I=I, fmt=cases.FMT_MXFP4, act=cases.ACT_SILU, act_a=0.0, act_b=0.0, nb=nb,
+             g=[e[0][0] for e in ex], u=[e[1][0] for e in ex], d=[e[2][0] for e in ex],
+             gs=[e[0][1] for e in ex], us=[e[1][1] for e in ex], ds=[e[2][1] for e in ex],
+             xg=xg, xoff=xoff, nr=nr, rows=rows, rw=rw, S=S)
+    base = rng.standard_normal((S, D)).astype(np.float32)
+    _, want = cases.run_block(port, c, out=base.copy())
+    args = (nb, D, I, cases.FMT_MXFP4, c["g"], c["u"], c["d"], c["gs"], c["us"], c["ds"])
+    out_a = base.copy()
+    assert moe.moe_block(*args, xg, xoff, nr, rows, rw, out_a, S, cases.ACT_SILU, 0.0, 0.0)
+    assert_close(out_a, want, "large rows")
+    x_r, out_b = xg.copy(), base.copy()
+    moe.host_register(x_r)
+    moe.host_register(out_b)
+    try:
+        assert moe.moe_block(*args, x_r, xoff, nr, rows, rw, out_b, S, cases.ACT_SILU, 0.0, 0.0)
+    finally:
+        moe.host_unregister(x_r)
+        moe.host_unregister(out_b)
+    np.testing.assert_array_equal(out_b, out_a)
