@@ -963,9 +963,10 @@ def main():
                          "algorithmic_bytes_per_step": alg_bytes,
                          "kernel_ms_per_step": k_ms},
             "phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
-            # per decode step: permute (member, count, offsets, place), gather,
-            # plan, tensor-map build, decode phase 1, decode phase 2, combine
-            "gpu_launches": 10 * args.steps,
+            # per decode step: permutation (one CTA at decode batch sizes),
+            # gather, plan, tensor-map build, decode phase 1, decode phase 2,
+            # combine
+            "gpu_launches": 7 * args.steps,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "mvllm_moe_layer_host",
                     "host_buffers": "caller x / out page-locked with mvllm_moe_host_register"},

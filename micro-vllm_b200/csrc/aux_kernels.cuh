@@ -396,6 +396,93 @@ __global__ void permute_place_kernel(const int *__restrict__ idx, int T, int K, 
     }
 }
 
+// Steps 1-4 in one CTA for small batches (decode: T <= kPermSmallT, so a
+// bitmap row is at most 8 words): the same arithmetic in one launch instead
+// of four plus the bitmap clear.  Global memory written by the CTA's own
+// threads is visible to all of them after each __syncthreads.
+constexpr int kPermSmallT = 256;
+__global__ void __launch_bounds__(1024)
+    permute_small_kernel(const int *__restrict__ idx, const float *__restrict__ wt, int T, int K,
+                         int E, int n_shared, int words, uint32_t *__restrict__ bitmap,
+                         int *__restrict__ wpre, float *__restrict__ wsum, int *__restrict__ nr,
+                         int *__restrict__ xoff, int *__restrict__ n_rows,
+                         int *__restrict__ rows, float *__restrict__ rw,
+                         int *__restrict__ tok_pos) {
+    __shared__ int warp_sums[32];
+    const int EE = E + n_shared, KK = K + n_shared;
+    for (int i = threadIdx.x; i < EE * words; i += blockDim.x)
+        bitmap[i] = 0u;
+    __syncthreads();
+    // step 1: membership and per-token weight sums (permute_member_kernel)
+    for (int c = threadIdx.x; c < T; c += blockDim.x) {
+        const int *ic = idx + static_cast<size_t>(c) * K;
+        const float *wc = wt + static_cast<size_t>(c) * K;
+        for (int t = 0; t < K; ++t) {
+            const int e = ic[t];
+            tok_pos[static_cast<size_t>(c) * KK + t] = -1;
+            if (e < 0 || e >= E)
+                continue;
+            bool dup = false;
+            for (int t2 = 0; t2 < t; ++t2)
+                dup |= (ic[t2] == e);
+            if (dup)
+                continue;
+            float s = 0.f;
+            for (int t2 = 0; t2 < K; ++t2)
+                if (ic[t2] == e)
+                    s = __fadd_rn(s, wc[t2]);
+            if (s == 0.f)
+                continue;
+            wsum[static_cast<size_t>(c) * KK + t] = s;
+            tok_pos[static_cast<size_t>(c) * KK + t] = -2;
+            atomicOr(&bitmap[static_cast<size_t>(e) * words + (c >> 5)], 1u << (c & 31));
+        }
+        if (n_shared) {
+            wsum[static_cast<size_t>(c) * KK + K] = 1.f;
+            tok_pos[static_cast<size_t>(c) * KK + K] = -2;
+            atomicOr(&bitmap[static_cast<size_t>(E) * words + (c >> 5)], 1u << (c & 31));
+        }
+    }
+    __syncthreads();
+    // step 2: word prefixes and member counts, a thread per expert
+    for (int e = threadIdx.x; e < EE; e += blockDim.x) {
+        int carry = 0;
+        for (int j = 0; j < words; ++j) {
+            wpre[static_cast<size_t>(e) * words + j] = carry;
+            carry += __popc(bitmap[static_cast<size_t>(e) * words + j]);
+        }
+        nr[e] = carry;
+    }
+    __syncthreads();
+    // step 3: segment starts in ascending expert id (permute_offsets_kernel)
+    int carry = 0;
+    for (int e0 = 0; e0 < EE; e0 += blockDim.x) {
+        const int e = e0 + threadIdx.x;
+        const int v = e < EE ? nr[e] : 0;
+        int tot;
+        const int ex = block_exclusive_scan(v, warp_sums, &tot);
+        if (e < EE)
+            xoff[e] = carry + ex;
+        carry += tot;
+    }
+    if (threadIdx.x == 0)
+        *n_rows = carry;
+    __syncthreads();
+    // step 4: positions (permute_place_kernel)
+    const int n = T * KK;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        if (tok_pos[i] != -2)
+            continue;
+        const int c = i / KK, sl = i - c * KK;
+        const int e = sl < K ? idx[static_cast<size_t>(c) * K + sl] : E;
+        const size_t wi = static_cast<size_t>(e) * words + (c >> 5);
+        const int pos = xoff[e] + wpre[wi] + __popc(bitmap[wi] & ((1u << (c & 31)) - 1u));
+        rows[pos] = c;
+        rw[pos] = wsum[i];
+        tok_pos[i] = pos;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Ordered combine, layer form: out[c] += wsum*y over the token's segment
 // positions in ascending order (= ascending expert id), one multiply and one

@@ -1430,6 +1430,13 @@ void carve_perm(Carve &cv, PermWs &p, int T, int K, int E, int n_shared) {
 int run_permute(cudaStream_t st, int sms, const int *idx, const float *wt, int T, int K, int E,
                 int n_shared, int *nr, int *xoff, int *rows, float *rw, int *tok_pos,
                 int *n_rows, const PermWs &p) {
+    if (T <= kPermSmallT && E + n_shared <= 4096) {
+        permute_small_kernel<<<1, 1024, 0, st>>>(idx, wt, T, K, E, n_shared, p.words, p.bitmap,
+                                                 p.wpre, p.wsum, nr, xoff, n_rows, rows, rw,
+                                                 tok_pos);
+        CUDA_TRY(cudaGetLastError());
+        return MVLLM_OK;
+    }
     CUDA_TRY(cudaMemsetAsync(p.bitmap, 0, size_t(E + n_shared) * p.words * 4, st));
     permute_member_kernel<<<std::max(1, std::min((T + 127) / 128, 4 * sms)), 128, 0, st>>>(
         idx, wt, T, K, E, n_shared, p.words, p.bitmap, p.wsum, tok_pos);
