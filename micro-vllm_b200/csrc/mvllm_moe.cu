@@ -2134,8 +2134,9 @@ __global__ void wait_selftest_kernel(int *err, int *result) {
 
 int mvllm_moe_wait_selftest(int *completed, int *timed_out) {
     Context &c = ctx();
-    if (!c.inited)
-        return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (int rc = ensure_current(c))
+        return rc;
     int *d = nullptr;
     CUDA_TRY(cudaMalloc(&d, 2 * sizeof(int)));
     int h[2] = {0, 0};
