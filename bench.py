@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--no-dsv4", action="store_true",
                     help="skip the DeepSeek-V4 expert-split (EP2) leg")
     ap.add_argument("--dsv4-steps", type=int, default=100)
+    ap.add_argument("--dsv4-all-ranks", action="store_true",
+                    help="run the DeepSeek-V4 leg on more than two ranks too")
     ap.add_argument("--prefill-tokens", type=int, default=4096,
                     help="config[3]: 4096; fewer only to size a profiler capture")
     ap.add_argument("--experts", type=int, default=256,
@@ -911,9 +913,10 @@ def main():
         ep_res["weak_scaling"] = (ep_bench(moe, torch, dist, rank, world, args.ep_steps, weak=True)
                                   if world > 1 else "same workload as the strong run at 1 GPU")
 
-    # DeepSeek-V4 MoE step, experts split over all ranks (two ranks = EP2)
+    # DeepSeek-V4 MoE step, experts split over the ranks: one GPU, or the
+    # reference's two-rank EP2 (more ranks with --dsv4-all-ranks)
     dsv4_res = None
-    if not args.no_dsv4:
+    if not args.no_dsv4 and (world <= 2 or args.dsv4_all_ranks):
         dsv4_res = dsv4_bench(moe, torch, dist, rank, world, wl, args.dsv4_steps)
 
     # config[3] prefill (tensor-core kernels), per rank
