@@ -10,7 +10,9 @@ expert-split step (micro-vllm_b200/dsv4.py) run as two gloo ranks.
 * route_moe_ep2 (parity split + allreduce_pair), bit for bit, with absent
   bank slots and with and without the shared expert.
 * dsv4.EP2Layer over two gloo ranks and emulated: bit-identical to the
-  oracle's route_moe_ep2 plus the layer tail.
+  oracle's route_moe_ep2 plus the layer tail; over three gloo ranks, the same
+  result on every rank, within tolerance.
+* the expert blob geometry (make_mx_geom and the blob order).
 """
 import os
 import socket
