@@ -98,3 +98,33 @@ def test_init_without_gpu_reports_error(lib):
     rc = lib.lib().mvllm_moe_init(0)
     assert rc in (lib.ERR_CUDA, lib.ERR_INVALID)
     assert lib.last_error()
+
+
+def _cpp_caller(lib):
+    """Builds and runs tests/cpp_caller.cpp; returns its stdout."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out_dir = os.path.join(root, "tests", "_build")
+    os.makedirs(out_dir, exist_ok=True)
+    exe = os.path.join(out_dir, "cpp_caller")
+    libdir = os.path.dirname(lib.LIB_PATH)
+    subprocess.run(["g++", "-std=c++17", "-O1", "-Wall", "-Werror",
+                    os.path.join(root, "tests", "cpp_caller.cpp"),
+                    "-I" + os.path.join(root, "include"), "-L" + libdir, "-lmvllm_moe",
+                    "-Wl,-rpath," + libdir, "-o", exe], check=True)
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "CPP-CALLER-OK" in r.stdout
+    return r.stdout
+
+
+def test_cpp_caller_links_and_runs(lib):
+    """A reference-style C++ translation unit links against the library through
+    include/mvllm_metal_ops.hpp and runs (tests/cpp_caller.cpp): argument
+    rejection and backend identity; the device call where a GPU is present."""
+    _cpp_caller(lib)
+
+
+@pytest.mark.gpu
+def test_cpp_caller_device_call(lib):
+    """The same C++ caller on a GPU: metal_ops::init and one moe_block call."""
+    assert "(no device)" not in _cpp_caller(lib)
