@@ -127,4 +127,7 @@ def test_cpp_caller_links_and_runs(lib):
 @pytest.mark.gpu
 def test_cpp_caller_device_call(lib):
     """The same C++ caller on a GPU: metal_ops::init and one moe_block call."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
     assert "(no device)" not in _cpp_caller(lib)
