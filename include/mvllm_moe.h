@@ -182,20 +182,22 @@ MVLLM_API int mvllm_moe_permute_dev(void *stream, const int *idx, const float *w
 
 /* The permutation above with no workspace argument and no allocation at
  * all.  No counterpart in the reference: it exists for callers that cannot
- * allocate device memory when they need the permutation -- code inside a CUDA
- * graph capture (cudaMalloc would break the capture), engines that fix their
- * HBM budget at start-up and forbid allocation in the decode loop, and
- * plugins whose host process owns the GPU allocator.  The scratch (bitmap and
- * per-token weight sums) is a file-scope __device__ array of
- * MVLLM_PERMUTE_STATIC_BYTES that every GPU loading the library keeps until
- * the process exits.  Sizes whose mvllm_moe_permute_workspace() exceeds it
- * are rejected with MVLLM_ERR_WORKSPACE (e.g. T=8192, K=8, E=384 fits).  The
- * first call on a device looks up the array's device address (once per
- * device, with that device current); make that first call before any stream
- * capture.  All calls share the one array: calls whose executions overlap
- * on the GPU (different streams, or graphs replayed concurrently) race.
- * Outputs, ordering and error codes are those of mvllm_moe_permute_dev; does
- * not require mvllm_moe_init. */
+ * allocate device memory when they need the permutation -- engines that fix
+ * their HBM budget at start-up and forbid allocation in the serving loop, and
+ * plugins living in a host process whose own allocator owns the GPU's memory
+ * (a cudaMalloc behind its back would take memory it has promised
+ * elsewhere).  The scratch (bitmap and per-token weight sums) is a
+ * file-scope __device__ array of MVLLM_PERMUTE_STATIC_BYTES that every GPU
+ * loading the library keeps until the process exits.  Sizes whose scratch
+ * exceeds it are rejected with MVLLM_ERR_WORKSPACE before any launch: the
+ * scratch is mvllm_moe_permute_workspace() minus its 256 bytes of alignment
+ * slack, so T=8192, K=8, E=384, n_shared=0 (exactly 1 MiB) fits and T=8193
+ * does not.  The first call on a device looks up the array's device address
+ * (once per device, with that device current); make that first call before
+ * any stream capture.  All calls share the one array, which keeps the last
+ * call's contents (each call clears what must start at zero): calls whose
+ * executions overlap on the GPU race.  Outputs, ordering and error codes are
+ * those of mvllm_moe_permute_dev; does not require mvllm_moe_init. */
 #define MVLLM_PERMUTE_STATIC_BYTES (1u << 20)
 MVLLM_API int mvllm_moe_permute_dev_noalloc(void *stream, const int *idx, const float *wt, int T,
                                             int K, int E, int n_shared, int *nr, int *xoff,

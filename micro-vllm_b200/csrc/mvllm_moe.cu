@@ -1454,13 +1454,21 @@ int run_permute(cudaStream_t st, int sms, const int *idx, const float *wt, int T
 }
 } // namespace
 
-size_t mvllm_moe_permute_workspace(int T, int K, int E, int n_shared) {
-    if (T < 1 || K < 1 || E < 1 || n_shared < 0 || n_shared > 1)
-        return 0;
+namespace {
+// Bytes the permutation's scratch takes from a 256-byte-aligned base (the
+// carve's own use, without the alignment slack a caller buffer needs).
+size_t perm_scratch_bytes(int T, int K, int E, int n_shared) {
     Carve cv(nullptr, ~size_t(0));
     PermWs p{};
     carve_perm(cv, p, T, K, E, n_shared);
-    return cv.used + 256;
+    return cv.used;
+}
+} // namespace
+
+size_t mvllm_moe_permute_workspace(int T, int K, int E, int n_shared) {
+    if (T < 1 || K < 1 || E < 1 || n_shared < 0 || n_shared > 1)
+        return 0;
+    return perm_scratch_bytes(T, K, E, n_shared) + 256;
 }
 
 int mvllm_moe_permute_dev(void *stream, const int *idx, const float *wt, int T, int K, int E,
@@ -1489,10 +1497,9 @@ int mvllm_moe_permute_dev(void *stream, const int *idx, const float *wt, int T, 
 
 // ------------------------------------------------ permutation, no allocation --
 // Some callers cannot allocate device memory at the moment they need the
-// permutation: code running while a CUDA graph is being captured (cudaMalloc
-// is not a stream operation and breaks the capture), engines that partition
-// HBM once at start-up and forbid allocation in the decode loop, and plugins
-// living inside a host process whose allocator owns the GPU.  For them
+// permutation: engines that partition HBM once at start-up and forbid
+// allocation in the serving loop, and plugins living inside a host process
+// whose own allocator owns the GPU's memory.  For them
 // mvllm_moe_permute_dev_noalloc keeps its scratch (membership bitmap and
 // per-token weight sums) in this file-scope device array.  Every GPU that
 // loads the library holds it until the process exits.
@@ -1535,7 +1542,8 @@ int mvllm_moe_permute_dev_noalloc(void *stream, const int *idx, const float *wt,
     if (!idx || !wt || T < 1 || K < 1 || E < 1 || n_shared < 0 || n_shared > 1 || !nr || !xoff ||
         !rows || !rw || !tok_pos || !n_rows)
         return fail(MVLLM_ERR_INVALID, "permute_dev_noalloc: invalid arguments");
-    const size_t need = mvllm_moe_permute_workspace(T, K, E, n_shared);
+    // g_permute_scratch is 256-byte aligned, so the carve needs no slack.
+    const size_t need = perm_scratch_bytes(T, K, E, n_shared);
     if (need > kPermuteStaticBytes)
         return fail(MVLLM_ERR_WORKSPACE,
                     "permute_dev_noalloc: T=%d K=%d E=%d n_shared=%d needs %zu bytes of scratch, "
