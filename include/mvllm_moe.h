@@ -54,10 +54,41 @@ enum {
     MVLLM_ERR_NOT_INIT = 6,    /* mvllm_moe_init has not succeeded */
     MVLLM_ERR_DEVICE = 7,      /* a device-side bounds check rejected an index */
     MVLLM_ERR_WORKSPACE = 8,   /* caller workspace smaller than required */
-    MVLLM_ERR_RANGE = 9        /* an MXFP4 scale code in 141..254 reached the tensor-core path,
-                                  whose f16 weights cannot hold it; the host-pointer entries
-                                  rerun such a call on the decode path and never return it */
+    MVLLM_ERR_RANGE = 9,       /* an MXFP4 scale code the tensor-core path cannot represent
+                                  as the reference decodes it (f16 mode: 141..254; block-scaled
+                                  modes: 255, which the MMA reads as NaN, not +inf); the
+                                  host-pointer entries rerun such a call on the decode path
+                                  and never return it */
+    MVLLM_ERR_ACT_RANGE = 10   /* a finite activation (a token row of x, or h = act(gate, up))
+                                  beyond the f16 operand range (|v| >= 65520): the reference
+                                  computes it in f32; this library refuses the call instead of
+                                  returning inf */
 };
+
+/* How experts on the tensor-core path (prefill-sized calls) compute with
+ * MXFP4 weights.  No counterpart in the reference (its matmul_mxfp4,
+ * src/quant/quant.cpp:298-321, is f32 throughout); every mode stays within
+ * the 1e-2 relative-L2 / 2e-2 max-abs tolerance only where noted:
+ *   F16      weights dequantised to f16 in tensor memory, tokens f16
+ *            (kind::f16).  Within tolerance.
+ *   MXF4_Xn  weights used as they are (e2m1 + ue8m0 per 32, kind::mxf4 with
+ *            the block scales in tensor memory); tokens as n block-scaled
+ *            e2m1 terms, each quantising the previous terms' residual.
+ *            n = 3 is within tolerance (measured ~3e-3 rel-L2); n = 1, 2
+ *            are not (~2e-1, ~3e-2) and exist to measure the native mode.
+ *   MXF8_Xn  weights as they are (kind::mxf8f6f4, e2m1 x e4m3); tokens as n
+ *            e4m3 terms.  n = 2 within tolerance (~6e-4), n = 1 not (~5e-2).
+ * The default is the fastest mode within tolerance; MVLLM_PREFILL_MODE
+ * (f16, mxf4x1, mxf4x2, mxf4x3, mxf8x1, mxf8x2) overrides it at first use. */
+enum {
+    MVLLM_PREFILL_F16 = 0,
+    MVLLM_PREFILL_MXF4_X1 = 1,
+    MVLLM_PREFILL_MXF4_X2 = 2,
+    MVLLM_PREFILL_MXF4_X3 = 3,
+    MVLLM_PREFILL_MXF8_X1 = 4,
+    MVLLM_PREFILL_MXF8_X2 = 5
+};
+#define MVLLM_PREFILL_DEFAULT MVLLM_PREFILL_MXF4_X3
 
 /* metal_ops::Act (src/gpu/metal_ops.hpp:44); any other value behaves as SILU. */
 enum { MVLLM_ACT_SILU = 0, MVLLM_ACT_CLAMP_SWIGLU = 1, MVLLM_ACT_SITU = 2 };
@@ -82,6 +113,20 @@ MVLLM_API void mvllm_moe_shutdown(void);
 MVLLM_API int mvllm_moe_available(void);
 MVLLM_API const char *mvllm_moe_backend_name(void); /* "cuda-sm100a" */
 MVLLM_API const char *mvllm_moe_last_error(void);   /* text of the last failure in this process */
+/* Process-wide prefill mode (MVLLM_PREFILL_*, or -1 for the default /
+ * MVLLM_PREFILL_MODE); MVLLM_ERR_INVALID otherwise.  get returns the mode in
+ * effect. */
+MVLLM_API int mvllm_moe_set_prefill_mode(int mode);
+MVLLM_API int mvllm_moe_get_prefill_mode(void);
+/* The block-scaled modes' token operand, on its own (no counterpart in the
+ * reference): f16 rows src [rows, K] (K % 32 == 0) as the mode's n terms,
+ * planes [n][rows][K/2] packed e2m1 (low nibble = even element; MXF4 modes)
+ * or [n][rows][K] e4m3 (MXF8 modes) and ue8m0 codes [n][rows][K/32].  Term t
+ * holds round(r_t / 2^(c-127)) of the residual r_t the earlier terms left,
+ * c the smallest code with 2^(c-127) >= max|r_t| / 6 (e2m1) or / 448 (e4m3)
+ * over each 32 elements; a block of zeros gets code 0. */
+MVLLM_API int mvllm_mx_terms_dev(void *stream, int mode, const void *src, int rows, int K,
+                                 void *planes, void *codes);
 
 /* coli_cuda::group_stats (src/gpu/coli_cuda.hpp:35-36): calls, experts, rows
  * and host-timed h2d / kernel / d2h milliseconds of the host-pointer entries. */

@@ -56,7 +56,8 @@ struct PlanArgs {
     int *base, *cnt, *off1, *off2, *total_rows;
     const int *xoff; // operand rows must satisfy 0 <= xoff[e], xoff[e]+nr[e] <= x_rows
     int x_rows;
-    int align16; // fast path: every weight and scale pointer must be 16-byte aligned
+    int align_mask; // fast path: every weight and scale pointer has these address bits clear
+                    // (15: 16-byte aligned; 31 for the mxf8f6f4 path's expanding TMA)
     int *err;
     // Tensor-core path: experts with at least tc_min rows get no decode items;
     // their 256-row token tiles (and a rest wider than tc_small rows) become
@@ -81,14 +82,14 @@ __global__ void plan_kernel(const PlanArgs a) {
             bool ok = n > 0 && a.g[e] && a.u[e] && a.d[e];
             if (a.fmt != MVLLM_FMT_F32)
                 ok = ok && a.gs[e] && a.us[e] && a.ds[e];
-            if (ok && a.align16) {
+            if (ok && a.align_mask) {
                 const uintptr_t bits = reinterpret_cast<uintptr_t>(a.g[e]) |
                                        reinterpret_cast<uintptr_t>(a.u[e]) |
                                        reinterpret_cast<uintptr_t>(a.d[e]) |
                                        reinterpret_cast<uintptr_t>(a.gs[e]) |
                                        reinterpret_cast<uintptr_t>(a.us[e]) |
                                        reinterpret_cast<uintptr_t>(a.ds[e]);
-                if (bits & 15u) {
+                if (bits & static_cast<uintptr_t>(a.align_mask)) {
                     set_error(a.err, MVLLM_ERR_DEVICE); // would break the bulk copies: skip
                     ok = false;
                 }
@@ -247,11 +248,12 @@ __global__ void stage_rows_kernel(const TIn *__restrict__ x, const int *__restri
 
 // Vectorised form for the fast path (D % 8 == 0): a CTA per row at a time,
 // a thread per aligned 8-column chunk, 16-byte stores of f16 in stage_pos
-// order (several chunks per thread in flight).
+// order (several chunks per thread in flight).  A finite value beyond the
+// f16 range records MVLLM_ERR_ACT_RANGE (it would otherwise become inf).
 template <typename TIn>
 __global__ void stage_rows_f16x8_kernel(const TIn *__restrict__ x, const int *__restrict__ index,
                                         const int *__restrict__ nrows_dev, int nrows_host, int D,
-                                        int fmt, __half *__restrict__ out) {
+                                        int fmt, __half *__restrict__ out, int *err) {
     const int nrows = nrows_dev ? *nrows_dev : nrows_host;
     const int chunks = D >> 3;
     for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
@@ -275,6 +277,12 @@ __global__ void stage_rows_f16x8_kernel(const TIn *__restrict__ x, const int *__
                     v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
                 }
             }
+            bool big = false;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                big |= beyond_f16(v[j]);
+            if (big)
+                set_error(err, MVLLM_ERR_ACT_RANGE);
             __half2 h[4];
             if (fmt == MVLLM_FMT_INT4_G64) { // k0,k4,k1,k5,k2,k6,k3,k7
 #pragma unroll

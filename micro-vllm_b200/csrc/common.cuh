@@ -40,6 +40,12 @@ __device__ __forceinline__ int load_volatile(const int *p) {
     return *reinterpret_cast<const volatile int *>(p);
 }
 
+// A finite value the f16 operands cannot hold (it would round to inf).
+__device__ __forceinline__ bool beyond_f16(float v) {
+    const float a = fabsf(v);
+    return a >= 65520.f && a <= 3.402823466e38f;
+}
+
 // Largest e with off[e] <= i, for off non-decreasing and off[nb] > i.
 __device__ __forceinline__ int find_owner(const int *off, int nb, int i) {
     int lo = 0, hi = nb;

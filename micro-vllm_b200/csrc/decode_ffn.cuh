@@ -473,6 +473,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
                             up += rd[(q * kDecodeRows + 32 + f) * L::RS + n];
                         }
                         const float hv = apply_act(gt, up, p.act, p.act_a, p.act_b);
+                        if (beyond_f16(hv))
+                            set_error(p.err, MVLLM_ERR_ACT_RANGE);
                         hp[static_cast<size_t>(orow0 + n) * p.O + stage_pos(rb * 32 + f, FMT)] =
                             __float2half_rn(hv);
                     }

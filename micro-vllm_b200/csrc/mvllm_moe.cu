@@ -6,6 +6,7 @@
 #include "aux_kernels.cuh"
 #include "decode_ffn.cuh"
 #include "tc_ffn.cuh"
+#include "tc_mx.cuh"
 #include "ep_kernels.cuh"
 #include "route_kernels.cuh"
 #include "dense_ffn.cuh"
@@ -14,6 +15,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cstdarg>
 #include <cstdio>
@@ -219,6 +221,11 @@ struct RunWs {
     void *xs; // staged operand (fast: f16, generic: f32)
     void *h;  // fast: f16 [rows, I]; generic: f32 [rows, I]
     float *y; // [rows, D]
+    // Block-scaled tensor-core path (fast path only): per-expert weight maps,
+    // and the token operands as block-scaled terms (planes + ue8m0 codes) of
+    // x [x_rows, D] and h [h_rows, I], sized for the widest mode.
+    uint8_t *mx_tmaps;
+    uint8_t *xq, *xc, *hq, *hc;
 };
 
 // Carves the expert-run workspace; x_rows = operand rows to stage (0 when the
@@ -242,6 +249,38 @@ void carve_run(Carve &cv, RunWs &w, int nb, int D, int I, bool fast, int rows_ca
     w.xs = cv.take<uint8_t>(size_t(std::max(x_rows, 1)) * D * esz);
     w.h = cv.take<uint8_t>(size_t(std::max(rows_cap, 1)) * I * esz);
     w.y = cv.take<float>(size_t(std::max(rows_cap, 1)) * D);
+    w.mx_tmaps = w.xq = w.xc = w.hq = w.hc = nullptr;
+    if (fast) {
+        // Widest modes: two e4m3 terms (2 bytes per element) or three e2m1
+        // terms (3 codes per 32 elements).
+        const size_t xr = size_t(std::max(x_rows, 1)), hr = size_t(std::max(rows_cap, 1));
+        w.mx_tmaps = cv.take<uint8_t>(size_t(nb) * kMxMapCount * kTcMapBytes);
+        w.xq = cv.take<uint8_t>(xr * D * 2);
+        w.xc = cv.take<uint8_t>(xr * (D / 32) * 3);
+        w.hq = cv.take<uint8_t>(hr * I * 2);
+        w.hc = cv.take<uint8_t>(hr * (I / 32) * 3);
+    }
+}
+
+// ------------------------------------------------- prefill (tensor-core) mode --
+// How experts on the tensor-core path compute with MXFP4 weights (header:
+// MVLLM_PREFILL_*): dequantised to f16 (kind::f16), or block-scaled with the
+// token operand as 1-3 e2m1 terms (kind::mxf4) or 1-2 e4m3 terms
+// (kind::mxf8f6f4).  Set by mvllm_moe_set_prefill_mode or MVLLM_PREFILL_MODE
+// (f16, mxf4x1, mxf4x2, mxf4x3, mxf8x1, mxf8x2).
+std::atomic<int> g_prefill_mode{-1};
+int prefill_mode() {
+    int m = g_prefill_mode.load();
+    if (m >= 0)
+        return m;
+    m = MVLLM_PREFILL_DEFAULT;
+    if (const char *e = getenv("MVLLM_PREFILL_MODE")) {
+        static const char *names[] = {"f16", "mxf4x1", "mxf4x2", "mxf4x3", "mxf8x1", "mxf8x2"};
+        for (int i = 0; i < 6; ++i)
+            if (!strcmp(e, names[i]))
+                m = i;
+    }
+    return m;
 }
 
 struct Tables {
@@ -409,6 +448,124 @@ int launch_tc(int fmt, const TcArgs &pair, const TcArgs &solo, const CUtensorMap
                                   : launch_tc_t<MVLLM_FMT_INT4_G64, PHASE, false>(solo, tok, st, sms);
 }
 
+// Weight maps of the block-scaled path: packed rows in boxes of 128 bytes of
+// one stage (mxf4: 256 packed e2m1; mxf8f6f4: 128 e2m1 as 16U4_ALIGN16B,
+// expanded to the padded form in shared memory) by 16 gate / up rows or 128
+// down rows, 128-byte swizzle; the rows' code windows as in tc_ffn.
+int make_mx_templates(TmapSet<kMxMapCount> *t, int kind, int D, int I, void *placeholder) {
+    const auto u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    const auto none = CU_TENSOR_MAP_SWIZZLE_NONE, sw = CU_TENSOR_MAP_SWIZZLE_128B;
+    int rc = 0;
+    if (kind == kMxF4) {
+        rc |= encode_2d(&t->m[kMxGateP], u8, placeholder, D / 2, I, D / 2, 128, 16, sw);
+        rc |= encode_2d(&t->m[kMxUpP], u8, placeholder, D / 2, I, D / 2, 128, 16, sw);
+        rc |= encode_2d(&t->m[kMxDownP], u8, placeholder, I / 2, D, I / 2, 128, 128, sw);
+    } else {
+        const auto u4 = CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B;
+        rc |= encode_2d(&t->m[kMxGateP], u4, placeholder, D, I, D / 2, 128, 16, sw);
+        rc |= encode_2d(&t->m[kMxUpP], u4, placeholder, D, I, D / 2, 128, 16, sw);
+        rc |= encode_2d(&t->m[kMxDownP], u4, placeholder, I, D, I / 2, 128, 128, sw);
+    }
+    rc |= encode_2d(&t->m[kMxGateS], u8, placeholder, D / 32, I, D / 32, 16, 64, none);
+    rc |= encode_2d(&t->m[kMxUpS], u8, placeholder, D / 32, I, D / 32, 16, 64, none);
+    rc |= encode_2d(&t->m[kMxDownS], u8, placeholder, I / 32, D, I / 32, 16, 128, none);
+    return rc ? MVLLM_ERR_CUDA : MVLLM_OK;
+}
+
+// 3-D map over NTERM planes of `rows` rows of `row_bytes` bytes each (term
+// planes or their code rows): box = box_inner bytes x 64 rows x 1 plane.
+int encode_planes(CUtensorMap *m, void *addr, uint64_t row_bytes, uint64_t rows, int nterm,
+                  uint32_t box_inner, CUtensorMapSwizzle swz) {
+    auto enc = tmap_encoder();
+    if (!enc)
+        return fail(MVLLM_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    const cuuint64_t dims[3] = {row_bytes, std::max<uint64_t>(rows, 1), uint64_t(nterm)};
+    const cuuint64_t strides[2] = {row_bytes, row_bytes * std::max<uint64_t>(rows, 1)};
+    const cuuint32_t box[3] = {box_inner, uint32_t(kTcTokBox), 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, addr, dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(MVLLM_ERR_CUDA, "cuTensorMapEncodeTiled (term planes) failed (%d)", int(r));
+    return MVLLM_OK;
+}
+
+int mode_kind(int mode) { return mode >= MVLLM_PREFILL_MXF8_X1 ? kMxF8 : kMxF4; }
+int mode_nterm(int mode) {
+    return mode >= MVLLM_PREFILL_MXF8_X1 ? mode - MVLLM_PREFILL_MXF8_X1 + 1 : mode;
+}
+
+// Term planes of f16 rows [rows, K] for the block-scaled path.
+int launch_terms(int mode, const void *src, int rows, int K, uint8_t *planes, uint8_t *codes,
+                 cudaStream_t st, int sms) {
+    const long long threads = static_cast<long long>(rows) * (K / 8);
+    const int blocks = static_cast<int>(std::max<long long>(
+        1, std::min<long long>((threads + 255) / 256, 16LL * sms)));
+    const __half *x = static_cast<const __half *>(src);
+    switch (mode) {
+    case MVLLM_PREFILL_MXF4_X1: mx_terms_kernel<kMxF4, 1><<<blocks, 256, 0, st>>>(x, rows, K, planes, codes); break;
+    case MVLLM_PREFILL_MXF4_X2: mx_terms_kernel<kMxF4, 2><<<blocks, 256, 0, st>>>(x, rows, K, planes, codes); break;
+    case MVLLM_PREFILL_MXF4_X3: mx_terms_kernel<kMxF4, 3><<<blocks, 256, 0, st>>>(x, rows, K, planes, codes); break;
+    case MVLLM_PREFILL_MXF8_X1: mx_terms_kernel<kMxF8, 1><<<blocks, 256, 0, st>>>(x, rows, K, planes, codes); break;
+    case MVLLM_PREFILL_MXF8_X2: mx_terms_kernel<kMxF8, 2><<<blocks, 256, 0, st>>>(x, rows, K, planes, codes); break;
+    default: return fail(MVLLM_ERR_INVALID, "unknown prefill mode %d", mode);
+    }
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+template <int KIND, int NTERM, int PHASE, bool PAIR>
+int launch_mx_t(const MxArgs &a, const CUtensorMap &tok, const CUtensorMap &tsc, cudaStream_t st,
+                int sms) {
+    using C = MxCfg<KIND, NTERM, PAIR>;
+    auto kern = tc_mx_kernel<KIND, NTERM, PHASE, PAIR>;
+    static bool attr = false;
+    if (!attr) {
+        CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr = true;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    if (PAIR) {
+        cfg.gridDim = dim3(std::max(2, sms & ~1));
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+    } else {
+        cfg.gridDim = dim3(sms * C::CTAS_PER_SM);
+    }
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, tok, tsc));
+    return MVLLM_OK;
+}
+
+template <int KIND, int NTERM, int PHASE>
+int launch_mx_pair_solo(const MxArgs &pair, const MxArgs &solo, const CUtensorMap &tok,
+                        const CUtensorMap &tsc, cudaStream_t st, int sms) {
+    if (int rc = launch_mx_t<KIND, NTERM, PHASE, true>(pair, tok, tsc, st, sms))
+        return rc;
+    return launch_mx_t<KIND, NTERM, PHASE, false>(solo, tok, tsc, st, sms);
+}
+
+template <int PHASE>
+int launch_mx(int mode, const MxArgs &pair, const MxArgs &solo, const CUtensorMap &tok,
+              const CUtensorMap &tsc, cudaStream_t st, int sms) {
+    switch (mode) {
+    case MVLLM_PREFILL_MXF4_X1: return launch_mx_pair_solo<kMxF4, 1, PHASE>(pair, solo, tok, tsc, st, sms);
+    case MVLLM_PREFILL_MXF4_X2: return launch_mx_pair_solo<kMxF4, 2, PHASE>(pair, solo, tok, tsc, st, sms);
+    case MVLLM_PREFILL_MXF4_X3: return launch_mx_pair_solo<kMxF4, 3, PHASE>(pair, solo, tok, tsc, st, sms);
+    case MVLLM_PREFILL_MXF8_X1: return launch_mx_pair_solo<kMxF8, 1, PHASE>(pair, solo, tok, tsc, st, sms);
+    case MVLLM_PREFILL_MXF8_X2: return launch_mx_pair_solo<kMxF8, 2, PHASE>(pair, solo, tok, tsc, st, sms);
+    default: return fail(MVLLM_ERR_INVALID, "unknown prefill mode %d", mode);
+    }
+}
+
 // Which experts take the tensor-core path: calls with at least
 // MVLLM_TC_MIN_TOTAL routed rows (default 1024: prefill chunks, not decode
 // batches) send their experts with at least MVLLM_TC_MIN_ROWS rows (default
@@ -466,6 +623,11 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
                 bool allow_tc = true) {
     const bool fast = fast_path_ok(fmt, D, I);
     const int tc_min = (fast && allow_tc) ? tc_min_rows(x_rows) : 0;
+    // Block-scaled MMAs for MXFP4 experts on the tensor-core path (the mode's
+    // term planes need the workspace's term buffers).
+    const int mode = (tc_min && fmt == MVLLM_FMT_MXFP4 && w.xq) ? prefill_mode()
+                                                                  : MVLLM_PREFILL_F16;
+    const bool mx = mode != MVLLM_PREFILL_F16;
     const int nt = chunk_tiles(avg_rows);
     const int mt = 8 * nt;
     PlanArgs pa{};
@@ -482,7 +644,8 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     }
     pa.base = w.base, pa.cnt = w.cnt, pa.off1 = w.off1, pa.off2 = w.off2;
     pa.total_rows = w.total_rows;
-    pa.xoff = xoff, pa.x_rows = x_rows, pa.err = w.err, pa.align16 = fast ? 1 : 0;
+    pa.xoff = xoff, pa.x_rows = x_rows, pa.err = w.err;
+    pa.align_mask = fast ? ((mx && mode_kind(mode) == kMxF8) ? 31 : 15) : 0;
     pa.tc_min = tc_min;
     pa.tc_small = getenv("MVLLM_TC_NO_SOLO") ? 0 : kTcSoloMax;
     pa.tc_blocks1 = I / tc_cols_per_item<1, true>();
@@ -501,11 +664,11 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             if (x_dtype == MVLLM_DTYPE_BF16)
                 stage_rows_f16x8_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
                     static_cast<const __nv_bfloat16 *>(x), nullptr, nullptr, x_rows, D, fmt,
-                    static_cast<__half *>(w.xs));
+                    static_cast<__half *>(w.xs), w.err);
             else
                 stage_rows_f16x8_kernel<float><<<blocks, 256, 0, st>>>(
                     static_cast<const float *>(x), nullptr, nullptr, x_rows, D, fmt,
-                    static_cast<__half *>(w.xs));
+                    static_cast<__half *>(w.xs), w.err);
             CUDA_TRY(cudaGetLastError());
             xop = w.xs;
         } else if (x_dtype == MVLLM_DTYPE_BF16) {
@@ -529,9 +692,35 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             tpl, TableSet<kTmapsPerExpert>{{tb.g, tb.u, tb.d, tb.gs, tb.us, tb.ds}}, nb, w.tmaps,
             w.tmaps_dirty);
         CUDA_TRY(cudaGetLastError());
-        CUtensorMap tok1{}, tok2{};
+        CUtensorMap tok1{}, tok2{}, tsc1{}, tsc2{};
         TcArgs t1{};
-        if (tc_min) {
+        const int kind = mode_kind(mode), nterm = mx ? mode_nterm(mode) : 0;
+        if (tc_min && mx) {
+            TmapSet<kMxMapCount> mtpl;
+            if (int rc = make_mx_templates(&mtpl, kind, D, I, w.y))
+                return rc;
+            const int nmx = nb * kMxMapCount;
+            build_tmaps_kernel<kMxMapCount><<<(nmx + 127) / 128, 128, 0, st>>>(
+                mtpl, TableSet<kMxMapCount>{{tb.g, tb.u, tb.d, tb.gs, tb.us, tb.ds}}, nb,
+                w.mx_tmaps, w.tmaps_dirty);
+            CUDA_TRY(cudaGetLastError());
+            // x as block-scaled terms, then the maps of both phases' operands.
+            if (int rc = launch_terms(mode, xop, x_rows, D, w.xq, w.xc, st, sms))
+                return rc;
+            const uint64_t xb = kind == kMxF4 ? D / 2 : D, hb = kind == kMxF4 ? I / 2 : I;
+            if (int rc = encode_planes(&tok1, w.xq, xb, x_rows, nterm, 128,
+                                       CU_TENSOR_MAP_SWIZZLE_128B))
+                return rc;
+            if (int rc = encode_planes(&tsc1, w.xc, D / 32, x_rows, nterm, 16,
+                                       CU_TENSOR_MAP_SWIZZLE_NONE))
+                return rc;
+            if (int rc = encode_planes(&tok2, w.hq, hb, w.h_rows, nterm, 128,
+                                       CU_TENSOR_MAP_SWIZZLE_128B))
+                return rc;
+            if (int rc = encode_planes(&tsc2, w.hc, I / 32, w.h_rows, nterm, 16,
+                                       CU_TENSOR_MAP_SWIZZLE_NONE))
+                return rc;
+        } else if (tc_min) {
             TmapSet<kTcMapCount> ttpl;
             if (int rc = make_tc_templates(&ttpl, fmt, D, I, w.y))
                 return rc;
@@ -544,6 +733,8 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
                 return rc;
             if (int rc = make_tok_map(&tok2, w.h, I, w.h_rows))
                 return rc;
+        }
+        if (tc_min) {
             t1.tmaps = w.tc_tmaps;
             t1.tmaps_dirty = w.tmaps_dirty;
             t1.s0 = tb.gs, t1.s1 = tb.us;
@@ -568,7 +759,15 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
         if (tc_min) {
             TcArgs s1 = t1;
             s1.item_off = w.soff1;
-            if ((rc = launch_tc<1>(fmt, t1, s1, tok1, st, sms)))
+            if (mx)
+                rc = launch_mx<1>(mode, MxArgs{t1, w.mx_tmaps}, MxArgs{s1, w.mx_tmaps}, tok1, tsc1,
+                                  st, sms);
+            else
+                rc = launch_tc<1>(fmt, t1, s1, tok1, st, sms);
+            if (rc)
+                return rc;
+            // h (every phase-1 row, f16) as terms for the block-scaled phase 2.
+            if (mx && (rc = launch_terms(mode, w.h, w.h_rows, I, w.hq, w.hc, st, sms)))
                 return rc;
         }
         prof_mark(st, kPhExpert1);
@@ -588,7 +787,12 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             t2.K = I, t2.O = D, t2.out = w.y;
             TcArgs s2 = t2;
             s2.item_off = w.soff2;
-            if ((rc = launch_tc<2>(fmt, t2, s2, tok2, st, sms)))
+            if (mx)
+                rc = launch_mx<2>(mode, MxArgs{t2, w.mx_tmaps}, MxArgs{s2, w.mx_tmaps}, tok2, tsc2,
+                                  st, sms);
+            else
+                rc = launch_tc<2>(fmt, t2, s2, tok2, st, sms);
+            if (rc)
                 return rc;
         }
         prof_mark(st, kPhExpert2);
@@ -812,6 +1016,33 @@ void mvllm_moe_shutdown(void) {
 }
 
 int mvllm_moe_available(void) { return ctx().inited ? 1 : 0; }
+
+int mvllm_moe_set_prefill_mode(int mode) {
+    if (mode < -1 || mode > MVLLM_PREFILL_MXF8_X2)
+        return fail(MVLLM_ERR_INVALID, "set_prefill_mode: unknown mode %d", mode);
+    g_prefill_mode.store(mode);
+    return MVLLM_OK;
+}
+
+int mvllm_moe_get_prefill_mode(void) { return prefill_mode(); }
+
+int mvllm_mx_terms_dev(void *stream, int mode, const void *src, int rows, int K, void *planes,
+                       void *codes) {
+    if (mode <= MVLLM_PREFILL_F16 || mode > MVLLM_PREFILL_MXF8_X2 || !src || !planes || !codes ||
+        rows < 1 || K < 32 || K % 32 != 0 || (reinterpret_cast<uintptr_t>(src) & 15u) ||
+        (reinterpret_cast<uintptr_t>(planes) & 7u))
+        return fail(MVLLM_ERR_INVALID, "mx_terms_dev: invalid arguments");
+    Context &c = ctx();
+    int sms;
+    {
+        std::lock_guard<std::mutex> lk(c.mu);
+        if (int rc = ensure_current(c))
+            return rc;
+        sms = c.sms;
+    }
+    return launch_terms(mode, src, rows, K, static_cast<uint8_t *>(planes),
+                        static_cast<uint8_t *>(codes), static_cast<cudaStream_t>(stream), sms);
+}
 
 const char *mvllm_moe_backend_name(void) { return "cuda-sm100a"; }
 
@@ -1623,11 +1854,11 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
         if (x_dtype == MVLLM_DTYPE_BF16)
             stage_rows_f16x8_kernel<__nv_bfloat16><<<vblocks, 256, 0, st>>>(
                 static_cast<const __nv_bfloat16 *>(x), l.rows, l.n_rows, 0, D, fmt,
-                static_cast<__half *>(l.run.xs));
+                static_cast<__half *>(l.run.xs), l.run.err);
         else
             stage_rows_f16x8_kernel<float><<<vblocks, 256, 0, st>>>(
                 static_cast<const float *>(x), l.rows, l.n_rows, 0, D, fmt,
-                static_cast<__half *>(l.run.xs));
+                static_cast<__half *>(l.run.xs), l.run.err);
     } else {
         if (x_dtype == MVLLM_DTYPE_BF16)
             stage_rows_kernel<__nv_bfloat16, float><<<gblocks, 256, 0, st>>>(

@@ -385,6 +385,130 @@ __device__ __forceinline__ void tc_dequant_row(const uint4 &w0, const uint4 &w1,
     }
 }
 
+// Epilogue warps (quadrant = warp % 4, chunk half = warp / 4): per item,
+// wait for the accumulator, read it (tcgen05.ld), release it, and write
+// phase 1's activations (f16, stage_pos order) or phase 2's rows (f32).  The
+// MMA issuer and this loop walk the same item sequence, so both keep the
+// accumulator-half state (TcAccState) identically.
+template <int FMT, int PHASE, bool PAIR>
+__device__ __forceinline__ void tc_epilogue(const TcArgs &p, const TcItemTab &tab, int unit,
+                                            int nunits, int total, uint32_t tmem, uint32_t rank,
+                                            uint64_t *acc_full, uint64_t *acc_empty, int warp,
+                                            int lane) {
+    using C = TcCfg<PAIR>;
+    const int q = warp & 3, whalf = warp >> 2;
+    constexpr int CH_STEP = 32 * (C::EPI_WARPS / 4);
+    const float ia = 1.f / p.act_a, ib = 1.f / p.act_b; // SiTU's divisions, once
+    const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
+    TcAccState acc;
+    bool ok = true;
+    for (int i = unit; ok && i < total; i += nunits) {
+        TcItem it;
+        tc_item<PHASE, PAIR>(p, tab, i, it);
+        const int b = acc.take(it.nmma > C::ACC_HALF);
+        bool got = true;
+        if (b != 1)
+            got = mbar_wait(&acc_full[0], acc.use[0] & 1u, p.err);
+        if (got && b != 0)
+            got = mbar_wait(&acc_full[1], acc.use[1] & 1u, p.err);
+        if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+        }
+        tc_fence_after();
+        const int orow = __ldg(p.orow + it.e) + it.t0;
+        const uint32_t accb =
+            tmem + lane_addr + (b == 1 ? static_cast<uint32_t>(C::ACC_HALF) : 0u);
+        // The accumulator is released as soon as it has been read, so the
+        // next tile's MMAs need not wait for the global stores: phase 1
+        // keeps every chunk's activations in registers (two tokens per
+        // word) and stores them after the release; phase 2 stores the rows
+        // of all chunks but the last as they are read, and the last after
+        // the release.
+        constexpr int MAXCH = (C::NT + CH_STEP - 1) / CH_STEP;
+        uint32_t hpk[PHASE == 1 ? MAXCH * 8 : 1];
+        uint32_t v[32];
+        int nch = 0;
+        const bool gate = lane < 16;
+#pragma unroll
+        for (int j = 0; j < MAXCH; ++j) {
+            const int ch = 32 * whalf + j * CH_STEP;
+            if (ch >= it.n)
+                break;
+            tc_ld32(accb + ch, v);
+            tc_wait_ld();
+            ++nch;
+            if (PHASE == 1) {
+#pragma unroll
+                for (int t = 0; t < 16; ++t) {
+                    const float mine_lo = __uint_as_float(v[t]);
+                    const float mine_hi = __uint_as_float(v[16 + t]);
+                    const float other =
+                        __shfl_xor_sync(0xffffffffu, gate ? mine_hi : mine_lo, 16);
+                    const float g = gate ? mine_lo : other;
+                    const float u = gate ? other : mine_hi;
+                    const float hv = apply_act_fast(g, u, p.act, p.act_a, p.act_b, ia, ib);
+                    if (beyond_f16(hv))
+                        set_error(p.err, MVLLM_ERR_ACT_RANGE);
+                    const uint32_t hb = __half_as_ushort(__float2half_rn(hv));
+                    if (t & 1)
+                        hpk[j * 8 + (t >> 1)] |= hb << 16;
+                    else
+                        hpk[j * 8 + (t >> 1)] = hb;
+                }
+            } else if (ch + CH_STEP < it.n) {
+                float *yp = static_cast<float *>(p.out);
+                const int col = it.c0 + static_cast<int>(rank) * 128 + 32 * q + lane;
+#pragma unroll
+                for (int t = 0; t < 32; ++t)
+                    if (ch + t < it.n)
+                        yp[static_cast<size_t>(orow + ch + t) * p.O + col] =
+                            __uint_as_float(v[t]);
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+            for (int h = 0; h < 2; ++h) {
+                if (b == 1 - h)
+                    continue;
+                if (PAIR)
+                    mbar_arrive_cluster(cluster_addr(&acc_empty[h], 0));
+                else
+                    mbar_arrive(&acc_empty[h]);
+            }
+        }
+        if (PHASE == 1) {
+            const int col = it.c0 + static_cast<int>(rank) * 64 + 16 * q + (lane & 15);
+            __half *hp = static_cast<__half *>(p.out);
+#pragma unroll
+            for (int j = 0; j < MAXCH; ++j) {
+                if (j >= nch)
+                    break;
+                const int tb = 32 * whalf + j * CH_STEP + (gate ? 0 : 16);
+#pragma unroll
+                for (int t = 0; t < 16; ++t)
+                    if (tb + t < it.n)
+                        hp[static_cast<size_t>(orow + tb + t) * p.O + stage_pos(col, FMT)] =
+                            __ushort_as_half(static_cast<unsigned short>(
+                                hpk[j * 8 + (t >> 1)] >> (16 * (t & 1))));
+            }
+        } else if (nch > 0) {
+            const int ch = 32 * whalf + (nch - 1) * CH_STEP;
+            float *yp = static_cast<float *>(p.out);
+            const int col = it.c0 + static_cast<int>(rank) * 128 + 32 * q + lane;
+#pragma unroll
+            for (int t = 0; t < 32; ++t)
+                if (ch + t < it.n)
+                    yp[static_cast<size_t>(orow + ch + t) * p.O + col] = __uint_as_float(v[t]);
+        }
+        if (b != 1)
+            ++acc.use[0];
+        if (b != 0)
+            ++acc.use[1];
+    }
+}
+
 template <int FMT, int PHASE, bool PAIR>
 __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM)
     tc_ffn_kernel(const TcArgs p, const __grid_constant__ CUtensorMap tok_map) {
@@ -759,116 +883,8 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
             }
         }
     } else if (warp < C::EPI_WARPS) {
-        // ------------------------------------------------------------- epilogue
-        const int q = warp & 3, whalf = warp >> 2;
-        constexpr int CH_STEP = 32 * (C::EPI_WARPS / 4);
-        const float ia = 1.f / p.act_a, ib = 1.f / p.act_b; // SiTU's divisions, once
-        const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
-        TcAccState acc;
-        bool ok = true;
-        for (int i = unit; ok && i < total; i += nunits) {
-            TcItem it;
-            tc_item<PHASE, PAIR>(p, tab, i, it);
-            const int b = acc.take(it.nmma > C::ACC_HALF);
-            bool got = true;
-            if (b != 1)
-                got = mbar_wait(&acc_full[0], acc.use[0] & 1u, p.err);
-            if (got && b != 0)
-                got = mbar_wait(&acc_full[1], acc.use[1] & 1u, p.err);
-            if (!__all_sync(0xffffffffu, got)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const int orow = __ldg(p.orow + it.e) + it.t0;
-            const uint32_t accb =
-                tmem + lane_addr + (b == 1 ? static_cast<uint32_t>(C::ACC_HALF) : 0u);
-            // The accumulator is released as soon as it has been read, so the
-            // next tile's MMAs need not wait for the global stores: phase 1
-            // keeps every chunk's activations in registers (two tokens per
-            // word) and stores them after the release; phase 2 stores the rows
-            // of all chunks but the last as they are read, and the last after
-            // the release.
-            constexpr int MAXCH = (C::NT + CH_STEP - 1) / CH_STEP;
-            uint32_t hpk[PHASE == 1 ? MAXCH * 8 : 1];
-            uint32_t v[32];
-            int nch = 0;
-            const bool gate = lane < 16;
-#pragma unroll
-            for (int j = 0; j < MAXCH; ++j) {
-                const int ch = 32 * whalf + j * CH_STEP;
-                if (ch >= it.n)
-                    break;
-                tc_ld32(accb + ch, v);
-                tc_wait_ld();
-                ++nch;
-                if (PHASE == 1) {
-#pragma unroll
-                    for (int t = 0; t < 16; ++t) {
-                        const float mine_lo = __uint_as_float(v[t]);
-                        const float mine_hi = __uint_as_float(v[16 + t]);
-                        const float other =
-                            __shfl_xor_sync(0xffffffffu, gate ? mine_hi : mine_lo, 16);
-                        const float g = gate ? mine_lo : other;
-                        const float u = gate ? other : mine_hi;
-                        const uint32_t hb = __half_as_ushort(__float2half_rn(
-                            apply_act_fast(g, u, p.act, p.act_a, p.act_b, ia, ib)));
-                        if (t & 1)
-                            hpk[j * 8 + (t >> 1)] |= hb << 16;
-                        else
-                            hpk[j * 8 + (t >> 1)] = hb;
-                    }
-                } else if (ch + CH_STEP < it.n) {
-                    float *yp = static_cast<float *>(p.out);
-                    const int col = it.c0 + static_cast<int>(rank) * 128 + 32 * q + lane;
-#pragma unroll
-                    for (int t = 0; t < 32; ++t)
-                        if (ch + t < it.n)
-                            yp[static_cast<size_t>(orow + ch + t) * p.O + col] =
-                                __uint_as_float(v[t]);
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                for (int h = 0; h < 2; ++h) {
-                    if (b == 1 - h)
-                        continue;
-                    if (PAIR)
-                        mbar_arrive_cluster(cluster_addr(&acc_empty[h], 0));
-                    else
-                        mbar_arrive(&acc_empty[h]);
-                }
-            }
-            if (PHASE == 1) {
-                const int col = it.c0 + static_cast<int>(rank) * 64 + 16 * q + (lane & 15);
-                __half *hp = static_cast<__half *>(p.out);
-#pragma unroll
-                for (int j = 0; j < MAXCH; ++j) {
-                    if (j >= nch)
-                        break;
-                    const int tb = 32 * whalf + j * CH_STEP + (gate ? 0 : 16);
-#pragma unroll
-                    for (int t = 0; t < 16; ++t)
-                        if (tb + t < it.n)
-                            hp[static_cast<size_t>(orow + tb + t) * p.O + stage_pos(col, FMT)] =
-                                __ushort_as_half(static_cast<unsigned short>(
-                                    hpk[j * 8 + (t >> 1)] >> (16 * (t & 1))));
-                }
-            } else if (nch > 0) {
-                const int ch = 32 * whalf + (nch - 1) * CH_STEP;
-                float *yp = static_cast<float *>(p.out);
-                const int col = it.c0 + static_cast<int>(rank) * 128 + 32 * q + lane;
-#pragma unroll
-                for (int t = 0; t < 32; ++t)
-                    if (ch + t < it.n)
-                        yp[static_cast<size_t>(orow + ch + t) * p.O + col] = __uint_as_float(v[t]);
-            }
-            if (b != 1)
-                ++acc.use[0];
-            if (b != 0)
-                ++acc.use[1];
-        }
+        tc_epilogue<FMT, PHASE, PAIR>(p, tab, unit, nunits, total, tmem, rank, acc_full, acc_empty,
+                                      warp, lane);
     }
 
     tc_fence_before();

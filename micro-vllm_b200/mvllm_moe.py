@@ -22,11 +22,15 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libmvllm_moe.so")
 
 OK, ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_NOT_INIT, ERR_DEVICE, \
-    ERR_WORKSPACE, ERR_RANGE = range(10)
+    ERR_WORKSPACE, ERR_RANGE, ERR_ACT_RANGE = range(11)
 ACT_SILU, ACT_CLAMP_SWIGLU, ACT_SITU = 0, 1, 2
 FMT_F32, FMT_INT4_G64, FMT_MXFP4, FMT_INT8_ROW, FMT_FP8_B128 = 0, 4, 7, 8, 9
 DTYPE_F32, DTYPE_BF16 = 0, 1
 SCORE_SIGMOID, SCORE_SQRT_SOFTPLUS = 0, 1
+# Tensor-core (prefill) modes for MXFP4 experts (mvllm_moe.h MVLLM_PREFILL_*).
+PREFILL_F16, PREFILL_MXF4_X1, PREFILL_MXF4_X2, PREFILL_MXF4_X3, PREFILL_MXF8_X1, \
+    PREFILL_MXF8_X2 = range(6)
+PREFILL_NAMES = ("f16", "mxf4x1", "mxf4x2", "mxf4x3", "mxf8x1", "mxf8x2")
 
 # Every symbol include/mvllm_moe.h declares (checked by tests/test_abi.py).
 C_SYMBOLS = (
@@ -44,6 +48,7 @@ C_SYMBOLS = (
     "mvllm_moe_epilogue_workspace", "mvllm_moe_epilogue_dev", "mvllm_moe_host_register",
     "mvllm_moe_host_unregister", "mvllm_moe_route_ex_dev", "mvllm_moe_ep_local_ids_dev",
     "mvllm_moe_dense_ffn_workspace", "mvllm_moe_dense_ffn_dev", "mvllm_moe_wait_selftest",
+    "mvllm_moe_set_prefill_mode", "mvllm_moe_get_prefill_mode", "mvllm_mx_terms_dev",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -113,6 +118,9 @@ def lib():
             "mvllm_moe_ep_local_ids_dev": (i, [vp, vp, i, i, i, i, vp, vp, i, vp]),
             "mvllm_moe_dense_ffn_workspace": (sz, [i, i, i]),
             "mvllm_moe_wait_selftest": (i, [vp, vp]),
+            "mvllm_moe_set_prefill_mode": (i, [i]),
+            "mvllm_moe_get_prefill_mode": (i, []),
+            "mvllm_mx_terms_dev": (i, [vp, i, vp, i, i, vp, vp]),
             "mvllm_moe_dense_ffn_dev": (i, [vp, i, i, i, i] + [vp] * 7 + [i, f, f, vp, i, vp,
                                                                          sz]),
         }
@@ -139,6 +147,30 @@ def init(device: int = 0) -> None:
 
 def shutdown() -> None:
     lib().mvllm_moe_shutdown()
+
+
+def set_prefill_mode(mode) -> None:
+    """Tensor-core mode for MXFP4 experts: a PREFILL_* value or its name;
+    -1 (or None) restores the default."""
+    if mode is None:
+        mode = -1
+    if isinstance(mode, str):
+        mode = PREFILL_NAMES.index(mode)
+    _check(lib().mvllm_moe_set_prefill_mode(int(mode)))
+
+
+def get_prefill_mode() -> int:
+    return int(lib().mvllm_moe_get_prefill_mode())
+
+
+def mx_terms_dev(mode, src, planes, codes, stream=None) -> None:
+    """Block-scaled terms of f16 device rows src [rows, K] (mvllm_mx_terms_dev)."""
+    if isinstance(mode, str):
+        mode = PREFILL_NAMES.index(mode)
+    rows, K = src.shape
+    _check(lib().mvllm_mx_terms_dev(_stream(stream), int(mode), C.c_void_p(src.data_ptr()),
+                                    rows, K, C.c_void_p(planes.data_ptr()),
+                                    C.c_void_p(codes.data_ptr())))
 
 
 def available() -> bool:
