@@ -52,6 +52,8 @@ def parse():
                     help="skip the config[3] prefill measurement")
     ap.add_argument("--prefill-steps", type=int, default=10)
     ap.add_argument("--no-ep", action="store_true", help="skip the config[4] expert-parallel leg")
+    ap.add_argument("--no-decode-configs", action="store_true",
+                    help="skip the config[0] and config[2] decode legs")
     ap.add_argument("--ep-steps", type=int, default=20)
     ap.add_argument("--no-dsv4", action="store_true",
                     help="skip the DeepSeek-V4 expert-split (EP2) leg")
@@ -226,6 +228,88 @@ def graph_throughput(moe, torch, wl, steps, warmup):
     ms = a.elapsed_time(b)
     del graph
     return wl.B * reps * N_INPUTS / (ms / 1e3), ms / (reps * N_INPUTS)
+
+
+# --------------------------------------------------- other decode configs --
+def decode_leg(moe, torch, name, D, I, E, K, fmt, act, a, b, batches, router, peak_gbs, seed,
+               reps=320):
+    """A decode config of BASELINE at each batch size through the device
+    layer (mvllm_moe_layer_dev), CUDA-graph replays of 16 routings: tokens/s,
+    ms per step and the HBM fraction of the step (the touched experts' weight
+    bytes + the activation rows in and out, over the step time).  Weights are
+    drawn N(0, 0.02) and packed on the GPU; activations bf16 N(0, 1)."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    gs_ = 64 if fmt == 4 else 32
+    sdt = torch.float32 if fmt == 4 else torch.uint8
+    pack = moe.quantize_int4_g64_dev if fmt == 4 else moe.pack_mxfp4_dev
+    per_expert = 3 * (I * D // 2 + I * D // gs_ * (4 if fmt == 4 else 1))
+    mats = []
+    for e in range(E):
+        m = []
+        for shape in ((I, D), (I, D), (D, I)):
+            w = torch.randn(shape, generator=g, device="cuda").mul_(0.02)
+            pk = torch.empty((shape[0], shape[1] // 2), dtype=torch.uint8, device="cuda")
+            sc = torch.empty((shape[0], shape[1] // gs_), dtype=sdt, device="cuda")
+            pack(w, pk, sc)
+            m.append((pk, sc))
+        mats.append(m)
+    tables = [torch.tensor([mats[e][k % 3][k // 3].data_ptr() for e in range(E)],
+                           dtype=torch.int64, device="cuda") for k in range(6)]
+    res = {}
+    for B in batches:
+        inputs, touched = [], []
+        for _ in range(N_INPUTS):
+            if router == "softmax":  # N(0,1) logits, softmax (temperature 1), top-K renormalised
+                choice = torch.softmax(torch.randn((B, E), generator=g, device="cuda"), dim=1)
+            else:
+                choice = torch.rand((B, E), generator=g, device="cuda")
+            vals, idx = torch.topk(choice, K, dim=1)
+            wt = (vals / vals.sum(1, keepdim=True)).float().contiguous()
+            x = torch.randn((B, D), generator=g, device="cuda").to(torch.bfloat16)
+            inputs.append((idx.int().contiguous(), wt, x))
+            touched.append(len(set(idx.flatten().tolist())))
+        out = torch.zeros((B, D), dtype=torch.float32, device="cuda")
+        ws = torch.empty(moe.layer_workspace_bytes(B, K, E, 0, D, I, fmt), dtype=torch.uint8,
+                         device="cuda")
+
+        def step(i):
+            idx, wt, x = inputs[i % N_INPUTS]
+            moe.layer_dev(B, K, E, 0, D, I, fmt, idx, wt, x, tables, out, act, a, b, ws)
+
+        for i in range(3):
+            step(i)
+        torch.cuda.synchronize()
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(graph, stream=st):
+                for i in range(N_INPUTS):
+                    step(i)
+        torch.cuda.synchronize()
+        n = max(1, reps // N_INPUTS)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (n * N_INPUTS)
+        del graph
+        nbytes = sum(touched) / len(touched) * per_expert + B * D * (2 + 4)
+        res[f"B{B}"] = {"tokens_per_s": B / (ms / 1e3), "ms_per_step": ms,
+                        "us_per_step": ms * 1e3, "experts_touched_mean": sum(touched) / len(touched),
+                        "algorithmic_bytes_per_step": nbytes,
+                        "hbm_gbs": nbytes / (ms / 1e3) / 1e9,
+                        "hbm_frac_of_step": nbytes / (ms / 1e3) / 1e9 / peak_gbs}
+    del mats, tables
+    torch.cuda.empty_cache()
+    return {"workload": name, "expert_bytes": per_expert,
+            "timing": "CUDA-graph replays of 16 routings through mvllm_moe_layer_dev; HBM "
+                      "fraction over the whole step (permutation, gather, plan, maps, both "
+                      "expert phases, combine)", **res}
 
 
 # ------------------------------------------------------------ prefill --
@@ -411,11 +495,56 @@ def epilogue_bench(moe, torch, peak_gbs, reps=200):
             "launches_per_call": 3}
 
 
+PREFILL_MODES = ("f16", "mxf4x1", "mxf4x2", "mxf4x3", "mxf8x1", "mxf8x2")
+# The tensor pipe each mode issues on (kind for mvllm_moe_mma_rate) and its
+# token terms; f16 dequantises the weights and runs kind::f16.
+MODE_PIPE = {"f16": ("f16", 2, 1), "mxf4x1": ("mxf4", 0, 1), "mxf4x2": ("mxf4", 0, 2),
+             "mxf4x3": ("mxf4", 0, 3), "mxf8x1": ("mxf8f6f4", 1, 1),
+             "mxf8x2": ("mxf8f6f4", 1, 2)}
+
+
+def mxfp4_dequant(torch, p, s):
+    """MXFP4 rows (packed e2m1 [O, I/2], ue8m0 [O, I/32]) as f64 values, the
+    reference's decoding (quant.hpp:12-20: code 0 -> +0, 255 -> +inf)."""
+    lut = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6],
+                       dtype=torch.float64, device=p.device)
+    O = p.shape[0]
+    v = torch.stack([lut[(p & 15).long()], lut[(p >> 4).long()]], -1).reshape(O, -1)
+    sc = torch.where(s == 0, torch.zeros((), dtype=torch.float64, device=p.device),
+                     torch.exp2(s.double() - 127))
+    return v * sc.repeat_interleave(32, dim=1)
+
+
+def prefill_reference(torch, wl, idx, wt, x, sample):
+    """The layer's output rows for `sample` tokens in f64 (torch on the GPU,
+    weights decoded as the reference decodes them): the yardstick of each
+    tensor-core mode's measured error."""
+    D, I, a, b = CFG["D"], CFG["I"], CFG["act_a"], CFG["act_b"]
+    xs = x[sample].double()
+    ids, ws = idx[sample].long(), wt[sample].double()
+    out = torch.zeros((len(sample), D), dtype=torch.float64, device="cuda")
+    for e in sorted(set(ids.flatten().tolist())):
+        m = (ids == e)
+        rows = m.any(1).nonzero().flatten()
+        w_e = (ws * m).sum(1)[rows]
+        g = xs[rows] @ mxfp4_dequant(torch, wl.gp[e], wl.gs[e]).T
+        u = xs[rows] @ mxfp4_dequant(torch, wl.up[e], wl.us[e]).T
+        h = a * torch.tanh(g / a) * torch.sigmoid(g) * b * torch.tanh(u / b)
+        y = h @ mxfp4_dequant(torch, wl.dp[e], wl.ds[e]).T
+        out[rows] += w_e[:, None] * y
+    return out
+
+
 def prefill_bench(moe, torch, wl, steps, peak_tf, peak_gbs, T=PREFILL_T):
     """Config[3]: 4096 tokens, the 256 routed MXFP4 experts of the decode
     workload (same shape and format), Zipf s=1.1 routing, no shared expert,
     bf16 activations, f32 accumulation.  Large experts run on the tensor-core
-    kernels, the smallest on the decode kernels."""
+    kernels, the smallest on the decode kernels.  Every tensor-core mode is
+    timed and its error measured against an f64 evaluation of the same
+    layer on every token; the headline is the library's default mode
+    (the fastest within the 1e-2 / 2e-2 tolerance).  Tensor fractions are
+    against the tensor pipe's rate measured in this run (mvllm_moe_mma_rate,
+    back-to-back MMAs of the same kind on every SM)."""
     D, I, E, K = CFG["D"], CFG["I"], CFG["E"], CFG["K"]
     g = torch.Generator(device="cuda").manual_seed(4242)
     idx, wt = zipf_routing(torch, T, E, K, g)
@@ -424,44 +553,78 @@ def prefill_bench(moe, torch, wl, steps, peak_tf, peak_gbs, T=PREFILL_T):
     ws = torch.empty(moe.layer_workspace_bytes(T, K, E, 0, D, I, CFG["fmt"]), dtype=torch.uint8,
                      device="cuda")
     cnt = torch.bincount(idx.flatten().long(), minlength=E).cpu()
+    sample = torch.arange(T, device="cuda")
+    ref = prefill_reference(torch, wl, idx, wt, x, sample)
+    pipes = {"mxf4": moe.mma_rate(0, 256, 1), "mxf8f6f4": moe.mma_rate(1, 256, 1),
+             "f16": moe.mma_rate(2, 128, 0)}
 
     def step():
         out.zero_()
         moe.layer_dev(T, K, E, 0, D, I, CFG["fmt"], idx, wt, x, wl.tables, out, CFG["act"],
                       CFG["act_a"], CFG["act_b"], ws)
 
-    for _ in range(3):
-        step()
-    torch.cuda.synchronize()
-    moe.profile_enable(True)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
-        step()
-    b.record()
-    torch.cuda.synchronize()
-    ph = moe.profile_read()
-    moe.profile_enable(False)
-    ms = a.elapsed_time(b) / steps
-    e_ms = (ph["expert_phase1"][0] + ph["expert_phase2"][0]) / steps
     flops = 2.0 * T * K * 3 * D * I
     touched = int((cnt > 0).sum())
     alg_bytes = touched * EXPERT_BYTES + T * D * 2 + T * D * 4
-    tf = flops / (e_ms / 1e3) / 1e12
+    default = moe.PREFILL_NAMES[moe.get_prefill_mode()]
+    modes = {}
+    for mode in PREFILL_MODES:
+        moe.set_prefill_mode(mode)
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        got = out[sample].double()
+        rel = float(torch.linalg.norm(got - ref) / torch.linalg.norm(ref))
+        mabs = float((got - ref).abs().max())
+        moe.profile_enable(True)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        ph = moe.profile_read()
+        moe.profile_enable(False)
+        ms = a.elapsed_time(b) / steps
+        e_ms = (ph["expert_phase1"][0] + ph["expert_phase2"][0]) / steps
+        pipe, _, nterm = MODE_PIPE[mode]
+        tf = flops / (e_ms / 1e3) / 1e12
+        modes[mode] = {
+            "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms,
+            "expert_kernels_ms_per_step": e_ms,
+            "rel_l2": rel, "max_abs": mabs, "within_tolerance": rel <= 1e-2 and mabs <= 2e-2,
+            "achieved_tflops": tf, "pipe": pipe, "token_terms": nterm,
+            "pipe_tflops_issued": tf * nterm, "pipe_peak_tflops": pipes[pipe],
+            "pipe_frac": tf * nterm / pipes[pipe],
+            "hbm_frac": alg_bytes / (ms / 1e3) / 1e9 / peak_gbs,
+            "phases_ms_per_step": {k: v[0] / steps for k, v in ph.items()},
+        }
+    moe.set_prefill_mode(None)
+    best = max((m for m in modes if modes[m]["within_tolerance"]),
+               key=lambda m: modes[m]["tokens_per_s"], default=None)
+    d = modes[default]
     return {
         "workload": f"config[3] MXFP4 prefill: {T} tokens, hidden 7168, inter 2048, {E} experts "
                     "top-8 (Zipf s=1.1 routing), SiTU(4,25), bf16 activations",
-        "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms, "steps": steps,
+        "mode": default, "fastest_mode_within_tolerance": best,
+        "tokens_per_s": d["tokens_per_s"], "ms_per_step": d["ms_per_step"], "steps": steps,
+        "rel_l2": d["rel_l2"], "max_abs": d["max_abs"],
+        "error_sample": f"all {T} tokens, against an f64 evaluation of the layer with the "
+                        "weights decoded as the reference decodes them",
         "expert_rows_per_expert": {"min": int(cnt.min()), "max": int(cnt.max()),
                                    "below_128": int((cnt < 128).sum())},
-        "phases_ms_per_step": {k: v[0] / steps for k, v in ph.items()},
-        "tensor": {"flops_per_step": flops, "achieved_tflops": tf, "peak_tflops": peak_tf,
-                   "frac": tf / peak_tf if peak_tf else None,
-                   "peak_kind": "measured bf16 dense (the kernels run kind::f16 MMAs)",
-                   "kernel_ms_per_step": e_ms},
+        "tensor": {"flops_per_step": flops, "achieved_tflops": d["achieved_tflops"],
+                   "pipe": d["pipe"], "pipe_peak_tflops": d["pipe_peak_tflops"],
+                   "pipe_frac": d["pipe_frac"],
+                   "peak_kind": "measured in this run: back-to-back MMAs of the pipe's kind on "
+                                "every SM (mvllm_moe_mma_rate)",
+                   "kernel_ms_per_step": d["expert_kernels_ms_per_step"],
+                   "bf16_cublas_peak_tflops": peak_tf},
         "hbm": {"algorithmic_bytes_per_step": alg_bytes,
-                "achieved_gbs": alg_bytes / (ms / 1e3) / 1e9, "peak_gbs": peak_gbs,
-                "frac": alg_bytes / (ms / 1e3) / 1e9 / peak_gbs},
+                "achieved_gbs": alg_bytes / (d["ms_per_step"] / 1e3) / 1e9, "peak_gbs": peak_gbs,
+                "frac": alg_bytes / (d["ms_per_step"] / 1e3) / 1e9 / peak_gbs},
+        "pipe_peaks_tflops": pipes,
+        "modes": modes,
     }
 
 
@@ -483,7 +646,7 @@ def ep_routing(torch, name, T, K, seed):
     return zipf_routing(torch, T, EP_E, K, gr, perm=perm)
 
 
-def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
+def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=None, e2e_steps=0):
     """Config[4]: 384 MXFP4 experts sharded over the ranks (expert e on rank
     e % world), top-8; uniform and Zipf s=1.1 routing.  Weights are drawn per
     global expert id, so the model is the same whatever the rank count.
@@ -493,7 +656,11 @@ def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
     layer).  tokens/s = all ranks' tokens / step time (max over ranks).
     Hot experts are replicated on every rank (ep.balance_replicas, at most
     2 per rank) from the loads of a separate calibration draw of the same
-    routing distribution; each rank serves its own tokens' rows for them."""
+    routing distribution; each rank serves its own tokens' rows for them.
+    The uniform run's timed region is sampled by `clk`; its expert kernels'
+    device time (phase events, max over ranks) gives the roofline; with
+    `e2e_steps` the same step also runs from host buffers (pinned x, idx, wt
+    copied in, out copied back inside the timed region)."""
     import ep
     D, I, K = CFG["D"], CFG["I"], CFG["K"]
     u8 = torch.uint8
@@ -513,6 +680,17 @@ def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
                 mats.append((pk, sc))
             wcache[e] = mats
         return wcache[e]
+
+    def max_over_ranks(vals):
+        t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
 
     g = torch.Generator(device="cuda").manual_seed(777)
     x_all = torch.randn((T_all, D), generator=g, device="cuda").to(torch.bfloat16)
@@ -542,31 +720,35 @@ def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
         idx = idx[rank * T_loc:(rank + 1) * T_loc].contiguous()
         wt = wt[rank * T_loc:(rank + 1) * T_loc].contiguous()
 
-        def step():
-            out.zero_()
+        def step(xx=x, ii=idx, ww=wt, oo=out):
+            oo.zero_()
             if world > 1:
-                return layer.forward(x, idx, wt, out, dist)
-            ep.emulate_step([layer], [x], [idx], [wt], [out], torch)
+                return layer.forward(xx, ii, ww, oo, dist)
+            ep.emulate_step([layer], [xx], [ii], [ww], [oo], torch)
             return None
 
-        for _ in range(2):
+        for _ in range(max(warmup, 2)):
             step()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+        barrier()
+        moe.profile_enable(True)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sampler = clk if (clk is not None and name == "uniform") else None
+        if sampler:
+            sampler.__enter__()
         a.record()
         info = None
         for _ in range(steps):
             info = step()
         b.record()
-        torch.cuda.synchronize()
-        ms = a.elapsed_time(b) / steps
-        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        barrier()
+        if sampler:
+            sampler.__exit__(None, None, None)
+        ph = moe.profile_read()
+        moe.profile_enable(False)
+        ms, e_ms = max_over_ranks([a.elapsed_time(b) / steps,
+                                   (ph["expert_phase1"][0] + ph["expert_phase2"][0]) / steps])
         res[name] = {"tokens_per_s": T_all / (ms / 1e3), "ms_per_step": ms, "steps": steps,
+                     "expert_kernels_ms_per_step_max_over_ranks": e_ms,
                      "replicated_experts": len(rep), "experts_per_rank": len(mine)}
         if world > 1:
             # One more step with phase events (not part of the timed steps).
@@ -574,12 +756,45 @@ def ep_bench(moe, torch, dist, rank, world, steps, weak=False):
             out.zero_()
             layer.forward(x, idx, wt, out, dist, timing=tm)
             keys = sorted(tm)
-            tt = torch.tensor([tm[k] for k in keys], dtype=torch.float64, device="cuda")
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            res[name]["phase_ms_max_over_ranks"] = dict(zip(keys, tt.tolist()))
+            res[name]["phase_ms_max_over_ranks"] = dict(zip(keys, max_over_ranks(
+                [tm[k] for k in keys])))
         if info:
             res[name]["rank0_sent_rows"] = info["sent_rows"]
             res[name]["rank0_received_rows"] = info["received_rows"]
+        if e2e_steps and name == "uniform":
+            # The same step from host buffers: x / idx / wt in pinned host
+            # memory copied in, out copied back, inside the timed region.
+            xh = x.cpu().pin_memory()
+            ih = idx.cpu().pin_memory()
+            wh = wt.cpu().pin_memory()
+            oh = torch.empty((T_loc, D), dtype=torch.float32).pin_memory()
+            xd, idd, wd = torch.empty_like(x), torch.empty_like(idx), torch.empty_like(wt)
+
+            def e2e_step():
+                xd.copy_(xh, non_blocking=True)
+                idd.copy_(ih, non_blocking=True)
+                wd.copy_(wh, non_blocking=True)
+                step(xd, idd, wd, out)
+                oh.copy_(out, non_blocking=True)
+
+            for _ in range(2):
+                e2e_step()
+            barrier()
+            a2, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            a2.record()
+            for _ in range(e2e_steps):
+                e2e_step()
+            b2.record()
+            barrier()
+            wall = time.perf_counter() - t0
+            ems, wall = max_over_ranks([a2.elapsed_time(b2) / e2e_steps, wall / e2e_steps])
+            res["e2e"] = {"value": T_all / (ems / 1e3), "unit": "tokens/s",
+                          "ms_per_step": ems, "host_wall_ms_per_step": wall * 1e3,
+                          "h2d_bytes_per_step": T_all * (D * 2 + K * 8),
+                          "d2h_bytes_per_step": T_all * D * 4,
+                          "api": "EPLayer.forward over the library's device entries (one rank: "
+                                 "the single-GPU layer), host buffers pinned"}
         del layer, ops, tabs, mats
     wcache.clear()
     torch.cuda.empty_cache()
@@ -903,7 +1118,23 @@ def main():
                                                               CFG["fmt"]),
                                     dtype=torch.uint8, device="cuda")
             tps, mstep = graph_throughput(moe, torch, wb, 320, 32)
-            sweep[f"B{bb}"] = {"tokens_per_s": tps * world, "ms_per_step": mstep}
+            touched = [len(set(i.flatten().tolist())) + CFG["n_shared"] for (i, _, _) in wb.inputs]
+            nb = sum(touched) / len(touched) * EXPERT_BYTES + bb * CFG["D"] * 6
+            sweep[f"B{bb}"] = {"tokens_per_s": tps * world, "ms_per_step": mstep,
+                               "algorithmic_bytes_per_step": nb,
+                               "hbm_gbs": nb / (mstep / 1e3) / 1e9,
+                               "hbm_frac_of_step": nb / (mstep / 1e3) / 1e9 / peak}
+
+    # config[2] (GLM-style int4-g64 decode) and config[0] (the reference's
+    # CPU-runnable case) at N = 1
+    glm = cfg0 = None
+    if world == 1 and not args.no_decode_configs:
+        glm = decode_leg(moe, torch, "config[2] int4-g64 decode: hidden 6144, inter 1536, 160 "
+                         "experts top-8, clamped SwiGLU (7), softmax router, bf16 activations",
+                         6144, 1536, 160, 8, 4, 1, 7.0, 0.0, (1, 16, 64), "softmax", peak, 2202)
+        cfg0 = decode_leg(moe, torch, "config[0] int4-g64: hidden 1024, inter 512, 16 experts "
+                          "top-4, 4 tokens, clamped SwiGLU (7), softmax router",
+                          1024, 512, 16, 4, 4, 1, 7.0, 0.0, (4,), "softmax", peak, 2200)
 
     # config[4] expert-parallel layer (all ranks together)
     ep_res = None
@@ -980,6 +1211,8 @@ def main():
             "expert_tier": tier,
             "epilogue": epilogue,
             "expert_parallel": ep_res,
+            "config2_glm_int4_decode": glm,
+            "config0_small_int4": cfg0,
             "dsv4_expert_split": dsv4_res,
         }
         if prefill and cpu and cpu.get("value"):

@@ -65,6 +65,7 @@ struct PlanArgs {
     // at most tc_small rows tc_sblocks{1,2} single-CTA items (soff1/soff2).
     // tc_min <= 0 disables the path.
     int tc_min, tc_small, tc_blocks1, tc_blocks2, tc_sblocks1, tc_sblocks2;
+    int tc_shift; // pair token tiles of 2^tc_shift rows
     int *toff1, *toff2, *soff1, *soff2;
 };
 
@@ -100,9 +101,8 @@ __global__ void plan_kernel(const PlanArgs a) {
             }
             c = ok ? n : 0;
             if (a.tc_min > 0 && c >= a.tc_min) {
-                const int f = c >> 8, r = c & 255;
-                const int npair = f + (r > a.tc_small ? 1 : 0);
-                const int nsolo = (r > 0 && r <= a.tc_small) ? 1 : 0;
+                int npair, nsolo;
+                tc_tiles(c, a.tc_small, a.tc_shift, npair, nsolo);
                 j1 = a.tc_blocks1 * npair;
                 j2 = a.tc_blocks2 * npair;
                 k1 = a.tc_sblocks1 * nsolo;

@@ -46,6 +46,17 @@ __device__ __forceinline__ bool beyond_f16(float v) {
     return a >= 65520.f && a <= 3.402823466e38f;
 }
 
+// Token tiles of an expert with c rows: full tiles of 2^tshift rows (256
+// for tc_ffn's pairs, 128 for the block-scaled kernel's) and the rest; the
+// rest runs on single CTAs when it has at most kTcSoloMax rows (small_max),
+// else as one more (narrower) pair tile.
+__host__ __device__ __forceinline__ void tc_tiles(int c, int small_max, int tshift, int &npair,
+                                                  int &nsolo) {
+    const int f = c >> tshift, r = c & ((1 << tshift) - 1);
+    npair = f + (r > small_max ? 1 : 0);
+    nsolo = (r > 0 && r <= small_max) ? 1 : 0;
+}
+
 // Largest e with off[e] <= i, for off non-decreasing and off[nb] > i.
 __device__ __forceinline__ int find_owner(const int *off, int nb, int i) {
     int lo = 0, hi = nb;

@@ -647,7 +647,9 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     pa.xoff = xoff, pa.x_rows = x_rows, pa.err = w.err;
     pa.align_mask = fast ? ((mx && mode_kind(mode) == kMxF8) ? 31 : 15) : 0;
     pa.tc_min = tc_min;
+    // 256-row pair tiles, rests of at most kTcSoloMax rows on single CTAs.
     pa.tc_small = getenv("MVLLM_TC_NO_SOLO") ? 0 : kTcSoloMax;
+    pa.tc_shift = 8;
     pa.tc_blocks1 = I / tc_cols_per_item<1, true>();
     pa.tc_blocks2 = D / tc_cols_per_item<2, true>();
     pa.tc_sblocks1 = I / tc_cols_per_item<1, false>();
@@ -740,6 +742,7 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             t1.s0 = tb.gs, t1.s1 = tb.us;
             t1.xrow = xoff, t1.orow = w.base, t1.cnt = w.cnt, t1.item_off = w.toff1, t1.nb = nb;
             t1.small_max = pa.tc_small; // the plan's split of each expert's tiles
+            t1.tshift = pa.tc_shift;
             t1.K = D, t1.O = I, t1.out = w.h;
             t1.act = act, t1.act_a = act_a, t1.act_b = act_b, t1.err = w.err;
         }
@@ -963,6 +966,52 @@ struct Resolver {
 } // namespace
 
 // =================================================================== C ABI ==
+namespace {
+template <int KIND, bool PAIR> int mma_rate_t(int n, int iters, int sms, double *tflops) {
+    auto kern = mma_rate_kernel<KIND, PAIR>;
+    // 120 KB of (unused) dynamic shared memory keeps one CTA per SM.
+    const int pad = 120 * 1024;
+    CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pad));
+    int *err = nullptr;
+    CUDA_TRY(cudaMalloc(&err, sizeof(int)));
+    CUDA_TRY(cudaMemset(err, 0, sizeof(int)));
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(128);
+    cfg.gridDim = dim3(PAIR ? (sms & ~1) : sms);
+    cfg.dynamicSmemBytes = pad;
+    cudaLaunchAttribute at[1];
+    if (PAIR) {
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+    }
+    cudaEvent_t e0, e1;
+    CUDA_TRY(cudaEventCreate(&e0));
+    CUDA_TRY(cudaEventCreate(&e1));
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, n, std::max(16, iters / 10), err)); // warm
+    CUDA_TRY(cudaEventRecord(e0));
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, n, iters, err));
+    CUDA_TRY(cudaEventRecord(e1));
+    CUDA_TRY(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    CUDA_TRY(cudaEventElapsedTime(&ms, e0, e1));
+    int herr = 0;
+    CUDA_TRY(cudaMemcpy(&herr, err, sizeof(int), cudaMemcpyDeviceToHost));
+    cudaFree(err);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (herr)
+        return fail(herr, "mma_rate: device error %d", herr);
+    const double kstep = KIND == 0 ? 64 : KIND == 1 ? 32 : 16;
+    const double units = PAIR ? (sms & ~1) / 2 : sms;
+    *tflops = 2.0 * (PAIR ? 256 : 128) * n * kstep * iters * units / (ms * 1e-3) / 1e12;
+    return MVLLM_OK;
+}
+} // namespace
+
 extern "C" {
 
 int mvllm_moe_init(int device) {
@@ -1025,6 +1074,24 @@ int mvllm_moe_set_prefill_mode(int mode) {
 }
 
 int mvllm_moe_get_prefill_mode(void) { return prefill_mode(); }
+
+
+int mvllm_moe_mma_rate(int kind, int n, int pair, int iters, double *tflops) {
+    if (kind < 0 || kind > 2 || n < 16 || n > 256 || n % 16 || iters < 1 || !tflops ||
+        (kind == 2 && pair))
+        return fail(MVLLM_ERR_INVALID, "mma_rate: invalid arguments");
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (int rc = ensure_current(c))
+        return rc;
+    if (kind == 0)
+        return pair ? mma_rate_t<0, true>(n, iters, c.sms, tflops)
+                    : mma_rate_t<0, false>(n, iters, c.sms, tflops);
+    if (kind == 1)
+        return pair ? mma_rate_t<1, true>(n, iters, c.sms, tflops)
+                    : mma_rate_t<1, false>(n, iters, c.sms, tflops);
+    return mma_rate_t<2, false>(n, iters, c.sms, tflops);
+}
 
 int mvllm_mx_terms_dev(void *stream, int mode, const void *src, int rows, int K, void *planes,
                        void *codes) {

@@ -107,6 +107,7 @@ struct TcArgs {
     const int *cnt;           // per expert: rows on this path (0 = decode path)
     const int *item_off;      // [nb + 1] item prefix of this list
     int small_max;            // rest tiles of at most this many rows are single-CTA items
+    int tshift;               // pair token tiles are 2^tshift rows (the plan's split)
     int nb;
     int K, O;                 // reduction length, output width (I or D)
     void *out;                // phase 1: f16 h [rows, I]; phase 2: f32 y [rows, D]
@@ -145,14 +146,6 @@ template <int PHASE, bool PAIR> __host__ __device__ constexpr int tc_cols_per_it
     return (PHASE == 1 ? 64 : 128) * (PAIR ? 2 : 1);
 }
 
-// Token tiles of an expert with c rows: full 256-row tiles and the rest; the
-// rest runs on single CTAs when it has at most kTcSoloMax rows (small_max),
-// else as one more (narrower) pair tile.
-__host__ __device__ __forceinline__ void tc_tiles(int c, int small_max, int &npair, int &nsolo) {
-    const int f = c >> 8, r = c & 255;
-    npair = f + (r > small_max ? 1 : 0);
-    nsolo = (r > 0 && r <= small_max) ? 1 : 0;
-}
 
 // k-blocks per 16-byte scale window of a row: 8 for MXFP4 (two ue8m0 bytes per
 // k-block), 4 for int4-g64 (one f32 per k-block).
@@ -336,12 +329,12 @@ __device__ __forceinline__ void tc_item(const TcArgs &p, const TcItemTab &tab, i
     const int local = i - tab.off[e];
     const int c = tab.cnt[e];
     int npair, nsolo;
-    tc_tiles(c, p.small_max, npair, nsolo);
+    tc_tiles(c, p.small_max, p.tshift, npair, nsolo);
     const int ntt = PAIR ? npair : 1;
     const int wg = local / ntt, tt = local - wg * ntt;
     it.e = e;
-    it.t0 = PAIR ? tt * 256 : (c >> 8) * 256;
-    it.n = min(C::NT, c - it.t0);
+    it.t0 = PAIR ? tt << p.tshift : (c >> p.tshift) << p.tshift;
+    it.n = min(PAIR ? (1 << p.tshift) : C::NT, c - it.t0);
     it.nmma = (it.n + C::NALIGN - 1) & ~(C::NALIGN - 1);
     it.c0 = wg * tc_cols_per_item<PHASE, PAIR>();
 }
@@ -390,7 +383,12 @@ __device__ __forceinline__ void tc_dequant_row(const uint4 &w0, const uint4 &w1,
 // phase 1's activations (f16, stage_pos order) or phase 2's rows (f32).  The
 // MMA issuer and this loop walk the same item sequence, so both keep the
 // accumulator-half state (TcAccState) identically.
-template <int FMT, int PHASE, bool PAIR>
+// NSUM > 1 (the block-scaled kernel's single-CTA form): the accumulator of a
+// tile holds NSUM column groups SUM_STRIDE apart, one per token term, and a
+// token's value is their sum; ACC_STRIDE is the column offset of the second
+// accumulator buffer.  With the defaults the layout is tc_ffn's.
+template <int FMT, int PHASE, bool PAIR, int NSUM = 1, int SUM_STRIDE = 0,
+          int ACC_STRIDE = TcCfg<PAIR>::ACC_HALF, int MAXN = TcCfg<PAIR>::NT>
 __device__ __forceinline__ void tc_epilogue(const TcArgs &p, const TcItemTab &tab, int unit,
                                             int nunits, int total, uint32_t tmem, uint32_t rank,
                                             uint64_t *acc_full, uint64_t *acc_empty, int warp,
@@ -405,7 +403,7 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs &p, const TcItemTab &ta
     for (int i = unit; ok && i < total; i += nunits) {
         TcItem it;
         tc_item<PHASE, PAIR>(p, tab, i, it);
-        const int b = acc.take(it.nmma > C::ACC_HALF);
+        const int b = acc.take(NSUM == 1 && it.nmma > C::ACC_HALF);
         bool got = true;
         if (b != 1)
             got = mbar_wait(&acc_full[0], acc.use[0] & 1u, p.err);
@@ -417,15 +415,14 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs &p, const TcItemTab &ta
         }
         tc_fence_after();
         const int orow = __ldg(p.orow + it.e) + it.t0;
-        const uint32_t accb =
-            tmem + lane_addr + (b == 1 ? static_cast<uint32_t>(C::ACC_HALF) : 0u);
+        const uint32_t accb = tmem + lane_addr + (b == 1 ? static_cast<uint32_t>(ACC_STRIDE) : 0u);
         // The accumulator is released as soon as it has been read, so the
         // next tile's MMAs need not wait for the global stores: phase 1
         // keeps every chunk's activations in registers (two tokens per
         // word) and stores them after the release; phase 2 stores the rows
         // of all chunks but the last as they are read, and the last after
         // the release.
-        constexpr int MAXCH = (C::NT + CH_STEP - 1) / CH_STEP;
+        constexpr int MAXCH = (MAXN + CH_STEP - 1) / CH_STEP;
         uint32_t hpk[PHASE == 1 ? MAXCH * 8 : 1];
         uint32_t v[32];
         int nch = 0;
@@ -436,6 +433,17 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs &p, const TcItemTab &ta
             if (ch >= it.n)
                 break;
             tc_ld32(accb + ch, v);
+            if (NSUM > 1) {
+                uint32_t w[32];
+#pragma unroll
+                for (int t = 1; t < NSUM; ++t) {
+                    tc_ld32(accb + ch + t * SUM_STRIDE, w);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int k = 0; k < 32; ++k)
+                        v[k] = __float_as_uint(__uint_as_float(v[k]) + __uint_as_float(w[k]));
+                }
+            }
             tc_wait_ld();
             ++nch;
             if (PHASE == 1) {

@@ -19,12 +19,11 @@
 //   x ~ s_1 q_1 + s_2 q_2 + ... ,  q_t e2m1 (mxf4) or e4m3 (mxf8f6f4),
 //   s_t = 2^(c_t - 127), one ue8m0 code c_t per 32 elements of a row,
 // each term quantising what the earlier ones left over (mx_terms_kernel).
-// All terms accumulate into one f32 accumulator: NTERM MMAs per K step.
-// Measured error against the f32 oracle (config[3] shapes, CPU emulation of
-// these formats): mxf4 x1 2e-1, x2 3e-2, x3 3e-3, x4 2e-4 relative L2;
-// e4m3 x1 5e-2, x2 6e-4.  The modes below the 1e-2 bar are mxf4 x3/x4 and
-// mxf8f6f4 x2; an mxf4 MMA runs at twice the mxf8f6f4 rate, so three mxf4
-// terms cost 3/4 of the f16 tensor time and no dequantisation at all.
+// The terms accumulate into one f32 accumulator.  Measured on B200 over the
+// config[3] layer (relative L2 / max-abs against f64): mxf4 x1 2.2e-1 / 1.5,
+// x2 2.8e-2 / 1.9e-1, x3 2.7e-3 / 1.9e-2; e4m3 x1 4.7e-2 / 3.5e-1, x2 7e-4 /
+// 5.7e-3.  Three mxf4 terms cost 3/4 of the f16 tensor time and need no
+// dequantisation; two e4m3 terms cost the f16 tensor time.
 //
 // Layout (per CTA; a CTA pair splits M = 256 weight rows 128/128 and the
 // token tile N/2 / N/2 as tc_ffn does):
@@ -56,48 +55,69 @@ namespace mvb {
 
 enum { kMxF4 = 0, kMxF8 = 1 }; // MMA kind: mxf4 (block32) or mxf8f6f4 (e2m1 x e4m3)
 
+// Two forms, as tc_ffn: CTA pairs (M = 256 weight rows per MMA, token tiles
+// of up to 256 rows: an N = 256 pair MMA runs at the tensor rate; the token
+// terms accumulate through separate MMAs) and single CTAs for the rest tiles
+// of at most 64 rows.  A narrow MMA costs almost as much tensor-pipe time as
+// a 128-wide one (about 46 cycles at N <= 64 on B200), so the single-CTA form
+// stacks a tile's terms along N instead: term t's 64 token rows are rows
+// 64t..64t+63 of one B operand, one MMA per K step covers all terms, and the
+// epilogue adds the terms' accumulator columns.  The three operand rings
+// (weights, token terms, block scales in TMEM) advance one K stage at a
+// time; one "stage consumed" commit per stage frees a stage's slot in all
+// three (a tcgen05.commit costs about as much as an MMA to issue).
 template <int KIND, int NTERM, bool PAIR> struct MxCfg {
     static constexpr int EPI_WARPS = TcCfg<PAIR>::EPI_WARPS;
     static constexpr int SF_WARP0 = EPI_WARPS;
     static constexpr int TOK_WARP = SF_WARP0 + 4;
     static constexpr int MMA_WARP = TOK_WARP + 1;
     static constexpr int W_WARP = TOK_WARP + 2;
-    static constexpr int THREADS = (W_WARP + 1) * 32;
-    static constexpr int CTAS_PER_SM = PAIR ? 1 : 2;
-    static constexpr int NT = TcCfg<PAIR>::NT;           // token tile of an item
+    static constexpr int THREADS = (W_WARP + 1) * 32;     // pair 480, single 352
+    static constexpr int TSHIFT = 8;                      // pair tiles of 256 rows
+    static constexpr int NT = TcCfg<PAIR>::NT;            // 256 / 64
+    // Stacking pays where it cuts three or more MMAs to one (measured); the
+    // stacked accumulators need a whole SM's TMEM, the unstacked single-CTA
+    // form runs two CTAs per SM (two issuing threads).
+    static constexpr bool STACK = !PAIR && NTERM >= 3;
+    static constexpr int CTAS_PER_SM = (PAIR || STACK) ? 1 : 2;
+    // Columns of one accumulator buffer (a pair tile wider than 128 takes both).
+    static constexpr int ACC_COLS = STACK ? NTERM * NT : TcCfg<PAIR>::ACC_HALF;
     static constexpr int ACC_HALF = TcCfg<PAIR>::ACC_HALF;
     static constexpr int KSTAGE = KIND == kMxF4 ? 256 : 128; // K elements per stage
     static constexpr int G = KSTAGE / 128;                  // 4-code scale groups per stage
     static constexpr int WST = 512 / KSTAGE;                // stages per 16-byte scale window
-    static constexpr int KSTEP = KIND == kMxF4 ? 64 : 32;   // K of one MMA
     static constexpr int TOK_ROWS = PAIR ? NT / 2 : NT;     // token rows one CTA holds
     static constexpr int PLANE = TOK_ROWS * 128;            // one term's rows, one stage
     static constexpr int B_SLOT = NTERM * PLANE;
     static constexpr int A_SLOT = 128 * 128;
-    static constexpr int SB = NTERM == 1 ? 3 : 2;           // token ring depth
+    static constexpr int SB = PAIR ? (B_SLOT <= 16384 ? 4 : 3)
+                                   : STACK ? 4 : (B_SLOT <= 8192 ? 3 : 2);
     static constexpr int NSC = 2;                           // scale-window ring depth
     static constexpr int SCA_SLOT = 128 * 16;               // weight rows' windows
     static constexpr int SCB_SLOT = NTERM * NT * 16;        // every token of the tile (full N)
-    // Token-code columns per (term, group): N / 32 rounded up to 4 (whole
-    // 128-token blocks, as the MMA's scale layout is defined per 128 rows).
-    static constexpr int NBMAX = NT / 32 > 4 ? NT / 32 : 4;
+    // Token-code columns per (term, group): pairs N / 32 (a whole block of
+    // 8); single CTAs 2 (64 rows), the terms of a group adjacent.
+    static constexpr int NBMAX = PAIR ? NT / 32 : STACK ? 2 : 4;
     static constexpr int SF_COLS = 4 * G + NTERM * G * NBMAX;
     static constexpr int SSF = 3;                           // scale stages in tensor memory
-    static constexpr int TMEM_COLS = PAIR ? 512 : 256;
-    static constexpr int SF_BASE = 2 * ACC_HALF;
+    static constexpr int TMEM_COLS = CTAS_PER_SM == 1 ? 512 : 256;
+    static constexpr int SF_BASE = PAIR ? 2 * ACC_HALF : 2 * ACC_COLS;
     static_assert(SF_BASE + SSF * SF_COLS <= TMEM_COLS, "TMEM budget");
     static constexpr int SMEM_BUDGET = 232448 / CTAS_PER_SM;
-    static constexpr int FIXED = SB * B_SLOT + NSC * (SCA_SLOT + SCB_SLOT) + 8192;
+    static constexpr int ITEM_TAB = 512;
+    static constexpr int FIXED = SB * B_SLOT + NSC * (SCA_SLOT + SCB_SLOT) + 2 * ITEM_TAB * 4 +
+                                 1024 + 512;
     static constexpr int SA_FIT = (SMEM_BUDGET - FIXED) / A_SLOT;
     static constexpr int SA = SA_FIT > 8 ? 8 : SA_FIT;      // weight ring depth
-    static_assert(SA >= 2, "weight ring");
+    static_assert(SA >= 3, "weight ring");
     static constexpr int OFF_A = SB * B_SLOT;
     static constexpr int OFF_SCA = OFF_A + SA * A_SLOT;
     static constexpr int OFF_SCB = OFF_SCA + NSC * SCA_SLOT;
     static constexpr int OFF_BAR = OFF_SCB + NSC * SCB_SLOT;
-    static constexpr int NBARS = 2 * SA + 2 * SB + 2 * SSF + 4 * NSC + 4 + 1;
-    static constexpr int ITEM_TAB = 512;
-    static constexpr int OFF_ITEMS = OFF_BAR + NBARS * 8 + 16;
+    static constexpr int SD = SA > SB ? (SA > SSF ? SA : SSF) : (SB > SSF ? SB : SSF);
+    static constexpr int NBARS = SA + SB + SSF + SD + 4 * NSC + 4 + 1;
+    static_assert(NBARS * 8 + 16 <= 512, "barrier area");
+    static constexpr int OFF_ITEMS = OFF_BAR + 512;
     static constexpr int SMEM = OFF_ITEMS + 2 * ITEM_TAB * 4 + 1024;
     static_assert(SMEM <= SMEM_BUDGET, "dynamic shared memory per SM");
     // Arrivals on the leader's scale-stage barrier: SF warps of both CTAs.
@@ -159,6 +179,11 @@ __device__ __forceinline__ void tc_st1(uint32_t taddr, uint32_t v) {
 __device__ __forceinline__ void tc_st2(uint32_t taddr, uint32_t v0, uint32_t v1) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(v0),
                  "r"(v1)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_st4(uint32_t taddr, const uint32_t (&v)[4]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr),
+                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3])
                  : "memory");
 }
 __device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&v)[8]) {
@@ -286,7 +311,124 @@ __global__ void __launch_bounds__(256) mx_terms_kernel(const __half *__restrict_
     }
 }
 
+// ---- tensor-pipe rate ----------------------------------------------------------
+// Back-to-back MMAs of one kind on a resident tile (zeros, block scales of
+// code 0): the tensor pipe's own rate for the kinds the expert FFN issues,
+// measured in the same run as the kernels that use it.  KIND 0: mxf4 (K 64
+// per MMA), 1: mxf8f6f4 (K 32), 2: f16 (K 16).  One CTA (or CTA pair) per SM,
+// 128 threads; `iters` MMAs per CTA, then one commit and a bounded wait.
+template <int KIND, bool PAIR>
+__global__ void __launch_bounds__(128) mma_rate_kernel(int n, int iters, int *err) {
+    __shared__ __align__(1024) uint8_t tile[2 * 128 * 128];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t tslot;
+    const int warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < 2 * 128 * 128 / 16; i += blockDim.x)
+        reinterpret_cast<uint4 *>(tile)[i] = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        if (PAIR) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(&tslot)),
+                         "r"(512)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(&tslot)),
+                         "r"(512)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    if (PAIR)
+        cluster_sync();
+    else
+        __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(&tslot);
+    // Block scales (codes 0) in columns 256..271 of every lane quadrant.
+    const uint32_t lane_addr = static_cast<uint32_t>(32 * warp) << 16;
+    const uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    tc_st8(tmem + lane_addr + 256, z);
+    tc_st8(tmem + lane_addr + 264, z);
+    tc_wait_st();
+    tc_fence_before();
+    if (PAIR)
+        cluster_sync();
+    else
+        __syncthreads();
+    tc_fence_after();
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    bool ok = true;
+    if (threadIdx.x == 0 && rank == 0) {
+        const uint32_t a0 = smem_u32(tile), b0 = smem_u32(tile + 128 * 128);
+        const int M = PAIR ? 256 : 128;
+        for (int it = 0; it < iters; ++it) {
+            const int kk = it & 3;
+            const uint64_t ad = tc_desc_sw128(a0 + kk * 32), bd = tc_desc_sw128(b0 + kk * 32);
+            if (KIND == 2) { // single-CTA form only (the host launches no f16 pair)
+                    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::
+                                     "r"(tmem),
+                                 "l"(ad), "l"(bd), "r"(tc_idesc(M, n)), "r"(it != 0 ? 1u : 0u)
+                                 : "memory");
+            } else {
+                mx_mma<KIND == 0 ? kMxF4 : kMxF8, PAIR>(tmem, ad, bd, mx_idesc(KIND == 0 ? kMxF4 : kMxF8, M, n, 0u),
+                                                       it != 0, tmem + 256, tmem + 264);
+            }
+        }
+        if (PAIR) {
+            tc_commit_pair(cluster_addr(&bar, 0));
+            tc_commit_pair(cluster_addr(&bar, 1));
+        } else {
+            tc_commit_solo(&bar);
+        }
+        ok = mbar_wait(&bar, 0, err);
+    } else if ((threadIdx.x & 31) == 0) {
+        ok = mbar_wait(&bar, 0, err);
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    // An MMA that never completed leaves its TMEM alone (the error word says so).
+    if (!__syncthreads_and(ok))
+        return;
+    tc_fence_before();
+    if (PAIR)
+        cluster_sync();
+    else
+        __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        if (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                         "r"(512)
+                         : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                         "r"(512)
+                         : "memory");
+    }
+}
+
 // ---- the block-scaled expert FFN -------------------------------------------
+// A ring slot of depth `depth` may be refilled for stage k once stage
+// k - depth is consumed: wait for that stage's phase of the stage-empty ring
+// (SD >= depth barriers, so the barrier cannot have moved on a whole phase
+// past it: the MMAs cannot pass stage k before this slot is refilled).
+template <int SD>
+__device__ __forceinline__ bool mx_slot_free(uint64_t *st_empty, uint32_t k, uint32_t depth,
+                                             int *err) {
+    if (k < depth)
+        return true;
+    const uint32_t j = k - depth;
+    return mbar_wait(&st_empty[j % SD], (j / SD) & 1u, err);
+}
+
 template <int KIND, int NTERM, int PHASE, bool PAIR>
 __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
                                   MxCfg<KIND, NTERM, PAIR>::CTAS_PER_SM)
@@ -297,10 +439,9 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
-    uint64_t *a_full = bars, *a_empty = a_full + C::SA;
-    uint64_t *b_full = a_empty + C::SA, *b_empty = b_full + C::SB;
-    uint64_t *sf_full = b_empty + C::SB, *sf_empty = sf_full + C::SSF;
-    uint64_t *sa_full = sf_empty + C::SSF, *sa_empty = sa_full + C::NSC;
+    uint64_t *a_full = bars, *b_full = a_full + C::SA, *sf_full = b_full + C::SB;
+    uint64_t *st_empty = sf_full + C::SSF; // [SD]: stage k consumed (k % SD)
+    uint64_t *sa_full = st_empty + C::SD, *sa_empty = sa_full + C::NSC;
     uint64_t *sb_full = sa_empty + C::NSC, *sb_empty = sb_full + C::NSC;
     uint64_t *acc_full = sb_empty + C::NSC, *acc_empty = acc_full + 2, *done = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
@@ -324,18 +465,14 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
         return; // no item (for a pair: both CTAs leave) -- before touching TMEM
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::SA; ++s) {
+        for (int s = 0; s < C::SA; ++s)
             mbar_init(&a_full[s], 1); // the weight producer's expect_tx (leader: both CTAs' bytes)
-            mbar_init(&a_empty[s], 1);
-        }
-        for (int s = 0; s < C::SB; ++s) {
+        for (int s = 0; s < C::SB; ++s)
             mbar_init(&b_full[s], 1);
-            mbar_init(&b_empty[s], 1);
-        }
-        for (int s = 0; s < C::SSF; ++s) {
+        for (int s = 0; s < C::SSF; ++s)
             mbar_init(&sf_full[s], C::SF_ARRIVALS);
-            mbar_init(&sf_empty[s], 1);
-        }
+        for (int s = 0; s < C::SD; ++s)
+            mbar_init(&st_empty[s], 1); // the (leader's) tcgen05.commit of the stage
         for (int s = 0; s < C::NSC; ++s) {
             mbar_init(&sa_full[s], 1);
             mbar_init(&sa_empty[s], 4);
@@ -382,6 +519,8 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
             for (int i = unit; ok && i < total; i += nunits) {
                 TcItem it;
                 tc_item<PHASE, PAIR>(p, tab, i, it);
+                if (C::STACK)
+                    it.nmma = C::NT; // stacked terms: whole 64-row planes
                 const int rows = PAIR ? it.nmma >> 1 : it.nmma; // this CTA's token rows
                 const int xr0 = __ldg(p.xrow + it.e) + it.t0;
                 const int xr = xr0 + static_cast<int>(rank) * rows;
@@ -404,7 +543,7 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
                         ++w_it;
                     }
                     const uint32_t s = b_it % C::SB;
-                    if (!mbar_wait(&b_empty[s], ((b_it / C::SB) & 1u) ^ 1u, p.err)) {
+                    if (!mx_slot_free<C::SD>(st_empty, b_it, C::SB, p.err)) {
                         ok = false;
                         break;
                     }
@@ -472,7 +611,7 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
                         ++w_it;
                     }
                     const uint32_t s = a_it % C::SA;
-                    if (!mbar_wait(&a_empty[s], ((a_it / C::SA) & 1u) ^ 1u, p.err)) {
+                    if (!mx_slot_free<C::SD>(st_empty, a_it, C::SA, p.err)) {
                         ok = false;
                         break;
                     }
@@ -531,7 +670,7 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
             for (int i = unit; ok && i < total; i += nunits) {
                 TcItem it;
                 tc_item<PHASE, PAIR>(p, tab, i, it);
-                const int b = acc.take(it.nmma > C::ACC_HALF);
+                const int b = acc.take(!C::STACK && it.nmma > C::ACC_HALF);
                 if (b != 1 && !mbar_wait(&acc_empty[0], (acc.use[0] & 1u) ^ 1u, p.err))
                     ok = false;
                 if (ok && b != 0 && !mbar_wait(&acc_empty[1], (acc.use[1] & 1u) ^ 1u, p.err))
@@ -539,8 +678,17 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
                 if (!ok)
                     break;
                 tc_fence_after();
-                const uint32_t d = tmem + (b == 1 ? static_cast<uint32_t>(C::ACC_HALF) : 0u);
-                const int M = PAIR ? 256 : 128;
+                const uint32_t d = tmem + (b == 1 ? static_cast<uint32_t>(C::ACC_COLS) : 0u);
+                // Everything an MMA needs is a per-item or per-stage base plus a
+                // compile-time offset: instruction descriptors for the two
+                // scale-byte positions, the operand descriptors (address >> 4
+                // in the low bits) and the scale columns.
+                const uint32_t id0 =
+                    mx_idesc(KIND, PAIR ? 256 : 128, C::STACK ? NTERM * C::NT : it.nmma, 0u);
+                constexpr uint32_t kSfStep = (1u << 4) | (1u << 29); // sf_id += 1 for A and B
+                // Ring bases as descriptors (start address >> 4 in bits 0..13;
+                // every address stays below 256 KB, so offsets add in place).
+                const uint64_t adesc_base = tc_desc_sw128(a_base), bdesc_base = tc_desc_sw128(b_base);
                 for (int kb = 0; kb < nk; ++kb) {
                     const uint32_t sa = a_it % C::SA, sb = b_it % C::SB, sf = f_it % C::SSF;
                     if (!mbar_wait(&a_full[sa], (a_it / C::SA) & 1u, p.err) ||
@@ -550,37 +698,40 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
                         break;
                     }
                     tc_fence_after();
+                    const uint64_t ad = adesc_base + ((sa * C::A_SLOT) >> 4);
+                    const uint64_t bd = bdesc_base + ((sb * C::B_SLOT) >> 4);
                     const uint32_t sfa0 = tmem + C::SF_BASE + sf * C::SF_COLS;
                     const uint32_t sfb0 = sfa0 + 4 * C::G;
+                    const uint32_t acc0 = kb != 0 ? 1u : 0u;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint32_t g = KIND == kMxF4 ? static_cast<uint32_t>(kk >> 1) : 0u;
                         const uint32_t id = KIND == kMxF4 ? static_cast<uint32_t>(kk & 1) * 2u
                                                           : static_cast<uint32_t>(kk);
-                        const uint32_t idesc = mx_idesc(KIND, M, it.nmma, id);
-                        const uint64_t adesc = tc_desc_sw128(a_base + sa * C::A_SLOT + kk * 32);
+                        const uint32_t idesc = id0 + id * kSfStep;
                         const uint32_t tsfa = (sfa0 + 4 * g) | (id << 30);
+                        if (C::STACK) {
+                            // All terms in one MMA: B rows 64t.. are term t's tokens.
+                            const uint32_t tsfb = (sfb0 + g * NTERM * C::NBMAX) | (id << 30);
+                            mx_mma<KIND, PAIR>(d, ad + 2 * kk, bd + 2 * kk, idesc,
+                                               kk != 0 ? 1u : acc0, tsfa, tsfb);
+                        } else {
 #pragma unroll
-                        for (int t = 0; t < NTERM; ++t) {
-                            const uint64_t bdesc =
-                                tc_desc_sw128(b_base + sb * C::B_SLOT + t * C::PLANE + kk * 32);
-                            const uint32_t tsfb =
-                                (sfb0 + (t * C::G + g) * C::NBMAX) | (id << 30);
-                            mx_mma<KIND, PAIR>(d, adesc, bdesc, idesc, (kb | kk | t) != 0, tsfa,
-                                               tsfb);
+                            for (int t = 0; t < NTERM; ++t) {
+                                const uint32_t tsfb =
+                                    (sfb0 + (t * C::G + g) * C::NBMAX) | (id << 30);
+                                mx_mma<KIND, PAIR>(d, ad + 2 * kk,
+                                                   bd + ((t * C::PLANE) >> 4) + 2 * kk, idesc,
+                                                   (kk | t) != 0 ? 1u : acc0, tsfa, tsfb);
+                            }
                         }
                     }
+                    const uint32_t se = a_it % C::SD; // a_it == b_it == f_it: the stage index
                     if (PAIR) {
-                        tc_commit_pair(cluster_addr(&a_empty[sa], 0));
-                        tc_commit_pair(cluster_addr(&a_empty[sa], 1));
-                        tc_commit_pair(cluster_addr(&b_empty[sb], 0));
-                        tc_commit_pair(cluster_addr(&b_empty[sb], 1));
-                        tc_commit_pair(cluster_addr(&sf_empty[sf], 0));
-                        tc_commit_pair(cluster_addr(&sf_empty[sf], 1));
+                        tc_commit_pair(cluster_addr(&st_empty[se], 0));
+                        tc_commit_pair(cluster_addr(&st_empty[se], 1));
                     } else {
-                        tc_commit_solo(&a_empty[sa]);
-                        tc_commit_solo(&b_empty[sb]);
-                        tc_commit_solo(&sf_empty[sf]);
+                        tc_commit_solo(&st_empty[se]);
                     }
                     ++a_it;
                     ++b_it;
@@ -622,6 +773,8 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
         for (int i = unit; ok && i < total; i += nunits) {
             TcItem it;
             tc_item<PHASE, PAIR>(p, tab, i, it);
+            if (C::STACK)
+                it.nmma = C::NT;
             const int nb = (it.nmma + 31) >> 5; // token-code columns in use
             uint32_t wa = 0, wb = 0;
             for (int kb = 0; kb < nk; ++kb) {
@@ -637,8 +790,7 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
                     }
                 }
                 const uint32_t sf = f_it % C::SSF;
-                if (!__all_sync(0xffffffffu,
-                                mbar_wait(&sf_empty[sf], ((f_it / C::SSF) & 1u) ^ 1u, p.err))) {
+                if (!__all_sync(0xffffffffu, mx_slot_free<C::SD>(st_empty, f_it, C::SSF, p.err))) {
                     ok = false;
                     break;
                 }
@@ -656,20 +808,23 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
                     tc_st1(col0 + 4 * g + q, va);
 #pragma unroll
                     for (int t = 0; t < NTERM; ++t) {
-                        const uint32_t cb = col0 + 4 * C::G + (t * C::G + g) * C::NBMAX;
+                        const uint32_t cb = col0 + 4 * C::G +
+                                            (C::STACK ? (g * NTERM + t) : (t * C::G + g)) * C::NBMAX;
                         if (PAIR) {
                             uint32_t vb[8];
 #pragma unroll
                             for (int n1 = 0; n1 < 8; ++n1)
-                                vb[n1] = n1 < nb ? lds32(smem_u32(winb + ((t * C::NT) + lane + 32 * n1) * 16 +
-                                                                  4 * word))
+                                vb[n1] = n1 < nb ? lds32(smem_u32(
+                                                       winb + ((t * C::NT) + lane + 32 * n1) * 16 +
+                                                       4 * word))
                                                  : 0u;
                             tc_st8(cb, vb);
                         } else {
                             const uint32_t v0 =
                                 lds32(smem_u32(winb + ((t * C::NT) + lane) * 16 + 4 * word));
                             const uint32_t v1 =
-                                nb > 1 ? lds32(smem_u32(winb + ((t * C::NT) + lane + 32) * 16 + 4 * word))
+                                nb > 1 ? lds32(smem_u32(winb + ((t * C::NT) + lane + 32) * 16 +
+                                                        4 * word))
                                        : 0u;
                             tc_st2(cb, v0, v1);
                         }
@@ -694,8 +849,12 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
             }
         }
     } else if (warp < C::EPI_WARPS) {
-        tc_epilogue<MVLLM_FMT_MXFP4, PHASE, PAIR>(p, tab, unit, nunits, total, tmem, rank, acc_full,
-                                                  acc_empty, warp, lane);
+        if (C::STACK)
+            tc_epilogue<MVLLM_FMT_MXFP4, PHASE, PAIR, NTERM, C::NT, C::ACC_COLS, C::NT>(
+                p, tab, unit, nunits, total, tmem, rank, acc_full, acc_empty, warp, lane);
+        else
+            tc_epilogue<MVLLM_FMT_MXFP4, PHASE, PAIR>(p, tab, unit, nunits, total, tmem, rank,
+                                                      acc_full, acc_empty, warp, lane);
     }
 
     tc_fence_before();

@@ -49,6 +49,7 @@ C_SYMBOLS = (
     "mvllm_moe_host_unregister", "mvllm_moe_route_ex_dev", "mvllm_moe_ep_local_ids_dev",
     "mvllm_moe_dense_ffn_workspace", "mvllm_moe_dense_ffn_dev", "mvllm_moe_wait_selftest",
     "mvllm_moe_set_prefill_mode", "mvllm_moe_get_prefill_mode", "mvllm_mx_terms_dev",
+    "mvllm_moe_mma_rate",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -121,6 +122,7 @@ def lib():
             "mvllm_moe_set_prefill_mode": (i, [i]),
             "mvllm_moe_get_prefill_mode": (i, []),
             "mvllm_mx_terms_dev": (i, [vp, i, vp, i, i, vp, vp]),
+            "mvllm_moe_mma_rate": (i, [i, i, i, i, vp]),
             "mvllm_moe_dense_ffn_dev": (i, [vp, i, i, i, i] + [vp] * 7 + [i, f, f, vp, i, vp,
                                                                          sz]),
         }
@@ -161,6 +163,13 @@ def set_prefill_mode(mode) -> None:
 
 def get_prefill_mode() -> int:
     return int(lib().mvllm_moe_get_prefill_mode())
+
+
+def mma_rate(kind, n, pair, iters=20000) -> float:
+    """Dense TFLOP/s of back-to-back MMAs (kind 0 mxf4, 1 mxf8f6f4, 2 f16)."""
+    v = C.c_double(0.0)
+    _check(lib().mvllm_moe_mma_rate(int(kind), int(n), int(pair), int(iters), C.byref(v)))
+    return v.value
 
 
 def mx_terms_dev(mode, src, planes, codes, stream=None) -> None:
