@@ -1,18 +1,22 @@
 #!/usr/bin/env python
-"""MoE-block tokens/s on B200 -- BASELINE config[1] (Kimi-K3-style MXFP4 decode).
+"""MoE-block tokens/s on B200 -- BASELINE config[4], the expert-parallel layer.
 
-One step = one routed MoE layer over a batch of B tokens: token permutation,
-expert FFN (gate/up + SiTU, down) over the 8 routed experts of every token plus
-the always-on shared expert, ordered combine.  Workload per rank: hidden 7168,
-expert intermediate 2048, 256 routed experts (top-8, uniform-random router
-draws) + 1 shared expert, MXFP4 weights (e2m1 + ue8m0 per 32) drawn N(0, 0.02)
-and packed on the GPU, bf16 activations N(0, 1).  Weights total 6.0 GB, far
-above L2, so no flush is needed between steps; 16 distinct routings cycle.
+One step = one routed MoE layer over 8192 tokens: 384 MXFP4 experts (e2m1 +
+ue8m0 per 32, drawn N(0, 0.02) and packed on the GPU), hidden 7168, expert
+intermediate 2048, top-8, SiTU(4,25), bf16 activations N(0, 1), uniform
+router draws.  At N GPUs (torchrun, one process per GPU, NCCL) the experts
+are strided over the ranks (e on rank e % N, hot experts replicated), each
+rank routes its 8192 / N tokens, dispatches them over an NCCL all-to-all,
+runs its experts and returns the partial sums (strong scaling); tokens/s
+over the slowest rank's step time.  At one GPU the same layer runs whole.
+Weights total 9.0 GB, far above L2, so no flush is needed between steps.
 
-N>1 (torchrun): each rank runs its own replica of the workload (decode
-replicas, weak scaling, no data-path collective); timing is the max over ranks.
-`--impl reference` times the reference's own CPU moe_block (oracle/_ref) on
-the host cores for the same config and metric.
+Beside the headline: the Zipf run and weak scaling of config[4], the
+decode path (config[1], HBM-bound, with its roofline), the prefill path
+(config[3], every tensor-core mode with its measured error), config[0] and
+config[2], the device expert tier, the layer epilogue, and the DeepSeek-V4
+expert split.  `--impl reference` times the reference's own CPU moe_block
+(oracle/_ref) on the host cores for config[4]'s metric.
 """
 from __future__ import annotations
 
@@ -31,15 +35,15 @@ sys.path.insert(0, os.path.join(ROOT, "micro-vllm_b200"))
 
 CFG = dict(D=7168, I=2048, E=256, K=8, n_shared=1, fmt=7, act=2, act_a=4.0, act_b=25.0)
 EXPERT_BYTES = 3 * (CFG["I"] * CFG["D"] // 2 + CFG["I"] * CFG["D"] // 32)  # 23,396,352
-METRIC = "MoE-block tokens/sec (config[1] MXFP4 decode)"
+METRIC = "MoE-block tokens/sec (config[4] expert-parallel MXFP4 layer, 8192 tokens per step)"
 N_INPUTS = 16
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
@@ -52,9 +56,14 @@ def parse():
                     help="skip the config[3] prefill measurement")
     ap.add_argument("--prefill-steps", type=int, default=10)
     ap.add_argument("--no-ep", action="store_true", help="skip the config[4] expert-parallel leg")
+    ap.add_argument("--no-decode", action="store_true", help="skip the config[1] decode leg")
+    ap.add_argument("--decode-steps", type=int, default=200)
     ap.add_argument("--no-decode-configs", action="store_true",
                     help="skip the config[0] and config[2] decode legs")
     ap.add_argument("--ep-steps", type=int, default=20)
+    ap.add_argument("--ep-chunks", type=int, default=2,
+                    help="token slices per expert-parallel step (N > 1): the exchanges of one "
+                         "slice overlap the experts of another")
     ap.add_argument("--no-dsv4", action="store_true",
                     help="skip the DeepSeek-V4 expert-split (EP2) leg")
     ap.add_argument("--dsv4-steps", type=int, default=100)
@@ -646,7 +655,8 @@ def ep_routing(torch, name, T, K, seed):
     return zipf_routing(torch, T, EP_E, K, gr, perm=perm)
 
 
-def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=None, e2e_steps=0):
+def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=None, e2e_steps=0,
+             chunks=1):
     """Config[4]: 384 MXFP4 experts sharded over the ranks (expert e on rank
     e % world), top-8; uniform and Zipf s=1.1 routing.  Weights are drawn per
     global expert id, so the model is the same whatever the rank count.
@@ -660,7 +670,9 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
     The uniform run's timed region is sampled by `clk`; its expert kernels'
     device time (phase events, max over ranks) gives the roofline; with
     `e2e_steps` the same step also runs from host buffers (pinned x, idx, wt
-    copied in, out copied back inside the timed region)."""
+    copied in, out copied back inside the timed region).  With `chunks` > 1
+    (N > 1) each step runs as that many token slices whose exchanges overlap
+    the expert kernels (EPLayer.forward_chunked)."""
     import ep
     D, I, K = CFG["D"], CFG["I"], CFG["K"]
     u8 = torch.uint8
@@ -722,6 +734,8 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
 
         def step(xx=x, ii=idx, ww=wt, oo=out):
             oo.zero_()
+            if world > 1 and chunks > 1:
+                return layer.forward_chunked(xx, ii, ww, oo, dist, chunks=chunks)
             if world > 1:
                 return layer.forward(xx, ii, ww, oo, dist)
             ep.emulate_step([layer], [xx], [ii], [ww], [oo], torch)
@@ -803,6 +817,7 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
                         f"ranks (hot experts replicated), hidden 7168, inter 2048, top-8, {per}, "
                         "bf16 activations; NCCL all-to-all dispatch and return",
             "n_gpus": world, "scaling": "weak" if weak else "strong", "tokens_per_step": T_all,
+            "slices_per_step": chunks if world > 1 else 1,
             **res}
 
 
@@ -908,12 +923,14 @@ def dsv4_cpu_reference(torch, wl, x, router, bias, idx, tokens=2):
         return {"tokens_per_s": None, "sample": f"unavailable: {ex}"}
 
 
-def cpu_reference_rate(n_threads, rounds, expert_rows_per_call, host_experts=None):
+def cpu_reference_rate(n_threads, rounds, expert_rows_per_call, host_experts=None,
+                       rows_per_token=9.0):
     """Reference moe_block (oracle/_ref) on host threads.
 
     Each thread calls the reference moe_block on one token row through
-    `expert_rows_per_call` experts of config[1]; returns (tokens/s, seconds,
-    tokens).  A config[1] token is 9 expert rows (8 routed + shared)."""
+    `expert_rows_per_call` MXFP4 experts (7168 / 2048); returns (tokens/s,
+    seconds, tokens) with `rows_per_token` expert rows per token (config[1]:
+    9, 8 routed + shared; config[4]: 8)."""
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     from oracle import Oracle
@@ -955,7 +972,7 @@ def cpu_reference_rate(n_threads, rounds, expert_rows_per_call, host_experts=Non
     for _ in range(rounds):
         one_round()
     sec = time.perf_counter() - t0
-    tokens = rounds * n_threads * ne / 9.0
+    tokens = rounds * n_threads * ne / rows_per_token
     return tokens / sec, sec, tokens
 
 
@@ -967,28 +984,31 @@ def host_threads():
 
 
 def run_reference(args):
+    """The reference's own CPU moe_block (oracle/_ref) on all host threads, on
+    config[4]'s expert rows (8 MXFP4 experts of 7168 / 2048 per token, SiTU):
+    each step a bounded sample of the workload, `threads` parallel calls of
+    one token row through a few experts, sized so the run ends in about 90 s.
+    Under torchrun rank 0 alone runs and prints."""
     rank, _, world = dist_env()
     if rank != 0:
         return
     threads = host_threads()
-    # Each step: `threads` parallel reference calls of a few expert rows,
-    # sized so steps+warmup finish in about 90 s (0.05 s per expert row).
     per_step_budget = 90.0 / max(args.steps + args.warmup, 1)
     rows = max(1, int(per_step_budget / 0.05))
-    cpu_reference_rate(threads, max(args.warmup, 0) and 1, rows)  # warm-up (1 round)
-    rate, sec, tokens = cpu_reference_rate(threads, args.steps, rows)
+    cpu_reference_rate(threads, max(args.warmup, 0) and 1, rows, rows_per_token=8.0)  # warm-up
+    rate, sec, tokens = cpu_reference_rate(threads, args.steps, rows, rows_per_token=8.0)
     line = {
         "impl": "reference", "metric": METRIC, "value": rate, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": sec * 1e3 / max(args.steps, 1), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config[1] MXFP4 decode, hidden 7168, inter 2048, 256 experts "
-                               "top-8 + 1 shared, SiTU(4,25)", "batch": args.batch,
-                   "parallelism": "host threads"},
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config[4] expert-parallel MXFP4 MoE layer: 384 experts, hidden "
+                               "7168, inter 2048, top-8, 8192 tokens per step, SiTU(4,25)",
+                   "global_batch": EP_T, "parallelism": "host threads"},
         "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": threads,
                          "kind": "reference",
                          "sample": f"per step {threads} threads x 1 token row through {rows} "
-                                   f"expert(s) of config[1] (9 expert rows = 1 token)"},
+                                   f"expert(s) of config[4] (8 expert rows = 1 token)"},
         "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -996,6 +1016,17 @@ def run_reference(args):
 
 
 # -------------------------------------------------------------------- ours --
+def launches_per_ep_step(world, mode):
+    """This library's kernels in one config[4] step (NCCL's own kernels not
+    counted): EP plan and pack (N > 1), the routed layer over the received
+    rows (permutation: memset + 4 kernels at these sizes; gather; expert plan;
+    2 tensor-map builds; phase 1 and phase 2 each on the decode kernel, CTA
+    pairs and single CTAs; the block-scaled modes add 2 term-quantisation
+    kernels; combine), and the EP combine (N > 1)."""
+    layer = 4 + 1 + 1 + 2 + 3 + 3 + 1 + (2 if mode != "f16" else 0)
+    return layer + (3 if world > 1 else 0)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1017,113 +1048,35 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     moe.init(local_rank)
-    B = args.batch
-    wl = Workload(moe, torch, B, seed=1234 + rank)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    # warm-up
-    for i in range(max(args.warmup, 3)):
-        wl.step(moe, i)
-    barrier()
-
-    # timed region (eager launches; each step is ~1 ms of device work, so the
-    # host stays ahead and the phase events measure device time)
-    moe.profile_enable(True)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clk:
-        a.record()
-        for i in range(args.steps):
-            wl.step(moe, i)
-        b.record()
-        barrier()
-    ms = a.elapsed_time(b)
-    phases = moe.profile_read()
-    moe.profile_enable(False)
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    tokens = B * args.steps * world
-    value = tokens / (ms_max / 1e3)
-
-    # roofline of the expert kernels (decode_ffn phase 1 + phase 2)
-    e_steps = [wl.experts_per_input[i % N_INPUTS] for i in range(args.steps)]
-    alg_bytes = sum(e_steps) * EXPERT_BYTES / args.steps  # per step
-    k_ms = (phases["expert_phase1"][0] + phases["expert_phase2"][0]) / args.steps
-    achieved = alg_bytes / (k_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
-    ratio = traffic_ratio()
+    mode = moe.PREFILL_NAMES[moe.get_prefill_mode()]
 
-    # end to end: host buffers through the C ABI (copies inside the region)
-    idx_h, wt_h, x_h = [], [], []
-    for (idx, wt, x) in wl.inputs:
-        idx_h.append(idx.cpu().numpy())
-        wt_h.append(wt.cpu().numpy())
-        x_h.append(x.float().cpu().numpy())
-    out_h = np.zeros((B, CFG["D"]), np.float32)
-    # The caller's activation and output rows live in page-locked memory (as a
-    # serving engine's I/O buffers do): registered once, copied directly.
-    for a in x_h + [out_h]:
-        moe.host_register(a)
-    for i in range(3):
-        moe.layer_host(B, CFG["K"], CFG["E"], CFG["n_shared"], CFG["D"], CFG["I"], CFG["fmt"],
-                       idx_h[i], wt_h[i], x_h[i], wl.host_tables, out_h, CFG["act"],
-                       CFG["act_a"], CFG["act_b"])
-    barrier()
-    # The call adds the layer's output into the caller's rows (out += ..., as
-    # the reference accumulates into acc); the rows are not reset between
-    # steps, so the loop times the call and its copies, not a host memset.
-    t0 = time.perf_counter()
-    for i in range(args.e2e_steps):
-        moe.layer_host(B, CFG["K"], CFG["E"], CFG["n_shared"], CFG["D"], CFG["I"], CFG["fmt"],
-                       idx_h[i % N_INPUTS], wt_h[i % N_INPUTS], x_h[i % N_INPUTS],
-                       wl.host_tables, out_h, CFG["act"], CFG["act_a"], CFG["act_b"])
-    e2e_s = time.perf_counter() - t0
-    for a in x_h + [out_h]:
-        moe.host_unregister(a)
-    t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    # ---- headline: config[4], the expert-parallel layer at N GPUs (strong
+    # scaling: 8192 tokens per step over all ranks), uniform routing; the Zipf
+    # run and, at N > 1, weak scaling beside it.
+    clk = ClockSampler(local_rank)
+    ep_res = ep_bench(moe, torch, dist, rank, world, args.steps, args.warmup, clk=clk,
+                      e2e_steps=args.e2e_steps, chunks=args.ep_chunks)
+    uni = ep_res["uniform"]
+    value, ms = uni["tokens_per_s"], uni["ms_per_step"]
+    flops = 2.0 * EP_T * CFG["K"] * 3 * CFG["D"] * CFG["I"]  # per step, all ranks
+    e_ms = uni["expert_kernels_ms_per_step_max_over_ranks"]
+    if mode == "f16":
+        tpeak, tpeak_kind = bf16_peak(), "measured (MEASURED_PEAKS.json bf16 dense, burst; the " \
+                                         "expert kernels run kind::f16 MMAs at the same rate)"
+    else:
+        pk, _, _ = MODE_PIPE[mode]
+        tpeak = moe.mma_rate(*((0, 256, 1) if pk == "mxf4" else (1, 256, 1)))
+        tpeak_kind = f"measured in this run: back-to-back {pk} MMAs on every SM"
+    achieved = flops / world / (e_ms / 1e3) / 1e12
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = B * args.e2e_steps * world / float(t.item())
-    EE = CFG["E"] + CFG["n_shared"]
-    h2d = 6 * EE * 8 + 2 * B * CFG["K"] * 4 + 2 * B * CFG["D"] * 4
-    d2h = B * CFG["D"] * 4
+        ep_res["weak_scaling"] = ep_bench(moe, torch, dist, rank, world, args.ep_steps,
+                                          args.warmup, weak=True, chunks=args.ep_chunks)
 
-    # batch sweep (graph replays; same per-rank workload shape)
-    sweep = None
-    if not args.no_sweep:
-        sweep = {}
-        for bb in (1, 8, 32):
-            wb = wl if bb == B else None
-            if wb is None:
-                wb = Workload.__new__(Workload)
-                wb.__dict__.update({k: v for k, v in wl.__dict__.items()
-                                    if k not in ("inputs", "out", "ws", "B")})
-                wb.B = bb
-                g = torch.Generator(device="cuda").manual_seed(99 + bb)
-                wb.inputs = []
-                for _ in range(N_INPUTS):
-                    choice = torch.rand((bb, CFG["E"]), generator=g, device="cuda")
-                    vals, idx = torch.topk(choice, CFG["K"], dim=1)
-                    wt = (vals / vals.sum(dim=1, keepdim=True)).float()
-                    x = torch.randn((bb, CFG["D"]), generator=g, device="cuda").to(torch.bfloat16)
-                    wb.inputs.append((idx.int().contiguous(), wt.contiguous(), x))
-                wb.out = torch.zeros((bb, CFG["D"]), dtype=torch.float32, device="cuda")
-                wb.ws = torch.empty(moe.layer_workspace_bytes(bb, CFG["K"], CFG["E"],
-                                                              CFG["n_shared"], CFG["D"], CFG["I"],
-                                                              CFG["fmt"]),
-                                    dtype=torch.uint8, device="cuda")
-            tps, mstep = graph_throughput(moe, torch, wb, 320, 32)
-            touched = [len(set(i.flatten().tolist())) + CFG["n_shared"] for (i, _, _) in wb.inputs]
-            nb = sum(touched) / len(touched) * EXPERT_BYTES + bb * CFG["D"] * 6
-            sweep[f"B{bb}"] = {"tokens_per_s": tps * world, "ms_per_step": mstep,
-                               "algorithmic_bytes_per_step": nb,
-                               "hbm_gbs": nb / (mstep / 1e3) / 1e9,
-                               "hbm_frac_of_step": nb / (mstep / 1e3) / 1e9 / peak}
+    # ---- config[1] decode (N = 1): the HBM-bound path -------------------------
+    decode = None
+    if world == 1 and not args.no_decode:
+        decode = decode_config1(moe, torch, args, peak)
 
     # config[2] (GLM-style int4-g64 decode) and config[0] (the reference's
     # CPU-runnable case) at N = 1
@@ -1136,94 +1089,180 @@ def main():
                           "top-4, 4 tokens, clamped SwiGLU (7), softmax router",
                           1024, 512, 16, 4, 4, 1, 7.0, 0.0, (4,), "softmax", peak, 2200)
 
-    # config[4] expert-parallel layer (all ranks together)
-    ep_res = None
-    if not args.no_ep:
-        ep_res = ep_bench(moe, torch, dist, rank, world, args.ep_steps)
-        # Weak scaling: 8192 tokens per rank (at 1 GPU the same run as above).
-        ep_res["weak_scaling"] = (ep_bench(moe, torch, dist, rank, world, args.ep_steps, weak=True)
-                                  if world > 1 else "same workload as the strong run at 1 GPU")
-
     # DeepSeek-V4 MoE step, experts split over the ranks: one GPU, or the
     # reference's two-rank EP2 (more ranks with --dsv4-all-ranks)
     dsv4_res = None
+    wl = decode["_workload"] if decode else None
     if not args.no_dsv4 and (world <= 2 or args.dsv4_all_ranks):
+        if wl is None:
+            wl = Workload(moe, torch, args.batch, seed=1234 + rank)
         dsv4_res = dsv4_bench(moe, torch, dist, rank, world, wl, args.dsv4_steps)
 
-    # config[3] prefill (tensor-core kernels), per rank
-    prefill = None
-    tier = None
-    if not args.no_tier and world == 1:
-        tier = tier_bench(moe, torch, wl, args.tier_steps)
-    epilogue = epilogue_bench(moe, torch, peak) if world == 1 else None
-    if not args.no_prefill:
-        prefill = prefill_bench(moe, torch, wl, args.prefill_steps, bf16_peak(), peak,
-                                args.prefill_tokens)
+    # config[3] prefill, the device expert tier and the layer epilogue (N = 1)
+    prefill = tier = epilogue = None
+    if world == 1:
+        if wl is None:
+            wl = Workload(moe, torch, args.batch, seed=1234)
+        if not args.no_tier:
+            tier = tier_bench(moe, torch, wl, args.tier_steps)
+        epilogue = epilogue_bench(moe, torch, peak)
+        if not args.no_prefill:
+            prefill = prefill_bench(moe, torch, wl, args.prefill_steps, bf16_peak(), peak,
+                                    args.prefill_tokens)
 
-    # CPU baseline (rank 0, N=1 only): reference moe_block on host threads
+    # CPU baseline (rank 0, N = 1): the reference moe_block on host threads,
+    # config[4] expert rows (8 per token, no shared expert)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            host_experts = []
-            for e in [int(v) for v in wl.inputs[0][0][0].tolist()] + [CFG["E"]]:
-                host_experts.append([(wl.gp[e].cpu().numpy(), wl.gs[e].cpu().numpy()),
-                                     (wl.up[e].cpu().numpy(), wl.us[e].cpu().numpy()),
-                                     (wl.dp[e].cpu().numpy(), wl.ds[e].cpu().numpy())])
             nth = min(host_threads(), 16)
-            rate, sec, toks = cpu_reference_rate(nth, 2, 9, host_experts)
+            rate, sec, toks = cpu_reference_rate(nth, 2, 8, rows_per_token=8.0)
             cpu = {"value": rate, "unit": "tokens/s", "cores": nth, "kind": "reference",
-                   "sample": f"{int(toks)} token rows of config[1] (token 0's 8 routed + shared "
-                             f"experts), {nth} threads x 2 rounds, {sec:.1f} s wall"}
+                   "sample": f"{toks:.0f} config[4] tokens: {nth} threads x 2 rounds of the "
+                             f"reference moe_block on one token row through 8 MXFP4 experts "
+                             f"(7168 / 2048), {sec:.1f} s wall"}
         except Exception as ex:  # the reference build may be absent
             cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
                    "sample": f"unavailable: {ex}"}
 
+    if decode:
+        decode.pop("_workload", None)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "mxfp4 weights, f16 MMA operands, f32 accumulate", "data": "synthetic",
-            "config": {"workload": "config[1] MXFP4 decode MoE block: hidden 7168, inter 2048, "
-                                   "256 experts top-8 + 1 shared, SiTU(4,25), bf16 activations",
-                       "batch_per_gpu": B, "global_batch": B * world,
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (6.0 GB of expert weights per rank, 16 "
-                             "distinct routings)"},
-            "roofline": {"bound": "hbm", "kernel": "decode_ffn (expert phase 1 + phase 2)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": None if ratio is None else ratio * alg_bytes,
-                         "algorithmic_bytes_per_step": alg_bytes,
-                         "kernel_ms_per_step": k_ms},
-            "phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
-            # per decode step: permutation (one CTA at decode batch sizes),
-            # gather, plan, tensor-map build, decode phase 1, decode phase 2,
-            # combine
-            "gpu_launches": 7 * args.steps,
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "api": "mvllm_moe_layer_host",
-                    "host_buffers": "caller x / out page-locked with mvllm_moe_host_register"},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": f"mxfp4 weights, {mode} tensor-core mode, f32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": "config[4] expert-parallel MXFP4 MoE layer: 384 experts "
+                                   "strided over the ranks (hot experts replicated), hidden "
+                                   "7168, inter 2048, top-8, 8192 tokens per step (strong "
+                                   "scaling), uniform routing, SiTU(4,25), bf16 activations",
+                       "global_batch": EP_T, "parallelism": f"expert parallel x{world}",
+                       "l2": "inputs larger than L2 (9.0 GB of expert weights over the ranks)"},
+            "roofline": {"bound": "tensor", "kernel": "expert FFN (phase 1 + phase 2, tensor-core "
+                                                     "and decode kernels), max over ranks",
+                         "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
+                         "frac": achieved / tpeak, "peak_kind": tpeak_kind,
+                         "traffic": None,
+                         "algorithmic_flops_per_step_per_gpu": flops / world,
+                         "kernel_ms_per_step": e_ms},
+            "gpu_launches": launches_per_ep_step(world, mode) * args.steps,
+            "e2e": ep_res.get("e2e"),
             "cpu_baseline": cpu,
             "clocks": clk.report(),
-            "sweep": sweep,
-            "prefill": prefill,
-            "expert_tier": tier,
-            "epilogue": epilogue,
             "expert_parallel": ep_res,
+            "decode_config1": decode,
+            "prefill": prefill,
             "config2_glm_int4_decode": glm,
             "config0_small_int4": cfg0,
+            "expert_tier": tier,
+            "epilogue": epilogue,
             "dsv4_expert_split": dsv4_res,
         }
         if prefill and cpu and cpu.get("value"):
-            # The reference's rate in expert rows/s (9 rows per config[1] token)
-            # extrapolated to one config[3] step of 32768 rows.
             prefill["cpu_reference_ms_per_step_extrapolated"] = (
-                args.prefill_tokens * CFG["K"] / (cpu["value"] * 9.0) * 1e3)
+                args.prefill_tokens / cpu["value"] * 1e3)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def decode_config1(moe, torch, args, peak):
+    """Config[1] MXFP4 decode at the decode batch (32 tokens + the shared
+    expert, 257 experts, 6 GB of weights): eager steps through
+    mvllm_moe_layer_dev with the expert kernels' HBM roofline, the same
+    batch end to end through mvllm_moe_layer_host, and batches 1 / 8 / 32
+    from CUDA-graph replays."""
+    import numpy as np
+    B = args.batch
+    wl = Workload(moe, torch, B, seed=1234)
+    for i in range(max(args.warmup, 3)):
+        wl.step(moe, i)
+    torch.cuda.synchronize()
+    steps = args.decode_steps
+    moe.profile_enable(True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        wl.step(moe, i)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    phases = moe.profile_read()
+    moe.profile_enable(False)
+    e_steps = [wl.experts_per_input[i % N_INPUTS] for i in range(steps)]
+    alg_bytes = sum(e_steps) * EXPERT_BYTES / steps
+    k_ms = (phases["expert_phase1"][0] + phases["expert_phase2"][0]) / steps
+    achieved = alg_bytes / (k_ms / 1e3) / 1e9
+    ratio = traffic_ratio()
+    # end to end through the host-pointer layer entry
+    idx_h, wt_h, x_h = [], [], []
+    for (idx, wt, x) in wl.inputs:
+        idx_h.append(idx.cpu().numpy())
+        wt_h.append(wt.cpu().numpy())
+        x_h.append(x.float().cpu().numpy())
+    out_h = np.zeros((B, CFG["D"]), np.float32)
+    for arr in x_h + [out_h]:
+        moe.host_register(arr)
+    args_l = (B, CFG["K"], CFG["E"], CFG["n_shared"], CFG["D"], CFG["I"], CFG["fmt"])
+    for i in range(3):
+        moe.layer_host(*args_l, idx_h[i], wt_h[i], x_h[i], wl.host_tables, out_h, CFG["act"],
+                       CFG["act_a"], CFG["act_b"])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.e2e_steps):
+        moe.layer_host(*args_l, idx_h[i % N_INPUTS], wt_h[i % N_INPUTS], x_h[i % N_INPUTS],
+                       wl.host_tables, out_h, CFG["act"], CFG["act_a"], CFG["act_b"])
+    e2e_s = time.perf_counter() - t0
+    for arr in x_h + [out_h]:
+        moe.host_unregister(arr)
+    sweep = {}
+    if not args.no_sweep:
+        for bb in (1, 8, 32):
+            wb = Workload.__new__(Workload)
+            wb.__dict__.update({k: v for k, v in wl.__dict__.items()
+                                if k not in ("inputs", "out", "ws", "B")})
+            wb.B = bb
+            g = torch.Generator(device="cuda").manual_seed(99 + bb)
+            wb.inputs = []
+            for _ in range(N_INPUTS):
+                choice = torch.rand((bb, CFG["E"]), generator=g, device="cuda")
+                vals, idx = torch.topk(choice, CFG["K"], dim=1)
+                wt = (vals / vals.sum(dim=1, keepdim=True)).float()
+                x = torch.randn((bb, CFG["D"]), generator=g, device="cuda").to(torch.bfloat16)
+                wb.inputs.append((idx.int().contiguous(), wt.contiguous(), x))
+            wb.out = torch.zeros((bb, CFG["D"]), dtype=torch.float32, device="cuda")
+            wb.ws = torch.empty(moe.layer_workspace_bytes(bb, CFG["K"], CFG["E"], CFG["n_shared"],
+                                                          CFG["D"], CFG["I"], CFG["fmt"]),
+                                dtype=torch.uint8, device="cuda")
+            tps, mstep = graph_throughput(moe, torch, wb, 320, 32)
+            touched = [len(set(i.flatten().tolist())) + CFG["n_shared"] for (i, _, _) in wb.inputs]
+            nb = sum(touched) / len(touched) * EXPERT_BYTES + bb * CFG["D"] * 6
+            sweep[f"B{bb}"] = {"tokens_per_s": tps, "ms_per_step": mstep,
+                               "algorithmic_bytes_per_step": nb,
+                               "hbm_gbs": nb / (mstep / 1e3) / 1e9,
+                               "hbm_frac_of_step": nb / (mstep / 1e3) / 1e9 / peak}
+    EE = CFG["E"] + CFG["n_shared"]
+    return {
+        "workload": "config[1] MXFP4 decode MoE block: hidden 7168, inter 2048, 256 experts "
+                    "top-8 + 1 shared, SiTU(4,25), bf16 activations",
+        "batch": B, "tokens_per_s": B / (ms / 1e3), "ms_per_step": ms, "steps": steps,
+        "roofline": {"bound": "hbm", "kernel": "decode_ffn (expert phase 1 + phase 2)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None if ratio is None else ratio * alg_bytes,
+                     "traffic_source": "DRAM/algorithmic ratio of the committed ncu summary "
+                                       "profiles/decode_ffn_config1.txt (64-expert capture, "
+                                       "scaled), not measured in this run",
+                     "algorithmic_bytes_per_step": alg_bytes, "kernel_ms_per_step": k_ms},
+        "phases_ms_per_step": {k: v[0] / steps for k, v in phases.items()},
+        "e2e": {"value": B * args.e2e_steps / e2e_s, "unit": "tokens/s",
+                "h2d_bytes_per_step": 6 * EE * 8 + 2 * B * CFG["K"] * 4 + 2 * B * CFG["D"] * 4,
+                "d2h_bytes_per_step": B * CFG["D"] * 4, "api": "mvllm_moe_layer_host",
+                "host_buffers": "caller x / out page-locked with mvllm_moe_host_register"},
+        "sweep": sweep, "_workload": wl,
+    }
 
 
 if __name__ == "__main__":

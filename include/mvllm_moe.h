@@ -120,6 +120,11 @@ MVLLM_API const char *mvllm_moe_last_error(void);   /* text of the last failure 
  * effect. */
 MVLLM_API int mvllm_moe_set_prefill_mode(int mode);
 MVLLM_API int mvllm_moe_get_prefill_mode(void);
+/* SMs the layer's persistent expert kernels fill (0: all, the default).  No
+ * counterpart in the reference: a caller that overlaps an NCCL exchange on
+ * another stream with the expert kernels (the chunked expert-parallel step)
+ * leaves it SMs.  Process-wide; takes effect at the next launch. */
+MVLLM_API int mvllm_moe_set_sm_limit(int sms);
 /* The block-scaled modes' token operand, on its own (no counterpart in the
  * reference): f16 rows src [rows, K] (K % 32 == 0) as the mode's n terms,
  * planes [n][rows][K/2] packed e2m1 (low nibble = even element; MXF4 modes)

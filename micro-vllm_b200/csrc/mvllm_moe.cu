@@ -49,6 +49,7 @@ struct Context {
     bool inited = false;
     int device = -1;
     int sms = 0;
+    int sm_limit = 0; // SMs the persistent expert kernels may fill (0: all)
     cudaStream_t stream = nullptr;
     cudaEvent_t ev[4] = {};
     DevBuf ws;        // workspace of the host-pointer entries
@@ -71,6 +72,13 @@ struct Context {
 Context &ctx() {
     static Context c;
     return c;
+}
+
+// SMs the layer's persistent kernels are sized for: all of them, or the
+// limit a caller set to leave SMs to concurrent work (an NCCL exchange on
+// another stream that should overlap the expert kernels).
+int launch_sms(const Context &c) {
+    return c.sm_limit > 0 ? std::max(2, std::min(c.sms, c.sm_limit)) : c.sms;
 }
 
 thread_local std::string g_last_error;
@@ -1075,6 +1083,15 @@ int mvllm_moe_set_prefill_mode(int mode) {
 
 int mvllm_moe_get_prefill_mode(void) { return prefill_mode(); }
 
+int mvllm_moe_set_sm_limit(int sms) {
+    if (sms < 0)
+        return fail(MVLLM_ERR_INVALID, "set_sm_limit: negative SM count");
+    Context &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    c.sm_limit = sms;
+    return MVLLM_OK;
+}
+
 
 int mvllm_moe_mma_rate(int kind, int n, int pair, int iters, double *tflops) {
     if (kind < 0 || kind > 2 || n < 16 || n > 256 || n % 16 || iters < 1 || !tflops ||
@@ -1105,7 +1122,7 @@ int mvllm_mx_terms_dev(void *stream, int mode, const void *src, int rows, int K,
         std::lock_guard<std::mutex> lk(c.mu);
         if (int rc = ensure_current(c))
             return rc;
-        sms = c.sms;
+        sms = launch_sms(c);
     }
     return launch_terms(mode, src, rows, K, static_cast<uint8_t *>(planes),
                         static_cast<uint8_t *>(codes), static_cast<cudaStream_t>(stream), sms);
@@ -1572,13 +1589,13 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     auto run_batch = [&](void *const *t) -> int {
         Tables tb{t, t + nb, t + 2 * nb, t + 3 * nb, t + 4 * nb, t + 5 * nb};
         if (fast)
-            return run_experts(c.stream, c.sms, nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
+            return run_experts(c.stream, launch_sms(c), nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
                                MVLLM_DTYPE_F32, int(x_rows), false, R / n_valid, act, act_a,
                                act_b, w, allow_tc);
         // Generic path reads the uploaded f32 rows directly.
         RunWs w2 = w;
         w2.xs = const_cast<float *>(d_x);
-        return run_experts(c.stream, c.sms, nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
+        return run_experts(c.stream, launch_sms(c), nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
                            MVLLM_DTYPE_F32, int(x_rows), true, R / n_valid, act, act_a, act_b,
                            w2);
     };
@@ -1684,7 +1701,7 @@ int mvllm_moe_block_dev(void *stream, int nb, int D, int Iinter, int fmt, const 
         std::lock_guard<std::mutex> lk(c.mu);
         if (int rc = ensure_current(c))
             return rc;
-        sms = c.sms;
+        sms = launch_sms(c);
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const bool fast = fast_path_ok(fmt, D, Iinter);
@@ -1784,7 +1801,7 @@ int mvllm_moe_permute_dev(void *stream, const int *idx, const float *wt, int T, 
         std::lock_guard<std::mutex> lk(c.mu);
         if (int rc = ensure_current(c))
             return rc;
-        sms = c.sms;
+        sms = launch_sms(c);
     }
     Carve cv(workspace, workspace_bytes);
     PermWs p{};
@@ -1982,7 +1999,7 @@ int mvllm_moe_layer_dev(void *stream, int T, int K, int E, int n_shared, int D, 
         std::lock_guard<std::mutex> lk(c.mu);
         if (int rc = ensure_current(c))
             return rc;
-        sms = c.sms;
+        sms = launch_sms(c);
     }
     Carve cv(workspace, workspace_bytes);
     LayerWs l{};
@@ -2016,7 +2033,7 @@ int mvllm_moe_layer_partial_dev(void *stream, int T, int K, int E, int n_shared,
         std::lock_guard<std::mutex> lk(c.mu);
         if (int rc = ensure_current(c))
             return rc;
-        sms = c.sms;
+        sms = launch_sms(c);
     }
     Carve cv(workspace, workspace_bytes);
     LayerWs l{};
@@ -2148,7 +2165,7 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
         CUDA_TRY(cudaMemcpyAsync(dout, hout, x_b, cudaMemcpyHostToDevice, c.stream));
         return MVLLM_OK;
     };
-    if (int rc = layer_dev_impl(c.stream, c.sms, T, K, E, n_shared, D, Iinter, fmt,
+    if (int rc = layer_dev_impl(c.stream, launch_sms(c), T, K, E, n_shared, D, Iinter, fmt,
                                 reinterpret_cast<const int *>(dptr(hidx)),
                                 reinterpret_cast<const float *>(dptr(hwt)), dptr(hx),
                                 MVLLM_DTYPE_F32, tb, dout, act, act_a, act_b, l, allow_tc, &hooks)) {

@@ -186,6 +186,15 @@ class CudaOps:
         else:
             moe.ep_combine_dev(back, pos, out)
 
+    def set_sm_reserve(self, n):
+        """Leave n SMs out of the expert kernels (0: use them all)."""
+        if n <= 0:
+            moe.set_sm_limit(0)
+        else:
+            sms = self.torch.cuda.get_device_properties(
+                self.torch.cuda.current_device()).multi_processor_count
+            moe.set_sm_limit(max(2, sms - n))
+
 
 class EPLayer:
     """The layer step of one rank; `ops` holds the device steps."""
@@ -200,6 +209,67 @@ class EPLayer:
 
     def pack(self, x, idx, wt, pos, send_splits):
         return self.ops.pack(x, idx, wt, pos, int(sum(send_splits)))
+
+    def forward_chunked(self, x, idx, wt, out, dist, chunks=2, group=None, sm_reserve=16):
+        """The step in `chunks` slices of the rank's tokens, pipelined so the
+        exchanges overlap the expert kernels: the dispatches of every slice
+        are queued at once (NCCL runs them on its own stream), slice c's
+        experts start when its dispatch has landed, and its return starts as
+        soon as its experts finish, under slice c + 1's experts.  The expert
+        kernels leave `sm_reserve` SMs to NCCL meanwhile.  All slices' counts
+        go in one exchange (one host synchronisation per step).  Same
+        results as `forward`: every row is computed by the same kernels and
+        combined in the same order per slice."""
+        t = self.ops.torch
+        T = x.shape[0]
+        C = max(1, min(chunks, T))
+        cuts = [T * c // C for c in range(C + 1)]
+        sl = [slice(cuts[c], cuts[c + 1]) for c in range(C)]
+        plans = [self.prepare(x[s], idx[s], wt[s]) for s in sl]
+        N = self.nranks
+        cnt = t.stack([p[1] for p in plans], dim=1).reshape(-1)  # destination-major [N, C]
+        rcnt = t.empty_like(cnt)
+        dist.all_to_all_single(rcnt, cnt, group=group)
+        sc_all = [int(v) for v in cnt.tolist()]
+        rc_all = [int(v) for v in rcnt.tolist()]
+        sc = [[sc_all[d * C + c] for d in range(N)] for c in range(C)]  # sc[c][d]
+        rc = [[rc_all[s * C + c] for s in range(N)] for c in range(C)]  # rc[c][s]
+        recv, works = [], []
+        for c in range(C):
+            sx, sidx, swt = self.pack(x[sl[c]], idx[sl[c]], wt[sl[c]], plans[c][0], sc[c])
+            R = sum(rc[c])
+            rx = t.empty((R, self.D), dtype=x.dtype, device=x.device)
+            ridx = t.empty((R, self.K), dtype=t.int32, device=x.device)
+            rwt = t.empty((R, self.K), dtype=t.float32, device=x.device)
+            works.append([dist.all_to_all_single(rx, sx, rc[c], sc[c], group=group,
+                                                 async_op=True),
+                          dist.all_to_all_single(ridx, sidx, rc[c], sc[c], group=group,
+                                                 async_op=True),
+                          dist.all_to_all_single(rwt, swt, rc[c], sc[c], group=group,
+                                                 async_op=True)])
+            recv.append((rx, ridx, rwt, sx, sidx, swt))
+        backs = []
+        lim = getattr(self.ops, "set_sm_reserve", None)
+        if lim and N > 1:
+            lim(sm_reserve)
+        try:
+            for c in range(C):
+                for w in works[c]:
+                    w.wait()
+                rx, ridx, rwt = recv[c][:3]
+                part = self.ops.compute(rx, ridx, rwt)
+                back = t.empty((sum(sc[c]),) + tuple(part.shape[1:]), dtype=part.dtype,
+                               device=x.device)
+                backs.append((back, part, dist.all_to_all_single(back, part, sc[c], rc[c],
+                                                                 group=group, async_op=True)))
+        finally:
+            if lim and N > 1:
+                lim(0)
+        for c in range(C):
+            back, _, w = backs[c]
+            w.wait()
+            self.ops.combine(back, plans[c][0], out[sl[c]])
+        return {"sent_rows": sum(sum(v) for v in sc), "received_rows": sum(sum(v) for v in rc)}
 
     def forward(self, x, idx, wt, out, dist, group=None, timing=None):
         """One step through torch.distributed (all ranks call it in step).

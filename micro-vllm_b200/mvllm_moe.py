@@ -49,7 +49,7 @@ C_SYMBOLS = (
     "mvllm_moe_host_unregister", "mvllm_moe_route_ex_dev", "mvllm_moe_ep_local_ids_dev",
     "mvllm_moe_dense_ffn_workspace", "mvllm_moe_dense_ffn_dev", "mvllm_moe_wait_selftest",
     "mvllm_moe_set_prefill_mode", "mvllm_moe_get_prefill_mode", "mvllm_mx_terms_dev",
-    "mvllm_moe_mma_rate",
+    "mvllm_moe_mma_rate", "mvllm_moe_set_sm_limit",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -123,6 +123,7 @@ def lib():
             "mvllm_moe_get_prefill_mode": (i, []),
             "mvllm_mx_terms_dev": (i, [vp, i, vp, i, i, vp, vp]),
             "mvllm_moe_mma_rate": (i, [i, i, i, i, vp]),
+            "mvllm_moe_set_sm_limit": (i, [i]),
             "mvllm_moe_dense_ffn_dev": (i, [vp, i, i, i, i] + [vp] * 7 + [i, f, f, vp, i, vp,
                                                                          sz]),
         }
@@ -163,6 +164,11 @@ def set_prefill_mode(mode) -> None:
 
 def get_prefill_mode() -> int:
     return int(lib().mvllm_moe_get_prefill_mode())
+
+
+def set_sm_limit(sms: int) -> None:
+    """SMs the persistent expert kernels fill (0: all)."""
+    _check(lib().mvllm_moe_set_sm_limit(int(sms)))
 
 
 def mma_rate(kind, n, pair, iters=20000) -> float:

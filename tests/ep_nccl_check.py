@@ -1,7 +1,9 @@
 """Two-rank expert-parallel check over NCCL (launched by tests/test_ep_gpu.py
 through torchrun, one rank per GPU): each rank holds half of the experts
-(strided), runs its tokens through ep.EPLayer.forward, and rank 0 compares the
-gathered output with the single-GPU layer over all tokens and experts.
+(strided), runs its tokens through ep.EPLayer.forward (and the chunked,
+overlapped forward_chunked, which must give the same bits), and rank 0
+compares the gathered output with the single-GPU layer over all tokens and
+experts.
 Prints EP-NCCL-OK on success."""
 import os
 import sys
@@ -55,10 +57,14 @@ def main():
     layer.forward(x, idx, wt, out, dist)
     again = torch.zeros_like(out)
     layer.forward(x, idx, wt, again, dist)
+    # The chunked step (exchanges on NCCL's stream overlapping the expert
+    # kernels, which leave SMs free meanwhile): the same bits.
+    sliced = torch.zeros_like(out)
+    layer.forward_chunked(x, idx, wt, sliced, dist, chunks=2)
     torch.cuda.synchronize()
     gathered = [torch.zeros_like(out) for _ in range(world)]
     dist.all_gather(gathered, out)
-    ok = torch.equal(out, again)
+    ok = torch.equal(out, again) and torch.equal(out, sliced)
     if rank == 0:
         tabs_all, keep_all = tables_of(c["experts"])
         ref = torch.zeros((world * T_LOC, D), device="cuda")

@@ -119,11 +119,18 @@ def _gloo_rank(rank, nranks, port_no, T_loc, out_dir):
     c, _ = layer(port, nranks * T_loc)
     sl = slice(rank * T_loc, (rank + 1) * T_loc)
     L = ep.EPLayer(rank_ops(port, c, rank, nranks), rank, nranks, CASE["D"], CASE["K"])
+    args = (torch.from_numpy(np.ascontiguousarray(c["x"][sl])),
+            torch.from_numpy(np.ascontiguousarray(c["idx"][sl])),
+            torch.from_numpy(np.ascontiguousarray(c["wt"][sl])))
     out = torch.zeros((T_loc, CASE["D"]))
-    L.forward(torch.from_numpy(np.ascontiguousarray(c["x"][sl])),
-              torch.from_numpy(np.ascontiguousarray(c["idx"][sl])),
-              torch.from_numpy(np.ascontiguousarray(c["wt"][sl])), out, dist)
+    L.forward(*args, out, dist)
     np.save(os.path.join(out_dir, f"out{rank}.npy"), out.numpy())
+    # The chunked step (exchanges queued per slice, overlapping the experts
+    # on a GPU): the same rows through the same computation, slice by slice.
+    for chunks in (2, 3):
+        outc = torch.zeros((T_loc, CASE["D"]))
+        L.forward_chunked(*args, outc, dist, chunks=chunks)
+        np.save(os.path.join(out_dir, f"out{rank}_c{chunks}.npy"), outc.numpy())
     dist.barrier()
     dist.destroy_process_group()
 
@@ -146,6 +153,9 @@ def test_ep_two_gloo_ranks(port, tmp_path):
     got = np.concatenate([np.load(tmp_path / f"out{r}.npy") for r in range(N)])
     _, want = layer(port, N * T_loc)
     assert_close(got, want, "2 gloo ranks EP")
+    for chunks in (2, 3):
+        gc = np.concatenate([np.load(tmp_path / f"out{r}_c{chunks}.npy") for r in range(N)])
+        assert_close(gc, want, f"2 gloo ranks EP, {chunks} slices")
 
 
 def test_ep_plan_positions(port):
