@@ -61,7 +61,11 @@ def parse():
     ap.add_argument("--no-decode-configs", action="store_true",
                     help="skip the config[0] and config[2] decode legs")
     ap.add_argument("--ep-steps", type=int, default=20)
-    ap.add_argument("--ep-chunks", type=int, default=2,
+    ap.add_argument("--ep-mode", default="auto", choices=["auto", "compact", "fixed"],
+                    help="exchange segments sized by host counts (compact) or fixed (no host "
+                         "synchronisation; auto: fixed up to 4 GPUs, where nearly every token "
+                         "goes to every rank, compact above)")
+    ap.add_argument("--ep-chunks", type=int, default=1,
                     help="token slices per expert-parallel step (N > 1): the exchanges of one "
                          "slice overlap the experts of another")
     ap.add_argument("--no-dsv4", action="store_true",
@@ -656,7 +660,7 @@ def ep_routing(torch, name, T, K, seed):
 
 
 def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=None, e2e_steps=0,
-             chunks=1):
+             chunks=1, ep_mode="compact"):
     """Config[4]: 384 MXFP4 experts sharded over the ranks (expert e on rank
     e % world), top-8; uniform and Zipf s=1.1 routing.  Weights are drawn per
     global expert id, so the model is the same whatever the rank count.
@@ -672,7 +676,9 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
     `e2e_steps` the same step also runs from host buffers (pinned x, idx, wt
     copied in, out copied back inside the timed region).  With `chunks` > 1
     (N > 1) each step runs as that many token slices whose exchanges overlap
-    the expert kernels (EPLayer.forward_chunked)."""
+    the expert kernels (EPLayer.forward_chunked); with `ep_mode` "fixed" the
+    exchanges use fixed-size segments and no counts reach the host
+    (EPLayer.forward_fixed)."""
     import ep
     D, I, K = CFG["D"], CFG["I"], CFG["K"]
     u8 = torch.uint8
@@ -734,6 +740,8 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
 
         def step(xx=x, ii=idx, ww=wt, oo=out):
             oo.zero_()
+            if world > 1 and ep_mode == "fixed":
+                return layer.forward_fixed(xx, ii, ww, oo, dist)
             if world > 1 and chunks > 1:
                 return layer.forward_chunked(xx, ii, ww, oo, dist, chunks=chunks)
             if world > 1:
@@ -818,6 +826,7 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
                         "bf16 activations; NCCL all-to-all dispatch and return",
             "n_gpus": world, "scaling": "weak" if weak else "strong", "tokens_per_step": T_all,
             "slices_per_step": chunks if world > 1 else 1,
+            "exchange": ep_mode if world > 1 else "none (one rank)",
             **res}
 
 
@@ -1055,8 +1064,10 @@ def main():
     # scaling: 8192 tokens per step over all ranks), uniform routing; the Zipf
     # run and, at N > 1, weak scaling beside it.
     clk = ClockSampler(local_rank)
+    if args.ep_mode == "auto":
+        args.ep_mode = "fixed" if world <= 4 else "compact"
     ep_res = ep_bench(moe, torch, dist, rank, world, args.steps, args.warmup, clk=clk,
-                      e2e_steps=args.e2e_steps, chunks=args.ep_chunks)
+                      e2e_steps=args.e2e_steps, chunks=args.ep_chunks, ep_mode=args.ep_mode)
     uni = ep_res["uniform"]
     value, ms = uni["tokens_per_s"], uni["ms_per_step"]
     flops = 2.0 * EP_T * CFG["K"] * 3 * CFG["D"] * CFG["I"]  # per step, all ranks
@@ -1071,7 +1082,8 @@ def main():
     achieved = flops / world / (e_ms / 1e3) / 1e12
     if world > 1:
         ep_res["weak_scaling"] = ep_bench(moe, torch, dist, rank, world, args.ep_steps,
-                                          args.warmup, weak=True, chunks=args.ep_chunks)
+                                          args.warmup, weak=True, chunks=args.ep_chunks,
+                                          ep_mode=args.ep_mode)
 
     # ---- config[1] decode (N = 1): the HBM-bound path -------------------------
     decode = None

@@ -346,6 +346,14 @@ MVLLM_API int mvllm_moe_route_ex_dev(void *stream, const void *x, int x_dtype, i
  * destination.  nranks <= 32. */
 MVLLM_API int mvllm_moe_ep_plan_dev(void *stream, const int *idx, int T, int K, int E, int nranks,
                                     const int *dest, int self_rank, int *pos, int *send_cnt);
+/* The plan with fixed-size send segments (no counterpart in the reference):
+ * destination d's rows start at d * capacity (capacity >= T: a token goes to
+ * a rank at most once), so every rank sends and receives nranks * capacity
+ * rows and the exchange needs no counts on the host.  Rows of a segment past
+ * send_cnt[d] carry no token: the caller sets their send_idx to -1. */
+MVLLM_API int mvllm_moe_ep_plan_fixed_dev(void *stream, const int *idx, int T, int K, int E,
+                                          int nranks, const int *dest, int self_rank,
+                                          int capacity, int *pos, int *send_cnt);
 /* Fills the send buffer from the plan: send_x[p] = x[c] (x_dtype rows of D,
  * D a multiple of 8), send_idx[p, k] = local id of idx[c, k] when rank d
  * serves it else -1, send_wt[p, k] = wt[c, k]. */

@@ -66,10 +66,12 @@ struct PlanArgs {
     // tc_min <= 0 disables the path.
     int tc_min, tc_small, tc_blocks1, tc_blocks2, tc_sblocks1, tc_sblocks2;
     int tc_shift; // pair token tiles of 2^tc_shift rows
+    int *clear_word; // zeroed once the plan is written (the tensor-map "rewritten" flag)
     int *toff1, *toff2, *soff1, *soff2;
 };
 
 __global__ void plan_kernel(const PlanArgs a) {
+    pdl_wait();
     __shared__ int warp_sums[32];
     __shared__ int carry[7];
     if (threadIdx.x < 7)
@@ -149,6 +151,8 @@ __global__ void plan_kernel(const PlanArgs a) {
         __syncthreads();
     }
     if (threadIdx.x == 0) {
+        if (a.clear_word)
+            *a.clear_word = 0;
         a.off1[a.nb] = carry[1];
         a.off2[a.nb] = carry[2];
         a.toff1[a.nb] = carry[3];
@@ -181,6 +185,7 @@ using TmapTemplates = TmapSet<kTmapsPerExpert>;
 template <int N>
 __global__ void build_tmaps_kernel(const __grid_constant__ TmapSet<N> tpl, const TableSet<N> tabs,
                                    int nb, uint8_t *__restrict__ out, int *dirty) {
+    pdl_wait();
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= nb * N)
         return;
@@ -254,6 +259,7 @@ template <typename TIn>
 __global__ void stage_rows_f16x8_kernel(const TIn *__restrict__ x, const int *__restrict__ index,
                                         const int *__restrict__ nrows_dev, int nrows_host, int D,
                                         int fmt, __half *__restrict__ out, int *err) {
+    pdl_wait();
     const int nrows = nrows_dev ? *nrows_dev : nrows_host;
     const int chunks = D >> 3;
     for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
@@ -416,6 +422,7 @@ __global__ void __launch_bounds__(1024)
                          int *__restrict__ xoff, int *__restrict__ n_rows,
                          int *__restrict__ rows, float *__restrict__ rw,
                          int *__restrict__ tok_pos) {
+    pdl_wait();
     __shared__ int warp_sums[32];
     const int EE = E + n_shared, KK = K + n_shared;
     for (int i = threadIdx.x; i < EE * words; i += blockDim.x)
@@ -498,6 +505,7 @@ __global__ void __launch_bounds__(1024)
 __global__ void combine_tokens_kernel(float *__restrict__ out, const float *__restrict__ y,
                                       const float *__restrict__ rw,
                                       const int *__restrict__ tok_pos, int T, int KK, int D) {
+    pdl_wait();
     constexpr int kB = 4; // rows loaded per batch
     for (int c = blockIdx.y; c < T; c += gridDim.y) {
         int pos[17];

@@ -30,6 +30,13 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream serialization attribute may start while the kernel before it on the
+// stream is still finishing; it waits here, before reading anything that
+// kernel wrote, until the earlier grid has completed and its writes are
+// visible.  Without the attribute this returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Records the first error code of a launch (later codes do not overwrite it).
 __device__ __forceinline__ void set_error(int *err, int code) {
     if (err)

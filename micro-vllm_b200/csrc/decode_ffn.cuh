@@ -304,6 +304,7 @@ template <int NT> __device__ __forceinline__ DecodeItem finish_item(const Decode
 
 template <int FMT, int PHASE, int KS, int NT>
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const DecodeArgs p) {
+    pdl_wait();
     static_assert(KS == 256 || KS == 512, "stage K-slice");
     using L = DecodeLayout<FMT, KS, NT>;
     extern __shared__ uint8_t smem_raw[];

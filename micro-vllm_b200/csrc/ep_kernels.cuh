@@ -62,9 +62,11 @@ __global__ void ep_local_ids_kernel(const int *__restrict__ idx, int n, int E, i
 // One CTA: per destination rank a block scan over the tokens gives the
 // position of each sent token among those of that rank; a second pass adds the
 // destination offsets.  pos[c * nranks + d] = send-buffer row or -1.
+// cap > 0: destination d's rows start at d * cap (fixed-size send segments,
+// so the exchange needs no counts on the host); else right after d - 1's.
 __global__ void ep_plan_kernel(const int *__restrict__ idx, int T, int K, int E, int nranks,
                                const int *__restrict__ dest, int self, int *__restrict__ pos,
-                               int *__restrict__ send_cnt) {
+                               int *__restrict__ send_cnt, int cap) {
     __shared__ int warp_sums[32];
     __shared__ int carry[32];
     __shared__ int off[33];
@@ -96,7 +98,7 @@ __global__ void ep_plan_kernel(const int *__restrict__ idx, int T, int K, int E,
         off[0] = 0;
         for (int d = 0; d < nranks; ++d) {
             send_cnt[d] = carry[d];
-            off[d + 1] = off[d] + carry[d];
+            off[d + 1] = cap > 0 ? (d + 1) * cap : off[d] + carry[d];
         }
     }
     __syncthreads();

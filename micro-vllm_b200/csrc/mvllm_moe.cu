@@ -116,6 +116,25 @@ void prof_mark(cudaStream_t st, int phase) {
     p.marks.push_back({e, phase});
 }
 
+// A launch that may begin while the previous kernel on the stream finishes
+// (programmatic dependent launch): the kernel waits in pdl_wait() before it
+// reads that kernel's results, so only launch latency is overlapped.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 int fail(int code, const char *fmt, ...) {
     char buf[512];
     va_list ap;
@@ -607,8 +626,7 @@ int launch_decode_t(DecodeArgs a, cudaStream_t st, int sms) {
         per_sm = std::max(occ, 1);
     }
     a.nstages = ns;
-    kern<<<sms * std::max(per_sm, 1), kDecodeThreads, smem, st>>>(a);
-    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(launch_pdl(kern, dim3(sms * std::max(per_sm, 1)), dim3(kDecodeThreads), smem, st, a));
     return MVLLM_OK;
 }
 
@@ -663,8 +681,8 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     pa.tc_sblocks1 = I / tc_cols_per_item<1, false>();
     pa.tc_sblocks2 = D / tc_cols_per_item<2, false>();
     pa.toff1 = w.toff1, pa.toff2 = w.toff2, pa.soff1 = w.soff1, pa.soff2 = w.soff2;
-    plan_kernel<<<1, 1024, 0, st>>>(pa);
-    CUDA_TRY(cudaGetLastError());
+    pa.clear_word = fast ? w.tmaps_dirty : nullptr;
+    CUDA_TRY(launch_pdl(plan_kernel, dim3(1), dim3(1024), 0, st, pa));
     prof_mark(st, kPhPlan);
 
     const void *xop = x;
@@ -672,13 +690,17 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
         if (fast) {
             const int blocks = std::max(1, std::min(x_rows, 8 * sms));
             if (x_dtype == MVLLM_DTYPE_BF16)
-                stage_rows_f16x8_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
-                    static_cast<const __nv_bfloat16 *>(x), nullptr, nullptr, x_rows, D, fmt,
-                    static_cast<__half *>(w.xs), w.err);
+                CUDA_TRY(launch_pdl(stage_rows_f16x8_kernel<__nv_bfloat16>, dim3(blocks), dim3(256),
+                                    0, st, static_cast<const __nv_bfloat16 *>(x),
+                                    static_cast<const int *>(nullptr),
+                                    static_cast<const int *>(nullptr), x_rows, D, fmt,
+                                    static_cast<__half *>(w.xs), w.err));
             else
-                stage_rows_f16x8_kernel<float><<<blocks, 256, 0, st>>>(
-                    static_cast<const float *>(x), nullptr, nullptr, x_rows, D, fmt,
-                    static_cast<__half *>(w.xs), w.err);
+                CUDA_TRY(launch_pdl(stage_rows_f16x8_kernel<float>, dim3(blocks), dim3(256), 0, st,
+                                    static_cast<const float *>(x),
+                                    static_cast<const int *>(nullptr),
+                                    static_cast<const int *>(nullptr), x_rows, D, fmt,
+                                    static_cast<__half *>(w.xs), w.err));
             CUDA_TRY(cudaGetLastError());
             xop = w.xs;
         } else if (x_dtype == MVLLM_DTYPE_BF16) {
@@ -697,11 +719,11 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
         if (int rc = make_templates(&tpl, fmt, D, I, pick_ks(D), pick_ks(I), w.y, &box3d))
             return rc;
         const int nmaps = nb * kTmapsPerExpert;
-        CUDA_TRY(cudaMemsetAsync(w.tmaps_dirty, 0, sizeof(int), st));
-        build_tmaps_kernel<kTmapsPerExpert><<<(nmaps + 127) / 128, 128, 0, st>>>(
-            tpl, TableSet<kTmapsPerExpert>{{tb.g, tb.u, tb.d, tb.gs, tb.us, tb.ds}}, nb, w.tmaps,
-            w.tmaps_dirty);
-        CUDA_TRY(cudaGetLastError());
+        // (the plan kernel cleared w.tmaps_dirty)
+        CUDA_TRY(launch_pdl(build_tmaps_kernel<kTmapsPerExpert>, dim3((nmaps + 127) / 128),
+                            dim3(128), 0, st, tpl,
+                            TableSet<kTmapsPerExpert>{{tb.g, tb.u, tb.d, tb.gs, tb.us, tb.ds}}, nb,
+                            w.tmaps, w.tmaps_dirty));
         CUtensorMap tok1{}, tok2{}, tsc1{}, tsc2{};
         TcArgs t1{};
         const int kind = mode_kind(mode), nterm = mx ? mode_nterm(mode) : 0;
@@ -1936,13 +1958,16 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
     if (fast) {
         const int vblocks = std::max(1, std::min(R, 8 * sms));
         if (x_dtype == MVLLM_DTYPE_BF16)
-            stage_rows_f16x8_kernel<__nv_bfloat16><<<vblocks, 256, 0, st>>>(
-                static_cast<const __nv_bfloat16 *>(x), l.rows, l.n_rows, 0, D, fmt,
-                static_cast<__half *>(l.run.xs), l.run.err);
+            CUDA_TRY(launch_pdl(stage_rows_f16x8_kernel<__nv_bfloat16>, dim3(vblocks), dim3(256), 0,
+                                st, static_cast<const __nv_bfloat16 *>(x),
+                                static_cast<const int *>(l.rows),
+                                static_cast<const int *>(l.n_rows), 0, D, fmt,
+                                static_cast<__half *>(l.run.xs), l.run.err));
         else
-            stage_rows_f16x8_kernel<float><<<vblocks, 256, 0, st>>>(
-                static_cast<const float *>(x), l.rows, l.n_rows, 0, D, fmt,
-                static_cast<__half *>(l.run.xs), l.run.err);
+            CUDA_TRY(launch_pdl(stage_rows_f16x8_kernel<float>, dim3(vblocks), dim3(256), 0, st,
+                                static_cast<const float *>(x), static_cast<const int *>(l.rows),
+                                static_cast<const int *>(l.n_rows), 0, D, fmt,
+                                static_cast<__half *>(l.run.xs), l.run.err));
     } else {
         if (x_dtype == MVLLM_DTYPE_BF16)
             stage_rows_kernel<__nv_bfloat16, float><<<gblocks, 256, 0, st>>>(
@@ -1971,7 +1996,9 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
                                                                          l.tok_pos, T, KK, D);
     } else {
         dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
-        combine_tokens_kernel<<<grid, 256, 0, st>>>(out, w.y, l.rw, l.tok_pos, T, KK, D);
+        CUDA_TRY(launch_pdl(combine_tokens_kernel, grid, dim3(256), 0, st, out,
+                            static_cast<const float *>(w.y), static_cast<const float *>(l.rw),
+                            static_cast<const int *>(l.tok_pos), T, KK, D));
     }
     CUDA_TRY(cudaGetLastError());
     prof_mark(st, kPhCombine);
@@ -2279,7 +2306,20 @@ int mvllm_moe_ep_plan_dev(void *stream, const int *idx, int T, int K, int E, int
         self_rank < 0 || self_rank >= nranks)
         return fail(MVLLM_ERR_INVALID, "ep_plan_dev: invalid arguments");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    ep_plan_kernel<<<1, 1024, 0, st>>>(idx, T, K, E, nranks, dest, self_rank, pos, send_cnt);
+    ep_plan_kernel<<<1, 1024, 0, st>>>(idx, T, K, E, nranks, dest, self_rank, pos, send_cnt, 0);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+int mvllm_moe_ep_plan_fixed_dev(void *stream, const int *idx, int T, int K, int E, int nranks,
+                                const int *dest, int self_rank, int capacity, int *pos,
+                                int *send_cnt) {
+    if (!idx || !pos || !send_cnt || T < 0 || K < 1 || E < 1 || nranks < 1 || nranks > 32 ||
+        self_rank < 0 || self_rank >= nranks || capacity < T)
+        return fail(MVLLM_ERR_INVALID, "ep_plan_fixed_dev: invalid arguments");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    ep_plan_kernel<<<1, 1024, 0, st>>>(idx, T, K, E, nranks, dest, self_rank, pos, send_cnt,
+                                       capacity);
     CUDA_TRY(cudaGetLastError());
     return MVLLM_OK;
 }

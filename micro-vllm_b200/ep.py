@@ -150,10 +150,24 @@ class CudaOps:
         moe.ep_plan_dev(idx, self.E, self.nranks, pos, cnt, self.dest, self.rank)
         return pos, cnt
 
-    def pack(self, x, idx, wt, pos, rows):
+    def plan_fixed(self, idx, capacity):
+        T = idx.shape[0]
+        pos = self.torch.empty((T, self.nranks), dtype=self.torch.int32, device=idx.device)
+        cnt = self.torch.empty(self.nranks, dtype=self.torch.int32, device=idx.device)
+        moe.ep_plan_fixed_dev(idx, self.E, self.nranks, capacity, pos, cnt, self.dest, self.rank)
+        return pos, cnt
+
+    def pack_fixed(self, x, idx, wt, pos, rows):
+        """pack() into segments of a fixed size: rows without a token keep
+        send_idx -1 (no expert), so the receiver skips them."""
+        send_x, send_idx, send_wt = self.pack(x, idx, wt, pos, rows, fill_idx=True)
+        return send_x, send_idx, send_wt
+
+    def pack(self, x, idx, wt, pos, rows, fill_idx=False):
         t = self.torch
         send_x = t.empty((rows, self.D), dtype=x.dtype, device=x.device)
-        send_idx = t.empty((rows, self.K), dtype=t.int32, device=x.device)
+        send_idx = (t.full((rows, self.K), -1, dtype=t.int32, device=x.device) if fill_idx else
+                    t.empty((rows, self.K), dtype=t.int32, device=x.device))
         send_wt = t.empty((rows, self.K), dtype=t.float32, device=x.device)
         if rows:
             moe.ep_pack_dev(x, idx, wt, self.E, self.nranks, pos, send_x, send_idx, send_wt,
@@ -209,6 +223,29 @@ class EPLayer:
 
     def pack(self, x, idx, wt, pos, send_splits):
         return self.ops.pack(x, idx, wt, pos, int(sum(send_splits)))
+
+    def forward_fixed(self, x, idx, wt, out, dist, group=None):
+        """The step with fixed-size exchange segments: every rank sends each
+        destination `T` rows (a token goes to a rank at most once; rows
+        without a token carry expert ids -1), so no counts travel to the host
+        and the step never waits on the GPU from the CPU.  Costs the padding
+        rows' bytes on the links; the received rows without an expert cost
+        nothing in the expert kernels (their permutation skips them).  Same
+        results as `forward`."""
+        t = self.ops.torch
+        T = x.shape[0]
+        N = self.nranks
+        pos, _ = self.ops.plan_fixed(idx, T)
+        sx, sidx, swt = self.ops.pack_fixed(x, idx, wt, pos, N * T)
+        rx, ridx, rwt = t.empty_like(sx), t.empty_like(sidx), t.empty_like(swt)
+        dist.all_to_all_single(rx, sx, group=group)
+        dist.all_to_all_single(ridx, sidx, group=group)
+        dist.all_to_all_single(rwt, swt, group=group)
+        part = self.ops.compute(rx, ridx, rwt)
+        back = t.empty_like(part)
+        dist.all_to_all_single(back, part, group=group)
+        self.ops.combine(back, pos, out)
+        return {"sent_rows": N * T, "received_rows": N * T}
 
     def forward_chunked(self, x, idx, wt, out, dist, chunks=2, group=None, sm_reserve=16):
         """The step in `chunks` slices of the rank's tokens, pipelined so the

@@ -49,7 +49,7 @@ C_SYMBOLS = (
     "mvllm_moe_host_unregister", "mvllm_moe_route_ex_dev", "mvllm_moe_ep_local_ids_dev",
     "mvllm_moe_dense_ffn_workspace", "mvllm_moe_dense_ffn_dev", "mvllm_moe_wait_selftest",
     "mvllm_moe_set_prefill_mode", "mvllm_moe_get_prefill_mode", "mvllm_mx_terms_dev",
-    "mvllm_moe_mma_rate", "mvllm_moe_set_sm_limit",
+    "mvllm_moe_mma_rate", "mvllm_moe_set_sm_limit", "mvllm_moe_ep_plan_fixed_dev",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -124,6 +124,7 @@ def lib():
             "mvllm_mx_terms_dev": (i, [vp, i, vp, i, i, vp, vp]),
             "mvllm_moe_mma_rate": (i, [i, i, i, i, vp]),
             "mvllm_moe_set_sm_limit": (i, [i]),
+            "mvllm_moe_ep_plan_fixed_dev": (i, [vp, vp, i, i, i, i, vp, i, i, vp, vp]),
             "mvllm_moe_dense_ffn_dev": (i, [vp, i, i, i, i] + [vp] * 7 + [i, f, f, vp, i, vp,
                                                                          sz]),
         }
@@ -436,6 +437,15 @@ def ep_plan_dev(idx, E, nranks, pos, send_cnt, dest=None, self_rank=0, stream=No
     T, K = idx.shape
     _check(lib().mvllm_moe_ep_plan_dev(_stream(stream), _dp(idx), T, K, E, nranks, _dp(dest),
                                        self_rank, _dp(pos), _dp(send_cnt)))
+
+
+def ep_plan_fixed_dev(idx, E, nranks, capacity, pos, send_cnt, dest=None, self_rank=0,
+                      stream=None):
+    """The plan with destination d's rows at d * capacity (no host counts)."""
+    T, K = idx.shape
+    _check(lib().mvllm_moe_ep_plan_fixed_dev(_stream(stream), _dp(idx), T, K, E, nranks,
+                                             _dp(dest), self_rank, capacity, _dp(pos),
+                                             _dp(send_cnt)))
 
 
 def ep_pack_dev(x, idx, wt, E, nranks, pos, send_x, send_idx, send_wt, dest=None, lid=None,

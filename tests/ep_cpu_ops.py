@@ -44,6 +44,18 @@ class CpuOps:
             pos[rows, d] = off[d] + np.arange(len(rows))
         return self.torch.from_numpy(pos), self.torch.from_numpy(cnt)
 
+    def plan_fixed(self, idx, capacity):
+        pos, cnt = self.plan(idx)
+        P = pos.numpy().copy()
+        off = np.concatenate([[0], np.cumsum(cnt.numpy())[:-1]])
+        for d in range(self.nranks):
+            m = P[:, d] >= 0
+            P[m, d] = P[m, d] - off[d] + d * capacity
+        return self.torch.from_numpy(P), cnt
+
+    def pack_fixed(self, x, idx, wt, pos, rows):
+        return self.pack(x, idx, wt, pos, rows)
+
     def pack(self, x, idx, wt, pos, rows):
         t = self.torch
         sx = t.zeros((rows, self.D), dtype=x.dtype)

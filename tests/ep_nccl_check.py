@@ -61,10 +61,13 @@ def main():
     # kernels, which leave SMs free meanwhile): the same bits.
     sliced = torch.zeros_like(out)
     layer.forward_chunked(x, idx, wt, sliced, dist, chunks=2)
+    # Fixed-size exchange segments (no counts on the host): the same bits.
+    fixed = torch.zeros_like(out)
+    layer.forward_fixed(x, idx, wt, fixed, dist)
     torch.cuda.synchronize()
     gathered = [torch.zeros_like(out) for _ in range(world)]
     dist.all_gather(gathered, out)
-    ok = torch.equal(out, again) and torch.equal(out, sliced)
+    ok = torch.equal(out, again) and torch.equal(out, sliced) and torch.equal(out, fixed)
     if rank == 0:
         tabs_all, keep_all = tables_of(c["experts"])
         ref = torch.zeros((world * T_LOC, D), device="cuda")

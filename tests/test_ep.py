@@ -131,6 +131,10 @@ def _gloo_rank(rank, nranks, port_no, T_loc, out_dir):
         outc = torch.zeros((T_loc, CASE["D"]))
         L.forward_chunked(*args, outc, dist, chunks=chunks)
         np.save(os.path.join(out_dir, f"out{rank}_c{chunks}.npy"), outc.numpy())
+    # Fixed-size exchange segments (no counts on the host).
+    outf = torch.zeros((T_loc, CASE["D"]))
+    L.forward_fixed(*args, outf, dist)
+    np.save(os.path.join(out_dir, f"out{rank}_fixed.npy"), outf.numpy())
     dist.barrier()
     dist.destroy_process_group()
 
@@ -156,6 +160,8 @@ def test_ep_two_gloo_ranks(port, tmp_path):
     for chunks in (2, 3):
         gc = np.concatenate([np.load(tmp_path / f"out{r}_c{chunks}.npy") for r in range(N)])
         assert_close(gc, want, f"2 gloo ranks EP, {chunks} slices")
+    gf = np.concatenate([np.load(tmp_path / f"out{r}_fixed.npy") for r in range(N)])
+    assert_close(gf, want, "2 gloo ranks EP, fixed-size segments")
 
 
 def test_ep_plan_positions(port):
