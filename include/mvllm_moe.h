@@ -54,11 +54,13 @@ enum {
     MVLLM_ERR_NOT_INIT = 6,    /* mvllm_moe_init has not succeeded */
     MVLLM_ERR_DEVICE = 7,      /* a device-side bounds check rejected an index */
     MVLLM_ERR_WORKSPACE = 8,   /* caller workspace smaller than required */
-    MVLLM_ERR_RANGE = 9,       /* an MXFP4 scale code the tensor-core path cannot represent
-                                  as the reference decodes it (f16 mode: 141..254; block-scaled
-                                  modes: 255, which the MMA reads as NaN, not +inf); the
-                                  host-pointer entries rerun such a call on the decode path
-                                  and never return it */
+    MVLLM_ERR_RANGE = 9,       /* an MXFP4 scale code the tensor-core operands cannot
+                                  represent as the reference decodes it (f16 mode: 141..254;
+                                  block-scaled modes: 255, which the MMA reads as NaN, not
+                                  +inf).  Not returned by the layer and moe_block entries:
+                                  their tensor-core kernels raise a redo word and the decode
+                                  kernels recompute the call's tensor-core experts on the
+                                  device, in the same call */
     MVLLM_ERR_ACT_RANGE = 10   /* a finite activation (a token row of x, or h = act(gate, up))
                                   beyond the f16 operand range (|v| >= 65520): the reference
                                   computes it in f32; this library refuses the call instead of
@@ -120,6 +122,15 @@ MVLLM_API const char *mvllm_moe_last_error(void);   /* text of the last failure 
  * effect. */
 MVLLM_API int mvllm_moe_set_prefill_mode(int mode);
 MVLLM_API int mvllm_moe_get_prefill_mode(void);
+/* Process-wide exact mode: 1 = the layer epilogue (mvllm_moe_epilogue_dev)
+ * and the router scores (mvllm_moe_route_dev / _route_ex_dev) keep the
+ * reference's summation order and roundings (bit-identical to its CPU
+ * functions, serial sums); 0 = tolerance-mode kernels (fused multiply-adds,
+ * tensor cores, reassociated sums: within 1e-2 relative L2 / 2e-2 max-abs of
+ * the reference, run-to-run identical); -1 = the default, 0 unless the
+ * environment sets MVLLM_EXACT=1.  get returns the mode in effect. */
+MVLLM_API int mvllm_moe_set_exact(int on);
+MVLLM_API int mvllm_moe_get_exact(void);
 /* SMs the layer's persistent expert kernels fill (0: all, the default).  No
  * counterpart in the reference: a caller that overlaps an NCCL exchange on
  * another stream with the expert kernels (the chunked expert-parallel step)

@@ -68,18 +68,21 @@ struct PlanArgs {
     int tc_shift; // pair token tiles of 2^tc_shift rows
     int *clear_word; // zeroed once the plan is written (the tensor-map "rewritten" flag)
     int *toff1, *toff2, *soff1, *soff2;
+    // Redo lists: the tensor-core experts' rows as decode items (offsets
+    // roff1/roff2), run when a tensor-core kernel raises *range_word (zeroed
+    // here) for scale codes its operands cannot represent.
+    int *roff1, *roff2, *range_word;
 };
 
-__global__ void plan_kernel(const PlanArgs a) {
-    pdl_wait();
+__device__ __forceinline__ void plan_body(const PlanArgs &a) {
     __shared__ int warp_sums[32];
-    __shared__ int carry[7];
-    if (threadIdx.x < 7)
+    __shared__ int carry[9];
+    if (threadIdx.x < 9)
         carry[threadIdx.x] = 0;
     __syncthreads();
     for (int e0 = 0; e0 < a.nb; e0 += blockDim.x) {
         const int e = e0 + threadIdx.x;
-        int n = 0, c = 0, i1 = 0, i2 = 0, j1 = 0, j2 = 0, k1 = 0, k2 = 0;
+        int n = 0, c = 0, i1 = 0, i2 = 0, j1 = 0, j2 = 0, k1 = 0, k2 = 0, r1 = 0, r2 = 0;
         if (e < a.nb) {
             n = max(a.nr[e], 0);
             bool ok = n > 0 && a.g[e] && a.u[e] && a.d[e];
@@ -109,6 +112,8 @@ __global__ void plan_kernel(const PlanArgs a) {
                 j2 = a.tc_blocks2 * npair;
                 k1 = a.tc_sblocks1 * nsolo;
                 k2 = a.tc_sblocks2 * nsolo;
+                r1 = a.blocks1 * ((c + a.chunk1 - 1) / a.chunk1);
+                r2 = a.blocks2 * ((c + a.chunk2 - 1) / a.chunk2);
             } else {
                 i1 = c ? a.blocks1 * ((c + a.chunk1 - 1) / a.chunk1) : 0;
                 i2 = c ? a.blocks2 * ((c + a.chunk2 - 1) / a.chunk2) : 0;
@@ -128,6 +133,11 @@ __global__ void plan_kernel(const PlanArgs a) {
         const int q1 = block_exclusive_scan(k1, warp_sums, &v1);
         int v2;
         const int q2 = block_exclusive_scan(k2, warp_sums, &v2);
+        int w1 = 0, w2 = 0, x1 = 0, x2 = 0;
+        if (a.roff1) {
+            x1 = block_exclusive_scan(r1, warp_sums, &w1);
+            x2 = block_exclusive_scan(r2, warp_sums, &w2);
+        }
         if (e < a.nb) {
             a.base[e] = carry[0] + b;
             a.cnt[e] = c;
@@ -137,6 +147,10 @@ __global__ void plan_kernel(const PlanArgs a) {
             a.toff2[e] = carry[4] + p2;
             a.soff1[e] = carry[5] + q1;
             a.soff2[e] = carry[6] + q2;
+            if (a.roff1) {
+                a.roff1[e] = carry[7] + x1;
+                a.roff2[e] = carry[8] + x2;
+            }
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -147,12 +161,20 @@ __global__ void plan_kernel(const PlanArgs a) {
             carry[4] += u2;
             carry[5] += v1;
             carry[6] += v2;
+            carry[7] += w1;
+            carry[8] += w2;
         }
         __syncthreads();
     }
     if (threadIdx.x == 0) {
         if (a.clear_word)
             *a.clear_word = 0;
+        if (a.range_word)
+            *a.range_word = 0;
+        if (a.roff1) {
+            a.roff1[a.nb] = carry[7];
+            a.roff2[a.nb] = carry[8];
+        }
         a.off1[a.nb] = carry[1];
         a.off2[a.nb] = carry[2];
         a.toff1[a.nb] = carry[3];
@@ -161,6 +183,11 @@ __global__ void plan_kernel(const PlanArgs a) {
         a.soff2[a.nb] = carry[6];
         *a.total_rows = carry[0];
     }
+}
+
+__global__ void plan_kernel(const PlanArgs a) {
+    pdl_wait();
+    plan_body(a);
 }
 
 // ---------------------------------------------------------------------------
@@ -181,12 +208,12 @@ template <int N> struct TableSet {
 };
 using TmapTemplates = TmapSet<kTmapsPerExpert>;
 
-// One thread per (expert, map): map k of expert e gets table t[k]'s entry e.
+// Map `idx` = (expert e, map k): table t[k]'s entry e swapped into template k;
+// `mine` is the thread's 128-byte shared-memory slot.
 template <int N>
-__global__ void build_tmaps_kernel(const __grid_constant__ TmapSet<N> tpl, const TableSet<N> tabs,
-                                   int nb, uint8_t *__restrict__ out, int *dirty) {
-    pdl_wait();
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void build_map_one(const TmapSet<N> &tpl, const TableSet<N> &tabs,
+                                              int nb, uint8_t *__restrict__ out, int *dirty,
+                                              int idx, uint4 *mine) {
     if (idx >= nb * N)
         return;
     const int e = idx / N, k = idx % N;
@@ -198,9 +225,7 @@ __global__ void build_tmaps_kernel(const __grid_constant__ TmapSet<N> tpl, const
     if (!src)
         return;
     uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<size_t>(idx) * 128);
-    // The wanted map in registers: template with the address swapped in.
-    __shared__ __align__(128) uint8_t staged[128 * 128];
-    uint4 *mine = reinterpret_cast<uint4 *>(staged + threadIdx.x * 128);
+    // The wanted map in shared memory: template with the address swapped in.
     const uint4 *from = reinterpret_cast<const uint4 *>(&tpl.m[k]);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -222,6 +247,16 @@ __global__ void build_tmaps_kernel(const __grid_constant__ TmapSet<N> tpl, const
         tmap_release();
         atomicExch(dirty, 1);
     }
+}
+
+// One thread per (expert, map): map k of expert e gets table t[k]'s entry e.
+template <int N>
+__global__ void build_tmaps_kernel(const __grid_constant__ TmapSet<N> tpl, const TableSet<N> tabs,
+                                   int nb, uint8_t *__restrict__ out, int *dirty) {
+    pdl_wait();
+    __shared__ __align__(128) uint8_t staged[128 * 128];
+    build_map_one<N>(tpl, tabs, nb, out, dirty, blockIdx.x * blockDim.x + threadIdx.x,
+                     reinterpret_cast<uint4 *>(staged + threadIdx.x * 128));
 }
 
 // ---------------------------------------------------------------------------
@@ -256,13 +291,14 @@ __global__ void stage_rows_kernel(const TIn *__restrict__ x, const int *__restri
 // order (several chunks per thread in flight).  A finite value beyond the
 // f16 range records MVLLM_ERR_ACT_RANGE (it would otherwise become inf).
 template <typename TIn>
-__global__ void stage_rows_f16x8_kernel(const TIn *__restrict__ x, const int *__restrict__ index,
-                                        const int *__restrict__ nrows_dev, int nrows_host, int D,
-                                        int fmt, __half *__restrict__ out, int *err) {
-    pdl_wait();
+__device__ __forceinline__ void stage_rows_body(const TIn *__restrict__ x,
+                                                const int *__restrict__ index,
+                                                const int *__restrict__ nrows_dev, int nrows_host,
+                                                int D, int fmt, __half *__restrict__ out,
+                                                int *err, int block, int nblocks) {
     const int nrows = nrows_dev ? *nrows_dev : nrows_host;
     const int chunks = D >> 3;
-    for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
+    for (int r = block; r < nrows; r += nblocks) {
         const int src = index ? __ldg(index + r) : r;
         const TIn *xr = x + static_cast<size_t>(src) * D;
         uint4 *orow = reinterpret_cast<uint4 *>(out + static_cast<size_t>(r) * D);
@@ -302,6 +338,35 @@ __global__ void stage_rows_f16x8_kernel(const TIn *__restrict__ x, const int *__
             orow[c] = *reinterpret_cast<const uint4 *>(h);
         }
     }
+}
+
+template <typename TIn>
+__global__ void stage_rows_f16x8_kernel(const TIn *__restrict__ x, const int *__restrict__ index,
+                                        const int *__restrict__ nrows_dev, int nrows_host, int D,
+                                        int fmt, __half *__restrict__ out, int *err) {
+    pdl_wait();
+    stage_rows_body(x, index, nrows_dev, nrows_host, D, fmt, out, err, blockIdx.x, gridDim.x);
+}
+
+// The gather-stage of the token rows (blocks [0, stage_blocks)) and the
+// decode kernels' per-expert tensor maps (the blocks after them, a thread per
+// map) in one launch: both only need the permutation and the plan.
+template <typename TIn>
+__global__ void __launch_bounds__(256)
+    stage_maps_kernel(const TIn *__restrict__ x, const int *__restrict__ index,
+                      const int *__restrict__ nrows_dev, int D, int fmt, __half *__restrict__ out,
+                      int *err, int stage_blocks, const __grid_constant__ TmapTemplates tpl,
+                      const TableSet<kTmapsPerExpert> tabs, int nb, uint8_t *__restrict__ maps,
+                      int *dirty) {
+    pdl_wait();
+    if (static_cast<int>(blockIdx.x) < stage_blocks) {
+        stage_rows_body(x, index, nrows_dev, 0, D, fmt, out, err, blockIdx.x, stage_blocks);
+        return;
+    }
+    __shared__ __align__(128) uint8_t staged[256 * 128];
+    build_map_one<kTmapsPerExpert>(
+        tpl, tabs, nb, maps, dirty, (blockIdx.x - stage_blocks) * blockDim.x + threadIdx.x,
+        reinterpret_cast<uint4 *>(staged + threadIdx.x * 128));
 }
 
 // ---------------------------------------------------------------------------
@@ -415,14 +480,11 @@ __global__ void permute_place_kernel(const int *__restrict__ idx, int T, int K, 
 // of four plus the bitmap clear.  Global memory written by the CTA's own
 // threads is visible to all of them after each __syncthreads.
 constexpr int kPermSmallT = 256;
-__global__ void __launch_bounds__(1024)
-    permute_small_kernel(const int *__restrict__ idx, const float *__restrict__ wt, int T, int K,
-                         int E, int n_shared, int words, uint32_t *__restrict__ bitmap,
-                         int *__restrict__ wpre, float *__restrict__ wsum, int *__restrict__ nr,
-                         int *__restrict__ xoff, int *__restrict__ n_rows,
-                         int *__restrict__ rows, float *__restrict__ rw,
-                         int *__restrict__ tok_pos) {
-    pdl_wait();
+__device__ __forceinline__ void permute_small_body(
+    const int *__restrict__ idx, const float *__restrict__ wt, int T, int K, int E, int n_shared,
+    int words, uint32_t *__restrict__ bitmap, int *__restrict__ wpre, float *__restrict__ wsum,
+    int *__restrict__ nr, int *__restrict__ xoff, int *__restrict__ n_rows,
+    int *__restrict__ rows, float *__restrict__ rw, int *__restrict__ tok_pos) {
     __shared__ int warp_sums[32];
     const int EE = E + n_shared, KK = K + n_shared;
     for (int i = threadIdx.x; i < EE * words; i += blockDim.x)
@@ -496,6 +558,46 @@ __global__ void __launch_bounds__(1024)
         rw[pos] = wsum[i];
         tok_pos[i] = pos;
     }
+}
+
+__global__ void __launch_bounds__(1024)
+    permute_small_kernel(const int *__restrict__ idx, const float *__restrict__ wt, int T, int K,
+                         int E, int n_shared, int words, uint32_t *__restrict__ bitmap,
+                         int *__restrict__ wpre, float *__restrict__ wsum, int *__restrict__ nr,
+                         int *__restrict__ xoff, int *__restrict__ n_rows,
+                         int *__restrict__ rows, float *__restrict__ rw,
+                         int *__restrict__ tok_pos) {
+    pdl_wait();
+    permute_small_body(idx, wt, T, K, E, n_shared, words, bitmap, wpre, wsum, nr, xoff, n_rows,
+                       rows, rw, tok_pos);
+}
+
+// Decode-sized layer calls (T <= kPermSmallT): the call's error word cleared,
+// the permutation, and the expert plan over its counts, in one CTA -- three
+// launches and a memset folded into one.  The plan reads nr / xoff that the
+// permutation wrote: global memory the CTA's own threads wrote is visible to
+// all of them after __syncthreads.
+struct PermSmallArgs {
+    const int *idx;
+    const float *wt;
+    int T, K, E, n_shared, words;
+    uint32_t *bitmap;
+    int *wpre;
+    float *wsum;
+    int *nr, *xoff, *n_rows, *rows;
+    float *rw;
+    int *tok_pos;
+};
+
+__global__ void __launch_bounds__(1024) layer_prep_small_kernel(const PermSmallArgs q,
+                                                                const PlanArgs a) {
+    pdl_wait();
+    if (threadIdx.x == 0)
+        *a.err = 0;
+    permute_small_body(q.idx, q.wt, q.T, q.K, q.E, q.n_shared, q.words, q.bitmap, q.wpre, q.wsum,
+                       q.nr, q.xoff, q.n_rows, q.rows, q.rw, q.tok_pos);
+    __syncthreads();
+    plan_body(a);
 }
 
 // ---------------------------------------------------------------------------

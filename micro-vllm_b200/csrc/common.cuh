@@ -36,6 +36,12 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // kernel wrote, until the earlier grid has completed and its writes are
 // visible.  Without the attribute this returns at once.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel in the stream (launched with programmatic stream
+// serialisation) start its prologue once every CTA of this grid issued it;
+// that kernel's griddepcontrol.wait still waits for this grid to complete.
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // Records the first error code of a launch (later codes do not overwrite it).
 __device__ __forceinline__ void set_error(int *err, int code) {

@@ -82,6 +82,7 @@ struct DecodeArgs {
     const int *tmaps_dirty; // non-zero: maps were rewritten, acquire before use
     int wbox3d;             // weight maps are 3-D: one box per matrix per stage
     int *err;
+    const int *enable;      // redo launch: runs only when *enable is non-zero (null: always)
 };
 
 template <int FMT, int KS, int NT> struct DecodeLayout {
@@ -304,7 +305,21 @@ template <int NT> __device__ __forceinline__ DecodeItem finish_item(const Decode
 
 template <int FMT, int PHASE, int KS, int NT>
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const DecodeArgs p) {
-    pdl_wait();
+    // Phase 1 lets phase 2 start as soon as its own inputs are complete:
+    // phase 2's item table, tensor maps and weights come from the kernels
+    // before phase 1, so its weight warp streams the first stages while
+    // phase 1 finishes; only phase 2's token rows (h, phase 1's output) wait
+    // for phase 1 (the side warp's griddepcontrol.wait below).  Every global
+    // write of phase 2 follows a stage that holds h.
+    if (p.enable) { // a redo launch: the word comes from the kernel before it
+        pdl_wait();
+        if (load_volatile(p.enable) == 0)
+            return;
+    }
+    if constexpr (PHASE == 1) {
+        pdl_wait();
+        pdl_trigger();
+    }
     static_assert(KS == 256 || KS == 512, "stage K-slice");
     using L = DecodeLayout<FMT, KS, NT>;
     extern __shared__ uint8_t smem_raw[];
@@ -353,6 +368,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
         // doing all of it the weight copies waited behind the small ones:
         // the split measured 10-15% faster on config[1].)
         const bool wprod = warp == kDecodeProducerWarp;
+        if (PHASE == 2 && !wprod)
+            pdl_wait(); // phase 1's output rows
         const uint64_t pol_w = policy_evict_first(); // weights: read once per step
         const uint64_t pol_x = policy_evict_last();  // operand rows: re-read per item
         uint32_t it = 0;

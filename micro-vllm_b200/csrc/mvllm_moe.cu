@@ -10,6 +10,7 @@
 #include "ep_kernels.cuh"
 #include "route_kernels.cuh"
 #include "dense_ffn.cuh"
+#include "epilogue.cuh"
 #include "expert_tier.hpp"
 
 #include <cudaTypedefs.h>
@@ -253,6 +254,10 @@ struct RunWs {
     // x [x_rows, D] and h [h_rows, I], sized for the widest mode.
     uint8_t *mx_tmaps;
     uint8_t *xq, *xc, *hq, *hc;
+    // Redo of the tensor-core experts on the decode kernels (fast path only):
+    // their decode item offsets [nb + 1] per phase, and the word a
+    // tensor-core kernel raises for scale codes it cannot represent.
+    int *roff1, *roff2, *range;
 };
 
 // Carves the expert-run workspace; x_rows = operand rows to stage (0 when the
@@ -277,7 +282,11 @@ void carve_run(Carve &cv, RunWs &w, int nb, int D, int I, bool fast, int rows_ca
     w.h = cv.take<uint8_t>(size_t(std::max(rows_cap, 1)) * I * esz);
     w.y = cv.take<float>(size_t(std::max(rows_cap, 1)) * D);
     w.mx_tmaps = w.xq = w.xc = w.hq = w.hc = nullptr;
+    w.roff1 = w.roff2 = w.range = nullptr;
     if (fast) {
+        w.roff1 = cv.take<int>(nb + 1);
+        w.roff2 = cv.take<int>(nb + 1);
+        w.range = cv.take<int>(1);
         // Widest modes: two e4m3 terms (2 bytes per element) or three e2m1
         // terms (3 codes per 32 elements).
         const size_t xr = size_t(std::max(x_rows, 1)), hr = size_t(std::max(rows_cap, 1));
@@ -308,6 +317,20 @@ int prefill_mode() {
                 m = i;
     }
     return m;
+}
+
+// Exact mode: the layer epilogue and the router scores keep the reference's
+// summation order and roundings (bit-identical results, serial sums); off,
+// they run the tolerance-mode kernels.  Set by mvllm_moe_set_exact or
+// MVLLM_EXACT=1.
+std::atomic<int> g_exact{-1};
+bool exact_mode() {
+    int m = g_exact.load();
+    if (m < 0) {
+        const char *e = getenv("MVLLM_EXACT");
+        m = (e && *e && strcmp(e, "0")) ? 1 : 0;
+    }
+    return m != 0;
 }
 
 struct Tables {
@@ -639,14 +662,17 @@ int launch_decode(const DecodeArgs &a, int ks, int nt, cudaStream_t st, int sms)
                    : launch_decode_t<FMT, PHASE, 256, 2>(a, st, sms);
 }
 
-// The expert FFN over nb experts: plan, optional operand staging, phase 1,
-// phase 2.  Leaves y [rows, D] (reference base order) in w.y.  When
-// `x_staged` is set, x already is the staged operand (f16 in stage_pos order
-// on the fast path, f32 on the generic path) indexed by xoff.
-int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const Tables &tb,
-                const int *nr, const int *xoff, const void *x, int x_dtype, int x_rows,
-                bool x_staged, int avg_rows, int act, float act_a, float act_b, RunWs &w,
-                bool allow_tc = true) {
+// The expert plan of a run: PlanArgs plus what the launches after it need.
+struct ExpertPlan {
+    PlanArgs pa;
+    bool fast, mx;
+    int tc_min, mode, nt;
+};
+
+ExpertPlan make_expert_plan(int nb, int D, int I, int fmt, const Tables &tb, const int *nr,
+                            const int *xoff, int x_rows, int avg_rows, const RunWs &w,
+                            bool allow_tc) {
+    ExpertPlan ep{};
     const bool fast = fast_path_ok(fmt, D, I);
     const int tc_min = (fast && allow_tc) ? tc_min_rows(x_rows) : 0;
     // Block-scaled MMAs for MXFP4 experts on the tensor-core path (the mode's
@@ -682,7 +708,63 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
     pa.tc_sblocks2 = D / tc_cols_per_item<2, false>();
     pa.toff1 = w.toff1, pa.toff2 = w.toff2, pa.soff1 = w.soff1, pa.soff2 = w.soff2;
     pa.clear_word = fast ? w.tmaps_dirty : nullptr;
-    CUDA_TRY(launch_pdl(plan_kernel, dim3(1), dim3(1024), 0, st, pa));
+    if (tc_min) {
+        pa.roff1 = w.roff1, pa.roff2 = w.roff2, pa.range_word = w.range;
+    }
+    ep.pa = pa;
+    ep.fast = fast, ep.mx = mx, ep.tc_min = tc_min, ep.mode = mode, ep.nt = nt;
+    return ep;
+}
+
+// Decode tensor-map templates per shape, encoded once (the address is swapped
+// in on the device, so the placeholder address does not matter).
+int decode_templates(TmapTemplates *tpl, int fmt, int D, int I, void *placeholder, int *box3d) {
+    struct Key {
+        int fmt, D, I, want3d;
+        bool operator<(const Key &o) const {
+            return std::tie(fmt, D, I, want3d) < std::tie(o.fmt, o.D, o.I, o.want3d);
+        }
+    };
+    struct Val {
+        TmapTemplates t;
+        int box3d;
+    };
+    static std::mutex mu;
+    static std::map<Key, Val> cache;
+    const Key k{fmt, D, I, *box3d};
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(k);
+    if (it == cache.end()) {
+        Val v{};
+        v.box3d = *box3d;
+        if (int rc = make_templates(&v.t, fmt, D, I, pick_ks(D), pick_ks(I), placeholder,
+                                    &v.box3d))
+            return rc;
+        it = cache.emplace(k, v).first;
+    }
+    *tpl = it->second.t;
+    *box3d = it->second.box3d;
+    return MVLLM_OK;
+}
+
+// The expert FFN over nb experts: plan, optional operand staging, phase 1,
+// phase 2.  Leaves y [rows, D] (reference base order) in w.y.  When
+// `x_staged` is set, x already is the staged operand (f16 in stage_pos order
+// on the fast path, f32 on the generic path) indexed by xoff.  With `pre`, the
+// plan and the decode tensor maps were already written (layer_prep_small_kernel
+// and stage_maps_kernel) from that same plan.
+int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const Tables &tb,
+                const int *nr, const int *xoff, const void *x, int x_dtype, int x_rows,
+                bool x_staged, int avg_rows, int act, float act_a, float act_b, RunWs &w,
+                bool allow_tc = true, const ExpertPlan *pre = nullptr) {
+    const ExpertPlan ep = pre ? *pre
+                              : make_expert_plan(nb, D, I, fmt, tb, nr, xoff, x_rows, avg_rows, w,
+                                                 allow_tc);
+    const PlanArgs &pa = ep.pa;
+    const bool fast = ep.fast, mx = ep.mx;
+    const int tc_min = ep.tc_min, mode = ep.mode, nt = ep.nt;
+    if (!pre)
+        CUDA_TRY(launch_pdl(plan_kernel, dim3(1), dim3(1024), 0, st, pa));
     prof_mark(st, kPhPlan);
 
     const void *xop = x;
@@ -716,14 +798,15 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
         // Per-expert tensor maps: host templates, device-side address swap.
         TmapTemplates tpl;
         int box3d = getenv("MVLLM_DECODE_2D_BOXES") ? 0 : 1;
-        if (int rc = make_templates(&tpl, fmt, D, I, pick_ks(D), pick_ks(I), w.y, &box3d))
+        if (int rc = decode_templates(&tpl, fmt, D, I, w.y, &box3d))
             return rc;
         const int nmaps = nb * kTmapsPerExpert;
         // (the plan kernel cleared w.tmaps_dirty)
-        CUDA_TRY(launch_pdl(build_tmaps_kernel<kTmapsPerExpert>, dim3((nmaps + 127) / 128),
-                            dim3(128), 0, st, tpl,
-                            TableSet<kTmapsPerExpert>{{tb.g, tb.u, tb.d, tb.gs, tb.us, tb.ds}}, nb,
-                            w.tmaps, w.tmaps_dirty));
+        if (!pre)
+            CUDA_TRY(launch_pdl(build_tmaps_kernel<kTmapsPerExpert>, dim3((nmaps + 127) / 128),
+                                dim3(128), 0, st, tpl,
+                                TableSet<kTmapsPerExpert>{{tb.g, tb.u, tb.d, tb.gs, tb.us, tb.ds}},
+                                nb, w.tmaps, w.tmaps_dirty));
         CUtensorMap tok1{}, tok2{}, tsc1{}, tsc2{};
         TcArgs t1{};
         const int kind = mode_kind(mode), nterm = mx ? mode_nterm(mode) : 0;
@@ -775,6 +858,7 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             t1.tshift = pa.tc_shift;
             t1.K = D, t1.O = I, t1.out = w.h;
             t1.act = act, t1.act_a = act_a, t1.act_b = act_b, t1.err = w.err;
+            t1.range = w.range;
         }
         DecodeArgs a{};
         a.tmaps = w.tmaps;
@@ -797,6 +881,16 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
                                   st, sms);
             else
                 rc = launch_tc<1>(fmt, t1, s1, tok1, st, sms);
+            if (rc)
+                return rc;
+            // Scale codes the tensor-core operands cannot represent: the
+            // decode kernels recompute h of every tensor-core expert (a
+            // launch that returns at once when nothing was raised).
+            DecodeArgs r = a;
+            r.item_off = w.roff1, r.enable = w.range;
+            rc = (fmt == MVLLM_FMT_MXFP4)
+                     ? launch_decode<MVLLM_FMT_MXFP4, 1>(r, pick_ks(D), nt, st, sms)
+                     : launch_decode<MVLLM_FMT_INT4_G64, 1>(r, pick_ks(D), nt, st, sms);
             if (rc)
                 return rc;
             // h (every phase-1 row, f16) as terms for the block-scaled phase 2.
@@ -825,6 +919,13 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
                                   st, sms);
             else
                 rc = launch_tc<2>(fmt, t2, s2, tok2, st, sms);
+            if (rc)
+                return rc;
+            DecodeArgs r = b;
+            r.item_off = w.roff2, r.enable = w.range;
+            rc = (fmt == MVLLM_FMT_MXFP4)
+                     ? launch_decode<MVLLM_FMT_MXFP4, 2>(r, pick_ks(I), nt, st, sms)
+                     : launch_decode<MVLLM_FMT_INT4_G64, 2>(r, pick_ks(I), nt, st, sms);
             if (rc)
                 return rc;
         }
@@ -920,6 +1021,13 @@ struct Resolver {
 
     explicit Resolver(Context &cc) : c(cc) {}
 
+    // The range the last lookup resolved (a registered buffer or a tier
+    // blob), checked before the maps: an expert's six arrays usually lie in
+    // one ExpertStore slot, so five of six lookups stop here.
+    uintptr_t memo_lo = 0, memo_hi = 0;
+    uint8_t *memo_dev = nullptr;
+    bool memo_late = false;
+
     // First pass: returns the cached device pointer or nullptr (to upload).
     void *cached(const void *host, size_t len) {
         if (!host)
@@ -929,8 +1037,11 @@ struct Resolver {
             return nullptr;
         --it;
         const uintptr_t start = it->first, h = reinterpret_cast<uintptr_t>(host);
-        if (h >= start && h + len <= start + it->second.bytes)
+        if (h >= start && h + len <= start + it->second.bytes) {
+            memo_lo = start, memo_hi = start + it->second.bytes;
+            memo_dev = static_cast<uint8_t *>(it->second.dev), memo_late = false;
             return static_cast<uint8_t *>(it->second.dev) + (h - start);
+        }
         return nullptr;
     }
 
@@ -957,8 +1068,9 @@ struct Resolver {
         for (TierEntry *s : stream_in)
             if (s == e)
                 tier_miss = true;
-        return static_cast<uint8_t *>(c.tier_arena) + size_t(slot) * c.tier.slot_bytes() +
-               (reinterpret_cast<uintptr_t>(host) - e->host);
+        uint8_t *base = static_cast<uint8_t *>(c.tier_arena) + size_t(slot) * c.tier.slot_bytes();
+        memo_lo = e->host, memo_hi = e->host + e->bytes, memo_dev = base, memo_late = tier_miss;
+        return base + (reinterpret_cast<uintptr_t>(host) - e->host);
     }
 
     // Returns an index into uploads (or -1 when cached/null) and, through
@@ -970,6 +1082,13 @@ struct Resolver {
             *late = false;
         if (!host)
             return -1;
+        const uintptr_t h = reinterpret_cast<uintptr_t>(host);
+        if (memo_dev && h >= memo_lo && h + len <= memo_hi) {
+            *dev = memo_dev + (h - memo_lo);
+            if (late)
+                *late = memo_late;
+            return -1;
+        }
         if (void *p = cached(host, len)) {
             *dev = p;
             return -1;
@@ -1104,6 +1223,15 @@ int mvllm_moe_set_prefill_mode(int mode) {
 }
 
 int mvllm_moe_get_prefill_mode(void) { return prefill_mode(); }
+
+int mvllm_moe_set_exact(int on) {
+    if (on < -1 || on > 1)
+        return fail(MVLLM_ERR_INVALID, "set_exact: %d is not -1, 0 or 1", on);
+    g_exact.store(on);
+    return MVLLM_OK;
+}
+
+int mvllm_moe_get_exact(void) { return exact_mode() ? 1 : 0; }
 
 int mvllm_moe_set_sm_limit(int sms) {
     if (sms < 0)
@@ -1937,6 +2065,10 @@ struct LayerHooks {
     std::function<int()> before_gather, before_combine;
 };
 
+static int layer_combine(cudaStream_t st, int sms, int T, int KK, int D, float *out,
+                         uint8_t *out16, const RunWs &w, const LayerWs &l,
+                         const LayerHooks *hooks);
+
 static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_shared, int D,
                           int Iinter, int fmt, const int *idx, const float *wt, const void *x,
                           int x_dtype, const Tables &tb, float *out, int act, float act_a,
@@ -1944,6 +2076,49 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
                           const LayerHooks *hooks = nullptr, uint8_t *out16 = nullptr) {
     const bool fast = fast_path_ok(fmt, D, Iinter);
     const int EE = E + n_shared, KK = K + n_shared, R = T * KK;
+    // Decode-sized calls on the fast path: error word, permutation and plan in
+    // one launch, the gather-stage and the decode tensor maps in the next.
+    const bool small = fast && T <= kPermSmallT && EE <= 4096;
+    ExpertPlan ep{};
+    if (small) {
+        ep = make_expert_plan(EE, D, Iinter, fmt, tb, l.nr, l.xoff, R, R / EE, l.run, allow_tc);
+        PermSmallArgs q{idx, wt, T, K, E, n_shared, l.perm.words, l.perm.bitmap, l.perm.wpre,
+                        l.perm.wsum, l.nr, l.xoff, l.n_rows, l.rows, l.rw, l.tok_pos};
+        prof_mark(st, kPhStart);
+        CUDA_TRY(launch_pdl(layer_prep_small_kernel, dim3(1), dim3(1024), 0, st, q, ep.pa));
+        prof_mark(st, kPhPermute);
+        if (hooks && hooks->before_gather)
+            if (int rc = hooks->before_gather())
+                return rc;
+        TmapTemplates tpl;
+        int box3d = getenv("MVLLM_DECODE_2D_BOXES") ? 0 : 1;
+        if (int rc = decode_templates(&tpl, fmt, D, Iinter, l.run.y, &box3d))
+            return rc;
+        const int sblocks = std::max(1, std::min(R, 8 * sms));
+        const int mblocks = (EE * kTmapsPerExpert + 255) / 256;
+        const TableSet<kTmapsPerExpert> tabs{{tb.g, tb.u, tb.d, tb.gs, tb.us, tb.ds}};
+        if (x_dtype == MVLLM_DTYPE_BF16)
+            CUDA_TRY(launch_pdl(stage_maps_kernel<__nv_bfloat16>, dim3(sblocks + mblocks),
+                                dim3(256), 0, st, static_cast<const __nv_bfloat16 *>(x),
+                                static_cast<const int *>(l.rows),
+                                static_cast<const int *>(l.n_rows), D, fmt,
+                                static_cast<__half *>(l.run.xs), l.run.err, sblocks, tpl, tabs,
+                                EE, l.run.tmaps, l.run.tmaps_dirty));
+        else
+            CUDA_TRY(launch_pdl(stage_maps_kernel<float>, dim3(sblocks + mblocks), dim3(256), 0,
+                                st, static_cast<const float *>(x),
+                                static_cast<const int *>(l.rows),
+                                static_cast<const int *>(l.n_rows), D, fmt,
+                                static_cast<__half *>(l.run.xs), l.run.err, sblocks, tpl, tabs,
+                                EE, l.run.tmaps, l.run.tmaps_dirty));
+        prof_mark(st, kPhGather);
+        RunWs w = l.run;
+        if (int rc = run_experts(st, sms, EE, D, Iinter, fmt, tb, l.nr, l.xoff, l.run.xs,
+                                 MVLLM_DTYPE_F32, R, true, R / EE, act, act_a, act_b, w, allow_tc,
+                                 &ep))
+            return rc;
+        return layer_combine(st, sms, T, KK, D, out, out16, w, l, hooks);
+    }
     CUDA_TRY(cudaMemsetAsync(l.run.err, 0, sizeof(int), st));
     prof_mark(st, kPhStart);
     if (int rc = run_permute(st, sms, idx, wt, T, K, E, n_shared, l.nr, l.xoff, l.rows, l.rw,
@@ -1984,6 +2159,13 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
     if (int rc = run_experts(st, sms, EE, D, Iinter, fmt, tb, l.nr, l.xoff, l.run.xs,
                              MVLLM_DTYPE_F32, R, true, R / EE, act, act_a, act_b, w, allow_tc))
         return rc;
+    return layer_combine(st, sms, T, KK, D, out, out16, w, l, hooks);
+}
+
+// The layer's ordered combine (f32 rows, or the partial-row form).
+static int layer_combine(cudaStream_t st, int sms, int T, int KK, int D, float *out,
+                         uint8_t *out16, const RunWs &w, const LayerWs &l,
+                         const LayerHooks *hooks) {
     if (hooks && hooks->before_combine)
         if (int rc = hooks->before_combine())
             return rc;
@@ -2238,9 +2420,8 @@ static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter,
 static int topk_launch(cudaStream_t st, const float *choice, const float *mix, int T, int E,
                        int K, float scale, int *idx, float *wt) {
     const int warps = 8;
-    topk_kernel<<<std::min((T + warps - 1) / warps, 65535), 32 * warps, 0, st>>>(
-        choice, mix, T, E, K, scale, idx, wt);
-    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(launch_pdl(topk_kernel, dim3(std::min((T + warps - 1) / warps, 65535)),
+                        dim3(32 * warps), 0, st, choice, mix, T, E, K, scale, idx, wt));
     return MVLLM_OK;
 }
 
@@ -2268,12 +2449,53 @@ int mvllm_moe_route_ex_dev(void *stream, const void *x, int x_dtype, int T, int 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if ((T + kSeqS - 1) / kSeqS > 65535)
         return fail(MVLLM_ERR_INVALID, "route_dev: T too large");
-    if (x_dtype == MVLLM_DTYPE_BF16)
+    // Tolerance mode: 32 experts per CTA (one wave of clusters at E = 256)
+    // when the slices fit shared memory, else 16.
+    const bool bf = x_dtype == MVLLM_DTYPE_BF16;
+    const size_t sm32 = bf ? rf_smem_bytes<__nv_bfloat16, 32>(H) : rf_smem_bytes<float, 32>(H);
+    const size_t sm16 = bf ? rf_smem_bytes<__nv_bfloat16, 16>(H) : rf_smem_bytes<float, 16>(H);
+    const int exp_per_cta = sm32 <= 200 * 1024 ? 32 : sm16 <= 200 * 1024 ? 16 : 0;
+    const bool fast = !exact_mode() && H % 8 == 0 && exp_per_cta > 0 &&
+                      (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                      (reinterpret_cast<uintptr_t>(router) & 15u) == 0;
+    if (fast) {
+        const size_t rf_sm = exp_per_cta == 32 ? sm32 : sm16;
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(kRfSplit * ((E + exp_per_cta - 1) / exp_per_cta), (T + 31) / 32);
+        cfg.blockDim = dim3(16 * exp_per_cta);
+        cfg.dynamicSmemBytes = rf_sm;
+        cfg.stream = st;
+        cudaLaunchAttribute at[2];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = kRfSplit, at[0].val.clusterDim.y = 1, at[0].val.clusterDim.z = 1;
+        at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 2;
+#define MVB_RF(TXT, N)                                                                         \
+    do {                                                                                       \
+        CUDA_TRY(cudaFuncSetAttribute(route_scores_fast_kernel<TXT, N>,                        \
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, int(rf_sm))); \
+        CUDA_TRY(cudaLaunchKernelEx(&cfg, route_scores_fast_kernel<TXT, N>,                    \
+                                    static_cast<const TXT *>(x), router, bias, T, H, E,        \
+                                    score_fn, scores, choice));                                \
+    } while (0)
+        if (bf && exp_per_cta == 32)
+            MVB_RF(__nv_bfloat16, 32);
+        else if (bf)
+            MVB_RF(__nv_bfloat16, 16);
+        else if (exp_per_cta == 32)
+            MVB_RF(float, 32);
+        else
+            MVB_RF(float, 16);
+#undef MVB_RF
+    } else if (x_dtype == MVLLM_DTYPE_BF16) {
         CUDA_TRY(route_scores_launch(st, static_cast<const __nv_bfloat16 *>(x), router, bias, T,
                                      H, E, score_fn, scores, choice));
-    else
+    } else {
         CUDA_TRY(route_scores_launch(st, static_cast<const float *>(x), router, bias, T, H, E,
                                      score_fn, scores, choice));
+    }
     return topk_launch(st, choice, scores, T, E, K, routed_scale, idx, wt);
 }
 
@@ -2449,6 +2671,50 @@ int mvllm_moe_epilogue_dev(void *stream, int T, int H, int L, const float *acc,
     if (!c.inited)
         return fail(MVLLM_ERR_NOT_INIT, "mvllm_moe_init has not been called");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (!exact_mode()) {
+        // Tolerance mode: one fused kernel (epilogue.cuh).
+        EpiArgs ea{acc, lat_n, eps, static_cast<const int8_t *>(up_w),
+                   static_cast<const float *>(up_scales), routed_scale, shared, h, T, H, L};
+        const bool a16 = (reinterpret_cast<uintptr_t>(up_w) & 15u) == 0 &&
+                         (reinterpret_cast<uintptr_t>(acc) & 15u) == 0 &&
+                         (!lat_n || (reinterpret_cast<uintptr_t>(lat_n) & 15u) == 0);
+        if (up_w && up_fmt == MVLLM_FMT_INT8_ROW && a16 && L % 64 == 0 && H % 16 == 0 &&
+            epi_ksl(L) <= kEpiWarps && epi_smem_bytes(L) <= 227 * 1024 &&
+            epi_ws_bytes(T, L) <= workspace_bytes) {
+            const int ksl = epi_ksl(L), rb = kEpiWarps / ksl;
+            const dim3 grid((H / 16 + rb - 1) / rb), block(kEpiWarps * 32);
+            const size_t sm = epi_smem_bytes(L);
+            __half *rows = static_cast<__half *>(workspace);
+            float *tinv = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) +
+                                                    size_t(T) * L * 2);
+            CUDA_TRY(launch_pdl(epilogue_stage_kernel, dim3(std::min(T, 8 * c.sms)), dim3(256),
+                                0, st, ea, rows, tinv));
+            switch (ksl) {
+#define MVB_EPI(K)                                                                           \
+    case K:                                                                                  \
+        CUDA_TRY(cudaFuncSetAttribute(epilogue_up_kernel<K>,                                \
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm))); \
+        CUDA_TRY(launch_pdl(epilogue_up_kernel<K>, grid, block, sm, st, ea,                  \
+                            static_cast<const __half *>(rows), static_cast<const float *>(tinv))); \
+        return MVLLM_OK;
+                MVB_EPI(1)
+                MVB_EPI(2)
+                MVB_EPI(4)
+                MVB_EPI(8)
+                MVB_EPI(16)
+#undef MVB_EPI
+            default:
+                break;
+            }
+        }
+        const bool h16 = (reinterpret_cast<uintptr_t>(h) & 15u) == 0 &&
+                         (!shared || (reinterpret_cast<uintptr_t>(shared) & 15u) == 0);
+        if (!up_w && lat_n && a16 && h16 && H % 4 == 0) {
+            CUDA_TRY(launch_pdl(epilogue_norm_kernel, dim3(std::min(T, 8 * c.sms)), dim3(256), 0,
+                                st, ea));
+            return MVLLM_OK;
+        }
+    }
     const float *src = acc;
     float *norm = static_cast<float *>(workspace);
     float *up = norm ? norm + size_t(T) * L : nullptr;

@@ -108,6 +108,169 @@ inline cudaError_t route_scores_launch(cudaStream_t st, const TX *x, const float
     return cudaGetLastError();
 }
 
+// ---- tolerance mode ---------------------------------------------------------
+// Router scores with f32 fused multiply-adds in a different order than the
+// reference: the dot products over H are split across a cluster of
+// kRfSplit CTAs (one H slice each).  A CTA covers EXP experts x 32 tokens:
+// warp w takes experts 2w and 2w+1, its lanes consecutive 8-column pieces of
+// the slice, each lane keeping 2 x 32 partial sums that a butterfly of
+// shuffles adds up.  Every rank stores its sums into the
+// rank-0 CTA's shared memory (distributed shared memory), which adds the
+// slices in rank order and applies the score function and the bias.
+// Scores differ from the reference's by f32 reassociation (about 1e-6
+// relative); the top-k that follows is the exact selection on those scores.
+constexpr int kRfSplit = 8;
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Store to the same shared-memory variable of CTA `rank` of the cluster.
+__device__ __forceinline__ void st_dsmem_f32(float *p, int rank, float v) {
+    uint32_t a = smem_u32(p), r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(r), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void load_x8(const float *p, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4 *>(p);
+    const float4 b = *reinterpret_cast<const float4 *>(p + 4);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+
+__device__ __forceinline__ void load_x8(const __nv_bfloat16 *p, float (&v)[8]) {
+    const uint4 q = *reinterpret_cast<const uint4 *>(p);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+
+// Shared memory of route_scores_fast_kernel: the CTA's slice of the 32 token
+// rows and of its experts' router rows, then the partial sums.
+template <typename TX, int EXP> __host__ __device__ inline size_t rf_smem_bytes(int H) {
+    const int per = (H / 8 + kRfSplit - 1) / kRfSplit;
+    return size_t(32) * per * 8 * sizeof(TX) + size_t(EXP) * per * 8 * 4 +
+           size_t(kRfSplit) * EXP * 32 * 4;
+}
+
+// Grid: x = kRfSplit * ceil(E / EXP) (clusters of kRfSplit along x), y =
+// ceil(T / 32); 16 * EXP threads (a warp per two experts); rf_smem_bytes of
+// dynamic shared memory.  H a multiple of 8, rows 16-byte aligned.  The
+// slices of the token rows and the router rows are staged in shared memory
+// first (coalesced, every load independent), so the dot products wait on
+// shared memory, not on a chain of global loads; tokens go in groups of 4 so
+// that eight independent FMA chains are in flight per lane.
+template <typename TX, int EXP>
+__global__ void __launch_bounds__(16 * EXP, 1)
+    route_scores_fast_kernel(const TX *__restrict__ x, const float *__restrict__ w,
+                             const float *__restrict__ bias, int T, int H, int E, int score_fn,
+                             float *__restrict__ scores, float *__restrict__ choice) {
+    extern __shared__ __align__(16) uint8_t rf_smem[];
+    const int rank = blockIdx.x % kRfSplit; // the CTA's rank in its cluster
+    const int e0 = (blockIdx.x / kRfSplit) * EXP;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.y * 32, nt = min(32, T - t0);
+    const int n8 = H / 8, per = (n8 + kRfSplit - 1) / kRfSplit;
+    const int c0 = rank * per, c1 = min(n8, (rank + 1) * per); // 8-column pieces of the slice
+    const int np = max(0, c1 - c0);
+    TX *xs = reinterpret_cast<TX *>(rf_smem); // [32][per * 8]
+    float *wsm = reinterpret_cast<float *>(rf_smem + size_t(32) * per * 8 * sizeof(TX));
+    // [kRfSplit][EXP][32]: every rank's partial sums, gathered in rank 0's copy
+    float *red = wsm + size_t(EXP) * per * 8;
+    // Both slices arrive by bulk copies (a row piece each, all in flight at
+    // once); the router rows' are issued before waiting for the kernels
+    // before this one, which they do not depend on.
+    __shared__ __align__(8) uint64_t bar;
+    const uint32_t xrow_b = uint32_t(np) * 8u * uint32_t(sizeof(TX)), wrow_b = uint32_t(np) * 32u;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(&bar, uint32_t(EXP) * wrow_b + uint32_t(nt) * xrow_b);
+        if (np > 0)
+            for (int el = 0; el < EXP; ++el)
+                bulk_g2s(wsm + static_cast<size_t>(el) * per * 8,
+                         w + static_cast<size_t>(min(e0 + el, E - 1)) * H + 8 * c0, wrow_b, &bar,
+                         policy_evict_first());
+    }
+    pdl_wait(); // x comes from the kernels before this one
+    if (threadIdx.x == 0 && np > 0)
+        for (int t = 0; t < nt; ++t)
+            bulk_g2s(xs + static_cast<size_t>(t) * per * 8,
+                     x + static_cast<size_t>(t0 + t) * H + 8 * c0, xrow_b, &bar,
+                     policy_evict_last());
+    for (int i = threadIdx.x; i < (32 - nt) * np; i += blockDim.x) { // padding tokens: zeros
+        const int t = nt + i / np, c = i % np;
+        float *z = reinterpret_cast<float *>(xs + static_cast<size_t>(t) * per * 8 + 8 * c);
+        *reinterpret_cast<uint4 *>(z) = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (sizeof(TX) == 4)
+            *reinterpret_cast<uint4 *>(z + 4) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    __syncthreads(); // the barrier's initialisation and the padding rows
+    mbar_wait(&bar, 0, nullptr);
+    const float *wa = wsm + static_cast<size_t>(2 * warp) * per * 8;
+    const float *wb = wa + static_cast<size_t>(per) * 8;
+    float sa[32], sb[32];
+#pragma unroll
+    for (int t = 0; t < 32; ++t)
+        sa[t] = sb[t] = 0.f;
+    for (int c = lane; c < np; c += 32) {
+        float va[8], vb[8];
+        load_x8(wa + 8 * c, va);
+        load_x8(wb + 8 * c, vb);
+#pragma unroll
+        for (int tg = 0; tg < 32; tg += 4) {
+            float xv[4][8];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                load_x8(xs + static_cast<size_t>(tg + u) * per * 8 + 8 * c, xv[u]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    sa[tg + u] = fmaf(xv[u][j], va[j], sa[tg + u]);
+                    sb[tg + u] = fmaf(xv[u][j], vb[j], sb[tg + u]);
+                }
+        }
+    }
+    // Butterfly: after it lane l holds token l's sums over the warp's lanes.
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int t = 0; t < off; ++t) {
+            // keep the half of the entries that matches this lane's bit
+            const float ka = upper ? sa[t + off] : sa[t], ga = upper ? sa[t] : sa[t + off];
+            const float kb = upper ? sb[t + off] : sb[t], gb = upper ? sb[t] : sb[t + off];
+            sa[t] = ka + __shfl_xor_sync(0xffffffffu, ga, off);
+            sb[t] = kb + __shfl_xor_sync(0xffffffffu, gb, off);
+        }
+    }
+    // Push this rank's sums into rank 0's shared memory (remote stores do
+    // not wait), then one cluster barrier.
+    st_dsmem_f32(red + (static_cast<size_t>(rank) * EXP + 2 * warp) * 32 + lane, 0, sa[0]);
+    st_dsmem_f32(red + (static_cast<size_t>(rank) * EXP + 2 * warp + 1) * 32 + lane, 0, sb[0]);
+    cluster_sync_all();
+    if (rank == 0) {
+        for (int i = threadIdx.x; i < EXP * 32; i += blockDim.x) {
+            const int el = i >> 5, tl = i & 31;
+            float sum = 0.f;
+#pragma unroll
+            for (int r = 0; r < kRfSplit; ++r)
+                sum += red[(static_cast<size_t>(r) * EXP + el) * 32 + tl];
+            const int e = e0 + el, tt = t0 + tl;
+            if (e < E && tt < T) {
+                const float sc = route_score(sum, score_fn);
+                scores[static_cast<size_t>(tt) * E + e] = sc;
+                choice[static_cast<size_t>(tt) * E + e] = bias ? sc + bias[e] : sc;
+            }
+        }
+    }
+}
+
 constexpr int kTopkMaxPerLane = 32; // E <= 1024
 constexpr int kTopkMaxK = 32;       // one lane per selected expert
 
@@ -120,6 +283,7 @@ constexpr int kTopkMaxK = 32;       // one lane per selected expert
 __global__ void topk_kernel(const float *__restrict__ choice, const float *__restrict__ mix, int T,
                             int E, int K, float scale, int *__restrict__ idx,
                             float *__restrict__ wt) {
+    pdl_wait(); // the scores come from the kernel before this one
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     const int per = (E + 31) >> 5;

@@ -30,8 +30,8 @@
 // f16 product it is exact for s in [104, 140] and for s = 0 (+0) and 255 (inf,
 // as the reference decodes it).  Codes below 104 lose bits below 2^-24
 // (absolute error under 2^-25 per weight).  Codes 141..254 would overflow:
-// the dequant warps record MVLLM_ERR_RANGE and the host reruns the call on
-// the decode path.  int4-g64 weights are (q-8) * scale rounded once to f16.
+// the dequant warps raise the call's redo word and the decode kernels
+// recompute the call's tensor-core experts (f32 scale arithmetic).  int4-g64 weights are (q-8) * scale rounded once to f16.
 //
 // Warp roles (608 threads per CTA, one CTA per SM, both CTAs of a pair walk
 // the pair's item list):
@@ -114,7 +114,19 @@ struct TcArgs {
     int act;
     float act_a, act_b;
     int *err;
+    int *range;               // raised for scale codes this kernel cannot represent: the
+                              // decode kernels then redo the call's tensor-core experts
 };
+
+// Scale codes the operands cannot represent: with a redo word the call's
+// tensor-core experts are recomputed on the decode kernels; without one the
+// call fails with MVLLM_ERR_RANGE.
+__device__ __forceinline__ void flag_range(const TcArgs &p) {
+    if (p.range)
+        *reinterpret_cast<volatile int *>(p.range) = 1;
+    else
+        set_error(p.err, MVLLM_ERR_RANGE);
+}
 
 // Per CTA: TMEM columns [0, 2 * ACC_HALF) accumulators -- one buffer of both
 // halves for a tile wider than a half, or two halves that alternate between
@@ -855,7 +867,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
                         const uint32_t e0 = (word >> (16 * (kw & 1))) & 0xFFu;
                         const uint32_t e1 = (word >> (16 * (kw & 1) + 8)) & 0xFFu;
                         if ((e0 > 140u && e0 != 255u) || (e1 > 140u && e1 != 255u))
-                            set_error(p.err, MVLLM_ERR_RANGE);
+                            flag_range(p);
                         sc0 = __float2half2_rn(ue8m0_to_f32(e0));
                         sc1 = __float2half2_rn(ue8m0_to_f32(e1));
                     } else {

@@ -804,7 +804,7 @@ __global__ void __launch_bounds__(MxCfg<KIND, NTERM, PAIR>::THREADS,
                     const uint32_t va = lds32(smem_u32(wina + 4 * word));
                     // 255 would be NaN to the MMA but +inf to the reference.
                     if (__vcmpeq4(va, 0xFFFFFFFFu))
-                        set_error(p.err, MVLLM_ERR_RANGE);
+                        flag_range(p);
                     tc_st1(col0 + 4 * g + q, va);
 #pragma unroll
                     for (int t = 0; t < NTERM; ++t) {

@@ -50,6 +50,7 @@ C_SYMBOLS = (
     "mvllm_moe_dense_ffn_workspace", "mvllm_moe_dense_ffn_dev", "mvllm_moe_wait_selftest",
     "mvllm_moe_set_prefill_mode", "mvllm_moe_get_prefill_mode", "mvllm_mx_terms_dev",
     "mvllm_moe_mma_rate", "mvllm_moe_set_sm_limit", "mvllm_moe_ep_plan_fixed_dev",
+    "mvllm_moe_set_exact", "mvllm_moe_get_exact",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -121,6 +122,8 @@ def lib():
             "mvllm_moe_wait_selftest": (i, [vp, vp]),
             "mvllm_moe_set_prefill_mode": (i, [i]),
             "mvllm_moe_get_prefill_mode": (i, []),
+            "mvllm_moe_set_exact": (i, [i]),
+            "mvllm_moe_get_exact": (i, []),
             "mvllm_mx_terms_dev": (i, [vp, i, vp, i, i, vp, vp]),
             "mvllm_moe_mma_rate": (i, [i, i, i, i, vp]),
             "mvllm_moe_set_sm_limit": (i, [i]),
@@ -165,6 +168,17 @@ def set_prefill_mode(mode) -> None:
 
 def get_prefill_mode() -> int:
     return int(lib().mvllm_moe_get_prefill_mode())
+
+
+def set_exact(on) -> None:
+    """Exact mode for the layer epilogue and the router scores: True keeps the
+    reference's summation order (bit-identical), False the tolerance-mode
+    kernels, None the default (MVLLM_EXACT, else off)."""
+    _check(lib().mvllm_moe_set_exact(-1 if on is None else int(bool(on))))
+
+
+def get_exact() -> bool:
+    return bool(lib().mvllm_moe_get_exact())
 
 
 def set_sm_limit(sms: int) -> None:

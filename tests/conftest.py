@@ -71,3 +71,12 @@ def moe():
     import mvllm_moe
     mvllm_moe.init(0)
     return mvllm_moe
+
+
+@pytest.fixture
+def exact(moe):
+    """Exact mode for the test (the epilogue and router scores keep the
+    reference's order and roundings), the default afterwards."""
+    moe.set_exact(True)
+    yield moe
+    moe.set_exact(None)

@@ -39,10 +39,11 @@ def dev(a):
 @pytest.mark.parametrize("E,H,rs,dtype", [(256, 1024, 1.0, "f32"), (64, 512, 2.5, "f32"),
                                           (5, 256, 1.0, "f32"), (256, 1024, 1.0, "bf16"),
                                           (96, 300, 1.0, "f32")])
-def test_route_sqrt_softplus(moe, port, E, H, rs, dtype):
+def test_route_sqrt_softplus(exact, port, E, H, rs, dtype):
     """f32 and bf16 activations; H = 300 is not a whole number of 16-byte
     pieces, so the router takes the register-staged tile instead of the
-    cp.async ring."""
+    cp.async ring.  Exact mode."""
+    moe = exact
     rng = np.random.default_rng(E * 7 + H)
     T = 96
     x = rng.standard_normal((T, H)).astype(np.float32)

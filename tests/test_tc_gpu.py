@@ -213,3 +213,49 @@ def test_block_scaled_modes_outside_tolerance(moe, port, monkeypatch, prefill_mo
     assert np.all(np.isfinite(got))
     rel = float(np.linalg.norm(got - want) / np.linalg.norm(want))
     assert rel < ceiling, rel
+
+
+@pytest.mark.parametrize("where", ["gate", "down"])
+@pytest.mark.parametrize("mode", ["f16", "mxf4x3"])
+def test_tc_scale_range_layer_dev(moe, port, monkeypatch, prefill_mode, where, mode):
+    """A device-pointer caller (mvllm_moe_layer_dev: no host round trip to
+    rerun from) with scale code 141 in the gate (phase 1) or the down
+    (phase 2) weights: in f16 mode the tensor-core kernel raises the call's
+    redo word and the decode kernels recompute the tensor-core experts on the
+    device, so `out` is the reference's result and no error is left."""
+    prefill_mode(mode)
+    rng = np.random.default_rng(37 if where == "gate" else 38)
+    D, I, n = 512, 512, 40
+    w = [(rng.standard_normal((o, i)) * 0.02).astype(np.float32)
+         for (o, i) in ((I, D), (I, D), (D, I))]
+    if where == "gate":
+        w[0][0, 5] = 65536.0  # scale code 141 in gate row 0, column group 0
+    else:
+        w[2][3, 7] = 65536.0  # scale code 141 in down row 3
+        w[0][7, :] = 0.0      # h[:, 7] = silu(0) * up = 0: the big weight adds nothing
+    packed = [port.pack_mxfp4(m) for m in w]
+    assert max(int(s.max()) for _, s in packed) > 140
+    x = cases.bf16_round(rng.standard_normal((n, D)).astype(np.float32))
+    if where == "gate":
+        x[:, 5] = 0.0  # keeps the reference's output finite
+    c = dict(D=D, I=I, fmt=cases.FMT_MXFP4, act=cases.ACT_SILU, act_a=0.0, act_b=0.0, nb=1,
+             g=[packed[0][0]], u=[packed[1][0]], d=[packed[2][0]], gs=[packed[0][1]],
+             us=[packed[1][1]], ds=[packed[2][1]], xg=x, xoff=np.array([0], np.int32),
+             nr=np.array([n], np.int32), rows=np.arange(n, dtype=np.int32),
+             rw=np.ones(n, np.float32), S=n)
+    _, want = cases.run_block(port, c)
+    assert np.isfinite(want).all()
+    keep = [torch.from_numpy(np.ascontiguousarray(a)).cuda()
+            for a in (packed[0][0], packed[1][0], packed[2][0], packed[0][1], packed[1][1],
+                      packed[2][1])]
+    tables = [torch.tensor([t.data_ptr()], dtype=torch.int64, device="cuda") for t in keep]
+    force_tc(monkeypatch)
+    ws = torch.empty(moe.layer_workspace_bytes(n, 1, 1, 0, D, I, cases.FMT_MXFP4),
+                     dtype=torch.uint8, device="cuda")
+    out = torch.zeros((n, D), dtype=torch.float32, device="cuda")
+    moe.layer_dev(n, 1, 1, 0, D, I, cases.FMT_MXFP4, torch.zeros((n, 1), dtype=torch.int32,
+                                                                  device="cuda"),
+                  torch.ones((n, 1), device="cuda"), torch.from_numpy(x).cuda(), tables, out,
+                  cases.ACT_SILU, 0.0, 0.0, ws)
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy(), want, f"layer_dev range redo ({where}, {mode})")
