@@ -75,6 +75,13 @@ def parse():
                     help="run the DeepSeek-V4 leg on more than two ranks too")
     ap.add_argument("--prefill-tokens", type=int, default=4096,
                     help="config[3]: 4096; fewer only to size a profiler capture")
+    ap.add_argument("--profile-decode-batch", type=int, default=0,
+                    help="only build the config[1] decode workload at this batch, time it from "
+                         "CUDA-graph replays, and run three layer steps between "
+                         "cudaProfilerStart/Stop (for ncu --profile-from-start off)")
+    ap.add_argument("--profile-epilogue-router", action="store_true",
+                    help="only run the layer epilogue and the router at the K3 / DeepSeek-V4 "
+                         "decode shape, two calls each between cudaProfilerStart/Stop")
     ap.add_argument("--experts", type=int, default=256,
                     help="routed experts (BASELINE config[1]: 256); fewer only to size a "
                          "profiler capture")
@@ -1108,6 +1115,59 @@ def launches_per_ep_step(world, mode):
     return layer + (3 if world > 1 else 0)
 
 
+def profile_only(moe, torch, args):
+    """A small, fixed workload for an ncu launch list or capture: the decode
+    layer at one batch size, or the layer epilogue and the router."""
+    if args.profile_decode_batch:
+        wl = Workload(moe, torch, args.profile_decode_batch, seed=7)
+        for i in range(20):
+            wl.step(moe, i)
+        torch.cuda.synchronize()
+        _, ms = graph_throughput(moe, torch, wl, 320, 32)
+        print(json.dumps({"profile": "decode", "batch": wl.B, "graph_ms_per_step": ms}),
+              flush=True)
+        torch.cuda.profiler.start()
+        for i in range(3):
+            wl.step(moe, i)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        return
+    T, H, L, E, K = 32, CFG["D"], 2048, 256, 6
+    g = torch.Generator(device="cuda").manual_seed(3)
+    acc = torch.randn((T, L), generator=g, device="cuda")
+    h = torch.randn((T, H), generator=g, device="cuda")
+    sh = torch.randn((T, H), generator=g, device="cuda")
+    lat_n = torch.ones(L, device="cuda")
+    q = torch.randint(-127, 128, (H, L), generator=g, device="cuda", dtype=torch.int32).to(
+        torch.int8)
+    sc = torch.full((H,), 0.01, device="cuda")
+    ws = torch.empty(moe.epilogue_workspace_bytes(T, H, L), dtype=torch.uint8, device="cuda")
+    x = torch.randn((T, H), generator=g, device="cuda").to(torch.bfloat16)
+    r = torch.randn((E, H), generator=g, device="cuda") * (1.0 / H ** 0.5)
+    bias = torch.randn(E, generator=g, device="cuda") * 0.01
+    idx = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    wt = torch.empty((T, K), device="cuda")
+    scores, choice = torch.empty((T, E), device="cuda"), torch.empty((T, E), device="cuda")
+
+    def epi():
+        moe.epilogue_dev(acc, h, 2.0, lat_n, 1e-6, 8, q, sc, sh, ws)
+
+    def rte():
+        moe.route_ex_dev(x, r, bias, K, idx, wt, scores, choice, moe.SCORE_SQRT_SOFTPLUS, 2.5)
+
+    for _ in range(10):
+        epi()
+        rte()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    for _ in range(2):
+        epi()
+        rte()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print(json.dumps({"profile": "epilogue+router", "tokens": T}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1131,6 +1191,9 @@ def main():
     moe.init(local_rank)
     peak, peak_kind = peaks()
     mode = moe.PREFILL_NAMES[moe.get_prefill_mode()]
+    if args.profile_decode_batch or args.profile_epilogue_router:
+        profile_only(moe, torch, args)
+        return
 
     # ---- headline: config[4], the expert-parallel layer at N GPUs (strong
     # scaling: 8192 tokens per step over all ranks), uniform routing; the Zipf

@@ -286,6 +286,14 @@ MVLLM_API int mvllm_moe_layer_dev(void *stream, int T, int K, int E, int n_share
                         const void *const *gs, const void *const *us, const void *const *ds,
                         float *out, int act, float act_a, float act_b, void *workspace,
                         size_t workspace_bytes);
+/* Device-side errors of mvllm_moe_layer_dev / _layer_partial_dev (an
+ * activation beyond the f16 range, a skipped misaligned or out-of-range
+ * expert, a bounded wait that ran out) are recorded in the call's workspace
+ * instead of being returned (the call does not synchronise): `out` is then
+ * left as the caller passed it (partial rows: zero rows).  This synchronises
+ * `stream` and returns the code of the last call that used `workspace`
+ * (MVLLM_OK when none). */
+MVLLM_API int mvllm_moe_layer_error(void *stream, const void *workspace);
 
 /* The same layer with HOST buffers (x f32 [T,D], idx/wt [T,K], out f32
  * [T,D] accumulated) and weights already resident on the device: the

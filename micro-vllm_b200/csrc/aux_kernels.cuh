@@ -606,8 +606,13 @@ __global__ void __launch_bounds__(1024) layer_prep_small_kernel(const PermSmallA
 // add per term as in glm53.cpp:1978-1984 (no fused multiply-add).
 __global__ void combine_tokens_kernel(float *__restrict__ out, const float *__restrict__ y,
                                       const float *__restrict__ rw,
-                                      const int *__restrict__ tok_pos, int T, int KK, int D) {
+                                      const int *__restrict__ tok_pos, int T, int KK, int D,
+                                      const int *err) {
     pdl_wait();
+    // A device-side error in this call (recorded in *err): `out` is left as
+    // the caller passed it; mvllm_moe_layer_error reports the code.
+    if (err && load_volatile(err) != 0)
+        return;
     constexpr int kB = 4; // rows loaded per batch
     for (int c = blockIdx.y; c < T; c += gridDim.y) {
         int pos[17];
@@ -663,8 +668,13 @@ __global__ void combine_tokens_kernel(float *__restrict__ out, const float *__re
 // the f32 row staged in shared memory (D floats) for the row maximum.
 __global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const float *__restrict__ y,
                                           const float *__restrict__ rw,
-                                          const int *__restrict__ tok_pos, int T, int KK, int D) {
+                                          const int *__restrict__ tok_pos, int T, int KK, int D,
+                                          const int *err) {
     extern __shared__ float4 srow[];
+    // A device-side error in this call (recorded in *err): zero rows (h = 0,
+    // scale 0), so the owners add nothing from this rank; the serving rank's
+    // mvllm_moe_layer_error reports the code.
+    const bool failed = err && load_volatile(err) != 0;
     __shared__ float wmax[32];
     const int n4 = D / 4;
     const size_t pitch = 2 * static_cast<size_t>(D) + 16;
@@ -715,12 +725,14 @@ __global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const flo
             const float4 a = srow[v];
             __half2 h[2] = {__floats2half2_rn(a.x * inv, a.y * inv),
                             __floats2half2_rn(a.z * inv, a.w * inv)};
+            if (failed)
+                h[0] = h[1] = __floats2half2_rn(0.f, 0.f);
             *reinterpret_cast<uint2 *>(row + 8 * static_cast<size_t>(v)) =
                 *reinterpret_cast<const uint2 *>(h);
         }
         if (threadIdx.x == 0)
             *reinterpret_cast<float4 *>(row + 2 * static_cast<size_t>(D)) =
-                make_float4(ldexpf(1.f, s), 0.f, 0.f, 0.f);
+                make_float4(failed ? 0.f : ldexpf(1.f, s), 0.f, 0.f, 0.f);
         __syncthreads();
     }
 }

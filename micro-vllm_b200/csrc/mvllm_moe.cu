@@ -2037,6 +2037,7 @@ struct LayerWs {
 void carve_layer(Carve &cv, LayerWs &l, int T, int K, int E, int n_shared, int D, int I,
                  bool fast) {
     const int EE = E + n_shared, R = T * (K + n_shared);
+    int *err = cv.take<int>(64); // the call's error word at the workspace's first bytes
     carve_perm(cv, l.perm, T, K, E, n_shared);
     l.nr = cv.take<int>(EE);
     l.xoff = cv.take<int>(EE);
@@ -2045,6 +2046,7 @@ void carve_layer(Carve &cv, LayerWs &l, int T, int K, int E, int n_shared, int D
     l.tok_pos = cv.take<int>(R);
     l.n_rows = cv.take<int>(1);
     carve_run(cv, l.run, EE, D, I, fast, R, R);
+    l.run.err = err;
 }
 } // namespace
 
@@ -2175,12 +2177,14 @@ static int layer_combine(cudaStream_t st, int sms, int T, int KK, int D, float *
             CUDA_TRY(cudaFuncSetAttribute(combine_tokens_f16_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
         combine_tokens_f16_kernel<<<std::min(T, 8 * sms), 256, sm, st>>>(out16, w.y, l.rw,
-                                                                         l.tok_pos, T, KK, D);
+                                                                         l.tok_pos, T, KK, D,
+                                                                         w.err);
     } else {
         dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
         CUDA_TRY(launch_pdl(combine_tokens_kernel, grid, dim3(256), 0, st, out,
                             static_cast<const float *>(w.y), static_cast<const float *>(l.rw),
-                            static_cast<const int *>(l.tok_pos), T, KK, D));
+                            static_cast<const int *>(l.tok_pos), T, KK, D,
+                            static_cast<const int *>(w.err)));
     }
     CUDA_TRY(cudaGetLastError());
     prof_mark(st, kPhCombine);
@@ -2251,6 +2255,16 @@ int mvllm_moe_layer_partial_dev(void *stream, int T, int K, int E, int n_shared,
     return layer_dev_impl(static_cast<cudaStream_t>(stream), sms, T, K, E, n_shared, D, Iinter,
                           fmt, idx, wt, x, x_dtype, tb, nullptr, act, act_a, act_b, l, true,
                           nullptr, static_cast<uint8_t *>(out16));
+}
+
+int mvllm_moe_layer_error(void *stream, const void *workspace) {
+    if (!workspace)
+        return fail(MVLLM_ERR_INVALID, "layer_error: no workspace");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    CUDA_TRY(cudaStreamSynchronize(st));
+    int code = 0;
+    CUDA_TRY(cudaMemcpy(&code, workspace, sizeof(int), cudaMemcpyDeviceToHost));
+    return code;
 }
 
 static int layer_host_impl(int T, int K, int E, int n_shared, int D, int Iinter, int fmt,

@@ -50,7 +50,7 @@ C_SYMBOLS = (
     "mvllm_moe_dense_ffn_workspace", "mvllm_moe_dense_ffn_dev", "mvllm_moe_wait_selftest",
     "mvllm_moe_set_prefill_mode", "mvllm_moe_get_prefill_mode", "mvllm_mx_terms_dev",
     "mvllm_moe_mma_rate", "mvllm_moe_set_sm_limit", "mvllm_moe_ep_plan_fixed_dev",
-    "mvllm_moe_set_exact", "mvllm_moe_get_exact",
+    "mvllm_moe_set_exact", "mvllm_moe_get_exact", "mvllm_moe_layer_error",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -123,6 +123,7 @@ def lib():
             "mvllm_moe_set_prefill_mode": (i, [i]),
             "mvllm_moe_get_prefill_mode": (i, []),
             "mvllm_moe_set_exact": (i, [i]),
+            "mvllm_moe_layer_error": (i, [vp, vp]),
             "mvllm_moe_get_exact": (i, []),
             "mvllm_mx_terms_dev": (i, [vp, i, vp, i, i, vp, vp]),
             "mvllm_moe_mma_rate": (i, [i, i, i, i, vp]),
@@ -357,6 +358,15 @@ def layer_dev(T, K, E, n_shared, D, Iinter, fmt, idx, wt, x, tables, out, act, a
                                      _dp(wt), _dp(x), x_dtype, *[_dp(t) for t in tables],
                                      _dp(out), act, act_a, act_b, _dp(workspace),
                                      workspace.numel() * workspace.element_size()))
+
+
+def layer_error(workspace, stream=None) -> int:
+    """The device-side status of the last layer_dev / layer_partial_dev call
+    that used ``workspace`` (synchronises the stream): 0 or an ERR_* code."""
+    rc = int(lib().mvllm_moe_layer_error(_stream(stream), _dp(workspace)))
+    if rc in (ERR_INVALID, ERR_CUDA):
+        _check(rc)
+    return rc
 
 
 def partial_row_bytes(D) -> int:

@@ -78,3 +78,39 @@ def test_beyond_f16_is_refused(moe, port, where):
         _run(moe, c, out)
     assert e.value.code == moe.ERR_ACT_RANGE
     np.testing.assert_array_equal(out, base)
+
+
+def test_layer_dev_error_leaves_out(moe, port):
+    """A device-pointer call (no host sync) with a token row beyond the f16
+    range: the combine does not run, so `out` keeps the caller's rows, and
+    mvllm_moe_layer_error reports MVLLM_ERR_ACT_RANGE; the next clean call
+    on the same workspace reports MVLLM_OK."""
+    D, I, E, K, T = 512, 512, 4, 2, 24
+    rng = np.random.default_rng(57)
+    ex = cases.make_experts(port, rng, cases.FMT_MXFP4, E, D, I)
+    tabs = [[], [], [], [], [], []]
+    keep = []
+    for (gp, gsc), (up, usc), (dp, dsc) in ex:
+        for k, a in enumerate((gp, up, dp, gsc, usc, dsc)):
+            t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+            keep.append(t)
+            tabs[k].append(t.data_ptr())
+    tables = [torch.tensor(t, dtype=torch.int64, device="cuda") for t in tabs]
+    idx = torch.from_numpy(rng.integers(0, E, (T, K)).astype(np.int32)).cuda()
+    wt = torch.full((T, K), 0.5, device="cuda")
+    x = rng.standard_normal((T, D)).astype(np.float32)
+    ws = torch.empty(moe.layer_workspace_bytes(T, K, E, 0, D, I, cases.FMT_MXFP4),
+                     dtype=torch.uint8, device="cuda")
+    base = torch.from_numpy(rng.standard_normal((T, D)).astype(np.float32)).cuda()
+    for bad, want_code in ((True, moe.ERR_ACT_RANGE), (False, 0)):
+        xx = x.copy()
+        if bad:
+            xx[3] *= np.float32(1e5 / 3.0)
+        out = base.clone()
+        moe.layer_dev(T, K, E, 0, D, I, cases.FMT_MXFP4, idx, wt, torch.from_numpy(xx).cuda(),
+                      tables, out, cases.ACT_SITU, 4.0, 25.0, ws)
+        assert moe.layer_error(ws) == want_code
+        if bad:
+            assert torch.equal(out, base)
+        else:
+            assert not torch.equal(out, base)
