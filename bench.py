@@ -37,6 +37,7 @@ CFG = dict(D=7168, I=2048, E=256, K=8, n_shared=1, fmt=7, act=2, act_a=4.0, act_
 EXPERT_BYTES = 3 * (CFG["I"] * CFG["D"] // 2 + CFG["I"] * CFG["D"] // 32)  # 23,396,352
 METRIC = "MoE-block tokens/sec (config[4] expert-parallel MXFP4 layer, 8192 tokens per step)"
 N_INPUTS = 16
+PROFILE_HEADLINE = False  # --profile-headline: two headline steps for ncu, nothing timed
 
 
 def parse():
@@ -79,6 +80,12 @@ def parse():
                     help="only build the config[1] decode workload at this batch, time it from "
                          "CUDA-graph replays, and run three layer steps between "
                          "cudaProfilerStart/Stop (for ncu --profile-from-start off)")
+    ap.add_argument("--profile-headline", action="store_true",
+                    help="only build the headline config[4] layer and run two steps between "
+                         "cudaProfilerStart/Stop after the warm-up (for ncu)")
+    ap.add_argument("--profile-scale", type=int, default=1,
+                    help="with --profile-headline: divide config[4]'s experts and tokens by "
+                         "this factor (the same rows per expert) to size an ncu capture")
     ap.add_argument("--profile-epilogue-router", action="store_true",
                     help="only run the layer epilogue and the router at the K3 / DeepSeek-V4 "
                          "decode shape, two calls each between cudaProfilerStart/Stop")
@@ -119,6 +126,20 @@ def traffic_ratio():
     with open(p) as f:
         for line in f:
             if line.startswith("dram_bytes_per_algorithmic_byte:"):
+                return float(line.split(":", 1)[1])
+    return None
+
+
+def headline_traffic():
+    """DRAM bytes per launch of the headline's dominant kernel (phase-1 CTA
+    pairs) at full size, from the committed ncu summary
+    (profiles/headline_config4_one_gpu.txt), or None."""
+    p = os.path.join(ROOT, "profiles", "headline_config4_one_gpu.txt")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            if line.startswith("phase1_pair_dram_bytes_per_launch_full_size:"):
                 return float(line.split(":", 1)[1])
     return None
 
@@ -818,19 +839,27 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
         wt = wt[rank * T_loc:(rank + 1) * T_loc].contiguous()
 
         def step(xx=x, ii=idx, ww=wt, oo=out):
-            oo.zero_()
+            # out += layer(x): the layer's contract (the residual stream); the
+            # rows stay the same buffer from step to step
             if world > 1 and ep_mode == "fixed":
                 return layer.forward_fixed(xx, ii, ww, oo, dist)
             if world > 1 and chunks > 1:
                 return layer.forward_chunked(xx, ii, ww, oo, dist, chunks=chunks)
             if world > 1:
                 return layer.forward(xx, ii, ww, oo, dist)
-            ep.emulate_step([layer], [xx], [ii], [ww], [oo], torch)
+            layer.forward_local(xx, ii, ww, oo)  # one rank: the single-GPU layer
             return None
 
         for _ in range(max(warmup, 2)):
             step()
         barrier()
+        if PROFILE_HEADLINE:  # two steps for an ncu launch list, nothing timed
+            torch.cuda.profiler.start()
+            for _ in range(2):
+                step()
+            barrier()
+            torch.cuda.profiler.stop()
+            return {"profiled": name}
         moe.profile_enable(True)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         sampler = clk if (clk is not None and name == "uniform") else None
@@ -890,12 +919,67 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
             barrier()
             wall = time.perf_counter() - t0
             ems, wall = max_over_ranks([a2.elapsed_time(b2) / e2e_steps, wall / e2e_steps])
-            res["e2e"] = {"value": T_all / (ems / 1e3), "unit": "tokens/s",
-                          "ms_per_step": ems, "host_wall_ms_per_step": wall * 1e3,
+            serial = {"value": T_all / (ems / 1e3), "ms_per_step": ems,
+                      "host_wall_ms_per_step": wall * 1e3}
+
+            # Pipelined: the same copies, each step's inputs and outputs in one
+            # of two device buffer sets, H2D on one copy stream and D2H on
+            # another, so step i's output read and step i+1's input copy run
+            # while step i+1 / i computes (PCIe is full duplex).
+            cs = torch.cuda.current_stream()
+            s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+            bufs = [(torch.empty_like(x), torch.empty_like(idx), torch.empty_like(wt),
+                     torch.zeros_like(out)) for _ in range(2)]
+            ohs = [oh, torch.empty_like(oh).pin_memory()]
+            ev = {k: [torch.cuda.Event() for _ in range(2)]
+                  for k in ("in_ready", "in_free", "out_ready", "out_free")}
+            for j in range(2):
+                ev["in_free"][j].record(cs)
+                ev["out_free"][j].record(cs)
+
+            def e2e_pipe_step(i):
+                j = i % 2
+                xb, ib, wb, ob = bufs[j]
+                with torch.cuda.stream(s_in):
+                    s_in.wait_event(ev["in_free"][j])
+                    xb.copy_(xh, non_blocking=True)
+                    ib.copy_(ih, non_blocking=True)
+                    wb.copy_(wh, non_blocking=True)
+                    ev["in_ready"][j].record(s_in)
+                cs.wait_event(ev["in_ready"][j])
+                cs.wait_event(ev["out_free"][j])
+                step(xb, ib, wb, ob)
+                ev["in_free"][j].record(cs)
+                ev["out_ready"][j].record(cs)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(ev["out_ready"][j])
+                    ohs[j].copy_(ob, non_blocking=True)
+                    ev["out_free"][j].record(s_out)
+
+            for i in range(2):
+                e2e_pipe_step(i)
+            torch.cuda.synchronize()
+            barrier()
+            a3, b3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            a3.record()
+            for i in range(e2e_steps):
+                e2e_pipe_step(i)
+            cs.wait_stream(s_out)  # the last step's output is on the host
+            b3.record()
+            barrier()
+            wall3 = time.perf_counter() - t0
+            pms, wall3 = max_over_ranks([a3.elapsed_time(b3) / e2e_steps, wall3 / e2e_steps])
+            res["e2e"] = {"value": T_all / (pms / 1e3), "unit": "tokens/s",
+                          "ms_per_step": pms, "host_wall_ms_per_step": wall3 * 1e3,
                           "h2d_bytes_per_step": T_all * (D * 2 + K * 8),
                           "d2h_bytes_per_step": T_all * D * 4,
                           "api": "EPLayer.forward over the library's device entries (one rank: "
-                                 "the single-GPU layer), host buffers pinned"}
+                                 "the single-GPU layer), host buffers pinned",
+                          "copies": "every step copies its x / idx / wt in and its out back; "
+                                    "two device buffer sets, H2D and D2H on their own streams "
+                                    "overlapping the neighbouring steps' compute",
+                          "serial": serial}
         del layer, ops, tabs, mats
     wcache.clear()
     torch.cuda.empty_cache()
@@ -1194,6 +1278,13 @@ def main():
     if args.profile_decode_batch or args.profile_epilogue_router:
         profile_only(moe, torch, args)
         return
+    if args.profile_headline:
+        global PROFILE_HEADLINE, EP_E, EP_T
+        PROFILE_HEADLINE = True
+        EP_E, EP_T = EP_E // args.profile_scale, EP_T // args.profile_scale
+        print(json.dumps(ep_bench(moe, torch, dist, rank, world, 2, args.warmup,
+                                  ep_mode="fixed" if world <= 4 else "compact")), flush=True)
+        return
 
     # ---- headline: config[4], the expert-parallel layer at N GPUs (strong
     # scaling: 8192 tokens per step over all ranks), uniform routing; the Zipf
@@ -1292,7 +1383,13 @@ def main():
                                                      "and decode kernels), max over ranks",
                          "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
                          "frac": achieved / tpeak, "peak_kind": tpeak_kind,
-                         "traffic": None,
+                         "traffic": headline_traffic() if world == 1 and mode == "f16" else None,
+                         "traffic_source": "DRAM read + write per launch of the dominant kernel "
+                                           "(tc_ffn phase-1 pairs) at full size, from the "
+                                           "committed ncu summary "
+                                           "profiles/headline_config4_one_gpu.txt (a 48-expert "
+                                           "capture with the same rows per expert, x 8); not "
+                                           "measured in this run",
                          "algorithmic_flops_per_step_per_gpu": flops / world,
                          "kernel_ms_per_step": e_ms},
             "gpu_launches": launches_per_ep_step(world, mode) * args.steps,

@@ -224,6 +224,19 @@ class EPLayer:
     def pack(self, x, idx, wt, pos, send_splits):
         return self.ops.pack(x, idx, wt, pos, int(sum(send_splits)))
 
+    def forward_local(self, x, idx, wt, out):
+        """One rank: the single-GPU routed layer (mvllm_moe_layer_dev over all
+        experts, out += layer(x)); no plan, pack, exchange or combine."""
+        if self.nranks != 1:
+            raise ValueError("forward_local is the one-rank step")
+        o = self.ops
+        T = x.shape[0]
+        if T > o.max_recv_rows:
+            raise ValueError(f"{T} tokens, above the {o.max_recv_rows} sized for")
+        moe.layer_dev(T, self.K, o.E_local, 0, self.D, o.I, o.fmt, idx, wt, x, o.tables, out,
+                      o.act, o.act_a, o.act_b, o.ws)
+        return {"sent_rows": 0, "received_rows": T}
+
     def forward_fixed(self, x, idx, wt, out, dist, group=None):
         """The step with fixed-size exchange segments: every rank sends each
         destination `T` rows (a token goes to a rank at most once; rows

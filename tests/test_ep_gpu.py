@@ -88,6 +88,12 @@ def test_ep_emulated_four_ranks_gpu(moe, port):
                   CASE["act"], CASE["act_a"], CASE["act_b"], ws)
     torch.cuda.synchronize()
     assert torch.equal(one, direct)
+    # ... and EPLayer.forward_local (the one-rank step bench.py times) is that layer.
+    local = torch.zeros_like(one)
+    ep.EPLayer(ops, 0, 1, CASE["D"], CASE["K"]).forward_local(
+        dev(c["x"]).to(torch.bfloat16), dev(c["idx"]), dev(c["wt"]), local)
+    torch.cuda.synchronize()
+    assert torch.equal(local, direct)
 
 
 def test_ep_emulated_replicated_experts_gpu(moe, port):
