@@ -72,17 +72,22 @@ struct PlanArgs {
     // roff1/roff2), run when a tensor-core kernel raises *range_word (zeroed
     // here) for scale codes its operands cannot represent.
     int *roff1, *roff2, *range_word;
+    // A rest of more than tc_small and at most tc_wide rows: tc_sblocks{1,2}
+    // wide single-CTA items (offsets woff1/woff2); tc_wide <= tc_small: none.
+    int tc_wide;
+    int *woff1, *woff2;
 };
 
 __device__ __forceinline__ void plan_body(const PlanArgs &a) {
     __shared__ int warp_sums[32];
-    __shared__ int carry[9];
-    if (threadIdx.x < 9)
+    __shared__ int carry[11];
+    if (threadIdx.x < 11)
         carry[threadIdx.x] = 0;
     __syncthreads();
     for (int e0 = 0; e0 < a.nb; e0 += blockDim.x) {
         const int e = e0 + threadIdx.x;
         int n = 0, c = 0, i1 = 0, i2 = 0, j1 = 0, j2 = 0, k1 = 0, k2 = 0, r1 = 0, r2 = 0;
+        int m1 = 0, m2 = 0;
         if (e < a.nb) {
             n = max(a.nr[e], 0);
             bool ok = n > 0 && a.g[e] && a.u[e] && a.d[e];
@@ -106,12 +111,14 @@ __device__ __forceinline__ void plan_body(const PlanArgs &a) {
             }
             c = ok ? n : 0;
             if (a.tc_min > 0 && c >= a.tc_min) {
-                int npair, nsolo;
-                tc_tiles(c, a.tc_small, a.tc_shift, npair, nsolo);
+                int npair, nsolo, nwide;
+                tc_tiles3(c, a.tc_small, a.tc_wide, a.tc_shift, npair, nsolo, nwide);
                 j1 = a.tc_blocks1 * npair;
                 j2 = a.tc_blocks2 * npair;
                 k1 = a.tc_sblocks1 * nsolo;
                 k2 = a.tc_sblocks2 * nsolo;
+                m1 = a.tc_sblocks1 * nwide;
+                m2 = a.tc_sblocks2 * nwide;
                 r1 = a.blocks1 * ((c + a.chunk1 - 1) / a.chunk1);
                 r2 = a.blocks2 * ((c + a.chunk2 - 1) / a.chunk2);
             } else {
@@ -133,10 +140,14 @@ __device__ __forceinline__ void plan_body(const PlanArgs &a) {
         const int q1 = block_exclusive_scan(k1, warp_sums, &v1);
         int v2;
         const int q2 = block_exclusive_scan(k2, warp_sums, &v2);
-        int w1 = 0, w2 = 0, x1 = 0, x2 = 0;
+        int w1 = 0, w2 = 0, x1 = 0, x2 = 0, z1 = 0, z2 = 0, y1 = 0, y2 = 0;
         if (a.roff1) {
             x1 = block_exclusive_scan(r1, warp_sums, &w1);
             x2 = block_exclusive_scan(r2, warp_sums, &w2);
+        }
+        if (a.woff1) {
+            y1 = block_exclusive_scan(m1, warp_sums, &z1);
+            y2 = block_exclusive_scan(m2, warp_sums, &z2);
         }
         if (e < a.nb) {
             a.base[e] = carry[0] + b;
@@ -151,6 +162,10 @@ __device__ __forceinline__ void plan_body(const PlanArgs &a) {
                 a.roff1[e] = carry[7] + x1;
                 a.roff2[e] = carry[8] + x2;
             }
+            if (a.woff1) {
+                a.woff1[e] = carry[9] + y1;
+                a.woff2[e] = carry[10] + y2;
+            }
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -163,6 +178,8 @@ __device__ __forceinline__ void plan_body(const PlanArgs &a) {
             carry[6] += v2;
             carry[7] += w1;
             carry[8] += w2;
+            carry[9] += z1;
+            carry[10] += z2;
         }
         __syncthreads();
     }
@@ -174,6 +191,10 @@ __device__ __forceinline__ void plan_body(const PlanArgs &a) {
         if (a.roff1) {
             a.roff1[a.nb] = carry[7];
             a.roff2[a.nb] = carry[8];
+        }
+        if (a.woff1) {
+            a.woff1[a.nb] = carry[9];
+            a.woff2[a.nb] = carry[10];
         }
         a.off1[a.nb] = carry[1];
         a.off2[a.nb] = carry[2];

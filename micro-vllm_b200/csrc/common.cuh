@@ -70,6 +70,18 @@ __host__ __device__ __forceinline__ void tc_tiles(int c, int small_max, int tshi
     nsolo = (r > 0 && r <= small_max) ? 1 : 0;
 }
 
+// The same split with a third form: a rest of more than small_max and at
+// most wide_max rows runs as one wide single-CTA tile (tc_ffn's one-CTA-per-SM
+// form); wide_max <= small_max leaves it out.
+__host__ __device__ __forceinline__ void tc_tiles3(int c, int small_max, int wide_max, int tshift,
+                                                   int &npair, int &nsolo, int &nwide) {
+    const int f = c >> tshift, r = c & ((1 << tshift) - 1);
+    const int top = wide_max > small_max ? wide_max : small_max;
+    npair = f + (r > top ? 1 : 0);
+    nsolo = (r > 0 && r <= small_max) ? 1 : 0;
+    nwide = (r > small_max && r <= top) ? 1 : 0;
+}
+
 // Largest e with off[e] <= i, for off non-decreasing and off[nb] > i.
 __device__ __forceinline__ int find_owner(const int *off, int nb, int i) {
     int lo = 0, hi = nb;

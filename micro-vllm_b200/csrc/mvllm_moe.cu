@@ -242,6 +242,7 @@ struct RunWs {
     int *base, *cnt, *off1, *off2, *total_rows, *err;
     int *toff1, *toff2; // tensor-core path, CTA-pair item offsets [nb + 1]
     int *soff1, *soff2; // tensor-core path, single-CTA item offsets [nb + 1]
+    int *woff1, *woff2; // tensor-core path, wide single-CTA item offsets [nb + 1]
     uint8_t *tc_tmaps;  // fast path: [nb][kTcMapCount] tensor maps
     int h_rows;         // rows of h and y
     int *tmaps_dirty; // set when build_tmaps_kernel rewrote a map this call
@@ -275,6 +276,8 @@ void carve_run(Carve &cv, RunWs &w, int nb, int D, int I, bool fast, int rows_ca
     w.toff2 = cv.take<int>(nb + 1);
     w.soff1 = cv.take<int>(nb + 1);
     w.soff2 = cv.take<int>(nb + 1);
+    w.woff1 = cv.take<int>(nb + 1);
+    w.woff2 = cv.take<int>(nb + 1);
     w.tc_tmaps = fast ? cv.take<uint8_t>(size_t(nb) * kTcMapCount * kTcMapBytes) : nullptr;
     w.h_rows = std::max(rows_cap, 1);
     const size_t esz = fast ? 2 : 4;
@@ -456,17 +459,17 @@ int make_tok_map(CUtensorMap *m, const void *rows_ptr, int cols, int rows) {
                      kTcTokBox, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int FMT, int PHASE, bool PAIR>
+template <int FMT, int PHASE, bool PAIR, bool WIDE = false>
 int launch_tc_t(const TcArgs &a, const CUtensorMap &tok, cudaStream_t st, int sms) {
-    using L = TcLayout<PAIR>;
-    auto kern = tc_ffn_kernel<FMT, PHASE, PAIR>;
+    using L = TcLayout<PAIR, WIDE>;
+    auto kern = tc_ffn_kernel<FMT, PHASE, PAIR, WIDE>;
     static bool attr = false;
     if (!attr) {
         CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
         attr = true;
     }
     cudaLaunchConfig_t cfg{};
-    cfg.blockDim = dim3(TcCfg<PAIR>::THREADS);
+    cfg.blockDim = dim3(TcCfg<PAIR, WIDE>::THREADS);
     cfg.dynamicSmemBytes = L::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
@@ -480,20 +483,27 @@ int launch_tc_t(const TcArgs &a, const CUtensorMap &tok, cudaStream_t st, int sm
         cfg.attrs = at;
         cfg.numAttrs = 1;
     } else {
-        cfg.gridDim = dim3(sms * TcCfg<PAIR>::CTAS_PER_SM);
+        cfg.gridDim = dim3(sms * TcCfg<PAIR, WIDE>::CTAS_PER_SM);
     }
     CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, tok));
     return MVLLM_OK;
 }
 
 template <int PHASE>
-int launch_tc(int fmt, const TcArgs &pair, const TcArgs &solo, const CUtensorMap &tok,
-              cudaStream_t st, int sms) {
+int launch_tc(int fmt, const TcArgs &pair, const TcArgs &solo, const TcArgs *wide,
+              const CUtensorMap &tok, cudaStream_t st, int sms) {
     int rc = fmt == MVLLM_FMT_MXFP4
                  ? launch_tc_t<MVLLM_FMT_MXFP4, PHASE, true>(pair, tok, st, sms)
                  : launch_tc_t<MVLLM_FMT_INT4_G64, PHASE, true>(pair, tok, st, sms);
     if (rc)
         return rc;
+    if (wide) {
+        rc = fmt == MVLLM_FMT_MXFP4
+                 ? launch_tc_t<MVLLM_FMT_MXFP4, PHASE, false, true>(*wide, tok, st, sms)
+                 : launch_tc_t<MVLLM_FMT_INT4_G64, PHASE, false, true>(*wide, tok, st, sms);
+        if (rc)
+            return rc;
+    }
     return fmt == MVLLM_FMT_MXFP4 ? launch_tc_t<MVLLM_FMT_MXFP4, PHASE, false>(solo, tok, st, sms)
                                   : launch_tc_t<MVLLM_FMT_INT4_G64, PHASE, false>(solo, tok, st, sms);
 }
@@ -707,6 +717,10 @@ ExpertPlan make_expert_plan(int nb, int D, int I, int fmt, const Tables &tb, con
     pa.tc_sblocks1 = I / tc_cols_per_item<1, false>();
     pa.tc_sblocks2 = D / tc_cols_per_item<2, false>();
     pa.toff1 = w.toff1, pa.toff2 = w.toff2, pa.soff1 = w.soff1, pa.soff2 = w.soff2;
+    // Rests of 65..192 rows on wide single CTAs (f16 mode; the block-scaled
+    // kernels have pairs and single CTAs only).
+    pa.tc_wide = (mx || getenv("MVLLM_TC_NO_WIDE")) ? 0 : kTcWideMax;
+    pa.woff1 = w.woff1, pa.woff2 = w.woff2;
     pa.clear_word = fast ? w.tmaps_dirty : nullptr;
     if (tc_min) {
         pa.roff1 = w.roff1, pa.roff2 = w.roff2, pa.range_word = w.range;
@@ -855,6 +869,7 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             t1.s0 = tb.gs, t1.s1 = tb.us;
             t1.xrow = xoff, t1.orow = w.base, t1.cnt = w.cnt, t1.item_off = w.toff1, t1.nb = nb;
             t1.small_max = pa.tc_small; // the plan's split of each expert's tiles
+            t1.wide_max = pa.tc_wide;
             t1.tshift = pa.tc_shift;
             t1.K = D, t1.O = I, t1.out = w.h;
             t1.act = act, t1.act_a = act_a, t1.act_b = act_b, t1.err = w.err;
@@ -879,8 +894,12 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             if (mx)
                 rc = launch_mx<1>(mode, MxArgs{t1, w.mx_tmaps}, MxArgs{s1, w.mx_tmaps}, tok1, tsc1,
                                   st, sms);
-            else
-                rc = launch_tc<1>(fmt, t1, s1, tok1, st, sms);
+            else {
+                TcArgs w1 = t1;
+                w1.item_off = w.woff1;
+                rc = launch_tc<1>(fmt, t1, s1, pa.tc_wide > pa.tc_small ? &w1 : nullptr, tok1,
+                                  st, sms);
+            }
             if (rc)
                 return rc;
             // Scale codes the tensor-core operands cannot represent: the
@@ -917,8 +936,12 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
             if (mx)
                 rc = launch_mx<2>(mode, MxArgs{t2, w.mx_tmaps}, MxArgs{s2, w.mx_tmaps}, tok2, tsc2,
                                   st, sms);
-            else
-                rc = launch_tc<2>(fmt, t2, s2, tok2, st, sms);
+            else {
+                TcArgs w2 = t2;
+                w2.item_off = w.woff2;
+                rc = launch_tc<2>(fmt, t2, s2, pa.tc_wide > pa.tc_small ? &w2 : nullptr, tok2,
+                                  st, sms);
+            }
             if (rc)
                 return rc;
             DecodeArgs r = b;

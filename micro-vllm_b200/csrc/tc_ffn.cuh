@@ -64,35 +64,43 @@ constexpr int kTcTokBox = 64;     // token rows per TMA box
 constexpr int kTcPkSlots = 8;     // packed-weight ring depth (2 k-blocks per slot)
 constexpr int kTcScSlots = 3;     // scale ring depth (one 16-byte window per row per slot)
 constexpr int kTcSoloMax = 64;    // token tiles of at most this many rows run on single CTAs
+constexpr int kTcWideMax = 192;   // ... of at most this many on wide single CTAs (one per SM)
 
-// The two forms of the kernel.  PAIR: CTA pairs, M = 256 weight rows per MMA,
-// token tiles of up to 256 rows, one CTA per SM.  Solo: one CTA, M = 128,
-// token tiles of up to 64 rows, two CTAs per SM.  A pair MMA takes about 108
-// cycles to issue whatever its N (measured on B200), a single-CTA MMA about
-// 45: the pair wins once N passes 128 (an N = 256 pair MMA runs at the tensor
-// rate), while a tile of a few dozen tokens is bound by issue, so it runs on
-// single CTAs, two per SM, each with its own issuing thread.
-template <bool PAIR> struct TcCfg {
-    static constexpr int EPI_WARPS = PAIR ? 8 : 4; // quadrant = warp % 4, chunk half = warp / 4
-    static constexpr int DQ_SETS = PAIR ? 2 : 1;   // sets of 4 dequant warps (k-block parity)
+// The three forms of the kernel.  PAIR: CTA pairs, M = 256 weight rows per
+// MMA, token tiles of up to 256 rows, one CTA per SM.  Solo: one CTA, M = 128,
+// token tiles of up to 64 rows, two CTAs per SM.  WIDE solo: one CTA per SM,
+// M = 128, token tiles of up to kTcWideMax rows, eight dequant and eight
+// epilogue warps.  A pair MMA takes about 108 cycles to issue whatever its N
+// (measured on B200), a single-CTA MMA about 45: the pair wins at N = 256 (it
+// runs at the tensor rate), a tile of a few dozen tokens is bound by issue,
+// so it runs on single CTAs, two per SM, each with its own issuing thread;
+// between the two (a 65..192-row rest, e.g. 171 rows per expert at config[4]),
+// one CTA per SM is bound by the tensor rate (N = 176: about 93 cycles of
+// tensor time per MMA against 45 of issue) where a pair would be bound by
+// its issue.
+template <bool PAIR, bool WIDE = false> struct TcCfg {
+    static constexpr bool BIG = PAIR || WIDE;     // one CTA per SM, 8 + 8 warps
+    static constexpr int EPI_WARPS = BIG ? 8 : 4; // quadrant = warp % 4, chunk half = warp / 4
+    static constexpr int DQ_SETS = BIG ? 2 : 1;   // sets of 4 dequant warps (k-block parity)
     static constexpr int DQ_WARP0 = EPI_WARPS;
     static constexpr int DQ_WARPS = 4 * DQ_SETS;
     static constexpr int PROD_WARP = DQ_WARP0 + DQ_WARPS;
     static constexpr int MMA_WARP = PROD_WARP + 1;
     static constexpr int PK_WARP = PROD_WARP + 2;
     static constexpr int THREADS = (PK_WARP + 1) * 32; // 608 / 352
-    static constexpr int CTAS_PER_SM = PAIR ? 1 : 2;
-    static constexpr int NT = PAIR ? 256 : kTcSoloMax; // token tile of an item
+    static constexpr int CTAS_PER_SM = BIG ? 1 : 2;
+    static constexpr int NT = PAIR ? 256 : WIDE ? kTcWideMax : kTcSoloMax; // item token tile
     static constexpr int NALIGN = PAIR ? 32 : 16;      // MMA N granularity
-    static constexpr int ACC_HALF = PAIR ? 128 : 64;   // TMEM columns of one accumulator half
+    static constexpr int ACC_HALF = BIG ? 128 : 64;    // TMEM columns of one accumulator half
     static constexpr int A_BASE = 2 * ACC_HALF;
-    static constexpr int STAGES = PAIR ? 4 : 2;        // token + A operand ring (2 k-blocks each)
+    static constexpr int STAGES = PAIR ? 4 : WIDE ? 3 : 2; // token + A ring (2 k-blocks each)
     static constexpr int PK_SLOTS = kTcPkSlots;        // packed-weight ring depth
-    static constexpr int TMEM_COLS = PAIR ? 512 : 256;
+    static constexpr int TMEM_COLS = BIG ? 512 : 256;
     static constexpr int TOK_ROWS = PAIR ? NT / 2 : NT; // token rows one CTA holds
-    static constexpr int FULL_ARRIVALS = 1 + (PAIR ? 16 : 4); // producer + dequant warps
+    static constexpr int FULL_ARRIVALS = 1 + (PAIR ? 16 : DQ_WARPS); // producer + dequant warps
     static constexpr int ACC_EMPTY_ARRIVALS = PAIR ? 2 * EPI_WARPS : EPI_WARPS;
     static_assert(A_BASE + STAGES * 64 <= TMEM_COLS, "TMEM budget");
+    static_assert(NT <= 2 * ACC_HALF, "accumulator columns");
 };
 enum { kTcGateP = 0, kTcUpP, kTcDownP, kTcGateS, kTcUpS, kTcDownS, kTcMapCount };
 constexpr int kTcMapBytes = 128;
@@ -107,6 +115,7 @@ struct TcArgs {
     const int *cnt;           // per expert: rows on this path (0 = decode path)
     const int *item_off;      // [nb + 1] item prefix of this list
     int small_max;            // rest tiles of at most this many rows are single-CTA items
+    int wide_max;             // ... of at most this many (above small_max) wide items
     int tshift;               // pair token tiles are 2^tshift rows (the plan's split)
     int nb;
     int K, O;                 // reduction length, output width (I or D)
@@ -134,8 +143,8 @@ __device__ __forceinline__ void flag_range(const TcArgs &p) {
 // one 64-column A stage (128 weight rows x 128 f16: two k-blocks) per ring
 // stage.  A stage holds two k-blocks so that one wait and one commit cover
 // eight MMAs.
-template <bool PAIR> struct TcLayout {
-    using C = TcCfg<PAIR>;
+template <bool PAIR, bool WIDE = false> struct TcLayout {
+    using C = TcCfg<PAIR, WIDE>;
     static constexpr int TOK_KB = C::TOK_ROWS * 128;   // this CTA's token rows, one k-block
     static constexpr int TOK_STAGE = 2 * TOK_KB;        // a stage holds two k-blocks
     static constexpr int PK_STAGE = 128 * 64;           // 128 weight rows x 64 B (2 k-blocks)
@@ -326,9 +335,9 @@ struct TcItemTab {
     const int *cnt; // [nb] rows per expert
 };
 
-template <int PHASE, bool PAIR>
+template <int PHASE, bool PAIR, bool WIDE = false>
 __device__ __forceinline__ void tc_item(const TcArgs &p, const TcItemTab &tab, int i, TcItem &it) {
-    using C = TcCfg<PAIR>;
+    using C = TcCfg<PAIR, WIDE>;
     int lo = 0, hi = p.nb;
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
@@ -340,8 +349,8 @@ __device__ __forceinline__ void tc_item(const TcArgs &p, const TcItemTab &tab, i
     const int e = lo;
     const int local = i - tab.off[e];
     const int c = tab.cnt[e];
-    int npair, nsolo;
-    tc_tiles(c, p.small_max, p.tshift, npair, nsolo);
+    int npair, nsolo, nwide;
+    tc_tiles3(c, p.small_max, p.wide_max, p.tshift, npair, nsolo, nwide);
     const int ntt = PAIR ? npair : 1;
     const int wg = local / ntt, tt = local - wg * ntt;
     it.e = e;
@@ -400,12 +409,12 @@ __device__ __forceinline__ void tc_dequant_row(const uint4 &w0, const uint4 &w1,
 // token's value is their sum; ACC_STRIDE is the column offset of the second
 // accumulator buffer.  With the defaults the layout is tc_ffn's.
 template <int FMT, int PHASE, bool PAIR, int NSUM = 1, int SUM_STRIDE = 0,
-          int ACC_STRIDE = TcCfg<PAIR>::ACC_HALF, int MAXN = TcCfg<PAIR>::NT>
+          int ACC_STRIDE = TcCfg<PAIR>::ACC_HALF, int MAXN = TcCfg<PAIR>::NT, bool WIDE = false>
 __device__ __forceinline__ void tc_epilogue(const TcArgs &p, const TcItemTab &tab, int unit,
                                             int nunits, int total, uint32_t tmem, uint32_t rank,
                                             uint64_t *acc_full, uint64_t *acc_empty, int warp,
                                             int lane) {
-    using C = TcCfg<PAIR>;
+    using C = TcCfg<PAIR, WIDE>;
     const int q = warp & 3, whalf = warp >> 2;
     constexpr int CH_STEP = 32 * (C::EPI_WARPS / 4);
     const float ia = 1.f / p.act_a, ib = 1.f / p.act_b; // SiTU's divisions, once
@@ -414,7 +423,7 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs &p, const TcItemTab &ta
     bool ok = true;
     for (int i = unit; ok && i < total; i += nunits) {
         TcItem it;
-        tc_item<PHASE, PAIR>(p, tab, i, it);
+        tc_item<PHASE, PAIR, WIDE>(p, tab, i, it);
         const int b = acc.take(NSUM == 1 && it.nmma > C::ACC_HALF);
         bool got = true;
         if (b != 1)
@@ -529,11 +538,11 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs &p, const TcItemTab &ta
     }
 }
 
-template <int FMT, int PHASE, bool PAIR>
-__global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM)
+template <int FMT, int PHASE, bool PAIR, bool WIDE = false>
+__global__ void __launch_bounds__(TcCfg<PAIR, WIDE>::THREADS, TcCfg<PAIR, WIDE>::CTAS_PER_SM)
     tc_ffn_kernel(const TcArgs p, const __grid_constant__ CUtensorMap tok_map) {
-    using C = TcCfg<PAIR>;
-    using L = TcLayout<PAIR>;
+    using C = TcCfg<PAIR, WIDE>;
+    using L = TcLayout<PAIR, WIDE>;
     constexpr int S = C::STAGES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -618,7 +627,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
             bool ok = true;
             for (int i = unit; ok && i < total; i += nunits) {
                 TcItem it;
-                tc_item<PHASE, PAIR>(p, tab, i, it);
+                tc_item<PHASE, PAIR, WIDE>(p, tab, i, it);
                 const int rows = PAIR ? it.nmma >> 1 : it.nmma; // this CTA's token rows
                 const int xr = __ldg(p.xrow + it.e) + it.t0 + static_cast<int>(rank) * rows;
                 const int nbox = (rows + kTcTokBox - 1) / kTcTokBox;
@@ -667,7 +676,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
             bool ok = true;
             for (int i = unit; ok && i < total; i += nunits) {
                 TcItem it;
-                tc_item<PHASE, PAIR>(p, tab, i, it);
+                tc_item<PHASE, PAIR, WIDE>(p, tab, i, it);
                 const uint8_t *tm = p.tmaps + static_cast<size_t>(it.e) * kTcMapCount * kTcMapBytes;
                 if (fence_maps)
                     for (int m = 0; m < kTcMapCount; ++m)
@@ -730,7 +739,7 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
             const uint32_t tok_base = smem_u32(smem);
             for (int i = unit; ok && i < total; i += nunits) {
                 TcItem it;
-                tc_item<PHASE, PAIR>(p, tab, i, it);
+                tc_item<PHASE, PAIR, WIDE>(p, tab, i, it);
                 const int b = acc.take(it.nmma > C::ACC_HALF);
                 if (b != 1 && !mbar_wait(&acc_empty[0], (acc.use[0] & 1u) ^ 1u, p.err))
                     ok = false;
@@ -903,7 +912,8 @@ __global__ void __launch_bounds__(TcCfg<PAIR>::THREADS, TcCfg<PAIR>::CTAS_PER_SM
             }
         }
     } else if (warp < C::EPI_WARPS) {
-        tc_epilogue<FMT, PHASE, PAIR>(p, tab, unit, nunits, total, tmem, rank, acc_full, acc_empty,
+        tc_epilogue<FMT, PHASE, PAIR, 1, 0, C::ACC_HALF, C::NT, WIDE>(
+            p, tab, unit, nunits, total, tmem, rank, acc_full, acc_empty,
                                       warp, lane);
     }
 
