@@ -14,7 +14,8 @@ rank r, for r's own tokens:
   3. pack      token rows, per-slot local expert ids (-1 where another rank
                owns the slot) and weights into the send buffer
                                                      (mvllm_moe_ep_pack_dev)
-  4. dispatch  all-to-all of rows, ids and weights                (NCCL)
+  4. dispatch  all-to-all of the rows, and one of ids + weights (one int32
+               buffer)                                           (NCCL)
   5. compute   the received rows through r's local experts: the routed layer
                on device (mvllm_moe_layer_dev) with E = r's expert count;
                slots marked -1 are skipped by its permutation
@@ -224,6 +225,18 @@ class EPLayer:
     def pack(self, x, idx, wt, pos, send_splits):
         return self.ops.pack(x, idx, wt, pos, int(sum(send_splits)))
 
+    def _meta(self, sidx, swt):
+        """The send rows' expert ids and weights in one int32 buffer [rows, 2K]
+        (the weights as their f32 bits), so both travel in one exchange.  The
+        token rows stay a buffer of their own: they are the experts' operand,
+        read in place on arrival."""
+        t = self.ops.torch
+        return t.cat([sidx, swt.view(t.int32)], dim=1)
+
+    def _split_meta(self, rmeta):
+        t = self.ops.torch
+        return rmeta[:, :self.K].contiguous(), rmeta[:, self.K:].contiguous().view(t.float32)
+
     def forward_local(self, x, idx, wt, out):
         """One rank: the single-GPU routed layer (mvllm_moe_layer_dev over all
         experts, out += layer(x)); no plan, pack, exchange or combine."""
@@ -250,10 +263,11 @@ class EPLayer:
         N = self.nranks
         pos, _ = self.ops.plan_fixed(idx, T)
         sx, sidx, swt = self.ops.pack_fixed(x, idx, wt, pos, N * T)
-        rx, ridx, rwt = t.empty_like(sx), t.empty_like(sidx), t.empty_like(swt)
+        smeta = self._meta(sidx, swt)
+        rx, rmeta = t.empty_like(sx), t.empty_like(smeta)
         dist.all_to_all_single(rx, sx, group=group)
-        dist.all_to_all_single(ridx, sidx, group=group)
-        dist.all_to_all_single(rwt, swt, group=group)
+        dist.all_to_all_single(rmeta, smeta, group=group)
+        ridx, rwt = self._split_meta(rmeta)
         part = self.ops.compute(rx, ridx, rwt)
         back = t.empty_like(part)
         dist.all_to_all_single(back, part, group=group)
@@ -287,17 +301,15 @@ class EPLayer:
         recv, works = [], []
         for c in range(C):
             sx, sidx, swt = self.pack(x[sl[c]], idx[sl[c]], wt[sl[c]], plans[c][0], sc[c])
+            smeta = self._meta(sidx, swt)
             R = sum(rc[c])
             rx = t.empty((R, self.D), dtype=x.dtype, device=x.device)
-            ridx = t.empty((R, self.K), dtype=t.int32, device=x.device)
-            rwt = t.empty((R, self.K), dtype=t.float32, device=x.device)
+            rmeta = t.empty((R, 2 * self.K), dtype=t.int32, device=x.device)
             works.append([dist.all_to_all_single(rx, sx, rc[c], sc[c], group=group,
                                                  async_op=True),
-                          dist.all_to_all_single(ridx, sidx, rc[c], sc[c], group=group,
-                                                 async_op=True),
-                          dist.all_to_all_single(rwt, swt, rc[c], sc[c], group=group,
+                          dist.all_to_all_single(rmeta, smeta, rc[c], sc[c], group=group,
                                                  async_op=True)])
-            recv.append((rx, ridx, rwt, sx, sidx, swt))
+            recv.append((rx, rmeta, sx, smeta))
         backs = []
         lim = getattr(self.ops, "set_sm_reserve", None)
         if lim and N > 1:
@@ -306,7 +318,8 @@ class EPLayer:
             for c in range(C):
                 for w in works[c]:
                     w.wait()
-                rx, ridx, rwt = recv[c][:3]
+                rx, rmeta = recv[c][:2]
+                ridx, rwt = self._split_meta(rmeta)
                 part = self.ops.compute(rx, ridx, rwt)
                 back = t.empty((sum(sc[c]),) + tuple(part.shape[1:]), dtype=part.dtype,
                                device=x.device)
@@ -343,14 +356,14 @@ class EPLayer:
         rc = [int(v) for v in rcnt.tolist()]
         mark()
         sx, sidx, swt = self.pack(x, idx, wt, pos, sc)
+        smeta = self._meta(sidx, swt)
         R = sum(rc)
         rx = t.empty((R, self.D), dtype=x.dtype, device=x.device)
-        ridx = t.empty((R, self.K), dtype=t.int32, device=x.device)
-        rwt = t.empty((R, self.K), dtype=t.float32, device=x.device)
+        rmeta = t.empty((R, 2 * self.K), dtype=t.int32, device=x.device)
         mark()
         dist.all_to_all_single(rx, sx, rc, sc, group=group)
-        dist.all_to_all_single(ridx, sidx, rc, sc, group=group)
-        dist.all_to_all_single(rwt, swt, rc, sc, group=group)
+        dist.all_to_all_single(rmeta, smeta, rc, sc, group=group)
+        ridx, rwt = self._split_meta(rmeta)
         mark()
         part = self.ops.compute(rx, ridx, rwt)
         mark()
