@@ -1189,13 +1189,16 @@ def run_reference(args):
 
 # -------------------------------------------------------------------- ours --
 def launches_per_ep_step(world, mode):
-    """This library's kernels in one config[4] step (NCCL's own kernels not
-    counted): EP plan and pack (N > 1), the routed layer over the received
-    rows (permutation: memset + 4 kernels at these sizes; gather; expert plan;
-    2 tensor-map builds; phase 1 and phase 2 each on the decode kernel, CTA
-    pairs and single CTAs; the block-scaled modes add 2 term-quantisation
-    kernels; combine), and the EP combine (N > 1)."""
-    layer = 4 + 1 + 1 + 2 + 3 + 3 + 1 + (2 if mode != "f16" else 0)
+    """This library's kernels in one config[4] step (NCCL's and torch's own
+    kernels not counted): EP plan and pack (N > 1), the routed layer over the
+    received rows (permutation: 4 kernels at these sizes; gather; expert plan;
+    2 tensor-map builds; each phase on the decode kernel, the tensor-core
+    kernels (f16: pairs, wide and small single CTAs; block-scaled: pairs and
+    single CTAs, plus one term-quantisation kernel) and the redo launch;
+    combine), and the EP combine (N > 1).  19 per step at one GPU, as the
+    committed launch list (profiles/headline_config4_one_gpu.txt) shows."""
+    per_phase = 5  # decode, 3 (f16) or 2 + terms (block-scaled) tensor-core launches, redo
+    layer = 4 + 1 + 1 + 2 + 2 * per_phase + 1
     return layer + (3 if world > 1 else 0)
 
 
@@ -1385,7 +1388,8 @@ def main():
                          "frac": achieved / tpeak, "peak_kind": tpeak_kind,
                          "traffic": headline_traffic() if world == 1 and mode == "f16" else None,
                          "traffic_source": "DRAM read + write per launch of the dominant kernel "
-                                           "(tc_ffn phase-1 pairs) at full size, from the "
+                                           "(tc_ffn phase 1, wide single CTAs) at full size, "
+                                           "from the "
                                            "committed ncu summary "
                                            "profiles/headline_config4_one_gpu.txt (a 48-expert "
                                            "capture with the same rows per expert, x 8); not "

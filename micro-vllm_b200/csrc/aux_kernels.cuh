@@ -41,6 +41,52 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int *warp_sums, int *
     return before;
 }
 
+// NV exclusive block scans at once (one set of barriers for all of them):
+// v[k] -> the sum of v[k] over the lower threads, tot[k] the block's total.
+// warp_sums holds NV x 32 ints.
+template <int NV>
+__device__ __forceinline__ void block_exclusive_scan_n(int (&v)[NV], int *warp_sums,
+                                                       int (&tot)[NV]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = blockDim.x >> 5;
+    int x[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        x[k] = v[k];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x[k], o);
+            if (lane >= o)
+                x[k] += y;
+        }
+        if (lane == 31)
+            warp_sums[k * 32 + warp] = x[k];
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            int s = lane < nwarps ? warp_sums[k * 32 + lane] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, s, o);
+                if (lane >= o)
+                    s += y;
+            }
+            if (lane < nwarps)
+                warp_sums[k * 32 + lane] = s; // inclusive
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int before = (warp > 0 ? warp_sums[k * 32 + warp - 1] : 0) + x[k] - v[k];
+        tot[k] = warp_sums[k * 32 + nwarps - 1];
+        v[k] = before;
+    }
+    __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // Plan (one CTA): the reference's per-expert bookkeeping of cpu_moe_block
 // (src/gpu/metal_ops.cpp:285-300): base advances by nr for every expert with
@@ -79,7 +125,7 @@ struct PlanArgs {
 };
 
 __device__ __forceinline__ void plan_body(const PlanArgs &a) {
-    __shared__ int warp_sums[32];
+    __shared__ int warp_sums[11 * 32];
     __shared__ int carry[11];
     if (threadIdx.x < 11)
         carry[threadIdx.x] = 0;
@@ -126,61 +172,31 @@ __device__ __forceinline__ void plan_body(const PlanArgs &a) {
                 i2 = c ? a.blocks2 * ((c + a.chunk2 - 1) / a.chunk2) : 0;
             }
         }
-        int tot;
-        const int b = block_exclusive_scan(n, warp_sums, &tot);
-        int t1;
-        const int o1 = block_exclusive_scan(i1, warp_sums, &t1);
-        int t2;
-        const int o2 = block_exclusive_scan(i2, warp_sums, &t2);
-        int u1;
-        const int p1 = block_exclusive_scan(j1, warp_sums, &u1);
-        int u2;
-        const int p2 = block_exclusive_scan(j2, warp_sums, &u2);
-        int v1;
-        const int q1 = block_exclusive_scan(k1, warp_sums, &v1);
-        int v2;
-        const int q2 = block_exclusive_scan(k2, warp_sums, &v2);
-        int w1 = 0, w2 = 0, x1 = 0, x2 = 0, z1 = 0, z2 = 0, y1 = 0, y2 = 0;
-        if (a.roff1) {
-            x1 = block_exclusive_scan(r1, warp_sums, &w1);
-            x2 = block_exclusive_scan(r2, warp_sums, &w2);
-        }
-        if (a.woff1) {
-            y1 = block_exclusive_scan(m1, warp_sums, &z1);
-            y2 = block_exclusive_scan(m2, warp_sums, &z2);
-        }
+        // One scan of all eleven lists: rows, decode items, pair / single /
+        // redo / wide items of both phases.
+        int v[11] = {n, i1, i2, j1, j2, k1, k2, r1, r2, m1, m2}, tot[11];
+        block_exclusive_scan_n<11>(v, warp_sums, tot);
         if (e < a.nb) {
-            a.base[e] = carry[0] + b;
+            a.base[e] = carry[0] + v[0];
             a.cnt[e] = c;
-            a.off1[e] = carry[1] + o1;
-            a.off2[e] = carry[2] + o2;
-            a.toff1[e] = carry[3] + p1;
-            a.toff2[e] = carry[4] + p2;
-            a.soff1[e] = carry[5] + q1;
-            a.soff2[e] = carry[6] + q2;
+            a.off1[e] = carry[1] + v[1];
+            a.off2[e] = carry[2] + v[2];
+            a.toff1[e] = carry[3] + v[3];
+            a.toff2[e] = carry[4] + v[4];
+            a.soff1[e] = carry[5] + v[5];
+            a.soff2[e] = carry[6] + v[6];
             if (a.roff1) {
-                a.roff1[e] = carry[7] + x1;
-                a.roff2[e] = carry[8] + x2;
+                a.roff1[e] = carry[7] + v[7];
+                a.roff2[e] = carry[8] + v[8];
             }
             if (a.woff1) {
-                a.woff1[e] = carry[9] + y1;
-                a.woff2[e] = carry[10] + y2;
+                a.woff1[e] = carry[9] + v[9];
+                a.woff2[e] = carry[10] + v[10];
             }
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            carry[0] += tot;
-            carry[1] += t1;
-            carry[2] += t2;
-            carry[3] += u1;
-            carry[4] += u2;
-            carry[5] += v1;
-            carry[6] += v2;
-            carry[7] += w1;
-            carry[8] += w2;
-            carry[9] += z1;
-            carry[10] += z2;
-        }
+        if (threadIdx.x < 11)
+            carry[threadIdx.x] += tot[threadIdx.x];
         __syncthreads();
     }
     if (threadIdx.x == 0) {
