@@ -61,9 +61,10 @@ enum {
                                   their tensor-core kernels raise a redo word and the decode
                                   kernels recompute the call's tensor-core experts on the
                                   device, in the same call */
-    MVLLM_ERR_ACT_RANGE = 10   /* a finite activation (a token row of x, or h = act(gate, up))
-                                  beyond the f16 operand range (|v| >= 65520): the reference
-                                  computes it in f32; this library refuses the call instead of
+    MVLLM_ERR_ACT_RANGE = 10   /* a finite activation (a token row of x, h = act(gate, up),
+                                  or an expert's output row y before its routing weight)
+                                  beyond the f16 range (|v| >= 65520): the reference computes
+                                  it in f32; this library refuses the call instead of
                                   returning inf */
 };
 

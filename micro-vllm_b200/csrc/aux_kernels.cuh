@@ -638,10 +638,25 @@ __global__ void __launch_bounds__(1024) layer_prep_small_kernel(const PermSmallA
 }
 
 // ---------------------------------------------------------------------------
+// Rows of the experts' outputs y: f16 on the fast path (the decode and
+// tensor-core kernels write them), f32 on the generic path.
+__device__ __forceinline__ float4 load_y4(const float *y, size_t i) {
+    return __ldcs(reinterpret_cast<const float4 *>(y + i));
+}
+__device__ __forceinline__ float4 load_y4(const __half *y, size_t i) {
+    const uint2 u = __ldcs(reinterpret_cast<const uint2 *>(y + i));
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ float load_y1(const float *y, size_t i) { return y[i]; }
+__device__ __forceinline__ float load_y1(const __half *y, size_t i) { return __half2float(y[i]); }
+
 // Ordered combine, layer form: out[c] += wsum*y over the token's segment
 // positions in ascending order (= ascending expert id), one multiply and one
 // add per term as in glm53.cpp:1978-1984 (no fused multiply-add).
-__global__ void combine_tokens_kernel(float *__restrict__ out, const float *__restrict__ y,
+template <typename TY>
+__global__ void combine_tokens_kernel(float *__restrict__ out, const TY *__restrict__ y,
                                       const float *__restrict__ rw,
                                       const int *__restrict__ tok_pos, int T, int KK, int D,
                                       const int *err) {
@@ -677,8 +692,7 @@ __global__ void combine_tokens_kernel(float *__restrict__ out, const float *__re
                     if (j0 + b < n) {
                         const int r = pos[j0 + b];
                         w[b] = __ldg(rw + r);
-                        v[b] = __ldcs(reinterpret_cast<const float4 *>(y + static_cast<size_t>(r) * D +
-                                                                       col));
+                        v[b] = load_y4(y, static_cast<size_t>(r) * D + col);
                     }
                 }
 #pragma unroll
@@ -703,7 +717,8 @@ __global__ void combine_tokens_kernel(float *__restrict__ out, const float *__re
 // tail.  Row pitch 2*D + 16 bytes; relative error at most 2^-11 per element
 // (f16 rounding), half the bytes of f32 rows.  One CTA per token at a time,
 // the f32 row staged in shared memory (D floats) for the row maximum.
-__global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const float *__restrict__ y,
+template <typename TY>
+__global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const TY *__restrict__ y,
                                           const float *__restrict__ rw,
                                           const int *__restrict__ tok_pos, int T, int KK, int D,
                                           const int *err) {
@@ -734,8 +749,8 @@ __global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const flo
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int j = 0; j < n; ++j) {
                 const float w = rw[pos[j]];
-                const float4 a = __ldcs(reinterpret_cast<const float4 *>(
-                    y + static_cast<size_t>(pos[j]) * D + 4 * static_cast<size_t>(v)));
+                const float4 a = load_y4(y, static_cast<size_t>(pos[j]) * D +
+                                                4 * static_cast<size_t>(v));
                 acc.x = __fadd_rn(acc.x, __fmul_rn(w, a.x));
                 acc.y = __fadd_rn(acc.y, __fmul_rn(w, a.y));
                 acc.z = __fadd_rn(acc.z, __fmul_rn(w, a.z));
@@ -776,7 +791,8 @@ __global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const flo
 
 // Ordered combine, moe_block form: CSR of destination rows (row ids ascending
 // within each destination), scatter order of metal_ops.cpp:328-339.
-__global__ void combine_csr_kernel(float *__restrict__ out, const float *__restrict__ y,
+template <typename TY>
+__global__ void combine_csr_kernel(float *__restrict__ out, const TY *__restrict__ y,
                                    const float *__restrict__ rw, const int *__restrict__ off,
                                    const int *__restrict__ ids, int S, int D) {
     for (int s = blockIdx.y; s < S; s += gridDim.y) {
@@ -787,7 +803,7 @@ __global__ void combine_csr_kernel(float *__restrict__ out, const float *__restr
         float acc = out[static_cast<size_t>(s) * D + col];
         for (int j = j0; j < j1; ++j) {
             const int r = ids[j];
-            acc = __fadd_rn(acc, __fmul_rn(rw[r], y[static_cast<size_t>(r) * D + col]));
+            acc = __fadd_rn(acc, __fmul_rn(rw[r], load_y1(y, static_cast<size_t>(r) * D + col)));
         }
         out[static_cast<size_t>(s) * D + col] = acc;
     }

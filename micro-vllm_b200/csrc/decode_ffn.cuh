@@ -6,7 +6,8 @@
 //   phase 1: item = (expert, 32 gate rows + the matching 32 up rows, chunk of
 //            <= 8*NT tokens) -> h = act(gate, up), f16, written straight into
 //            the operand layout phase 2 reads;
-//   phase 2: item = (expert, 64 down rows, chunk) -> y, f32.
+//   phase 2: item = (expert, 64 down rows, chunk) -> y, f16 (a value beyond
+//            the f16 range records MVLLM_ERR_ACT_RANGE).
 //
 // CTA = 16 consumer warps (4 row blocks x 4 K quarters of a stage, 4 warps per
 // scheduler) + 2 producer warps + 2 epilogue warps.  Each stage of the
@@ -497,14 +498,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_ffn_kernel(const Dec
                             __float2half_rn(hv);
                     }
                 } else {
-                    float *y = static_cast<float *>(p.out);
+                    __half *y = static_cast<__half *>(p.out); // f16 rows of y
                     for (int idx = et; idx < kDecodeRows * nv; idx += kDecodeEpilogue) {
                         const int r = idx & 63, n = idx >> 6;
                         float v = 0.f;
 #pragma unroll
                         for (int q = 0; q < kDecodeKParts; ++q)
                             v += rd[(q * kDecodeRows + r) * L::RS + n];
-                        y[static_cast<size_t>(orow0 + n) * p.O + rb * 64 + r] = v;
+                        if (beyond_f16(v))
+                            set_error(p.err, MVLLM_ERR_ACT_RANGE);
+                        y[static_cast<size_t>(orow0 + n) * p.O + rb * 64 + r] =
+                            __float2half_rn(v);
                     }
                 }
             }

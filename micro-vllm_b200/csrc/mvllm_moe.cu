@@ -249,7 +249,8 @@ struct RunWs {
     uint8_t *tmaps;   // fast path: [nb][6] tensor maps
     void *xs; // staged operand (fast: f16, generic: f32)
     void *h;  // fast: f16 [rows, I]; generic: f32 [rows, I]
-    float *y; // [rows, D]
+    float *y; // [rows, D]: f16 rows on the fast path (y16), f32 on the generic path
+    bool y16;
     // Block-scaled tensor-core path (fast path only): per-expert weight maps,
     // and the token operands as block-scaled terms (planes + ue8m0 codes) of
     // x [x_rows, D] and h [h_rows, I], sized for the widest mode.
@@ -776,6 +777,7 @@ int run_experts(cudaStream_t st, int sms, int nb, int D, int I, int fmt, const T
                                                  allow_tc);
     const PlanArgs &pa = ep.pa;
     const bool fast = ep.fast, mx = ep.mx;
+    w.y16 = fast; // the decode and tensor-core kernels write f16 rows of y
     const int tc_min = ep.tc_min, mode = ep.mode, nt = ep.nt;
     if (!pre)
         CUDA_TRY(launch_pdl(plan_kernel, dim3(1), dim3(1024), 0, st, pa));
@@ -1791,10 +1793,15 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     CUDA_TRY(cudaStreamWaitEvent(c.stream, c.out_in, 0));
     {
         dim3 grid((D + 255) / 256, std::min(S_ext, 65535));
-        combine_csr_kernel<<<grid, 256, 0, c.stream>>>(
-            d_out, w.y, reinterpret_cast<const float *>(db + o_rw),
-            reinterpret_cast<const int *>(db + o_coff), reinterpret_cast<const int *>(db + o_cids),
-            S_ext, D);
+        const float *crw = reinterpret_cast<const float *>(db + o_rw);
+        const int *coff = reinterpret_cast<const int *>(db + o_coff);
+        const int *cids = reinterpret_cast<const int *>(db + o_cids);
+        if (w.y16)
+            combine_csr_kernel<__half><<<grid, 256, 0, c.stream>>>(
+                d_out, reinterpret_cast<const __half *>(w.y), crw, coff, cids, S_ext, D);
+        else
+            combine_csr_kernel<float><<<grid, 256, 0, c.stream>>>(d_out, w.y, crw, coff, cids,
+                                                                   S_ext, D);
         CUDA_TRY(cudaGetLastError());
         prof_mark(c.stream, kPhCombine);
     }
@@ -1895,7 +1902,11 @@ int mvllm_moe_block_dev(void *stream, int nb, int D, int Iinter, int fmt, const 
     build_csr_kernel<<<1, 1024, 0, st>>>(rows, w.base, w.cnt, nb, w.total_rows, S, hist, off, ids);
     CUDA_TRY(cudaGetLastError());
     dim3 grid((D + 255) / 256, std::min(S, 65535));
-    combine_csr_kernel<<<grid, 256, 0, st>>>(out, w.y, rw, off, ids, S, D);
+    if (w.y16)
+        combine_csr_kernel<__half><<<grid, 256, 0, st>>>(
+            out, reinterpret_cast<const __half *>(w.y), rw, off, ids, S, D);
+    else
+        combine_csr_kernel<float><<<grid, 256, 0, st>>>(out, w.y, rw, off, ids, S, D);
     CUDA_TRY(cudaGetLastError());
     prof_mark(st, kPhCombine);
     return MVLLM_OK;
@@ -2196,18 +2207,35 @@ static int layer_combine(cudaStream_t st, int sms, int T, int KK, int D, float *
             return rc;
     if (out16) {
         const size_t sm = size_t(D) * 4;
-        if (sm > 48 * 1024)
-            CUDA_TRY(cudaFuncSetAttribute(combine_tokens_f16_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
-        combine_tokens_f16_kernel<<<std::min(T, 8 * sms), 256, sm, st>>>(out16, w.y, l.rw,
-                                                                         l.tok_pos, T, KK, D,
-                                                                         w.err);
+        const dim3 grid(std::min(T, 8 * sms));
+        if (w.y16) {
+            if (sm > 48 * 1024)
+                CUDA_TRY(cudaFuncSetAttribute(combine_tokens_f16_kernel<__half>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              int(sm)));
+            combine_tokens_f16_kernel<__half><<<grid, 256, sm, st>>>(
+                out16, reinterpret_cast<const __half *>(w.y), l.rw, l.tok_pos, T, KK, D, w.err);
+        } else {
+            if (sm > 48 * 1024)
+                CUDA_TRY(cudaFuncSetAttribute(combine_tokens_f16_kernel<float>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              int(sm)));
+            combine_tokens_f16_kernel<float><<<grid, 256, sm, st>>>(out16, w.y, l.rw, l.tok_pos,
+                                                                    T, KK, D, w.err);
+        }
     } else {
         dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
-        CUDA_TRY(launch_pdl(combine_tokens_kernel, grid, dim3(256), 0, st, out,
-                            static_cast<const float *>(w.y), static_cast<const float *>(l.rw),
-                            static_cast<const int *>(l.tok_pos), T, KK, D,
-                            static_cast<const int *>(w.err)));
+        if (w.y16)
+            CUDA_TRY(launch_pdl(combine_tokens_kernel<__half>, grid, dim3(256), 0, st, out,
+                                reinterpret_cast<const __half *>(w.y),
+                                static_cast<const float *>(l.rw),
+                                static_cast<const int *>(l.tok_pos), T, KK, D,
+                                static_cast<const int *>(w.err)));
+        else
+            CUDA_TRY(launch_pdl(combine_tokens_kernel<float>, grid, dim3(256), 0, st, out,
+                                static_cast<const float *>(w.y), static_cast<const float *>(l.rw),
+                                static_cast<const int *>(l.tok_pos), T, KK, D,
+                                static_cast<const int *>(w.err)));
     }
     CUDA_TRY(cudaGetLastError());
     prof_mark(st, kPhCombine);

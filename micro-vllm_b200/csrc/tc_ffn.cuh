@@ -4,7 +4,7 @@
 // Same contract as the decode kernels (decode_ffn.cuh): phase 1 computes
 //   h[r, j] = act(sum_k x[r,k] g[j,k], sum_k x[r,k] u[j,k])   (f16, stage_pos order)
 // and phase 2 computes
-//   y[r, n] = sum_j h[r,j] d[n,j]                             (f32)
+//   y[r, n] = sum_j h[r,j] d[n,j]           (f32 sums, stored as f16)
 // for the rows r of every expert the plan gave to this path
 // (reference: moe_block's per-expert loop, metal_ops.cpp:466-509, through
 // matmul_mxfp4 / matmul_int4_g64 in quant.cpp:104-123 / 61-102).
@@ -119,7 +119,7 @@ struct TcArgs {
     int tshift;               // pair token tiles are 2^tshift rows (the plan's split)
     int nb;
     int K, O;                 // reduction length, output width (I or D)
-    void *out;                // phase 1: f16 h [rows, I]; phase 2: f32 y [rows, D]
+    void *out;                // phase 1: f16 h [rows, I]; phase 2: f16 y [rows, D]
     int act;
     float act_a, act_b;
     int *err;
@@ -401,7 +401,7 @@ __device__ __forceinline__ void tc_dequant_row(const uint4 &w0, const uint4 &w1,
 
 // Epilogue warps (quadrant = warp % 4, chunk half = warp / 4): per item,
 // wait for the accumulator, read it (tcgen05.ld), release it, and write
-// phase 1's activations (f16, stage_pos order) or phase 2's rows (f32).  The
+// phase 1's activations (f16, stage_pos order) or phase 2's rows (f16).  The
 // MMA issuer and this loop walk the same item sequence, so both keep the
 // accumulator-half state (TcAccState) identically.
 // NSUM > 1 (the block-scaled kernel's single-CTA form): the accumulator of a
@@ -486,13 +486,18 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs &p, const TcItemTab &ta
                         hpk[j * 8 + (t >> 1)] = hb;
                 }
             } else if (ch + CH_STEP < it.n) {
-                float *yp = static_cast<float *>(p.out);
+                __half *yp = static_cast<__half *>(p.out); // f16 rows of y
                 const int col = it.c0 + static_cast<int>(rank) * 128 + 32 * q + lane;
+                bool big = false;
 #pragma unroll
                 for (int t = 0; t < 32; ++t)
-                    if (ch + t < it.n)
-                        yp[static_cast<size_t>(orow + ch + t) * p.O + col] =
-                            __uint_as_float(v[t]);
+                    if (ch + t < it.n) {
+                        const float yv = __uint_as_float(v[t]);
+                        big |= beyond_f16(yv);
+                        yp[static_cast<size_t>(orow + ch + t) * p.O + col] = __float2half_rn(yv);
+                    }
+                if (big)
+                    set_error(p.err, MVLLM_ERR_ACT_RANGE);
             }
         }
         tc_fence_before();
@@ -524,12 +529,18 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs &p, const TcItemTab &ta
             }
         } else if (nch > 0) {
             const int ch = 32 * whalf + (nch - 1) * CH_STEP;
-            float *yp = static_cast<float *>(p.out);
+            __half *yp = static_cast<__half *>(p.out);
             const int col = it.c0 + static_cast<int>(rank) * 128 + 32 * q + lane;
+            bool big = false;
 #pragma unroll
             for (int t = 0; t < 32; ++t)
-                if (ch + t < it.n)
-                    yp[static_cast<size_t>(orow + ch + t) * p.O + col] = __uint_as_float(v[t]);
+                if (ch + t < it.n) {
+                    const float yv = __uint_as_float(v[t]);
+                    big |= beyond_f16(yv);
+                    yp[static_cast<size_t>(orow + ch + t) * p.O + col] = __float2half_rn(yv);
+                }
+            if (big)
+                set_error(p.err, MVLLM_ERR_ACT_RANGE);
         }
         if (b != 1)
             ++acc.use[0];

@@ -5,7 +5,7 @@
 // Same contract, items and epilogue as tc_ffn.cuh: phase 1 computes
 //   h[r, j] = act(sum_k x[r,k] g[j,k], sum_k x[r,k] u[j,k])   (f16)
 // and phase 2 computes
-//   y[r, n] = sum_j h[r,j] d[n,j]                             (f32)
+//   y[r, n] = sum_j h[r,j] d[n,j]           (f32 sums, stored as f16)
 // for the rows r the plan gave to the tensor-core path (reference:
 // moe_block's per-expert loop, metal_ops.cpp:278-342, through matmul_mxfp4,
 // quant.cpp:298-321).
