@@ -62,10 +62,10 @@ def parse():
     ap.add_argument("--no-decode-configs", action="store_true",
                     help="skip the config[0] and config[2] decode legs")
     ap.add_argument("--ep-steps", type=int, default=20)
-    ap.add_argument("--ep-mode", default="auto", choices=["auto", "compact", "fixed"],
-                    help="exchange segments sized by host counts (compact) or fixed (no host "
-                         "synchronisation; auto: fixed up to 4 GPUs, where nearly every token "
-                         "goes to every rank, compact above)")
+    ap.add_argument("--ep-mode", default="auto", choices=["auto", "compact", "fixed", "peer"],
+                    help="NCCL exchange with segments sized by host counts (compact) or fixed "
+                         "(no host synchronisation), or stores over NVLink into the ranks' "
+                         "IPC-mapped windows (peer); auto: peer up to 4 GPUs, compact above")
     ap.add_argument("--ep-chunks", type=int, default=1,
                     help="token slices per expert-parallel step (N > 1): the exchanges of one "
                          "slice overlap the experts of another")
@@ -778,7 +778,9 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
     (N > 1) each step runs as that many token slices whose exchanges overlap
     the expert kernels (EPLayer.forward_chunked); with `ep_mode` "fixed" the
     exchanges use fixed-size segments and no counts reach the host
-    (EPLayer.forward_fixed)."""
+    (EPLayer.forward_fixed); with "peer" the dispatch and return are stores
+    over NVLink into the ranks' IPC-mapped windows inside the dispatch kernel
+    and the experts' combine kernel (EPLayer.forward_peer)."""
     import ep
     D, I, K = CFG["D"], CFG["I"], CFG["K"]
     u8 = torch.uint8
@@ -838,9 +840,14 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
         idx = idx[rank * T_loc:(rank + 1) * T_loc].contiguous()
         wt = wt[rank * T_loc:(rank + 1) * T_loc].contiguous()
 
+        win = (ep.PeerWindows(torch, world, T_loc, K, D).connect(rank, dist)
+               if world > 1 and ep_mode == "peer" else None)
+
         def step(xx=x, ii=idx, ww=wt, oo=out):
             # out += layer(x): the layer's contract (the residual stream); the
             # rows stay the same buffer from step to step
+            if win is not None:
+                return layer.forward_peer(xx, ii, ww, oo, dist, win)
             if world > 1 and ep_mode == "fixed":
                 return layer.forward_fixed(xx, ii, ww, oo, dist)
             if world > 1 and chunks > 1:
@@ -884,7 +891,10 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
             # One more step with phase events (not part of the timed steps).
             tm = {}
             out.zero_()
-            layer.forward(x, idx, wt, out, dist, timing=tm)
+            if win is not None:
+                layer.forward_peer(x, idx, wt, out, dist, win, timing=tm)
+            else:
+                layer.forward(x, idx, wt, out, dist, timing=tm)
             keys = sorted(tm)
             res[name]["phase_ms_max_over_ranks"] = dict(zip(keys, max_over_ranks(
                 [tm[k] for k in keys])))
@@ -980,13 +990,18 @@ def ep_bench(moe, torch, dist, rank, world, steps, warmup=3, weak=False, clk=Non
                                     "two device buffer sets, H2D and D2H on their own streams "
                                     "overlapping the neighbouring steps' compute",
                           "serial": serial}
+        if win is not None:
+            win.close(dist)
         del layer, ops, tabs, mats
     wcache.clear()
     torch.cuda.empty_cache()
     per = "8192 tokens per rank per step" if weak else "8192 tokens per step"
     return {"workload": "config[4] expert-parallel MXFP4 layer: 384 experts strided over the "
                         f"ranks (hot experts replicated), hidden 7168, inter 2048, top-8, {per}, "
-                        "bf16 activations; NCCL all-to-all dispatch and return",
+                        "bf16 activations; "
+                        + ("one rank: the single-GPU layer, no exchange" if world == 1 else
+                           "dispatch and return as stores over NVLink into IPC-mapped windows"
+                           if ep_mode == "peer" else "dispatch and return over NCCL all-to-all"),
             "n_gpus": world, "scaling": "weak" if weak else "strong", "tokens_per_step": T_all,
             "slices_per_step": chunks if world > 1 else 1,
             "exchange": ep_mode if world > 1 else "none (one rank)",
@@ -1188,6 +1203,13 @@ def run_reference(args):
 
 
 # -------------------------------------------------------------------- ours --
+def auto_ep_mode(world):
+    """The exchange form `--ep-mode auto` picks: stores over NVLink into the
+    ranks' IPC-mapped windows (EPLayer.forward_peer) up to 4 GPUs, where it
+    measured fastest; the compact NCCL form above."""
+    return "peer" if world <= 4 else "compact"
+
+
 def launches_per_ep_step(world, mode):
     """This library's kernels in one config[4] step (NCCL's and torch's own
     kernels not counted): EP plan and pack (N > 1), the routed layer over the
@@ -1286,7 +1308,7 @@ def main():
         PROFILE_HEADLINE = True
         EP_E, EP_T = EP_E // args.profile_scale, EP_T // args.profile_scale
         print(json.dumps(ep_bench(moe, torch, dist, rank, world, 2, args.warmup,
-                                  ep_mode="fixed" if world <= 4 else "compact")), flush=True)
+                                  ep_mode=auto_ep_mode(world))), flush=True)
         return
 
     # ---- headline: config[4], the expert-parallel layer at N GPUs (strong
@@ -1294,7 +1316,7 @@ def main():
     # run and, at N > 1, weak scaling beside it.
     clk = ClockSampler(local_rank)
     if args.ep_mode == "auto":
-        args.ep_mode = "fixed" if world <= 4 else "compact"
+        args.ep_mode = auto_ep_mode(world)
     ep_res = ep_bench(moe, torch, dist, rank, world, args.steps, args.warmup, clk=clk,
                       e2e_steps=args.e2e_steps, chunks=args.ep_chunks, ep_mode=args.ep_mode)
     uni = ep_res["uniform"]

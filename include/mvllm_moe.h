@@ -403,6 +403,68 @@ MVLLM_API int mvllm_moe_ep_combine_dev(void *stream, const float *back, const in
  * out[c] += f16 value x scale, ranks ascending.  D a multiple of 8. */
 MVLLM_API int mvllm_moe_ep_combine16_dev(void *stream, const void *back16, const int *pos,
                                          int T, int nranks, int D, float *out);
+/* ---- the exchange over peer memory (no counterpart in the reference, whose
+ *      experts all run on one host): each rank owns one exchange window that
+ *      the other ranks map through CUDA IPC and write over NVLink, so the
+ *      dispatch and the return are stores inside the producing kernels and
+ *      no NCCL transfer carries rows.  Window of rank r, nranks * seg rows
+ *      (seg = tokens per rank per step; rank s's rows for r are rows
+ *      s*seg .. s*seg + seg - 1), regions at the offsets of
+ *      mvllm_moe_ep_window_layout:
+ *        [0] x    [nranks*seg, D] token rows received (x_dtype)
+ *        [1] ids  [nranks*seg, K] int32 local expert ids, -1 = no slot here
+ *        [2] wt   [nranks*seg, K] f32 routing weights
+ *        [3] back [nranks*seg, 2*D + 16] partial rows returned to rank r:
+ *            row d*seg + j = rank d's partial sum of r's token that the
+ *            fixed plan put at row d*seg + j (pos[c, d]), so
+ *            mvllm_moe_ep_combine16_dev(back, pos, ...) adds them.
+ *      A step: ep_plan_fixed_dev (capacity = seg), ep_dispatch_peer_dev,
+ *      a barrier over the ranks, layer_partial_peer_dev, a barrier,
+ *      ep_combine16_dev.  The barriers must order every rank's preceding
+ *      kernels before every rank's following ones (a stream-ordered
+ *      collective such as an NCCL all-reduce of one word does).  One
+ *      window serves every step: a rank writes into a peer's window only
+ *      after a barrier that the peer enters once it has finished reading. */
+#define MVLLM_PEER_HANDLE_BYTES 64
+/* cudaMalloc'd window of `bytes` (zeroed) and its IPC handle (64 bytes) for
+ * the other processes' mvllm_moe_peer_open. */
+MVLLM_API int mvllm_moe_peer_alloc(size_t bytes, void **ptr, void *handle);
+/* Maps another process's window (peer access enabled on first use). */
+MVLLM_API int mvllm_moe_peer_open(const void *handle, void **ptr);
+MVLLM_API int mvllm_moe_peer_close(void *ptr);
+MVLLM_API int mvllm_moe_peer_free(void *ptr);
+/* Window bytes (0 for invalid arguments) and, if offsets is not NULL, the
+ * byte offsets of its four regions (x, ids, wt, back), each 256-aligned.
+ * nranks <= 32, K <= 16, D a multiple of 8, x_dtype F32 or BF16. */
+MVLLM_API size_t mvllm_moe_ep_window_layout(int nranks, int seg, int K, int D, int x_dtype,
+                                            size_t *offsets);
+/* The dispatch as stores into the ranks' windows (replaces ep_pack_dev and
+ * the dispatch exchanges): with pos / send_cnt from ep_plan_fixed_dev
+ * (capacity = seg, T <= seg), token c planned at row d*seg + j for rank d
+ * goes to row self_rank*seg + j of d's window (x row, local ids or -1,
+ * weights); rows j >= send_cnt[d] of that segment get ids -1.
+ * windows: device array [nranks] of the window bases (own at self_rank). */
+MVLLM_API int mvllm_moe_ep_dispatch_peer_dev(void *stream, const void *x, int x_dtype,
+                                             const int *idx, const float *wt, int T, int K,
+                                             int D, int E, int nranks, const int *dest,
+                                             const int *lid, int self_rank, int seg,
+                                             const int *pos, const int *send_cnt,
+                                             void *const *windows);
+/* The rank's experts over the nranks*seg rows of its own window (`window`,
+ * the host value of windows[self_rank]), the routed layer of
+ * mvllm_moe_layer_partial_dev with each token's partial row stored into its
+ * owner's window instead of a local buffer: received row o*seg + j goes to
+ * row self_rank*seg + j of the back region of rank o's window.  Rows with no
+ * slot on this rank are not written.  Workspace: mvllm_moe_layer_workspace(
+ * nranks*seg, K, E, 0, D, Iinter, fmt).  Errors as layer_partial_dev. */
+MVLLM_API int mvllm_moe_layer_partial_peer_dev(void *stream, int nranks, int seg, int self_rank,
+                                               int K, int E, int D, int Iinter, int fmt,
+                                               int x_dtype, void *window, void *const *windows,
+                                               const void *const *g, const void *const *u,
+                                               const void *const *d, const void *const *gs,
+                                               const void *const *us, const void *const *ds,
+                                               int act, float act_a, float act_b,
+                                               void *workspace, size_t workspace_bytes);
 /* mvllm_moe_layer_dev whose per-token result goes to a partial row for the
  * expert-parallel return instead of being added into f32 `out`: row c of
  * out16 (pitch 2*D + 16 bytes, 16-byte aligned) holds the D values of the

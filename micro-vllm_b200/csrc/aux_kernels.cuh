@@ -710,6 +710,17 @@ __global__ void combine_tokens_kernel(float *__restrict__ out, const TY *__restr
     }
 }
 
+// Where the partial rows of an expert-parallel rank go when the return is
+// fused into their producer: row c of the call (the rank received it from
+// rank c / seg as that rank's row c % seg) is stored over NVLink into row
+// self * seg + c % seg of the back region of rank (c / seg)'s exchange window.
+// win == nullptr: rows stay local, row c of out16.
+struct PeerRows {
+    uint8_t *const *win;  // device array [nranks] of window bases (own at self)
+    size_t back_off;      // byte offset of the back region in every window
+    int seg, self;
+};
+
 // Partial-sum rows for the expert-parallel return: the sums of
 // combine_tokens_kernel taken from zero, stored as f16 of v / 2^s with one
 // power-of-two scale per row (the row's largest |v| / 2^s lands in
@@ -717,11 +728,15 @@ __global__ void combine_tokens_kernel(float *__restrict__ out, const TY *__restr
 // tail.  Row pitch 2*D + 16 bytes; relative error at most 2^-11 per element
 // (f16 rounding), half the bytes of f32 rows.  One CTA per token at a time,
 // the f32 row staged in shared memory (D floats) for the row maximum.
+// With peer.win the rows are stored into the owners' windows (PeerRows);
+// rows without a slot on this rank are then not written (their owner reads
+// none), and every thread ends with a system-scope fence so that the rows are
+// visible to the owners once the kernel has completed.
 template <typename TY>
 __global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const TY *__restrict__ y,
                                           const float *__restrict__ rw,
                                           const int *__restrict__ tok_pos, int T, int KK, int D,
-                                          const int *err) {
+                                          const int *err, const PeerRows peer) {
     extern __shared__ float4 srow[];
     // A device-side error in this call (recorded in *err): zero rows (h = 0,
     // scale 0), so the owners add nothing from this rank; the serving rank's
@@ -744,6 +759,8 @@ __global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const TY 
                 pos[j] = p;
             }
         }
+        if (peer.win && n == 0)
+            continue;  // uniform over the block: every thread read the same slots
         float m = 0.f;
         for (int v = threadIdx.x; v < n4; v += blockDim.x) {
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -773,6 +790,11 @@ __global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const TY 
         const int s = (M > 0.f && M <= 3.4e38f) ? ilogbf(M) - 14 : 0;
         const float inv = ldexpf(1.f, -s);
         uint8_t *row = out16 + static_cast<size_t>(c) * pitch;
+        if (peer.win) {
+            const int o = c / peer.seg, j = c - o * peer.seg;
+            row = peer.win[o] + peer.back_off +
+                  (static_cast<size_t>(peer.self) * peer.seg + j) * pitch;
+        }
         for (int v = threadIdx.x; v < n4; v += blockDim.x) {
             const float4 a = srow[v];
             __half2 h[2] = {__floats2half2_rn(a.x * inv, a.y * inv),
@@ -787,6 +809,8 @@ __global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const TY 
                 make_float4(failed ? 0.f : ldexpf(1.f, s), 0.f, 0.f, 0.f);
         __syncthreads();
     }
+    if (peer.win)
+        __threadfence_system();
 }
 
 // Ordered combine, moe_block form: CSR of destination rows (row ids ascending

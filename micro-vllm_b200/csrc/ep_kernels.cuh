@@ -138,6 +138,82 @@ __global__ void ep_pack_kernel(const TX *__restrict__ x, const int *__restrict__
     }
 }
 
+// ---- exchange over peer memory ------------------------------------------
+// Every rank owns one exchange window (cudaMalloc'd, mapped by the others
+// through CUDA IPC) of nranks * seg rows, seg = the tokens a rank owns per
+// step (fixed segments: rank s's rows for rank d are rows s*seg .. s*seg +
+// seg - 1 of d's window).  Regions, each 256-byte aligned:
+//   x    [nranks*seg, D]   the received token rows (the caller's x dtype)
+//   ids  [nranks*seg, K]   int32 local expert ids (-1: no slot here)
+//   wt   [nranks*seg, K]   f32 routing weights
+//   back [nranks*seg, 2D+16] partial rows returned to this rank (row d*seg + j:
+//                         rank d's partial sum for this rank's j-th token sent to d)
+struct WindowLayout {
+    size_t x, ids, wt, back, total;
+};
+inline WindowLayout ep_window_layout(int nranks, int seg, int K, int D, size_t xsize) {
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    const size_t rows = size_t(nranks) * seg;
+    WindowLayout w;
+    w.x = 0;
+    w.ids = up(rows * D * xsize);
+    w.wt = w.ids + up(rows * K * 4);
+    w.back = w.wt + up(rows * K * 4);
+    w.total = w.back + up(rows * (2 * size_t(D) + 16));
+    return w;
+}
+
+// Dispatch by stores into the destinations' windows (the pack and both
+// dispatch exchanges in one kernel): token c of rank `self`, planned into
+// row d*seg + j for rank d (pos from ep_plan_kernel with cap = seg), goes to
+// row self*seg + j of d's window -- its x row, the slots' local ids (-1 where
+// another rank serves the slot) and weights.  Rows j >= send_cnt[d] of that
+// segment get ids -1, so d's experts skip them.  Own rows (d == self) go to
+// this rank's own window.  Every thread ends with a system-scope fence: the
+// rows are visible to the destinations once the kernel has completed.
+template <typename TX>
+__global__ void ep_dispatch_peer_kernel(const TX *__restrict__ x, const int *__restrict__ idx,
+                                        const float *__restrict__ wt, int T, int K, int D, int E,
+                                        int nranks, const int *__restrict__ dest,
+                                        const int *__restrict__ lid, int self, int seg,
+                                        const int *__restrict__ pos,
+                                        const int *__restrict__ send_cnt,
+                                        uint8_t *const *__restrict__ win, WindowLayout lay) {
+    constexpr int VEC = 16 / sizeof(TX);
+    for (int c = blockIdx.x; c < T; c += gridDim.x) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(c) * D);
+        for (int d = 0; d < nranks; ++d) {
+            const int p = pos[static_cast<size_t>(c) * nranks + d];
+            if (p < 0)
+                continue;
+            const size_t q = static_cast<size_t>(self) * seg + (p - d * seg);
+            uint8_t *w = win[d];
+            uint4 *dst = reinterpret_cast<uint4 *>(w + lay.x + q * D * sizeof(TX));
+            for (int v = threadIdx.x; v < D / VEC; v += blockDim.x)
+                dst[v] = src[v];
+            int *di = reinterpret_cast<int *>(w + lay.ids) + q * K;
+            float *dw = reinterpret_cast<float *>(w + lay.wt) + q * K;
+            for (int k = threadIdx.x; k < K; k += blockDim.x) {
+                const int e = idx[static_cast<size_t>(c) * K + k];
+                const bool mine = e >= 0 && e < E && ep_dest(e, nranks, dest, self) == d;
+                di[k] = mine ? ep_local_id(e, nranks, lid) : -1;
+                dw[k] = wt[static_cast<size_t>(c) * K + k];
+            }
+        }
+    }
+    // The unused rows of this rank's segment on every destination.
+    const size_t n = static_cast<size_t>(nranks) * seg * K;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int d = static_cast<int>(i / (static_cast<size_t>(seg) * K));
+        const int j = static_cast<int>((i / K) % seg);
+        if (j >= send_cnt[d])
+            reinterpret_cast<int *>(win[d] + lay.ids)[(static_cast<size_t>(self) * seg + j) * K +
+                                                      i % K] = -1;
+    }
+    __threadfence_system();
+}
+
 // out[c] += sum over ranks d ascending of back[pos[c, d]] (f32, float4).
 __global__ void ep_combine_kernel(const float *__restrict__ back, const int *__restrict__ pos,
                                   int T, int nranks, int D, float *__restrict__ out) {

@@ -18,6 +18,7 @@
 #include <algorithm>
 #include <atomic>
 #include <chrono>
+#include <cstring>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -2099,6 +2100,7 @@ size_t mvllm_moe_layer_workspace(int T, int K, int E, int n_shared, int D, int I
 // ahead of them.
 struct LayerHooks {
     std::function<int()> before_gather, before_combine;
+    PeerRows peer{};  // partial rows into the owners' exchange windows
 };
 
 static int layer_combine(cudaStream_t st, int sms, int T, int KK, int D, float *out,
@@ -2206,6 +2208,7 @@ static int layer_combine(cudaStream_t st, int sms, int T, int KK, int D, float *
         if (int rc = hooks->before_combine())
             return rc;
     if (out16) {
+        const PeerRows peer = hooks ? hooks->peer : PeerRows{};
         const size_t sm = size_t(D) * 4;
         const dim3 grid(std::min(T, 8 * sms));
         if (w.y16) {
@@ -2214,14 +2217,15 @@ static int layer_combine(cudaStream_t st, int sms, int T, int KK, int D, float *
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               int(sm)));
             combine_tokens_f16_kernel<__half><<<grid, 256, sm, st>>>(
-                out16, reinterpret_cast<const __half *>(w.y), l.rw, l.tok_pos, T, KK, D, w.err);
+                out16, reinterpret_cast<const __half *>(w.y), l.rw, l.tok_pos, T, KK, D, w.err,
+                peer);
         } else {
             if (sm > 48 * 1024)
                 CUDA_TRY(cudaFuncSetAttribute(combine_tokens_f16_kernel<float>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               int(sm)));
             combine_tokens_f16_kernel<float><<<grid, 256, sm, st>>>(out16, w.y, l.rw, l.tok_pos,
-                                                                    T, KK, D, w.err);
+                                                                    T, KK, D, w.err, peer);
         }
     } else {
         dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
@@ -2666,6 +2670,145 @@ int mvllm_moe_ep_combine_dev(void *stream, const float *back, const int *pos, in
     ep_combine_kernel<<<grid, 256, 0, st>>>(back, pos, T, nranks, D, out);
     CUDA_TRY(cudaGetLastError());
     return MVLLM_OK;
+}
+
+// ------------------------------------ expert-parallel exchange over NVLink --
+int mvllm_moe_peer_alloc(size_t bytes, void **ptr, void *handle) {
+    if (!bytes || !ptr || !handle)
+        return fail(MVLLM_ERR_INVALID, "peer_alloc: invalid arguments");
+    static_assert(sizeof(cudaIpcMemHandle_t) == MVLLM_PEER_HANDLE_BYTES, "IPC handle size");
+    Context &c = ctx();
+    {
+        std::lock_guard<std::mutex> lk(c.mu);
+        if (int rc = ensure_current(c))
+            return rc;
+    }
+    void *p = nullptr;
+    CUDA_TRY(cudaMalloc(&p, bytes));
+    cudaIpcMemHandle_t h;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        const cudaError_t e = cudaGetLastError();
+        cudaFree(p);
+        return fail(MVLLM_ERR_CUDA, "peer_alloc: %s", cudaGetErrorString(e));
+    }
+    std::memcpy(handle, &h, sizeof(h));
+    *ptr = p;
+    return MVLLM_OK;
+}
+
+int mvllm_moe_peer_open(const void *handle, void **ptr) {
+    if (!handle || !ptr)
+        return fail(MVLLM_ERR_INVALID, "peer_open: invalid arguments");
+    Context &c = ctx();
+    {
+        std::lock_guard<std::mutex> lk(c.mu);
+        if (int rc = ensure_current(c))
+            return rc;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void *p = nullptr;
+    CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    *ptr = p;
+    return MVLLM_OK;
+}
+
+int mvllm_moe_peer_close(void *ptr) {
+    if (!ptr)
+        return fail(MVLLM_ERR_INVALID, "peer_close: null pointer");
+    CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+    return MVLLM_OK;
+}
+
+int mvllm_moe_peer_free(void *ptr) {
+    if (!ptr)
+        return fail(MVLLM_ERR_INVALID, "peer_free: null pointer");
+    CUDA_TRY(cudaFree(ptr));
+    return MVLLM_OK;
+}
+
+static size_t dtype_size(int x_dtype) {
+    return x_dtype == MVLLM_DTYPE_BF16 ? 2 : x_dtype == MVLLM_DTYPE_F32 ? 4 : 0;
+}
+
+size_t mvllm_moe_ep_window_layout(int nranks, int seg, int K, int D, int x_dtype,
+                                  size_t *offsets) {
+    if (nranks < 1 || nranks > 32 || seg < 1 || K < 1 || K > 16 || D < 8 || D % 8 != 0 ||
+        !dtype_size(x_dtype))
+        return 0;
+    const WindowLayout w = ep_window_layout(nranks, seg, K, D, dtype_size(x_dtype));
+    if (offsets) {
+        offsets[0] = w.x;
+        offsets[1] = w.ids;
+        offsets[2] = w.wt;
+        offsets[3] = w.back;
+    }
+    return w.total;
+}
+
+int mvllm_moe_ep_dispatch_peer_dev(void *stream, const void *x, int x_dtype, const int *idx,
+                                   const float *wt, int T, int K, int D, int E, int nranks,
+                                   const int *dest, const int *lid, int self_rank, int seg,
+                                   const int *pos, const int *send_cnt, void *const *windows) {
+    if (!x || !idx || !wt || !pos || !send_cnt || !windows || T < 0 || T > seg || K < 1 ||
+        K > 16 || D < 8 || D % 8 != 0 || E < 1 || nranks < 1 || nranks > 32 || self_rank < 0 ||
+        self_rank >= nranks || (!dest != !lid) || !dtype_size(x_dtype) ||
+        (reinterpret_cast<uintptr_t>(x) & 15u))
+        return fail(MVLLM_ERR_INVALID, "ep_dispatch_peer_dev: invalid arguments");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const WindowLayout lay = ep_window_layout(nranks, seg, K, D, dtype_size(x_dtype));
+    const int blocks = std::max(1, std::min(std::max(T, (nranks * seg * K + 255) / 256), 65535));
+    uint8_t *const *win = reinterpret_cast<uint8_t *const *>(windows);
+    if (x_dtype == MVLLM_DTYPE_BF16)
+        ep_dispatch_peer_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+            static_cast<const __nv_bfloat16 *>(x), idx, wt, T, K, D, E, nranks, dest, lid,
+            self_rank, seg, pos, send_cnt, win, lay);
+    else
+        ep_dispatch_peer_kernel<float><<<blocks, 256, 0, st>>>(
+            static_cast<const float *>(x), idx, wt, T, K, D, E, nranks, dest, lid, self_rank,
+            seg, pos, send_cnt, win, lay);
+    CUDA_TRY(cudaGetLastError());
+    return MVLLM_OK;
+}
+
+int mvllm_moe_layer_partial_peer_dev(void *stream, int nranks, int seg, int self_rank, int K,
+                                     int E, int D, int Iinter, int fmt, int x_dtype,
+                                     void *window, void *const *windows, const void *const *g,
+                                     const void *const *u, const void *const *d,
+                                     const void *const *gs, const void *const *us,
+                                     const void *const *ds, int act, float act_a, float act_b,
+                                     void *workspace, size_t workspace_bytes) {
+    if (nranks < 1 || nranks > 32 || seg < 1 || self_rank < 0 || self_rank >= nranks || K < 1 ||
+        K > 16 || E < 1 || D < 8 || D % 8 != 0 || D > 32768 || Iinter < 1 ||
+        (fmt != 0 && fmt != 4 && fmt != 7) || !dtype_size(x_dtype) || !window || !windows ||
+        !g || !u || !d || (fmt != MVLLM_FMT_F32 && (!gs || !us || !ds)) ||
+        (reinterpret_cast<uintptr_t>(window) & 255u))
+        return fail(MVLLM_ERR_INVALID, "layer_partial_peer_dev: invalid arguments");
+    const int T = nranks * seg;
+    const size_t need = mvllm_moe_layer_workspace(T, K, E, 0, D, Iinter, fmt);
+    if (!workspace || workspace_bytes < need)
+        return fail(MVLLM_ERR_WORKSPACE, "layer_partial_peer_dev: workspace %zu < %zu",
+                    workspace_bytes, need);
+    Context &c = ctx();
+    int sms;
+    {
+        std::lock_guard<std::mutex> lk(c.mu);
+        if (int rc = ensure_current(c))
+            return rc;
+        sms = launch_sms(c);
+    }
+    const WindowLayout lay = ep_window_layout(nranks, seg, K, D, dtype_size(x_dtype));
+    uint8_t *base = static_cast<uint8_t *>(window);
+    Carve cv(workspace, workspace_bytes);
+    LayerWs l{};
+    carve_layer(cv, l, T, K, E, 0, D, Iinter, fast_path_ok(fmt, D, Iinter));
+    Tables tb{g, u, d, gs, us, ds};
+    LayerHooks hooks;
+    hooks.peer = PeerRows{reinterpret_cast<uint8_t *const *>(windows), lay.back, seg, self_rank};
+    return layer_dev_impl(static_cast<cudaStream_t>(stream), sms, T, K, E, 0, D, Iinter, fmt,
+                          reinterpret_cast<const int *>(base + lay.ids),
+                          reinterpret_cast<const float *>(base + lay.wt), base + lay.x, x_dtype,
+                          tb, nullptr, act, act_a, act_b, l, true, &hooks, base + lay.back);
 }
 
 // ------------------------------------------------------------ packers etc --

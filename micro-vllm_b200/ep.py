@@ -201,6 +201,23 @@ class CudaOps:
         else:
             moe.ep_combine_dev(back, pos, out)
 
+    # ---- the exchange over peer memory (EPLayer.forward_peer)
+    def dispatch_peer(self, x, idx, wt, pos, cnt, win, rank):
+        moe.ep_dispatch_peer_dev(x, idx, wt, self.E, self.nranks, win.seg, pos, cnt, win.table,
+                                 self.dest, self.lid, rank)
+
+    def compute_peer(self, win, rank):
+        R = self.nranks * win.seg
+        if R > self.max_recv_rows:
+            raise ValueError(f"{R} window rows, above the {self.max_recv_rows} sized for")
+        if self.E_local:
+            moe.layer_partial_peer_dev(self.nranks, win.seg, rank, self.K, self.E_local, self.D,
+                                       self.I, self.fmt, win.x_dtype, win.addr, win.table,
+                                       self.tables, self.act, self.act_a, self.act_b, self.ws)
+
+    def combine_peer(self, win, pos, out):
+        moe.ep_combine16_dev(win.addr + win.off["back"], pos, out)
+
     def set_sm_reserve(self, n):
         """Leave n SMs out of the expert kernels (0: use them all)."""
         if n <= 0:
@@ -211,11 +228,113 @@ class CudaOps:
             moe.set_sm_limit(max(2, sms - n))
 
 
+class PeerWindows:
+    """The exchange window of one rank for `EPLayer.forward_peer`: one
+    cudaMalloc'd block (mvllm_moe_peer_alloc) of nranks * seg rows -- token
+    rows, local ids and weights received, and the partial rows returned to
+    this rank -- that every other rank maps through CUDA IPC and writes over
+    NVLink.  `table` is the device array of every rank's window address."""
+
+    def __init__(self, torch, nranks, seg, K, D, x_dtype=moe.DTYPE_BF16):
+        self.torch, self.nranks, self.seg, self.x_dtype = torch, nranks, seg, x_dtype
+        self.total, self.off = moe.ep_window_layout(nranks, seg, K, D, x_dtype)
+        self.addr, self.handle = moe.peer_alloc(self.total)
+        self.opened, self.table = [], None
+
+    def connect(self, rank, dist=None, group=None, peers=None):
+        """Builds `table`: from the other processes' IPC handles (an all-gather
+        of the 64-byte handles over `dist`, each peer's window mapped here) or,
+        for ranks emulated in one process, from their PeerWindows (`peers`)."""
+        t = self.torch
+        if peers is not None:
+            addrs = [p.addr for p in peers]
+        else:
+            n = moe.PEER_HANDLE_BYTES
+            mine = t.tensor(list(self.handle), dtype=t.uint8, device="cuda")
+            every = t.empty(self.nranks * n, dtype=t.uint8, device="cuda")
+            dist.all_gather_into_tensor(every, mine, group=group)
+            raw = bytes(every.cpu().tolist())
+            addrs = []
+            for r in range(self.nranks):
+                if r == rank:
+                    addrs.append(self.addr)
+                else:
+                    a = moe.peer_open(raw[r * n:(r + 1) * n])
+                    self.opened.append(a)
+                    addrs.append(a)
+        self.table = t.tensor(addrs, dtype=t.int64, device="cuda")
+        return self
+
+    def close(self, dist=None, group=None):
+        """Unmaps the peers' windows, waits for every rank to have done the
+        same (dist), then frees this rank's own."""
+        self.torch.cuda.synchronize()
+        for a in self.opened:
+            moe.peer_close(a)
+        self.opened = []
+        if dist is not None and self.nranks > 1:
+            dist.barrier(group=group)
+        if self.addr:
+            moe.peer_free(self.addr)
+            self.addr = 0
+
+
 class EPLayer:
     """The layer step of one rank; `ops` holds the device steps."""
 
     def __init__(self, ops, rank, nranks, D, K):
         self.ops, self.rank, self.nranks, self.D, self.K = ops, rank, nranks, D, K
+        self._flag = None
+
+    def _barrier(self, dist, group):
+        """Orders every rank's preceding kernels before every rank's following
+        ones: an all-reduce of one word, queued on the stream like a kernel
+        (no host synchronisation)."""
+        if self.nranks > 1:
+            t = self.ops.torch
+            if self._flag is None:
+                self._flag = t.zeros(1, dtype=t.int32, device="cuda")
+            dist.all_reduce(self._flag, group=group)
+
+    def forward_peer(self, x, idx, wt, out, dist, win, group=None, timing=None):
+        """The step with the exchanges as stores over NVLink (no NCCL transfer
+        carries rows): the fixed plan (segments of win.seg rows), the dispatch
+        kernel storing each token row, its local ids and weights into the
+        destinations' windows, a barrier, the rank's experts over its window
+        with each partial row stored into its owner's window, a barrier, and
+        the combine of the rows returned to this rank (ranks ascending).  The
+        same rows and sums as `forward_fixed`, so the same bits."""
+        T = x.shape[0]
+        if T > win.seg:
+            raise ValueError(f"{T} tokens, above the window's {win.seg} per rank")
+        t, ev = self.ops.torch, []
+
+        def mark():
+            if timing is not None:
+                e = t.cuda.Event(enable_timing=True)
+                e.record()
+                ev.append(e)
+
+        mark()
+        pos, cnt = self.ops.plan_fixed(idx, win.seg)
+        mark()
+        self.ops.dispatch_peer(x, idx, wt, pos, cnt, win, self.rank)
+        mark()
+        self._barrier(dist, group)
+        mark()
+        self.ops.compute_peer(win, self.rank)
+        mark()
+        self._barrier(dist, group)
+        mark()
+        self.ops.combine_peer(win, pos, out)
+        mark()
+        if timing is not None:
+            t.cuda.synchronize()
+            names = ("plan", "dispatch_stores", "barrier1", "experts_and_return_stores",
+                     "barrier2", "combine")
+            for n, a, b in zip(names, ev[:-1], ev[1:]):
+                timing[n] = timing.get(n, 0.0) + a.elapsed_time(b)
+        return {"sent_rows": self.nranks * win.seg, "received_rows": self.nranks * win.seg}
 
     # ---- phases (the distributed forward and the in-process emulation both use them)
     def prepare(self, x, idx, wt):
@@ -378,6 +497,22 @@ class EPLayer:
             for n, a, b in zip(names, ev[:-1], ev[1:]):
                 timing[n] = timing.get(n, 0.0) + a.elapsed_time(b)
         return {"sent_rows": sum(sc), "received_rows": R}
+
+
+def emulate_step_peer(layers, wins, xs, idxs, wts, outs):
+    """forward_peer for all ranks in one process on one GPU: the windows are
+    the ranks' own allocations (PeerWindows.connect with `peers`), and the
+    stream order of the phases (every rank's dispatch, then every rank's
+    experts, then every rank's combine) stands in for the barriers."""
+    plans = []
+    for L, w, x, i, t in zip(layers, wins, xs, idxs, wts):
+        pos, cnt = L.ops.plan_fixed(i, w.seg)
+        L.ops.dispatch_peer(x, i, t, pos, cnt, w, L.rank)
+        plans.append(pos)
+    for L, w in zip(layers, wins):
+        L.ops.compute_peer(w, L.rank)
+    for L, w, pos, o in zip(layers, wins, plans, outs):
+        L.ops.combine_peer(w, pos, o)
 
 
 def emulate_step(layers, xs, idxs, wts, outs, torch):

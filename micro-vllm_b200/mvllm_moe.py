@@ -51,6 +51,9 @@ C_SYMBOLS = (
     "mvllm_moe_set_prefill_mode", "mvllm_moe_get_prefill_mode", "mvllm_mx_terms_dev",
     "mvllm_moe_mma_rate", "mvllm_moe_set_sm_limit", "mvllm_moe_ep_plan_fixed_dev",
     "mvllm_moe_set_exact", "mvllm_moe_get_exact", "mvllm_moe_layer_error",
+    "mvllm_moe_peer_alloc", "mvllm_moe_peer_open", "mvllm_moe_peer_close", "mvllm_moe_peer_free",
+    "mvllm_moe_ep_window_layout", "mvllm_moe_ep_dispatch_peer_dev",
+    "mvllm_moe_layer_partial_peer_dev",
 )
 PHASES = ("permute", "gather", "plan", "expert_phase1", "expert_phase2", "combine")
 
@@ -129,6 +132,15 @@ def lib():
             "mvllm_moe_mma_rate": (i, [i, i, i, i, vp]),
             "mvllm_moe_set_sm_limit": (i, [i]),
             "mvllm_moe_ep_plan_fixed_dev": (i, [vp, vp, i, i, i, i, vp, i, i, vp, vp]),
+            "mvllm_moe_peer_alloc": (i, [sz, vp, vp]),
+            "mvllm_moe_peer_open": (i, [vp, vp]),
+            "mvllm_moe_peer_close": (i, [vp]),
+            "mvllm_moe_peer_free": (i, [vp]),
+            "mvllm_moe_ep_window_layout": (sz, [i, i, i, i, i, vp]),
+            "mvllm_moe_ep_dispatch_peer_dev": (i, [vp, vp, i, vp, vp] + [i] * 5 +
+                                               [vp, vp, i, i, vp, vp, vp]),
+            "mvllm_moe_layer_partial_peer_dev": (i, [vp] + [i] * 9 + [vp, vp] + [vp] * 6 +
+                                                 [i, f, f, vp, sz]),
             "mvllm_moe_dense_ffn_dev": (i, [vp, i, i, i, i] + [vp] * 7 + [i, f, f, vp, i, vp,
                                                                          sz]),
         }
@@ -482,6 +494,74 @@ def ep_pack_dev(x, idx, wt, E, nranks, pos, send_x, send_idx, send_wt, dest=None
                                        _dp(send_x), _dp(send_idx), _dp(send_wt)))
 
 
+# ---- the exchange over peer memory (windows mapped through CUDA IPC)
+PEER_HANDLE_BYTES = 64
+
+
+def _ptr(v):
+    """A device pointer from a tensor or a raw integer address."""
+    if v is None or isinstance(v, int):
+        return C.c_void_p(v)
+    return C.c_void_p(v.data_ptr())
+
+
+def peer_alloc(nbytes):
+    """A new zeroed device window: (address, 64-byte IPC handle)."""
+    p = C.c_void_p()
+    h = (C.c_ubyte * PEER_HANDLE_BYTES)()
+    _check(lib().mvllm_moe_peer_alloc(nbytes, C.byref(p), h))
+    return p.value, bytes(h)
+
+
+def peer_open(handle: bytes) -> int:
+    """Maps another process's window from its handle; returns the address."""
+    if len(handle) != PEER_HANDLE_BYTES:
+        raise ValueError("an IPC handle has 64 bytes")
+    p = C.c_void_p()
+    h = (C.c_ubyte * PEER_HANDLE_BYTES).from_buffer_copy(handle)
+    _check(lib().mvllm_moe_peer_open(h, C.byref(p)))
+    return p.value
+
+
+def peer_close(addr: int) -> None:
+    _check(lib().mvllm_moe_peer_close(C.c_void_p(addr)))
+
+
+def peer_free(addr: int) -> None:
+    _check(lib().mvllm_moe_peer_free(C.c_void_p(addr)))
+
+
+def ep_window_layout(nranks, seg, K, D, x_dtype):
+    """(window bytes, {"x", "ids", "wt", "back"} byte offsets)."""
+    off = (C.c_size_t * 4)()
+    total = lib().mvllm_moe_ep_window_layout(nranks, seg, K, D, x_dtype, off)
+    if total == 0:
+        raise MoeError(ERR_INVALID, "ep_window_layout: invalid arguments")
+    return total, dict(zip(("x", "ids", "wt", "back"), list(off)))
+
+
+def ep_dispatch_peer_dev(x, idx, wt, E, nranks, seg, pos, send_cnt, windows, dest=None, lid=None,
+                         self_rank=0, stream=None):
+    """Token rows, local ids and weights stored into the ranks' windows
+    (windows: device int64 [nranks] of window addresses)."""
+    T, K = idx.shape
+    D = x.shape[1]
+    x_dtype = DTYPE_BF16 if str(x.dtype) == "torch.bfloat16" else DTYPE_F32
+    _check(lib().mvllm_moe_ep_dispatch_peer_dev(
+        _stream(stream), _dp(x), x_dtype, _dp(idx), _dp(wt), T, K, D, E, nranks, _dp(dest),
+        _dp(lid), self_rank, seg, _dp(pos), _dp(send_cnt), _dp(windows)))
+
+
+def layer_partial_peer_dev(nranks, seg, self_rank, K, E, D, Iinter, fmt, x_dtype, window,
+                           windows, tables, act, act_a, act_b, workspace, stream=None):
+    """The rank's experts over its own window's rows, partial rows stored into
+    the owners' windows (window: own address; windows: device int64 [nranks])."""
+    _check(lib().mvllm_moe_layer_partial_peer_dev(
+        _stream(stream), nranks, seg, self_rank, K, E, D, Iinter, fmt, x_dtype,
+        C.c_void_p(window), _dp(windows), *[_dp(t) for t in tables], act, act_a, act_b,
+        _dp(workspace), workspace.numel() * workspace.element_size()))
+
+
 def ep_combine_dev(back, pos, out, stream=None):
     T, nranks = pos.shape
     D = out.shape[1]
@@ -490,10 +570,12 @@ def ep_combine_dev(back, pos, out, stream=None):
 
 
 def ep_combine16_dev(back16, pos, out, stream=None):
+    """back16: a uint8 tensor of partial rows or the raw address of a
+    window's back region."""
     T, nranks = pos.shape
     D = out.shape[1]
-    _check(lib().mvllm_moe_ep_combine16_dev(_stream(stream), _dp(back16), _dp(pos), T, nranks, D,
-                                            _dp(out)))
+    _check(lib().mvllm_moe_ep_combine16_dev(_stream(stream), _ptr(back16), _dp(pos), T, nranks,
+                                            D, _dp(out)))
 
 
 # ------------------------------------------------------------------ routing --

@@ -105,3 +105,55 @@ class CpuOps:
             for d in range(self.nranks):
                 if P[c, d] >= 0:
                     out[c] += back[P[c, d]]
+
+    # ---- the exchange over peer memory (ep.EPLayer.forward_peer): the
+    # windows are CPU buffers of ranks emulated in one process, written with
+    # the index arithmetic of the device kernels (ep_dispatch_peer_kernel and
+    # the peer form of combine_tokens_f16_kernel).
+    def dispatch_peer(self, x, idx, wt, pos, cnt, win, rank):
+        P, ids, seg = pos.numpy(), idx.numpy(), win.seg
+        for c in range(P.shape[0]):
+            for d in range(self.nranks):
+                p = P[c, d]
+                if p < 0:
+                    continue
+                q = rank * seg + (p - d * seg)
+                w = win.table[d]
+                w.x[q] = x[c]
+                for k in range(self.K):
+                    e = int(ids[c, k])
+                    mine = 0 <= e < self.E and self._serving(e) == d
+                    w.ids[q, k] = self._lid(e) if mine else -1
+                w.wt[q] = wt[c]
+        for d in range(self.nranks):
+            for j in range(int(cnt[d]), seg):
+                win.table[d].ids[rank * seg + j] = -1
+
+    def compute_peer(self, win, rank):
+        part = self.compute(win.x, win.ids, win.wt)
+        live = (win.ids.numpy() >= 0).any(axis=1)
+        for c in range(part.shape[0]):
+            if live[c]:
+                o, j = divmod(c, win.seg)
+                win.table[o].back[rank * win.seg + j] = part[c]
+
+    def combine_peer(self, win, pos, out):
+        self.combine(win.back, pos, out)
+
+
+class CpuWindow:
+    """A rank's exchange window for the CPU double: the regions of the device
+    window (x, ids, wt, back) as CPU tensors; `table` lists every rank's."""
+
+    def __init__(self, torch, nranks, seg, K, D, x_dtype):
+        rows = nranks * seg
+        self.seg = seg
+        self.x = torch.zeros((rows, D), dtype=x_dtype)
+        self.ids = torch.full((rows, K), 7, dtype=torch.int32)  # stale ids until written
+        self.wt = torch.zeros((rows, K), dtype=torch.float32)
+        self.back = torch.full((rows, D), float("nan"))  # unread unless returned
+        self.table = None
+
+    def connect(self, rank, peers):
+        self.table = list(peers)
+        return self

@@ -1,9 +1,11 @@
 """Two-rank expert-parallel check over NCCL (launched by tests/test_ep_gpu.py
 through torchrun, one rank per GPU): each rank holds half of the experts
-(strided), runs its tokens through ep.EPLayer.forward (and the chunked,
-overlapped forward_chunked, which must give the same bits), and rank 0
-compares the gathered output with the single-GPU layer over all tokens and
-experts.
+(strided), runs its tokens through ep.EPLayer.forward and through the other
+exchange forms, which must give the same bits: the chunked, overlapped
+forward_chunked, forward_fixed (fixed segments), and forward_peer (rows
+stored over NVLink into the ranks' IPC-mapped windows, twice through the same
+windows).  Rank 0 compares the gathered output with the single-GPU layer over
+all tokens and experts.
 Prints EP-NCCL-OK on success."""
 import os
 import sys
@@ -64,10 +66,22 @@ def main():
     # Fixed-size exchange segments (no counts on the host): the same bits.
     fixed = torch.zeros_like(out)
     layer.forward_fixed(x, idx, wt, fixed, dist)
+    # The exchanges as stores over NVLink into the ranks' IPC-mapped windows:
+    # the same bits, twice through the same windows.
+    win = ep.PeerWindows(torch, world, T_LOC, K, D).connect(rank, dist)
+    peer, peer2 = torch.zeros_like(out), torch.zeros_like(out)
+    layer.forward_peer(x, idx, wt, peer, dist, win)
+    layer.forward_peer(x, idx, wt, peer2, dist, win)
     torch.cuda.synchronize()
+    win.close(dist)
     gathered = [torch.zeros_like(out) for _ in range(world)]
     dist.all_gather(gathered, out)
-    ok = torch.equal(out, again) and torch.equal(out, sliced) and torch.equal(out, fixed)
+    ok = (torch.equal(out, again) and torch.equal(out, sliced) and torch.equal(out, fixed) and
+          torch.equal(out, peer) and torch.equal(out, peer2))
+    if not ok:
+        print(f"rank {rank}: again {torch.equal(out, again)} sliced {torch.equal(out, sliced)} "
+              f"fixed {torch.equal(out, fixed)} peer {torch.equal(out, peer)} "
+              f"peer2 {torch.equal(out, peer2)}", flush=True)
     if rank == 0:
         tabs_all, keep_all = tables_of(c["experts"])
         ref = torch.zeros((world * T_LOC, D), device="cuda")

@@ -174,7 +174,18 @@ def test_config4_ep_eight_ranks_emulated(moe, port):
         wts.append(torch.from_numpy(wt[sl]).cuda())
         outs.append(torch.zeros((T_loc, D), device="cuda"))
     ep.emulate_step(layers, xs, idxs, wts, outs, torch)
+    # The exchange over peer memory (forward_peer's kernels, windows as
+    # separate allocations on this GPU): the same bits.
+    wins = [ep.PeerWindows(torch, N, T_loc, K, D) for _ in range(N)]
+    for r, w in enumerate(wins):
+        w.connect(r, peers=wins)
+    peer = [torch.zeros_like(o) for o in outs]
+    ep.emulate_step_peer(layers, wins, xs, idxs, wts, peer)
     torch.cuda.synchronize()
+    for w in wins:
+        w.close()
+    for o, p in zip(outs, peer):
+        assert torch.equal(o, p)
     got = torch.cat(outs).cpu().numpy()
     tokens = [int(t) for t in np.linspace(0, T - 1, 32)]
     used = sorted(set(idx[tokens].reshape(-1).tolist()))

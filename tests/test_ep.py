@@ -96,6 +96,35 @@ def test_ep_emulated_three_ranks(port):
     assert_close(got, want, "emulated 3-rank EP")
 
 
+def test_ep_emulated_peer_windows(port):
+    """The peer-memory step (forward_peer's dispatch into the destinations'
+    windows, experts over the own window, partial rows into the owners'
+    windows, combine) on the CPU double: the same output as the exchange
+    through send buffers, exactly; windows start with stale ids, which the
+    dispatch must overwrite (-1 for unused segment rows)."""
+    import ep
+    from ep_cpu_ops import CpuWindow
+    N, T_loc = 3, 7
+    c, want = layer(port, N * T_loc)
+    layers, xs, idxs, wts, outs, ref = [], [], [], [], [], []
+    for r in range(N):
+        sl = slice(r * T_loc, (r + 1) * T_loc)
+        layers.append(ep.EPLayer(rank_ops(port, c, r, N), r, N, CASE["D"], CASE["K"]))
+        xs.append(torch.from_numpy(np.ascontiguousarray(c["x"][sl])))
+        idxs.append(torch.from_numpy(np.ascontiguousarray(c["idx"][sl])))
+        wts.append(torch.from_numpy(np.ascontiguousarray(c["wt"][sl])))
+        outs.append(torch.zeros((T_loc, CASE["D"])))
+        ref.append(torch.zeros((T_loc, CASE["D"])))
+    wins = [CpuWindow(torch, N, T_loc + 2, CASE["K"], CASE["D"], xs[0].dtype) for _ in range(N)]
+    for r, w in enumerate(wins):
+        w.connect(r, wins)
+    ep.emulate_step_peer(layers, wins, xs, idxs, wts, outs)
+    ep.emulate_step(layers, xs, idxs, wts, ref, torch)
+    for o, f in zip(outs, ref):
+        assert torch.equal(o, f)
+    assert_close(torch.cat(outs).numpy(), want, "emulated 3-rank EP, peer windows")
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))

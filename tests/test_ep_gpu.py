@@ -96,6 +96,53 @@ def test_ep_emulated_four_ranks_gpu(moe, port):
     assert torch.equal(local, direct)
 
 
+@pytest.mark.parametrize("replicated", [(), (5, 1)])
+def test_ep_peer_windows_emulated_gpu(moe, port, replicated):
+    """The exchange over peer memory (forward_peer's kernels: dispatch stores
+    into the destinations' windows, experts with partial rows stored into the
+    owners' windows, combine) with 4 ranks emulated on one GPU, their windows
+    separate allocations: bit-identical to the exchange through send buffers
+    (emulate_step) and within tolerance of the oracle; two steps with
+    different routing through the same windows (the first step's rows and ids
+    must not leak into the second)."""
+    import ep
+    N, T_loc = 4, 40
+    pl = ep.Placement(CASE["E"], N, replicated=list(replicated))
+    wins = [ep.PeerWindows(torch, N, T_loc, CASE["K"], CASE["D"]) for _ in range(N)]
+    for r, w in enumerate(wins):
+        w.connect(r, peers=wins)
+    keep = []
+    try:
+        for seed in (61, 62):
+            c = cases.layer_case(port, seed, CASE["D"], CASE["I"], CASE["E"], CASE["K"],
+                                 N * T_loc, CASE["fmt"], CASE["act"], CASE["act_a"],
+                                 CASE["act_b"], bf16_x=True)
+            _, want = cases.run_block(port, c)
+            layers, xs, idxs, wts, outs, ref = [], [], [], [], [], []
+            for r in range(N):
+                tabs, k = tables_of([c["experts"][e] for e in pl.local_experts(r)])
+                keep.append(k)
+                ops = ep.CudaOps(torch, CASE["E"], CASE["K"], CASE["D"], CASE["I"], CASE["fmt"],
+                                 CASE["act"], CASE["act_a"], CASE["act_b"], tabs, N, N * T_loc,
+                                 placement=pl, rank=r)
+                layers.append(ep.EPLayer(ops, r, N, CASE["D"], CASE["K"]))
+                sl = slice(r * T_loc, (r + 1) * T_loc)
+                xs.append(dev(c["x"][sl]).to(torch.bfloat16))
+                idxs.append(dev(c["idx"][sl]))
+                wts.append(dev(c["wt"][sl]))
+                outs.append(torch.zeros((T_loc, CASE["D"]), device="cuda"))
+                ref.append(torch.zeros((T_loc, CASE["D"]), device="cuda"))
+            ep.emulate_step_peer(layers, wins, xs, idxs, wts, outs)
+            ep.emulate_step(layers, xs, idxs, wts, ref, torch)
+            torch.cuda.synchronize()
+            for o, f in zip(outs, ref):
+                assert torch.equal(o, f)
+            assert_close(torch.cat(outs).cpu().numpy(), want, "4-rank EP over peer windows")
+    finally:
+        for w in wins:
+            w.close()
+
+
 def test_ep_emulated_replicated_experts_gpu(moe, port):
     """Experts 1 and 5 replicated on every rank (served locally for each
     rank's own tokens), the rest strided: the layer output is unchanged."""
