@@ -652,10 +652,105 @@ __device__ __forceinline__ float4 load_y4(const __half *y, size_t i) {
 __device__ __forceinline__ float load_y1(const float *y, size_t i) { return y[i]; }
 __device__ __forceinline__ float load_y1(const __half *y, size_t i) { return __half2float(y[i]); }
 
+// CW consecutive values of a y row (f16 or f32), streamed (read once): the
+// raw words, converted to floats where they are added (fewer registers held
+// while the loads are in flight).
+template <typename TY, int CW> struct YWords;
+template <> struct YWords<__half, 8> {
+    uint4 u;
+    __device__ __forceinline__ void load(const __half *y, size_t i) {
+        u = __ldcs(reinterpret_cast<const uint4 *>(y + i));
+    }
+    __device__ __forceinline__ float get(int q) const {
+        const uint32_t w = q < 2 ? u.x : q < 4 ? u.y : q < 6 ? u.z : u.w;
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w));
+        return (q & 1) ? f.y : f.x;
+    }
+};
+template <> struct YWords<__half, 4> {
+    uint2 u;
+    __device__ __forceinline__ void load(const __half *y, size_t i) {
+        u = __ldcs(reinterpret_cast<const uint2 *>(y + i));
+    }
+    __device__ __forceinline__ float get(int q) const {
+        const uint32_t w = q < 2 ? u.x : u.y;
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w));
+        return (q & 1) ? f.y : f.x;
+    }
+};
+template <int CW> struct YWords<float, CW> {
+    float4 f[CW / 4];
+    __device__ __forceinline__ void load(const float *y, size_t i) {
+#pragma unroll
+        for (int q = 0; q < CW / 4; ++q)
+            f[q] = __ldcs(reinterpret_cast<const float4 *>(y + i) + q);
+    }
+    __device__ __forceinline__ float get(int q) const {
+        const float4 &a = f[q >> 2];
+        return (q & 3) == 0 ? a.x : (q & 3) == 1 ? a.y : (q & 3) == 2 ? a.z : a.w;
+    }
+};
+
+// The token's slot rows spos[0..n) (ascending) in order: acc += w * y, one
+// multiply and one add per term.  Up to eight rows' loads are in flight
+// before their ordered adds.
+template <int CW, typename TY>
+__device__ __forceinline__ void ordered_sum(float (&acc)[CW], const TY *__restrict__ y,
+                                            const float *__restrict__ rw, const int *spos, int n,
+                                            size_t col, int D) {
+    constexpr int kB = 8;
+    for (int j0 = 0; j0 < n; j0 += kB) {
+        YWords<TY, CW> v[kB];
+        float w[kB];
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+            if (j0 + b < n) {
+                const int r = spos[j0 + b];
+                w[b] = __ldg(rw + r);
+                v[b].load(y, static_cast<size_t>(r) * D + col);
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+            if (j0 + b < n) {
+#pragma unroll
+                for (int q = 0; q < CW; ++q)
+                    acc[q] = __fadd_rn(acc[q], __fmul_rn(w[b], v[b].get(q)));
+            }
+        }
+    }
+}
+
+// The block's token c: its slot positions (tok_pos row, -1 = no slot) sorted
+// ascending into spos[0..n) in shared memory by the first warp (each lane
+// places its value by the count of smaller ones; positions are distinct).
+// Returns n to every thread.  KK <= 32.
+__device__ __forceinline__ int token_slots_shared(const int *__restrict__ tok_pos, int c, int KK,
+                                                  int *spos, int *sn) {
+    __syncthreads();  // the previous token's readers are done with spos
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        const int p = lane < KK ? tok_pos[static_cast<size_t>(c) * KK + lane] : -1;
+        const uint32_t valid = __ballot_sync(0xffffffffu, p >= 0);
+        int rank = 0;
+        for (int u = 0; u < KK; ++u) {
+            const int q = __shfl_sync(0xffffffffu, p, u);
+            rank += (q >= 0 && q < p) ? 1 : 0;
+        }
+        if (p >= 0)
+            spos[rank] = p;
+        if (lane == 0)
+            *sn = __popc(valid);
+    }
+    __syncthreads();
+    return *sn;
+}
+
 // Ordered combine, layer form: out[c] += wsum*y over the token's segment
 // positions in ascending order (= ascending expert id), one multiply and one
-// add per term as in glm53.cpp:1978-1984 (no fused multiply-add).
-template <typename TY>
+// add per term as in glm53.cpp:1978-1984 (no fused multiply-add).  CW
+// columns per thread (8 when D is a multiple of 8: 16-byte f16 loads).
+template <typename TY, int CW>
 __global__ void combine_tokens_kernel(float *__restrict__ out, const TY *__restrict__ y,
                                       const float *__restrict__ rw,
                                       const int *__restrict__ tok_pos, int T, int KK, int D,
@@ -665,47 +760,23 @@ __global__ void combine_tokens_kernel(float *__restrict__ out, const TY *__restr
     // the caller passed it; mvllm_moe_layer_error reports the code.
     if (err && load_volatile(err) != 0)
         return;
-    constexpr int kB = 4; // rows loaded per batch
+    __shared__ int spos[32], sn;
     for (int c = blockIdx.y; c < T; c += gridDim.y) {
-        int pos[17];
-        int n = 0;
-        for (int t = 0; t < KK && n < 17; ++t) {
-            const int p = tok_pos[static_cast<size_t>(c) * KK + t];
-            if (p >= 0) {
-                int j = n++;
-                while (j > 0 && pos[j - 1] > p) {
-                    pos[j] = pos[j - 1];
-                    --j;
-                }
-                pos[j] = p;
-            }
-        }
-        for (int col = (blockIdx.x * blockDim.x + threadIdx.x) * 4; col < D;
-             col += gridDim.x * blockDim.x * 4) {
-            float4 acc = *reinterpret_cast<const float4 *>(out + static_cast<size_t>(c) * D + col);
-            for (int j0 = 0; j0 < n; j0 += kB) {
-                // Every row of the batch in flight before the ordered adds.
-                float4 v[kB];
-                float w[kB];
+        const int n = token_slots_shared(tok_pos, c, KK, spos, &sn);
+        for (int col = (blockIdx.x * blockDim.x + threadIdx.x) * CW; col < D;
+             col += gridDim.x * blockDim.x * CW) {
+            float *o = out + static_cast<size_t>(c) * D + col;
+            float acc[CW];
 #pragma unroll
-                for (int b = 0; b < kB; ++b) {
-                    if (j0 + b < n) {
-                        const int r = pos[j0 + b];
-                        w[b] = __ldg(rw + r);
-                        v[b] = load_y4(y, static_cast<size_t>(r) * D + col);
-                    }
-                }
-#pragma unroll
-                for (int b = 0; b < kB; ++b) {
-                    if (j0 + b < n) {
-                        acc.x = __fadd_rn(acc.x, __fmul_rn(w[b], v[b].x));
-                        acc.y = __fadd_rn(acc.y, __fmul_rn(w[b], v[b].y));
-                        acc.z = __fadd_rn(acc.z, __fmul_rn(w[b], v[b].z));
-                        acc.w = __fadd_rn(acc.w, __fmul_rn(w[b], v[b].w));
-                    }
-                }
+            for (int q = 0; q < CW; q += 4) {
+                const float4 a = *reinterpret_cast<const float4 *>(o + q);
+                acc[q] = a.x, acc[q + 1] = a.y, acc[q + 2] = a.z, acc[q + 3] = a.w;
             }
-            *reinterpret_cast<float4 *>(out + static_cast<size_t>(c) * D + col) = acc;
+            ordered_sum<CW>(acc, y, rw, spos, n, col, D);
+#pragma unroll
+            for (int q = 0; q < CW; q += 4)
+                *reinterpret_cast<float4 *>(o + q) =
+                    make_float4(acc[q], acc[q + 1], acc[q + 2], acc[q + 3]);
         }
     }
 }
@@ -743,38 +814,22 @@ __global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const TY 
     // mvllm_moe_layer_error reports the code.
     const bool failed = err && load_volatile(err) != 0;
     __shared__ float wmax[32];
-    const int n4 = D / 4;
+    const int n8 = D / 8;
     const size_t pitch = 2 * static_cast<size_t>(D) + 16;
+    __shared__ int spos[32], sn;
     for (int c = blockIdx.x; c < T; c += gridDim.x) {
-        int pos[17];
-        int n = 0;
-        for (int t = 0; t < KK && n < 17; ++t) {
-            const int p = tok_pos[static_cast<size_t>(c) * KK + t];
-            if (p >= 0) {
-                int j = n++;
-                while (j > 0 && pos[j - 1] > p) {
-                    pos[j] = pos[j - 1];
-                    --j;
-                }
-                pos[j] = p;
-            }
-        }
+        const int n = token_slots_shared(tok_pos, c, KK, spos, &sn);
         if (peer.win && n == 0)
             continue;  // uniform over the block: every thread read the same slots
         float m = 0.f;
-        for (int v = threadIdx.x; v < n4; v += blockDim.x) {
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int j = 0; j < n; ++j) {
-                const float w = rw[pos[j]];
-                const float4 a = load_y4(y, static_cast<size_t>(pos[j]) * D +
-                                                4 * static_cast<size_t>(v));
-                acc.x = __fadd_rn(acc.x, __fmul_rn(w, a.x));
-                acc.y = __fadd_rn(acc.y, __fmul_rn(w, a.y));
-                acc.z = __fadd_rn(acc.z, __fmul_rn(w, a.z));
-                acc.w = __fadd_rn(acc.w, __fmul_rn(w, a.w));
-            }
-            srow[v] = acc;
-            m = fmaxf(m, fmaxf(fmaxf(fabsf(acc.x), fabsf(acc.y)), fmaxf(fabsf(acc.z), fabsf(acc.w))));
+        for (int v = threadIdx.x; v < n8; v += blockDim.x) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            ordered_sum<8>(acc, y, rw, spos, n, 8 * static_cast<size_t>(v), D);
+            srow[2 * v] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            srow[2 * v + 1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                m = fmaxf(m, fabsf(acc[q]));
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1)
@@ -795,14 +850,16 @@ __global__ void combine_tokens_f16_kernel(uint8_t *__restrict__ out16, const TY 
             row = peer.win[o] + peer.back_off +
                   (static_cast<size_t>(peer.self) * peer.seg + j) * pitch;
         }
-        for (int v = threadIdx.x; v < n4; v += blockDim.x) {
-            const float4 a = srow[v];
-            __half2 h[2] = {__floats2half2_rn(a.x * inv, a.y * inv),
-                            __floats2half2_rn(a.z * inv, a.w * inv)};
+        for (int v = threadIdx.x; v < n8; v += blockDim.x) {
+            const float4 a = srow[2 * v], b = srow[2 * v + 1];
+            __half2 h[4] = {__floats2half2_rn(a.x * inv, a.y * inv),
+                            __floats2half2_rn(a.z * inv, a.w * inv),
+                            __floats2half2_rn(b.x * inv, b.y * inv),
+                            __floats2half2_rn(b.z * inv, b.w * inv)};
             if (failed)
-                h[0] = h[1] = __floats2half2_rn(0.f, 0.f);
-            *reinterpret_cast<uint2 *>(row + 8 * static_cast<size_t>(v)) =
-                *reinterpret_cast<const uint2 *>(h);
+                h[0] = h[1] = h[2] = h[3] = __floats2half2_rn(0.f, 0.f);
+            *reinterpret_cast<uint4 *>(row + 16 * static_cast<size_t>(v)) =
+                *reinterpret_cast<const uint4 *>(h);
         }
         if (threadIdx.x == 0)
             *reinterpret_cast<float4 *>(row + 2 * static_cast<size_t>(D)) =

@@ -2228,18 +2228,24 @@ static int layer_combine(cudaStream_t st, int sms, int T, int KK, int D, float *
                                                                     T, KK, D, w.err, peer);
         }
     } else {
-        dim3 grid(std::max(1, std::min((D / 4 + 255) / 256, 8)), std::min(T, 65535));
-        if (w.y16)
-            CUDA_TRY(launch_pdl(combine_tokens_kernel<__half>, grid, dim3(256), 0, st, out,
-                                reinterpret_cast<const __half *>(w.y),
-                                static_cast<const float *>(l.rw),
-                                static_cast<const int *>(l.tok_pos), T, KK, D,
-                                static_cast<const int *>(w.err)));
-        else
-            CUDA_TRY(launch_pdl(combine_tokens_kernel<float>, grid, dim3(256), 0, st, out,
-                                static_cast<const float *>(w.y), static_cast<const float *>(l.rw),
-                                static_cast<const int *>(l.tok_pos), T, KK, D,
-                                static_cast<const int *>(w.err)));
+        const bool cw8 = D % 8 == 0;
+        const int cw = cw8 ? 8 : 4;
+        dim3 grid(std::max(1, std::min((D / cw + 255) / 256, 8)), std::min(T, 65535));
+        const float *rw = l.rw;
+        const int *tp = l.tok_pos, *err = w.err;
+        if (w.y16) {
+            const __half *y = reinterpret_cast<const __half *>(w.y);
+            CUDA_TRY(cw8 ? launch_pdl(combine_tokens_kernel<__half, 8>, grid, dim3(256), 0, st,
+                                      out, y, rw, tp, T, KK, D, err)
+                         : launch_pdl(combine_tokens_kernel<__half, 4>, grid, dim3(256), 0, st,
+                                      out, y, rw, tp, T, KK, D, err));
+        } else {
+            const float *y = w.y;
+            CUDA_TRY(cw8 ? launch_pdl(combine_tokens_kernel<float, 8>, grid, dim3(256), 0, st,
+                                      out, y, rw, tp, T, KK, D, err)
+                         : launch_pdl(combine_tokens_kernel<float, 4>, grid, dim3(256), 0, st,
+                                      out, y, rw, tp, T, KK, D, err));
+        }
     }
     CUDA_TRY(cudaGetLastError());
     prof_mark(st, kPhCombine);
