@@ -65,7 +65,7 @@ def parse():
     ap.add_argument("--ep-mode", default="auto", choices=["auto", "compact", "fixed", "peer"],
                     help="NCCL exchange with segments sized by host counts (compact) or fixed "
                          "(no host synchronisation), or stores over NVLink into the ranks' "
-                         "IPC-mapped windows (peer); auto: peer up to 4 GPUs, compact above")
+                         "IPC-mapped windows (peer); auto: peer")
     ap.add_argument("--ep-chunks", type=int, default=1,
                     help="token slices per expert-parallel step (N > 1): the exchanges of one "
                          "slice overlap the experts of another")
@@ -1205,9 +1205,9 @@ def run_reference(args):
 # -------------------------------------------------------------------- ours --
 def auto_ep_mode(world):
     """The exchange form `--ep-mode auto` picks: stores over NVLink into the
-    ranks' IPC-mapped windows (EPLayer.forward_peer) up to 4 GPUs, where it
-    measured fastest; the compact NCCL form above."""
-    return "peer" if world <= 4 else "compact"
+    ranks' IPC-mapped windows (EPLayer.forward_peer), the fastest measured at
+    2, 4 and 8 GPUs."""
+    return "peer"
 
 
 def launches_per_ep_step(world, mode):
