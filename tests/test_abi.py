@@ -88,6 +88,46 @@ def test_backend_identity_and_uninitialised_errors(lib):
     assert lib.lib().mvllm_moe_layer_workspace(4, 2, 8, 0, 512, 512, 7) > 0
 
 
+def test_peer_window_layout_and_argument_checks(lib):
+    """The exchange window's layout (a host function) and the peer entries'
+    argument checks, which return before any device work."""
+    D, K, N, seg = 7168, 8, 8, 1024
+    total, off = lib.ep_window_layout(N, seg, K, D, lib.DTYPE_BF16)
+    rows = N * seg
+    assert off["x"] == 0
+    assert off["ids"] >= rows * D * 2 and off["wt"] >= off["ids"] + rows * K * 4
+    assert off["back"] >= off["wt"] + rows * K * 4
+    assert total >= off["back"] + rows * lib.partial_row_bytes(D)
+    assert all(v % 256 == 0 for v in off.values()) and total % 256 == 0
+    assert total - off["back"] < rows * lib.partial_row_bytes(D) + 256
+    f32, _ = lib.ep_window_layout(N, seg, K, D, lib.DTYPE_F32)
+    assert f32 > total
+    L = lib.lib()
+    for bad in ((0, seg, K, D, 1), (33, seg, K, D, 1), (N, 0, K, D, 1), (N, seg, 17, D, 1),
+                (N, seg, K, 12, 1), (N, seg, K, D, 5)):
+        assert L.mvllm_moe_ep_window_layout(*bad, None) == 0
+    with pytest.raises(lib.MoeError):
+        lib.ep_window_layout(0, seg, K, D, lib.DTYPE_BF16)
+    nul = C.c_void_p()
+    assert L.mvllm_moe_peer_open(None, C.byref(nul)) == lib.ERR_INVALID
+    assert L.mvllm_moe_peer_close(None) == lib.ERR_INVALID
+    assert L.mvllm_moe_peer_free(None) == lib.ERR_INVALID
+    assert L.mvllm_moe_peer_alloc(0, C.byref(nul), None) == lib.ERR_INVALID
+    with pytest.raises(ValueError):
+        lib.peer_open(b"short")
+    p = C.c_void_p(4096)
+    # dispatch: T above the segment, then nranks 0
+    assert L.mvllm_moe_ep_dispatch_peer_dev(None, p, 1, p, p, 9, K, D, 384, N, None, None, 0, 8,
+                                            p, p, p) == lib.ERR_INVALID
+    assert L.mvllm_moe_ep_dispatch_peer_dev(None, p, 1, p, p, 8, K, D, 384, 0, None, None, 0, 8,
+                                            p, p, p) == lib.ERR_INVALID
+    # partial-peer: a window address that is not 256-byte aligned
+    tabs = [p] * 6
+    assert L.mvllm_moe_layer_partial_peer_dev(None, N, seg, 0, K, 48, D, 2048, 7, 1,
+                                              C.c_void_p(4096 + 16), p, *tabs, 2, 4.0, 25.0,
+                                              p, 1 << 30) == lib.ERR_INVALID
+
+
 def test_init_without_gpu_reports_error(lib):
     try:
         import torch
