@@ -1385,6 +1385,13 @@ def main():
                    "sample": f"{toks:.0f} config[4] tokens: {nth} threads x 2 rounds of the "
                              f"reference moe_block on one token row through 8 MXFP4 experts "
                              f"(7168 / 2048), {sec:.1f} s wall"}
+            # The reference moe_block is single-threaded: its one-core rate
+            # is the primary CPU figure, the threaded one above a secondary.
+            r1, s1, t1 = cpu_reference_rate(1, 2, 8, rows_per_token=8.0)
+            cpu["single_core"] = {
+                "value": r1, "unit": "tokens/s", "cores": 1,
+                "sample": f"{t1:.0f} config[4] tokens, one after another on one thread, "
+                          f"{s1:.1f} s wall"}
         except Exception as ex:  # the reference build may be absent
             cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
                    "sample": f"unavailable: {ex}"}

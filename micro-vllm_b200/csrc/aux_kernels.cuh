@@ -323,10 +323,47 @@ __global__ void stage_rows_kernel(const TIn *__restrict__ x, const int *__restri
     }
 }
 
+// Eight consecutive values of row xr (the aligned 8-column chunk c) as the 16
+// bytes of f16 the staged row holds there, in stage_pos order.  `big` is set
+// when a finite value lies beyond the f16 range (it would otherwise become inf).
+template <typename TIn>
+__device__ __forceinline__ uint4 stage_chunk8(const TIn *__restrict__ xr, int c, int fmt,
+                                              bool &big) {
+    float v[8];
+    if constexpr (sizeof(TIn) == 4) {
+        const float4 *p = reinterpret_cast<const float4 *>(xr) + 2 * c;
+        const float4 a = __ldg(p), b = __ldg(p + 1);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+        v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    } else {
+        const uint4 a = __ldg(reinterpret_cast<const uint4 *>(xr) + c);
+        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            v[2 * j] = __uint_as_float(w[j] << 16);
+            v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        big |= beyond_f16(v[j]);
+    __half2 h[4];
+    if (fmt == MVLLM_FMT_INT4_G64) { // k0,k4,k1,k5,k2,k6,k3,k7
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            h[j] = __floats2half2_rn(v[j], v[j + 4]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+    }
+    return *reinterpret_cast<const uint4 *>(h);
+}
+
 // Vectorised form for the fast path (D % 8 == 0): a CTA per row at a time,
 // a thread per aligned 8-column chunk, 16-byte stores of f16 in stage_pos
 // order (several chunks per thread in flight).  A finite value beyond the
-// f16 range records MVLLM_ERR_ACT_RANGE (it would otherwise become inf).
+// f16 range records MVLLM_ERR_ACT_RANGE.
 template <typename TIn>
 __device__ __forceinline__ void stage_rows_body(const TIn *__restrict__ x,
                                                 const int *__restrict__ index,
@@ -341,38 +378,11 @@ __device__ __forceinline__ void stage_rows_body(const TIn *__restrict__ x,
         uint4 *orow = reinterpret_cast<uint4 *>(out + static_cast<size_t>(r) * D);
 #pragma unroll 4
         for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
-            float v[8];
-            if constexpr (sizeof(TIn) == 4) {
-                const float4 *p = reinterpret_cast<const float4 *>(xr) + 2 * c;
-                const float4 a = __ldg(p), b = __ldg(p + 1);
-                v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
-                v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-            } else {
-                const uint4 a = __ldg(reinterpret_cast<const uint4 *>(xr) + c);
-                const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    v[2 * j] = __uint_as_float(w[j] << 16);
-                    v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
-                }
-            }
             bool big = false;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                big |= beyond_f16(v[j]);
+            const uint4 v = stage_chunk8(xr, c, fmt, big);
             if (big)
                 set_error(err, MVLLM_ERR_ACT_RANGE);
-            __half2 h[4];
-            if (fmt == MVLLM_FMT_INT4_G64) { // k0,k4,k1,k5,k2,k6,k3,k7
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    h[j] = __floats2half2_rn(v[j], v[j + 4]);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-            }
-            orow[c] = *reinterpret_cast<const uint4 *>(h);
+            orow[c] = v;
         }
     }
 }
@@ -744,6 +754,37 @@ __device__ __forceinline__ int token_slots_shared(const int *__restrict__ tok_po
     }
     __syncthreads();
     return *sn;
+}
+
+// Token-major gather-stage for large calls (fast path, D % 8 == 0, KK <= 32):
+// a CTA per token at a time reads the token's row once, converts each
+// 8-column chunk once (stage_chunk8) and stores it at every expert-major
+// position the permutation gave the token's slots (tok_pos >= 0).  The bytes
+// written are those of stage_rows_body over rows[]; x is read once per token
+// instead of once per slot, so its reads do not depend on x staying in L2
+// while the K-fold larger staged rows stream through it.  A token without a
+// slot is neither read nor range-checked, as in the row form.
+template <typename TIn>
+__global__ void __launch_bounds__(256)
+    stage_tokens_f16x8_kernel(const TIn *__restrict__ x, const int *__restrict__ tok_pos, int T,
+                              int KK, int D, int fmt, __half *__restrict__ out, int *err) {
+    pdl_wait();
+    __shared__ int spos[32], sn;
+    const int chunks = D >> 3;
+    for (int c = blockIdx.x; c < T; c += gridDim.x) {
+        const int n = token_slots_shared(tok_pos, c, KK, spos, &sn);
+        if (n == 0)
+            continue; // uniform over the block
+        const TIn *xr = x + static_cast<size_t>(c) * D;
+        for (int k = threadIdx.x; k < chunks; k += blockDim.x) {
+            bool big = false;
+            const uint4 v = stage_chunk8(xr, k, fmt, big);
+            if (big)
+                set_error(err, MVLLM_ERR_ACT_RANGE);
+            for (int j = 0; j < n; ++j)
+                reinterpret_cast<uint4 *>(out + static_cast<size_t>(spos[j]) * D)[k] = v;
+        }
+    }
 }
 
 // Ordered combine, layer form: out[c] += wsum*y over the token's segment

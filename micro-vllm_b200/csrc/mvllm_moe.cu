@@ -2166,21 +2166,20 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
     if (hooks && hooks->before_gather)
         if (int rc = hooks->before_gather())
             return rc;
-    // Gather + stage the token rows into expert-major order.
+    // Gather + stage the token rows into expert-major order: token-major on
+    // the fast path (each x row read once, stored at its slots' positions).
     const int gblocks = std::min(R, 8 * sms);
     if (fast) {
-        const int vblocks = std::max(1, std::min(R, 8 * sms));
+        const int tblocks = std::max(1, std::min(T, 8 * sms));
         if (x_dtype == MVLLM_DTYPE_BF16)
-            CUDA_TRY(launch_pdl(stage_rows_f16x8_kernel<__nv_bfloat16>, dim3(vblocks), dim3(256), 0,
-                                st, static_cast<const __nv_bfloat16 *>(x),
-                                static_cast<const int *>(l.rows),
-                                static_cast<const int *>(l.n_rows), 0, D, fmt,
+            CUDA_TRY(launch_pdl(stage_tokens_f16x8_kernel<__nv_bfloat16>, dim3(tblocks),
+                                dim3(256), 0, st, static_cast<const __nv_bfloat16 *>(x),
+                                static_cast<const int *>(l.tok_pos), T, KK, D, fmt,
                                 static_cast<__half *>(l.run.xs), l.run.err));
         else
-            CUDA_TRY(launch_pdl(stage_rows_f16x8_kernel<float>, dim3(vblocks), dim3(256), 0, st,
-                                static_cast<const float *>(x), static_cast<const int *>(l.rows),
-                                static_cast<const int *>(l.n_rows), 0, D, fmt,
-                                static_cast<__half *>(l.run.xs), l.run.err));
+            CUDA_TRY(launch_pdl(stage_tokens_f16x8_kernel<float>, dim3(tblocks), dim3(256), 0, st,
+                                static_cast<const float *>(x), static_cast<const int *>(l.tok_pos),
+                                T, KK, D, fmt, static_cast<__half *>(l.run.xs), l.run.err));
     } else {
         if (x_dtype == MVLLM_DTYPE_BF16)
             stage_rows_kernel<__nv_bfloat16, float><<<gblocks, 256, 0, st>>>(

@@ -80,12 +80,16 @@ def test_beyond_f16_is_refused(moe, port, where):
     np.testing.assert_array_equal(out, base)
 
 
-def test_layer_dev_error_leaves_out(moe, port):
+@pytest.mark.parametrize("T", [24, 300])
+def test_layer_dev_error_leaves_out(moe, port, T):
     """A device-pointer call (no host sync) with a token row beyond the f16
     range: the combine does not run, so `out` keeps the caller's rows, and
     mvllm_moe_layer_error reports MVLLM_ERR_ACT_RANGE; the next clean call
-    on the same workspace reports MVLLM_OK."""
-    D, I, E, K, T = 512, 512, 4, 2, 24
+    on the same workspace reports MVLLM_OK.  T = 24 takes the decode-sized
+    chain (row-order staging), T = 300 the large one (token-order staging).
+    In both, a token routed to no expert is not staged, so a huge value in
+    it is not an error (the clean call carries one)."""
+    D, I, E, K = 512, 512, 4, 2
     rng = np.random.default_rng(57)
     ex = cases.make_experts(port, rng, cases.FMT_MXFP4, E, D, I)
     tabs = [[], [], [], [], [], []]
@@ -96,9 +100,12 @@ def test_layer_dev_error_leaves_out(moe, port):
             keep.append(t)
             tabs[k].append(t.data_ptr())
     tables = [torch.tensor(t, dtype=torch.int64, device="cuda") for t in tabs]
-    idx = torch.from_numpy(rng.integers(0, E, (T, K)).astype(np.int32)).cuda()
+    idx_h = rng.integers(0, E, (T, K)).astype(np.int32)
+    idx_h[T - 2] = -1  # token T-2 goes to no expert
+    idx = torch.from_numpy(idx_h).cuda()
     wt = torch.full((T, K), 0.5, device="cuda")
     x = rng.standard_normal((T, D)).astype(np.float32)
+    x[T - 2] *= np.float32(1e6)
     ws = torch.empty(moe.layer_workspace_bytes(T, K, E, 0, D, I, cases.FMT_MXFP4),
                      dtype=torch.uint8, device="cuda")
     base = torch.from_numpy(rng.standard_normal((T, D)).astype(np.float32)).cuda()
