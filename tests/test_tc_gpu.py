@@ -105,10 +105,15 @@ def test_tc_mixed_paths(moe, port, monkeypatch, prefill_mode, mode):
 
 
 @pytest.mark.parametrize("mode", MODES_OK)
-def test_tc_device_layer(moe, port, monkeypatch, prefill_mode, mode):
-    """The device-pointer layer entry (permute -> gather -> experts -> combine)."""
+@pytest.mark.parametrize("name", ["mxfp4_one_tile", "mxfp4_two_tiles", "int4_two_tiles"])
+def test_tc_device_layer(moe, port, monkeypatch, prefill_mode, mode, name):
+    """The device-pointer layer entry (permute -> gather -> experts -> combine).
+    One tile (T = 160) takes the decode-sized chain; two tiles (T = 600 bf16,
+    T = 450 f32 int4 rows) the large one, whose gather-stage runs token-major."""
+    if mode != "f16" and not name.startswith("mxfp4"):
+        pytest.skip("block-scaled modes apply to MXFP4 experts")
     prefill_mode(mode)
-    c = make(port, "mxfp4_one_tile")
+    c = make(port, name)
     _, want = cases.run_block(port, c)
     force_tc(monkeypatch)
     T, K, E, ns, D, I = c["T"], c["K"], c["E"], c["n_shared"], c["D"], c["I"]
@@ -122,12 +127,14 @@ def test_tc_device_layer(moe, port, monkeypatch, prefill_mode, mode):
     ws = torch.empty(moe.layer_workspace_bytes(T, K, E, ns, D, I, c["fmt"]), dtype=torch.uint8,
                      device="cuda")
     out = torch.zeros((T, D), dtype=torch.float32, device="cuda")
-    xd = torch.from_numpy(c["x"]).cuda().to(torch.bfloat16)
+    xd = torch.from_numpy(c["x"]).cuda()
+    if CASES[name]["bf16_x"]:
+        xd = xd.to(torch.bfloat16)
     moe.layer_dev(T, K, E, ns, D, I, c["fmt"], torch.from_numpy(c["idx"]).cuda(),
                   torch.from_numpy(c["wt"]).cuda(), xd, tables, out, c["act"], c["act_a"],
                   c["act_b"], ws)
     torch.cuda.synchronize()
-    assert_close(out.cpu().numpy(), want, "layer_dev tensor-core")
+    assert_close(out.cpu().numpy(), want, f"layer_dev tensor-core {name} {mode}")
 
 
 @pytest.mark.parametrize("mode", MODES_OK)
