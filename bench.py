@@ -89,6 +89,14 @@ def parse():
     ap.add_argument("--profile-epilogue-router", action="store_true",
                     help="only run the layer epilogue and the router at the K3 / DeepSeek-V4 "
                          "decode shape, two calls each between cudaProfilerStart/Stop")
+    ap.add_argument("--profile-prefill-modes", default="",
+                    help="only build the config[3] prefill layer and, per listed tensor-core "
+                         "mode (comma-separated names), time five steps and run one between "
+                         "cudaProfilerStart/Stop (for ncu --profile-from-start off)")
+    ap.add_argument("--mma-rates", action="store_true",
+                    help="only print the tensor pipes' measured rates over MMA widths: "
+                         "kind::f16 on single CTAs (A and B from shared memory) and "
+                         "kind::mxf8f6f4 on single CTAs and CTA pairs")
     ap.add_argument("--experts", type=int, default=256,
                     help="routed experts (BASELINE config[1]: 256); fewer only to size a "
                          "profiler capture")
@@ -1277,6 +1285,56 @@ def profile_only(moe, torch, args):
     print(json.dumps({"profile": "epilogue+router", "tokens": T}), flush=True)
 
 
+def profile_prefill_modes(moe, torch, modes):
+    """Config[3] (the prefill leg's workload: 4096 tokens, Zipf routing) in
+    each listed tensor-core mode: five timed steps, then one step between
+    cudaProfilerStart/Stop, so an ncu launch list holds one step per mode in
+    the order given."""
+    D, I, E, K = CFG["D"], CFG["I"], CFG["E"], CFG["K"]
+    wl = Workload(moe, torch, 32, seed=1234)
+    g = torch.Generator(device="cuda").manual_seed(4242)
+    idx, wt = zipf_routing(torch, PREFILL_T, E, K, g)
+    x = torch.randn((PREFILL_T, D), generator=g, device="cuda").to(torch.bfloat16)
+    out = torch.zeros((PREFILL_T, D), dtype=torch.float32, device="cuda")
+    ws = torch.empty(moe.layer_workspace_bytes(PREFILL_T, K, E, 0, D, I, CFG["fmt"]),
+                     dtype=torch.uint8, device="cuda")
+
+    def step():
+        moe.layer_dev(PREFILL_T, K, E, 0, D, I, CFG["fmt"], idx, wt, x, wl.tables, out,
+                      CFG["act"], CFG["act_a"], CFG["act_b"], ws)
+
+    res = {}
+    for mode in modes:
+        moe.set_prefill_mode(mode)
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(5):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        res[mode] = a.elapsed_time(b) / 5
+        torch.cuda.profiler.start()
+        step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+    moe.set_prefill_mode(None)
+    print(json.dumps({"profile": "prefill modes", "tokens": PREFILL_T, "ms_per_step": res}),
+          flush=True)
+
+
+def mma_rates(moe):
+    """The tensor pipes' measured rates (TFLOP/s, back-to-back MMAs on every
+    SM) over the MMA's N: kind::f16 on single CTAs (M = 128), kind::mxf8f6f4
+    on single CTAs and CTA pairs."""
+    res = {"f16_solo": {n: moe.mma_rate(2, n, 0) for n in (64, 128, 176, 192, 256)},
+           "mxf8f6f4_solo": {n: moe.mma_rate(1, n, 0) for n in (128, 176, 192, 256)},
+           "mxf8f6f4_pair": {n: moe.mma_rate(1, n, 1) for n in (128, 176, 192, 256)}}
+    print(json.dumps({"profile": "mma rates", "tflops": res}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1302,6 +1360,12 @@ def main():
     mode = moe.PREFILL_NAMES[moe.get_prefill_mode()]
     if args.profile_decode_batch or args.profile_epilogue_router:
         profile_only(moe, torch, args)
+        return
+    if args.profile_prefill_modes:
+        profile_prefill_modes(moe, torch, args.profile_prefill_modes.split(","))
+        return
+    if args.mma_rates:
+        mma_rates(moe)
         return
     if args.profile_headline:
         global PROFILE_HEADLINE, EP_E, EP_T

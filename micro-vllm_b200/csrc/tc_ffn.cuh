@@ -75,9 +75,11 @@ constexpr int kTcWideMax = 192;   // ... of at most this many on wide single CTA
 // runs at the tensor rate), a tile of a few dozen tokens is bound by issue,
 // so it runs on single CTAs, two per SM, each with its own issuing thread;
 // between the two (a 65..192-row rest, e.g. 171 rows per expert at config[4]),
-// one CTA per SM is bound by the tensor rate (N = 176: about 93 cycles of
-// tensor time per MMA against 45 of issue) where a pair would be bound by
-// its issue.
+// one CTA per SM (about 123 cycles per N = 176 MMA) beats a pair bound by its
+// issue.  The wide tile is bound by shared-memory bandwidth: per MMA its
+// token slice (5.6 KB) is written by TMA and read by the MMA, with 1 KB of
+// packed weights read by the dequant warps, about 96 cycles at 128 B/clk;
+// the tensor pipe alone would take 88.
 template <bool PAIR, bool WIDE = false> struct TcCfg {
     static constexpr bool BIG = PAIR || WIDE;     // one CTA per SM, 8 + 8 warps
     static constexpr int EPI_WARPS = BIG ? 8 : 4; // quadrant = warp % 4, chunk half = warp / 4
