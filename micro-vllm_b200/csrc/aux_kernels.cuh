@@ -124,7 +124,36 @@ struct PlanArgs {
     int *woff1, *woff2;
 };
 
-__device__ __forceinline__ void plan_body(const PlanArgs &a) {
+// An expert's six weight / scale pointers, loaded ahead of their use.
+struct ExpertPtrs {
+    uintptr_t p[6];
+};
+__device__ __forceinline__ ExpertPtrs expert_ptrs(const PlanArgs &a, int e) {
+    ExpertPtrs r;
+    r.p[0] = reinterpret_cast<uintptr_t>(a.g[e]);
+    r.p[1] = reinterpret_cast<uintptr_t>(a.u[e]);
+    r.p[2] = reinterpret_cast<uintptr_t>(a.d[e]);
+    const bool more = a.fmt != MVLLM_FMT_F32 || a.align_mask;
+    r.p[3] = more ? reinterpret_cast<uintptr_t>(a.gs[e]) : 0;
+    r.p[4] = more ? reinterpret_cast<uintptr_t>(a.us[e]) : 0;
+    r.p[5] = more ? reinterpret_cast<uintptr_t>(a.ds[e]) : 0;
+    return r;
+}
+// Bit 0: every array the format needs is present; bit 1: one of them breaks
+// the fast path's alignment (a.align_mask).
+__device__ __forceinline__ int expert_ptr_bits(const PlanArgs &a, const ExpertPtrs &r) {
+    bool present = r.p[0] && r.p[1] && r.p[2];
+    if (a.fmt != MVLLM_FMT_F32)
+        present = present && r.p[3] && r.p[4] && r.p[5];
+    if (!present)
+        return 0;
+    const uintptr_t any = r.p[0] | r.p[1] | r.p[2] | r.p[3] | r.p[4] | r.p[5];
+    return (a.align_mask && (any & static_cast<uintptr_t>(a.align_mask))) ? 3 : 1;
+}
+
+// tab_pre >= 0: expert_ptr_bits of expert threadIdx.x, computed by the caller
+// from pointers it loaded earlier (only when a.nb <= blockDim.x).
+__device__ __forceinline__ void plan_body(const PlanArgs &a, int tab_pre = -1) {
     __shared__ int warp_sums[11 * 32];
     __shared__ int carry[11];
     if (threadIdx.x < 11)
@@ -136,17 +165,11 @@ __device__ __forceinline__ void plan_body(const PlanArgs &a) {
         int m1 = 0, m2 = 0;
         if (e < a.nb) {
             n = max(a.nr[e], 0);
-            bool ok = n > 0 && a.g[e] && a.u[e] && a.d[e];
-            if (a.fmt != MVLLM_FMT_F32)
-                ok = ok && a.gs[e] && a.us[e] && a.ds[e];
-            if (ok && a.align_mask) {
-                const uintptr_t bits = reinterpret_cast<uintptr_t>(a.g[e]) |
-                                       reinterpret_cast<uintptr_t>(a.u[e]) |
-                                       reinterpret_cast<uintptr_t>(a.d[e]) |
-                                       reinterpret_cast<uintptr_t>(a.gs[e]) |
-                                       reinterpret_cast<uintptr_t>(a.us[e]) |
-                                       reinterpret_cast<uintptr_t>(a.ds[e]);
-                if (bits & static_cast<uintptr_t>(a.align_mask)) {
+            bool ok = n > 0;
+            if (ok) {
+                const int tb = tab_pre >= 0 ? tab_pre : expert_ptr_bits(a, expert_ptrs(a, e));
+                ok = (tb & 1) != 0;
+                if (ok && (tb & 2)) {
                     set_error(a.err, MVLLM_ERR_DEVICE); // would break the bulk copies: skip
                     ok = false;
                 }
@@ -619,6 +642,122 @@ __global__ void __launch_bounds__(1024)
                        rows, rw, tok_pos);
 }
 
+// The same four steps for the layer's decode-sized calls (K <= KMAX), with
+// every array the CTA reads back in shared memory: the membership bitmap and
+// word prefixes (bm, wp, [E + n_shared][words]), the counts and segment
+// starts (nr_s, xoff_s, [E + n_shared]) and per slot the weight sum and state
+// (ws, tk, [T][K + n_shared]; tk = the slot's expert while it waits to be
+// placed, -1 for none).  A token's ids and weights are loaded once into
+// registers.  Outputs (nr, xoff, n_rows, rows, rw, tok_pos) are those of
+// permute_small_body, bit for bit: the same membership, the same ascending
+// order of the weight sums.
+template <int KMAX>
+__device__ __forceinline__ void permute_small_smem_body(
+    const int *__restrict__ idx, const float *__restrict__ wt, int T, int K, int E, int n_shared,
+    int words, uint32_t *bm, int *wp, float *ws, int *tk, int *nr_s, int *xoff_s,
+    int *__restrict__ nr, int *__restrict__ xoff, int *__restrict__ n_rows,
+    int *__restrict__ rows, float *__restrict__ rw, int *__restrict__ tok_pos) {
+    __shared__ int warp_sums[32];
+    const int EE = E + n_shared, KK = K + n_shared;
+    for (int i = threadIdx.x; i < EE * words; i += blockDim.x)
+        bm[i] = 0u;
+    __syncthreads();
+    // step 1: membership and per-token weight sums
+    for (int c = threadIdx.x; c < T; c += blockDim.x) {
+        const int *ic = idx + static_cast<size_t>(c) * K;
+        const float *wc = wt + static_cast<size_t>(c) * K;
+        int ids[KMAX];
+        float w[KMAX];
+#pragma unroll
+        for (int t = 0; t < KMAX; ++t) {
+            ids[t] = t < K ? ic[t] : -1;
+            w[t] = t < K ? wc[t] : 0.f;
+        }
+#pragma unroll
+        for (int t = 0; t < KMAX; ++t) {
+            if (t >= K)
+                continue; // (not break: the loop stays fully unrolled, ids / w in registers)
+            const int e = ids[t];
+            int st = -1;
+            if (e >= 0 && e < E) {
+                bool dup = false;
+#pragma unroll
+                for (int t2 = 0; t2 < t; ++t2)
+                    dup |= (ids[t2] == e);
+                if (!dup) {
+                    float sum = 0.f;
+#pragma unroll
+                    for (int t2 = 0; t2 < KMAX; ++t2)
+                        if (t2 < K && ids[t2] == e)
+                            sum = __fadd_rn(sum, w[t2]);
+                    if (sum != 0.f) {
+                        ws[c * KK + t] = sum;
+                        st = e;
+                        atomicOr(&bm[e * words + (c >> 5)], 1u << (c & 31));
+                    }
+                }
+            }
+            tk[c * KK + t] = st;
+        }
+        if (n_shared) {
+            ws[c * KK + K] = 1.f;
+            tk[c * KK + K] = E;
+            atomicOr(&bm[E * words + (c >> 5)], 1u << (c & 31));
+        }
+    }
+    __syncthreads();
+    // step 2: word prefixes and member counts, a thread per expert
+    for (int e = threadIdx.x; e < EE; e += blockDim.x) {
+        int carry = 0;
+        for (int j = 0; j < words; ++j) {
+            wp[e * words + j] = carry;
+            carry += __popc(bm[e * words + j]);
+        }
+        nr_s[e] = carry;
+        nr[e] = carry;
+    }
+    __syncthreads();
+    // step 3: segment starts in ascending expert id
+    int carry = 0;
+    for (int e0 = 0; e0 < EE; e0 += blockDim.x) {
+        const int e = e0 + threadIdx.x;
+        const int v = e < EE ? nr_s[e] : 0;
+        int tot;
+        const int ex = block_exclusive_scan(v, warp_sums, &tot);
+        if (e < EE) {
+            xoff_s[e] = carry + ex;
+            xoff[e] = carry + ex;
+        }
+        carry += tot;
+    }
+    if (threadIdx.x == 0)
+        *n_rows = carry;
+    __syncthreads();
+    // step 4: positions; every slot's tok_pos written (-1 where none)
+    const int n = T * KK;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = tk[i];
+        if (e < 0) {
+            tok_pos[i] = -1;
+            continue;
+        }
+        const int c = i / KK;
+        const int wi = e * words + (c >> 5);
+        const int pos = xoff_s[e] + wp[wi] + __popc(bm[wi] & ((1u << (c & 31)) - 1u));
+        rows[pos] = c;
+        rw[pos] = ws[i];
+        tok_pos[i] = pos;
+    }
+}
+
+// Shared-memory bytes permute_small_smem_body needs (its arrays, 4 bytes
+// each), for the launch's dynamic shared memory.
+__host__ __device__ constexpr size_t perm_smem_bytes(int T, int KK, int EE, int words) {
+    return (size_t(2) * EE * words + size_t(2) * EE + size_t(2) * T * KK) * 4;
+}
+constexpr int kPermSmemMaxK = 16;
+constexpr size_t kPermSmemMaxBytes = 40 * 1024;
+
 // Decode-sized layer calls (T <= kPermSmallT): the call's error word cleared,
 // the permutation, and the expert plan over its counts, in one CTA -- three
 // launches and a memset folded into one.  The plan reads nr / xoff that the
@@ -636,15 +775,46 @@ struct PermSmallArgs {
     int *tok_pos;
 };
 
+//
+// smem != 0 (K <= kPermSmemMaxK, perm_smem_bytes in the launch's dynamic
+// shared memory): the permutation keeps what it reads back in shared memory
+// and the plan reads the counts and segment starts from there; the experts'
+// pointer tables are loaded at the start (one expert per thread when they
+// fit) and checked only in the plan, so their latency overlaps the
+// permutation.
 __global__ void __launch_bounds__(1024) layer_prep_small_kernel(const PermSmallArgs q,
-                                                                const PlanArgs a) {
+                                                                const PlanArgs a, int smem) {
+    extern __shared__ __align__(16) int psm[];
     pdl_wait();
+    const bool pre = smem && a.nb <= static_cast<int>(blockDim.x);
+    ExpertPtrs ptrs{};
+    if (pre && static_cast<int>(threadIdx.x) < a.nb)
+        ptrs = expert_ptrs(a, threadIdx.x);
     if (threadIdx.x == 0)
         *a.err = 0;
-    permute_small_body(q.idx, q.wt, q.T, q.K, q.E, q.n_shared, q.words, q.bitmap, q.wpre, q.wsum,
-                       q.nr, q.xoff, q.n_rows, q.rows, q.rw, q.tok_pos);
+    if (!smem) {
+        permute_small_body(q.idx, q.wt, q.T, q.K, q.E, q.n_shared, q.words, q.bitmap, q.wpre,
+                           q.wsum, q.nr, q.xoff, q.n_rows, q.rows, q.rw, q.tok_pos);
+        __syncthreads();
+        plan_body(a);
+        return;
+    }
+    const int EE = q.E + q.n_shared, KK = q.K + q.n_shared;
+    uint32_t *bm = reinterpret_cast<uint32_t *>(psm);
+    int *wp = psm + EE * q.words;
+    int *nr_s = wp + EE * q.words;
+    int *xoff_s = nr_s + EE;
+    int *tk = xoff_s + EE;
+    float *ws = reinterpret_cast<float *>(tk + q.T * KK);
+    permute_small_smem_body<kPermSmemMaxK>(q.idx, q.wt, q.T, q.K, q.E, q.n_shared, q.words, bm,
+                                           wp, ws, tk, nr_s, xoff_s, q.nr, q.xoff, q.n_rows,
+                                           q.rows, q.rw, q.tok_pos);
     __syncthreads();
-    plan_body(a);
+    PlanArgs as = a;
+    as.nr = nr_s;
+    as.xoff = xoff_s;
+    plan_body(as, pre ? (static_cast<int>(threadIdx.x) < a.nb ? expert_ptr_bits(a, ptrs) : 0)
+                      : -1);
 }
 
 // ---------------------------------------------------------------------------

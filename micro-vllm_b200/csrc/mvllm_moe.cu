@@ -2123,7 +2123,10 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
         PermSmallArgs q{idx, wt, T, K, E, n_shared, l.perm.words, l.perm.bitmap, l.perm.wpre,
                         l.perm.wsum, l.nr, l.xoff, l.n_rows, l.rows, l.rw, l.tok_pos};
         prof_mark(st, kPhStart);
-        CUDA_TRY(launch_pdl(layer_prep_small_kernel, dim3(1), dim3(1024), 0, st, q, ep.pa));
+        const size_t psm = perm_smem_bytes(T, KK, EE, l.perm.words);
+        const int smem = K <= kPermSmemMaxK && psm <= kPermSmemMaxBytes ? 1 : 0;
+        CUDA_TRY(launch_pdl(layer_prep_small_kernel, dim3(1), dim3(1024), smem ? psm : 0, st, q,
+                            ep.pa, smem));
         prof_mark(st, kPhPermute);
         if (hooks && hooks->before_gather)
             if (int rc = hooks->before_gather())
