@@ -905,12 +905,13 @@ __device__ __forceinline__ void ordered_sum(float (&acc)[CW], const TY *__restri
 // ascending into spos[0..n) in shared memory by the first warp (each lane
 // places its value by the count of smaller ones; positions are distinct).
 // Returns n to every thread.  KK <= 32.
-__device__ __forceinline__ int token_slots_shared(const int *__restrict__ tok_pos, int c, int KK,
-                                                  int *spos, int *sn) {
+// token_slots_from takes the first warp's tok_pos values loaded by the
+// caller (lane < KK: tok_pos[c * KK + lane], else -1), so the load can be
+// issued ahead of other loads.
+__device__ __forceinline__ int token_slots_from(int p, int KK, int *spos, int *sn) {
     __syncthreads();  // the previous token's readers are done with spos
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
-        const int p = lane < KK ? tok_pos[static_cast<size_t>(c) * KK + lane] : -1;
         const uint32_t valid = __ballot_sync(0xffffffffu, p >= 0);
         int rank = 0;
         for (int u = 0; u < KK; ++u) {
@@ -924,6 +925,14 @@ __device__ __forceinline__ int token_slots_shared(const int *__restrict__ tok_po
     }
     __syncthreads();
     return *sn;
+}
+__device__ __forceinline__ int token_slot_load(const int *__restrict__ tok_pos, int c, int KK) {
+    return threadIdx.x < static_cast<unsigned>(KK) ? tok_pos[static_cast<size_t>(c) * KK + threadIdx.x]
+                                                   : -1;
+}
+__device__ __forceinline__ int token_slots_shared(const int *__restrict__ tok_pos, int c, int KK,
+                                                  int *spos, int *sn) {
+    return token_slots_from(token_slot_load(tok_pos, c, KK), KK, spos, sn);
 }
 
 // Token-major gather-stage for large calls (fast path, D % 8 == 0, KK <= 32):
@@ -962,26 +971,46 @@ __global__ void __launch_bounds__(256)
 // add per term as in glm53.cpp:1978-1984 (no fused multiply-add).  CW
 // columns per thread (8 when D is a multiple of 8: 16-byte f16 loads).
 template <typename TY, int CW>
-__global__ void combine_tokens_kernel(float *__restrict__ out, const TY *__restrict__ y,
+__global__ void __launch_bounds__(256, sizeof(TY) == 2 ? 3 : 2)
+    combine_tokens_kernel(float *__restrict__ out, const TY *__restrict__ y,
                                       const float *__restrict__ rw,
                                       const int *__restrict__ tok_pos, int T, int KK, int D,
                                       const int *err) {
     pdl_wait();
     // A device-side error in this call (recorded in *err): `out` is left as
-    // the caller passed it; mvllm_moe_layer_error reports the code.
-    if (err && load_volatile(err) != 0)
-        return;
+    // the caller passed it; mvllm_moe_layer_error reports the code.  The
+    // error word, the token's slot positions and the thread's first `out`
+    // columns are loaded together, one round trip before the y rows.
+    const bool failed = err && load_volatile(err) != 0;
     __shared__ int spos[32], sn;
+    const int col0 = (blockIdx.x * blockDim.x + threadIdx.x) * CW;
     for (int c = blockIdx.y; c < T; c += gridDim.y) {
-        const int n = token_slots_shared(tok_pos, c, KK, spos, &sn);
-        for (int col = (blockIdx.x * blockDim.x + threadIdx.x) * CW; col < D;
-             col += gridDim.x * blockDim.x * CW) {
-            float *o = out + static_cast<size_t>(c) * D + col;
-            float acc[CW];
+        const int p = token_slot_load(tok_pos, c, KK);
+        float first[CW];
+        if (col0 < D) {
+            const float *o = out + static_cast<size_t>(c) * D + col0;
 #pragma unroll
             for (int q = 0; q < CW; q += 4) {
                 const float4 a = *reinterpret_cast<const float4 *>(o + q);
-                acc[q] = a.x, acc[q + 1] = a.y, acc[q + 2] = a.z, acc[q + 3] = a.w;
+                first[q] = a.x, first[q + 1] = a.y, first[q + 2] = a.z, first[q + 3] = a.w;
+            }
+        }
+        if (failed)
+            return; // uniform over the grid, before any barrier of this token
+        const int n = token_slots_from(p, KK, spos, &sn);
+        for (int col = col0; col < D; col += gridDim.x * blockDim.x * CW) {
+            float *o = out + static_cast<size_t>(c) * D + col;
+            float acc[CW];
+            if (col == col0) {
+#pragma unroll
+                for (int q = 0; q < CW; ++q)
+                    acc[q] = first[q];
+            } else {
+#pragma unroll
+                for (int q = 0; q < CW; q += 4) {
+                    const float4 a = *reinterpret_cast<const float4 *>(o + q);
+                    acc[q] = a.x, acc[q + 1] = a.y, acc[q + 2] = a.z, acc[q + 3] = a.w;
+                }
             }
             ordered_sum<CW>(acc, y, rw, spos, n, col, D);
 #pragma unroll
