@@ -386,17 +386,20 @@ __device__ __forceinline__ uint4 stage_chunk8(const TIn *__restrict__ xr, int c,
 // Vectorised form for the fast path (D % 8 == 0): a CTA per row at a time,
 // a thread per aligned 8-column chunk, 16-byte stores of f16 in stage_pos
 // order (several chunks per thread in flight).  A finite value beyond the
-// f16 range records MVLLM_ERR_ACT_RANGE.
+// f16 range records MVLLM_ERR_ACT_RANGE.  `index`, when given, holds at least
+// nblocks entries: the block's first one is loaded together with the row
+// count.
 template <typename TIn>
 __device__ __forceinline__ void stage_rows_body(const TIn *__restrict__ x,
                                                 const int *__restrict__ index,
                                                 const int *__restrict__ nrows_dev, int nrows_host,
                                                 int D, int fmt, __half *__restrict__ out,
                                                 int *err, int block, int nblocks) {
+    const int src0 = index ? __ldg(index + block) : block;
     const int nrows = nrows_dev ? *nrows_dev : nrows_host;
     const int chunks = D >> 3;
     for (int r = block; r < nrows; r += nblocks) {
-        const int src = index ? __ldg(index + r) : r;
+        const int src = r == block ? src0 : index ? __ldg(index + r) : r;
         const TIn *xr = x + static_cast<size_t>(src) * D;
         uint4 *orow = reinterpret_cast<uint4 *>(out + static_cast<size_t>(r) * D);
 #pragma unroll 4

@@ -2125,8 +2125,12 @@ static int layer_dev_impl(cudaStream_t st, int sms, int T, int K, int E, int n_s
         prof_mark(st, kPhStart);
         const size_t psm = perm_smem_bytes(T, KK, EE, l.perm.words);
         const int smem = K <= kPermSmemMaxK && psm <= kPermSmemMaxBytes ? 1 : 0;
-        CUDA_TRY(launch_pdl(layer_prep_small_kernel, dim3(1), dim3(1024), smem ? psm : 0, st, q,
-                            ep.pa, smem));
+        // One thread per expert or slot, whichever is more (the steps loop
+        // beyond 1024): fewer warps make each of the CTA's barriers and block
+        // scans cheaper.
+        const int pthreads = std::min(1024, (std::max({EE, T * KK, 32}) + 31) / 32 * 32);
+        CUDA_TRY(launch_pdl(layer_prep_small_kernel, dim3(1), dim3(pthreads), smem ? psm : 0, st,
+                            q, ep.pa, smem));
         prof_mark(st, kPhPermute);
         if (hooks && hooks->before_gather)
             if (int rc = hooks->before_gather())
