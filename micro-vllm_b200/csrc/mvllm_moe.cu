@@ -67,6 +67,7 @@ struct Context {
     cudaStream_t copy_stream = nullptr; // stream-ins of cold blobs, caller rows of layer_host
     cudaEvent_t copy_done = nullptr;
     cudaEvent_t call_start = nullptr, x_in = nullptr, out_in = nullptr; // caller-row copies
+    cudaEvent_t x_head = nullptr; // moe_block: the head part of xg is on the device
     uint64_t calls = 0, experts = 0, rows = 0;
     double h2d_ms = 0, kernel_ms = 0, d2h_ms = 0;
 };
@@ -1019,7 +1020,7 @@ int init_locked(Context &c, int device) {
     CUDA_TRY(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
     CUDA_TRY(cudaStreamCreateWithFlags(&c.copy_stream, cudaStreamNonBlocking));
     CUDA_TRY(cudaEventCreateWithFlags(&c.copy_done, cudaEventDisableTiming));
-    for (cudaEvent_t *e : {&c.call_start, &c.x_in, &c.out_in})
+    for (cudaEvent_t *e : {&c.call_start, &c.x_in, &c.out_in, &c.x_head})
         CUDA_TRY(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
     for (auto &e : c.ev)
         CUDA_TRY(cudaEventCreate(&e));
@@ -1227,9 +1228,9 @@ void mvllm_moe_shutdown(void) {
     for (auto &e : c.ev)
         cudaEventDestroy(e);
     cudaEventDestroy(c.copy_done);
-    for (cudaEvent_t e : {c.call_start, c.x_in, c.out_in})
+    for (cudaEvent_t e : {c.call_start, c.x_in, c.out_in, c.x_head})
         cudaEventDestroy(e);
-    c.call_start = c.x_in = c.out_in = nullptr;
+    c.call_start = c.x_in = c.out_in = c.x_head = nullptr;
     cudaStreamDestroy(c.copy_stream);
     cudaStreamDestroy(c.stream);
     c.stream = nullptr;
@@ -1675,11 +1676,28 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     // experts' pointers as null (skipped, their row base still advancing --
     // the plan's rule), the second batch the reverse; both write their own y
     // rows and the combine runs once.
+    // Without them, on the fast path, a call with at least kXgSplitBytes of
+    // gathered rows uploads xg in two parts: the experts whose rows all lie in
+    // the head part (below row x_split) run as a first batch once it has
+    // arrived, while the tail copies; the others run after the tail.
     const size_t xb = size_t(x_rows) * D * 4, ob = size_t(S_ext) * D * 4;
-    const int n_groups = two_batches ? 2 : 1;
+    constexpr size_t kXgSplitBytes = size_t(1) << 20;
+    int x_split = 0; // rows in the head part; 0: one upload, one batch
+    if (!two_batches && fast && n_valid >= 2 && xb >= kXgSplitBytes) {
+        const int half = int(x_rows / 2);
+        int head = 0;
+        for (int e = 0; e < nb; ++e)
+            if (valid[e] && xoff[e] + nr[e] <= half)
+                ++head;
+        if (head > 0 && head < n_valid)
+            x_split = half;
+    }
+    const int n_groups = (two_batches || x_split) ? 2 : 1;
     std::vector<int> grp(size_t(nb), 0);
     for (int e = 0; e < nb; ++e)
-        grp[size_t(e)] = (two_batches && late[size_t(e)]) ? 1 : 0;
+        grp[size_t(e)] = two_batches ? (late[size_t(e)] ? 1 : 0)
+                         : x_split   ? (valid[e] && xoff[e] + nr[e] > x_split ? 1 : 0)
+                                     : 0;
     std::vector<void *> tab(size_t(6) * n_groups * nb, nullptr);
     for (int e = 0; e < nb; ++e)
         for (int k = 0; k < 6; ++k)
@@ -1745,7 +1763,15 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
         CUDA_TRY(cudaEventRecord(c.call_start, c.stream));
         CUDA_TRY(cudaStreamWaitEvent(c.copy_stream, c.call_start, 0));
     }
-    CUDA_TRY(cudaMemcpyAsync(db + o_x, x_src, xb, cudaMemcpyHostToDevice, rows_st));
+    if (x_split) {
+        const size_t hb = size_t(x_split) * D * 4;
+        CUDA_TRY(cudaMemcpyAsync(db + o_x, x_src, hb, cudaMemcpyHostToDevice, rows_st));
+        CUDA_TRY(cudaEventRecord(c.x_head, rows_st));
+        CUDA_TRY(cudaMemcpyAsync(db + o_x + hb, static_cast<const uint8_t *>(x_src) + hb, xb - hb,
+                                 cudaMemcpyHostToDevice, rows_st));
+    } else {
+        CUDA_TRY(cudaMemcpyAsync(db + o_x, x_src, xb, cudaMemcpyHostToDevice, rows_st));
+    }
     CUDA_TRY(cudaEventRecord(c.x_in, rows_st));
     if (S_ext > 0) {
         CUDA_TRY(cudaMemcpyAsync(db + o_out, o_src, ob, cudaMemcpyHostToDevice, rows_st));
@@ -1754,7 +1780,7 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
                                      rows_st));
     }
     CUDA_TRY(cudaEventRecord(c.out_in, rows_st));
-    CUDA_TRY(cudaStreamWaitEvent(c.stream, c.x_in, 0));
+    CUDA_TRY(cudaStreamWaitEvent(c.stream, x_split ? c.x_head : c.x_in, 0));
     CUDA_TRY(cudaEventRecord(c.ev[1], c.stream));
     prof_mark(c.stream, kPhStart);
     void *const *dt = reinterpret_cast<void *const *>(db + o_tab);
@@ -1762,29 +1788,36 @@ static int moe_block_impl(int nb, int D, int Iinter, int fmt, const void *const 
     const int *d_xoff = reinterpret_cast<const int *>(db + o_xoff);
     float *d_out = reinterpret_cast<float *>(db + o_out);
     const float *d_x = reinterpret_cast<const float *>(db + o_x);
-    auto run_batch = [&](void *const *t) -> int {
+    auto run_batch = [&](void *const *t, int xr) -> int {
         Tables tb{t, t + nb, t + 2 * nb, t + 3 * nb, t + 4 * nb, t + 5 * nb};
         if (fast)
             return run_experts(c.stream, launch_sms(c), nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
-                               MVLLM_DTYPE_F32, int(x_rows), false, R / n_valid, act, act_a,
-                               act_b, w, allow_tc);
+                               MVLLM_DTYPE_F32, xr, false, R / n_valid, act, act_a, act_b, w,
+                               allow_tc);
         // Generic path reads the uploaded f32 rows directly.
         RunWs w2 = w;
         w2.xs = const_cast<float *>(d_x);
         return run_experts(c.stream, launch_sms(c), nb, D, Iinter, fmt_run, tb, d_nr, d_xoff, d_x,
-                           MVLLM_DTYPE_F32, int(x_rows), true, R / n_valid, act, act_a, act_b,
-                           w2);
+                           MVLLM_DTYPE_F32, xr, true, R / n_valid, act, act_a, act_b, w2);
     };
     int rc = MVLLM_OK;
     if (two_batches) {
         if (n_late < n_valid)
-            rc = run_batch(dt);
+            rc = run_batch(dt, int(x_rows));
         if (!rc) {
             CUDA_TRY(cudaStreamWaitEvent(c.stream, c.copy_done, 0));
-            rc = run_batch(dt + 6 * nb);
+            rc = run_batch(dt + 6 * nb, int(x_rows));
+        }
+    } else if (x_split) {
+        // The head batch stages only the head rows (the tail may still be
+        // copying); the tail batch stages them all.
+        rc = run_batch(dt, x_split);
+        if (!rc) {
+            CUDA_TRY(cudaStreamWaitEvent(c.stream, c.x_in, 0));
+            rc = run_batch(dt + 6 * nb, int(x_rows));
         }
     } else {
-        rc = run_batch(dt);
+        rc = run_batch(dt, int(x_rows));
     }
     if (rc) {
         cudaStreamSynchronize(c.copy_stream);
