@@ -154,7 +154,10 @@ MVLLM_API int mvllm_mx_terms_dev(void *stream, int mode, const void *src, int ro
                                  void *planes, void *codes);
 
 /* coli_cuda::group_stats (src/gpu/coli_cuda.hpp:35-36): calls, experts, rows
- * and host-timed h2d / kernel / d2h milliseconds of the host-pointer entries. */
+ * and host-timed h2d / kernel / d2h milliseconds of the host-pointer entries.
+ * h2d counts the copies before the first expert kernel starts; copies that
+ * overlap the kernels (mvllm_moe_block's tail of a two-part activation
+ * upload) count as kernel time. */
 MVLLM_API void mvllm_moe_stats(uint64_t *calls, uint64_t *experts, uint64_t *rows, double *h2d_ms,
                      double *kernel_ms, double *d2h_ms);
 
