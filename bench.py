@@ -1488,7 +1488,14 @@ def main():
                                            "capture with the same rows per expert, x 8); not "
                                            "measured in this run",
                          "algorithmic_flops_per_step_per_gpu": flops / world,
-                         "kernel_ms_per_step": e_ms},
+                         "kernel_ms_per_step": e_ms,
+                         "limiter": "the dominant kernel (wide single-CTA tiles, N = 176 "
+                                    "tokens per MMA) is bound by shared-memory bandwidth: per "
+                                    "MMA its token slice is written by TMA and read by the MMA "
+                                    "(5.6 KB each) with 1 KB of packed weights read by the "
+                                    "dequant warps, about 96 cycles at 128 B/clk against 88 "
+                                    "of tensor time; single-CTA f16 MMAs run at the full "
+                                    "rate from N = 128 (bench.py --mma-rates)"},
             "gpu_launches": launches_per_ep_step(world, mode) * args.steps,
             "e2e": ep_res.get("e2e"),
             "cpu_baseline": cpu,
