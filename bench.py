@@ -147,7 +147,7 @@ def headline_traffic():
         return None
     with open(p) as f:
         for line in f:
-            if line.startswith("phase1_pair_dram_bytes_per_launch_full_size:"):
+            if line.startswith("phase1_wide_dram_bytes_per_launch_full_size:"):
                 return float(line.split(":", 1)[1])
     return None
 
